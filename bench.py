@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Memory-layer forward benchmark (B200).
+
+One step = one forward of the memory-layer block of KumarDev7/model
+(model.py:108-120 around memory.py:119-227) over T = 8192 tokens per GPU at
+the single-layer configuration: d_model 256, H 4, d_key 256,
+n_sub_keys 512 (262,144 slots), top_k 16, d_value 256, float32 values.
+Inputs are synthetic and seeded: hidden ~ N(0,1), Glorot-uniform router /
+gate / output kernels, sub_keys ~ N(0, 1/128), values ~ N(0, 0.02).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``value`` is whole-job tokens/s from CUDA
+events around each step (inputs resident in HBM; L2 flushed before every
+step), max over ranks; ``e2e`` is the same through the C ABI with the hidden
+states copied in from pinned host memory and the layer output copied back
+inside the timed region.  ``--impl reference`` times the CPU oracle (a
+float32 restatement of the reference layer) on the host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = dict(name="cfg0_layer_forward", tokens_per_gpu=8192, d_model=256, heads=4, d_key=256, n_sub_keys=512,
+                top_k=16, d_value=256, values_dtype="f32", seed=0)
+FLUSH_BYTES = 256 << 20          # > 126 MB L2
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--values-dtype", choices=["f32", "f16", "bf16"], default="f32")
+    ap.add_argument("--tokens", type=int, default=WORKLOAD["tokens_per_gpu"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls NVML (SM clock, max clock, clock-event reasons) on a thread."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index: int, period: float = 0.005):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.period, self._stop = period, threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable
+            self.err = str(e)
+        self.t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples), "source": "nvml"}
+
+
+# ---------------------------------------------------------------- inputs
+def make_inputs(torch, device, W, values_dtype, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    T, dm, H, dk, n, d = (W[k] for k in ("tokens_per_gpu", "d_model", "heads", "d_key", "n_sub_keys", "d_value"))
+
+    def glorot(fi, fo):
+        lim = math.sqrt(6.0 / (fi + fo))
+        return (torch.rand(fi, fo, device=device, generator=g) * 2 - 1) * lim
+
+    vdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[values_dtype]
+    x = {
+        "h": torch.randn(T, dm, device=device, generator=g),
+        "w_router": glorot(dm, H * dk), "b_router": torch.zeros(H * dk, device=device),
+        "sub_keys": torch.randn(H, 2, n, dk // 2, device=device, generator=g) * math.sqrt(1 / 128),
+        "log_t": torch.full((1,), math.log(10.0), device=device),
+        "values": (torch.randn(n * n, d, device=device, generator=g) * 0.02).to(vdt),
+        "w_gate": glorot(dm, d), "b_gate": torch.zeros(d, device=device),
+        "w_out": glorot(d, dm), "b_out": torch.zeros(dm, device=device),
+    }
+    return x
+
+
+class LayerCall:
+    """Pre-built C-ABI call of memlayer_layer_forward on resident buffers."""
+
+    def __init__(self, torch, L, W, x, device, values_dtype):
+        T, H, k, d, dm = (W[k] for k in ("tokens_per_gpu", "heads", "top_k", "d_value", "d_model"))
+        dt = {"f32": L.F32, "f16": L.F16, "bf16": L.BF16}[values_dtype]
+        self.L, self.torch = L, torch
+        self.cfg = L.MemlayerConfig(tokens=T, heads=H, n_sub_keys=W["n_sub_keys"], d_key=W["d_key"], d_value=d,
+                                    top_k=k, d_model=dm, values_dtype=dt, routing_noise=1.0, min_temperature=10.0,
+                                    max_temperature=100.0, query_scale=0, balance_temperature_grad=0)
+        self.y = torch.empty(T, dm, device=device)
+        self.slots = torch.empty(T, H, k, dtype=torch.int32, device=device)
+        self.weights = torch.empty(T, H, k, device=device)
+        self.top1 = torch.empty(1, device=device)
+        self.temp = torch.empty(1, device=device)
+        self.events = L.MemlayerStageEvents()
+        pool = L.MemlayerPoolArgs(sub_keys=x["sub_keys"].data_ptr(), log_temperature=x["log_t"].data_ptr(),
+                                  values=x["values"].data_ptr(), slots=self.slots.data_ptr(),
+                                  weights=self.weights.data_ptr(), top1_weight=self.top1.data_ptr(),
+                                  temperature=self.temp.data_ptr(), stage_events=C.pointer(self.events))
+        self.args = L.MemlayerLayerArgs(h=x["h"].data_ptr(), w_router=x["w_router"].data_ptr(),
+                                        b_router=x["b_router"].data_ptr(), w_gate=x["w_gate"].data_ptr(),
+                                        b_gate=x["b_gate"].data_ptr(), w_out=x["w_out"].data_ptr(),
+                                        b_out=x["b_out"].data_ptr(), y=self.y.data_ptr(), mem=None, pool=pool)
+        nb = C.c_size_t()
+        L.check(L.lib().memlayer_layer_workspace_size(C.byref(self.cfg), C.byref(nb)), "workspace_size")
+        self.ws = torch.empty(nb.value, dtype=torch.uint8, device=device)
+        self.ws_bytes = nb.value
+
+    def __call__(self, stream, events=None):
+        for i in range(self.L.STAGE_EVENTS):
+            self.events.events[i] = None if events is None else events[i].cuda_event
+        self.L.check(self.L.lib().memlayer_layer_forward(C.byref(self.cfg), C.byref(self.args),
+                                                         self.ws.data_ptr(), self.ws_bytes, stream.cuda_stream),
+                     "memlayer_layer_forward")
+
+
+def gather_bytes(W, values_dtype):
+    """Algorithmic bytes of one combine+gather launch (the dominant HBM
+    kernel): value rows + stage-1 lists + gate in + gated output + slots/weights."""
+    T, H, k, d = W["tokens_per_gpu"], W["heads"], W["top_k"], W["d_value"]
+    es = {"f32": 4, "f16": 2, "bf16": 2}[values_dtype]
+    rows = T * H * k * d * es
+    io = T * H * 2 * k * 12 + T * d * 4 * 2 + T * H * k * 8 + T * H * 4
+    return rows, rows + io
+
+
+def load_traffic(kernel):
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f).get(kernel)
+
+
+# ---------------------------------------------------------------- CPU oracle timing
+def cpu_oracle_rate(W, tokens, repeats=3, threads=None):
+    """tokens/s of the CPU oracle layer forward on `tokens` tokens of the
+    workload, token chunks spread over a thread pool of all host cores."""
+    import concurrent.futures as cf
+
+    import numpy as np
+
+    from oracle import memlayer_ref as ref
+    threads = threads or os.cpu_count() or 1
+    rng = np.random.default_rng(W["seed"])
+    H, dk, n, d, dm, k = (W[x] for x in ("heads", "d_key", "n_sub_keys", "d_value", "d_model", "top_k"))
+    values = rng.standard_normal((n * n, d), dtype=np.float32) * np.float32(0.02)
+    sk = rng.standard_normal((H, 2, n, dk // 2), dtype=np.float32) * np.float32(math.sqrt(1 / 128))
+
+    def glorot(fi, fo):
+        lim = math.sqrt(6.0 / (fi + fo))
+        return rng.uniform(-lim, lim, (fi, fo)).astype(np.float32)
+    wr, wg, wo = glorot(dm, H * dk), glorot(dm, d), glorot(d, dm)
+    h = rng.standard_normal((tokens, dm), dtype=np.float32)
+    cfg = ref.PoolConfig(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k)
+    z = lambda m: np.zeros(m, np.float32)  # noqa: E731
+    log_t = np.log(np.float32(10.0))
+    chunk = max(64, tokens // threads)
+
+    def one(s):
+        return ref.layer_forward(cfg, h[s:s + chunk], wr, z(H * dk), sk, log_t, values, wg, z(d), wo, z(dm))[0]
+
+    with cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(one, range(0, min(tokens, chunk * threads), chunk)))   # warm-up
+        times = []
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            list(ex.map(one, range(0, tokens, chunk)))
+            times.append(time.perf_counter() - t0)
+    return tokens / statistics.median(times), threads, f"{tokens} tokens x {repeats} runs (median), " \
+        f"{chunk}-token chunks over {threads} threads, numpy float32"
+
+
+# ---------------------------------------------------------------- arms
+def run_reference(args, W, rank):
+    if rank != 0:
+        return None
+    tokens = min(2048, args.tokens)
+    steps = max(1, args.steps // 20)
+    rate, cores, sample = cpu_oracle_rate(W, tokens, repeats=steps)
+    line = {"impl": "reference", "metric": "memory-layer tokens/s", "value": rate, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": 1, "ms_per_step": 1000.0 * tokens / rate,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": W["name"], **{k: W[k] for k in W if k != "name"}},
+            "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    return line
+
+
+def run_ours(args, W, rank, world):
+    import torch
+
+    from model_b200 import _lib as L
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(device)
+    lib = L.lib()
+    x = make_inputs(torch, device, W, args.values_dtype, W["seed"] + rank)
+    call = LayerCall(torch, L, W, x, device, args.values_dtype)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    T = W["tokens_per_gpu"]
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        call(stream)
+    torch.cuda.synchronize()
+
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(L.STAGE_EVENTS)] for _ in range(K)]
+    for row in ev:                 # create the driver events before handing them to the library
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize()
+    launches0 = lib.memlayer_kernel_launch_count()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index) as clk:
+        for i in range(K):
+            flush.zero_()
+            call(stream, ev[i])
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    launches = (lib.memlayer_kernel_launch_count() - launches0) // K
+    step_ms = [ev[i][0].elapsed_time(ev[i][5]) for i in range(K)]
+    stage = lambda a, b: statistics.mean(ev[i][a].elapsed_time(ev[i][b]) for i in range(K))  # noqa: E731
+    stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
+              "combine_gather": stage(3, 4), "finalize_out": stage(4, 5)}
+    ms = statistics.mean(step_ms)
+
+    # ---- e2e through the C ABI with host buffers ----
+    h_host = x["h"].cpu().pin_memory()
+    y_host = torch.empty_like(call.y, device="cpu").pin_memory()
+    e0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for _ in range(max(1, args.warmup // 2)):
+        x["h"].copy_(h_host, non_blocking=True)
+        call(stream)
+        y_host.copy_(call.y, non_blocking=True)
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.zero_()
+        e0[i].record(stream)
+        x["h"].copy_(h_host, non_blocking=True)
+        call(stream)
+        y_host.copy_(call.y, non_blocking=True)
+        e1[i].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
+
+    stats = torch.tensor([ms, e2e_ms, stages["combine_gather"]], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms, gather_ms = stats.tolist()
+    if rank != 0:
+        return None
+
+    hbm, src = peaks()
+    rows_b, alg_b = gather_bytes(W, args.values_dtype)
+    achieved = alg_b / (gather_ms * 1e-3) / 1e9
+    traffic = load_traffic("combine_gather_kernel")
+    line = {
+        "metric": "memory-layer tokens/s", "value": T * world / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded: hidden N(0,1), Glorot kernels, sub_keys N(0,1/128), values N(0,0.02))",
+        "config": {"workload": W["name"], **{k: W[k] for k in W if k != "name"},
+                   "values_dtype": args.values_dtype,
+                   "l2": "flushed before every step (256 MiB write, outside the step events)",
+                   "parallelism": f"replicas{world}" if world > 1 else "single"},
+        "roofline": {"kernel": "combine_gather_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm,
+                     "peak_source": src, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
+                     "algorithmic_bytes_per_launch": alg_b, "row_bytes_per_launch": rows_b},
+        "gather_gbs": rows_b / (gather_ms * 1e-3) / 1e9,
+        "stages_ms": stages,
+        "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h_host.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
+        "gpu_launches": int(launches) * K,
+        "gpu_launches_per_step": int(launches),
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        rate, cores, sample = cpu_oracle_rate(W, 2048)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    return line
+
+
+def main():
+    args = parse()
+    W = dict(WORKLOAD, values_dtype=args.values_dtype, tokens_per_gpu=args.tokens)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    if args.impl == "reference":
+        line = run_reference(args, W, rank)
+    else:
+        line = run_ours(args, W, rank, world)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1 and args.impl == "ours":
+        import torch
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/*
+ * memlayer.h -- C ABI of the B200 (sm_100a) product-key memory layer.
+ *
+ * Drop-in boundary for the memory layer of KumarDev7/model:
+ *   - memlayer_pool_forward   replaces MemoryPool.__call__
+ *                             (memory_pool_model/memory.py:119-227);
+ *   - memlayer_layer_forward  replaces the memory-layer block of
+ *                             MemoryPoolLM.__call__ (memory_pool_model/model.py:108-120):
+ *                             router Dense -> MemoryPool -> silu(Dense) gate -> Dense.
+ * A jax.ffi handler (or any other host) binds these symbols directly.
+ *
+ * Conventions
+ *   - Every pointer in the argument structs is a device pointer unless its
+ *     comment says otherwise.  All float tensors are float32, row-major,
+ *     contiguous; the value table may be float32, float16 or bfloat16.
+ *   - The library allocates nothing on these paths: the caller passes a
+ *     device workspace of at least memlayer_*_workspace_size() bytes, 256-byte
+ *     aligned.  The workspace's contents need not be initialised.
+ *   - Calls are stream-ordered on the given cudaStream_t (passed as void*),
+ *     return as soon as the work is enqueued and never synchronise the device.
+ *   - No C++ exception crosses this boundary; errors are memlayer_status codes.
+ *     Argument errors are detected on the host before anything is enqueued.
+ *   - Thread safety: calls on different streams may run concurrently from
+ *     different host threads as long as they use different workspaces and
+ *     output buffers.
+ */
+#ifndef MEMLAYER_H_
+#define MEMLAYER_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MEMLAYER_ABI_VERSION 1
+
+typedef enum {
+  MEMLAYER_OK = 0,
+  MEMLAYER_ERR_BAD_SHAPE = 1,     /* a dimension is out of range or inconsistent */
+  MEMLAYER_ERR_BAD_POINTER = 2,   /* a required pointer is NULL or misaligned */
+  MEMLAYER_ERR_UNSUPPORTED = 3,   /* a valid reference setting this build does not implement */
+  MEMLAYER_ERR_WORKSPACE = 4,     /* workspace missing or smaller than required */
+  MEMLAYER_ERR_CUDA = 5,          /* a CUDA launch or runtime call failed */
+  MEMLAYER_ERR_PEER_TIMEOUT = 6   /* a bounded wait on another GPU gave up */
+} memlayer_status;
+
+typedef enum {
+  MEMLAYER_F32 = 0,
+  MEMLAYER_F16 = 1,
+  MEMLAYER_BF16 = 2
+} memlayer_dtype;
+
+/* The MemoryPool fields (memory.py:72-97, config.py:35-59) plus the call's
+ * leading size.  d_model is used only by memlayer_layer_forward. */
+typedef struct {
+  int64_t tokens;                /* M: product of the queries' leading dims */
+  int32_t heads;                 /* pool_heads (H) */
+  int32_t n_sub_keys;            /* n; the pool has n*n slots */
+  int32_t d_key;                 /* even; each half has d_key/2 dims */
+  int32_t d_value;               /* d */
+  int32_t top_k;                 /* k, 1 <= k <= min(n, 32) */
+  int32_t d_model;               /* hidden size for the layer entry */
+  int32_t values_dtype;          /* memlayer_dtype of the value table */
+  float routing_noise;           /* scale of the Gumbel selection noise */
+  float min_temperature;         /* clamp of exp(log_temperature) */
+  float max_temperature;
+  int32_t query_scale;           /* scale scores by |q_half| / sqrt(d_key/2) */
+  int32_t balance_temperature_grad; /* P uses the full scores (with q_len) */
+} memlayer_config;
+
+/* Optional stage timestamps for profiling: cudaEvent_t handles (as void*)
+ * that the call records on its stream at fixed stage boundaries.  NULL
+ * entries are skipped.  Boundaries:
+ *   0 start                       3 after score GEMM + per-half top-k
+ *   1 after router / gate GEMMs   4 after k*k combine + softmax + gather
+ *   2 after key / query prep      5 end (stats, output projection done)   */
+#define MEMLAYER_STAGE_EVENTS 6
+typedef struct {
+  void* events[MEMLAYER_STAGE_EVENTS];
+} memlayer_stage_events;
+
+/* Per-call inputs/outputs of MemoryPool.__call__. */
+typedef struct {
+  /* inputs */
+  const float* queries;          /* [M, H, d_key] router queries */
+  const float* sub_keys;         /* [H, 2, n, d_key/2] (normalised inside, as memory.py:139) */
+  const float* log_temperature;  /* [1] */
+  const void* values;            /* [n*n, d] of values_dtype; 16-byte aligned */
+  const float* gumbel;           /* [M, H, 2, n] standard Gumbel sample, or NULL */
+  float noise_scale;             /* multiplies routing_noise (memory.py:158) */
+  int32_t train;                 /* selection noise is applied only when train != 0 */
+  int32_t shuffle_reads;         /* read (slot + N/2 + 1) % N (memory.py:179) */
+  /* outputs */
+  float* out;                    /* [M, d] */
+  int32_t* slots;                /* [M, H, k] */
+  float* weights;                /* [M, H, k] */
+  /* optional aux outputs (NULL = not computed) */
+  float* queries_unit;           /* [M, H, 2, d_key/2] aux["queries"] */
+  float* subkey_counts;          /* [H, 2, n] */
+  float* slot_counts;            /* [n*n] */
+  float* balance_loss;           /* [1] */
+  float* top1_weight;            /* [1] */
+  float* temperature;            /* [1] */
+  const memlayer_stage_events* stage_events;  /* optional profiling hook, or NULL */
+} memlayer_pool_args;
+
+/* Per-call inputs/outputs of the memory-layer block (model.py:108-120):
+ *   q   = h @ w_router + b_router                      (router_i)
+ *   mem = MemoryPool(q)                                (pool)
+ *   y   = (mem * silu(h @ w_gate + b_gate)) @ w_out + b_out   (mem_gate_i, mem_out_i)
+ * y is the term the reference adds into the residual-stream update. */
+typedef struct {
+  const float* h;                /* [M, d_model] layer-normalised hidden state */
+  const float* w_router;         /* [d_model, H*d_key] */
+  const float* b_router;         /* [H*d_key] or NULL (zero bias) */
+  const float* w_gate;           /* [d_model, d] */
+  const float* b_gate;           /* [d] or NULL */
+  const float* w_out;            /* [d, d_model] */
+  const float* b_out;            /* [d_model] or NULL */
+  float* y;                      /* [M, d_model] output */
+  float* mem;                    /* [M, d] pool output before the gate, or NULL */
+  memlayer_pool_args pool;       /* pool.queries is ignored (computed from h);
+                                    pool.out may be NULL */
+} memlayer_layer_args;
+
+/* ABI version of the loaded library (MEMLAYER_ABI_VERSION at build time). */
+int32_t memlayer_abi_version(void);
+
+/* Human-readable name of a status code (static storage). */
+const char* memlayer_status_string(int32_t status);
+
+/* Diagnostics: number of kernels this library has launched in this process
+ * (all devices, all threads).  Has no counterpart in the reference. */
+int64_t memlayer_kernel_launch_count(void);
+
+/* Bytes of device workspace memlayer_pool_forward needs for cfg. */
+int32_t memlayer_pool_workspace_size(const memlayer_config* cfg, size_t* bytes);
+
+/* MemoryPool.__call__ (memory.py:119-227).  Reference interface replaced:
+ * memory_pool_model/memory.py:119 `MemoryPool.__call__(queries, *, train,
+ * sparse_grad, noise_scale, shuffle_reads) -> (out, aux)`; sparse_grad only
+ * affects differentiation and has no forward effect. */
+int32_t memlayer_pool_forward(const memlayer_config* cfg, const memlayer_pool_args* args,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of device workspace memlayer_layer_forward needs for cfg. */
+int32_t memlayer_layer_workspace_size(const memlayer_config* cfg, size_t* bytes);
+
+/* Memory-layer block of MemoryPoolLM.__call__ (model.py:108-120).
+ * Reference interface replaced: model.py:110-119 (router_i Dense, pool call,
+ * mem_gate_i / mem_out_i Dense) inside each layer in cfg.memory_layers. */
+int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_args* args,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEMLAYER_H_ */

@@ -1,0 +1,125 @@
+"""ctypes binding of ``include/memlayer.h`` (the library's C ABI).
+
+The structures below mirror the header field for field.  Loading fails
+loudly if ``libmemlayer.so`` has not been built: there is no fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmemlayer.so")
+
+OK, ERR_BAD_SHAPE, ERR_BAD_POINTER, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA, ERR_PEER_TIMEOUT = range(7)
+F32, F16, BF16 = 0, 1, 2
+
+
+class MemlayerConfig(C.Structure):
+    _fields_ = [
+        ("tokens", C.c_int64),
+        ("heads", C.c_int32),
+        ("n_sub_keys", C.c_int32),
+        ("d_key", C.c_int32),
+        ("d_value", C.c_int32),
+        ("top_k", C.c_int32),
+        ("d_model", C.c_int32),
+        ("values_dtype", C.c_int32),
+        ("routing_noise", C.c_float),
+        ("min_temperature", C.c_float),
+        ("max_temperature", C.c_float),
+        ("query_scale", C.c_int32),
+        ("balance_temperature_grad", C.c_int32),
+    ]
+
+
+STAGE_EVENTS = 6
+
+
+class MemlayerStageEvents(C.Structure):
+    _fields_ = [("events", C.c_void_p * STAGE_EVENTS)]
+
+
+class MemlayerPoolArgs(C.Structure):
+    _fields_ = [
+        ("queries", C.c_void_p),
+        ("sub_keys", C.c_void_p),
+        ("log_temperature", C.c_void_p),
+        ("values", C.c_void_p),
+        ("gumbel", C.c_void_p),
+        ("noise_scale", C.c_float),
+        ("train", C.c_int32),
+        ("shuffle_reads", C.c_int32),
+        ("out", C.c_void_p),
+        ("slots", C.c_void_p),
+        ("weights", C.c_void_p),
+        ("queries_unit", C.c_void_p),
+        ("subkey_counts", C.c_void_p),
+        ("slot_counts", C.c_void_p),
+        ("balance_loss", C.c_void_p),
+        ("top1_weight", C.c_void_p),
+        ("temperature", C.c_void_p),
+        ("stage_events", C.POINTER(MemlayerStageEvents)),
+    ]
+
+
+class MemlayerLayerArgs(C.Structure):
+    _fields_ = [
+        ("h", C.c_void_p),
+        ("w_router", C.c_void_p),
+        ("b_router", C.c_void_p),
+        ("w_gate", C.c_void_p),
+        ("b_gate", C.c_void_p),
+        ("w_out", C.c_void_p),
+        ("b_out", C.c_void_p),
+        ("y", C.c_void_p),
+        ("mem", C.c_void_p),
+        ("pool", MemlayerPoolArgs),
+    ]
+
+
+class MemlayerError(RuntimeError):
+    """A non-zero memlayer_status."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        super().__init__(f"{where}: {status_string(status)} (status {status})")
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m model_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        L.memlayer_abi_version.restype = C.c_int32
+        L.memlayer_status_string.restype = C.c_char_p
+        L.memlayer_status_string.argtypes = [C.c_int32]
+        for name in ("memlayer_pool_workspace_size", "memlayer_layer_workspace_size"):
+            f = getattr(L, name)
+            f.restype = C.c_int32
+            f.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(C.c_size_t)]
+        L.memlayer_pool_forward.restype = C.c_int32
+        L.memlayer_pool_forward.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerPoolArgs), C.c_void_p,
+                                            C.c_size_t, C.c_void_p]
+        L.memlayer_layer_forward.restype = C.c_int32
+        L.memlayer_layer_forward.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs), C.c_void_p,
+                                             C.c_size_t, C.c_void_p]
+        if L.memlayer_abi_version() != 1:
+            raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
+        _lib = L
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().memlayer_status_string(status).decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != OK:
+        raise MemlayerError(status, where)

@@ -1,0 +1,259 @@
+// C ABI of the memory layer (include/memlayer.h): argument validation,
+// workspace layout and the launch sequence of one forward call.
+#include <math.h>
+#include <string.h>
+
+#include <atomic>
+
+#include "common.cuh"
+
+namespace ml {
+
+static std::atomic<int64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+namespace {
+
+constexpr size_t ALIGN = 256;
+
+inline size_t up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
+
+struct Flags {
+  bool layer = false;
+  bool balance = false;   // balance_loss requested
+};
+
+int check_config(const memlayer_config* c, Dims* D, bool layer) {
+  if (!c || !D) return MEMLAYER_ERR_BAD_POINTER;
+  if (c->tokens < 0 || c->heads < 1 || c->heads > 32 || c->n_sub_keys < 1 || c->d_key < 2 || c->d_key % 2 ||
+      c->d_value < 1 || c->top_k < 1 || c->top_k > c->n_sub_keys)
+    return MEMLAYER_ERR_BAD_SHAPE;
+  if (c->n_sub_keys > 46340) return MEMLAYER_ERR_BAD_SHAPE;       // n*n must fit int32 slot ids
+  if (c->top_k > 32 || c->d_key > 256 || c->d_value > 1024) return MEMLAYER_ERR_UNSUPPORTED;
+  if (c->values_dtype != MEMLAYER_F32 && c->values_dtype != MEMLAYER_F16 && c->values_dtype != MEMLAYER_BF16)
+    return MEMLAYER_ERR_UNSUPPORTED;
+  if (c->values_dtype != MEMLAYER_F32 && c->d_value % 8) return MEMLAYER_ERR_UNSUPPORTED;
+  if (c->values_dtype == MEMLAYER_F32 && c->d_value % 4 && c->d_value > 256) return MEMLAYER_ERR_UNSUPPORTED;
+  if (layer && c->d_model < 1) return MEMLAYER_ERR_BAD_SHAPE;
+  if (!(c->min_temperature > 0.f) || !(c->max_temperature >= c->min_temperature)) return MEMLAYER_ERR_BAD_SHAPE;
+  D->M = c->tokens;
+  D->H = c->heads;
+  D->n = c->n_sub_keys;
+  D->dk = c->d_key;
+  D->half = c->d_key / 2;
+  D->d = c->d_value;
+  D->k = c->top_k;
+  D->kmax = c->top_k <= 4 ? 4 : c->top_k <= 8 ? 8 : c->top_k <= 16 ? 16 : 32;
+  D->dm = c->d_model;
+  D->vdtype = c->values_dtype;
+  D->N = (int64_t)c->n_sub_keys * c->n_sub_keys;
+  D->qscale = c->query_scale != 0;
+  D->btgrad = c->balance_temperature_grad != 0;
+  D->noise_coef = 0.f;
+  D->noisy = false;
+  D->shuffle = false;
+  return MEMLAYER_OK;
+}
+
+// Carve the workspace (ws == nullptr: only measure).  Returns total bytes.
+size_t layout(const Dims& D, const Flags& f, char* ws, Work* W) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> void* {
+    void* p = ws ? ws + off : nullptr;
+    off += up(bytes);
+    return p;
+  };
+  const int64_t rows = D.M * D.H * 2;
+  const int64_t tiles = (D.M + SCORE_TM - 1) / SCORE_TM;
+  Work w;
+  w.scal = (float*)take(4 * sizeof(float));
+  w.keys_n = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
+  w.qn = (float*)take(sizeof(float) * rows * D.half);
+  w.qlen = (float*)take(sizeof(float) * rows);
+  w.sub_idx = (int*)take(sizeof(int) * rows * D.k);
+  w.sub_score = (float*)take(sizeof(float) * rows * D.k);
+  w.sub_sel = (float*)take(sizeof(float) * rows * D.k);
+  w.top1_part = (float*)take(sizeof(float) * D.M * D.H);
+  if (f.balance) {
+    w.clean_idx = (int*)take(sizeof(int) * rows * D.k);
+    w.row_max = (float*)take(sizeof(float) * rows);
+    w.row_sum = (float*)take(sizeof(float) * rows);
+    w.p_part = (float*)take(sizeof(float) * tiles * D.H * 2 * D.n);
+    w.clean_cnt = (float*)take(sizeof(float) * D.H * 2 * D.n);
+  }
+  if (f.layer) {
+    w.qraw = (float*)take(sizeof(float) * D.M * D.H * D.dk);
+    w.gate = (float*)take(sizeof(float) * D.M * D.d);
+    w.memg = (float*)take(sizeof(float) * D.M * D.d);
+    w.slots = (int*)take(sizeof(int) * D.M * D.H * D.k);
+    w.weights = (float*)take(sizeof(float) * D.M * D.H * D.k);
+  }
+  if (W) *W = w;
+  return off;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int check_pool_args(const Dims& D, const memlayer_pool_args* a, bool layer) {
+  if (!a) return MEMLAYER_ERR_BAD_POINTER;
+  if (!a->sub_keys || !a->log_temperature || !a->values) return MEMLAYER_ERR_BAD_POINTER;
+  if (D.M == 0) return MEMLAYER_OK;
+  if (!layer && !a->queries) return MEMLAYER_ERR_BAD_POINTER;
+  if (!layer && (!a->out || !a->slots || !a->weights)) return MEMLAYER_ERR_BAD_POINTER;
+  if (D.vdtype != MEMLAYER_F32 && !aligned16(a->values)) return MEMLAYER_ERR_BAD_POINTER;
+  return MEMLAYER_OK;
+}
+
+void resolve_noise(Dims* D, const memlayer_config* c, const memlayer_pool_args* a) {
+  // memory.py:155-159: select = scores + routing_noise * noise_scale * gumbel (train only)
+  const double coef = (double)c->routing_noise * (double)a->noise_scale;
+  D->noisy = a->train && c->routing_noise > 0.f && coef != 0.0;
+  D->noise_coef = (float)coef;
+  D->shuffle = a->shuffle_reads != 0;
+}
+
+#define ML_TRY(x)                              \
+  do {                                         \
+    cudaError_t e_ = (x);                      \
+    if (e_ != cudaSuccess) return MEMLAYER_ERR_CUDA; \
+  } while (0)
+
+cudaError_t mark(const memlayer_pool_args* a, int i, cudaStream_t s) {
+  if (!a->stage_events || !a->stage_events->events[i]) return cudaSuccess;
+  return cudaEventRecord((cudaEvent_t)a->stage_events->events[i], s);
+}
+
+// The shared pool sequence; q is [M, H, d_key] (caller queries or router output).
+int run_pool(const Dims& D, const memlayer_config* c, const memlayer_pool_args* a, const Work& W, const float* q,
+             int* slots, float* weights, float* out, float* memg, const float* gate, cudaStream_t s) {
+  ML_TRY(launch_prep_keys(D, a->sub_keys, a->log_temperature, c->min_temperature, c->max_temperature, W.keys_n,
+                          W.scal, s));
+  float* qn = a->queries_unit ? a->queries_unit : W.qn;
+  ML_TRY(launch_normalize_queries(D, q, qn, W.qlen, s));
+  ML_TRY(mark(a, 2, s));
+  Work w2 = W;
+  w2.qn = qn;
+  const bool bal = a->balance_loss != nullptr;
+  ML_TRY(launch_score_topk(D, w2, a->gumbel, bal, s));
+  if (bal) ML_TRY(launch_balance(D, w2, a->balance_loss, s));
+  if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
+  if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
+  ML_TRY(mark(a, 3, s));
+  ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, gate, a->slot_counts,
+                               a->subkey_counts, s));
+  ML_TRY(mark(a, 4, s));
+  ML_TRY(launch_finalize(D, w2, a->top1_weight, a->temperature, s));
+  return MEMLAYER_OK;
+}
+
+}  // namespace
+}  // namespace ml
+
+using namespace ml;
+
+extern "C" {
+
+int32_t memlayer_abi_version(void) { return MEMLAYER_ABI_VERSION; }
+
+int64_t memlayer_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+const char* memlayer_status_string(int32_t s) {
+  switch (s) {
+    case MEMLAYER_OK: return "ok";
+    case MEMLAYER_ERR_BAD_SHAPE: return "bad shape";
+    case MEMLAYER_ERR_BAD_POINTER: return "bad pointer";
+    case MEMLAYER_ERR_UNSUPPORTED: return "unsupported setting";
+    case MEMLAYER_ERR_WORKSPACE: return "workspace too small";
+    case MEMLAYER_ERR_CUDA: return "CUDA error";
+    case MEMLAYER_ERR_PEER_TIMEOUT: return "peer timeout";
+    default: return "unknown status";
+  }
+}
+
+int32_t memlayer_pool_workspace_size(const memlayer_config* cfg, size_t* bytes) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.balance = true;  // sized for the largest request
+  *bytes = layout(D, f, nullptr, nullptr);
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_layer_workspace_size(const memlayer_config* cfg, size_t* bytes) {
+  Dims D;
+  int st = check_config(cfg, &D, true);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.balance = true;
+  f.layer = true;
+  *bytes = layout(D, f, nullptr, nullptr);
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_pool_forward(const memlayer_config* cfg, const memlayer_pool_args* a, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  st = check_pool_args(D, a, false);
+  if (st) return st;
+  resolve_noise(&D, cfg, a);
+  if (D.noisy && !a->gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.balance = a->balance_loss != nullptr;
+  size_t need = layout(D, f, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  Work W;
+  layout(D, f, (char*)workspace, &W);
+  cudaStream_t s = (cudaStream_t)stream;
+  ML_TRY(mark(a, 0, s));
+  ML_TRY(mark(a, 1, s));
+  st = run_pool(D, cfg, a, W, a->queries, a->slots, a->weights, a->out, nullptr, nullptr, s);
+  if (st) return st;
+  ML_TRY(mark(a, 5, s));
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_args* a, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, true);
+  if (st) return st;
+  if (!a) return MEMLAYER_ERR_BAD_POINTER;
+  st = check_pool_args(D, &a->pool, true);
+  if (st) return st;
+  if (D.M > 0 && (!a->h || !a->w_router || !a->w_gate || !a->w_out || !a->y)) return MEMLAYER_ERR_BAD_POINTER;
+  resolve_noise(&D, cfg, &a->pool);
+  if (D.noisy && !a->pool.gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.layer = true;
+  f.balance = a->pool.balance_loss != nullptr;
+  size_t need = layout(D, f, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  Work W;
+  layout(D, f, (char*)workspace, &W);
+  cudaStream_t s = (cudaStream_t)stream;
+  ML_TRY(mark(&a->pool, 0, s));
+  // model.py:110 router, model.py:118 gate pre-activation + silu
+  ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
+  ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
+  ML_TRY(mark(&a->pool, 1, s));
+  int* slots = a->pool.slots ? a->pool.slots : W.slots;
+  float* weights = a->pool.weights ? a->pool.weights : W.weights;
+  float* out = a->mem ? a->mem : a->pool.out;
+  st = run_pool(D, cfg, &a->pool, W, W.qraw, slots, weights, out, W.memg, W.gate, s);
+  if (st) return st;
+  if (a->mem && a->pool.out && a->pool.out != a->mem && D.M > 0)
+    ML_TRY(cudaMemcpyAsync(a->pool.out, a->mem, sizeof(float) * D.M * D.d, cudaMemcpyDeviceToDevice, s));
+  // model.py:119 output projection
+  ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));
+  ML_TRY(mark(&a->pool, 5, s));
+  return MEMLAYER_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,161 @@
+// Normalisation, temperature, float32 GEMM (router / gate / output
+// projections) and the final aux reductions of the memory layer.
+#include "common.cuh"
+
+namespace ml {
+
+// One warp per sub-key row: keys_n = x * rsqrt(sum(x*x) + 1e-6)
+// (memory.py:30-31,139).  Block 0 also writes the clamped temperature.
+__global__ void prep_keys_kernel(const float* __restrict__ keys, float* __restrict__ keys_n, int64_t rows,
+                                 int half, const float* __restrict__ log_t, float min_t, float max_t,
+                                 float* __restrict__ scal) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) scal[0] = clamped_temperature(log_t[0], min_t, max_t);
+  int lane = threadIdx.x & 31;
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* x = keys + row * half;
+  float ss = 0.f;
+  for (int i = lane; i < half; i += 32) ss = fmaf(x[i], x[i], ss);
+  ss = warp_sum(ss);
+  float r = 1.0f / sqrtf(ss + 1e-6f);
+  float* y = keys_n + row * half;
+  for (int i = lane; i < half; i += 32) y[i] = x[i] * r;
+}
+
+// One warp per (token, head, half): q_len (memory.py:137) and unit q (:138).
+__global__ void normalize_q_kernel(const float* __restrict__ q, float* __restrict__ qn, float* __restrict__ qlen,
+                                   int64_t rows, int half) {
+  int lane = threadIdx.x & 31;
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* x = q + row * half;
+  float ss = 0.f;
+  for (int i = lane; i < half; i += 32) ss = fmaf(x[i], x[i], ss);
+  ss = warp_sum(ss);
+  float t = ss + 1e-6f;
+  if (lane == 0) qlen[row] = sqrtf(t) / sqrtf((float)half);
+  float r = 1.0f / sqrtf(t);
+  float* y = qn + row * half;
+  for (int i = lane; i < half; i += 32) y[i] = x[i] * r;
+}
+
+cudaError_t launch_prep_keys(const Dims& D, const float* sub_keys, const float* log_t, float min_t, float max_t,
+                             float* keys_n, float* scal, cudaStream_t s) {
+  int64_t rows = (int64_t)D.H * 2 * D.n;
+  int wpb = 8;
+  prep_keys_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(sub_keys, keys_n, rows, D.half, log_t,
+                                                                            min_t, max_t, scal);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, float* qlen, cudaStream_t s) {
+  int64_t rows = D.M * D.H * 2;
+  if (rows == 0) return cudaSuccess;
+  int wpb = 8;
+  normalize_q_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(q, qn, qlen, rows, D.half);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// float32 SIMT GEMM: C[M,N] = A[M,K] @ B[K,N] + bias (+ silu), all row-major.
+// 64x64 tile, 16-deep k-slices, 256 threads, 4x4 outputs per thread.
+// ---------------------------------------------------------------------------
+constexpr int GB_M = 64, GB_N = 64, GB_K = 16;
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                       const float* __restrict__ bias, float* __restrict__ C,
+                                                       int64_t M, int N, int K, int silu) {
+  __shared__ float As[GB_K][GB_M + 4];
+  __shared__ float Bs[GB_K][GB_N + 4];
+  int tid = threadIdx.x;
+  int ty = tid / 16, tx = tid % 16;
+  int64_t m0 = (int64_t)blockIdx.y * GB_M;
+  int n0 = blockIdx.x * GB_N;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += GB_K) {
+    // A tile: 64 rows x 16 k (1024 elements, 4 per thread)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      int e = tid + r * 256;
+      int mi = e / GB_K, ki = e % GB_K;
+      int64_t gm = m0 + mi;
+      int gk = k0 + ki;
+      As[ki][mi] = (gm < M && gk < K) ? A[gm * K + gk] : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      int e = tid + r * 256;
+      int ki = e / GB_N, ni = e % GB_N;
+      int gk = k0 + ki, gn = n0 + ni;
+      Bs[ki][ni] = (gk < K && gn < N) ? B[(int64_t)gk * N + gn] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < GB_K; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int64_t gm = m0 + ty * 4 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int gn = n0 + tx * 4 + j;
+      if (gn >= N) continue;
+      float v = acc[i][j] + (bias ? bias[gn] : 0.f);
+      if (silu) v = v / (1.0f + expf(-v));
+      C[gm * N + gn] = v;
+    }
+  }
+}
+
+cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float* C, int64_t M, int N, int K,
+                        bool silu, cudaStream_t s) {
+  if (M == 0) return cudaSuccess;
+  dim3 grid((N + GB_N - 1) / GB_N, (unsigned)((M + GB_M - 1) / GB_M));
+  gemm_f32_kernel<<<grid, 256, 0, s>>>(A, B, bias, C, M, N, K, silu ? 1 : 0);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// aux finalisation: top1_weight = mean over (token, head) of the max weight
+// (memory.py:225), summed in a fixed order (deterministic), plus temperature.
+// ---------------------------------------------------------------------------
+__global__ void finalize_kernel(const float* __restrict__ top1_part, int64_t count, float* __restrict__ top1,
+                                const float* __restrict__ scal, float* __restrict__ temperature) {
+  __shared__ double red[32];
+  double acc = 0.0;
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) acc += (double)top1_part[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    if (top1) top1[0] = count > 0 ? (float)(t / (double)count) : __int_as_float(0x7fc00000);
+    if (temperature) temperature[0] = scal[0];
+  }
+}
+
+cudaError_t launch_finalize(const Dims& D, const Work& W, float* top1, float* temperature, cudaStream_t s) {
+  if (!top1 && !temperature) return cudaSuccess;
+  finalize_kernel<<<1, 1024, 0, s>>>(W.top1_part, D.M * D.H, top1, W.scal, temperature);
+  count_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace ml

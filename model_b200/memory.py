@@ -1,0 +1,239 @@
+"""Host-side mirror of the reference memory layer over the CUDA C ABI.
+
+``MemoryPool`` keeps the field names, defaults, parameter names, call
+signature, aux dictionary and assertion behaviour of the reference's Flax
+module (memory_pool_model/memory.py:64-227); ``MemoryLayer`` covers the
+router / gate / output projections around it (model.py:108-120).  Arrays are
+torch tensors on a CUDA device; every step runs in ``libmemlayer.so``.
+There is no CPU path: a tensor on another device raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+import math
+from typing import Any, Dict, Optional, Tuple
+
+import torch
+
+from . import _lib as L
+
+_DTYPES = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _cuda_f32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor (no CPU path)")
+    return t.to(torch.float32).contiguous()
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    # torch's caching allocator hands out 512-byte aligned blocks
+    return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+
+
+@dataclasses.dataclass
+class MemoryPool:
+    """A pool of ``n_sub_keys ** 2`` value vectors read through product keys.
+
+    Fields match memory.py:72-97.  ``apply(variables, queries, ...)`` takes
+    ``variables = {"params": {"sub_keys", "values", "log_temperature"}}``
+    (the reference's parameter names and shapes) and returns
+    ``(out [..., d_value], aux)``.
+    """
+
+    n_sub_keys: int
+    heads: int
+    d_key: int
+    d_value: int
+    top_k: int
+    routing_noise: float = 1.0
+    init_temperature: float = 10.0
+    min_temperature: float = 10.0
+    balance_temperature_grad: bool = False
+    max_temperature: float = 100.0
+    query_scale: bool = False
+    host_pool: str = ""
+
+    def __post_init__(self):
+        # memory.py:95-96
+        assert self.d_key % 2 == 0, "d_key must be even (split into two halves)"
+        assert self.top_k <= self.n_sub_keys
+        if self.host_pool:
+            raise NotImplementedError("host_pool tables are not served by the B200 memory layer")
+
+    @property
+    def pool_size(self) -> int:
+        return self.n_sub_keys ** 2
+
+    # -- parameters (memory.py:94-113) --
+    def init(self, seed: int = 0, device="cuda", values_dtype=torch.float32,
+             values_std: Optional[float] = None) -> Dict[str, Dict[str, torch.Tensor]]:
+        """Parameters with the reference's initialisers: unit-sphere sub_keys,
+        N(0, d_value^-0.5) values, log(init_temperature)."""
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        half = self.d_key // 2
+        sk = torch.randn(self.heads, 2, self.n_sub_keys, half, generator=g)
+        sk = sk * torch.rsqrt((sk * sk).sum(-1, keepdim=True) + 1e-6)
+        std = self.d_value ** -0.5 if values_std is None else values_std
+        values = (torch.randn(self.pool_size, self.d_value, generator=g) * std).to(values_dtype)
+        return {"params": {
+            "sub_keys": sk.to(device),
+            "values": values.to(device),
+            "log_temperature": torch.tensor(math.log(self.init_temperature), dtype=torch.float32, device=device),
+        }}
+
+    def config(self, tokens: int, values_dtype: torch.dtype, d_model: int = 0) -> L.MemlayerConfig:
+        if values_dtype not in _DTYPES:
+            raise TypeError(f"values dtype {values_dtype} is not float32/float16/bfloat16")
+        return L.MemlayerConfig(
+            tokens=tokens, heads=self.heads, n_sub_keys=self.n_sub_keys, d_key=self.d_key, d_value=self.d_value,
+            top_k=self.top_k, d_model=d_model, values_dtype=_DTYPES[values_dtype],
+            routing_noise=self.routing_noise, min_temperature=self.min_temperature,
+            max_temperature=self.max_temperature, query_scale=int(self.query_scale),
+            balance_temperature_grad=int(self.balance_temperature_grad))
+
+    def _noise(self, shape, train: bool, noise_scale: float, rngs, gumbel, device) -> Optional[torch.Tensor]:
+        if not (train and self.routing_noise > 0 and noise_scale != 0):
+            return None
+        if gumbel is None:
+            # the reference draws from the "routing" RNG stream (memory.py:156)
+            seed = 0 if rngs is None else int(rngs.get("routing", 0)) if isinstance(rngs, dict) else int(rngs)
+            gen = torch.Generator(device=device).manual_seed(seed)
+            u = torch.rand(shape, generator=gen, device=device).clamp_(min=torch.finfo(torch.float32).tiny)
+            gumbel = -torch.log(-torch.log(u))
+        return _cuda_f32(gumbel, "gumbel")
+
+    def _pool_args(self, params, M, device, *, train, noise_scale, shuffle_reads, rngs, gumbel, stats):
+        p = params["params"] if "params" in params else params
+        sub_keys = _cuda_f32(p["sub_keys"], "sub_keys")
+        values = p["values"]
+        if not values.is_cuda:
+            raise TypeError("values must be a CUDA tensor (no CPU path)")
+        values = values.contiguous()
+        log_t = _cuda_f32(torch.as_tensor(p["log_temperature"], device=device).reshape(1), "log_temperature")
+        H, k, n = self.heads, self.top_k, self.n_sub_keys
+        keep = dict(sub_keys=sub_keys, values=values, log_t=log_t)
+        keep["gumbel"] = self._noise((M, H, 2, n), train, noise_scale, rngs, gumbel, device)
+        keep["slots"] = torch.empty(M, H, k, dtype=torch.int32, device=device)
+        keep["weights"] = torch.empty(M, H, k, dtype=torch.float32, device=device)
+        keep["temperature"] = torch.empty(1, dtype=torch.float32, device=device)
+        keep["top1"] = torch.empty(1, dtype=torch.float32, device=device)
+        if stats:
+            keep["queries_unit"] = torch.empty(M, H, 2, self.d_key // 2, dtype=torch.float32, device=device)
+            keep["subkey_counts"] = torch.empty(H, 2, n, dtype=torch.float32, device=device)
+            keep["slot_counts"] = torch.empty(self.pool_size, dtype=torch.float32, device=device)
+            keep["balance_loss"] = torch.empty(1, dtype=torch.float32, device=device)
+        a = L.MemlayerPoolArgs(
+            sub_keys=_ptr(sub_keys), log_temperature=_ptr(log_t), values=_ptr(values),
+            gumbel=_ptr(keep["gumbel"]), noise_scale=float(noise_scale), train=int(bool(train)),
+            shuffle_reads=int(bool(shuffle_reads)), slots=_ptr(keep["slots"]), weights=_ptr(keep["weights"]),
+            queries_unit=_ptr(keep.get("queries_unit")), subkey_counts=_ptr(keep.get("subkey_counts")),
+            slot_counts=_ptr(keep.get("slot_counts")), balance_loss=_ptr(keep.get("balance_loss")),
+            top1_weight=_ptr(keep["top1"]), temperature=_ptr(keep["temperature"]))
+        return a, keep
+
+    def _aux(self, keep, lead, stats) -> Dict[str, Any]:
+        H, k = self.heads, self.top_k
+        aux = {
+            "slots": keep["slots"].reshape(*lead, H, k),
+            "weights": keep["weights"].reshape(*lead, H, k),
+            "temperature": keep["temperature"].reshape(()),
+            "top1_weight": keep["top1"].reshape(()),
+        }
+        if stats:
+            aux.update(balance_loss=keep["balance_loss"].reshape(()), subkey_counts=keep["subkey_counts"],
+                       slot_counts=keep["slot_counts"], queries=keep["queries_unit"])
+        return aux
+
+    def apply(self, variables, queries: torch.Tensor, *, train: bool = False, sparse_grad: bool = False,
+              noise_scale: float = 1.0, shuffle_reads: bool = False, rngs=None,
+              gumbel: Optional[torch.Tensor] = None, stats: bool = True,
+              stream: Optional[torch.cuda.Stream] = None) -> Tuple[torch.Tensor, Dict[str, Any]]:
+        """MemoryPool.__call__ (memory.py:119-227).  ``gumbel`` optionally
+        supplies the standard Gumbel sample used when ``train`` (else one is
+        drawn from ``rngs["routing"]``); ``stats=False`` skips the routing
+        statistics that only training consumes."""
+        del sparse_grad  # affects differentiation only
+        queries = _cuda_f32(queries, "queries")
+        lead = tuple(queries.shape[:-2])
+        if tuple(queries.shape[-2:]) != (self.heads, self.d_key):
+            raise ValueError(f"queries must end in [heads={self.heads}, d_key={self.d_key}]")
+        M = int(math.prod(lead)) if lead else 1
+        device = queries.device
+        p = variables["params"] if "params" in variables else variables
+        cfg = self.config(M, p["values"].dtype)
+        a, keep = self._pool_args(variables, M, device, train=train, noise_scale=noise_scale,
+                                  shuffle_reads=shuffle_reads, rngs=rngs, gumbel=gumbel, stats=stats)
+        out = torch.empty(*lead, self.d_value, dtype=torch.float32, device=device)
+        a.queries = queries.data_ptr()
+        a.out = out.data_ptr()
+        nbytes = C.c_size_t()
+        L.check(L.lib().memlayer_pool_workspace_size(C.byref(cfg), C.byref(nbytes)), "memlayer_pool_workspace_size")
+        ws = _workspace(nbytes.value, device)
+        s = (stream or torch.cuda.current_stream(device)).cuda_stream
+        L.check(L.lib().memlayer_pool_forward(C.byref(cfg), C.byref(a), ws.data_ptr(), nbytes.value, s),
+                "memlayer_pool_forward")
+        return out, self._aux(keep, lead, stats)
+
+
+@dataclasses.dataclass
+class MemoryLayer:
+    """The memory-layer block of MemoryPoolLM (model.py:108-120) for one
+    layer index i: router_i Dense -> MemoryPool -> silu(mem_gate_i Dense)
+    gate -> mem_out_i Dense.  Parameter names follow the reference's Flax
+    tree: ``router_i``, ``mem_gate_i``, ``mem_out_i`` with ``kernel`` /
+    ``bias`` leaves, and ``pool`` with the MemoryPool parameters."""
+
+    pool: MemoryPool
+    d_model: int
+    layer: int = 1
+
+    def init(self, seed: int = 0, device="cuda", values_dtype=torch.float32) -> Dict[str, Any]:
+        g = torch.Generator(device="cpu").manual_seed(seed + 1)
+        P = self.pool
+
+        def dense(fan_in, fan_out):  # flax Dense default: lecun_normal kernel, zero bias
+            return {"kernel": (torch.randn(fan_in, fan_out, generator=g) / math.sqrt(fan_in)).to(device),
+                    "bias": torch.zeros(fan_out, device=device)}
+        return {
+            f"router_{self.layer}": dense(self.d_model, P.heads * P.d_key),
+            f"mem_gate_{self.layer}": dense(self.d_model, P.d_value),
+            f"mem_out_{self.layer}": dense(P.d_value, self.d_model),
+            "pool": P.init(seed, device, values_dtype)["params"],
+        }
+
+    def apply(self, params, h: torch.Tensor, *, train: bool = False, noise_scale: float = 1.0,
+              shuffle_reads: bool = False, rngs=None, gumbel=None, stats: bool = False,
+              stream: Optional[torch.cuda.Stream] = None):
+        """Returns (y [..., d_model], mem [..., d_value], aux); y is the term
+        model.py:119 adds into the layer's update."""
+        P = self.pool
+        h = _cuda_f32(h, "h")
+        lead = tuple(h.shape[:-1])
+        M = int(math.prod(lead)) if lead else 1
+        device = h.device
+        r, g_, o = (params[f"{n}_{self.layer}"] for n in ("router", "mem_gate", "mem_out"))
+        cfg = P.config(M, params["pool"]["values"].dtype, self.d_model)
+        a, keep = P._pool_args(params["pool"], M, device, train=train, noise_scale=noise_scale,
+                               shuffle_reads=shuffle_reads, rngs=rngs, gumbel=gumbel, stats=stats)
+        w = {k: _cuda_f32(v, k) for k, v in (("wr", r["kernel"]), ("br", r["bias"]), ("wg", g_["kernel"]),
+                                             ("bg", g_["bias"]), ("wo", o["kernel"]), ("bo", o["bias"]))}
+        y = torch.empty(*lead, self.d_model, dtype=torch.float32, device=device)
+        mem = torch.empty(*lead, P.d_value, dtype=torch.float32, device=device)
+        la = L.MemlayerLayerArgs(h=h.data_ptr(), w_router=_ptr(w["wr"]), b_router=_ptr(w["br"]),
+                                 w_gate=_ptr(w["wg"]), b_gate=_ptr(w["bg"]), w_out=_ptr(w["wo"]),
+                                 b_out=_ptr(w["bo"]), y=y.data_ptr(), mem=mem.data_ptr(), pool=a)
+        nbytes = C.c_size_t()
+        L.check(L.lib().memlayer_layer_workspace_size(C.byref(cfg), C.byref(nbytes)),
+                "memlayer_layer_workspace_size")
+        ws = _workspace(nbytes.value, device)
+        s = (stream or torch.cuda.current_stream(device)).cuda_stream
+        L.check(L.lib().memlayer_layer_forward(C.byref(cfg), C.byref(la), ws.data_ptr(), nbytes.value, s),
+                "memlayer_layer_forward")
+        return y, mem, P._aux(keep, lead, stats)

@@ -57,16 +57,19 @@ def top_k(x: np.ndarray, k: int) -> Tuple[np.ndarray, np.ndarray]:
     if k == n:
         sel = np.broadcast_to(np.arange(n), flat.shape)
     else:
-        # k-th largest value per row, then: every element > thr, plus the
-        # lowest-index elements == thr until k are taken.
-        thr = -np.partition(-flat, k - 1, axis=-1)[:, k - 1:k]
-        gt = flat > thr
-        eq = flat == thr
-        need = k - gt.sum(-1, keepdims=True)
-        take_eq = eq & (np.cumsum(eq, axis=-1) <= need)
-        chosen = gt | take_eq
-        # indices of the chosen elements in ascending index order
-        sel = np.argsort(~chosen, axis=-1, kind="stable")[:, :k]
+        # any k elements holding the k largest values ...
+        sel = np.argpartition(-flat, k - 1, axis=-1)[:, :k]
+        thr = np.take_along_axis(flat, sel, axis=-1).min(-1, keepdims=True)
+        # ... which is the lax.top_k set unless the k-th value is tied with
+        # an element left out; those rows take the lowest-index tied elements
+        amb = np.flatnonzero((flat == thr).sum(-1) > (np.take_along_axis(flat, sel, -1) == thr).sum(-1))
+        if amb.size:
+            f, t = flat[amb], thr[amb]
+            gt, eq = f > t, f == t
+            take = gt | (eq & (np.cumsum(eq, axis=-1) <= k - gt.sum(-1, keepdims=True)))
+            sel = sel.copy()
+            sel[amb] = np.nonzero(take)[1].reshape(amb.size, k)
+        sel = np.sort(sel, axis=-1)
     vals = np.take_along_axis(flat, sel, axis=-1)
     # stable sort on the negated values keeps ascending index among ties
     order = np.argsort(-vals, axis=-1, kind="stable")

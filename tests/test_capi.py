@@ -1,0 +1,114 @@
+"""The C ABI library: loads, exports every declared symbol, and rejects bad
+arguments on the host (these calls return before touching a GPU)."""
+
+import ctypes as C
+import glob
+import os
+import re
+
+import pytest
+
+from model_b200 import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(\w+)\s*\(", text, flags=re.M)
+    return sorted(set(n for n in names if n.startswith(("memlayer_", "mlshard_"))))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    names = declared_functions()
+    assert "memlayer_pool_forward" in names and "memlayer_layer_forward" in names
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/ but not exported"
+    assert lib.memlayer_abi_version() == 1
+
+
+def test_struct_sizes_match_header_layout():
+    # int64 + 12 * 4-byte fields
+    assert C.sizeof(L.MemlayerConfig) == 8 + 12 * 4
+    assert C.sizeof(L.MemlayerPoolArgs) == 5 * 8 + 4 * 3 + 4 + 10 * 8  # 4 bytes of padding before `out`
+    assert C.sizeof(L.MemlayerLayerArgs) == 9 * 8 + C.sizeof(L.MemlayerPoolArgs)
+
+
+def cfg(**kw):
+    base = dict(tokens=8192, heads=4, n_sub_keys=512, d_key=256, d_value=256, top_k=16, d_model=256,
+                values_dtype=L.F32, routing_noise=1.0, min_temperature=10.0, max_temperature=100.0,
+                query_scale=0, balance_temperature_grad=0)
+    base.update(kw)
+    return L.MemlayerConfig(**base)
+
+
+def ws_size(c, layer=False):
+    n = C.c_size_t()
+    f = L.lib().memlayer_layer_workspace_size if layer else L.lib().memlayer_pool_workspace_size
+    return f(C.byref(c), C.byref(n)), n.value
+
+
+def test_workspace_size_scales_with_tokens():
+    st, a = ws_size(cfg(tokens=1024))
+    st2, b = ws_size(cfg(tokens=2048))
+    assert st == st2 == L.OK and 0 < a < b
+    st, c = ws_size(cfg(tokens=1024), layer=True)
+    assert st == L.OK and c > a
+
+
+@pytest.mark.parametrize("bad,status", [
+    (dict(d_key=7), L.ERR_BAD_SHAPE),                  # memory.py:95 d_key must be even
+    (dict(top_k=513), L.ERR_BAD_SHAPE),                # memory.py:96 top_k <= n_sub_keys
+    (dict(heads=0), L.ERR_BAD_SHAPE),
+    (dict(tokens=-1), L.ERR_BAD_SHAPE),
+    (dict(n_sub_keys=50000), L.ERR_BAD_SHAPE),         # n*n must fit int32 slot ids
+    (dict(top_k=33, n_sub_keys=64), L.ERR_UNSUPPORTED),
+    (dict(values_dtype=7), L.ERR_UNSUPPORTED),
+    (dict(values_dtype=L.F16, d_value=12), L.ERR_UNSUPPORTED),
+    (dict(min_temperature=0.0), L.ERR_BAD_SHAPE),
+])
+def test_bad_configs_are_rejected_on_the_host(bad, status):
+    st, _ = ws_size(cfg(**bad))
+    assert st == status
+    a = L.MemlayerPoolArgs()
+    assert L.lib().memlayer_pool_forward(C.byref(cfg(**bad)), C.byref(a), None, 0, None) == status
+
+
+def test_missing_pointers_and_workspace_are_rejected():
+    c = cfg(tokens=16)
+    a = L.MemlayerPoolArgs()  # all NULL
+    assert L.lib().memlayer_pool_forward(C.byref(c), C.byref(a), None, 0, None) == L.ERR_BAD_POINTER
+    # every pointer set (never dereferenced: the workspace check fails first)
+    fake = 1 << 20
+    a = L.MemlayerPoolArgs(queries=fake, sub_keys=fake, log_temperature=fake, values=fake, out=fake,
+                           slots=fake, weights=fake)
+    assert L.lib().memlayer_pool_forward(C.byref(c), C.byref(a), None, 0, None) == L.ERR_WORKSPACE
+    _, need = ws_size(c)
+    assert L.lib().memlayer_pool_forward(C.byref(c), C.byref(a), fake, 1024, None) == L.ERR_WORKSPACE
+    assert L.lib().memlayer_pool_forward(C.byref(c), C.byref(a), fake + 8, need, None) == L.ERR_WORKSPACE
+    # training with selection noise but no Gumbel sample
+    a.train = 1
+    a.noise_scale = 1.0
+    assert L.lib().memlayer_pool_forward(C.byref(c), C.byref(a), fake, need, None) == L.ERR_BAD_POINTER
+
+
+def test_status_strings():
+    for s in range(7):
+        assert L.status_string(s)
+    assert "unknown" in L.status_string(99)
+
+
+def test_pool_mirror_keeps_reference_assertions():
+    from model_b200 import MemoryPool
+    with pytest.raises(AssertionError):
+        MemoryPool(n_sub_keys=16, heads=2, d_key=7, d_value=12, top_k=4)
+    with pytest.raises(AssertionError):
+        MemoryPool(n_sub_keys=4, heads=2, d_key=8, d_value=12, top_k=5)
+    pool = MemoryPool(n_sub_keys=16, heads=2, d_key=8, d_value=12, top_k=4)
+    import torch
+    with pytest.raises(TypeError):
+        pool.apply({"params": {}}, torch.zeros(3, 2, 8))  # CPU tensor: no CPU path

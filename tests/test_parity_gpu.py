@@ -1,0 +1,144 @@
+"""GPU parity: the CUDA memory layer (through the C ABI) against the golden
+fixtures of the reference's memory.py and against the CPU oracle.
+
+Tolerances: slot ids bit-exact except inside near-tie groups (relative gap
+<= 1e-6, see parity.check_slots); weights and float32-value outputs within
+1e-5 relative; float16/bfloat16-value outputs within 2e-2 relative.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from cases import case_inputs, pool_config, run_oracle
+from conftest import golden_names, load_golden
+from oracle import memlayer_ref as ref
+from parity import OUT_RTOL_F32, OUT_RTOL_HALF, assert_rel, check_slots
+
+pytestmark = pytest.mark.gpu
+
+DT = {None: torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+def _dev(x, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).to("cuda", dtype)
+
+
+def run_gpu(recipe, stats=True):
+    from model_b200 import MemoryLayer, MemoryPool
+    cfg = pool_config(recipe)
+    x = case_inputs(recipe)
+    pool = MemoryPool(**{f.name: getattr(cfg, f.name) for f in cfg.__dataclass_fields__.values()})
+    vdt = DT[recipe.get("values_dtype")]
+    params = {"sub_keys": _dev(x["sub_keys"]), "values": _dev(x["values"], vdt),
+              "log_temperature": torch.tensor(float(x["log_t"]), device="cuda")}
+    kw = dict(train=recipe.get("train", False), noise_scale=recipe.get("noise_scale", 1.0),
+              shuffle_reads=recipe.get("shuffle_reads", False), stats=stats)
+    if "gumbel" in x:
+        kw["gumbel"] = _dev(x["gumbel"])
+    if recipe.get("layer"):
+        layer = MemoryLayer(pool, d_model=recipe["d_model"], layer=1)
+        lp = {"router_1": {"kernel": _dev(x["w_router"]), "bias": _dev(x["b_router"])},
+              "mem_gate_1": {"kernel": _dev(x["w_gate"]), "bias": _dev(x["b_gate"])},
+              "mem_out_1": {"kernel": _dev(x["w_out"]), "bias": _dev(x["b_out"])},
+              "pool": params}
+        y, mem, aux = layer.apply(lp, _dev(x["h"]), **kw)
+        res = {"y": y, "out": mem}
+    else:
+        out, aux = pool.apply({"params": params}, _dev(x["queries"]), **kw)
+        res = {"out": out}
+    torch.cuda.synchronize()
+    res.update(aux)
+    return {k: (v.cpu().numpy() if isinstance(v, torch.Tensor) else v) for k, v in res.items()}
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_gpu_matches_golden(name):
+    recipe, exp = load_golden(name)
+    got = run_gpu(recipe)
+    orc = run_oracle(recipe)
+    n = recipe["n_sub_keys"]
+    swapped = check_slots(got["slots"], exp["slots"], orc["route"]["scores"], n)
+    tol = OUT_RTOL_HALF if recipe.get("values_dtype") else OUT_RTOL_F32
+    # weights are the softmax of the oracle scores at the slots the GPU chose
+    from parity import slot_scores
+    M, H, k = exp["slots"].shape
+    w_ref = ref.softmax(slot_scores(orc["route"]["scores"], got["slots"].reshape(M, H, k).astype(np.int64), n))
+    assert_rel(got["weights"].reshape(M, H, k), w_ref, OUT_RTOL_F32, "weights")
+    x = case_inputs(recipe)
+    if swapped == 0:
+        np.testing.assert_array_equal(got["slots"].astype(np.int64), exp["slots"])
+        assert_rel(got["weights"], exp["weights"], OUT_RTOL_F32, "weights vs golden")
+        assert_rel(got["out"], exp["out"], tol, "out vs golden")
+        if "y" in exp:
+            assert_rel(got["y"], exp["y"], OUT_RTOL_F32, "y vs golden")
+        np.testing.assert_array_equal(got["subkey_counts"], exp["subkey_counts"])
+        if "slot_counts" in exp:
+            np.testing.assert_array_equal(got["slot_counts"], exp["slot_counts"])
+    # output of the chosen slots, mixed by the oracle
+    mix = ref.gather_mix(x["values"], got["slots"].reshape(M, H, k).astype(np.int64), got["weights"].reshape(M, H, k),
+                         recipe.get("shuffle_reads", False))
+    assert_rel(got["out"].reshape(M, -1), mix, tol, "out vs oracle mix of chosen slots")
+    assert abs(float(got["balance_loss"]) - float(exp["balance_loss"])) <= 1e-5 * abs(float(exp["balance_loss"])) + 1e-6
+    assert abs(float(got["temperature"]) - float(exp["temperature"])) <= 1e-6 * float(exp["temperature"])
+    assert abs(float(got["top1_weight"]) - float(exp["top1_weight"])) <= 1e-5
+    if "queries_aux" in exp:
+        assert_rel(got["queries"], exp["queries_aux"], 1e-6, "queries")
+
+
+def test_gpu_noise_anneal_and_eval_are_clean():
+    """test_memory_pool.py:66-76 on the CUDA path."""
+    r = dict(n_sub_keys=16, heads=2, d_key=8, d_value=12, top_k=4, M=15, seed=21, noise=5.0)
+    clean = run_gpu(r)
+    noisy = run_gpu(dict(r, train=True))
+    off = run_gpu(dict(r, train=True, noise_scale=0.0))
+    assert not np.array_equal(clean["slots"], noisy["slots"])
+    np.testing.assert_array_equal(clean["slots"], off["slots"])
+
+
+def test_gpu_empty_input():
+    from model_b200 import MemoryPool
+    pool = MemoryPool(n_sub_keys=16, heads=2, d_key=8, d_value=12, top_k=4)
+    params = pool.init(0)
+    out, aux = pool.apply(params, torch.zeros(0, 2, 8, device="cuda"))
+    torch.cuda.synchronize()
+    assert out.shape == (0, 12) and aux["slots"].shape == (0, 2, 4)
+    assert float(aux["slot_counts"].sum()) == 0.0
+
+
+def test_gpu_leading_dims_and_query_scale_keeps_picks():
+    """test_memory_pool.py:118-125 with [3, 5, H, d_key] queries."""
+    from model_b200 import MemoryPool
+    pool = MemoryPool(n_sub_keys=16, heads=2, d_key=8, d_value=12, top_k=4, query_scale=True)
+    params = pool.init(1)
+    q = torch.randn(3, 5, 2, 8, device="cuda", generator=torch.Generator("cuda").manual_seed(0))
+    out_a, a = pool.apply(params, q)
+    out_b, b = pool.apply(params, q * 10.0)
+    assert out_a.shape == (3, 5, 12) and a["slots"].shape == (3, 5, 2, 4)
+    assert torch.equal(a["slots"], b["slots"])
+    assert float(b["top1_weight"]) > float(a["top1_weight"])
+
+
+@pytest.mark.parametrize("values_dtype", ["f32", "bf16"])
+def test_gpu_full_config0_against_oracle(values_dtype):
+    """configs[0] at full size (T=8192, n=512, H=4, k=16, d=256): routing and
+    outputs against the oracle on the same seeded inputs."""
+    recipe = dict(n_sub_keys=512, heads=4, d_key=256, d_value=256, top_k=16, M=8192, seed=0, layer=True,
+                  d_model=256, key_std=float(np.sqrt(1 / 128)))
+    if values_dtype == "bf16":
+        recipe["values_dtype"] = "bf16"
+    got = run_gpu(recipe, stats=True)
+    orc = run_oracle(recipe)
+    M, H, k = orc["slots"].shape
+    swapped = check_slots(got["slots"], orc["slots"], orc["route"]["scores"], 512)
+    assert swapped <= M * H // 1000, swapped
+    x = case_inputs(recipe)
+    mix = ref.gather_mix(x["values"], got["slots"].astype(np.int64), got["weights"])
+    tol = OUT_RTOL_HALF if values_dtype == "bf16" else OUT_RTOL_F32
+    assert_rel(got["out"], mix, tol, "out")
+    if swapped == 0:
+        assert_rel(got["y"], orc["y"], OUT_RTOL_F32, "y")
+        np.testing.assert_array_equal(got["subkey_counts"], orc["aux"]["subkey_counts"])
+    np.testing.assert_allclose(got["weights"].sum(-1), 1.0, rtol=1e-5)
+    assert got["slot_counts"].sum() == M * H * k
+    assert abs(float(got["balance_loss"]) - float(orc["aux"]["balance_loss"])) <= 1e-5 * float(orc["aux"]["balance_loss"])
