@@ -67,8 +67,15 @@ size_t layout(const Dims& D, const Flags& f, char* ws, Work* W) {
   const int64_t tiles = (D.M + SCORE_TM - 1) / SCORE_TM;
   Work w;
   w.scal = (float*)take(4 * sizeof(float));
+  w.err = (int*)take(sizeof(int));
   w.keys_n = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
   w.qn = (float*)take(sizeof(float) * rows * D.half);
+  if (score_tc_supported(D)) {
+    w.k_hi = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
+    w.k_lo = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
+    w.q_hi = (float*)take(sizeof(float) * rows * D.half);
+    w.q_lo = (float*)take(sizeof(float) * rows * D.half);
+  }
   w.qlen = (float*)take(sizeof(float) * rows);
   w.sub_idx = (int*)take(sizeof(int) * rows * D.k);
   w.sub_score = (float*)take(sizeof(float) * rows * D.k);
@@ -127,14 +134,17 @@ cudaError_t mark(const memlayer_pool_args* a, int i, cudaStream_t s) {
 int run_pool(const Dims& D, const memlayer_config* c, const memlayer_pool_args* a, const Work& W, const float* q,
              int* slots, float* weights, float* out, float* memg, const float* gate, cudaStream_t s) {
   ML_TRY(launch_prep_keys(D, a->sub_keys, a->log_temperature, c->min_temperature, c->max_temperature, W.keys_n,
-                          W.scal, s));
+                          W.k_hi, W.k_lo, W.scal, W.err, s));
   float* qn = a->queries_unit ? a->queries_unit : W.qn;
-  ML_TRY(launch_normalize_queries(D, q, qn, W.qlen, s));
+  ML_TRY(launch_normalize_queries(D, q, qn, W.qlen, W.q_hi, W.q_lo, s));
   ML_TRY(mark(a, 2, s));
   Work w2 = W;
   w2.qn = qn;
   const bool bal = a->balance_loss != nullptr;
-  ML_TRY(launch_score_topk(D, w2, a->gumbel, bal, s));
+  if (W.q_hi)
+    ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, bal, s));
+  else
+    ML_TRY(launch_score_topk(D, w2, a->gumbel, bal, s));
   if (bal) ML_TRY(launch_balance(D, w2, a->balance_loss, s));
   if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
   if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));

@@ -35,6 +35,11 @@ struct Dims {
 // Device pointers carved out of the caller's workspace.
 struct Work {
   float* keys_n = nullptr;     // [H,2,n,half] unit sub-keys
+  float* k_hi = nullptr;       // [H*2,n,half] rna_tf32(keys_n)          (tensor-core path)
+  float* k_lo = nullptr;       // [H*2,n,half] rna_tf32(keys_n - k_hi)
+  float* q_hi = nullptr;       // [H*2,M,half] rna_tf32(qn), codebook-major
+  float* q_lo = nullptr;       // [H*2,M,half] rna_tf32(qn - q_hi)
+  int* err = nullptr;          // [1] device error code (bounded waits)
   float* qn = nullptr;         // [M,H,2,half] unit query halves
   float* qlen = nullptr;       // [M,H,2] |q_half| / sqrt(half)
   int* sub_idx = nullptr;      // [M,H,2,k] stage-1 sub-key ids (selection order)
@@ -170,8 +175,12 @@ void count_launch(int n = 1);
 
 // ---- host-side launchers (one per kernel family) ----
 cudaError_t launch_prep_keys(const Dims& D, const float* sub_keys, const float* log_t, float min_t, float max_t,
-                             float* keys_n, float* scal, cudaStream_t s);
-cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, float* qlen, cudaStream_t s);
+                             float* keys_n, float* k_hi, float* k_lo, float* scal, int* err, cudaStream_t s);
+cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, float* qlen, float* q_hi,
+                                     float* q_lo, cudaStream_t s);
+bool score_tc_supported(const Dims& D);
+cudaError_t launch_score_topk_tc(const Dims& D, const Work& W, const float* gumbel, bool want_balance,
+                                 cudaStream_t s);
 cudaError_t launch_score_topk(const Dims& D, const Work& W, const float* gumbel, bool want_balance,
                               cudaStream_t s);
 cudaError_t launch_balance(const Dims& D, const Work& W, float* balance_loss, cudaStream_t s);

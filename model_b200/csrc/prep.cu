@@ -1,15 +1,19 @@
 // Normalisation, temperature, float32 GEMM (router / gate / output
 // projections) and the final aux reductions of the memory layer.
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace ml {
 
 // One warp per sub-key row: keys_n = x * rsqrt(sum(x*x) + 1e-6)
 // (memory.py:30-31,139).  Block 0 also writes the clamped temperature.
-__global__ void prep_keys_kernel(const float* __restrict__ keys, float* __restrict__ keys_n, int64_t rows,
-                                 int half, const float* __restrict__ log_t, float min_t, float max_t,
-                                 float* __restrict__ scal) {
-  if (blockIdx.x == 0 && threadIdx.x == 0) scal[0] = clamped_temperature(log_t[0], min_t, max_t);
+__global__ void prep_keys_kernel(const float* __restrict__ keys, float* __restrict__ keys_n,
+                                 float* __restrict__ k_hi, float* __restrict__ k_lo, int64_t rows, int half,
+                                 const float* __restrict__ log_t, float min_t, float max_t,
+                                 float* __restrict__ scal, int* __restrict__ err) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    scal[0] = clamped_temperature(log_t[0], min_t, max_t);
+    *err = 0;  // device error code of this call's bounded waits
+  }
   int lane = threadIdx.x & 31;
   int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -19,12 +23,21 @@ __global__ void prep_keys_kernel(const float* __restrict__ keys, float* __restri
   ss = warp_sum(ss);
   float r = 1.0f / sqrtf(ss + 1e-6f);
   float* y = keys_n + row * half;
-  for (int i = lane; i < half; i += 32) y[i] = x[i] * r;
+  for (int i = lane; i < half; i += 32) {
+    const float v = x[i] * r;
+    y[i] = v;
+    if (k_hi) {
+      const float hi = tc::to_tf32(v);
+      k_hi[row * half + i] = hi;
+      k_lo[row * half + i] = tc::to_tf32(v - hi);
+    }
+  }
 }
 
 // One warp per (token, head, half): q_len (memory.py:137) and unit q (:138).
 __global__ void normalize_q_kernel(const float* __restrict__ q, float* __restrict__ qn, float* __restrict__ qlen,
-                                   int64_t rows, int half) {
+                                   float* __restrict__ q_hi, float* __restrict__ q_lo, int64_t rows, int half,
+                                   int hc_count, int64_t M) {
   int lane = threadIdx.x & 31;
   int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -36,24 +49,36 @@ __global__ void normalize_q_kernel(const float* __restrict__ q, float* __restric
   if (lane == 0) qlen[row] = sqrtf(t) / sqrtf((float)half);
   float r = 1.0f / sqrtf(t);
   float* y = qn + row * half;
-  for (int i = lane; i < half; i += 32) y[i] = x[i] * r;
+  // codebook-major copy for the tensor-core path: [hc][m][half]
+  const int64_t tr = (row % hc_count) * M + row / hc_count;
+  for (int i = lane; i < half; i += 32) {
+    const float v = x[i] * r;
+    y[i] = v;
+    if (q_hi) {
+      const float hi = tc::to_tf32(v);
+      q_hi[tr * half + i] = hi;
+      q_lo[tr * half + i] = tc::to_tf32(v - hi);
+    }
+  }
 }
 
 cudaError_t launch_prep_keys(const Dims& D, const float* sub_keys, const float* log_t, float min_t, float max_t,
-                             float* keys_n, float* scal, cudaStream_t s) {
+                             float* keys_n, float* k_hi, float* k_lo, float* scal, int* err, cudaStream_t s) {
   int64_t rows = (int64_t)D.H * 2 * D.n;
   int wpb = 8;
-  prep_keys_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(sub_keys, keys_n, rows, D.half, log_t,
-                                                                            min_t, max_t, scal);
+  prep_keys_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(sub_keys, keys_n, k_hi, k_lo, rows,
+                                                                            D.half, log_t, min_t, max_t, scal, err);
   count_launch();
   return cudaGetLastError();
 }
 
-cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, float* qlen, cudaStream_t s) {
+cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, float* qlen, float* q_hi,
+                                     float* q_lo, cudaStream_t s) {
   int64_t rows = D.M * D.H * 2;
   if (rows == 0) return cudaSuccess;
   int wpb = 8;
-  normalize_q_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(q, qn, qlen, rows, D.half);
+  normalize_q_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(q, qn, qlen, q_hi, q_lo, rows, D.half,
+                                                                              D.H * 2, D.M);
   count_launch();
   return cudaGetLastError();
 }

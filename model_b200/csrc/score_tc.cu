@@ -1,0 +1,379 @@
+// Stage 1 of the product-key search on the 5th-generation tensor cores
+// (memory.py:149-164): cos = q_hat . k_hat for every (token, head, half,
+// sub-key), scaled by the temperature (and |q| under query_scale), with the
+// per-(token, head, half) top-k taken in the TMEM epilogue, so the
+// [M, H, 2, n] score tensor never reaches global memory.
+//
+// Precision: routing must reproduce float32 slot selection, which a single
+// tf32 product (10-bit mantissa) does not.  Each operand is split into
+// x = hi + lo with hi = rna_tf32(x), lo = rna_tf32(x - hi) (|x - hi - lo| <=
+// 2^-22 |x|), and the score is accumulated in float32 TMEM as
+// hi.hi + hi.lo + lo.hi (three kind::tf32 MMAs per K step), which keeps the
+// cosine within a few float32 ulps of a float32 dot product.
+//
+// CTA = 6 warps, persistent over work units (128-token tile, head, half):
+//   warp 0     TMA producer: A = q_hi / q_lo [128 x 32] and B = k_hi / k_lo
+//              [BN x 32] tiles (128-byte swizzle) into a multi-stage ring;
+//   warp 1     TMEM allocator and MMA issuer (one thread): 128 x BN float32
+//              accumulators, double-buffered in TMEM (2 x 256 columns);
+//   warps 2-5  epilogue: thread t owns token row t of the tile (its TMEM
+//              lane), scans BN scores per chunk with tcgen05.ld and keeps a
+//              sorted register top-k (value desc, index asc).
+// Every mbarrier wait is bounded; a timeout sets an error code and unwinds.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tc_common.cuh"
+
+namespace ml {
+
+namespace {
+
+constexpr int TC_M = 128;          // tokens per tile (UMMA M)
+constexpr int TC_K = 32;           // float32 elements per 128-byte swizzled row
+constexpr int TC_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_STRIDE = 256;    // TMEM columns per accumulator buffer
+
+struct TcShape {
+  int BN;        // keys per MMA / chunk
+  int stages;    // smem ring depth
+  int kchunks;   // half / 32
+  int m_tiles;
+  int n_chunks;
+  uint32_t a_bytes, b_bytes, stage_bytes;
+};
+
+struct Ctl {
+  uint64_t full[8], empty[8], tfull[2], tempty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int KM, bool NOISY, bool BAL>
+struct Epi {
+  float v[KM], sc[KM], cv[NOISY && BAL ? KM : 1];
+  int ix[KM], cix[NOISY && BAL ? KM : 1];
+  float rmax, rsum;
+
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int j = 0; j < KM; ++j) {
+      v[j] = -INFINITY;
+      sc[j] = -INFINITY;
+      ix[j] = 0;
+    }
+    if constexpr (NOISY && BAL) {
+#pragma unroll
+      for (int j = 0; j < KM; ++j) {
+        cv[j] = -INFINITY;
+        cix[j] = 0;
+      }
+    }
+    rmax = -INFINITY;
+    rsum = 0.f;
+  }
+
+  __device__ __forceinline__ void push(const Dims& D, float cosv, int key, float T, float ql, float g) {
+    float score = __fmul_rn(cosv, T);                     // memory.py:150
+    if (D.qscale) score = __fmul_rn(score, ql);           // memory.py:151-152
+    float sel = score;
+    if constexpr (NOISY) sel = __fadd_rn(score, __fmul_rn(D.noise_coef, g));  // memory.py:158
+    if (sel > v[KM - 1]) list_insert3<KM>(v, ix, sc, sel, key, score);
+    if constexpr (NOISY && BAL) {
+      if (score > cv[KM - 1]) list_insert<KM>(cv, cix, score, key);
+    }
+    if constexpr (BAL) {
+      const float p = D.btgrad ? score : __fmul_rn(cosv, T);  // memory.py:211
+      if (p > rmax) {
+        rsum = rsum * expf(rmax - p) + 1.f;
+        rmax = p;
+      } else {
+        rsum += expf(p - rmax);
+      }
+    }
+  }
+};
+
+template <int KM, bool NOISY, bool BAL>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    score_topk_tc_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
+                         const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
+                         Dims D, TcShape S, const float* __restrict__ qlen, const float* __restrict__ gumbel,
+                         const float* __restrict__ scal, int* __restrict__ sub_idx, float* __restrict__ sub_score,
+                         float* __restrict__ sub_sel, int* __restrict__ clean_idx, float* __restrict__ row_max,
+                         float* __restrict__ row_sum, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Ctl* ctl = reinterpret_cast<Ctl*>(smem);
+  uint8_t* tiles = smem + 1024;
+  volatile int* abort = &ctl->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = S.m_tiles * D.H * 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S.stages; ++s) {
+      tc::mbar_init(&ctl->full[s], 1);
+      tc::mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&ctl->tfull[b], 1);
+      tc::mbar_init(&ctl->tempty[b], 4);
+    }
+    ctl->abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tc::prefetch_tmap(&tA_hi);
+      tc::prefetch_tmap(&tA_lo);
+      tc::prefetch_tmap(&tB_hi);
+      tc::prefetch_tmap(&tB_lo);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        const int hc = u / S.m_tiles, mt = u - hc * S.m_tiles;
+        const int arow = (int)(hc * D.M + (int64_t)mt * TC_M);
+        for (int j = 0; ok && j < S.n_chunks; ++j) {
+          const int brow = hc * D.n + j * S.BN;
+          for (int kc = 0; kc < S.kchunks; ++kc) {
+            if (!tc::mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 11)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = tiles + (size_t)s * S.stage_bytes;
+            tc::mbar_expect_tx(&ctl->full[s], S.stage_bytes);
+            tc::tma_load_2d(st, &tA_hi, &ctl->full[s], kc * TC_K, arow);
+            tc::tma_load_2d(st + S.a_bytes, &tA_lo, &ctl->full[s], kc * TC_K, arow);
+            tc::tma_load_2d(st + 2 * S.a_bytes, &tB_hi, &ctl->full[s], kc * TC_K, brow);
+            tc::tma_load_2d(st + 2 * S.a_bytes + S.b_bytes, &tB_lo, &ctl->full[s], kc * TC_K, brow);
+            if (++s == S.stages) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_tf32(TC_M, S.BN);
+      int s = 0, acc = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        for (int j = 0; ok && j < S.n_chunks; ++j) {
+          if (!tc::mbar_wait(&ctl->tempty[acc], aph ^ 1, abort, err, 12)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t d = tmem_base + (uint32_t)(acc * ACC_STRIDE);
+          for (int kc = 0; kc < S.kchunks; ++kc) {
+            if (!tc::mbar_wait(&ctl->full[s], ph, abort, err, 13)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
+            const uint32_t a_hi = tc::smem_u32(tiles + (size_t)s * S.stage_bytes);
+            const uint32_t a_lo = a_hi + S.a_bytes, b_hi = a_hi + 2 * S.a_bytes, b_lo = b_hi + S.b_bytes;
+#pragma unroll
+            for (int k8 = 0; k8 < TC_K / 8; ++k8) {
+              const uint32_t off = k8 * 32;  // 8 tf32 = 32 bytes along K inside the swizzled row
+              const uint64_t dah = tc::sdesc_k_sw128(a_hi + off), dal = tc::sdesc_k_sw128(a_lo + off);
+              const uint64_t dbh = tc::sdesc_k_sw128(b_hi + off), dbl = tc::sdesc_k_sw128(b_lo + off);
+              tc::mma_tf32(d, dah, dbh, idesc, (kc | k8) != 0);
+              tc::mma_tf32(d, dah, dbl, idesc, 1);
+              tc::mma_tf32(d, dal, dbh, idesc, 1);
+            }
+            tc::mma_commit(&ctl->empty[s]);  // the stage is free once these MMAs have read it
+            if (++s == S.stages) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+          if (!ok) break;
+          tc::mma_commit(&ctl->tfull[acc]);  // accumulator complete
+          acc ^= 1;
+          if (acc == 0) aph ^= 1;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: per-row top-k ----------------
+    const int quarter = warp & 3;
+    const int r_in_tile = quarter * 32 + lane;
+    const float T = scal[0];
+    Epi<KM, NOISY, BAL> E;
+    int acc = 0;
+    uint32_t aph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      const int hc = u / S.m_tiles, mt = u - hc * S.m_tiles;
+      const int h = hc >> 1, c = hc & 1;
+      const int64_t m = (int64_t)mt * TC_M + r_in_tile;
+      const bool owner = m < D.M;
+      const int64_t row = (m * D.H + h) * 2 + c;
+      const float ql = (owner && D.qscale) ? qlen[row] : 1.f;
+      const float* grow = (NOISY && owner) ? gumbel + row * D.n : nullptr;
+      E.reset();
+      for (int j = 0; j < S.n_chunks; ++j) {
+        if (!tc::mbar_wait(&ctl->tfull[acc], aph, abort, err, 14)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const int key0 = j * S.BN;
+        const int valid = min(S.BN, D.n - key0);
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * ACC_STRIDE);
+        for (int cc = 0; cc < S.BN; cc += 32) {
+          uint32_t r[32];
+          tc::tmem_ld32(taddr + cc, r);
+          tc::tmem_wait_ld();
+          if (owner) {
+            const int lim = min(32, valid - cc);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              if (t < lim) {
+                const float g = NOISY ? grow[key0 + cc + t] : 0.f;
+                E.push(D, __uint_as_float(r[t]), key0 + cc + t, T, ql, g);
+              }
+            }
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ctl->tempty[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
+      if (!ok || !owner) continue;
+      const int64_t o = row * D.k;
+#pragma unroll
+      for (int j = 0; j < KM; ++j) {
+        if (j < D.k) {
+          sub_idx[o + j] = E.ix[j];
+          sub_sel[o + j] = E.v[j];
+          sub_score[o + j] = E.sc[j];
+          if constexpr (NOISY && BAL) clean_idx[o + j] = E.cix[j];
+        }
+      }
+      if constexpr (BAL) {
+        row_max[row] = E.rmax;
+        row_sum[row] = E.rsum;
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+TcShape tc_shape(const Dims& D) {
+  TcShape S;
+  S.BN = D.n >= 256 ? 256 : ((D.n + 15) / 16) * 16;
+  S.kchunks = D.half / TC_K;
+  S.m_tiles = (int)((D.M + TC_M - 1) / TC_M);
+  S.n_chunks = (D.n + S.BN - 1) / S.BN;
+  S.a_bytes = TC_M * TC_K * 4;
+  S.b_bytes = S.BN * TC_K * 4;
+  S.stage_bytes = 2 * S.a_bytes + 2 * S.b_bytes;
+  const uint32_t budget = 227 * 1024 - 2048;
+  S.stages = (int)(budget / S.stage_bytes);
+  if (S.stages > 6) S.stages = 6;
+  return S;
+}
+
+template <int KM, bool NOISY, bool BAL>
+cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaStream_t s) {
+  TcShape S = tc_shape(D);
+  CUtensorMap m[4];
+  cudaError_t e;
+  const uint64_t arows = (uint64_t)D.M * D.H * 2, brows = (uint64_t)D.n * D.H * 2;
+  if ((e = make_tmap_f32(&m[0], W.q_hi, arows, D.half, TC_M)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[1], W.q_lo, arows, D.half, TC_M)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[2], W.k_hi, brows, D.half, S.BN)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[3], W.k_lo, brows, D.half, S.BN)) != cudaSuccess) return e;
+  const size_t smem = 1024 + 1024 + (size_t)S.stages * S.stage_bytes;
+  auto kern = score_topk_tc_kernel<KM, NOISY, BAL>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+    return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int units = S.m_tiles * D.H * 2;
+  const int grid = units < sms ? units : sms;
+  kern<<<grid, TC_THREADS, smem, s>>>(m[0], m[1], m[2], m[3], D, S, W.qlen, gumbel, W.scal, W.sub_idx, W.sub_score,
+                                      W.sub_sel, W.clean_idx, W.row_max, W.row_sum, W.err);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <int KM>
+cudaError_t launch_tc_k(const Dims& D, const Work& W, const float* gumbel, bool bal, cudaStream_t s) {
+  if (D.noisy) return bal ? launch_tc_t<KM, true, true>(D, W, gumbel, s) : launch_tc_t<KM, true, false>(D, W, gumbel, s);
+  return bal ? launch_tc_t<KM, false, true>(D, W, gumbel, s) : launch_tc_t<KM, false, false>(D, W, gumbel, s);
+}
+
+}  // namespace
+
+cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * sizeof(float)};
+  cuuint32_t box[2] = {(cuuint32_t)TC_K, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+bool score_tc_supported(const Dims& D) {
+  // the tensor maps' boxes (128 query rows, BN key rows) must fit inside the
+  // [H*2*M, half] / [H*2*n, half] matrices
+  const int BN = D.n >= 256 ? 256 : ((D.n + 15) / 16) * 16;
+  return D.half % TC_K == 0 && D.half >= TC_K && D.M * D.H * 2 >= TC_M && (int64_t)D.n * D.H * 2 >= BN &&
+         D.M * D.H * 2 < (1ll << 31);
+}
+
+cudaError_t launch_score_topk_tc(const Dims& D, const Work& W, const float* gumbel, bool want_balance,
+                                 cudaStream_t s) {
+  switch (D.kmax) {
+    case 4: return launch_tc_k<4>(D, W, gumbel, want_balance, s);
+    case 8: return launch_tc_k<8>(D, W, gumbel, want_balance, s);
+    case 16: return launch_tc_k<16>(D, W, gumbel, want_balance, s);
+    case 32: return launch_tc_k<32>(D, W, gumbel, want_balance, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace ml
