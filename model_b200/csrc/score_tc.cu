@@ -11,14 +11,20 @@
 // hi.hi + hi.lo + lo.hi (three kind::tf32 MMAs per K step), which keeps the
 // cosine within a few float32 ulps of a float32 dot product.
 //
-// CTA = 6 warps, persistent over work units (128-token tile, head, half):
+// CTA = 10 warps, persistent over work units (128-token tile, head, half):
 //   warp 0     TMA producer: A = q_hi / q_lo [128 x 32] and B = k_hi / k_lo
 //              [BN x 32] tiles (128-byte swizzle) into a multi-stage ring;
 //   warp 1     TMEM allocator and MMA issuer (one thread): 128 x BN float32
 //              accumulators, double-buffered in TMEM (2 x 256 columns);
-//   warps 2-5  epilogue: thread t owns token row t of the tile (its TMEM
-//              lane), scans BN scores per chunk with tcgen05.ld and keeps a
-//              sorted register top-k (value desc, index asc).
+//   warps 2-9  epilogue.  TMEM lane = token row; the two warps that share a
+//              lane quarter split each chunk's columns in halves.  Each
+//              thread keeps a sorted register top-k (value desc, index asc)
+//              of its row's half.  Per chunk a group-max pass gives a lower
+//              bound of the chunk's k-th best score; values beating both it
+//              and the list's k-th are collected 16 at a time as a bit mask
+//              and inserted in lockstep across the warp (no per-value
+//              divergence).  At the end of a unit the two halves of every
+//              row are merged through shared memory.
 // Every mbarrier wait is bounded; a timeout sets an error code and unwinds.
 #include <cudaTypedefs.h>
 
@@ -32,9 +38,11 @@ namespace {
 
 constexpr int TC_M = 128;          // tokens per tile (UMMA M)
 constexpr int TC_K = 32;           // float32 elements per 128-byte swizzled row
-constexpr int TC_THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int TC_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_STRIDE = 256;    // TMEM columns per accumulator buffer
+constexpr int SMEM_LIMIT = 227 * 1024;
 
 struct TcShape {
   int BN;        // keys per MMA / chunk
@@ -42,57 +50,94 @@ struct TcShape {
   int kchunks;   // half / 32
   int m_tiles;
   int n_chunks;
-  uint32_t a_bytes, b_bytes, stage_bytes;
+  uint32_t a_bytes, b_bytes, stage_bytes, merge_off;
 };
 
 struct Ctl {
-  uint64_t full[8], empty[8], tfull[2], tempty[2];
+  uint64_t full[8], empty[8], tfull[2], tempty[2], pair[4];
   uint32_t tmem_base;
   int abort;
 };
 
+// Bounded rendezvous of the two epilogue warps that share a TMEM lane quarter.
+__device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t& parity, int lane, volatile int* abort, int* err) {
+  __syncwarp();
+  if (lane == 0) tc::mbar_arrive(bar);
+  const bool ok = tc::mbar_wait(bar, parity, abort, err, 15);
+  parity ^= 1;
+  return __all_sync(FULL, ok);
+}
+
+// a[t] for a runtime t in [0, 16): select tree, no local memory.
+__device__ __forceinline__ float pick16(const float (&a)[16], int t) {
+  float l8[8], l4[4], l2[2];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) l8[i] = (t & 8) ? a[i + 8] : a[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) l4[i] = (t & 4) ? l8[i + 4] : l8[i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) l2[i] = (t & 2) ? l4[i + 2] : l4[i];
+  return (t & 1) ? l2[1] : l2[0];
+}
+
+// Insertion of (s, i) at its (value desc, index asc) rank, for any index.
+// Precondition: (s, i) ranks before the list's last element.
+template <int KM>
+__device__ __forceinline__ void list_insert_any(float (&v)[KM], int (&ix)[KM], float s, int i) {
+#pragma unroll
+  for (int j = KM - 1; j >= 0; --j) {
+    const bool before_j = ranks_before(v[j], ix[j], s, i);
+    const bool before_prev = j == 0 || ranks_before(v[j - 1], ix[j - 1], s, i);
+    if (!before_prev) {
+      v[j] = v[j - 1];
+      ix[j] = ix[j - 1];
+    } else if (!before_j) {
+      v[j] = s;
+      ix[j] = i;
+    }
+  }
+}
+
+template <int KM>
+__device__ __forceinline__ void list_insert_any3(float (&v)[KM], int (&ix)[KM], float (&a)[KM], float s, int i,
+                                                 float x) {
+#pragma unroll
+  for (int j = KM - 1; j >= 0; --j) {
+    const bool before_j = ranks_before(v[j], ix[j], s, i);
+    const bool before_prev = j == 0 || ranks_before(v[j - 1], ix[j - 1], s, i);
+    if (!before_prev) {
+      v[j] = v[j - 1];
+      ix[j] = ix[j - 1];
+      a[j] = a[j - 1];
+    } else if (!before_j) {
+      v[j] = s;
+      ix[j] = i;
+      a[j] = x;
+    }
+  }
+}
+
+// Per-thread state of one (token, head, half) row, over this warp's columns.
 template <int KM, bool NOISY, bool BAL>
-struct Epi {
-  float v[KM], sc[KM], cv[NOISY && BAL ? KM : 1];
-  int ix[KM], cix[NOISY && BAL ? KM : 1];
+struct RowState {
+  static constexpr bool CLEAN = NOISY && BAL;   // separate clean top-k for the balance counts
+  float v[KM], sc[NOISY ? KM : 1], cv[CLEAN ? KM : 1];
+  int ix[KM], cix[CLEAN ? KM : 1];
   float rmax, rsum;
 
   __device__ __forceinline__ void reset() {
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       v[j] = -INFINITY;
-      sc[j] = -INFINITY;
       ix[j] = 0;
-    }
-    if constexpr (NOISY && BAL) {
-#pragma unroll
-      for (int j = 0; j < KM; ++j) {
+      if constexpr (NOISY) sc[j] = -INFINITY;
+      if constexpr (CLEAN) {
         cv[j] = -INFINITY;
         cix[j] = 0;
       }
     }
     rmax = -INFINITY;
     rsum = 0.f;
-  }
-
-  __device__ __forceinline__ void push(const Dims& D, float cosv, int key, float T, float ql, float g) {
-    float score = __fmul_rn(cosv, T);                     // memory.py:150
-    if (D.qscale) score = __fmul_rn(score, ql);           // memory.py:151-152
-    float sel = score;
-    if constexpr (NOISY) sel = __fadd_rn(score, __fmul_rn(D.noise_coef, g));  // memory.py:158
-    if (sel > v[KM - 1]) list_insert3<KM>(v, ix, sc, sel, key, score);
-    if constexpr (NOISY && BAL) {
-      if (score > cv[KM - 1]) list_insert<KM>(cv, cix, score, key);
-    }
-    if constexpr (BAL) {
-      const float p = D.btgrad ? score : __fmul_rn(cosv, T);  // memory.py:211
-      if (p > rmax) {
-        rsum = rsum * expf(rmax - p) + 1.f;
-        rmax = p;
-      } else {
-        rsum += expf(p - rmax);
-      }
-    }
   }
 };
 
@@ -119,8 +164,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&ctl->tfull[b], 1);
-      tc::mbar_init(&ctl->tempty[b], 4);
+      tc::mbar_init(&ctl->tempty[b], EPI_WARPS);
     }
+    for (int q = 0; q < 4; ++q) tc::mbar_init(&ctl->pair[q], 2);
     ctl->abort = 0;
     tc::fence_mbar_init();
   }
@@ -211,12 +257,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- epilogue: per-row top-k ----------------
-    const int quarter = warp & 3;
+    using RS = RowState<KM, NOISY, BAL>;
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may read
+    const int hf = (warp - 2) >> 2;          // column half of every chunk
     const int r_in_tile = quarter * 32 + lane;
+    const int half_bn = S.BN >> 1;
     const float T = scal[0];
-    Epi<KM, NOISY, BAL> E;
+    // merge buffer: [128 rows][KM] values, indices (+ clean-score copies)
+    float* mv = reinterpret_cast<float*>(smem + S.merge_off);
+    int* mi = reinterpret_cast<int*>(mv + TC_M * KM);
+    float* mx = reinterpret_cast<float*>(mi + TC_M * KM);   // NOISY: sc; later the clean list
+    float* mrow = mx + (NOISY ? TC_M * KM : 0);             // BAL: rmax, rsum per row
+    RS R;
     int acc = 0;
-    uint32_t aph = 0;
+    uint32_t aph = 0, pph = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
       const int hc = u / S.m_tiles, mt = u - hc * S.m_tiles;
@@ -226,27 +280,103 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int64_t row = (m * D.H + h) * 2 + c;
       const float ql = (owner && D.qscale) ? qlen[row] : 1.f;
       const float* grow = (NOISY && owner) ? gumbel + row * D.n : nullptr;
-      E.reset();
+      R.reset();
       for (int j = 0; j < S.n_chunks; ++j) {
-        if (!tc::mbar_wait(&ctl->tfull[acc], aph, abort, err, 14)) {
+        // warp-uniform outcome, so every lane leaves together on a timeout
+        if (!__all_sync(FULL, tc::mbar_wait(&ctl->tfull[acc], aph, abort, err, 14))) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
         const int key0 = j * S.BN;
         const int valid = min(S.BN, D.n - key0);
+        const int cb = hf * half_bn, ce = min(cb + half_bn, valid);
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * ACC_STRIDE);
-        for (int cc = 0; cc < S.BN; cc += 32) {
-          uint32_t r[32];
-          tc::tmem_ld32(taddr + cc, r);
-          tc::tmem_wait_ld();
-          if (owner) {
-            const int lim = min(32, valid - cc);
+
+        // pass A: a lower bound of this half-chunk's k-th best selection score
+        // (min over KM group maxima of KM disjoint groups)
+        // (min over k group maxima of k disjoint groups of the half-chunk)
+        float tau = -INFINITY;
+        if constexpr (!NOISY) {
+          const int gs = half_bn / D.k;
+          if (ce - cb == half_bn && half_bn % 16 == 0 && gs >= 1 && half_bn % D.k == 0 && (gs & (gs - 1)) == 0) {
+            const int gmask = gs - 1;
+            float gmin = INFINITY, gmax = -INFINITY;
+            for (int cc = cb; cc < ce; cc += 16) {
+              uint32_t r[16];
+              tc::tmem_ld16(taddr + cc, r);
+              tc::tmem_wait_ld();
 #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              if (t < lim) {
-                const float g = NOISY ? grow[key0 + cc + t] : 0.f;
-                E.push(D, __uint_as_float(r[t]), key0 + cc + t, T, ql, g);
+              for (int t = 0; t < 16; ++t) {
+                float sc0 = __fmul_rn(__uint_as_float(r[t]), T);
+                if (D.qscale) sc0 = __fmul_rn(sc0, ql);
+                gmax = fmaxf(gmax, sc0);
+                if (((cc - cb + t) & gmask) == gmask) {
+                  gmin = fminf(gmin, gmax);
+                  gmax = -INFINITY;
+                }
+              }
+            }
+            tau = gmin;
+          }
+        }
+
+        // pass B: candidates beating max(tau, list k-th), inserted in lockstep
+        for (int cc = cb; cc < ce; cc += 16) {
+          uint32_t r[16];
+          tc::tmem_ld16(taddr + cc, r);
+          tc::tmem_wait_ld();
+          float sel[16], scr[NOISY ? 16 : 1];
+          uint32_t mask = 0, cmask = 0;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const float cosv = __uint_as_float(r[t]);
+            float score = __fmul_rn(cosv, T);                          // memory.py:150
+            if (D.qscale) score = __fmul_rn(score, ql);                // memory.py:151-152
+            float s_sel = score;
+            const bool in = owner && (cc + t < ce);
+            if constexpr (NOISY) {
+              const float g = in ? grow[key0 + cc + t] : 0.f;
+              s_sel = __fadd_rn(score, __fmul_rn(D.noise_coef, g));    // memory.py:158
+              scr[t] = score;
+            }
+            sel[t] = s_sel;
+            if (in && s_sel >= tau && s_sel > R.v[KM - 1]) mask |= 1u << t;
+            if constexpr (RS::CLEAN) {
+              if (in && score > R.cv[KM - 1]) cmask |= 1u << t;
+            }
+            if constexpr (BAL) {
+              if (in) {
+                const float p = D.btgrad ? score : __fmul_rn(cosv, T);  // memory.py:211
+                if (p > R.rmax) {
+                  R.rsum = R.rsum * expf(R.rmax - p) + 1.f;
+                  R.rmax = p;
+                } else {
+                  R.rsum += expf(p - R.rmax);
+                }
+              }
+            }
+          }
+          while (__any_sync(FULL, mask != 0)) {
+            if (mask) {
+              const int t = __ffs(mask) - 1;
+              mask &= mask - 1;
+              const float s = pick16(sel, t);
+              if (s > R.v[KM - 1]) {
+                if constexpr (NOISY)
+                  list_insert3<KM>(R.v, R.ix, R.sc, s, key0 + cc + t, pick16(scr, t));
+                else
+                  list_insert<KM>(R.v, R.ix, s, key0 + cc + t);
+              }
+            }
+          }
+          if constexpr (RS::CLEAN) {
+            while (__any_sync(FULL, cmask != 0)) {
+              if (cmask) {
+                const int t = __ffs(cmask) - 1;
+                cmask &= cmask - 1;
+                const float s = pick16(scr, t);
+                if (s > R.cv[KM - 1]) list_insert<KM>(R.cv, R.cix, s, key0 + cc + t);
               }
             }
           }
@@ -257,21 +387,87 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         acc ^= 1;
         if (acc == 0) aph ^= 1;
       }
-      if (!ok || !owner) continue;
-      const int64_t o = row * D.k;
+      if (!ok) break;
+
+      // ---- merge the two column halves of each row (warp pair of a quarter)
+      uint64_t* pb = &ctl->pair[quarter];
+      if (hf == 1) {
 #pragma unroll
-      for (int j = 0; j < KM; ++j) {
-        if (j < D.k) {
-          sub_idx[o + j] = E.ix[j];
-          sub_sel[o + j] = E.v[j];
-          sub_score[o + j] = E.sc[j];
-          if constexpr (NOISY && BAL) clean_idx[o + j] = E.cix[j];
+        for (int j = 0; j < KM; ++j) {
+          mv[r_in_tile * KM + j] = R.v[j];
+          mi[r_in_tile * KM + j] = R.ix[j];
+          if constexpr (NOISY) mx[r_in_tile * KM + j] = R.sc[j];
+        }
+        if constexpr (BAL) {
+          mrow[2 * r_in_tile] = R.rmax;
+          mrow[2 * r_in_tile + 1] = R.rsum;
         }
       }
-      if constexpr (BAL) {
-        row_max[row] = E.rmax;
-        row_sum[row] = E.rsum;
+      if (!pair_sync(pb, pph, lane, abort, err)) break;
+      if (hf == 0) {
+        bool done = !owner;
+        for (int j = 0; __any_sync(FULL, !done) && j < KM; ++j) {
+          if (!done) {
+            const float s = mv[r_in_tile * KM + j];
+            const int i = mi[r_in_tile * KM + j];
+            if (ranks_before(s, i, R.v[KM - 1], R.ix[KM - 1])) {
+              if constexpr (NOISY)
+                list_insert_any3<KM>(R.v, R.ix, R.sc, s, i, mx[r_in_tile * KM + j]);
+              else
+                list_insert_any<KM>(R.v, R.ix, s, i);
+            } else {
+              done = true;  // the other list is sorted: nothing further can enter
+            }
+          }
+        }
+        if constexpr (BAL) {
+          const float m2 = mrow[2 * r_in_tile], s2 = mrow[2 * r_in_tile + 1];
+          const float mm = fmaxf(R.rmax, m2);
+          R.rsum = (R.rsum > 0.f ? R.rsum * expf(R.rmax - mm) : 0.f) + (s2 > 0.f ? s2 * expf(m2 - mm) : 0.f);
+          R.rmax = mm;
+        }
       }
+      if constexpr (RS::CLEAN) {
+        if (!pair_sync(pb, pph, lane, abort, err)) break;
+        if (hf == 1) {
+#pragma unroll
+          for (int j = 0; j < KM; ++j) {
+            mv[r_in_tile * KM + j] = R.cv[j];
+            mi[r_in_tile * KM + j] = R.cix[j];
+          }
+        }
+        if (!pair_sync(pb, pph, lane, abort, err)) break;
+        if (hf == 0) {
+          bool done = !owner;
+          for (int j = 0; __any_sync(FULL, !done) && j < KM; ++j) {
+            if (!done) {
+              const float s = mv[r_in_tile * KM + j];
+              const int i = mi[r_in_tile * KM + j];
+              if (ranks_before(s, i, R.cv[KM - 1], R.cix[KM - 1]))
+                list_insert_any<KM>(R.cv, R.cix, s, i);
+              else
+                done = true;
+            }
+          }
+        }
+      }
+      if (hf == 0 && owner) {
+        const int64_t o = row * D.k;
+#pragma unroll
+        for (int j = 0; j < KM; ++j) {
+          if (j < D.k) {
+            sub_idx[o + j] = R.ix[j];
+            sub_sel[o + j] = R.v[j];
+            sub_score[o + j] = NOISY ? R.sc[j] : R.v[j];
+            if constexpr (RS::CLEAN) clean_idx[o + j] = R.cix[j];
+          }
+        }
+        if constexpr (BAL) {
+          row_max[row] = R.rmax;
+          row_sum[row] = R.rsum;
+        }
+      }
+      if (!pair_sync(pb, pph, lane, abort, err)) break;   // the merge buffer is reused by the next unit
     }
   }
 
@@ -296,24 +492,37 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+inline int bn_for(const Dims& D) {
+  // k = 32 lists need a 48 KB merge buffer: use 128-key chunks to make room
+  const int cap = D.kmax >= 32 ? 128 : 256;
+  return D.n >= cap ? cap : ((D.n + 15) / 16) * 16;
+}
+
+inline uint32_t merge_bytes(const Dims& D) {
+  const uint32_t per = 8u + (D.noisy ? 4u : 0u);
+  return TC_M * D.kmax * per + TC_M * 8u;
+}
+
 TcShape tc_shape(const Dims& D) {
   TcShape S;
-  S.BN = D.n >= 256 ? 256 : ((D.n + 15) / 16) * 16;
+  S.BN = bn_for(D);
   S.kchunks = D.half / TC_K;
   S.m_tiles = (int)((D.M + TC_M - 1) / TC_M);
   S.n_chunks = (D.n + S.BN - 1) / S.BN;
   S.a_bytes = TC_M * TC_K * 4;
   S.b_bytes = S.BN * TC_K * 4;
   S.stage_bytes = 2 * S.a_bytes + 2 * S.b_bytes;
-  const uint32_t budget = 227 * 1024 - 2048;
-  S.stages = (int)(budget / S.stage_bytes);
+  const uint32_t fixed = 2048 + merge_bytes(D);
+  S.stages = (int)((SMEM_LIMIT - fixed) / S.stage_bytes);
   if (S.stages > 6) S.stages = 6;
+  S.merge_off = 1024 + S.stages * S.stage_bytes;
   return S;
 }
 
 template <int KM, bool NOISY, bool BAL>
 cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaStream_t s) {
   TcShape S = tc_shape(D);
+  if (S.stages < 2) return cudaErrorInvalidConfiguration;
   CUtensorMap m[4];
   cudaError_t e;
   const uint64_t arows = (uint64_t)D.M * D.H * 2, brows = (uint64_t)D.n * D.H * 2;
@@ -321,7 +530,7 @@ cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaS
   if ((e = make_tmap_f32(&m[1], W.q_lo, arows, D.half, TC_M)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[2], W.k_hi, brows, D.half, S.BN)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[3], W.k_lo, brows, D.half, S.BN)) != cudaSuccess) return e;
-  const size_t smem = 1024 + 1024 + (size_t)S.stages * S.stage_bytes;
+  const size_t smem = 1024 + (size_t)S.merge_off + merge_bytes(D);
   auto kern = score_topk_tc_kernel<KM, NOISY, BAL>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
     return e;
@@ -360,7 +569,7 @@ cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, ui
 bool score_tc_supported(const Dims& D) {
   // the tensor maps' boxes (128 query rows, BN key rows) must fit inside the
   // [H*2*M, half] / [H*2*n, half] matrices
-  const int BN = D.n >= 256 ? 256 : ((D.n + 15) / 16) * 16;
+  const int BN = bn_for(D);
   return D.half % TC_K == 0 && D.half >= TC_K && D.M * D.H * 2 >= TC_M && (int64_t)D.n * D.H * 2 >= BN &&
          D.M * D.H * 2 < (1ll << 31);
 }
