@@ -12,7 +12,8 @@
  * Conventions
  *   - Every pointer in the argument structs is a device pointer unless its
  *     comment says otherwise.  All float tensors are float32, row-major,
- *     contiguous; the value table may be float32, float16 or bfloat16.
+ *     contiguous and 16-byte aligned; the value table may be float32,
+ *     float16 or bfloat16.
  *   - The library allocates nothing on these paths: the caller passes a
  *     device workspace of at least memlayer_*_workspace_size() bytes, 256-byte
  *     aligned.  The workspace's contents need not be initialised.

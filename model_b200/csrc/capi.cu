@@ -89,9 +89,22 @@ size_t layout(const Dims& D, const Flags& f, char* ws, Work* W) {
     w.clean_cnt = (float*)take(sizeof(float) * D.H * 2 * D.n);
   }
   if (f.layer) {
-    w.qraw = (float*)take(sizeof(float) * D.M * D.H * D.dk);
+    const int64_t NRD = (int64_t)D.H * D.dk + D.d;
     w.gate = (float*)take(sizeof(float) * D.M * D.d);
-    w.memg = (float*)take(sizeof(float) * D.M * D.d);
+    if (proj_tc_supported(D)) {
+      w.h_hi = (float*)take(sizeof(float) * D.M * D.dm);
+      w.h_lo = (float*)take(sizeof(float) * D.M * D.dm);
+      w.wrg_hi = (float*)take(sizeof(float) * NRD * D.dm);
+      w.wrg_lo = (float*)take(sizeof(float) * NRD * D.dm);
+      w.bias_rg = (float*)take(sizeof(float) * NRD);
+      w.wo_hi = (float*)take(sizeof(float) * D.dm * D.d);
+      w.wo_lo = (float*)take(sizeof(float) * D.dm * D.d);
+      w.memg_hi = (float*)take(sizeof(float) * D.M * D.d);
+      w.memg_lo = (float*)take(sizeof(float) * D.M * D.d);
+    } else {
+      w.qraw = (float*)take(sizeof(float) * D.M * D.H * D.dk);
+      w.memg = (float*)take(sizeof(float) * D.M * D.d);
+    }
     w.slots = (int*)take(sizeof(int) * D.M * D.H * D.k);
     w.weights = (float*)take(sizeof(float) * D.M * D.H * D.k);
   }
@@ -130,14 +143,11 @@ cudaError_t mark(const memlayer_pool_args* a, int i, cudaStream_t s) {
   return cudaEventRecord((cudaEvent_t)a->stage_events->events[i], s);
 }
 
-// The shared pool sequence; q is [M, H, d_key] (caller queries or router output).
-int run_pool(const Dims& D, const memlayer_config* c, const memlayer_pool_args* a, const Work& W, const float* q,
-             int* slots, float* weights, float* out, float* memg, const float* gate, cudaStream_t s) {
-  ML_TRY(launch_prep_keys(D, a->sub_keys, a->log_temperature, c->min_temperature, c->max_temperature, W.keys_n,
-                          W.k_hi, W.k_lo, W.scal, W.err, s));
-  float* qn = a->queries_unit ? a->queries_unit : W.qn;
-  ML_TRY(launch_normalize_queries(D, q, qn, W.qlen, W.q_hi, W.q_lo, s));
-  ML_TRY(mark(a, 2, s));
+// Routing from prepared unit queries onward: score + per-half top-k,
+// balance statistics, k*k combine + softmax + gather (+ gate), aux finalise.
+int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, float* qn, int* slots,
+                  float* weights, float* out, float* memg, float* memg_hi, float* memg_lo, const float* gate,
+                  cudaStream_t s) {
   Work w2 = W;
   w2.qn = qn;
   const bool bal = a->balance_loss != nullptr;
@@ -149,10 +159,16 @@ int run_pool(const Dims& D, const memlayer_config* c, const memlayer_pool_args* 
   if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
   if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
   ML_TRY(mark(a, 3, s));
-  ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, gate, a->slot_counts,
+  ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, memg_hi, memg_lo, gate, a->slot_counts,
                                a->subkey_counts, s));
   ML_TRY(mark(a, 4, s));
   ML_TRY(launch_finalize(D, w2, a->top1_weight, a->temperature, s));
+  return MEMLAYER_OK;
+}
+
+int prep_keys(const Dims& D, const memlayer_config* c, const memlayer_pool_args* a, const Work& W, cudaStream_t s) {
+  ML_TRY(launch_prep_keys(D, a->sub_keys, a->log_temperature, c->min_temperature, c->max_temperature, W.keys_n,
+                          W.k_hi, W.k_lo, W.scal, W.err, s));
   return MEMLAYER_OK;
 }
 
@@ -222,8 +238,11 @@ int32_t memlayer_pool_forward(const memlayer_config* cfg, const memlayer_pool_ar
   cudaStream_t s = (cudaStream_t)stream;
   ML_TRY(mark(a, 0, s));
   ML_TRY(mark(a, 1, s));
-  st = run_pool(D, cfg, a, W, a->queries, a->slots, a->weights, a->out, nullptr, nullptr, s);
-  if (st) return st;
+  if ((st = prep_keys(D, cfg, a, W, s))) return st;
+  float* qn = a->queries_unit ? a->queries_unit : W.qn;
+  ML_TRY(launch_normalize_queries(D, a->queries, qn, W.qlen, W.q_hi, W.q_lo, s));
+  ML_TRY(mark(a, 2, s));
+  if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, a->out, nullptr, nullptr, nullptr, nullptr, s))) return st;
   ML_TRY(mark(a, 5, s));
   return MEMLAYER_OK;
 }
@@ -237,6 +256,8 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
   st = check_pool_args(D, &a->pool, true);
   if (st) return st;
   if (D.M > 0 && (!a->h || !a->w_router || !a->w_gate || !a->w_out || !a->y)) return MEMLAYER_ERR_BAD_POINTER;
+  if (!aligned16(a->h) || !aligned16(a->y) || !aligned16(a->mem) || !aligned16(a->pool.out))
+    return MEMLAYER_ERR_BAD_POINTER;
   resolve_noise(&D, cfg, &a->pool);
   if (D.noisy && !a->pool.gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
   Flags f;
@@ -248,21 +269,41 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
   Work W;
   layout(D, f, (char*)workspace, &W);
   cudaStream_t s = (cudaStream_t)stream;
-  ML_TRY(mark(&a->pool, 0, s));
-  // model.py:110 router, model.py:118 gate pre-activation + silu
-  ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
-  ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
-  ML_TRY(mark(&a->pool, 1, s));
-  int* slots = a->pool.slots ? a->pool.slots : W.slots;
-  float* weights = a->pool.weights ? a->pool.weights : W.weights;
-  float* out = a->mem ? a->mem : a->pool.out;
-  st = run_pool(D, cfg, &a->pool, W, W.qraw, slots, weights, out, W.memg, W.gate, s);
-  if (st) return st;
-  if (a->mem && a->pool.out && a->pool.out != a->mem && D.M > 0)
-    ML_TRY(cudaMemcpyAsync(a->pool.out, a->mem, sizeof(float) * D.M * D.d, cudaMemcpyDeviceToDevice, s));
-  // model.py:119 output projection
-  ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));
-  ML_TRY(mark(&a->pool, 5, s));
+  const memlayer_pool_args* pa = &a->pool;
+  ML_TRY(mark(pa, 0, s));
+  if ((st = prep_keys(D, cfg, pa, W, s))) return st;
+  int* slots = pa->slots ? pa->slots : W.slots;
+  float* weights = pa->weights ? pa->weights : W.weights;
+  float* out = a->mem ? a->mem : pa->out;
+  float* qn = pa->queries_unit ? pa->queries_unit : W.qn;
+  if (W.h_hi) {
+    // tensor-core projections: K-major tf32 halves of the Dense kernels and
+    // the hidden state, then one GEMM for router (model.py:110) + gate (:118)
+    const int NR = D.H * D.dk;
+    ML_TRY(launch_transpose_split(a->w_router, D.dm, NR, W.wrg_hi, W.wrg_lo, 0, s));
+    ML_TRY(launch_transpose_split(a->w_gate, D.dm, D.d, W.wrg_hi, W.wrg_lo, NR, s));
+    ML_TRY(launch_concat_bias(a->b_router, NR, a->b_gate, D.d, W.bias_rg, s));
+    ML_TRY(launch_transpose_split(a->w_out, D.d, D.dm, W.wo_hi, W.wo_lo, 0, s));
+    ML_TRY(launch_split(a->h, D.M * D.dm, W.h_hi, W.h_lo, s));
+    // unit queries in float32 only when the aux output asks or the SIMT score path reads them
+    ML_TRY(launch_router_gate_tc(D, W, W.bias_rg, (pa->queries_unit || !W.q_hi) ? qn : nullptr, s));
+    ML_TRY(mark(pa, 1, s));
+    ML_TRY(mark(pa, 2, s));
+    if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, nullptr, W.memg_hi, W.memg_lo, W.gate, s))) return st;
+    ML_TRY(launch_out_tc(D, W, a->b_out, a->y, s));                           // model.py:119
+  } else {
+    // SIMT float32 projections
+    ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
+    ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
+    ML_TRY(mark(pa, 1, s));
+    ML_TRY(launch_normalize_queries(D, W.qraw, qn, W.qlen, W.q_hi, W.q_lo, s));
+    ML_TRY(mark(pa, 2, s));
+    if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, W.memg, nullptr, nullptr, W.gate, s))) return st;
+    ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));  // model.py:119
+  }
+  if (a->mem && pa->out && pa->out != a->mem && D.M > 0)
+    ML_TRY(cudaMemcpyAsync(pa->out, a->mem, sizeof(float) * D.M * D.d, cudaMemcpyDeviceToDevice, s));
+  ML_TRY(mark(pa, 5, s));
   return MEMLAYER_OK;
 }
 

@@ -25,6 +25,12 @@ namespace ml {
 
 namespace {
 
+__device__ __forceinline__ float tc_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 template <typename VT, int VEC>
 __device__ __forceinline__ void load_group(const VT* p, float (&o)[VEC]) {
   if constexpr (VEC == 1) {
@@ -38,8 +44,9 @@ template <int KM, typename VT, int VEC, int CH>
 __global__ void __launch_bounds__(1024) combine_gather_kernel(
     Dims D, const int* __restrict__ sub_idx, const float* __restrict__ sub_score, const float* __restrict__ sub_sel,
     const VT* __restrict__ values, int* __restrict__ slots, float* __restrict__ weights, float* __restrict__ out,
-    float* __restrict__ memg, const float* __restrict__ gate, float* __restrict__ slot_counts,
-    float* __restrict__ subkey_counts, float* __restrict__ top1_part) {
+    float* __restrict__ memg, float* __restrict__ memg_hi, float* __restrict__ memg_lo,
+    const float* __restrict__ gate, float* __restrict__ slot_counts, float* __restrict__ subkey_counts,
+    float* __restrict__ top1_part) {
   extern __shared__ float red[];  // [H][d]
   constexpr int CPL = (KM * KM + 31) / 32;
   const int64_t m = blockIdx.x;
@@ -149,18 +156,27 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
     float o = 0.f;
     for (int hh = 0; hh < D.H; ++hh) o += red[hh * d + i];   // heads summed (memory.py:192)
     if (out) out[m * d + i] = o;
-    if (memg) memg[m * d + i] = o * gate[m * d + i];         // model.py:119 mem * gate
+    if (memg || memg_hi) {
+      const float g = o * gate[m * d + i];                   // model.py:119 mem * gate
+      if (memg) memg[m * d + i] = g;
+      if (memg_hi) {                                         // tf32 halves for the tensor-core out GEMM
+        const float hi = tc_round(g);
+        memg_hi[m * d + i] = hi;
+        memg_lo[m * d + i] = tc_round(g - hi);
+      }
+    }
   }
 }
 
 template <int KM, typename VT, int VEC>
 cudaError_t launch_ch(const Dims& D, int ch, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Work& W,
-                      const VT* values, int* slots, float* weights, float* out, float* memg, const float* gate,
-                      float* slot_counts, float* subkey_counts) {
-#define ML_CG(CHV)                                                                                              \
-  combine_gather_kernel<KM, VT, VEC, CHV><<<grid, block, smem, s>>>(D, W.sub_idx, W.sub_score, W.sub_sel,     \
-                                                                    values, slots, weights, out, memg, gate, \
-                                                                    slot_counts, subkey_counts, W.top1_part)
+                      const VT* values, int* slots, float* weights, float* out, float* memg, float* mhi, float* mlo,
+                      const float* gate, float* slot_counts, float* subkey_counts) {
+#define ML_CG(CHV)                                                                                             \
+  combine_gather_kernel<KM, VT, VEC, CHV><<<grid, block, smem, s>>>(D, W.sub_idx, W.sub_score, W.sub_sel,    \
+                                                                    values, slots, weights, out, memg, mhi, \
+                                                                    mlo, gate, slot_counts, subkey_counts,  \
+                                                                    W.top1_part)
   switch (ch) {
     case 1: ML_CG(1); break;
     case 2: ML_CG(2); break;
@@ -180,37 +196,41 @@ inline int ch_for(int groups) {
 
 template <int KM>
 cudaError_t launch_k(const Dims& D, const Work& W, const void* values, int* slots, float* weights, float* out,
-                     float* memg, const float* gate, float* slot_counts, float* subkey_counts, cudaStream_t s) {
+                     float* memg, float* mhi, float* mlo, const float* gate, float* slot_counts,
+                     float* subkey_counts, cudaStream_t s) {
   dim3 grid((unsigned)D.M), block(32 * D.H);
   size_t smem = sizeof(float) * D.H * D.d;
   const bool aligned = (reinterpret_cast<uintptr_t>(values) & 15) == 0;
   if (D.vdtype == MEMLAYER_F16)
     return launch_ch<KM, __half, 8>(D, ch_for(D.d / 8), grid, block, smem, s, W, (const __half*)values, slots,
-                                    weights, out, memg, gate, slot_counts, subkey_counts);
+                                    weights, out, memg, mhi, mlo, gate, slot_counts, subkey_counts);
   if (D.vdtype == MEMLAYER_BF16)
     return launch_ch<KM, __nv_bfloat16, 8>(D, ch_for(D.d / 8), grid, block, smem, s, W,
-                                           (const __nv_bfloat16*)values, slots, weights, out, memg, gate,
-                                           slot_counts, subkey_counts);
+                                           (const __nv_bfloat16*)values, slots, weights, out, memg, mhi, mlo,
+                                           gate, slot_counts, subkey_counts);
   if (D.d % 4 == 0 && aligned)
     return launch_ch<KM, float, 4>(D, ch_for(D.d / 4), grid, block, smem, s, W, (const float*)values, slots,
-                                   weights, out, memg, gate, slot_counts, subkey_counts);
+                                   weights, out, memg, mhi, mlo, gate, slot_counts, subkey_counts);
   return launch_ch<KM, float, 1>(D, ch_for(D.d), grid, block, smem, s, W, (const float*)values, slots, weights,
-                                 out, memg, gate, slot_counts, subkey_counts);
+                                 out, memg, mhi, mlo, gate, slot_counts, subkey_counts);
 }
 
 }  // namespace
 
 cudaError_t launch_combine_gather(const Dims& D, const Work& W, const void* values, int* slots, float* weights,
-                                  float* out, float* mem_gated, const float* gate, float* slot_counts,
-                                  float* subkey_counts, cudaStream_t s) {
+                                  float* out, float* mem_gated, float* memg_hi, float* memg_lo, const float* gate,
+                                  float* slot_counts, float* subkey_counts, cudaStream_t s) {
   if (D.M == 0) return cudaSuccess;
+#define ML_K(KV) \
+  launch_k<KV>(D, W, values, slots, weights, out, mem_gated, memg_hi, memg_lo, gate, slot_counts, subkey_counts, s)
   switch (D.kmax) {
-    case 4: return launch_k<4>(D, W, values, slots, weights, out, mem_gated, gate, slot_counts, subkey_counts, s);
-    case 8: return launch_k<8>(D, W, values, slots, weights, out, mem_gated, gate, slot_counts, subkey_counts, s);
-    case 16: return launch_k<16>(D, W, values, slots, weights, out, mem_gated, gate, slot_counts, subkey_counts, s);
-    case 32: return launch_k<32>(D, W, values, slots, weights, out, mem_gated, gate, slot_counts, subkey_counts, s);
+    case 4: return ML_K(4);
+    case 8: return ML_K(8);
+    case 16: return ML_K(16);
+    case 32: return ML_K(32);
     default: return cudaErrorInvalidValue;
   }
+#undef ML_K
 }
 
 }  // namespace ml

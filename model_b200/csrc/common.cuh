@@ -40,6 +40,15 @@ struct Work {
   float* q_hi = nullptr;       // [H*2,M,half] rna_tf32(qn), codebook-major
   float* q_lo = nullptr;       // [H*2,M,half] rna_tf32(qn - q_hi)
   int* err = nullptr;          // [1] device error code (bounded waits)
+  float* h_hi = nullptr;       // [M,dm] tf32 halves of the hidden state   (tensor-core projections)
+  float* h_lo = nullptr;
+  float* wrg_hi = nullptr;     // [H*dk + d, dm] router | gate kernels, K-major
+  float* wrg_lo = nullptr;
+  float* bias_rg = nullptr;    // [H*dk + d] router | gate biases
+  float* wo_hi = nullptr;      // [dm, d] output kernel, K-major
+  float* wo_lo = nullptr;
+  float* memg_hi = nullptr;    // [M,d] tf32 halves of mem * gate
+  float* memg_lo = nullptr;
   float* qn = nullptr;         // [M,H,2,half] unit query halves
   float* qlen = nullptr;       // [M,H,2] |q_half| / sqrt(half)
   int* sub_idx = nullptr;      // [M,H,2,k] stage-1 sub-key ids (selection order)
@@ -185,8 +194,14 @@ cudaError_t launch_score_topk(const Dims& D, const Work& W, const float* gumbel,
                               cudaStream_t s);
 cudaError_t launch_balance(const Dims& D, const Work& W, float* balance_loss, cudaStream_t s);
 cudaError_t launch_combine_gather(const Dims& D, const Work& W, const void* values, int* slots, float* weights,
-                                  float* out, float* mem_gated, const float* gate, float* slot_counts,
-                                  float* subkey_counts, cudaStream_t s);
+                                  float* out, float* mem_gated, float* memg_hi, float* memg_lo, const float* gate,
+                                  float* slot_counts, float* subkey_counts, cudaStream_t s);
+bool proj_tc_supported(const Dims& D);
+cudaError_t launch_split(const float* x, int64_t n, float* hi, float* lo, cudaStream_t s);
+cudaError_t launch_transpose_split(const float* W, int K, int N, float* hi, float* lo, int row0, cudaStream_t s);
+cudaError_t launch_concat_bias(const float* a, int na, const float* b, int nb, float* out, cudaStream_t s);
+cudaError_t launch_router_gate_tc(const Dims& D, const Work& W, const float* bias_rg, float* qn_out, cudaStream_t s);
+cudaError_t launch_out_tc(const Dims& D, const Work& W, const float* b_out, float* y, cudaStream_t s);
 cudaError_t launch_finalize(const Dims& D, const Work& W, float* top1, float* temperature, cudaStream_t s);
 cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float* C, int64_t M, int N, int K,
                         bool silu, cudaStream_t s);

@@ -1,0 +1,311 @@
+// Projection GEMMs of the memory-layer block on the tensor cores
+// (model.py:110-111 router Dense, model.py:118 mem_gate Dense + silu,
+// model.py:119 mem_out Dense), float32-faithful through the same 3xTF32
+// split as the score kernel: C = A B^T with A [M, K] and B [N, K] both
+// K-major, given as tf32 hi / lo halves.
+//
+// Epilogues (8 warps; TMEM lane = output row; the two warps of a lane
+// quarter take the two 128-column halves of the 256-column tile):
+//   ROUTER_GATE  columns [0, NR): q = acc + b_router, split per query half
+//                into q_len = |q_half| / sqrt(half) and the unit half
+//                q_hat = q * rsqrt(|q_half|^2 + 1e-6) (memory.py:136-138),
+//                written as tf32 hi / lo in codebook-major [H*2][M][half]
+//                for the score kernel (and as float32 [M,H,2,half] when the
+//                aux queries are requested);
+//                columns [NR, NR + d): gate = silu(acc + b_gate).
+//   BIAS         y = acc + bias.
+#include "tc_pipeline.cuh"
+
+namespace ml {
+
+namespace {
+
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr int BN_MAX = 256;
+
+enum { EPI_ROUTER_GATE = 0, EPI_BIAS = 1 };
+
+struct ProjArgs {
+  int64_t M;
+  int N, K;
+  const float* bias;   // [N] or nullptr
+  // ROUTER_GATE
+  int NR;              // router columns H * d_key
+  int half;            // d_key / 2 (32, 64 or 128)
+  int hc_count;        // H * 2
+  float* q_hi;         // [hc][M][half]
+  float* q_lo;
+  float* qlen;         // [M][hc]
+  float* qn;           // [M][hc][half] or nullptr
+  float* gate;         // [M][N - NR]
+  // BIAS
+  float* out;          // [M][N]
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    proj_gemm_tc_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
+                        const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
+                        ProjArgs G, tc::PipeShape P, int m_tiles, int n_tiles, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  tc::PipeCtl* ctl = reinterpret_cast<tc::PipeCtl*>(smem);
+  uint8_t* tiles = smem + 1024;
+  volatile int* abort = &ctl->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = m_tiles * n_tiles;
+  // unit u = (n tile, m tile), m fastest: neighbouring CTAs share the B tile
+  auto coords = [&](int u, int& arow, int& brow0, int& nch) {
+    const int nt = u / m_tiles, mt = u - nt * m_tiles;
+    arow = mt * tc::PIPE_M;
+    brow0 = nt * P.BN;
+    nch = 1;
+  };
+  const uint32_t tmem_base = tc::pipe_init(ctl, P, EPI_WARPS);
+
+  if (warp == 0) {
+    if (lane == 0) tc::pipe_produce(ctl, P, tiles, units, &tA_hi, &tA_lo, &tB_hi, &tB_lo, coords, err);
+  } else if (warp == 1) {
+    if (lane == 0) tc::pipe_mma(ctl, P, tiles, units, tmem_base, coords, err);
+  } else {
+    const int quarter = warp & 3;
+    const int hf = (warp - 2) >> 2;
+    const int half_bn = P.BN >> 1;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int nt = u / m_tiles, mt = u - nt * m_tiles;
+      const int64_t row = (int64_t)mt * tc::PIPE_M + quarter * 32 + lane;
+      const bool rok = row < G.M;
+      if (!__all_sync(FULL, tc::mbar_wait(&ctl->tfull[acc], aph, abort, err, 14))) break;
+      tc::fence_after_sync();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * tc::PIPE_ACC_STRIDE);
+      const int c0 = hf * half_bn;                 // first tile column of this warp
+      const int n0 = nt * P.BN + c0;               // first output column of this warp
+      const int ncols = min(half_bn, G.N - n0);    // valid columns of this warp
+
+      if (EPI == EPI_ROUTER_GATE && n0 < G.NR) {
+        // router columns: whole query halves (half divides 128, NR % 128 == 0)
+        for (int seg = 0; seg < ncols; seg += G.half) {
+          const int ns = n0 + seg;                  // first column of this query half
+          const int hc = ns / G.half;               // head * 2 + half
+          float ss = 0.f;
+          for (int cc = 0; cc < G.half; cc += 16) {
+            uint32_t r[16];
+            tc::tmem_ld16(taddr + c0 + seg + cc, r);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const float q = __uint_as_float(r[t]) + (G.bias ? __ldg(&G.bias[ns + cc + t]) : 0.f);
+              ss = fmaf(q, q, ss);
+            }
+          }
+          const float tt = ss + 1e-6f;
+          const float rn = 1.0f / sqrtf(tt);
+          if (rok) G.qlen[row * G.hc_count + hc] = sqrtf(tt) / sqrtf((float)G.half);
+          float* dhi = G.q_hi ? G.q_hi + ((int64_t)hc * G.M + row) * G.half : nullptr;
+          float* dlo = G.q_lo ? G.q_lo + ((int64_t)hc * G.M + row) * G.half : nullptr;
+          float* dqn = G.qn ? G.qn + (row * G.hc_count + hc) * G.half : nullptr;
+          for (int cc = 0; cc < G.half; cc += 16) {
+            uint32_t r[16];
+            tc::tmem_ld16(taddr + c0 + seg + cc, r);
+            tc::tmem_wait_ld();
+            if (rok && dhi) {
+              float hi[16], lo[16], qv[16];
+#pragma unroll
+              for (int t = 0; t < 16; ++t) {
+                const float q = __uint_as_float(r[t]) + (G.bias ? __ldg(&G.bias[ns + cc + t]) : 0.f);
+                qv[t] = q * rn;
+                hi[t] = tc::to_tf32(qv[t]);
+                lo[t] = tc::to_tf32(qv[t] - hi[t]);
+              }
+#pragma unroll
+              for (int t = 0; t < 16; t += 4) {
+                *reinterpret_cast<float4*>(dhi + cc + t) = make_float4(hi[t], hi[t + 1], hi[t + 2], hi[t + 3]);
+                *reinterpret_cast<float4*>(dlo + cc + t) = make_float4(lo[t], lo[t + 1], lo[t + 2], lo[t + 3]);
+                if (dqn) *reinterpret_cast<float4*>(dqn + cc + t) = make_float4(qv[t], qv[t + 1], qv[t + 2], qv[t + 3]);
+              }
+            } else if (rok && dqn) {
+#pragma unroll
+              for (int t = 0; t < 16; ++t)
+                dqn[cc + t] = (__uint_as_float(r[t]) + (G.bias ? __ldg(&G.bias[ns + cc + t]) : 0.f)) * rn;
+            }
+          }
+        }
+      } else {
+        // gate columns (silu) or plain bias columns
+        const int ld = EPI == EPI_ROUTER_GATE ? G.N - G.NR : G.N;
+        float* dst = EPI == EPI_ROUTER_GATE ? G.gate + row * ld + (n0 - G.NR) : G.out + row * ld + n0;
+        for (int cc = 0; cc < ncols; cc += 16) {
+          uint32_t r[16];
+          tc::tmem_ld16(taddr + c0 + cc, r);
+          tc::tmem_wait_ld();
+          if (rok) {
+            float v[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              float x = __uint_as_float(r[t]) + ((G.bias && cc + t < ncols) ? __ldg(&G.bias[n0 + cc + t]) : 0.f);
+              if (EPI == EPI_ROUTER_GATE) x = x / (1.0f + expf(-x));      // model.py:118 silu
+              v[t] = x;
+            }
+            if (cc + 16 <= ncols) {
+#pragma unroll
+              for (int t = 0; t < 16; t += 4)
+                *reinterpret_cast<float4*>(dst + cc + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+            } else {
+#pragma unroll
+              for (int t = 0; t < 16; ++t)
+                if (cc + t < ncols) dst[cc + t] = v[t];
+            }
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ctl->tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+  }
+  tc::pipe_finish(ctl, tmem_base);
+}
+
+inline int bn_for(int N) { return N >= BN_MAX ? BN_MAX : ((N + 15) / 16) * 16; }
+
+template <int EPI>
+cudaError_t launch_proj(const ProjArgs& G, const float* a_hi, const float* a_lo, const float* b_hi,
+                        const float* b_lo, int* err, cudaStream_t s) {
+  if (G.M == 0) return cudaSuccess;
+  const int BN = bn_for(G.N);
+  tc::PipeShape P = tc::pipe_shape(BN, G.K, 0);
+  CUtensorMap m[4];
+  cudaError_t e;
+  if ((e = make_tmap_f32(&m[0], a_hi, G.M, G.K, tc::PIPE_M)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[1], a_lo, G.M, G.K, tc::PIPE_M)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[2], b_hi, G.N, G.K, BN)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[3], b_lo, G.N, G.K, BN)) != cudaSuccess) return e;
+  const size_t smem = 2048 + (size_t)P.stages * P.stage_bytes;
+  auto kern = proj_gemm_tc_kernel<EPI>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+    return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int m_tiles = (int)((G.M + tc::PIPE_M - 1) / tc::PIPE_M), n_tiles = (G.N + BN - 1) / BN;
+  const int units = m_tiles * n_tiles;
+  kern<<<units < sms ? units : sms, THREADS, smem, s>>>(m[0], m[1], m[2], m[3], G, P, m_tiles, n_tiles, err);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---- operand preparation ------------------------------------------------------
+// x -> (rna_tf32(x), rna_tf32(x - hi)), elementwise.
+__global__ void split_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t n4 = n / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+    float4 h, l;
+    h.x = tc::to_tf32(v.x); l.x = tc::to_tf32(v.x - h.x);
+    h.y = tc::to_tf32(v.y); l.y = tc::to_tf32(v.y - h.y);
+    h.z = tc::to_tf32(v.z); l.z = tc::to_tf32(v.z - h.z);
+    h.w = tc::to_tf32(v.w); l.w = tc::to_tf32(v.w - h.w);
+    reinterpret_cast<float4*>(hi)[i] = h;
+    reinterpret_cast<float4*>(lo)[i] = l;
+  }
+  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    hi[i] = tc::to_tf32(v);
+    lo[i] = tc::to_tf32(v - hi[i]);
+  }
+}
+
+// W [K, N] row-major (a Dense kernel) -> rows [row0, row0 + N) of a K-major
+// [*, K] matrix, split into tf32 hi / lo.  32 x 32 tiles through shared memory.
+__global__ void transpose_split_kernel(const float* __restrict__ W, int K, int N, float* __restrict__ hi,
+                                       float* __restrict__ lo, int row0) {
+  __shared__ float t[32][33];
+  const int n_base = blockIdx.x * 32, k_base = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int k = k_base + i, n = n_base + threadIdx.x;
+    t[i][threadIdx.x] = (k < K && n < N) ? W[(int64_t)k * N + n] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int n = n_base + i, k = k_base + threadIdx.x;
+    if (n < N && k < K) {
+      const float v = t[threadIdx.x][i];
+      const float h = tc::to_tf32(v);
+      hi[(int64_t)(row0 + n) * K + k] = h;
+      lo[(int64_t)(row0 + n) * K + k] = tc::to_tf32(v - h);
+    }
+  }
+}
+
+__global__ void concat_bias_kernel(const float* __restrict__ a, int na, const float* __restrict__ b, int nb,
+                                   float* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < na + nb; i += gridDim.x * blockDim.x)
+    out[i] = i < na ? (a ? a[i] : 0.f) : (b ? b[i - na] : 0.f);
+}
+
+}  // namespace
+
+bool proj_tc_supported(const Dims& D) {
+  const int NR = D.H * D.dk;
+  return D.M >= tc::PIPE_M && D.dm % tc::PIPE_K == 0 && D.d % tc::PIPE_K == 0 && NR % 128 == 0 &&
+         (D.half == 32 || D.half == 64 || D.half == 128) && D.d % 16 == 0 && (D.dm >= BN_MAX || D.dm % 16 == 0) &&
+         D.M < (1ll << 31);
+}
+
+cudaError_t launch_split(const float* x, int64_t n, float* hi, float* lo, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  int64_t blocks = (n / 4 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  split_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, n, hi, lo);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_split(const float* W, int K, int N, float* hi, float* lo, int row0, cudaStream_t s) {
+  dim3 grid((N + 31) / 32, (K + 31) / 32), block(32, 8);
+  transpose_split_kernel<<<grid, block, 0, s>>>(W, K, N, hi, lo, row0);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_concat_bias(const float* a, int na, const float* b, int nb, float* out, cudaStream_t s) {
+  concat_bias_kernel<<<(na + nb + 255) / 256, 256, 0, s>>>(a, na, b, nb, out);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router_gate_tc(const Dims& D, const Work& W, const float* bias_rg, float* qn_out,
+                                  cudaStream_t s) {
+  ProjArgs G{};
+  G.M = D.M;
+  G.NR = D.H * D.dk;
+  G.N = G.NR + D.d;
+  G.K = D.dm;
+  G.bias = bias_rg;
+  G.half = D.half;
+  G.hc_count = D.H * 2;
+  G.q_hi = W.q_hi;
+  G.q_lo = W.q_lo;
+  G.qlen = W.qlen;
+  G.qn = qn_out;
+  G.gate = W.gate;
+  return launch_proj<EPI_ROUTER_GATE>(G, W.h_hi, W.h_lo, W.wrg_hi, W.wrg_lo, W.err, s);
+}
+
+cudaError_t launch_out_tc(const Dims& D, const Work& W, const float* b_out, float* y, cudaStream_t s) {
+  ProjArgs G{};
+  G.M = D.M;
+  G.N = D.dm;
+  G.K = D.d;
+  G.bias = b_out;
+  G.out = y;
+  return launch_proj<EPI_BIAS>(G, W.memg_hi, W.memg_lo, W.wo_hi, W.wo_lo, W.err, s);
+}
+
+}  // namespace ml

@@ -30,42 +30,36 @@
 
 #include <mutex>
 
-#include "tc_common.cuh"
+#include "tc_pipeline.cuh"
 
 namespace ml {
 
 namespace {
 
-constexpr int TC_M = 128;          // tokens per tile (UMMA M)
-constexpr int TC_K = 32;           // float32 elements per 128-byte swizzled row
+constexpr int TC_M = tc::PIPE_M;   // tokens per tile (UMMA M)
+constexpr int TC_K = tc::PIPE_K;   // float32 elements per 128-byte swizzled row
 constexpr int EPI_WARPS = 8;
 constexpr int TC_THREADS = 64 + 32 * EPI_WARPS;
-constexpr int TMEM_COLS = 512;
-constexpr int ACC_STRIDE = 256;    // TMEM columns per accumulator buffer
-constexpr int SMEM_LIMIT = 227 * 1024;
+constexpr int ACC_STRIDE = tc::PIPE_ACC_STRIDE;
 
 struct TcShape {
-  int BN;        // keys per MMA / chunk
-  int stages;    // smem ring depth
-  int kchunks;   // half / 32
+  tc::PipeShape P;
   int m_tiles;
   int n_chunks;
-  uint32_t a_bytes, b_bytes, stage_bytes, merge_off;
+  uint32_t merge_off;
 };
 
-struct Ctl {
-  uint64_t full[8], empty[8], tfull[2], tempty[2], pair[4];
-  uint32_t tmem_base;
-  int abort;
-};
+// Smallest float32 strictly greater than v (v not NaN, v < +inf).
+__device__ __forceinline__ float succ_f32(float v) {
+  if (v == 0.f) return __int_as_float(1);
+  const int b = __float_as_int(v);
+  return __int_as_float(v > 0.f ? b + 1 : b - 1);
+}
 
-// Bounded rendezvous of the two epilogue warps that share a TMEM lane quarter.
-__device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t& parity, int lane, volatile int* abort, int* err) {
-  __syncwarp();
-  if (lane == 0) tc::mbar_arrive(bar);
-  const bool ok = tc::mbar_wait(bar, parity, abort, err, 15);
-  parity ^= 1;
-  return __all_sync(FULL, ok);
+// Index of the single set bit of a one-hot 16-bit word, on the ALU pipe.
+__device__ __forceinline__ int low_bit_index16(uint32_t low) {
+  return ((low & 0xFF00u) ? 8 : 0) | ((low & 0xF0F0u) ? 4 : 0) | ((low & 0xCCCCu) ? 2 : 0) |
+         ((low & 0xAAAAu) ? 1 : 0);
 }
 
 // a[t] for a runtime t in [0, 16): select tree, no local memory.
@@ -141,7 +135,7 @@ struct RowState {
   }
 };
 
-template <int KM, bool NOISY, bool BAL>
+template <int KM, bool NOISY, bool BAL, bool QS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     score_topk_tc_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
                          const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
@@ -151,117 +145,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                          float* __restrict__ row_sum, int* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Ctl* ctl = reinterpret_cast<Ctl*>(smem);
+  tc::PipeCtl* ctl = reinterpret_cast<tc::PipeCtl*>(smem);
   uint8_t* tiles = smem + 1024;
   volatile int* abort = &ctl->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = S.m_tiles * D.H * 2;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S.stages; ++s) {
-      tc::mbar_init(&ctl->full[s], 1);
-      tc::mbar_init(&ctl->empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      tc::mbar_init(&ctl->tfull[b], 1);
-      tc::mbar_init(&ctl->tempty[b], EPI_WARPS);
-    }
-    for (int q = 0; q < 4; ++q) tc::mbar_init(&ctl->pair[q], 2);
-    ctl->abort = 0;
-    tc::fence_mbar_init();
-  }
-  if (warp == 1) tc::tmem_alloc(&ctl->tmem_base, TMEM_COLS);
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem_base = ctl->tmem_base;
+  const tc::PipeShape& P = S.P;
+  // unit u = (codebook hc, 128-token tile mt): A rows of q in [hc][M][half],
+  // B rows of the codebook's keys in [hc][n][half]
+  auto coords = [&](int u, int& arow, int& brow0, int& nch) {
+    const int hc = u / S.m_tiles, mt = u - hc * S.m_tiles;
+    arow = (int)(hc * D.M + (int64_t)mt * TC_M);
+    brow0 = hc * D.n;
+    nch = S.n_chunks;
+  };
+  const uint32_t tmem_base = tc::pipe_init(ctl, P, EPI_WARPS);
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      tc::prefetch_tmap(&tA_hi);
-      tc::prefetch_tmap(&tA_lo);
-      tc::prefetch_tmap(&tB_hi);
-      tc::prefetch_tmap(&tB_lo);
-      int s = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-        const int hc = u / S.m_tiles, mt = u - hc * S.m_tiles;
-        const int arow = (int)(hc * D.M + (int64_t)mt * TC_M);
-        for (int j = 0; ok && j < S.n_chunks; ++j) {
-          const int brow = hc * D.n + j * S.BN;
-          for (int kc = 0; kc < S.kchunks; ++kc) {
-            if (!tc::mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 11)) {
-              ok = false;
-              break;
-            }
-            uint8_t* st = tiles + (size_t)s * S.stage_bytes;
-            tc::mbar_expect_tx(&ctl->full[s], S.stage_bytes);
-            tc::tma_load_2d(st, &tA_hi, &ctl->full[s], kc * TC_K, arow);
-            tc::tma_load_2d(st + S.a_bytes, &tA_lo, &ctl->full[s], kc * TC_K, arow);
-            tc::tma_load_2d(st + 2 * S.a_bytes, &tB_hi, &ctl->full[s], kc * TC_K, brow);
-            tc::tma_load_2d(st + 2 * S.a_bytes + S.b_bytes, &tB_lo, &ctl->full[s], kc * TC_K, brow);
-            if (++s == S.stages) {
-              s = 0;
-              ph ^= 1;
-            }
-          }
-        }
-      }
-    }
+    if (lane == 0) tc::pipe_produce(ctl, P, tiles, units, &tA_hi, &tA_lo, &tB_hi, &tB_lo, coords, err);
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc = tc::idesc_tf32(TC_M, S.BN);
-      int s = 0, acc = 0;
-      uint32_t ph = 0, aph = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-        for (int j = 0; ok && j < S.n_chunks; ++j) {
-          if (!tc::mbar_wait(&ctl->tempty[acc], aph ^ 1, abort, err, 12)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after_sync();
-          const uint32_t d = tmem_base + (uint32_t)(acc * ACC_STRIDE);
-          for (int kc = 0; kc < S.kchunks; ++kc) {
-            if (!tc::mbar_wait(&ctl->full[s], ph, abort, err, 13)) {
-              ok = false;
-              break;
-            }
-            tc::fence_after_sync();
-            const uint32_t a_hi = tc::smem_u32(tiles + (size_t)s * S.stage_bytes);
-            const uint32_t a_lo = a_hi + S.a_bytes, b_hi = a_hi + 2 * S.a_bytes, b_lo = b_hi + S.b_bytes;
-#pragma unroll
-            for (int k8 = 0; k8 < TC_K / 8; ++k8) {
-              const uint32_t off = k8 * 32;  // 8 tf32 = 32 bytes along K inside the swizzled row
-              const uint64_t dah = tc::sdesc_k_sw128(a_hi + off), dal = tc::sdesc_k_sw128(a_lo + off);
-              const uint64_t dbh = tc::sdesc_k_sw128(b_hi + off), dbl = tc::sdesc_k_sw128(b_lo + off);
-              tc::mma_tf32(d, dah, dbh, idesc, (kc | k8) != 0);
-              tc::mma_tf32(d, dah, dbl, idesc, 1);
-              tc::mma_tf32(d, dal, dbh, idesc, 1);
-            }
-            tc::mma_commit(&ctl->empty[s]);  // the stage is free once these MMAs have read it
-            if (++s == S.stages) {
-              s = 0;
-              ph ^= 1;
-            }
-          }
-          if (!ok) break;
-          tc::mma_commit(&ctl->tfull[acc]);  // accumulator complete
-          acc ^= 1;
-          if (acc == 0) aph ^= 1;
-        }
-      }
-    }
+    if (lane == 0) tc::pipe_mma(ctl, P, tiles, units, tmem_base, coords, err);
   } else {
     // ---------------- epilogue: per-row top-k ----------------
     using RS = RowState<KM, NOISY, BAL>;
+    // full half-chunk width and the prefilter's group size (>= k groups)
+    constexpr int HALF_BN_FULL = (KM >= 32 ? 128 : 256) / 2;
+    constexpr int GS = HALF_BN_FULL / KM;
     const int quarter = warp & 3;            // TMEM lane quarter this warp may read
     const int hf = (warp - 2) >> 2;          // column half of every chunk
     const int r_in_tile = quarter * 32 + lane;
-    const int half_bn = S.BN >> 1;
+    const int half_bn = P.BN >> 1;
     const float T = scal[0];
     // merge buffer: [128 rows][KM] values, indices (+ clean-score copies)
     float* mv = reinterpret_cast<float*>(smem + S.merge_off);
@@ -278,7 +191,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int64_t m = (int64_t)mt * TC_M + r_in_tile;
       const bool owner = m < D.M;
       const int64_t row = (m * D.H + h) * 2 + c;
-      const float ql = (owner && D.qscale) ? qlen[row] : 1.f;
+      const float ql = (QS && owner) ? qlen[row] : 1.f;
       const float* grow = (NOISY && owner) ? gumbel + row * D.n : nullptr;
       R.reset();
       for (int j = 0; j < S.n_chunks; ++j) {
@@ -288,65 +201,76 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           break;
         }
         tc::fence_after_sync();
-        const int key0 = j * S.BN;
-        const int valid = min(S.BN, D.n - key0);
+        const int key0 = j * P.BN;
+        const int valid = min(P.BN, D.n - key0);
         const int cb = hf * half_bn, ce = min(cb + half_bn, valid);
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * ACC_STRIDE);
 
-        // pass A: a lower bound of this half-chunk's k-th best selection score
-        // (min over KM group maxima of KM disjoint groups)
-        // (min over k group maxima of k disjoint groups of the half-chunk)
-        float tau = -INFINITY;
+        // pass A: a lower bound of this half-chunk's k-th best selection
+        // score: min over the maxima of HALF_BN_FULL / KM disjoint groups
+        // (at least k groups).  Computed on raw cosines: the scaling
+        // s = (cos * T) [* q_len] is monotone, so it commutes with max / min.
+        float thr_base = -INFINITY;
         if constexpr (!NOISY) {
-          const int gs = half_bn / D.k;
-          if (ce - cb == half_bn && half_bn % 16 == 0 && gs >= 1 && half_bn % D.k == 0 && (gs & (gs - 1)) == 0) {
-            const int gmask = gs - 1;
-            float gmin = INFINITY, gmax = -INFINITY;
+          if (ce - cb == HALF_BN_FULL) {
+            float gmin = INFINITY, carry = -INFINITY;
             for (int cc = cb; cc < ce; cc += 16) {
               uint32_t r[16];
               tc::tmem_ld16(taddr + cc, r);
               tc::tmem_wait_ld();
+              if constexpr (GS >= 16) {
 #pragma unroll
-              for (int t = 0; t < 16; ++t) {
-                float sc0 = __fmul_rn(__uint_as_float(r[t]), T);
-                if (D.qscale) sc0 = __fmul_rn(sc0, ql);
-                gmax = fmaxf(gmax, sc0);
-                if (((cc - cb + t) & gmask) == gmask) {
-                  gmin = fminf(gmin, gmax);
-                  gmax = -INFINITY;
+                for (int t = 0; t < 16; ++t) carry = fmaxf(carry, __uint_as_float(r[t]));
+                if (((cc - cb + 16) % GS) == 0) {
+                  gmin = fminf(gmin, carry);
+                  carry = -INFINITY;
+                }
+              } else {
+#pragma unroll
+                for (int g = 0; g < 16 / GS; ++g) {
+                  float gm = __uint_as_float(r[g * GS]);
+#pragma unroll
+                  for (int t = 1; t < GS; ++t) gm = fmaxf(gm, __uint_as_float(r[g * GS + t]));
+                  gmin = fminf(gmin, gm);
                 }
               }
             }
-            tau = gmin;
+            float tau = __fmul_rn(gmin, T);
+            if constexpr (QS) tau = __fmul_rn(tau, ql);
+            thr_base = tau;
           }
         }
+        if (!owner) thr_base = INFINITY;
 
         // pass B: candidates beating max(tau, list k-th), inserted in lockstep
         for (int cc = cb; cc < ce; cc += 16) {
           uint32_t r[16];
           tc::tmem_ld16(taddr + cc, r);
           tc::tmem_wait_ld();
+          const int nv = min(16, ce - cc);
           float sel[16], scr[NOISY ? 16 : 1];
           uint32_t mask = 0, cmask = 0;
+          // s > v[KM-1] and s >= tau  <=>  s >= max(tau, succ(v[KM-1]))
+          const float thr = fmaxf(thr_base, succ_f32(R.v[KM - 1]));
+          const float cthr = RS::CLEAN ? (owner ? succ_f32(R.cv[KM - 1]) : INFINITY) : 0.f;
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
             const float cosv = __uint_as_float(r[t]);
             float score = __fmul_rn(cosv, T);                          // memory.py:150
-            if (D.qscale) score = __fmul_rn(score, ql);                // memory.py:151-152
+            if constexpr (QS) score = __fmul_rn(score, ql);            // memory.py:151-152
             float s_sel = score;
-            const bool in = owner && (cc + t < ce);
             if constexpr (NOISY) {
-              const float g = in ? grow[key0 + cc + t] : 0.f;
+              const float g = (owner && t < nv) ? grow[key0 + cc + t] : 0.f;
               s_sel = __fadd_rn(score, __fmul_rn(D.noise_coef, g));    // memory.py:158
               scr[t] = score;
             }
             sel[t] = s_sel;
-            if (in && s_sel >= tau && s_sel > R.v[KM - 1]) mask |= 1u << t;
+            if (s_sel >= thr) mask |= 1u << t;
             if constexpr (RS::CLEAN) {
-              if (in && score > R.cv[KM - 1]) cmask |= 1u << t;
+              if (score >= cthr) cmask |= 1u << t;
             }
             if constexpr (BAL) {
-              if (in) {
+              if (owner && t < nv) {
                 const float p = D.btgrad ? score : __fmul_rn(cosv, T);  // memory.py:211
                 if (p > R.rmax) {
                   R.rsum = R.rsum * expf(R.rmax - p) + 1.f;
@@ -357,10 +281,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               }
             }
           }
+          if (nv < 16) {
+            mask &= (1u << nv) - 1u;
+            cmask &= (1u << nv) - 1u;
+          }
           while (__any_sync(FULL, mask != 0)) {
             if (mask) {
-              const int t = __ffs(mask) - 1;
-              mask &= mask - 1;
+              const uint32_t low = mask & (0u - mask);
+              mask ^= low;
+              const int t = low_bit_index16(low);
               const float s = pick16(sel, t);
               if (s > R.v[KM - 1]) {
                 if constexpr (NOISY)
@@ -373,8 +302,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if constexpr (RS::CLEAN) {
             while (__any_sync(FULL, cmask != 0)) {
               if (cmask) {
-                const int t = __ffs(cmask) - 1;
-                cmask &= cmask - 1;
+                const uint32_t low = cmask & (0u - cmask);
+                cmask ^= low;
+                const int t = low_bit_index16(low);
                 const float s = pick16(scr, t);
                 if (s > R.cv[KM - 1]) list_insert<KM>(R.cv, R.cix, s, key0 + cc + t);
               }
@@ -403,7 +333,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           mrow[2 * r_in_tile + 1] = R.rsum;
         }
       }
-      if (!pair_sync(pb, pph, lane, abort, err)) break;
+      if (!tc::pair_sync(pb, pph, lane, abort, err)) break;
       if (hf == 0) {
         bool done = !owner;
         for (int j = 0; __any_sync(FULL, !done) && j < KM; ++j) {
@@ -428,7 +358,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       if constexpr (RS::CLEAN) {
-        if (!pair_sync(pb, pph, lane, abort, err)) break;
+        if (!tc::pair_sync(pb, pph, lane, abort, err)) break;
         if (hf == 1) {
 #pragma unroll
           for (int j = 0; j < KM; ++j) {
@@ -436,7 +366,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mi[r_in_tile * KM + j] = R.cix[j];
           }
         }
-        if (!pair_sync(pb, pph, lane, abort, err)) break;
+        if (!tc::pair_sync(pb, pph, lane, abort, err)) break;
         if (hf == 0) {
           bool done = !owner;
           for (int j = 0; __any_sync(FULL, !done) && j < KM; ++j) {
@@ -467,16 +397,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           row_sum[row] = R.rsum;
         }
       }
-      if (!pair_sync(pb, pph, lane, abort, err)) break;   // the merge buffer is reused by the next unit
+      if (!tc::pair_sync(pb, pph, lane, abort, err)) break;   // the merge buffer is reused by the next unit
     }
   }
 
-  tc::fence_before_sync();
-  __syncthreads();
-  if (warp == 1) {
-    tc::fence_after_sync();
-    tc::tmem_dealloc(tmem_base, TMEM_COLS);
-  }
+  tc::pipe_finish(ctl, tmem_base);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -505,33 +430,26 @@ inline uint32_t merge_bytes(const Dims& D) {
 
 TcShape tc_shape(const Dims& D) {
   TcShape S;
-  S.BN = bn_for(D);
-  S.kchunks = D.half / TC_K;
+  S.P = tc::pipe_shape(bn_for(D), D.half, merge_bytes(D));
   S.m_tiles = (int)((D.M + TC_M - 1) / TC_M);
-  S.n_chunks = (D.n + S.BN - 1) / S.BN;
-  S.a_bytes = TC_M * TC_K * 4;
-  S.b_bytes = S.BN * TC_K * 4;
-  S.stage_bytes = 2 * S.a_bytes + 2 * S.b_bytes;
-  const uint32_t fixed = 2048 + merge_bytes(D);
-  S.stages = (int)((SMEM_LIMIT - fixed) / S.stage_bytes);
-  if (S.stages > 6) S.stages = 6;
-  S.merge_off = 1024 + S.stages * S.stage_bytes;
+  S.n_chunks = (D.n + S.P.BN - 1) / S.P.BN;
+  S.merge_off = 1024 + S.P.stages * S.P.stage_bytes;
   return S;
 }
 
-template <int KM, bool NOISY, bool BAL>
+template <int KM, bool NOISY, bool BAL, bool QS>
 cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaStream_t s) {
   TcShape S = tc_shape(D);
-  if (S.stages < 2) return cudaErrorInvalidConfiguration;
+  if (S.P.stages < 2) return cudaErrorInvalidConfiguration;
   CUtensorMap m[4];
   cudaError_t e;
   const uint64_t arows = (uint64_t)D.M * D.H * 2, brows = (uint64_t)D.n * D.H * 2;
   if ((e = make_tmap_f32(&m[0], W.q_hi, arows, D.half, TC_M)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[1], W.q_lo, arows, D.half, TC_M)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[2], W.k_hi, brows, D.half, S.BN)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[3], W.k_lo, brows, D.half, S.BN)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[2], W.k_hi, brows, D.half, S.P.BN)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[3], W.k_lo, brows, D.half, S.P.BN)) != cudaSuccess) return e;
   const size_t smem = 1024 + (size_t)S.merge_off + merge_bytes(D);
-  auto kern = score_topk_tc_kernel<KM, NOISY, BAL>;
+  auto kern = score_topk_tc_kernel<KM, NOISY, BAL, QS>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
     return e;
   int dev = 0, sms = 148;
@@ -545,10 +463,16 @@ cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaS
   return cudaGetLastError();
 }
 
+template <int KM, bool QS>
+cudaError_t launch_tc_q(const Dims& D, const Work& W, const float* gumbel, bool bal, cudaStream_t s) {
+  if (D.noisy)
+    return bal ? launch_tc_t<KM, true, true, QS>(D, W, gumbel, s) : launch_tc_t<KM, true, false, QS>(D, W, gumbel, s);
+  return bal ? launch_tc_t<KM, false, true, QS>(D, W, gumbel, s) : launch_tc_t<KM, false, false, QS>(D, W, gumbel, s);
+}
+
 template <int KM>
 cudaError_t launch_tc_k(const Dims& D, const Work& W, const float* gumbel, bool bal, cudaStream_t s) {
-  if (D.noisy) return bal ? launch_tc_t<KM, true, true>(D, W, gumbel, s) : launch_tc_t<KM, true, false>(D, W, gumbel, s);
-  return bal ? launch_tc_t<KM, false, true>(D, W, gumbel, s) : launch_tc_t<KM, false, false>(D, W, gumbel, s);
+  return D.qscale ? launch_tc_q<KM, true>(D, W, gumbel, bal, s) : launch_tc_q<KM, false>(D, W, gumbel, bal, s);
 }
 
 }  // namespace

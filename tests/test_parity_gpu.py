@@ -157,6 +157,13 @@ SHAPES = {
     "btgrad_bf16": dict(n_sub_keys=128, heads=4, d_key=64, d_value=128, top_k=8, M=512, seed=36, query_scale=True,
                         balance_temperature_grad=True, values_dtype="bf16"),
     "k4_n64": dict(n_sub_keys=64, heads=1, d_key=64, d_value=16, top_k=4, M=130, seed=37),
+    # layer block with tensor-core projections (M >= 128), biases on, ragged M
+    "layer_cfg1_m300": dict(n_sub_keys=512, heads=4, d_key=128, d_value=256, top_k=16, M=300, seed=38, layer=True,
+                            d_model=256, biases=True, values_dtype="fp16"),
+    "layer_h8_m257": dict(n_sub_keys=256, heads=8, d_key=64, d_value=64, top_k=32, M=257, seed=39, layer=True,
+                          d_model=96, biases=True),
+    "layer_qscale_noise": dict(n_sub_keys=128, heads=2, d_key=256, d_value=128, top_k=8, M=384, seed=40, layer=True,
+                               d_model=128, query_scale=True, noise=1.0, train=True, clustered=True),
 }
 
 
@@ -181,3 +188,7 @@ def test_gpu_shapes_against_oracle(name):
     assert abs(float(got["balance_loss"]) - float(orc["aux"]["balance_loss"])) <= 1e-5 * float(orc["aux"]["balance_loss"])
     if swapped == 0:
         np.testing.assert_array_equal(got["subkey_counts"], orc["aux"]["subkey_counts"])
+        if "y" in orc:
+            assert_rel(got["y"], orc["y"], tol if recipe.get("values_dtype") else OUT_RTOL_F32, "y")
+    if recipe.get("layer"):
+        assert_rel(got["queries"].reshape(M, H, 2, -1), orc["route"]["q"], 1e-5, "unit queries")
