@@ -8,9 +8,10 @@
 //      (i, j) is dominated by every (i', j') with i' <= i, j' <= j, which
 //      rank ahead of it under (value desc, flat index asc); with
 //      (i+1)(j+1) > k at least k candidates rank ahead, so only the
-//      candidates with (i+1)(j+1) <= k can be selected.  The top-k of those
-//      is taken by k rounds of warp arg-max with lowest-flat-index ties,
-//      which is lax.top_k's order on the full k*k list (memory.py:171);
+//      candidates with (i+1)(j+1) <= k can be selected (8 / 20 / 50 / 119
+//      of them for k = 4 / 8 / 16 / 32).  Those are sorted across the warp
+//      by a bitonic network on (value desc, flat index asc), which is
+//      lax.top_k's order on the full k*k list (memory.py:171);
 //   2. turns the k winners into slot ids idx_a * n + idx_b (memory.py:172-175)
 //      and softmax weights (memory.py:178);
 //   3. streams its k value rows (16-byte loads, float32 accumulation in
@@ -40,15 +41,70 @@ __device__ __forceinline__ void load_group(const VT* p, float (&o)[VEC]) {
   }
 }
 
+// Eligible stage-2 candidates (i, j) with (i+1)(j+1) <= k, row-major.
+struct PairTable {
+  uint16_t ij[128];  // i | j << 8
+  int count;
+};
+
+// Bitonic sort of 32*C (value, flat) pairs held C per lane (position
+// lane*C + r) into (value desc, flat asc) order.  Flats must be distinct.
+template <int C>
+__device__ __forceinline__ void warp_sort_desc(float (&v)[C], int (&f)[C], int lane) {
+  constexpr int N = 32 * C;
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride < C) {
+#pragma unroll
+        for (int r = 0; r < C; ++r) {
+          const int rp = r ^ stride;
+          if (rp > r) {
+            const bool desc = ((lane * C + r) & size) == 0;
+            const bool swap = desc ? ranks_before(v[rp], f[rp], v[r], f[r]) : ranks_before(v[r], f[r], v[rp], f[rp]);
+            if (swap) {
+              const float tv = v[r];
+              v[r] = v[rp];
+              v[rp] = tv;
+              const int tf = f[r];
+              f[r] = f[rp];
+              f[rp] = tf;
+            }
+          }
+        }
+      } else {
+        const int ls = stride / C;
+#pragma unroll
+        for (int r = 0; r < C; ++r) {
+          const float ov = __shfl_xor_sync(FULL, v[r], ls);
+          const int of = __shfl_xor_sync(FULL, f[r], ls);
+          const bool lower = (lane & ls) == 0;
+          const bool desc = ((lane * C + r) & size) == 0;
+          const bool mine_better = ranks_before(v[r], f[r], ov, of);
+          if (mine_better != (lower == desc)) {
+            v[r] = ov;
+            f[r] = of;
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int KM, typename VT, int VEC, int CH>
 __global__ void __launch_bounds__(1024) combine_gather_kernel(
-    Dims D, const int* __restrict__ sub_idx, const float* __restrict__ sub_score, const float* __restrict__ sub_sel,
+    Dims D, const __grid_constant__ PairTable pairs, const int* __restrict__ sub_idx,
+    const float* __restrict__ sub_score, const float* __restrict__ sub_sel,
     const VT* __restrict__ values, int* __restrict__ slots, float* __restrict__ weights, float* __restrict__ out,
     float* __restrict__ memg, float* __restrict__ memg_hi, float* __restrict__ memg_lo,
     const float* __restrict__ gate, float* __restrict__ slot_counts, float* __restrict__ subkey_counts,
     float* __restrict__ top1_part) {
   extern __shared__ float red[];  // [H][d]
-  constexpr int CPL = (KM * KM + 31) / 32;
+  __shared__ uint16_t tab[128];   // pair table, staged for divergent per-lane reads
+  constexpr int C = KM <= 8 ? 1 : KM <= 16 ? 2 : 4;   // candidate slots per lane (32*C >= eligible count)
+  for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
+  __syncthreads();
   const int64_t m = blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k = D.k, d = D.d;
@@ -62,42 +118,27 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
   const int ai = lk ? sub_idx[ra + lane] : 0;
   const int bi = lk ? sub_idx[rb + lane] : 0;
 
-  // candidate f = lane + 32 t  (i = f / k, j = f % k)
-  float cv[CPL];
-  uint32_t used = 0;
+  // eligible candidates into slots lane*C + r; padding ranks last
+  float cv[C];
+  int cf[C];
 #pragma unroll
-  for (int t = 0; t < CPL; ++t) {
-    const int f = lane + 32 * t;
-    const int i = f / k, j = f - (f / k) * k;
-    const float x = __shfl_sync(FULL, as, i & 31);
-    const float y = __shfl_sync(FULL, bs, j & 31);
-    const bool ok = f < k * k && (i + 1) * (j + 1) <= k;
-    cv[t] = x + y;
-    if (!ok) used |= 1u << t;
+  for (int r = 0; r < C; ++r) {
+    const int slot = lane * C + r;
+    const bool ok = slot < pairs.count;
+    const int ij = ok ? tab[slot] : 0;
+    const int i = ij & 0xFF, j = ij >> 8;
+    const float x = __shfl_sync(FULL, as, i);
+    const float y = __shfl_sync(FULL, bs, j);
+    cv[r] = ok ? x + y : -INFINITY;                  // memory.py:168 cand_select
+    cf[r] = ok ? i * k + j : (1 << 30) + slot;       // flat index in the k*k grid
   }
+  warp_sort_desc<C>(cv, cf, lane);
+  // lane r < k takes sorted position r
   int my_flat = 0;
-  for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
-    int bf = INT_MAX;
 #pragma unroll
-    for (int t = 0; t < CPL; ++t) {
-      const int f = lane + 32 * t;
-      if (!((used >> t) & 1u) && ranks_before(cv[t], f, bv, bf)) {
-        bv = cv[t];
-        bf = f;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(FULL, bv, o);
-      const int of = __shfl_xor_sync(FULL, bf, o);
-      if (ranks_before(ov, of, bv, bf)) {
-        bv = ov;
-        bf = of;
-      }
-    }
-    if (lane == (bf & 31)) used |= 1u << (bf >> 5);
-    if (lane == r) my_flat = bf;
+  for (int r = 0; r < C; ++r) {
+    const int f = __shfl_sync(FULL, cf[r], lane / C);
+    if ((lane % C) == r) my_flat = f;
   }
   const int fi = lk ? my_flat / k : 0, fj = lk ? my_flat - (my_flat / k) * k : 0;
   const float s = __shfl_sync(FULL, ac, fi) + __shfl_sync(FULL, bc, fj);     // memory.py:172
@@ -168,12 +209,22 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
   }
 }
 
+inline PairTable make_pairs(int k) {
+  PairTable t{};
+  int c = 0;
+  for (int i = 0; i < k; ++i)
+    for (int j = 0; j < k && (i + 1) * (j + 1) <= k; ++j) t.ij[c++] = (uint16_t)(i | (j << 8));
+  t.count = c;
+  return t;
+}
+
 template <int KM, typename VT, int VEC>
 cudaError_t launch_ch(const Dims& D, int ch, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Work& W,
                       const VT* values, int* slots, float* weights, float* out, float* memg, float* mhi, float* mlo,
                       const float* gate, float* slot_counts, float* subkey_counts) {
+  const PairTable pairs = make_pairs(D.k);
 #define ML_CG(CHV)                                                                                             \
-  combine_gather_kernel<KM, VT, VEC, CHV><<<grid, block, smem, s>>>(D, W.sub_idx, W.sub_score, W.sub_sel,    \
+  combine_gather_kernel<KM, VT, VEC, CHV><<<grid, block, smem, s>>>(D, pairs, W.sub_idx, W.sub_score, W.sub_sel, \
                                                                     values, slots, weights, out, memg, mhi, \
                                                                     mlo, gate, slot_counts, subkey_counts,  \
                                                                     W.top1_part)

@@ -52,6 +52,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   tc::PipeCtl* ctl = reinterpret_cast<tc::PipeCtl*>(smem);
   uint8_t* tiles = smem + 1024;
+  // bias vector staged once per CTA (read as a broadcast by every row)
+  float* sbias = reinterpret_cast<float*>(tiles + (size_t)P.stages * P.stage_bytes);
+  for (int i = threadIdx.x; i < G.N; i += blockDim.x) sbias[i] = G.bias ? G.bias[i] : 0.f;
   volatile int* abort = &ctl->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = m_tiles * n_tiles;
@@ -97,7 +100,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::tmem_wait_ld();
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
-              const float q = __uint_as_float(r[t]) + (G.bias ? __ldg(&G.bias[ns + cc + t]) : 0.f);
+              const float q = __uint_as_float(r[t]) + sbias[ns + cc + t];
               ss = fmaf(q, q, ss);
             }
           }
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               float hi[16], lo[16], qv[16];
 #pragma unroll
               for (int t = 0; t < 16; ++t) {
-                const float q = __uint_as_float(r[t]) + (G.bias ? __ldg(&G.bias[ns + cc + t]) : 0.f);
+                const float q = __uint_as_float(r[t]) + sbias[ns + cc + t];
                 qv[t] = q * rn;
                 hi[t] = tc::to_tf32(qv[t]);
                 lo[t] = tc::to_tf32(qv[t] - hi[t]);
@@ -129,7 +132,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             } else if (rok && dqn) {
 #pragma unroll
               for (int t = 0; t < 16; ++t)
-                dqn[cc + t] = (__uint_as_float(r[t]) + (G.bias ? __ldg(&G.bias[ns + cc + t]) : 0.f)) * rn;
+                dqn[cc + t] = (__uint_as_float(r[t]) + sbias[ns + cc + t]) * rn;
             }
           }
         }
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             float v[16];
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
-              float x = __uint_as_float(r[t]) + ((G.bias && cc + t < ncols) ? __ldg(&G.bias[n0 + cc + t]) : 0.f);
+              float x = __uint_as_float(r[t]) + (cc + t < ncols ? sbias[n0 + cc + t] : 0.f);
               if (EPI == EPI_ROUTER_GATE) x = x / (1.0f + expf(-x));      // model.py:118 silu
               v[t] = x;
             }
@@ -171,21 +174,29 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc::pipe_finish(ctl, tmem_base);
 }
 
-inline int bn_for(int N) { return N >= BN_MAX ? BN_MAX : ((N + 15) / 16) * 16; }
+// The router / gate GEMM keeps 256-column tiles (each warp's 128 columns
+// hold whole query halves); narrow GEMMs use 128-column tiles so that more
+// CTAs share the work.
+inline int bn_for(int EPI, int N) {
+  const int cap = EPI == EPI_ROUTER_GATE ? BN_MAX : (N > 256 ? BN_MAX : 128);
+  return N >= cap ? cap : ((N + 15) / 16) * 16;
+}
 
 template <int EPI>
 cudaError_t launch_proj(const ProjArgs& G, const float* a_hi, const float* a_lo, const float* b_hi,
                         const float* b_lo, int* err, cudaStream_t s) {
   if (G.M == 0) return cudaSuccess;
-  const int BN = bn_for(G.N);
-  tc::PipeShape P = tc::pipe_shape(BN, G.K, 0);
+  const int BN = bn_for(EPI, G.N);
+  const uint32_t bias_bytes = ((uint32_t)G.N * 4 + 1023) / 1024 * 1024;
+  tc::PipeShape P = tc::pipe_shape(BN, G.K, bias_bytes);
+  if (P.stages < 2) return cudaErrorInvalidConfiguration;
   CUtensorMap m[4];
   cudaError_t e;
   if ((e = make_tmap_f32(&m[0], a_hi, G.M, G.K, tc::PIPE_M)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[1], a_lo, G.M, G.K, tc::PIPE_M)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[2], b_hi, G.N, G.K, BN)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[3], b_lo, G.N, G.K, BN)) != cudaSuccess) return e;
-  const size_t smem = 2048 + (size_t)P.stages * P.stage_bytes;
+  const size_t smem = 2048 + (size_t)P.stages * P.stage_bytes + bias_bytes;
   auto kern = proj_gemm_tc_kernel<EPI>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
     return e;
@@ -253,6 +264,7 @@ __global__ void concat_bias_kernel(const float* __restrict__ a, int na, const fl
 bool proj_tc_supported(const Dims& D) {
   const int NR = D.H * D.dk;
   return D.M >= tc::PIPE_M && D.dm % tc::PIPE_K == 0 && D.d % tc::PIPE_K == 0 && NR % 128 == 0 &&
+         (NR + D.d) * 4 <= 16384 && D.dm * 4 <= 16384 &&
          (D.half == 32 || D.half == 64 || D.half == 128) && D.d % 16 == 0 && (D.dm >= BN_MAX || D.dm % 16 == 0) &&
          D.M < (1ll << 31);
 }
