@@ -74,6 +74,186 @@ __device__ __forceinline__ float pick16(const float (&a)[16], int t) {
   return (t & 1) ? l2[1] : l2[0];
 }
 
+// ---- sorting networks (all indices compile-time; registers only) ----------
+// Bitonic sort of N values into descending order.
+template <int N>
+__device__ __forceinline__ void sort_desc_v(float (&v)[N]) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int l = i ^ stride;
+        if (l > i) {
+          const float a = v[i], b = v[l];
+          if ((i & size) == 0) {
+            v[i] = fmaxf(a, b);
+            v[l] = fminf(a, b);
+          } else {
+            v[i] = fminf(a, b);
+            v[l] = fmaxf(a, b);
+          }
+        }
+      }
+}
+
+// Bitonic sort of N (value, index) pairs into (value desc, index asc) order.
+template <int N>
+__device__ __forceinline__ void sort_desc_pairs(float (&v)[N], int (&ix)[N]) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int l = i ^ stride;
+        if (l > i) {
+          const bool lb = ranks_before(v[l], ix[l], v[i], ix[i]);
+          const bool swap = ((i & size) == 0) ? lb : !lb;
+          if (swap) {
+            const float tv = v[i];
+            v[i] = v[l];
+            v[l] = tv;
+            const int ti = ix[i];
+            ix[i] = ix[l];
+            ix[l] = ti;
+          }
+        }
+      }
+}
+
+// a := top N of (a, b), both sorted (value desc, index asc); result sorted.
+template <int N>
+__device__ __forceinline__ void merge_top_pairs(float (&a)[N], int (&ia)[N], const float (&b)[N],
+                                                const int (&ib)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    if (ranks_before(b[N - 1 - i], ib[N - 1 - i], a[i], ia[i])) {
+      a[i] = b[N - 1 - i];
+      ia[i] = ib[N - 1 - i];
+    }
+  }
+  // a is now bitonic: clean it into descending order
+#pragma unroll
+  for (int stride = N >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const int l = i ^ stride;
+      if (l > i && ranks_before(a[l], ia[l], a[i], ia[i])) {
+        const float tv = a[i];
+        a[i] = a[l];
+        a[l] = tv;
+        const int ti = ia[i];
+        ia[i] = ia[l];
+        ia[l] = ti;
+      }
+    }
+}
+
+// Exact top-16 of one 128-column half-chunk merged into the running list
+// (clean selection, no query noise).  Returns false (warp-uniform) when a
+// lane's candidates overflow the buffer or the 16th score is tied; the
+// caller then takes the general path for this half-chunk.
+//   A. 32 group maxima (groups of 4); their 16th largest g16 bounds the
+//      half-chunk's 16th largest cosine from below (16 distinct values are
+//      >= g16).  Two 16-sorts give g16 = min_i max(lo[i], hi[15 - i]).
+//   B. scores >= score(g16) go to a per-thread shared-memory buffer (<= 32).
+//   C. value-only top-16 of the buffer: t* = the 16th largest score.
+//   D. second TMEM scan: (score, key) of the values >= t*, in key order;
+//      exactly 16 unless t* is tied.  Sort them and merge into the list.
+// buf: this thread's slot 0; slots are 256 floats apart (bank-conflict free).
+template <bool QS>
+__device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, float ql, bool owner,
+                                           float (&rv)[16], int (&ri)[16], float* buf) {
+  float lo[16], hi[16];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    uint32_t r[16];
+    tc::tmem_ld16(taddr + b * 16, r);
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float m4 = fmaxf(fmaxf(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1])),
+                             fmaxf(__uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+      if (b < 4)
+        lo[b * 4 + g] = m4;
+      else
+        hi[(b - 4) * 4 + g] = m4;
+    }
+  }
+  sort_desc_v<16>(lo);
+  sort_desc_v<16>(hi);
+  float g16 = INFINITY;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) g16 = fminf(g16, fmaxf(lo[i], hi[15 - i]));
+  float tau = __fmul_rn(g16, T);
+  if (QS) tau = __fmul_rn(tau, ql);
+  if (!owner) tau = INFINITY;
+
+  int cnt = 0;
+#pragma unroll 2
+  for (int b = 0; b < 8; ++b) {
+    uint32_t r[16];
+    tc::tmem_ld16(taddr + b * 16, r);
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float sc = __fmul_rn(__uint_as_float(r[t]), T);
+      if (QS) sc = __fmul_rn(sc, ql);
+      if (sc >= tau) {
+        buf[(cnt & 31) * 256] = sc;
+        ++cnt;
+      }
+    }
+  }
+  if (__any_sync(FULL, cnt > 32)) return false;
+
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = i < cnt ? buf[i * 256] : -INFINITY;
+  float va[16], vb[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = v[i];
+    vb[i] = v[16 + i];
+  }
+  sort_desc_v<16>(va);
+  sort_desc_v<16>(vb);
+  float tstar = INFINITY;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) tstar = fminf(tstar, fmaxf(va[i], vb[15 - i]));
+
+  int cnt2 = 0;
+#pragma unroll 2
+  for (int b = 0; b < 8; ++b) {
+    uint32_t r[16];
+    tc::tmem_ld16(taddr + b * 16, r);
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float sc = __fmul_rn(__uint_as_float(r[t]), T);
+      if (QS) sc = __fmul_rn(sc, ql);
+      if (owner && sc >= tstar) {
+        buf[(cnt2 & 15) * 256] = sc;
+        buf[(16 + (cnt2 & 15)) * 256] = __int_as_float(key0 + b * 16 + t);
+        ++cnt2;
+      }
+    }
+  }
+  if (__any_sync(FULL, owner && cnt2 != 16)) return false;
+  float pv[16];
+  int pc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    pv[i] = owner ? buf[i * 256] : -INFINITY;
+    pc[i] = owner ? __float_as_int(buf[(16 + i) * 256]) : (1 << 30) + i;
+  }
+  sort_desc_pairs<16>(pv, pc);
+  merge_top_pairs<16>(rv, ri, pv, pc);
+  return true;
+}
+
 // Insertion of (s, i) at its (value desc, index asc) rank, for any index.
 // Precondition: (s, i) ranks before the list's last element.
 template <int KM>
@@ -168,6 +348,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ---------------- epilogue: per-row top-k ----------------
     using RS = RowState<KM, NOISY, BAL>;
+    constexpr bool FAST16 = KM == 16 && !NOISY && !BAL;
+    float* fbuf = reinterpret_cast<float*>(smem + S.merge_off) + (threadIdx.x - 64);
     // full half-chunk width and the prefilter's group size (>= k groups)
     constexpr int HALF_BN_FULL = (KM >= 32 ? 128 : 256) / 2;
     constexpr int GS = HALF_BN_FULL / KM;
@@ -206,6 +388,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int cb = hf * half_bn, ce = min(cb + half_bn, valid);
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * ACC_STRIDE);
 
+        // exact per-half-chunk top-16 (clean selection), else the general path
+        bool fast_done = false;
+        if constexpr (FAST16) {
+          if (ce - cb == HALF_BN_FULL)
+            fast_done = fast_top16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
+        }
+        if (!fast_done) {
         // pass A: a lower bound of this half-chunk's k-th best selection
         // score: min over the maxima of HALF_BN_FULL / KM disjoint groups
         // (at least k groups).  Computed on raw cosines: the scaling
@@ -311,6 +500,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
         }
+        }  // general path
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ctl->tempty[acc]);
@@ -318,6 +508,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (acc == 0) aph ^= 1;
       }
       if (!ok) break;
+      // the merge buffer aliases the fast-path buffer: both warps of the
+      // quarter must be done with their chunks first
+      if (FAST16 && !tc::pair_sync(&ctl->pair[quarter], pph, lane, abort, err)) break;
 
       // ---- merge the two column halves of each row (warp pair of a quarter)
       uint64_t* pb = &ctl->pair[quarter];
@@ -423,9 +616,13 @@ inline int bn_for(const Dims& D) {
   return D.n >= cap ? cap : ((D.n + 15) / 16) * 16;
 }
 
+// Epilogue shared memory: the row-merge buffer, aliased with the 32-slot
+// per-thread candidate buffer of the k <= 16 clean fast path.
 inline uint32_t merge_bytes(const Dims& D) {
   const uint32_t per = 8u + (D.noisy ? 4u : 0u);
-  return TC_M * D.kmax * per + TC_M * 8u;
+  const uint32_t merge = TC_M * D.kmax * per + TC_M * 8u;
+  const uint32_t fast = 32u * 4u * (TC_THREADS - 64);
+  return merge > fast ? merge : fast;
 }
 
 TcShape tc_shape(const Dims& D) {
