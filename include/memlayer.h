@@ -155,6 +155,12 @@ int32_t memlayer_layer_workspace_size(const memlayer_config* cfg, size_t* bytes)
 int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_args* args,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Device-side status of the last call that used this workspace: 0, or a
+ * code recorded by a kernel (a bounded wait that gave up, an out-of-range
+ * sub-key id).  Copies one word to the host and synchronises `stream`.
+ * Has no counterpart in the reference (its errors are Python exceptions). */
+int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* workspace, int32_t* code, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

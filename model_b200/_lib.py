@@ -79,6 +79,11 @@ class MemlayerLayerArgs(C.Structure):
     ]
 
 
+DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "MMA wait timed out",
+                 14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
+                 21: "sub-key id out of range"}
+
+
 class MemlayerError(RuntimeError):
     """A non-zero memlayer_status."""
 
@@ -110,6 +115,10 @@ def lib() -> C.CDLL:
         L.memlayer_layer_forward.restype = C.c_int32
         L.memlayer_layer_forward.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs), C.c_void_p,
                                              C.c_size_t, C.c_void_p]
+        L.memlayer_workspace_status.restype = C.c_int32
+        L.memlayer_workspace_status.argtypes = [C.POINTER(MemlayerConfig), C.c_void_p, C.POINTER(C.c_int32),
+                                                C.c_void_p]
+        L.memlayer_kernel_launch_count.restype = C.c_int64
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L
@@ -123,3 +132,15 @@ def status_string(status: int) -> str:
 def check(status: int, where: str) -> None:
     if status != OK:
         raise MemlayerError(status, where)
+
+
+def device_status(cfg, workspace_ptr: int, stream_ptr: int) -> int:
+    """The device status word of the last call on this workspace (syncs)."""
+    code = C.c_int32(0)
+    check(lib().memlayer_workspace_status(C.byref(cfg), workspace_ptr, C.byref(code), stream_ptr),
+          "memlayer_workspace_status")
+    return code.value
+
+
+class DeviceError(RuntimeError):
+    """A kernel recorded a failure in the workspace status word."""

@@ -307,4 +307,18 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
   return MEMLAYER_OK;
 }
 
+int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* workspace, int32_t* code, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!workspace || !code) return MEMLAYER_ERR_BAD_POINTER;
+  Work W;
+  layout(D, Flags{}, (char*)workspace, &W);   // the error word sits at the same offset in every layout
+  int v = 0;
+  ML_TRY(cudaMemcpyAsync(&v, W.err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  ML_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+  *code = v;
+  return MEMLAYER_OK;
+}
+
 }  // extern "C"

@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
     const VT* __restrict__ values, int* __restrict__ slots, float* __restrict__ weights, float* __restrict__ out,
     float* __restrict__ memg, float* __restrict__ memg_hi, float* __restrict__ memg_lo,
     const float* __restrict__ gate, float* __restrict__ slot_counts, float* __restrict__ subkey_counts,
-    float* __restrict__ top1_part) {
+    float* __restrict__ top1_part, int* __restrict__ err) {
   extern __shared__ float red[];  // [H][d]
   __shared__ uint16_t tab[128];   // pair table, staged for divergent per-lane reads
   constexpr int C = KM <= 8 ? 1 : KM <= 16 ? 2 : 4;   // candidate slots per lane (32*C >= eligible count)
@@ -142,7 +142,14 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
   }
   const int fi = lk ? my_flat / k : 0, fj = lk ? my_flat - (my_flat / k) * k : 0;
   const float s = __shfl_sync(FULL, ac, fi) + __shfl_sync(FULL, bc, fj);     // memory.py:172
-  const int ia = __shfl_sync(FULL, ai, fi), ib = __shfl_sync(FULL, bi, fj);  // memory.py:173-174
+  int ia = __shfl_sync(FULL, ai, fi), ib = __shfl_sync(FULL, bi, fj);        // memory.py:173-174
+  if (lk && ((unsigned)ia >= (unsigned)D.n || (unsigned)ib >= (unsigned)D.n)) {
+    // a sub-key id out of range can only come from a bug upstream: record
+    // it (status read by the host) and read row 0 instead of faulting
+    atomicCAS(err, 0, 21);
+    ia = 0;
+    ib = 0;
+  }
   const int slot = ia * D.n + ib;                                            // memory.py:175
   const float mx = warp_max(lk ? s : -INFINITY);
   const float e = lk ? expf(s - mx) : 0.f;
@@ -227,7 +234,7 @@ cudaError_t launch_ch(const Dims& D, int ch, dim3 grid, dim3 block, size_t smem,
   combine_gather_kernel<KM, VT, VEC, CHV><<<grid, block, smem, s>>>(D, pairs, W.sub_idx, W.sub_score, W.sub_sel, \
                                                                     values, slots, weights, out, memg, mhi, \
                                                                     mlo, gate, slot_counts, subkey_counts,  \
-                                                                    W.top1_part)
+                                                                    W.top1_part, W.err)
   switch (ch) {
     case 1: ML_CG(1); break;
     case 2: ML_CG(2); break;

@@ -508,12 +508,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (acc == 0) aph ^= 1;
       }
       if (!ok) break;
-      // the merge buffer aliases the fast-path buffer: both warps of the
-      // quarter must be done with their chunks first
-      if (FAST16 && !tc::pair_sync(&ctl->pair[quarter], pph, lane, abort, err)) break;
 
       // ---- merge the two column halves of each row (warp pair of a quarter)
       uint64_t* pb = &ctl->pair[quarter];
+      if constexpr (FAST16) {
+        // through the thread pair's own candidate slots (warp w + 4 is the
+        // partner of warp w): no other thread touches them
+        if (hf == 1) {
+#pragma unroll
+          for (int j = 0; j < KM; ++j) {
+            fbuf[j * 256] = R.v[j];
+            fbuf[(KM + j) * 256] = __int_as_float(R.ix[j]);
+          }
+        }
+        if (!tc::pair_sync(pb, pph, lane, abort, err)) break;
+        if (hf == 0 && owner) {
+          float ov[KM];
+          int oi[KM];
+#pragma unroll
+          for (int j = 0; j < KM; ++j) {
+            ov[j] = fbuf[128 + j * 256];
+            oi[j] = __float_as_int(fbuf[128 + (KM + j) * 256]);
+          }
+          merge_top_pairs<KM>(R.v, R.ix, ov, oi);
+        }
+      } else {
       if (hf == 1) {
 #pragma unroll
         for (int j = 0; j < KM; ++j) {
@@ -574,6 +593,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       }
+      }  // general merge
       if (hf == 0 && owner) {
         const int64_t o = row * D.k;
 #pragma unroll

@@ -32,6 +32,12 @@ def _cuda_f32(t: torch.Tensor, name: str) -> torch.Tensor:
     return t.to(torch.float32).contiguous()
 
 
+def _raise_device_status(cfg, ws: torch.Tensor, stream_ptr: int) -> None:
+    code = L.device_status(cfg, ws.data_ptr(), stream_ptr)
+    if code:
+        raise L.DeviceError(f"device status {code}: {L.DEVICE_ERRORS.get(code, 'unknown')}")
+
+
 def _workspace(nbytes: int, device) -> torch.Tensor:
     # torch's caching allocator hands out 512-byte aligned blocks
     return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
@@ -154,7 +160,7 @@ class MemoryPool:
     def apply(self, variables, queries: torch.Tensor, *, train: bool = False, sparse_grad: bool = False,
               noise_scale: float = 1.0, shuffle_reads: bool = False, rngs=None,
               gumbel: Optional[torch.Tensor] = None, stats: bool = True,
-              stream: Optional[torch.cuda.Stream] = None) -> Tuple[torch.Tensor, Dict[str, Any]]:
+              stream: Optional[torch.cuda.Stream] = None, check: bool = False) -> Tuple[torch.Tensor, Dict[str, Any]]:
         """MemoryPool.__call__ (memory.py:119-227).  ``gumbel`` optionally
         supplies the standard Gumbel sample used when ``train`` (else one is
         drawn from ``rngs["routing"]``); ``stats=False`` skips the routing
@@ -179,6 +185,8 @@ class MemoryPool:
         s = (stream or torch.cuda.current_stream(device)).cuda_stream
         L.check(L.lib().memlayer_pool_forward(C.byref(cfg), C.byref(a), ws.data_ptr(), nbytes.value, s),
                 "memlayer_pool_forward")
+        if check:
+            _raise_device_status(cfg, ws, s)
         return out, self._aux(keep, lead, stats)
 
 
@@ -210,7 +218,7 @@ class MemoryLayer:
 
     def apply(self, params, h: torch.Tensor, *, train: bool = False, noise_scale: float = 1.0,
               shuffle_reads: bool = False, rngs=None, gumbel=None, stats: bool = False,
-              stream: Optional[torch.cuda.Stream] = None):
+              stream: Optional[torch.cuda.Stream] = None, check: bool = False):
         """Returns (y [..., d_model], mem [..., d_value], aux); y is the term
         model.py:119 adds into the layer's update."""
         P = self.pool
@@ -236,4 +244,6 @@ class MemoryLayer:
         s = (stream or torch.cuda.current_stream(device)).cuda_stream
         L.check(L.lib().memlayer_layer_forward(C.byref(cfg), C.byref(la), ws.data_ptr(), nbytes.value, s),
                 "memlayer_layer_forward")
+        if check:
+            _raise_device_status(cfg, ws, s)
         return y, mem, P._aux(keep, lead, stats)

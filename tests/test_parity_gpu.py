@@ -33,7 +33,7 @@ def run_gpu(recipe, stats=True):
     params = {"sub_keys": _dev(x["sub_keys"]), "values": _dev(x["values"], vdt),
               "log_temperature": torch.tensor(float(x["log_t"]), device="cuda")}
     kw = dict(train=recipe.get("train", False), noise_scale=recipe.get("noise_scale", 1.0),
-              shuffle_reads=recipe.get("shuffle_reads", False), stats=stats)
+              shuffle_reads=recipe.get("shuffle_reads", False), stats=stats, check=True)
     if "gumbel" in x:
         kw["gumbel"] = _dev(x["gumbel"])
     if recipe.get("layer"):
