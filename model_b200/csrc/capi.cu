@@ -68,6 +68,8 @@ size_t layout(const Dims& D, const Flags& f, char* ws, Work* W) {
   Work w;
   w.scal = (float*)take(4 * sizeof(float));
   w.err = (int*)take(sizeof(int));
+  w.fin_ctr = (int*)take(sizeof(int));
+  w.fin_part = (double*)take(sizeof(double) * 64);
   w.keys_n = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
   w.qn = (float*)take(sizeof(float) * rows * D.half);
   if (score_tc_supported(D)) {
@@ -168,7 +170,7 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
 
 int prep_keys(const Dims& D, const memlayer_config* c, const memlayer_pool_args* a, const Work& W, cudaStream_t s) {
   ML_TRY(launch_prep_keys(D, a->sub_keys, a->log_temperature, c->min_temperature, c->max_temperature, W.keys_n,
-                          W.k_hi, W.k_lo, W.scal, W.err, s));
+                          W.k_hi, W.k_lo, W.scal, W.err, W.fin_ctr, s));
   return MEMLAYER_OK;
 }
 
@@ -271,7 +273,6 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
   cudaStream_t s = (cudaStream_t)stream;
   const memlayer_pool_args* pa = &a->pool;
   ML_TRY(mark(pa, 0, s));
-  if ((st = prep_keys(D, cfg, pa, W, s))) return st;
   int* slots = pa->slots ? pa->slots : W.slots;
   float* weights = pa->weights ? pa->weights : W.weights;
   float* out = a->mem ? a->mem : pa->out;
@@ -280,11 +281,17 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
     // tensor-core projections: K-major tf32 halves of the Dense kernels and
     // the hidden state, then one GEMM for router (model.py:110) + gate (:118)
     const int NR = D.H * D.dk;
-    ML_TRY(launch_transpose_split(a->w_router, D.dm, NR, W.wrg_hi, W.wrg_lo, 0, s));
-    ML_TRY(launch_transpose_split(a->w_gate, D.dm, D.d, W.wrg_hi, W.wrg_lo, NR, s));
-    ML_TRY(launch_concat_bias(a->b_router, NR, a->b_gate, D.d, W.bias_rg, s));
-    ML_TRY(launch_transpose_split(a->w_out, D.d, D.dm, W.wo_hi, W.wo_lo, 0, s));
-    ML_TRY(launch_split(a->h, D.M * D.dm, W.h_hi, W.h_lo, s));
+    if (W.k_hi) {
+      ML_TRY(launch_prep_layer(D, W, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature,
+                               a->h, a->w_router, a->b_router, a->w_gate, a->b_gate, a->w_out, s));
+    } else {
+      if ((st = prep_keys(D, cfg, pa, W, s))) return st;
+      ML_TRY(launch_transpose_split(a->w_router, D.dm, NR, W.wrg_hi, W.wrg_lo, 0, s));
+      ML_TRY(launch_transpose_split(a->w_gate, D.dm, D.d, W.wrg_hi, W.wrg_lo, NR, s));
+      ML_TRY(launch_concat_bias(a->b_router, NR, a->b_gate, D.d, W.bias_rg, s));
+      ML_TRY(launch_transpose_split(a->w_out, D.d, D.dm, W.wo_hi, W.wo_lo, 0, s));
+      ML_TRY(launch_split(a->h, D.M * D.dm, W.h_hi, W.h_lo, s));
+    }
     // unit queries in float32 only when the aux output asks or the SIMT score path reads them
     ML_TRY(launch_router_gate_tc(D, W, W.bias_rg, (pa->queries_unit || !W.q_hi) ? qn : nullptr, s));
     ML_TRY(mark(pa, 1, s));
@@ -293,6 +300,7 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
     ML_TRY(launch_out_tc(D, W, a->b_out, a->y, s));                           // model.py:119
   } else {
     // SIMT float32 projections
+    if ((st = prep_keys(D, cfg, pa, W, s))) return st;
     ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
     ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
     ML_TRY(mark(pa, 1, s));

@@ -40,6 +40,8 @@ struct Work {
   float* q_hi = nullptr;       // [H*2,M,half] rna_tf32(qn), codebook-major
   float* q_lo = nullptr;       // [H*2,M,half] rna_tf32(qn - q_hi)
   int* err = nullptr;          // [1] device error code (bounded waits)
+  int* fin_ctr = nullptr;      // [1] blocks done in the aux reduction (reset by the prep kernels)
+  double* fin_part = nullptr;  // [64] per-block partial sums of the aux reduction
   float* h_hi = nullptr;       // [M,dm] tf32 halves of the hidden state   (tensor-core projections)
   float* h_lo = nullptr;
   float* wrg_hi = nullptr;     // [H*dk + d, dm] router | gate kernels, K-major
@@ -184,7 +186,8 @@ void count_launch(int n = 1);
 
 // ---- host-side launchers (one per kernel family) ----
 cudaError_t launch_prep_keys(const Dims& D, const float* sub_keys, const float* log_t, float min_t, float max_t,
-                             float* keys_n, float* k_hi, float* k_lo, float* scal, int* err, cudaStream_t s);
+                             float* keys_n, float* k_hi, float* k_lo, float* scal, int* err, int* fin_ctr,
+                             cudaStream_t s);
 cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, float* qlen, float* q_hi,
                                      float* q_lo, cudaStream_t s);
 bool score_tc_supported(const Dims& D);
@@ -203,6 +206,9 @@ cudaError_t launch_concat_bias(const float* a, int na, const float* b, int nb, f
 cudaError_t launch_router_gate_tc(const Dims& D, const Work& W, const float* bias_rg, float* qn_out, cudaStream_t s);
 cudaError_t launch_out_tc(const Dims& D, const Work& W, const float* b_out, float* y, cudaStream_t s);
 cudaError_t launch_finalize(const Dims& D, const Work& W, float* top1, float* temperature, cudaStream_t s);
+cudaError_t launch_prep_layer(const Dims& D, const Work& W, const float* sub_keys, const float* log_t, float min_t,
+                              float max_t, const float* h, const float* w_router, const float* b_router,
+                              const float* w_gate, const float* b_gate, const float* w_out, cudaStream_t s);
 cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float* C, int64_t M, int N, int K,
                         bool silu, cudaStream_t s);
 

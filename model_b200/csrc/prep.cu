@@ -9,10 +9,11 @@ namespace ml {
 __global__ void prep_keys_kernel(const float* __restrict__ keys, float* __restrict__ keys_n,
                                  float* __restrict__ k_hi, float* __restrict__ k_lo, int64_t rows, int half,
                                  const float* __restrict__ log_t, float min_t, float max_t,
-                                 float* __restrict__ scal, int* __restrict__ err) {
+                                 float* __restrict__ scal, int* __restrict__ err, int* __restrict__ fin_ctr) {
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     scal[0] = clamped_temperature(log_t[0], min_t, max_t);
-    *err = 0;  // device error code of this call's bounded waits
+    *err = 0;      // device error code of this call's bounded waits
+    *fin_ctr = 0;  // block ticket of the aux reduction
   }
   int lane = threadIdx.x & 31;
   int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -63,11 +64,12 @@ __global__ void normalize_q_kernel(const float* __restrict__ q, float* __restric
 }
 
 cudaError_t launch_prep_keys(const Dims& D, const float* sub_keys, const float* log_t, float min_t, float max_t,
-                             float* keys_n, float* k_hi, float* k_lo, float* scal, int* err, cudaStream_t s) {
+                             float* keys_n, float* k_hi, float* k_lo, float* scal, int* err, int* fin_ctr,
+                             cudaStream_t s) {
   int64_t rows = (int64_t)D.H * 2 * D.n;
   int wpb = 8;
   prep_keys_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, s>>>(sub_keys, keys_n, k_hi, k_lo, rows,
-                                                                            D.half, log_t, min_t, max_t, scal, err);
+                                                                            D.half, log_t, min_t, max_t, scal, err, fin_ctr);
   count_launch();
   return cudaGetLastError();
 }
@@ -157,28 +159,48 @@ cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float
 
 // ---------------------------------------------------------------------------
 // aux finalisation: top1_weight = mean over (token, head) of the max weight
-// (memory.py:225), summed in a fixed order (deterministic), plus temperature.
+// (memory.py:225) and the temperature.  FIN_BLOCKS blocks sum fixed
+// contiguous ranges in double; the last block to finish (ticket counter)
+// adds the partials in block order, so the result is deterministic.
 // ---------------------------------------------------------------------------
-__global__ void finalize_kernel(const float* __restrict__ top1_part, int64_t count, float* __restrict__ top1,
-                                const float* __restrict__ scal, float* __restrict__ temperature) {
-  __shared__ double red[32];
+constexpr int FIN_BLOCKS = 64;
+
+__global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ top1_part, int64_t count,
+                                                       float* __restrict__ top1, const float* __restrict__ scal,
+                                                       float* __restrict__ temperature, double* __restrict__ part,
+                                                       int* __restrict__ ctr) {
+  __shared__ double red[8];
+  __shared__ bool last;
+  const int64_t chunk = (count + FIN_BLOCKS - 1) / FIN_BLOCKS;
+  const int64_t lo = blockIdx.x * chunk, hi = lo + chunk < count ? lo + chunk : count;
   double acc = 0.0;
-  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) acc += (double)top1_part[i];
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) acc += (double)top1_part[i];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
   if (threadIdx.x == 0) {
     double t = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    for (int w = 0; w < 8; ++w) t += red[w];
+    part[blockIdx.x] = t;
+    __threadfence();
+    last = atomicAdd(ctr, 1) == FIN_BLOCKS - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    double t = 0.0;
+    for (int b = 0; b < FIN_BLOCKS; ++b) t += ((volatile double*)part)[b];
     if (top1) top1[0] = count > 0 ? (float)(t / (double)count) : __int_as_float(0x7fc00000);
     if (temperature) temperature[0] = scal[0];
+    *ctr = 0;
   }
 }
 
 cudaError_t launch_finalize(const Dims& D, const Work& W, float* top1, float* temperature, cudaStream_t s) {
   if (!top1 && !temperature) return cudaSuccess;
-  finalize_kernel<<<1, 1024, 0, s>>>(W.top1_part, D.M * D.H, top1, W.scal, temperature);
+  finalize_kernel<<<FIN_BLOCKS, 256, 0, s>>>(W.top1_part, D.M * D.H, top1, W.scal, temperature, W.fin_part,
+                                             W.fin_ctr);
   count_launch();
   return cudaGetLastError();
 }

@@ -163,23 +163,45 @@ __device__ __forceinline__ void merge_top_pairs(float (&a)[N], int (&ia)[N], con
 //   D. second TMEM scan: (score, key) of the values >= t*, in key order;
 //      exactly 16 unless t* is tied.  Sort them and merge into the list.
 // buf: this thread's slot 0; slots are 256 floats apart (bank-conflict free).
+// Predicated shared store (no branch).
+__device__ __forceinline__ void st_shared_if(float* p, float v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.shared.f32 [%0], %1;\n\t}" ::"r"(
+                   tc::smem_u32(p)),
+               "f"(v), "r"((int)pred)
+               : "memory");
+}
+
+template <bool QS>
+__device__ __forceinline__ float score_of(uint32_t bits, float T, float ql) {
+  float sc = __fmul_rn(__uint_as_float(bits), T);   // memory.py:150
+  if (QS) sc = __fmul_rn(sc, ql);                   // memory.py:151-152
+  return sc;
+}
+
+// 64 consecutive TMEM columns of this warp's lanes: two loads, one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&x)[64]) {
+  tc::tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+  tc::tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+  tc::tmem_wait_ld();
+}
+
 template <bool QS>
 __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, float ql, bool owner,
                                            float (&rv)[16], int (&ri)[16], float* buf) {
+  // A. 16th largest of the 32 group maxima (groups of 4 cosines)
   float lo[16], hi[16];
 #pragma unroll
-  for (int b = 0; b < 8; ++b) {
-    uint32_t r[16];
-    tc::tmem_ld16(taddr + b * 16, r);
-    tc::tmem_wait_ld();
+  for (int part = 0; part < 2; ++part) {
+    uint32_t x[64];
+    tmem_ld64(taddr + part * 64, x);
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const float m4 = fmaxf(fmaxf(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1])),
-                             fmaxf(__uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
-      if (b < 4)
-        lo[b * 4 + g] = m4;
+    for (int g = 0; g < 16; ++g) {
+      const float m4 = fmaxf(fmaxf(__uint_as_float(x[4 * g]), __uint_as_float(x[4 * g + 1])),
+                             fmaxf(__uint_as_float(x[4 * g + 2]), __uint_as_float(x[4 * g + 3])));
+      if (part == 0)
+        lo[g] = m4;
       else
-        hi[(b - 4) * 4 + g] = m4;
+        hi[g] = m4;
     }
   }
   sort_desc_v<16>(lo);
@@ -187,36 +209,31 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
   float g16 = INFINITY;
 #pragma unroll
   for (int i = 0; i < 16; ++i) g16 = fminf(g16, fmaxf(lo[i], hi[15 - i]));
-  float tau = __fmul_rn(g16, T);
-  if (QS) tau = __fmul_rn(tau, ql);
+  float tau = score_of<QS>(__float_as_uint(g16), T, ql);
   if (!owner) tau = INFINITY;
 
+  // B. candidate scores (>= tau) into this thread's buffer slots
   int cnt = 0;
-#pragma unroll 2
-  for (int b = 0; b < 8; ++b) {
-    uint32_t r[16];
-    tc::tmem_ld16(taddr + b * 16, r);
-    tc::tmem_wait_ld();
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      float sc = __fmul_rn(__uint_as_float(r[t]), T);
-      if (QS) sc = __fmul_rn(sc, ql);
-      if (sc >= tau) {
-        buf[(cnt & 31) * 256] = sc;
-        ++cnt;
-      }
+  for (int part = 0; part < 2; ++part) {
+    uint32_t x[64];
+    tmem_ld64(taddr + part * 64, x);
+#pragma unroll
+    for (int t = 0; t < 64; ++t) {
+      const float sc = score_of<QS>(x[t], T, ql);
+      const bool c = sc >= tau;
+      st_shared_if(buf + (cnt & 31) * 256, sc, c);
+      cnt += c;
     }
   }
   if (__any_sync(FULL, cnt > 32)) return false;
 
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = i < cnt ? buf[i * 256] : -INFINITY;
+  // C. value-only top-16 of the candidates: t* = their 16th largest
   float va[16], vb[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    va[i] = v[i];
-    vb[i] = v[16 + i];
+    va[i] = i < cnt ? buf[i * 256] : -INFINITY;
+    vb[i] = 16 + i < cnt ? buf[(16 + i) * 256] : -INFINITY;
   }
   sort_desc_v<16>(va);
   sort_desc_v<16>(vb);
@@ -224,21 +241,19 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
 #pragma unroll
   for (int i = 0; i < 16; ++i) tstar = fminf(tstar, fmaxf(va[i], vb[15 - i]));
 
+  // D. (score, key) of every value >= t*, in key order (16 unless t* is tied)
   int cnt2 = 0;
-#pragma unroll 2
-  for (int b = 0; b < 8; ++b) {
-    uint32_t r[16];
-    tc::tmem_ld16(taddr + b * 16, r);
-    tc::tmem_wait_ld();
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      float sc = __fmul_rn(__uint_as_float(r[t]), T);
-      if (QS) sc = __fmul_rn(sc, ql);
-      if (owner && sc >= tstar) {
-        buf[(cnt2 & 15) * 256] = sc;
-        buf[(16 + (cnt2 & 15)) * 256] = __int_as_float(key0 + b * 16 + t);
-        ++cnt2;
-      }
+  for (int part = 0; part < 2; ++part) {
+    uint32_t x[64];
+    tmem_ld64(taddr + part * 64, x);
+#pragma unroll
+    for (int t = 0; t < 64; ++t) {
+      const float sc = score_of<QS>(x[t], T, ql);
+      const bool c = owner && sc >= tstar;
+      st_shared_if(buf + (cnt2 & 15) * 256, sc, c);
+      st_shared_if(buf + (16 + (cnt2 & 15)) * 256, __int_as_float(key0 + part * 64 + t), c);
+      cnt2 += c;
     }
   }
   if (__any_sync(FULL, owner && cnt2 != 16)) return false;
