@@ -43,6 +43,58 @@ struct ProjArgs {
   float* out;          // [M][N]
 };
 
+// One query half of one row: q = acc + b_router, q_len and the unit half as
+// tf32 hi / lo (+ float32 when requested), memory.py:136-138.  TMEM is read
+// in pieces of up to 64 columns with one wait each: once for |q|^2, once to
+// write.
+template <int HALF>
+__device__ __forceinline__ void router_half(const ProjArgs& G, uint32_t taddr, int ns, int64_t row, bool rok,
+                                            const float* sbias) {
+  constexpr int P = HALF < 64 ? HALF : 64;
+  float ss = 0.f;
+#pragma unroll
+  for (int p0 = 0; p0 < HALF; p0 += P) {
+    uint32_t r[P];
+#pragma unroll
+    for (int c = 0; c < P; c += 32) tc::tmem_ld32(taddr + p0 + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int t = 0; t < P; ++t) {
+      const float q = __uint_as_float(r[t]) + sbias[ns + p0 + t];
+      ss = fmaf(q, q, ss);
+    }
+  }
+  const int hc = ns / HALF;                 // head * 2 + half
+  const float tt = ss + 1e-6f;
+  const float rn = 1.0f / sqrtf(tt);
+  if (rok) G.qlen[row * G.hc_count + hc] = sqrtf(tt) / sqrtf((float)HALF);
+  float* dqn = (rok && G.qn) ? G.qn + (row * G.hc_count + hc) * HALF : nullptr;
+  float* dhi = (rok && G.q_hi) ? G.q_hi + ((int64_t)hc * G.M + row) * HALF : nullptr;
+  float* dlo = (rok && G.q_hi) ? G.q_lo + ((int64_t)hc * G.M + row) * HALF : nullptr;
+#pragma unroll
+  for (int p0 = 0; p0 < HALF; p0 += P) {
+    uint32_t r[P];
+#pragma unroll
+    for (int c = 0; c < P; c += 32) tc::tmem_ld32(taddr + p0 + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int t = 0; t < P; t += 4) {
+      float h4[4], l4[4], u4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        u4[j] = (__uint_as_float(r[t + j]) + sbias[ns + p0 + t + j]) * rn;
+        h4[j] = tc::to_tf32(u4[j]);
+        l4[j] = tc::to_tf32(u4[j] - h4[j]);
+      }
+      if (dhi) {
+        *reinterpret_cast<float4*>(dhi + p0 + t) = make_float4(h4[0], h4[1], h4[2], h4[3]);
+        *reinterpret_cast<float4*>(dlo + p0 + t) = make_float4(l4[0], l4[1], l4[2], l4[3]);
+      }
+      if (dqn) *reinterpret_cast<float4*>(dqn + p0 + t) = make_float4(u4[0], u4[1], u4[2], u4[3]);
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     proj_gemm_tc_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
@@ -91,74 +143,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (EPI == EPI_ROUTER_GATE && n0 < G.NR) {
         // router columns: whole query halves (half divides 128, NR % 128 == 0)
         for (int seg = 0; seg < ncols; seg += G.half) {
-          const int ns = n0 + seg;                  // first column of this query half
-          const int hc = ns / G.half;               // head * 2 + half
-          float ss = 0.f;
-          for (int cc = 0; cc < G.half; cc += 16) {
-            uint32_t r[16];
-            tc::tmem_ld16(taddr + c0 + seg + cc, r);
-            tc::tmem_wait_ld();
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              const float q = __uint_as_float(r[t]) + sbias[ns + cc + t];
-              ss = fmaf(q, q, ss);
-            }
-          }
-          const float tt = ss + 1e-6f;
-          const float rn = 1.0f / sqrtf(tt);
-          if (rok) G.qlen[row * G.hc_count + hc] = sqrtf(tt) / sqrtf((float)G.half);
-          float* dhi = G.q_hi ? G.q_hi + ((int64_t)hc * G.M + row) * G.half : nullptr;
-          float* dlo = G.q_lo ? G.q_lo + ((int64_t)hc * G.M + row) * G.half : nullptr;
-          float* dqn = G.qn ? G.qn + (row * G.hc_count + hc) * G.half : nullptr;
-          for (int cc = 0; cc < G.half; cc += 16) {
-            uint32_t r[16];
-            tc::tmem_ld16(taddr + c0 + seg + cc, r);
-            tc::tmem_wait_ld();
-            if (rok && dhi) {
-              float hi[16], lo[16], qv[16];
-#pragma unroll
-              for (int t = 0; t < 16; ++t) {
-                const float q = __uint_as_float(r[t]) + sbias[ns + cc + t];
-                qv[t] = q * rn;
-                hi[t] = tc::to_tf32(qv[t]);
-                lo[t] = tc::to_tf32(qv[t] - hi[t]);
-              }
-#pragma unroll
-              for (int t = 0; t < 16; t += 4) {
-                *reinterpret_cast<float4*>(dhi + cc + t) = make_float4(hi[t], hi[t + 1], hi[t + 2], hi[t + 3]);
-                *reinterpret_cast<float4*>(dlo + cc + t) = make_float4(lo[t], lo[t + 1], lo[t + 2], lo[t + 3]);
-                if (dqn) *reinterpret_cast<float4*>(dqn + cc + t) = make_float4(qv[t], qv[t + 1], qv[t + 2], qv[t + 3]);
-              }
-            } else if (rok && dqn) {
-#pragma unroll
-              for (int t = 0; t < 16; ++t)
-                dqn[cc + t] = (__uint_as_float(r[t]) + sbias[ns + cc + t]) * rn;
-            }
-          }
+          if (G.half == 128)
+            router_half<128>(G, taddr + c0 + seg, n0 + seg, row, rok, sbias);
+          else if (G.half == 64)
+            router_half<64>(G, taddr + c0 + seg, n0 + seg, row, rok, sbias);
+          else
+            router_half<32>(G, taddr + c0 + seg, n0 + seg, row, rok, sbias);
         }
       } else {
-        // gate columns (silu) or plain bias columns
+        // gate columns (silu) or plain bias columns, 32 at a time
         const int ld = EPI == EPI_ROUTER_GATE ? G.N - G.NR : G.N;
         float* dst = EPI == EPI_ROUTER_GATE ? G.gate + row * ld + (n0 - G.NR) : G.out + row * ld + n0;
-        for (int cc = 0; cc < ncols; cc += 16) {
-          uint32_t r[16];
-          tc::tmem_ld16(taddr + c0 + cc, r);
+        for (int cc = 0; cc < ncols; cc += 32) {
+          uint32_t r[32];
+          tc::tmem_ld32(taddr + c0 + cc, r);
           tc::tmem_wait_ld();
           if (rok) {
-            float v[16];
+            float v[32];
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
+            for (int t = 0; t < 32; ++t) {
               float x = __uint_as_float(r[t]) + (cc + t < ncols ? sbias[n0 + cc + t] : 0.f);
               if (EPI == EPI_ROUTER_GATE) x = x / (1.0f + expf(-x));      // model.py:118 silu
               v[t] = x;
             }
-            if (cc + 16 <= ncols) {
+            if (cc + 32 <= ncols) {
 #pragma unroll
-              for (int t = 0; t < 16; t += 4)
+              for (int t = 0; t < 32; t += 4)
                 *reinterpret_cast<float4*>(dst + cc + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
             } else {
 #pragma unroll
-              for (int t = 0; t < 16; ++t)
+              for (int t = 0; t < 32; ++t)
                 if (cc + t < ncols) dst[cc + t] = v[t];
             }
           }

@@ -269,6 +269,42 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
   return true;
 }
 
+// Later chunks of a row: the running list's 16th score is already a tight
+// threshold.  Keys here are larger than every key in the list, so a value
+// enters only if it beats the 16th strictly.  The (score, key) pairs that do
+// (at most 16, else false) are sorted and merged into the list.
+template <bool QS>
+__device__ __forceinline__ bool fast_merge16(uint32_t taddr, int key0, float T, float ql, bool owner,
+                                             float (&rv)[16], int (&ri)[16], float* buf) {
+  const float thr = owner ? rv[15] : INFINITY;
+  int cnt = 0;
+#pragma unroll
+  for (int part = 0; part < 2; ++part) {
+    uint32_t x[64];
+    tmem_ld64(taddr + part * 64, x);
+#pragma unroll
+    for (int t = 0; t < 64; ++t) {
+      const float sc = score_of<QS>(x[t], T, ql);
+      const bool c = sc > thr;
+      st_shared_if(buf + (cnt & 15) * 256, sc, c);
+      st_shared_if(buf + (16 + (cnt & 15)) * 256, __int_as_float(key0 + part * 64 + t), c);
+      cnt += c;
+    }
+  }
+  if (__any_sync(FULL, cnt > 16)) return false;
+  if (!__any_sync(FULL, cnt > 0)) return true;
+  float pv[16];
+  int pc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    pv[i] = i < cnt ? buf[i * 256] : -INFINITY;
+    pc[i] = i < cnt ? __float_as_int(buf[(16 + i) * 256]) : (1 << 30) + i;
+  }
+  sort_desc_pairs<16>(pv, pc);
+  merge_top_pairs<16>(rv, ri, pv, pc);
+  return true;
+}
+
 // Insertion of (s, i) at its (value desc, index asc) rank, for any index.
 // Precondition: (s, i) ranks before the list's last element.
 template <int KM>
@@ -406,8 +442,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // exact per-half-chunk top-16 (clean selection), else the general path
         bool fast_done = false;
         if constexpr (FAST16) {
-          if (ce - cb == HALF_BN_FULL)
-            fast_done = fast_top16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
+          if (ce - cb == HALF_BN_FULL) {
+            // first chunk of the row: exact top-16 of the half-chunk;
+            // later chunks: filter by the running 16th
+            if (__any_sync(FULL, R.v[KM - 1] != -INFINITY))
+              fast_done = fast_merge16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
+            if (!fast_done) fast_done = fast_top16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
+          }
         }
         if (!fast_done) {
         // pass A: a lower bound of this half-chunk's k-th best selection
