@@ -113,8 +113,10 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
   const bool lk = lane < k;
   const float as = lk ? sub_sel[ra + lane] : -INFINITY;
   const float bs = lk ? sub_sel[rb + lane] : -INFINITY;
-  const float ac = lk ? sub_score[ra + lane] : 0.f;
-  const float bc = lk ? sub_score[rb + lane] : 0.f;
+  // without selection noise the clean scores are the selection scores
+  const float* scs = D.noisy ? sub_score : sub_sel;
+  const float ac = lk ? scs[ra + lane] : 0.f;
+  const float bc = lk ? scs[rb + lane] : 0.f;
   const int ai = lk ? sub_idx[ra + lane] : 0;
   const int bi = lk ? sub_idx[rb + lane] : 0;
 

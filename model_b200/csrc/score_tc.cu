@@ -98,6 +98,23 @@ __device__ __forceinline__ void sort_desc_v(float (&v)[N]) {
       }
 }
 
+// (value desc, index asc) order without short-circuit branches.
+__device__ __forceinline__ bool before_nb(float va, int ia, float vb, int ib) {
+  return (va > vb) | ((va == vb) & (ia < ib));
+}
+
+// Compare-exchange of pairs i, l: the better one goes to i when `desc`.
+__device__ __forceinline__ void ce_pairs(float& vi, int& xi, float& vl, int& xl, bool desc) {
+  const bool lb = before_nb(vl, xl, vi, xi);
+  const bool sw = desc ? lb : !lb;
+  const float a = vi, b = vl;
+  const int ia = xi, ib = xl;
+  vi = sw ? b : a;
+  vl = sw ? a : b;
+  xi = sw ? ib : ia;
+  xl = sw ? ia : ib;
+}
+
 // Bitonic sort of N (value, index) pairs into (value desc, index asc) order.
 template <int N>
 __device__ __forceinline__ void sort_desc_pairs(float (&v)[N], int (&ix)[N]) {
@@ -108,18 +125,7 @@ __device__ __forceinline__ void sort_desc_pairs(float (&v)[N], int (&ix)[N]) {
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         const int l = i ^ stride;
-        if (l > i) {
-          const bool lb = ranks_before(v[l], ix[l], v[i], ix[i]);
-          const bool swap = ((i & size) == 0) ? lb : !lb;
-          if (swap) {
-            const float tv = v[i];
-            v[i] = v[l];
-            v[l] = tv;
-            const int ti = ix[i];
-            ix[i] = ix[l];
-            ix[l] = ti;
-          }
-        }
+        if (l > i) ce_pairs(v[i], ix[i], v[l], ix[l], (i & size) == 0);
       }
 }
 
@@ -129,10 +135,9 @@ __device__ __forceinline__ void merge_top_pairs(float (&a)[N], int (&ia)[N], con
                                                 const int (&ib)[N]) {
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    if (ranks_before(b[N - 1 - i], ib[N - 1 - i], a[i], ia[i])) {
-      a[i] = b[N - 1 - i];
-      ia[i] = ib[N - 1 - i];
-    }
+    const bool take = before_nb(b[N - 1 - i], ib[N - 1 - i], a[i], ia[i]);
+    a[i] = take ? b[N - 1 - i] : a[i];
+    ia[i] = take ? ib[N - 1 - i] : ia[i];
   }
   // a is now bitonic: clean it into descending order
 #pragma unroll
@@ -140,14 +145,7 @@ __device__ __forceinline__ void merge_top_pairs(float (&a)[N], int (&ia)[N], con
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       const int l = i ^ stride;
-      if (l > i && ranks_before(a[l], ia[l], a[i], ia[i])) {
-        const float tv = a[i];
-        a[i] = a[l];
-        a[l] = tv;
-        const int ti = ia[i];
-        ia[i] = ia[l];
-        ia[l] = ti;
-      }
+      if (l > i) ce_pairs(a[i], ia[i], a[l], ia[l], true);
     }
 }
 
@@ -212,18 +210,27 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
   float tau = score_of<QS>(__float_as_uint(g16), T, ql);
   if (!owner) tau = INFINITY;
 
-  // B. candidate scores (>= tau) into this thread's buffer slots
+  // B. candidate scores (>= tau) into this thread's buffer slots.  Slot
+  // offsets come from per-8-value prefix counts, so the running count is
+  // a chain of 16 additions, not 128.
   int cnt = 0;
 #pragma unroll
   for (int part = 0; part < 2; ++part) {
     uint32_t x[64];
     tmem_ld64(taddr + part * 64, x);
 #pragma unroll
-    for (int t = 0; t < 64; ++t) {
-      const float sc = score_of<QS>(x[t], T, ql);
-      const bool c = sc >= tau;
-      st_shared_if(buf + (cnt & 31) * 256, sc, c);
-      cnt += c;
+    for (int g = 0; g < 8; ++g) {
+      float sc[8];
+      int off[8], run = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        sc[i] = score_of<QS>(x[8 * g + i], T, ql);
+        off[i] = run;
+        run += sc[i] >= tau;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) st_shared_if(buf + ((cnt + off[i]) & 31) * 256, sc[i], sc[i] >= tau);
+      cnt += run;
     }
   }
   if (__any_sync(FULL, cnt > 32)) return false;
@@ -243,17 +250,29 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
 
   // D. (score, key) of every value >= t*, in key order (16 unless t* is tied)
   int cnt2 = 0;
+  const float tst = owner ? tstar : INFINITY;
 #pragma unroll
   for (int part = 0; part < 2; ++part) {
     uint32_t x[64];
     tmem_ld64(taddr + part * 64, x);
 #pragma unroll
-    for (int t = 0; t < 64; ++t) {
-      const float sc = score_of<QS>(x[t], T, ql);
-      const bool c = owner && sc >= tstar;
-      st_shared_if(buf + (cnt2 & 15) * 256, sc, c);
-      st_shared_if(buf + (16 + (cnt2 & 15)) * 256, __int_as_float(key0 + part * 64 + t), c);
-      cnt2 += c;
+    for (int g = 0; g < 8; ++g) {
+      float sc[8];
+      int off[8], run = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        sc[i] = score_of<QS>(x[8 * g + i], T, ql);
+        off[i] = run;
+        run += sc[i] >= tst;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const bool c = sc[i] >= tst;
+        const int slot = (cnt2 + off[i]) & 15;
+        st_shared_if(buf + slot * 256, sc[i], c);
+        st_shared_if(buf + (16 + slot) * 256, __int_as_float(key0 + part * 64 + 8 * g + i), c);
+      }
+      cnt2 += run;
     }
   }
   if (__any_sync(FULL, owner && cnt2 != 16)) return false;
@@ -263,42 +282,6 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
   for (int i = 0; i < 16; ++i) {
     pv[i] = owner ? buf[i * 256] : -INFINITY;
     pc[i] = owner ? __float_as_int(buf[(16 + i) * 256]) : (1 << 30) + i;
-  }
-  sort_desc_pairs<16>(pv, pc);
-  merge_top_pairs<16>(rv, ri, pv, pc);
-  return true;
-}
-
-// Later chunks of a row: the running list's 16th score is already a tight
-// threshold.  Keys here are larger than every key in the list, so a value
-// enters only if it beats the 16th strictly.  The (score, key) pairs that do
-// (at most 16, else false) are sorted and merged into the list.
-template <bool QS>
-__device__ __forceinline__ bool fast_merge16(uint32_t taddr, int key0, float T, float ql, bool owner,
-                                             float (&rv)[16], int (&ri)[16], float* buf) {
-  const float thr = owner ? rv[15] : INFINITY;
-  int cnt = 0;
-#pragma unroll
-  for (int part = 0; part < 2; ++part) {
-    uint32_t x[64];
-    tmem_ld64(taddr + part * 64, x);
-#pragma unroll
-    for (int t = 0; t < 64; ++t) {
-      const float sc = score_of<QS>(x[t], T, ql);
-      const bool c = sc > thr;
-      st_shared_if(buf + (cnt & 15) * 256, sc, c);
-      st_shared_if(buf + (16 + (cnt & 15)) * 256, __int_as_float(key0 + part * 64 + t), c);
-      cnt += c;
-    }
-  }
-  if (__any_sync(FULL, cnt > 16)) return false;
-  if (!__any_sync(FULL, cnt > 0)) return true;
-  float pv[16];
-  int pc[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    pv[i] = i < cnt ? buf[i * 256] : -INFINITY;
-    pc[i] = i < cnt ? __float_as_int(buf[(16 + i) * 256]) : (1 << 30) + i;
   }
   sort_desc_pairs<16>(pv, pc);
   merge_top_pairs<16>(rv, ri, pv, pc);
@@ -442,13 +425,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // exact per-half-chunk top-16 (clean selection), else the general path
         bool fast_done = false;
         if constexpr (FAST16) {
-          if (ce - cb == HALF_BN_FULL) {
-            // first chunk of the row: exact top-16 of the half-chunk;
-            // later chunks: filter by the running 16th
-            if (__any_sync(FULL, R.v[KM - 1] != -INFINITY))
-              fast_done = fast_merge16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
-            if (!fast_done) fast_done = fast_top16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
-          }
+          if (ce - cb == HALF_BN_FULL)
+            fast_done = fast_top16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
         }
         if (!fast_done) {
         // pass A: a lower bound of this half-chunk's k-th best selection
@@ -652,13 +630,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }  // general merge
       if (hf == 0 && owner) {
         const int64_t o = row * D.k;
+        if (D.k == KM && KM % 4 == 0) {
+          // whole list: 16-byte stores (rows are k * 4 bytes apart)
 #pragma unroll
-        for (int j = 0; j < KM; ++j) {
-          if (j < D.k) {
-            sub_idx[o + j] = R.ix[j];
-            sub_sel[o + j] = R.v[j];
-            sub_score[o + j] = NOISY ? R.sc[j] : R.v[j];
-            if constexpr (RS::CLEAN) clean_idx[o + j] = R.cix[j];
+          for (int j = 0; j < KM; j += 4) {
+            *reinterpret_cast<int4*>(sub_idx + o + j) = make_int4(R.ix[j], R.ix[j + 1], R.ix[j + 2], R.ix[j + 3]);
+            *reinterpret_cast<float4*>(sub_sel + o + j) = make_float4(R.v[j], R.v[j + 1], R.v[j + 2], R.v[j + 3]);
+            if constexpr (NOISY)
+              *reinterpret_cast<float4*>(sub_score + o + j) = make_float4(R.sc[j], R.sc[j + 1], R.sc[j + 2], R.sc[j + 3]);
+            if constexpr (RS::CLEAN)
+              *reinterpret_cast<int4*>(clean_idx + o + j) = make_int4(R.cix[j], R.cix[j + 1], R.cix[j + 2], R.cix[j + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < KM; ++j) {
+            if (j < D.k) {
+              sub_idx[o + j] = R.ix[j];
+              sub_sel[o + j] = R.v[j];
+              if constexpr (NOISY) sub_score[o + j] = R.sc[j];
+              if constexpr (RS::CLEAN) clean_idx[o + j] = R.cix[j];
+            }
           }
         }
         if constexpr (BAL) {
