@@ -161,6 +161,23 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
  * Has no counterpart in the reference (its errors are Python exceptions). */
 int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* workspace, int32_t* code, void* stream);
 
+/* Size of the library's built-in scratch array used by
+ * memlayer_pool_forward_noalloc (64 MiB, held on every GPU that loads the
+ * library until the process exits). */
+#define MEMLAYER_NOALLOC_SCRATCH_BYTES (64u << 20)
+
+/* MemoryPool.__call__ for callers that cannot allocate or pass a device
+ * workspace (for example a runtime whose custom-call operands are fixed at
+ * compile time, or a per-token serving loop that must not enter the CUDA
+ * allocator).  No counterpart in the reference.  Same arguments and results
+ * as memlayer_pool_forward, but the workspace is the library's own fixed
+ * array; the library allocates nothing.  Returns MEMLAYER_ERR_WORKSPACE when
+ * memlayer_pool_workspace_size(cfg) exceeds MEMLAYER_NOALLOC_SCRATCH_BYTES.
+ * The first call on a device (with it current) resolves the array's device
+ * address; make it before any stream capture.  All calls share the array:
+ * calls that can run concurrently on the GPU (unordered streams) race. */
+int32_t memlayer_pool_forward_noalloc(const memlayer_config* cfg, const memlayer_pool_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
