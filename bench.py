@@ -10,6 +10,11 @@ gate / output kernels, sub_keys ~ N(0, 1/128), values ~ N(0, 0.02).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
+With N > 1 (torchrun, one process per GPU) the value table is row-sharded
+over the ranks (--pool sharded, the default: slot s on rank s % N) and each
+rank routes its own 8192 tokens, so the work per GPU is fixed (weak
+scaling); --pool replicated runs N independent replicas instead.
+
 Prints one JSON line (rank 0).  ``value`` is whole-job tokens/s from CUDA
 events around each step (inputs resident in HBM; L2 flushed before every
 step), max over ranks; ``e2e`` is the same through the C ABI with the hidden
@@ -48,6 +53,8 @@ def parse():
     ap.add_argument("--values-dtype", choices=["f32", "f16", "bf16"], default="f32")
     ap.add_argument("--tokens", type=int, default=WORKLOAD["tokens_per_gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pool", choices=["sharded", "replicated"], default="sharded",
+                    help="N>1: row-shard the value table over the ranks (default) or replicate it")
     return ap.parse_args()
 
 
@@ -112,7 +119,9 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- inputs
-def make_inputs(torch, device, W, values_dtype, seed):
+def make_inputs(torch, device, W, values_dtype, seed, value_rows=None):
+    """Seeded synthetic inputs; ``value_rows`` < n^2 draws only this rank's
+    rows of a row-sharded table (same distribution)."""
     g = torch.Generator(device=device).manual_seed(seed)
     T, dm, H, dk, n, d = (W[k] for k in ("tokens_per_gpu", "d_model", "heads", "d_key", "n_sub_keys", "d_value"))
 
@@ -126,7 +135,8 @@ def make_inputs(torch, device, W, values_dtype, seed):
         "w_router": glorot(dm, H * dk), "b_router": torch.zeros(H * dk, device=device),
         "sub_keys": torch.randn(H, 2, n, dk // 2, device=device, generator=g) * math.sqrt(1 / 128),
         "log_t": torch.full((1,), math.log(10.0), device=device),
-        "values": (torch.randn(n * n, d, device=device, generator=g) * 0.02).to(vdt),
+        "values": (torch.randn(n * n if value_rows is None else value_rows, d, device=device, generator=g)
+                   * 0.02).to(vdt),
         "w_gate": glorot(dm, d), "b_gate": torch.zeros(d, device=device),
         "w_out": glorot(d, dm), "b_out": torch.zeros(dm, device=device),
     }
@@ -168,6 +178,46 @@ class LayerCall:
         self.L.check(self.L.lib().memlayer_layer_forward(C.byref(self.cfg), C.byref(self.args),
                                                          self.ws.data_ptr(), self.ws_bytes, stream.cuda_stream),
                      "memlayer_layer_forward")
+
+
+class ShardedLayerCall(LayerCall):
+    """memlayer_layer_forward_sharded on resident buffers: this rank's local
+    rows of the row-sharded table, the three phases issued back to back on
+    one stream (events between them time the owner-side gather)."""
+
+    def __init__(self, torch, L, W, x, device, values_dtype):
+        from model_b200.shard import connect
+        super().__init__(torch, L, W, x, device, values_dtype)
+        self.comm = connect(self.cfg)                   # collective over the default group
+        self.world = self.comm.world
+        nb = C.c_size_t()
+        L.check(L.lib().memlayer_shard_workspace_size(C.byref(self.cfg), self.world, 1, C.byref(nb)),
+                "shard_workspace_size")
+        self.ws = torch.empty(nb.value, dtype=torch.uint8, device=device)
+        self.ws_bytes = nb.value
+
+    def __call__(self, stream, events=None, phase_events=None):
+        for i in range(self.L.STAGE_EVENTS):
+            self.events.events[i] = None if events is None else events[i].cuda_event
+        f = self.L.lib().memlayer_layer_forward_sharded
+        for j, ph in enumerate((self.L.PHASE_ROUTE, self.L.PHASE_GATHER, self.L.PHASE_REDUCE)):
+            self.L.check(f(C.byref(self.cfg), C.byref(self.args), self.comm.handle, ph, self.ws.data_ptr(),
+                           self.ws_bytes, stream.cuda_stream), "memlayer_layer_forward_sharded")
+            if phase_events is not None and j < 2:
+                phase_events[j].record(stream)
+
+
+def shard_gather_bytes(W, values_dtype, world):
+    """Algorithmic bytes of one owner-side gather launch on one rank, for the
+    expected even spread of slots over ranks: the rank's share of all ranks'
+    value rows, its inbox entries, and the partial rows it stores (local
+    and over NVLink); plus the partial bytes that cross NVLink."""
+    T, H, k, d = W["tokens_per_gpu"], W["heads"], W["top_k"], W["d_value"]
+    es = {"f32": 4, "f16": 2, "bf16": 2}[values_dtype]
+    rows = T * H * k * d * es                       # world * T tokens' fetches / world owners
+    entries = T * H * k * 8 + world * T * 4
+    partials = world * T * d * 4
+    return rows, rows + entries + partials, (world - 1) * T * d * 4
 
 
 def gather_bytes(W, values_dtype):
@@ -264,8 +314,13 @@ def run_ours(args, W, rank, world):
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(device)
     lib = L.lib()
-    x = make_inputs(torch, device, W, args.values_dtype, W["seed"] + rank)
-    call = LayerCall(torch, L, W, x, device, args.values_dtype)
+    sharded = world > 1 and args.pool == "sharded"
+    rows = None
+    if sharded:
+        from model_b200.shard import shard_rows
+        rows = shard_rows(W["n_sub_keys"] ** 2, rank, world)
+    x = make_inputs(torch, device, W, args.values_dtype, W["seed"] + rank, rows)
+    call = (ShardedLayerCall if sharded else LayerCall)(torch, L, W, x, device, args.values_dtype)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     T = W["tokens_per_gpu"]
@@ -277,6 +332,7 @@ def run_ours(args, W, rank, world):
 
     K = args.steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(L.STAGE_EVENTS)] for _ in range(K)]
+    pev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)] if sharded else None
     for row in ev:                 # create the driver events before handing them to the library
         for e in row:
             e.record(stream)
@@ -288,7 +344,10 @@ def run_ours(args, W, rank, world):
     with ClockSampler(device.index) as clk:
         for i in range(K):
             flush.zero_()
-            call(stream, ev[i])
+            if sharded:
+                call(stream, ev[i], pev[i])
+            else:
+                call(stream, ev[i])
         torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -297,6 +356,13 @@ def run_ours(args, W, rank, world):
     stage = lambda a, b: statistics.mean(ev[i][a].elapsed_time(ev[i][b]) for i in range(K))  # noqa: E731
     stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
               "combine_gather": stage(3, 4), "finalize_out": stage(4, 5)}
+    if sharded:
+        pstage = lambda f: statistics.mean(f(i) for i in range(K))  # noqa: E731
+        stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
+                  "combine_push": stage(3, 4),
+                  "finalize": pstage(lambda i: ev[i][4].elapsed_time(pev[i][0])),
+                  "shard_gather": pstage(lambda i: pev[i][0].elapsed_time(pev[i][1])),
+                  "reduce_out": pstage(lambda i: pev[i][1].elapsed_time(ev[i][5]))}
     ms = statistics.mean(step_ms)
 
     # ---- e2e through the C ABI with host buffers ----
@@ -319,25 +385,33 @@ def run_ours(args, W, rank, world):
     torch.cuda.synchronize()
     e2e_ms = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
 
-    stats = torch.tensor([ms, e2e_ms, stages["combine_gather"], stages["score_topk"]], dtype=torch.float64,
-                         device=device)
+    gather_stage = stages["shard_gather"] if sharded else stages["combine_gather"]
+    stats = torch.tensor([ms, e2e_ms, gather_stage, stages["score_topk"]], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms, gather_ms, score_ms = stats.tolist()
+    if sharded:                    # every rank's kernels are done before the peers are unmapped
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        call.comm.close()
     if rank != 0:
         return None
 
     hbm, src = peaks()
     bf16, _ = tensor_peak()
-    rows_b, alg_b = gather_bytes(W, args.values_dtype)
+    gname = "shard_gather_kernel" if sharded else "combine_gather_kernel"
+    if sharded:
+        rows_b, alg_b, nvlink_b = shard_gather_bytes(W, args.values_dtype, world)
+    else:
+        (rows_b, alg_b), nvlink_b = gather_bytes(W, args.values_dtype), 0
     achieved = alg_b / (gather_ms * 1e-3) / 1e9
-    traffic = load_traffic("combine_gather_kernel")
+    traffic = load_traffic(gname)
     score_flops = score_gemm_flops(W)
     score_tf = score_flops / (score_ms * 1e-3) / 1e12
     kernels = {
-        "combine_gather_kernel": {"bound": "hbm", "ms": gather_ms, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                                  "frac": achieved / hbm, "algorithmic_bytes_per_launch": alg_b,
-                                  "traffic": None if traffic is None else traffic.get("bytes_per_launch")},
+        gname: {"bound": "hbm", "ms": gather_ms, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "algorithmic_bytes_per_launch": alg_b,
+                "traffic": None if traffic is None else traffic.get("bytes_per_launch")},
         "score_topk_tc_kernel": {"bound": "tensor", "ms": score_ms, "achieved": score_tf, "peak": bf16,
                                  "unit": "TFLOP/s", "frac": score_tf / bf16, "algorithmic_flops_per_launch": score_flops,
                                  "note": "float32-faithful score GEMM issued as 3 tf32 MMAs per product; "
@@ -354,11 +428,13 @@ def run_ours(args, W, rank, world):
         "config": {"workload": W["name"], **{k: W[k] for k in W if k != "name"},
                    "values_dtype": args.values_dtype,
                    "l2": "flushed before every step (256 MiB write, outside the step events)",
-                   "parallelism": f"replicas{world}" if world > 1 else "single"},
+                   "parallelism": (f"pool-row-shard{world}" if sharded else f"replicas{world}") if world > 1
+                   else "single"},
         "roofline": {"kernel": dominant, "peak_source": src,
                      **{k: v for k, v in kernels[dominant].items() if k != "ms"}},
         "roofline_kernels": kernels,
         "gather_gbs": rows_b / (gather_ms * 1e-3) / 1e9,
+        **({"nvlink_partial_gbs_per_gpu": nvlink_b / (gather_ms * 1e-3) / 1e9} if sharded else {}),
         "stages_ms": stages,
         "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h_host.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},

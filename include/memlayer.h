@@ -161,6 +161,89 @@ int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_
  * Has no counterpart in the reference (its errors are Python exceptions). */
 int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* workspace, int32_t* code, void* stream);
 
+/* ---- Row-sharded value table over the GPUs of one node -------------------
+ * No counterpart in the reference, which replicates every parameter,
+ * the value table included, on each device of its data-parallel mesh
+ * (memory_pool_model/train.py:229-236,267); these calls serve tables larger
+ * than one GPU.  One process per GPU; slot s lives on rank s % world as its
+ * local row s / world (memlayer_shard_rows gives each rank's row count).
+ * Sub-keys and the Dense kernels are replicated.  Each rank routes its own
+ * tokens; a forward is three phases per rank:
+ *   ROUTE   routing + stage 2; (local row, weight) entries are stored into
+ *           the owner ranks' inboxes over NVLink;
+ *   GATHER  each owner gathers its rows for every rank's tokens and stores
+ *           one float32 partial row per (token, owner) into the token
+ *           owner's buffer;
+ *   REDUCE  the token owner adds the partials in rank order (deterministic),
+ *           then gate and output projection (layer entry).
+ * A call with MEMLAYER_PHASE_ALL runs all three.  Ranks hand over through
+ * flags in each other's buffers, with bounded waits (about 2 s): a wait that
+ * gives up records code 31/32 in the workspace status word and skips its
+ * work.  Calling the phases separately lets one process drive several
+ * communicators on one GPU (all ranks' ROUTE, then all GATHER, then all
+ * REDUCE, on one stream), where waits never depend on later launches. */
+#define MEMLAYER_MAX_SHARDS 8
+#define MEMLAYER_IPC_HANDLE_BYTES 64
+
+typedef struct memlayer_shard_comm memlayer_shard_comm;
+
+typedef enum {
+  MEMLAYER_PHASE_ROUTE = 1,
+  MEMLAYER_PHASE_GATHER = 2,
+  MEMLAYER_PHASE_REDUCE = 4,
+  MEMLAYER_PHASE_ALL = 7
+} memlayer_shard_phase;
+
+/* Value rows held by `rank`: the slots s < pool_size with s % world == rank. */
+int64_t memlayer_shard_rows(int64_t pool_size, int32_t rank, int32_t world);
+
+/* Create this rank's communicator on the current device, sized for cfg
+ * (cfg->tokens = the most tokens any rank passes in one call).  Every rank
+ * must pass the same cfg: ranks address each other's buffers with their own
+ * offsets.  Allocates
+ * and zeroes one device buffer (inboxes, partial rows, flags); this is the
+ * only allocation of the sharded path and happens here, not per call. */
+int32_t memlayer_shard_comm_create(const memlayer_config* cfg, int32_t rank, int32_t world,
+                                   memlayer_shard_comm** comm);
+
+/* The communicator's rank, world size, CUDA device ordinal and buffer
+ * bytes (any pointer may be NULL). */
+int32_t memlayer_shard_comm_info(const memlayer_shard_comm* comm, int32_t* rank, int32_t* world, int32_t* device,
+                                 size_t* bytes);
+
+/* CUDA IPC handle (MEMLAYER_IPC_HANDLE_BYTES bytes, host memory) of this
+ * rank's buffer, to be all-gathered by the caller (for instance with
+ * torch.distributed.all_gather_object). */
+int32_t memlayer_shard_comm_ipc_handle(const memlayer_shard_comm* comm, void* handle);
+
+/* Map every other rank's buffer: handles = world consecutive handles in
+ * rank order (host memory; this rank's own entry is ignored). */
+int32_t memlayer_shard_comm_open_peers(memlayer_shard_comm* comm, const void* handles);
+
+/* Use another communicator of this process (same device, or a device with
+ * peer access enabled) as rank `peer` instead of an IPC mapping. */
+int32_t memlayer_shard_comm_set_peer(memlayer_shard_comm* comm, int32_t peer, const memlayer_shard_comm* other);
+
+/* Unmap the peers and free the buffer (after all calls have completed). */
+int32_t memlayer_shard_comm_destroy(memlayer_shard_comm* comm);
+
+/* Workspace bytes of the sharded forward (layer != 0: layer entry). */
+int32_t memlayer_shard_workspace_size(const memlayer_config* cfg, int32_t world, int32_t layer, size_t* bytes);
+
+/* Sharded MemoryPool.__call__ / memory-layer block: same arguments as
+ * memlayer_pool_forward / memlayer_layer_forward, with `values` = this
+ * rank's local rows [memlayer_shard_rows(n*n, rank, world), d] (16-byte
+ * aligned, d a multiple of 4).  cfg must match the communicator's shapes,
+ * with cfg->tokens no larger than its capacity.  slot_counts /
+ * subkey_counts / balance_loss / top1_weight cover this rank's tokens.
+ * Pass the same workspace to every phase of one call. */
+int32_t memlayer_pool_forward_sharded(const memlayer_config* cfg, const memlayer_pool_args* args,
+                                      memlayer_shard_comm* comm, int32_t phases, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+int32_t memlayer_layer_forward_sharded(const memlayer_config* cfg, const memlayer_layer_args* args,
+                                       memlayer_shard_comm* comm, int32_t phases, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
 /* Size of the library's built-in scratch array used by
  * memlayer_pool_forward_noalloc (64 MiB, held on every GPU that loads the
  * library until the process exits). */

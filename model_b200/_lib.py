@@ -35,6 +35,9 @@ class MemlayerConfig(C.Structure):
 
 
 STAGE_EVENTS = 6
+MAX_SHARDS = 8
+IPC_HANDLE_BYTES = 64
+PHASE_ROUTE, PHASE_GATHER, PHASE_REDUCE, PHASE_ALL = 1, 2, 4, 7
 
 
 class MemlayerStageEvents(C.Structure):
@@ -81,7 +84,8 @@ class MemlayerLayerArgs(C.Structure):
 
 DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "MMA wait timed out",
                  14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
-                 21: "sub-key id out of range"}
+                 21: "sub-key id out of range", 22: "sharded row id out of range",
+                 31: "peer inbox wait timed out", 32: "peer partial-sum wait timed out"}
 
 
 class MemlayerError(RuntimeError):
@@ -119,6 +123,31 @@ def lib() -> C.CDLL:
         L.memlayer_workspace_status.argtypes = [C.POINTER(MemlayerConfig), C.c_void_p, C.POINTER(C.c_int32),
                                                 C.c_void_p]
         L.memlayer_kernel_launch_count.restype = C.c_int64
+        L.memlayer_shard_rows.restype = C.c_int64
+        L.memlayer_shard_rows.argtypes = [C.c_int64, C.c_int32, C.c_int32]
+        L.memlayer_shard_comm_create.restype = C.c_int32
+        L.memlayer_shard_comm_create.argtypes = [C.POINTER(MemlayerConfig), C.c_int32, C.c_int32,
+                                                 C.POINTER(C.c_void_p)]
+        L.memlayer_shard_comm_info.restype = C.c_int32
+        L.memlayer_shard_comm_info.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                               C.POINTER(C.c_int32), C.POINTER(C.c_size_t)]
+        L.memlayer_shard_comm_ipc_handle.restype = C.c_int32
+        L.memlayer_shard_comm_ipc_handle.argtypes = [C.c_void_p, C.c_void_p]
+        L.memlayer_shard_comm_open_peers.restype = C.c_int32
+        L.memlayer_shard_comm_open_peers.argtypes = [C.c_void_p, C.c_void_p]
+        L.memlayer_shard_comm_set_peer.restype = C.c_int32
+        L.memlayer_shard_comm_set_peer.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+        L.memlayer_shard_comm_destroy.restype = C.c_int32
+        L.memlayer_shard_comm_destroy.argtypes = [C.c_void_p]
+        L.memlayer_shard_workspace_size.restype = C.c_int32
+        L.memlayer_shard_workspace_size.argtypes = [C.POINTER(MemlayerConfig), C.c_int32, C.c_int32,
+                                                    C.POINTER(C.c_size_t)]
+        L.memlayer_pool_forward_sharded.restype = C.c_int32
+        L.memlayer_pool_forward_sharded.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerPoolArgs),
+                                                    C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_layer_forward_sharded.restype = C.c_int32
+        L.memlayer_layer_forward_sharded.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
+                                                     C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

@@ -5,7 +5,10 @@
 
 #include <atomic>
 
+#include <new>
+
 #include "common.cuh"
+#include "shard.cuh"
 
 namespace ml {
 
@@ -21,6 +24,7 @@ inline size_t up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
 struct Flags {
   bool layer = false;
   bool balance = false;   // balance_loss requested
+  int world = 0;          // ranks of the row-sharded pool (0: single GPU)
 };
 
 int check_config(const memlayer_config* c, Dims* D, bool layer) {
@@ -110,6 +114,7 @@ size_t layout(const Dims& D, const Flags& f, char* ws, Work* W) {
     w.slots = (int*)take(sizeof(int) * D.M * D.H * D.k);
     w.weights = (float*)take(sizeof(float) * D.M * D.H * D.k);
   }
+  if (f.world > 0) w.own_cnt = (int*)take(sizeof(int) * D.M * f.world);
   if (W) *W = w;
   return off;
 }
@@ -147,9 +152,11 @@ cudaError_t mark(const memlayer_pool_args* a, int i, cudaStream_t s) {
 
 // Routing from prepared unit queries onward: score + per-half top-k,
 // balance statistics, k*k combine + softmax + gather (+ gate), aux finalise.
+// With `sh` (row-sharded pool) stage 2 pushes its entries to the owner ranks
+// instead of gathering; out / memg / gate are then unused.
 int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, float* qn, int* slots,
                   float* weights, float* out, float* memg, float* memg_hi, float* memg_lo, const float* gate,
-                  cudaStream_t s) {
+                  cudaStream_t s, const ShardK* sh = nullptr) {
   Work w2 = W;
   w2.qn = qn;
   const bool bal = a->balance_loss != nullptr;
@@ -161,8 +168,11 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
   if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
   if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
   ML_TRY(mark(a, 3, s));
-  ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, memg_hi, memg_lo, gate, a->slot_counts,
-                               a->subkey_counts, s));
+  if (sh)
+    ML_TRY(launch_shard_push(D, w2, *sh, slots, weights, a->slot_counts, a->subkey_counts, W.own_cnt, s));
+  else
+    ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, memg_hi, memg_lo, gate,
+                                 a->slot_counts, a->subkey_counts, s));
   ML_TRY(mark(a, 4, s));
   ML_TRY(launch_finalize(D, w2, a->top1_weight, a->temperature, s));
   return MEMLAYER_OK;
@@ -171,6 +181,187 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
 int prep_keys(const Dims& D, const memlayer_config* c, const memlayer_pool_args* a, const Work& W, cudaStream_t s) {
   ML_TRY(launch_prep_keys(D, a->sub_keys, a->log_temperature, c->min_temperature, c->max_temperature, W.keys_n,
                           W.k_hi, W.k_lo, W.scal, W.err, W.fin_ctr, s));
+  return MEMLAYER_OK;
+}
+
+// Sharded calls: shapes must be the communicator's, tokens within capacity,
+// every peer mapped, and this thread on the communicator's device.
+int check_shard(const memlayer_config* c, const void* values, const memlayer_shard_comm* comm) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  const memlayer_config& k = comm->cfg;
+  if (c->heads != k.heads || c->n_sub_keys != k.n_sub_keys || c->d_key != k.d_key || c->d_value != k.d_value ||
+      c->top_k != k.top_k || c->values_dtype != k.values_dtype || c->tokens > k.tokens)
+    return MEMLAYER_ERR_BAD_SHAPE;
+  if (c->d_value % 4) return MEMLAYER_ERR_UNSUPPORTED;
+  if (!aligned16(values)) return MEMLAYER_ERR_BAD_POINTER;
+  for (int p = 0; p < comm->world; ++p)
+    if (!comm->peer[p]) return MEMLAYER_ERR_BAD_POINTER;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return MEMLAYER_ERR_CUDA;
+  return MEMLAYER_OK;
+}
+
+int64_t shard_rows(int64_t pool, int rank, int world) {
+  return pool > rank ? (pool - rank + world - 1) / world : 0;
+}
+
+ShardK shard_k(const memlayer_shard_comm* comm, const Dims& D) {
+  ShardK S{};
+  for (int p = 0; p < comm->world; ++p) S.peer[p] = comm->peer[p];
+  S.off = comm->off;
+  S.rank = comm->rank;
+  S.world = comm->world;
+  S.mcap = comm->cfg.tokens > 0 ? comm->cfg.tokens : 1;
+  S.hk = D.H * D.k;
+  S.d = D.d;
+  S.rows = shard_rows(D.N, comm->rank, comm->world);
+  S.epoch = comm->epoch;
+  return S;
+}
+
+// MemoryPool.__call__, single GPU (comm == nullptr) or row-sharded.
+int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* workspace, size_t workspace_bytes,
+              cudaStream_t s, memlayer_shard_comm* comm, int phases) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  st = check_pool_args(D, a, false);
+  if (st) return st;
+  if (comm && (st = check_shard(cfg, a->values, comm))) return st;
+  resolve_noise(&D, cfg, a);
+  if (D.noisy && !a->gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.balance = a->balance_loss != nullptr;
+  f.world = comm ? comm->world : 0;
+  size_t need = layout(D, f, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  Work W;
+  layout(D, f, (char*)workspace, &W);
+  float* qn = a->queries_unit ? a->queries_unit : W.qn;
+  if (!comm) {
+    ML_TRY(mark(a, 0, s));
+    ML_TRY(mark(a, 1, s));
+    if ((st = prep_keys(D, cfg, a, W, s))) return st;
+    ML_TRY(launch_normalize_queries(D, a->queries, qn, W.qlen, W.q_hi, W.q_lo, s));
+    ML_TRY(mark(a, 2, s));
+    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, a->out, nullptr, nullptr, nullptr, nullptr, s)))
+      return st;
+    ML_TRY(mark(a, 5, s));
+    return MEMLAYER_OK;
+  }
+  if (phases & MEMLAYER_PHASE_ROUTE) {
+    ++comm->epoch;
+    const ShardK S = shard_k(comm, D);
+    ML_TRY(mark(a, 0, s));
+    ML_TRY(mark(a, 1, s));
+    if ((st = prep_keys(D, cfg, a, W, s))) return st;
+    ML_TRY(launch_normalize_queries(D, a->queries, qn, W.qlen, W.q_hi, W.q_lo, s));
+    ML_TRY(mark(a, 2, s));
+    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, nullptr, nullptr, nullptr, nullptr, nullptr, s, &S)))
+      return st;
+  }
+  const ShardK S = shard_k(comm, D);
+  if (phases & MEMLAYER_PHASE_GATHER) ML_TRY(launch_shard_gather(D, S, a->values, W.err, s));
+  if (phases & MEMLAYER_PHASE_REDUCE) {
+    ML_TRY(launch_shard_reduce(D, S, W.own_cnt, nullptr, a->out, nullptr, nullptr, nullptr, W.err, s));
+    ML_TRY(mark(a, 5, s));
+  }
+  return MEMLAYER_OK;
+}
+
+// Memory-layer block (model.py:108-120), single GPU or row-sharded.
+int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* workspace, size_t workspace_bytes,
+               cudaStream_t s, memlayer_shard_comm* comm, int phases) {
+  Dims D;
+  int st = check_config(cfg, &D, true);
+  if (st) return st;
+  if (!a) return MEMLAYER_ERR_BAD_POINTER;
+  st = check_pool_args(D, &a->pool, true);
+  if (st) return st;
+  if (D.M > 0 && (!a->h || !a->w_router || !a->w_gate || !a->w_out || !a->y)) return MEMLAYER_ERR_BAD_POINTER;
+  if (!aligned16(a->h) || !aligned16(a->y) || !aligned16(a->mem) || !aligned16(a->pool.out))
+    return MEMLAYER_ERR_BAD_POINTER;
+  if (comm && (st = check_shard(cfg, a->pool.values, comm))) return st;
+  resolve_noise(&D, cfg, &a->pool);
+  if (D.noisy && !a->pool.gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.layer = true;
+  f.balance = a->pool.balance_loss != nullptr;
+  f.world = comm ? comm->world : 0;
+  size_t need = layout(D, f, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  Work W;
+  layout(D, f, (char*)workspace, &W);
+  const memlayer_pool_args* pa = &a->pool;
+  int* slots = pa->slots ? pa->slots : W.slots;
+  float* weights = pa->weights ? pa->weights : W.weights;
+  float* out = a->mem ? a->mem : pa->out;
+  float* qn = pa->queries_unit ? pa->queries_unit : W.qn;
+  const bool route = !comm || (phases & MEMLAYER_PHASE_ROUTE);
+  const bool reduce = !comm || (phases & MEMLAYER_PHASE_REDUCE);
+  ShardK S{};
+  if (comm) {
+    if (route) ++comm->epoch;
+    S = shard_k(comm, D);
+  }
+  const ShardK* sh = comm ? &S : nullptr;
+  if (W.h_hi) {
+    if (route) {
+      ML_TRY(mark(pa, 0, s));
+      // tensor-core projections: K-major tf32 halves of the Dense kernels and
+      // the hidden state, then one GEMM for router (model.py:110) + gate (:118)
+      const int NR = D.H * D.dk;
+      if (W.k_hi) {
+        ML_TRY(launch_prep_layer(D, W, pa->sub_keys, pa->log_temperature, cfg->min_temperature,
+                                 cfg->max_temperature, a->h, a->w_router, a->b_router, a->w_gate, a->b_gate,
+                                 a->w_out, s));
+      } else {
+        if ((st = prep_keys(D, cfg, pa, W, s))) return st;
+        ML_TRY(launch_transpose_split(a->w_router, D.dm, NR, W.wrg_hi, W.wrg_lo, 0, s));
+        ML_TRY(launch_transpose_split(a->w_gate, D.dm, D.d, W.wrg_hi, W.wrg_lo, NR, s));
+        ML_TRY(launch_concat_bias(a->b_router, NR, a->b_gate, D.d, W.bias_rg, s));
+        ML_TRY(launch_transpose_split(a->w_out, D.d, D.dm, W.wo_hi, W.wo_lo, 0, s));
+        ML_TRY(launch_split(a->h, D.M * D.dm, W.h_hi, W.h_lo, s));
+      }
+      // unit queries in float32 only when the aux output asks or the SIMT score path reads them
+      ML_TRY(launch_router_gate_tc(D, W, W.bias_rg, (pa->queries_unit || !W.q_hi) ? qn : nullptr, s));
+      ML_TRY(mark(pa, 1, s));
+      ML_TRY(mark(pa, 2, s));
+      if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, nullptr, W.memg_hi, W.memg_lo, W.gate, s, sh)))
+        return st;
+    }
+    if (comm && (phases & MEMLAYER_PHASE_GATHER)) ML_TRY(launch_shard_gather(D, S, pa->values, W.err, s));
+    if (reduce) {
+      if (comm)
+        ML_TRY(launch_shard_reduce(D, S, W.own_cnt, W.gate, out, nullptr, W.memg_hi, W.memg_lo, W.err, s));
+      ML_TRY(launch_out_tc(D, W, a->b_out, a->y, s));                           // model.py:119
+    }
+  } else {
+    // SIMT float32 projections
+    if (route) {
+      ML_TRY(mark(pa, 0, s));
+      if ((st = prep_keys(D, cfg, pa, W, s))) return st;
+      ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
+      ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
+      ML_TRY(mark(pa, 1, s));
+      ML_TRY(launch_normalize_queries(D, W.qraw, qn, W.qlen, W.q_hi, W.q_lo, s));
+      ML_TRY(mark(pa, 2, s));
+      if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, W.memg, nullptr, nullptr, W.gate, s, sh)))
+        return st;
+    }
+    if (comm && (phases & MEMLAYER_PHASE_GATHER)) ML_TRY(launch_shard_gather(D, S, pa->values, W.err, s));
+    if (reduce) {
+      if (comm) ML_TRY(launch_shard_reduce(D, S, W.own_cnt, W.gate, out, W.memg, nullptr, nullptr, W.err, s));
+      ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));  // model.py:119
+    }
+  }
+  if (reduce) {
+    if (a->mem && pa->out && pa->out != a->mem && D.M > 0)
+      ML_TRY(cudaMemcpyAsync(pa->out, a->mem, sizeof(float) * D.M * D.d, cudaMemcpyDeviceToDevice, s));
+    ML_TRY(mark(pa, 5, s));
+  }
   return MEMLAYER_OK;
 }
 
@@ -223,96 +414,12 @@ int32_t memlayer_layer_workspace_size(const memlayer_config* cfg, size_t* bytes)
 
 int32_t memlayer_pool_forward(const memlayer_config* cfg, const memlayer_pool_args* a, void* workspace,
                               size_t workspace_bytes, void* stream) {
-  Dims D;
-  int st = check_config(cfg, &D, false);
-  if (st) return st;
-  st = check_pool_args(D, a, false);
-  if (st) return st;
-  resolve_noise(&D, cfg, a);
-  if (D.noisy && !a->gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
-  Flags f;
-  f.balance = a->balance_loss != nullptr;
-  size_t need = layout(D, f, nullptr, nullptr);
-  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
-    return MEMLAYER_ERR_WORKSPACE;
-  Work W;
-  layout(D, f, (char*)workspace, &W);
-  cudaStream_t s = (cudaStream_t)stream;
-  ML_TRY(mark(a, 0, s));
-  ML_TRY(mark(a, 1, s));
-  if ((st = prep_keys(D, cfg, a, W, s))) return st;
-  float* qn = a->queries_unit ? a->queries_unit : W.qn;
-  ML_TRY(launch_normalize_queries(D, a->queries, qn, W.qlen, W.q_hi, W.q_lo, s));
-  ML_TRY(mark(a, 2, s));
-  if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, a->out, nullptr, nullptr, nullptr, nullptr, s))) return st;
-  ML_TRY(mark(a, 5, s));
-  return MEMLAYER_OK;
+  return pool_impl(cfg, a, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, MEMLAYER_PHASE_ALL);
 }
 
 int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_args* a, void* workspace,
                                size_t workspace_bytes, void* stream) {
-  Dims D;
-  int st = check_config(cfg, &D, true);
-  if (st) return st;
-  if (!a) return MEMLAYER_ERR_BAD_POINTER;
-  st = check_pool_args(D, &a->pool, true);
-  if (st) return st;
-  if (D.M > 0 && (!a->h || !a->w_router || !a->w_gate || !a->w_out || !a->y)) return MEMLAYER_ERR_BAD_POINTER;
-  if (!aligned16(a->h) || !aligned16(a->y) || !aligned16(a->mem) || !aligned16(a->pool.out))
-    return MEMLAYER_ERR_BAD_POINTER;
-  resolve_noise(&D, cfg, &a->pool);
-  if (D.noisy && !a->pool.gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
-  Flags f;
-  f.layer = true;
-  f.balance = a->pool.balance_loss != nullptr;
-  size_t need = layout(D, f, nullptr, nullptr);
-  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
-    return MEMLAYER_ERR_WORKSPACE;
-  Work W;
-  layout(D, f, (char*)workspace, &W);
-  cudaStream_t s = (cudaStream_t)stream;
-  const memlayer_pool_args* pa = &a->pool;
-  ML_TRY(mark(pa, 0, s));
-  int* slots = pa->slots ? pa->slots : W.slots;
-  float* weights = pa->weights ? pa->weights : W.weights;
-  float* out = a->mem ? a->mem : pa->out;
-  float* qn = pa->queries_unit ? pa->queries_unit : W.qn;
-  if (W.h_hi) {
-    // tensor-core projections: K-major tf32 halves of the Dense kernels and
-    // the hidden state, then one GEMM for router (model.py:110) + gate (:118)
-    const int NR = D.H * D.dk;
-    if (W.k_hi) {
-      ML_TRY(launch_prep_layer(D, W, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature,
-                               a->h, a->w_router, a->b_router, a->w_gate, a->b_gate, a->w_out, s));
-    } else {
-      if ((st = prep_keys(D, cfg, pa, W, s))) return st;
-      ML_TRY(launch_transpose_split(a->w_router, D.dm, NR, W.wrg_hi, W.wrg_lo, 0, s));
-      ML_TRY(launch_transpose_split(a->w_gate, D.dm, D.d, W.wrg_hi, W.wrg_lo, NR, s));
-      ML_TRY(launch_concat_bias(a->b_router, NR, a->b_gate, D.d, W.bias_rg, s));
-      ML_TRY(launch_transpose_split(a->w_out, D.d, D.dm, W.wo_hi, W.wo_lo, 0, s));
-      ML_TRY(launch_split(a->h, D.M * D.dm, W.h_hi, W.h_lo, s));
-    }
-    // unit queries in float32 only when the aux output asks or the SIMT score path reads them
-    ML_TRY(launch_router_gate_tc(D, W, W.bias_rg, (pa->queries_unit || !W.q_hi) ? qn : nullptr, s));
-    ML_TRY(mark(pa, 1, s));
-    ML_TRY(mark(pa, 2, s));
-    if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, nullptr, W.memg_hi, W.memg_lo, W.gate, s))) return st;
-    ML_TRY(launch_out_tc(D, W, a->b_out, a->y, s));                           // model.py:119
-  } else {
-    // SIMT float32 projections
-    if ((st = prep_keys(D, cfg, pa, W, s))) return st;
-    ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
-    ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
-    ML_TRY(mark(pa, 1, s));
-    ML_TRY(launch_normalize_queries(D, W.qraw, qn, W.qlen, W.q_hi, W.q_lo, s));
-    ML_TRY(mark(pa, 2, s));
-    if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, W.memg, nullptr, nullptr, W.gate, s))) return st;
-    ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));  // model.py:119
-  }
-  if (a->mem && pa->out && pa->out != a->mem && D.M > 0)
-    ML_TRY(cudaMemcpyAsync(pa->out, a->mem, sizeof(float) * D.M * D.d, cudaMemcpyDeviceToDevice, s));
-  ML_TRY(mark(pa, 5, s));
-  return MEMLAYER_OK;
+  return layer_impl(cfg, a, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, MEMLAYER_PHASE_ALL);
 }
 
 int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* workspace, int32_t* code, void* stream) {
@@ -327,6 +434,132 @@ int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* worksp
   ML_TRY(cudaStreamSynchronize((cudaStream_t)stream));
   *code = v;
   return MEMLAYER_OK;
+}
+
+// ---- row-sharded pool ----
+
+int64_t memlayer_shard_rows(int64_t pool_size, int32_t rank, int32_t world) {
+  if (world < 1 || rank < 0 || rank >= world || pool_size < 0) return 0;
+  return shard_rows(pool_size, rank, world);
+}
+
+int32_t memlayer_shard_comm_create(const memlayer_config* cfg, int32_t rank, int32_t world,
+                                   memlayer_shard_comm** comm) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  *comm = nullptr;
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (world < 1 || world > MEMLAYER_MAX_SHARDS || rank < 0 || rank >= world) return MEMLAYER_ERR_BAD_SHAPE;
+  if (D.d % 4) return MEMLAYER_ERR_UNSUPPORTED;
+  memlayer_shard_comm* c = new (std::nothrow) memlayer_shard_comm;
+  if (!c) return MEMLAYER_ERR_CUDA;
+  c->rank = rank;
+  c->world = world;
+  c->cfg = *cfg;
+  if (cudaGetDevice(&c->device) != cudaSuccess) {
+    delete c;
+    return MEMLAYER_ERR_CUDA;
+  }
+  c->off = shard_layout(world, cfg->tokens > 0 ? cfg->tokens : 1, D.H * D.k, D.d);
+  if (cudaMalloc(&c->base, (size_t)c->off.bytes) != cudaSuccess) {
+    delete c;
+    return MEMLAYER_ERR_CUDA;
+  }
+  if (cudaMemset(c->base, 0, (size_t)c->off.bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(c->base);
+    delete c;
+    return MEMLAYER_ERR_CUDA;
+  }
+  c->peer[rank] = c->base;
+  *comm = c;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_shard_comm_info(const memlayer_shard_comm* comm, int32_t* rank, int32_t* world, int32_t* device,
+                                 size_t* bytes) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if (rank) *rank = comm->rank;
+  if (world) *world = comm->world;
+  if (device) *device = comm->device;
+  if (bytes) *bytes = (size_t)comm->off.bytes;
+  return MEMLAYER_OK;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == MEMLAYER_IPC_HANDLE_BYTES, "IPC handle size");
+
+int32_t memlayer_shard_comm_ipc_handle(const memlayer_shard_comm* comm, void* handle) {
+  if (!comm || !handle) return MEMLAYER_ERR_BAD_POINTER;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, comm->base) != cudaSuccess) return MEMLAYER_ERR_CUDA;
+  memcpy(handle, &h, sizeof(h));
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_shard_comm_open_peers(memlayer_shard_comm* comm, const void* handles) {
+  if (!comm || !handles) return MEMLAYER_ERR_BAD_POINTER;
+  for (int p = 0; p < comm->world; ++p) {
+    if (p == comm->rank || comm->opened[p]) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, (const char*)handles + (size_t)p * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return MEMLAYER_ERR_CUDA;
+    comm->peer[p] = (char*)ptr;
+    comm->opened[p] = true;
+  }
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_shard_comm_set_peer(memlayer_shard_comm* comm, int32_t peer, const memlayer_shard_comm* other) {
+  if (!comm || !other) return MEMLAYER_ERR_BAD_POINTER;
+  if (peer < 0 || peer >= comm->world || peer == comm->rank || comm->opened[peer]) return MEMLAYER_ERR_BAD_SHAPE;
+  // peers address each other's buffers with their own offsets: shapes must agree
+  if (other->world != comm->world || other->rank != peer || other->off.bytes != comm->off.bytes ||
+      other->cfg.tokens != comm->cfg.tokens || other->cfg.heads != comm->cfg.heads ||
+      other->cfg.top_k != comm->cfg.top_k || other->cfg.d_value != comm->cfg.d_value)
+    return MEMLAYER_ERR_BAD_SHAPE;
+  comm->peer[peer] = other->base;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_shard_comm_destroy(memlayer_shard_comm* comm) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  int st = MEMLAYER_OK;
+  for (int p = 0; p < comm->world; ++p)
+    if (comm->opened[p] && cudaIpcCloseMemHandle(comm->peer[p]) != cudaSuccess) st = MEMLAYER_ERR_CUDA;
+  if (comm->base && cudaFree(comm->base) != cudaSuccess) st = MEMLAYER_ERR_CUDA;
+  delete comm;
+  return st;
+}
+
+int32_t memlayer_shard_workspace_size(const memlayer_config* cfg, int32_t world, int32_t layer, size_t* bytes) {
+  Dims D;
+  int st = check_config(cfg, &D, layer != 0);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  if (world < 1 || world > MEMLAYER_MAX_SHARDS) return MEMLAYER_ERR_BAD_SHAPE;
+  Flags f;
+  f.balance = true;
+  f.layer = layer != 0;
+  f.world = world;
+  *bytes = layout(D, f, nullptr, nullptr);
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_pool_forward_sharded(const memlayer_config* cfg, const memlayer_pool_args* args,
+                                      memlayer_shard_comm* comm, int32_t phases, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if (phases < 1 || phases > MEMLAYER_PHASE_ALL) return MEMLAYER_ERR_BAD_SHAPE;
+  return pool_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
+}
+
+int32_t memlayer_layer_forward_sharded(const memlayer_config* cfg, const memlayer_layer_args* args,
+                                       memlayer_shard_comm* comm, int32_t phases, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if (phases < 1 || phases > MEMLAYER_PHASE_ALL) return MEMLAYER_ERR_BAD_SHAPE;
+  return layer_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
 }
 
 }  // extern "C"

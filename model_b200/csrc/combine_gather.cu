@@ -3,94 +3,19 @@
 // SiLU gate of the layer block (model.py:118), fused in one kernel.
 //
 // One CTA per token, one warp per head.  Each warp
-//   1. forms the k x k cartesian candidates a_i + b_j of its two stage-1
-//      lists.  Both lists are sorted (value desc, index asc), so candidate
-//      (i, j) is dominated by every (i', j') with i' <= i, j' <= j, which
-//      rank ahead of it under (value desc, flat index asc); with
-//      (i+1)(j+1) > k at least k candidates rank ahead, so only the
-//      candidates with (i+1)(j+1) <= k can be selected (8 / 20 / 50 / 119
-//      of them for k = 4 / 8 / 16 / 32).  Those are sorted across the warp
-//      by a bitonic network on (value desc, flat index asc), which is
-//      lax.top_k's order on the full k*k list (memory.py:171);
-//   2. turns the k winners into slot ids idx_a * n + idx_b (memory.py:172-175)
-//      and softmax weights (memory.py:178);
-//   3. streams its k value rows (16-byte loads, float32 accumulation in
+//   1. runs stage 2 (combine.cuh: k x k re-top-k over the eligible
+//      candidates, slot ids, softmax weights);
+//   2. streams its k value rows (16-byte loads, float32 accumulation in
 //      registers) into a per-head partial sum.
 // The CTA then sums the heads in a fixed order (deterministic) and applies
 // the gate.  Counters use integer-valued float atomics (exact, order-free).
 #include <float.h>
 
-#include "common.cuh"
+#include "combine.cuh"
 
 namespace ml {
 
 namespace {
-
-__device__ __forceinline__ float tc_round(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
-template <typename VT, int VEC>
-__device__ __forceinline__ void load_group(const VT* p, float (&o)[VEC]) {
-  if constexpr (VEC == 1) {
-    o[0] = VecLoad<VT>::scalar(p);
-  } else {
-    VecLoad<VT>::load(p, o);
-  }
-}
-
-// Eligible stage-2 candidates (i, j) with (i+1)(j+1) <= k, row-major.
-struct PairTable {
-  uint16_t ij[128];  // i | j << 8
-  int count;
-};
-
-// Bitonic sort of 32*C (value, flat) pairs held C per lane (position
-// lane*C + r) into (value desc, flat asc) order.  Flats must be distinct.
-template <int C>
-__device__ __forceinline__ void warp_sort_desc(float (&v)[C], int (&f)[C], int lane) {
-  constexpr int N = 32 * C;
-#pragma unroll
-  for (int size = 2; size <= N; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride < C) {
-#pragma unroll
-        for (int r = 0; r < C; ++r) {
-          const int rp = r ^ stride;
-          if (rp > r) {
-            const bool desc = ((lane * C + r) & size) == 0;
-            const bool swap = desc ? ranks_before(v[rp], f[rp], v[r], f[r]) : ranks_before(v[r], f[r], v[rp], f[rp]);
-            if (swap) {
-              const float tv = v[r];
-              v[r] = v[rp];
-              v[rp] = tv;
-              const int tf = f[r];
-              f[r] = f[rp];
-              f[rp] = tf;
-            }
-          }
-        }
-      } else {
-        const int ls = stride / C;
-#pragma unroll
-        for (int r = 0; r < C; ++r) {
-          const float ov = __shfl_xor_sync(FULL, v[r], ls);
-          const int of = __shfl_xor_sync(FULL, f[r], ls);
-          const bool lower = (lane & ls) == 0;
-          const bool desc = ((lane * C + r) & size) == 0;
-          const bool mine_better = ranks_before(v[r], f[r], ov, of);
-          if (mine_better != (lower == desc)) {
-            v[r] = ov;
-            f[r] = of;
-          }
-        }
-      }
-    }
-  }
-}
 
 template <int KM, typename VT, int VEC, int CH>
 __global__ void __launch_bounds__(1024) combine_gather_kernel(
@@ -102,61 +27,17 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
     float* __restrict__ top1_part, int* __restrict__ err) {
   extern __shared__ float red[];  // [H][d]
   __shared__ uint16_t tab[128];   // pair table, staged for divergent per-lane reads
-  constexpr int C = KM <= 8 ? 1 : KM <= 16 ? 2 : 4;   // candidate slots per lane (32*C >= eligible count)
   for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
   __syncthreads();
   const int64_t m = blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k = D.k, d = D.d;
-  const int64_t ra = ((m * D.H + h) * 2) * k, rb = ra + k;
+  const int64_t ra = ((m * D.H + h) * 2) * k;
 
   const bool lk = lane < k;
-  const float as = lk ? sub_sel[ra + lane] : -INFINITY;
-  const float bs = lk ? sub_sel[rb + lane] : -INFINITY;
-  // without selection noise the clean scores are the selection scores
-  const float* scs = D.noisy ? sub_score : sub_sel;
-  const float ac = lk ? scs[ra + lane] : 0.f;
-  const float bc = lk ? scs[rb + lane] : 0.f;
-  const int ai = lk ? sub_idx[ra + lane] : 0;
-  const int bi = lk ? sub_idx[rb + lane] : 0;
-
-  // eligible candidates into slots lane*C + r; padding ranks last
-  float cv[C];
-  int cf[C];
-#pragma unroll
-  for (int r = 0; r < C; ++r) {
-    const int slot = lane * C + r;
-    const bool ok = slot < pairs.count;
-    const int ij = ok ? tab[slot] : 0;
-    const int i = ij & 0xFF, j = ij >> 8;
-    const float x = __shfl_sync(FULL, as, i);
-    const float y = __shfl_sync(FULL, bs, j);
-    cv[r] = ok ? x + y : -INFINITY;                  // memory.py:168 cand_select
-    cf[r] = ok ? i * k + j : (1 << 30) + slot;       // flat index in the k*k grid
-  }
-  warp_sort_desc<C>(cv, cf, lane);
-  // lane r < k takes sorted position r
-  int my_flat = 0;
-#pragma unroll
-  for (int r = 0; r < C; ++r) {
-    const int f = __shfl_sync(FULL, cf[r], lane / C);
-    if ((lane % C) == r) my_flat = f;
-  }
-  const int fi = lk ? my_flat / k : 0, fj = lk ? my_flat - (my_flat / k) * k : 0;
-  const float s = __shfl_sync(FULL, ac, fi) + __shfl_sync(FULL, bc, fj);     // memory.py:172
-  int ia = __shfl_sync(FULL, ai, fi), ib = __shfl_sync(FULL, bi, fj);        // memory.py:173-174
-  if (lk && ((unsigned)ia >= (unsigned)D.n || (unsigned)ib >= (unsigned)D.n)) {
-    // a sub-key id out of range can only come from a bug upstream: record
-    // it (status read by the host) and read row 0 instead of faulting
-    atomicCAS(err, 0, 21);
-    ia = 0;
-    ib = 0;
-  }
-  const int slot = ia * D.n + ib;                                            // memory.py:175
-  const float mx = warp_max(lk ? s : -INFINITY);
-  const float e = lk ? expf(s - mx) : 0.f;
-  const float w = e / warp_sum(e);                                           // memory.py:178
-  const float top1 = warp_max(lk ? w : -INFINITY);
+  const HeadPick p = combine_head<KM>(D, tab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
+  const int slot = p.slot, ia = p.ia, ib = p.ib;
+  const float w = p.w, top1 = p.top1;
   const int64_t ow = (m * D.H + h) * k;
   if (lk) {
     slots[ow + lane] = slot;
@@ -216,15 +97,6 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
       }
     }
   }
-}
-
-inline PairTable make_pairs(int k) {
-  PairTable t{};
-  int c = 0;
-  for (int i = 0; i < k; ++i)
-    for (int j = 0; j < k && (i + 1) * (j + 1) <= k; ++j) t.ij[c++] = (uint16_t)(i | (j << 8));
-  t.count = c;
-  return t;
 }
 
 template <int KM, typename VT, int VEC>

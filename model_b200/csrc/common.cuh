@@ -69,6 +69,7 @@ struct Work {
   int* slots = nullptr;        // [M,H,k] when the caller passes none
   float* weights = nullptr;    // [M,H,k] when the caller passes none
   float* out = nullptr;        // [M,d] when the caller passes none
+  int* own_cnt = nullptr;      // [M,world] entries each owner rank gathers (row-sharded pool)
 };
 
 constexpr int SCORE_TM = 128;   // tokens per score tile

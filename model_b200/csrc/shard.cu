@@ -1,0 +1,341 @@
+// Row-sharded value table over the GPUs of one node (one process per GPU).
+//
+// Slot s lives on rank s % world as local row s / world (striped, so a
+// popular cluster of slots spreads over every rank).  One forward is three
+// kernels per rank, each fused with its transfer over NVLink:
+//
+//   push    stage 2 of the search for this rank's tokens (as the single-GPU
+//           gather kernel), then every (local row, weight) entry is stored
+//           straight into its owner's inbox (peer memory), grouped per
+//           (source rank, token) in (head, rank) order;
+//   gather  each owner streams its local rows for every source rank's
+//           tokens (16-byte loads, float32 accumulation) and stores one
+//           partial row per (token, owner) straight into the token owner's
+//           buffer -- d floats cross NVLink instead of the H*k/world rows;
+//   reduce  the token owner adds the partials in rank order (deterministic)
+//           and applies the SiLU gate for the output projection.
+//
+// Hand-off between ranks: the last CTA of a kernel (completion ticket) makes
+// every CTA's peer stores visible (fence.acq_rel.sys) and release-stores
+// the call's epoch into a flag in each peer's buffer; consumers acquire-load
+// the flag before reading.  Every wait is bounded (about 2 s, global timer);
+// on timeout the kernel records a code in the caller's status word and
+// skips the work.  Buffers are reused across calls without a reset: a rank
+// cannot overwrite a peer's inbox or partials before the peer has consumed
+// them, because each rank's next push follows its own reduce, which waited
+// for every owner's gather of the previous call.
+#include <stdlib.h>
+
+#include "combine.cuh"
+#include "shard.cuh"
+
+namespace ml {
+
+namespace {
+
+constexpr long long kPeerWaitNs = 2000000000LL;   // 2 s
+
+__device__ __forceinline__ long long global_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Wait until *flag has reached epoch (wrap-safe).  Gives up after the time
+// limit, or at once when another wait of this call already gave up.
+__device__ bool wait_epoch(const int* flag, int epoch, int* err, int code) {
+  if (ld_acquire_sys(flag) - epoch >= 0) return true;
+  const long long t0 = global_ns();
+  while (true) {
+    if (*(volatile int*)err != 0) return false;
+    __nanosleep(128);
+    if (ld_acquire_sys(flag) - epoch >= 0) return true;
+    if (global_ns() - t0 > kPeerWaitNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ int* flag_ptr(const ShardK& S, int rank, int64_t off, int slot) {
+  return reinterpret_cast<int*>(S.peer[rank] + off) + slot;
+}
+
+// Called by thread 0 of every CTA after the CTA's stores: the last CTA
+// publishes the epoch into `flag_off`[S.rank] of every rank (and, when
+// meta >= 0, the token count into meta[S.rank] first).
+__device__ void publish_when_last(const ShardK& S, int ticket_slot, int64_t flag_off, int meta) {
+  fence_sys();
+  int* ticket = reinterpret_cast<int*>(S.peer[S.rank] + S.off.tickets) + ticket_slot;
+  if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
+  *ticket = 0;   // every CTA has counted: ready for the next call
+  fence_sys();
+  for (int o = 0; o < S.world; ++o) {
+    if (meta >= 0) *flag_ptr(S, o, S.off.meta, S.rank) = meta;
+    st_release_sys(flag_ptr(S, o, flag_off, S.rank), S.epoch);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// push: one CTA per token, one warp per head
+// ---------------------------------------------------------------------------
+template <int KM>
+__global__ void __launch_bounds__(1024) shard_push_kernel(
+    Dims D, const __grid_constant__ PairTable pairs, const __grid_constant__ ShardK S, const int* __restrict__ sub_idx,
+    const float* __restrict__ sub_score, const float* __restrict__ sub_sel, int* __restrict__ slots,
+    float* __restrict__ weights, float* __restrict__ slot_counts, float* __restrict__ subkey_counts,
+    float* __restrict__ top1_part, int* __restrict__ own_cnt, int* __restrict__ err) {
+  __shared__ uint16_t tab[128];
+  __shared__ int cnt_s[32][MEMLAYER_MAX_SHARDS];   // [head][owner] entries
+  for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
+  __syncthreads();
+  const int64_t m = blockIdx.x;
+  const bool active = m < D.M;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k = D.k, P = S.world;
+  const bool lk = lane < k;
+  int own = -1, pos = 0, lrow = 0;
+  float w = 0.f;
+  if (active) {
+    const int64_t ra = ((m * D.H + h) * 2) * k;
+    const HeadPick p = combine_head<KM>(D, tab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
+    w = p.w;
+    const int64_t ow = (m * D.H + h) * k;
+    if (lk) {
+      slots[ow + lane] = p.slot;
+      weights[ow + lane] = p.w;
+      if (slot_counts) atomicAdd(&slot_counts[p.slot], 1.f);                   // memory.py:216
+      if (subkey_counts) {                                                    // memory.py:205
+        atomicAdd(&subkey_counts[(int64_t)(h * 2) * D.n + p.ia], 1.f);
+        atomicAdd(&subkey_counts[(int64_t)(h * 2 + 1) * D.n + p.ib], 1.f);
+      }
+    }
+    if (lane == 0 && top1_part) top1_part[m * D.H + h] = p.top1;
+    // read (slot + N/2 + 1) % N under shuffle_reads (memory.py:179)
+    const int64_t rs = D.shuffle ? ((int64_t)p.slot + D.N / 2 + 1) % D.N : (int64_t)p.slot;
+    own = lk ? (int)(rs % P) : -1;
+    lrow = (int)(rs / P);
+    const unsigned lt = (1u << lane) - 1u;
+    for (int o = 0; o < P; ++o) {
+      const unsigned mk = __ballot_sync(FULL, own == o);
+      if (own == o) pos = __popc(mk & lt);
+      if (lane == 0) cnt_s[h][o] = __popc(mk);
+    }
+  }
+  __syncthreads();
+  if (active) {
+    if (own >= 0) {
+      int base = 0;
+      for (int hh = 0; hh < h; ++hh) base += cnt_s[hh][own];
+      int2* dst = reinterpret_cast<int2*>(S.peer[own] + S.off.inbox) + ((int64_t)S.rank * S.mcap + m) * S.hk +
+                  base + pos;
+      *dst = make_int2(lrow, __float_as_int(w));
+    }
+    if (threadIdx.x < P) {
+      const int o = threadIdx.x;
+      int total = 0;
+      for (int hh = 0; hh < D.H; ++hh) total += cnt_s[hh][o];
+      reinterpret_cast<int*>(S.peer[o] + S.off.cnt)[(int64_t)S.rank * S.mcap + m] = total;
+      own_cnt[m * P + o] = total;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) publish_when_last(S, 0, S.off.flags_in, (int)D.M);
+}
+
+// ---------------------------------------------------------------------------
+// gather: one warp per (source rank, token); this rank's own tokens first
+// ---------------------------------------------------------------------------
+template <typename VT, int VEC, int CH>
+__global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant__ ShardK S,
+                                                           const VT* __restrict__ values, int* __restrict__ err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * 8 + warp;
+  const int P = S.world, d = S.d;
+  if (gw < (int64_t)P * S.mcap) {
+    const int srot = (int)(gw / S.mcap);
+    const int64_t m = gw - (int64_t)srot * S.mcap;
+    const int src = (S.rank + srot) % P;
+    const char* mine = S.peer[S.rank];
+    if (wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + src, S.epoch, err, 31)) {
+      const int m_src = reinterpret_cast<const volatile int*>(mine + S.off.meta)[src];
+      const int64_t grp = (int64_t)src * S.mcap + m;
+      const int c = m < m_src ? reinterpret_cast<const volatile int*>(mine + S.off.cnt)[grp] : 0;
+      if (c > 0) {
+        const int2* ent = reinterpret_cast<const int2*>(mine + S.off.inbox) + grp * S.hk;
+        float acc[CH][VEC];
+#pragma unroll
+        for (int a = 0; a < CH; ++a)
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) acc[a][v] = 0.f;
+        const int groups = d / VEC;
+        for (int b0 = 0; b0 < c; b0 += 32) {
+          const int2 e = (b0 + lane < c) ? __ldcg(ent + b0 + lane) : make_int2(0, 0);
+          const int nb = min(32, c - b0);
+#pragma unroll 4
+          for (int j = 0; j < nb; ++j) {
+            const int row = __shfl_sync(FULL, e.x, j);
+            const float wr = __int_as_float(__shfl_sync(FULL, e.y, j));
+            if ((unsigned)row >= (unsigned)S.rows) {   // only a bug upstream can cause this
+              if (lane == 0) atomicCAS(err, 0, 22);
+              continue;
+            }
+            const VT* base = values + (int64_t)row * d;
+#pragma unroll
+            for (int a = 0; a < CH; ++a) {
+              const int g = a * 32 + lane;
+              if (g < groups) {
+                float x[VEC];
+                load_group<VT, VEC>(base + g * VEC, x);
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) acc[a][v] = fmaf(wr, x[v], acc[a][v]);
+              }
+            }
+          }
+        }
+        // the partial goes straight to the token owner's buffer
+        float* dst = reinterpret_cast<float*>(S.peer[src] + S.off.part) + ((int64_t)S.rank * S.mcap + m) * d;
+#pragma unroll
+        for (int a = 0; a < CH; ++a) {
+          const int g = a * 32 + lane;
+          if (g < groups) {
+#pragma unroll
+            for (int v = 0; v < VEC; v += 4)
+              *reinterpret_cast<float4*>(dst + g * VEC + v) =
+                  make_float4(acc[a][v], acc[a][v + 1], acc[a][v + 2], acc[a][v + 3]);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) publish_when_last(S, 1, S.off.flags_part, -1);
+}
+
+// ---------------------------------------------------------------------------
+// reduce: d/4 threads per token, float4 each
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) shard_reduce_kernel(const __grid_constant__ ShardK S, int64_t M,
+                                                           const int* __restrict__ own_cnt,
+                                                           const float* __restrict__ gate, float* __restrict__ out,
+                                                           float* __restrict__ memg, float* __restrict__ memg_hi,
+                                                           float* __restrict__ memg_lo, int* __restrict__ err) {
+  const int P = S.world, d4 = S.d / 4;
+  const char* mine = S.peer[S.rank];
+  bool ok = true;
+  for (int o = 0; o < P && ok; ++o)
+    ok = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_part) + o, S.epoch, err, 32);
+  const int per = blockDim.x / d4;
+  const int t = threadIdx.x / d4, i = threadIdx.x - t * d4;
+  const int64_t m = (int64_t)blockIdx.x * per + t;
+  if (!ok || t >= per || m >= M) return;
+  const float4* part = reinterpret_cast<const float4*>(mine + S.off.part);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int o = 0; o < P; ++o) {          // owners in rank order: deterministic
+    if (own_cnt[m * P + o] == 0) continue;
+    const float4 x = __ldcg(part + ((int64_t)o * S.mcap + m) * d4 + i);
+    acc.x += x.x;
+    acc.y += x.y;
+    acc.z += x.z;
+    acc.w += x.w;
+  }
+  const int64_t at = m * d4 + i;
+  if (out) reinterpret_cast<float4*>(out)[at] = acc;
+  if (memg || memg_hi) {
+    const float4 g = reinterpret_cast<const float4*>(gate)[at];      // model.py:119 mem * gate
+    const float4 v = make_float4(acc.x * g.x, acc.y * g.y, acc.z * g.z, acc.w * g.w);
+    if (memg) reinterpret_cast<float4*>(memg)[at] = v;
+    if (memg_hi) {
+      const float4 hi = make_float4(tc_round(v.x), tc_round(v.y), tc_round(v.z), tc_round(v.w));
+      reinterpret_cast<float4*>(memg_hi)[at] = hi;
+      reinterpret_cast<float4*>(memg_lo)[at] =
+          make_float4(tc_round(v.x - hi.x), tc_round(v.y - hi.y), tc_round(v.z - hi.z), tc_round(v.w - hi.w));
+    }
+  }
+}
+
+inline int ch_for(int groups) {
+  int ch = (groups + 31) / 32;
+  return ch <= 1 ? 1 : ch <= 2 ? 2 : ch <= 4 ? 4 : ch <= 8 ? 8 : -1;
+}
+
+template <typename VT, int VEC>
+cudaError_t gather_ch(const ShardK& S, const VT* values, int* err, cudaStream_t s) {
+  const int64_t warps = (int64_t)S.world * S.mcap;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+  switch (ch_for(S.d / VEC)) {
+    case 1: shard_gather_kernel<VT, VEC, 1><<<grid, 256, 0, s>>>(S, values, err); break;
+    case 2: shard_gather_kernel<VT, VEC, 2><<<grid, 256, 0, s>>>(S, values, err); break;
+    case 4: shard_gather_kernel<VT, VEC, 4><<<grid, 256, 0, s>>>(S, values, err); break;
+    case 8: shard_gather_kernel<VT, VEC, 8><<<grid, 256, 0, s>>>(S, values, err); break;
+    default: return cudaErrorInvalidValue;
+  }
+  count_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+ShardOff shard_layout(int world, int64_t mcap, int hk, int d) {
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  ShardOff o;
+  o.flags_in = 0;
+  o.flags_part = 256;
+  o.meta = 512;
+  o.tickets = 768;
+  o.cnt = 1024;
+  o.inbox = o.cnt + up((int64_t)world * mcap * 4);
+  o.part = o.inbox + up((int64_t)world * mcap * hk * 8);
+  o.bytes = o.part + up((int64_t)world * mcap * d * 4);
+  return o;
+}
+
+cudaError_t launch_shard_push(const Dims& D, const Work& W, const ShardK& S, int* slots, float* weights,
+                              float* slot_counts, float* subkey_counts, int* own_cnt, cudaStream_t s) {
+  const PairTable pairs = make_pairs(D.k);
+  const unsigned grid = (unsigned)(D.M > 0 ? D.M : 1);   // one CTA still publishes an empty call
+  const dim3 block(32 * D.H);
+#define ML_SP(KV)                                                                                          \
+  shard_push_kernel<KV><<<grid, block, 0, s>>>(D, pairs, S, W.sub_idx, W.sub_score, W.sub_sel, slots, weights, \
+                                               slot_counts, subkey_counts, W.top1_part, own_cnt, W.err)
+  switch (D.kmax) {
+    case 4: ML_SP(4); break;
+    case 8: ML_SP(8); break;
+    case 16: ML_SP(16); break;
+    case 32: ML_SP(32); break;
+    default: return cudaErrorInvalidValue;
+  }
+#undef ML_SP
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_shard_gather(const Dims& D, const ShardK& S, const void* values, int* err, cudaStream_t s) {
+  if (D.vdtype == MEMLAYER_F16) return gather_ch<__half, 8>(S, (const __half*)values, err, s);
+  if (D.vdtype == MEMLAYER_BF16) return gather_ch<__nv_bfloat16, 8>(S, (const __nv_bfloat16*)values, err, s);
+  return gather_ch<float, 4>(S, (const float*)values, err, s);
+}
+
+cudaError_t launch_shard_reduce(const Dims& D, const ShardK& S, const int* own_cnt, const float* gate, float* out,
+                                float* memg, float* memg_hi, float* memg_lo, int* err, cudaStream_t s) {
+  const int d4 = S.d / 4;
+  const int per = 256 / d4;
+  const unsigned grid = (unsigned)(D.M > 0 ? (D.M + per - 1) / per : 1);
+  shard_reduce_kernel<<<grid, 256, 0, s>>>(S, D.M, own_cnt, gate, out, memg, memg_hi, memg_lo, err);
+  count_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace ml

@@ -1,0 +1,204 @@
+"""Row-sharded value table over the GPUs of one node (host side).
+
+The reference replicates every parameter, the value table included, on each
+device of its data-parallel mesh (memory_pool_model/train.py:229-236,267);
+this module serves tables larger than one GPU.  Slot ``s`` lives on rank
+``s % world`` as local row ``s // world``; sub-keys and the Dense kernels
+are replicated.  Each rank routes its own tokens, the owners gather their
+rows and return one float32 partial row per (token, owner) over NVLink, and
+the token owner adds the partials in rank order (see
+``model_b200/csrc/shard.cu``).
+
+One process per GPU: :func:`connect` creates this rank's communicator and
+maps every peer's buffer through CUDA IPC handles exchanged with
+``torch.distributed.all_gather_object``.  :class:`ShardedCall` also runs the
+three phases separately, which lets one process drive several emulated ranks
+on one GPU (tests).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from . import _lib as L
+from .memory import MemoryLayer, MemoryPool, _cuda_f32, _ptr, _raise_device_status, _workspace
+
+
+def shard_rows(pool_size: int, rank: int, world: int) -> int:
+    """Rows held by ``rank``: slots s < pool_size with s % world == rank."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    return max(0, (pool_size - rank + world - 1) // world)
+
+
+def shard_values(values: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's local rows of a full table (row s // world of rank s % world)."""
+    return values[rank::world].contiguous()
+
+
+def owner_of(slots: torch.Tensor, world: int):
+    """(owner rank, local row) of each slot id."""
+    return slots % world, slots // world
+
+
+class ShardComm:
+    """This rank's communicator (memlayer_shard_comm) for one set of shapes."""
+
+    def __init__(self, cfg: L.MemlayerConfig, rank: int, world: int):
+        self.rank, self.world = rank, world
+        self.cfg = cfg
+        h = C.c_void_p()
+        L.check(L.lib().memlayer_shard_comm_create(C.byref(cfg), rank, world, C.byref(h)),
+                "memlayer_shard_comm_create")
+        self.handle = h
+        dev, nbytes = C.c_int32(), C.c_size_t()
+        L.check(L.lib().memlayer_shard_comm_info(h, None, None, C.byref(dev), C.byref(nbytes)),
+                "memlayer_shard_comm_info")
+        self.device, self.nbytes = dev.value, nbytes.value
+        if self.device != torch.cuda.current_device():
+            self.close()
+            raise RuntimeError(f"library device {self.device} != torch current device "
+                               f"{torch.cuda.current_device()}: call torch.cuda.set_device first")
+
+    def ipc_handle(self) -> bytes:
+        buf = (C.c_char * L.IPC_HANDLE_BYTES)()
+        L.check(L.lib().memlayer_shard_comm_ipc_handle(self.handle, buf), "memlayer_shard_comm_ipc_handle")
+        return bytes(buf)
+
+    def open_peers(self, handles: Sequence[bytes]) -> None:
+        if len(handles) != self.world or any(len(h) != L.IPC_HANDLE_BYTES for h in handles):
+            raise ValueError(f"need {self.world} handles of {L.IPC_HANDLE_BYTES} bytes")
+        blob = b"".join(handles)
+        L.check(L.lib().memlayer_shard_comm_open_peers(self.handle, blob), "memlayer_shard_comm_open_peers")
+
+    def set_peer(self, other: "ShardComm") -> None:
+        L.check(L.lib().memlayer_shard_comm_set_peer(self.handle, other.rank, other.handle),
+                "memlayer_shard_comm_set_peer")
+
+    def close(self) -> None:
+        if self.handle:
+            L.check(L.lib().memlayer_shard_comm_destroy(self.handle), "memlayer_shard_comm_destroy")
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def exchange_handles(handle: bytes, group=None) -> List[bytes]:
+    """All ranks' IPC handles in rank order (any torch.distributed backend)."""
+    import torch.distributed as dist
+
+    out: List[Optional[bytes]] = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, handle, group=group)
+    return [bytes(h) for h in out]
+
+
+def connect(cfg: L.MemlayerConfig, group=None) -> ShardComm:
+    """Create this rank's communicator and map every peer's buffer.  Collective
+    over ``group``: every rank calls it with the same shapes."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    shapes: List[Optional[tuple]] = [None] * world
+    mine = tuple(getattr(cfg, f) for f, _ in cfg._fields_)
+    dist.all_gather_object(shapes, mine, group=group)
+    if any(s != mine for s in shapes):
+        raise ValueError("every rank must create its communicator with the same config")
+    comm = ShardComm(cfg, dist.get_rank(group), world)
+    comm.open_peers(exchange_handles(comm.ipc_handle(), group))
+    dist.barrier(group)
+    return comm
+
+
+def emulated_comms(cfg: L.MemlayerConfig, world: int) -> List[ShardComm]:
+    """``world`` communicators in this process on the current device, wired to
+    each other directly (no IPC): for driving every rank from one process."""
+    comms = [ShardComm(cfg, r, world) for r in range(world)]
+    for c in comms:
+        for o in comms:
+            if o is not c:
+                c.set_peer(o)
+    return comms
+
+
+class ShardedCall:
+    """One sharded memory-layer forward on one rank, with its buffers kept
+    alive so that the three phases can be run separately."""
+
+    def __init__(self, layer: MemoryLayer, comm: ShardComm, params: Dict, h: torch.Tensor, *,
+                 train: bool = False, noise_scale: float = 1.0,
+                 shuffle_reads: bool = False, rngs=None, gumbel=None, stats: bool = False):
+        P = layer.pool
+        self.layer, self.comm, self.stats = layer, comm, stats
+        h = _cuda_f32(h, "h")
+        self.lead = tuple(h.shape[:-1])
+        M = int(math.prod(self.lead)) if self.lead else 1
+        device = h.device
+        if device.index != comm.device:
+            raise ValueError(f"h is on {device}, the communicator on cuda:{comm.device}")
+        pool = params["pool"]
+        values = pool["values"]
+        if M > comm.cfg.tokens:
+            raise ValueError(f"{M} tokens exceed the communicator's capacity {comm.cfg.tokens}")
+        want = shard_rows(P.pool_size, comm.rank, comm.world)
+        if values.shape[0] != want:
+            raise ValueError(f"rank {comm.rank} holds {want} rows, values has {values.shape[0]}")
+        self.cfg = P.config(M, values.dtype, layer.d_model)
+        r, g_, o = (params[f"{n}_{layer.layer}"] for n in ("router", "mem_gate", "mem_out"))
+        a, self.keep = P._pool_args(pool, M, device, train=train, noise_scale=noise_scale,
+                                    shuffle_reads=shuffle_reads, rngs=rngs, gumbel=gumbel, stats=stats)
+        self.w = {k: _cuda_f32(v, k) for k, v in (("wr", r["kernel"]), ("br", r["bias"]), ("wg", g_["kernel"]),
+                                                  ("bg", g_["bias"]), ("wo", o["kernel"]), ("bo", o["bias"]))}
+        self.h = h
+        self.y = torch.empty(*self.lead, layer.d_model, dtype=torch.float32, device=device)
+        self.mem = torch.empty(*self.lead, P.d_value, dtype=torch.float32, device=device)
+        w = self.w
+        self.args = L.MemlayerLayerArgs(h=h.data_ptr(), w_router=_ptr(w["wr"]), b_router=_ptr(w["br"]),
+                                        w_gate=_ptr(w["wg"]), b_gate=_ptr(w["bg"]), w_out=_ptr(w["wo"]),
+                                        b_out=_ptr(w["bo"]), y=self.y.data_ptr(), mem=self.mem.data_ptr(), pool=a)
+        nbytes = C.c_size_t()
+        L.check(L.lib().memlayer_shard_workspace_size(C.byref(self.cfg), comm.world, 1, C.byref(nbytes)),
+                "memlayer_shard_workspace_size")
+        self.nbytes = nbytes.value
+        self.ws = _workspace(self.nbytes, device)
+
+    def run(self, phases: int = L.PHASE_ALL, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.h.device)).cuda_stream
+        L.check(L.lib().memlayer_layer_forward_sharded(C.byref(self.cfg), C.byref(self.args), self.comm.handle,
+                                                       phases, self.ws.data_ptr(), self.nbytes, s),
+                "memlayer_layer_forward_sharded")
+
+    def check(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.h.device)).cuda_stream
+        _raise_device_status(self.cfg, self.ws, s)
+
+    def result(self):
+        """(y, mem, aux) as MemoryLayer.apply returns them."""
+        return self.y, self.mem, self.layer.pool._aux(self.keep, self.lead, self.stats)
+
+
+class ShardedMemoryLayer:
+    """MemoryLayer whose value table is row-sharded over a communicator's
+    ranks.  ``params["pool"]["values"]`` is this rank's local shard
+    (:func:`shard_values`)."""
+
+    def __init__(self, layer: MemoryLayer, comm: ShardComm):
+        self.layer, self.comm = layer, comm
+
+    @property
+    def pool(self) -> MemoryPool:
+        return self.layer.pool
+
+    def apply(self, params, h: torch.Tensor, *, check: bool = False, stream=None, **kw):
+        call = ShardedCall(self.layer, self.comm, params, h, **kw)
+        call.run(L.PHASE_ALL, stream)
+        if check:
+            call.check(stream)
+        return call.result()
