@@ -244,6 +244,53 @@ int32_t memlayer_layer_forward_sharded(const memlayer_config* cfg, const memlaye
                                        memlayer_shard_comm* comm, int32_t phases, void* workspace,
                                        size_t workspace_bytes, void* stream);
 
+/* ---- Fetched-row gradients and row-wise Adagrad (training) ---------------
+ * With sparse_grad the value table gets no dense gradient; the trainer
+ * reads dL/d(read output) from zero "probes" added to each read
+ * (model.py:114-115) and turns it into per-row gradients of the fetched
+ * rows only.  One read = one memory layer's call on the shared pool. */
+#define MEMLAYER_MAX_READS 8
+
+typedef struct {
+  const int32_t* slots;          /* [tokens, H, k] the read's aux["slots"] */
+  const float* weights;          /* [tokens, H, k] the read's aux["weights"] */
+  const float* grad;             /* [tokens, d] dL/d(read output), 16-byte aligned */
+  int64_t tokens;
+} memlayer_read;
+
+/* Workspace bytes for `fetches` = sum over the reads of tokens * H * k. */
+int32_t memlayer_rowgrad_workspace_size(const memlayer_config* cfg, int64_t fetches, size_t* bytes);
+
+/* fetched_row_grads + _merge_rows (memory_pool_model/train.py:146-172):
+ * uniq [cap] = the distinct fetched slots in ascending order, padded with
+ * n*n; rows [cap, d] = for each, the sum over its fetches of w * grad[token]
+ * (zero rows for the padding); cap = min(fetches, n*n).  Fetches of every
+ * slot are summed in fetch order (reads in argument order, then token,
+ * head, rank), so results are deterministic.  rows, n_unique [1] and
+ * sq_norm [1] (sum of rows^2, for the global-norm clip) may be NULL.
+ * cfg supplies heads, top_k, n_sub_keys and d_value (tokens is ignored). */
+int32_t memlayer_fetched_row_grads(const memlayer_config* cfg, const memlayer_read* reads, int32_t n_reads,
+                                   int32_t* uniq, float* rows, int32_t* n_unique, float* sq_norm,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
+typedef struct {
+  float* values;                 /* [n*n, d] float32 value table, updated in place */
+  float* accum;                  /* [n*n] Adagrad accumulator (the trainer's pool_v), updated in place */
+  float lr;                      /* schedule(step) * pool_lr_mult */
+  float grad_clip;               /* global-norm clip threshold (train.py grad_clip) */
+  const float* rest_sq_norm;     /* [1] squared norm of all other gradients, or NULL for 0 */
+  float* clip_scale;             /* [1] optional output: min(1, clip / (norm + 1e-6)) */
+  int32_t* n_unique;             /* [1] optional output: touched rows */
+} memlayer_adagrad_args;
+
+/* Row-wise Adagrad on the fetched rows (train.py:378-383 clip by the
+ * global norm of both parts, :396-399 update): with g = scale * row grad,
+ * accum[s] += mean(g^2); values[s] -= lr / (sqrt(accum[s]) + 1e-8) * g,
+ * for every touched slot s only.  Float32 tables only. */
+int32_t memlayer_row_adagrad(const memlayer_config* cfg, const memlayer_read* reads, int32_t n_reads,
+                             const memlayer_adagrad_args* args, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* Size of the library's built-in scratch array used by
  * memlayer_pool_forward_noalloc (64 MiB, held on every GPU that loads the
  * library until the process exits). */

@@ -82,9 +82,29 @@ class MemlayerLayerArgs(C.Structure):
     ]
 
 
+MAX_READS = 8
+
+
+class MemlayerRead(C.Structure):
+    _fields_ = [("slots", C.c_void_p), ("weights", C.c_void_p), ("grad", C.c_void_p), ("tokens", C.c_int64)]
+
+
+class MemlayerAdagradArgs(C.Structure):
+    _fields_ = [
+        ("values", C.c_void_p),
+        ("accum", C.c_void_p),
+        ("lr", C.c_float),
+        ("grad_clip", C.c_float),
+        ("rest_sq_norm", C.c_void_p),
+        ("clip_scale", C.c_void_p),
+        ("n_unique", C.c_void_p),
+    ]
+
+
 DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "MMA wait timed out",
                  14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
                  21: "sub-key id out of range", 22: "sharded row id out of range",
+                 23: "fetched slot id out of range",
                  31: "peer inbox wait timed out", 32: "peer partial-sum wait timed out"}
 
 
@@ -148,6 +168,15 @@ def lib() -> C.CDLL:
         L.memlayer_layer_forward_sharded.restype = C.c_int32
         L.memlayer_layer_forward_sharded.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
                                                      C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_rowgrad_workspace_size.restype = C.c_int32
+        L.memlayer_rowgrad_workspace_size.argtypes = [C.POINTER(MemlayerConfig), C.c_int64, C.POINTER(C.c_size_t)]
+        L.memlayer_fetched_row_grads.restype = C.c_int32
+        L.memlayer_fetched_row_grads.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerRead), C.c_int32,
+                                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                 C.c_size_t, C.c_void_p]
+        L.memlayer_row_adagrad.restype = C.c_int32
+        L.memlayer_row_adagrad.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerRead), C.c_int32,
+                                           C.POINTER(MemlayerAdagradArgs), C.c_void_p, C.c_size_t, C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

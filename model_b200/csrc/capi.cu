@@ -8,6 +8,7 @@
 #include <new>
 
 #include "common.cuh"
+#include "rowgrad.cuh"
 #include "shard.cuh"
 
 namespace ml {
@@ -365,6 +366,35 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
   return MEMLAYER_OK;
 }
 
+// Reads of a row-gradient call: shapes, pointers and fetch offsets.
+int rowgrad_setup(const memlayer_config* cfg, const memlayer_read* reads, int n_reads, RowGradK* R) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!reads) return MEMLAYER_ERR_BAD_POINTER;
+  if (n_reads < 1 || n_reads > MEMLAYER_MAX_READS) return MEMLAYER_ERR_BAD_SHAPE;
+  if (D.d % 4) return MEMLAYER_ERR_UNSUPPORTED;
+  *R = RowGradK{};
+  R->n_reads = n_reads;
+  R->N = D.N;
+  R->hk = D.H * D.k;
+  R->d = D.d;
+  R->off[0] = 0;
+  for (int r = 0; r < n_reads; ++r) {
+    const memlayer_read& x = reads[r];
+    if (x.tokens < 0) return MEMLAYER_ERR_BAD_SHAPE;
+    if (x.tokens > 0 && (!x.slots || !x.weights || !x.grad)) return MEMLAYER_ERR_BAD_POINTER;
+    if (!aligned16(x.grad)) return MEMLAYER_ERR_BAD_POINTER;
+    R->slots[r] = x.slots;
+    R->weights[r] = x.weights;
+    R->grad[r] = x.grad;
+    R->off[r + 1] = R->off[r] + x.tokens * R->hk;
+  }
+  R->F = R->off[n_reads];
+  if (R->F >= (1LL << 31)) return MEMLAYER_ERR_BAD_SHAPE;   // fetch ids are 32-bit
+  return MEMLAYER_OK;
+}
+
 }  // namespace
 }  // namespace ml
 
@@ -560,6 +590,49 @@ int32_t memlayer_layer_forward_sharded(const memlayer_config* cfg, const memlaye
   if (!comm) return MEMLAYER_ERR_BAD_POINTER;
   if (phases < 1 || phases > MEMLAYER_PHASE_ALL) return MEMLAYER_ERR_BAD_SHAPE;
   return layer_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
+}
+
+// ---- fetched-row gradients / row-wise Adagrad ----
+
+int32_t memlayer_rowgrad_workspace_size(const memlayer_config* cfg, int64_t fetches, size_t* bytes) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  if (fetches < 0 || fetches >= (1LL << 31)) return MEMLAYER_ERR_BAD_SHAPE;
+  *bytes = (size_t)rowgrad_layout(fetches, D.N, D.d).bytes;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_fetched_row_grads(const memlayer_config* cfg, const memlayer_read* reads, int32_t n_reads,
+                                   int32_t* uniq, float* rows, int32_t* n_unique, float* sq_norm,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  RowGradK R;
+  int st = rowgrad_setup(cfg, reads, n_reads, &R);
+  if (st) return st;
+  if ((!uniq && R.F > 0) || !aligned16(rows)) return MEMLAYER_ERR_BAD_POINTER;
+  const RowGradLayout L = rowgrad_layout(R.F, R.N, R.d);
+  if (!workspace || workspace_bytes < (size_t)L.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  ML_TRY(launch_rowgrad(R, L, (char*)workspace, uniq, rows, n_unique, sq_norm, nullptr, (cudaStream_t)stream));
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_row_adagrad(const memlayer_config* cfg, const memlayer_read* reads, int32_t n_reads,
+                             const memlayer_adagrad_args* args, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  RowGradK R;
+  int st = rowgrad_setup(cfg, reads, n_reads, &R);
+  if (st) return st;
+  if (!args || !args->values || !args->accum || !aligned16(args->values)) return MEMLAYER_ERR_BAD_POINTER;
+  if (cfg->values_dtype != MEMLAYER_F32) return MEMLAYER_ERR_UNSUPPORTED;
+  const RowGradLayout L = rowgrad_layout(R.F, R.N, R.d);
+  if (!workspace || workspace_bytes < (size_t)L.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  RowAdagrad A{args->values, args->accum, args->lr, args->grad_clip, args->rest_sq_norm, args->clip_scale,
+               args->n_unique};
+  ML_TRY(launch_rowgrad(R, L, (char*)workspace, nullptr, nullptr, nullptr, nullptr, &A, (cudaStream_t)stream));
+  return MEMLAYER_OK;
 }
 
 }  // extern "C"

@@ -89,66 +89,72 @@ __device__ void publish_when_last(const ShardK& S, int ticket_slot, int64_t flag
 }
 
 // ---------------------------------------------------------------------------
-// push: one CTA per token, one warp per head
+// push: TPC tokens per CTA (one warp per (token, head)), grid-stride over the
+// tokens with one completion fence per CTA
 // ---------------------------------------------------------------------------
 template <int KM>
 __global__ void __launch_bounds__(1024) shard_push_kernel(
-    Dims D, const __grid_constant__ PairTable pairs, const __grid_constant__ ShardK S, const int* __restrict__ sub_idx,
-    const float* __restrict__ sub_score, const float* __restrict__ sub_sel, int* __restrict__ slots,
-    float* __restrict__ weights, float* __restrict__ slot_counts, float* __restrict__ subkey_counts,
-    float* __restrict__ top1_part, int* __restrict__ own_cnt, int* __restrict__ err) {
+    Dims D, int tpc, const __grid_constant__ PairTable pairs, const __grid_constant__ ShardK S,
+    const int* __restrict__ sub_idx, const float* __restrict__ sub_score, const float* __restrict__ sub_sel,
+    int* __restrict__ slots, float* __restrict__ weights, float* __restrict__ slot_counts,
+    float* __restrict__ subkey_counts, float* __restrict__ top1_part, int* __restrict__ own_cnt,
+    int* __restrict__ err) {
   __shared__ uint16_t tab[128];
-  __shared__ int cnt_s[32][MEMLAYER_MAX_SHARDS];   // [head][owner] entries
+  __shared__ int cnt_s[32][MEMLAYER_MAX_SHARDS];   // [warp][owner] entries
   for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
-  __syncthreads();
-  const int64_t m = blockIdx.x;
-  const bool active = m < D.M;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = wid / D.H, h = wid - t * D.H;        // token slot in the CTA, head
   const int k = D.k, P = S.world;
   const bool lk = lane < k;
-  int own = -1, pos = 0, lrow = 0;
-  float w = 0.f;
-  if (active) {
-    const int64_t ra = ((m * D.H + h) * 2) * k;
-    const HeadPick p = combine_head<KM>(D, tab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
-    w = p.w;
-    const int64_t ow = (m * D.H + h) * k;
-    if (lk) {
-      slots[ow + lane] = p.slot;
-      weights[ow + lane] = p.w;
-      if (slot_counts) atomicAdd(&slot_counts[p.slot], 1.f);                   // memory.py:216
-      if (subkey_counts) {                                                    // memory.py:205
-        atomicAdd(&subkey_counts[(int64_t)(h * 2) * D.n + p.ia], 1.f);
-        atomicAdd(&subkey_counts[(int64_t)(h * 2 + 1) * D.n + p.ib], 1.f);
+  const unsigned lt = (1u << lane) - 1u;
+  for (int64_t m0 = (int64_t)blockIdx.x * tpc; m0 < D.M; m0 += (int64_t)gridDim.x * tpc) {
+    const int64_t m = m0 + t;
+    const bool active = m < D.M;
+    int own = -1, pos = 0, lrow = 0;
+    float w = 0.f;
+    __syncthreads();                                 // tab staged / previous cnt_s consumed
+    if (active) {
+      const int64_t ra = ((m * D.H + h) * 2) * k;
+      const HeadPick p = combine_head<KM>(D, tab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
+      w = p.w;
+      const int64_t ow = (m * D.H + h) * k;
+      if (lk) {
+        slots[ow + lane] = p.slot;
+        weights[ow + lane] = p.w;
+        if (slot_counts) atomicAdd(&slot_counts[p.slot], 1.f);                   // memory.py:216
+        if (subkey_counts) {                                                    // memory.py:205
+          atomicAdd(&subkey_counts[(int64_t)(h * 2) * D.n + p.ia], 1.f);
+          atomicAdd(&subkey_counts[(int64_t)(h * 2 + 1) * D.n + p.ib], 1.f);
+        }
+      }
+      if (lane == 0 && top1_part) top1_part[m * D.H + h] = p.top1;
+      // read (slot + N/2 + 1) % N under shuffle_reads (memory.py:179)
+      const int64_t rs = D.shuffle ? ((int64_t)p.slot + D.N / 2 + 1) % D.N : (int64_t)p.slot;
+      own = lk ? (int)(rs % P) : -1;
+      lrow = (int)(rs / P);
+      for (int o = 0; o < P; ++o) {
+        const unsigned mk = __ballot_sync(FULL, own == o);
+        if (own == o) pos = __popc(mk & lt);
+        if (lane == 0) cnt_s[wid][o] = __popc(mk);
       }
     }
-    if (lane == 0 && top1_part) top1_part[m * D.H + h] = p.top1;
-    // read (slot + N/2 + 1) % N under shuffle_reads (memory.py:179)
-    const int64_t rs = D.shuffle ? ((int64_t)p.slot + D.N / 2 + 1) % D.N : (int64_t)p.slot;
-    own = lk ? (int)(rs % P) : -1;
-    lrow = (int)(rs / P);
-    const unsigned lt = (1u << lane) - 1u;
-    for (int o = 0; o < P; ++o) {
-      const unsigned mk = __ballot_sync(FULL, own == o);
-      if (own == o) pos = __popc(mk & lt);
-      if (lane == 0) cnt_s[h][o] = __popc(mk);
-    }
-  }
-  __syncthreads();
-  if (active) {
-    if (own >= 0) {
-      int base = 0;
-      for (int hh = 0; hh < h; ++hh) base += cnt_s[hh][own];
-      int2* dst = reinterpret_cast<int2*>(S.peer[own] + S.off.inbox) + ((int64_t)S.rank * S.mcap + m) * S.hk +
-                  base + pos;
-      *dst = make_int2(lrow, __float_as_int(w));
-    }
-    if (threadIdx.x < P) {
-      const int o = threadIdx.x;
-      int total = 0;
-      for (int hh = 0; hh < D.H; ++hh) total += cnt_s[hh][o];
-      reinterpret_cast<int*>(S.peer[o] + S.off.cnt)[(int64_t)S.rank * S.mcap + m] = total;
-      own_cnt[m * P + o] = total;
+    __syncthreads();
+    if (active) {
+      // entries of (token, owner) in (head, rank) order
+      if (own >= 0) {
+        int base = 0;
+        for (int hh = 0; hh < h; ++hh) base += cnt_s[t * D.H + hh][own];
+        int2* dst = reinterpret_cast<int2*>(S.peer[own] + S.off.inbox) +
+                    ((int64_t)S.rank * S.mcap + m) * S.hk + base + pos;
+        *dst = make_int2(lrow, __float_as_int(w));
+      }
+      if (h == 0 && lane < P) {
+        const int o = lane;
+        int total = 0;
+        for (int hh = 0; hh < D.H; ++hh) total += cnt_s[t * D.H + hh][o];
+        reinterpret_cast<int*>(S.peer[o] + S.off.cnt)[(int64_t)S.rank * S.mcap + m] = total;
+        own_cnt[m * P + o] = total;
+      }
     }
   }
   __syncthreads();
@@ -305,10 +311,15 @@ ShardOff shard_layout(int world, int64_t mcap, int hk, int d) {
 cudaError_t launch_shard_push(const Dims& D, const Work& W, const ShardK& S, int* slots, float* weights,
                               float* slot_counts, float* subkey_counts, int* own_cnt, cudaStream_t s) {
   const PairTable pairs = make_pairs(D.k);
-  const unsigned grid = (unsigned)(D.M > 0 ? D.M : 1);   // one CTA still publishes an empty call
-  const dim3 block(32 * D.H);
-#define ML_SP(KV)                                                                                          \
-  shard_push_kernel<KV><<<grid, block, 0, s>>>(D, pairs, S, W.sub_idx, W.sub_score, W.sub_sel, slots, weights, \
+  // TPC tokens per CTA of up to 512 threads; at most one wave of CTAs (each
+  // pays one system-scope fence), at least one CTA to publish an empty call
+  const int tpc = D.H >= 16 ? 1 : 16 / D.H;
+  const dim3 block(32 * D.H * tpc);
+  const int per_sm = 2048 / (int)block.x;
+  const int64_t groups = (D.M + tpc - 1) / tpc;
+  const unsigned grid = (unsigned)(groups < 1 ? 1 : groups < 148LL * per_sm ? groups : 148LL * per_sm);
+#define ML_SP(KV)                                                                                               \
+  shard_push_kernel<KV><<<grid, block, 0, s>>>(D, tpc, pairs, S, W.sub_idx, W.sub_score, W.sub_sel, slots, weights, \
                                                slot_counts, subkey_counts, W.top1_part, own_cnt, W.err)
   switch (D.kmax) {
     case 4: ML_SP(4); break;

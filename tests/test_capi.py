@@ -36,6 +36,8 @@ def test_struct_sizes_match_header_layout():
     assert C.sizeof(L.MemlayerConfig) == 8 + 12 * 4
     assert C.sizeof(L.MemlayerPoolArgs) == 5 * 8 + 4 * 3 + 4 + 10 * 8  # 4 bytes of padding before `out`
     assert C.sizeof(L.MemlayerLayerArgs) == 9 * 8 + C.sizeof(L.MemlayerPoolArgs)
+    assert C.sizeof(L.MemlayerRead) == 4 * 8
+    assert C.sizeof(L.MemlayerAdagradArgs) == 2 * 8 + 2 * 4 + 3 * 8
 
 
 def cfg(**kw):
