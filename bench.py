@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--values-dtype", choices=["f32", "f16", "bf16"], default="f32")
     ap.add_argument("--tokens", type=int, default=WORKLOAD["tokens_per_gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--host-chunks", type=int, default=4,
+                    help="chunks of the host-buffer pipeline timed as e2e (memlayer_layer_forward_host)")
     ap.add_argument("--pool", choices=["sharded", "replicated"], default="sharded",
                     help="N>1: row-shard the value table over the ranks (default) or replicate it")
     return ap.parse_args()
@@ -366,30 +368,72 @@ def run_ours(args, W, rank, world):
     ms = statistics.mean(step_ms)
 
     # ---- e2e through the C ABI with host buffers ----
-    h_host = x["h"].cpu().pin_memory()
-    y_host = torch.empty_like(call.y, device="cpu").pin_memory()
-    e0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    e1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    for _ in range(max(1, args.warmup // 2)):
-        x["h"].copy_(h_host, non_blocking=True)
-        call(stream)
-        y_host.copy_(call.y, non_blocking=True)
-    torch.cuda.synchronize()
-    for i in range(K):
-        flush.zero_()
-        e0[i].record(stream)
-        x["h"].copy_(h_host, non_blocking=True)
-        call(stream)
-        y_host.copy_(call.y, non_blocking=True)
-        e1[i].record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
+    # Two calls in flight on two streams (double-buffered host / staging
+    # buffers): one call's host-to-device copy overlaps the other's layer.
+    # Every step copies its hidden state in from pinned host memory and its
+    # output back; e2e = K steps of tokens over the device time of all K.
+    # `e2e_serial` is the same with one call at a time.
+    streams = [stream, torch.cuda.Stream(device)]
+    h_hosts = [x["h"].cpu().pin_memory() for _ in range(2)]
+    y_hosts = [torch.empty_like(call.y, device="cpu").pin_memory() for _ in range(2)]
+    if sharded:
 
+        def host_step(j):
+            # the sharded call runs on the default stream (all ranks in lockstep)
+            x["h"].copy_(h_hosts[j], non_blocking=True)
+            call(stream)
+            y_hosts[j].copy_(call.y, non_blocking=True)
+        inflight = 1
+        e2e_api = "memlayer_layer_forward_sharded with host copies around it"
+    else:
+        hnb = C.c_size_t()
+        L.check(lib.memlayer_layer_host_workspace_size(C.byref(call.cfg), args.host_chunks, C.byref(hnb)), "host ws")
+        hws = [torch.empty(hnb.value, dtype=torch.uint8, device=device) for _ in range(2)]
+        hargs = []
+        for j in range(2):
+            a_ = L.MemlayerLayerArgs.from_buffer_copy(call.args)
+            a_.h, a_.y = h_hosts[j].data_ptr(), y_hosts[j].data_ptr()
+            a_.pool.top1_weight = None
+            a_.pool.stage_events = None
+            if j:   # the second call in flight writes its own routing outputs
+                extra = [torch.empty_like(call.slots), torch.empty_like(call.weights), torch.empty_like(call.temp)]
+                a_.pool.slots, a_.pool.weights, a_.pool.temperature = (t.data_ptr() for t in extra)
+                hargs_keep = extra
+            hargs.append(a_)
+
+        def host_step(j):
+            L.check(lib.memlayer_layer_forward_host(C.byref(call.cfg), C.byref(hargs[j]), args.host_chunks,
+                                                    hws[j].data_ptr(), hnb.value, streams[j].cuda_stream),
+                    "memlayer_layer_forward_host")
+        inflight = 2
+        e2e_api = (f"memlayer_layer_forward_host ({args.host_chunks} chunk(s), pinned host h / y), "
+                   "2 calls in flight on 2 streams")
+
+    def e2e_run(n_inflight, steps):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for st in streams[1:n_inflight]:
+            st.wait_event(start)
+        for i in range(steps):
+            with torch.cuda.stream(streams[i % n_inflight]):
+                host_step(i % n_inflight)
+        for st in streams[1:n_inflight]:
+            stream.wait_stream(st)
+        end.record(stream)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / steps
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_run(inflight, 2)
+    e2e_ms = e2e_run(inflight, K)
+    e2e_serial_ms = e2e_run(1, max(1, K // 2))
     gather_stage = stages["shard_gather"] if sharded else stages["combine_gather"]
-    stats = torch.tensor([ms, e2e_ms, gather_stage, stages["score_topk"]], dtype=torch.float64, device=device)
+    stats = torch.tensor([ms, e2e_ms, gather_stage, stages["score_topk"], e2e_serial_ms], dtype=torch.float64,
+                         device=device)
     if world > 1:
         torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
-    ms, e2e_ms, gather_ms, score_ms = stats.tolist()
+    ms, e2e_ms, gather_ms, score_ms, e2e_serial_ms = stats.tolist()
     if sharded:                    # every rank's kernels are done before the peers are unmapped
         torch.cuda.synchronize()
         torch.distributed.barrier()
@@ -437,7 +481,11 @@ def run_ours(args, W, rank, world):
         **({"nvlink_partial_gbs_per_gpu": nvlink_b / (gather_ms * 1e-3) / 1e9} if sharded else {}),
         "stages_ms": stages,
         "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": h_host.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4},
+                "h2d_bytes_per_step": h_hosts[0].numel() * 4, "d2h_bytes_per_step": y_hosts[0].numel() * 4,
+                "api": e2e_api, "ms_per_step": e2e_ms, "calls_in_flight": inflight,
+                "l2": "not flushed: every step reads the 268 MB value table, larger than L2"},
+        "e2e_serial": {"value": T * world / (e2e_serial_ms * 1e-3), "unit": "tokens/s",
+                       "ms_per_step": e2e_serial_ms, "calls_in_flight": 1},
         "gpu_launches": int(launches) * K,
         "gpu_launches_per_step": int(launches),
         "clocks": clk.summary(),

@@ -155,6 +155,26 @@ int32_t memlayer_layer_workspace_size(const memlayer_config* cfg, size_t* bytes)
 int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_args* args,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Most chunks memlayer_layer_forward_host splits a call into. */
+#define MEMLAYER_HOST_MAX_CHUNKS 16
+
+/* Bytes of device workspace memlayer_layer_forward_host needs. */
+int32_t memlayer_layer_host_workspace_size(const memlayer_config* cfg, int32_t chunks, size_t* bytes);
+
+/* memlayer_layer_forward with the hidden state and the output in HOST
+ * memory (args->h, args->y; pinned memory lets the copies overlap).  The
+ * tokens are split into `chunks` (at most MEMLAYER_HOST_MAX_CHUNKS, fewer
+ * when a chunk would hold under 256 tokens); the copy of chunk c+1 in, the
+ * layer on chunk c and the copy of chunk c-1 out run concurrently on two
+ * copy streams the library keeps per device and on `stream`, which covers
+ * the whole call when it returns (synchronise it before reading y).  The
+ * other pointers are device pointers as in memlayer_layer_forward;
+ * subkey_counts, slot_counts, balance_loss and top1_weight must be NULL.
+ * Same reference interface as memlayer_layer_forward (model.py:110-119),
+ * for callers whose activations live on the host. */
+int32_t memlayer_layer_forward_host(const memlayer_config* cfg, const memlayer_layer_args* args, int32_t chunks,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* Device-side status of the last call that used this workspace: 0, or a
  * code recorded by a kernel (a bounded wait that gave up, an out-of-range
  * sub-key id).  Copies one word to the host and synchronises `stream`.

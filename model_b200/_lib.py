@@ -168,6 +168,11 @@ def lib() -> C.CDLL:
         L.memlayer_layer_forward_sharded.restype = C.c_int32
         L.memlayer_layer_forward_sharded.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
                                                      C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_layer_host_workspace_size.restype = C.c_int32
+        L.memlayer_layer_host_workspace_size.argtypes = [C.POINTER(MemlayerConfig), C.c_int32, C.POINTER(C.c_size_t)]
+        L.memlayer_layer_forward_host.restype = C.c_int32
+        L.memlayer_layer_forward_host.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs), C.c_int32,
+                                                  C.c_void_p, C.c_size_t, C.c_void_p]
         L.memlayer_rowgrad_workspace_size.restype = C.c_int32
         L.memlayer_rowgrad_workspace_size.argtypes = [C.POINTER(MemlayerConfig), C.c_int64, C.POINTER(C.c_size_t)]
         L.memlayer_fetched_row_grads.restype = C.c_int32

@@ -5,6 +5,7 @@
 
 #include <atomic>
 
+#include <mutex>
 #include <new>
 
 #include "common.cuh"
@@ -272,8 +273,12 @@ int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* wor
 }
 
 // Memory-layer block (model.py:108-120), single GPU or row-sharded.
+// later_chunk: a chunk after the first of memlayer_layer_forward_host, whose
+// sub-key / Dense-kernel preparation and status reset already ran on this
+// workspace; only the hidden state is split again.
 int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* workspace, size_t workspace_bytes,
-               cudaStream_t s, memlayer_shard_comm* comm, int phases) {
+               cudaStream_t s, memlayer_shard_comm* comm, int phases, bool later_chunk = false,
+               const Work* given = nullptr) {
   Dims D;
   int st = check_config(cfg, &D, true);
   if (st) return st;
@@ -290,11 +295,15 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
   f.layer = true;
   f.balance = a->pool.balance_loss != nullptr;
   f.world = comm ? comm->world : 0;
-  size_t need = layout(D, f, nullptr, nullptr);
-  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
-    return MEMLAYER_ERR_WORKSPACE;
   Work W;
-  layout(D, f, (char*)workspace, &W);
+  if (given) {
+    W = *given;
+  } else {
+    size_t need = layout(D, f, nullptr, nullptr);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+      return MEMLAYER_ERR_WORKSPACE;
+    layout(D, f, (char*)workspace, &W);
+  }
   const memlayer_pool_args* pa = &a->pool;
   int* slots = pa->slots ? pa->slots : W.slots;
   float* weights = pa->weights ? pa->weights : W.weights;
@@ -314,7 +323,9 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
       // tensor-core projections: K-major tf32 halves of the Dense kernels and
       // the hidden state, then one GEMM for router (model.py:110) + gate (:118)
       const int NR = D.H * D.dk;
-      if (W.k_hi) {
+      if (later_chunk) {
+        ML_TRY(launch_split(a->h, D.M * D.dm, W.h_hi, W.h_lo, s));
+      } else if (W.k_hi) {
         ML_TRY(launch_prep_layer(D, W, pa->sub_keys, pa->log_temperature, cfg->min_temperature,
                                  cfg->max_temperature, a->h, a->w_router, a->b_router, a->w_gate, a->b_gate,
                                  a->w_out, s));
@@ -343,7 +354,7 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
     // SIMT float32 projections
     if (route) {
       ML_TRY(mark(pa, 0, s));
-      if ((st = prep_keys(D, cfg, pa, W, s))) return st;
+      if (!later_chunk && (st = prep_keys(D, cfg, pa, W, s))) return st;
       ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
       ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
       ML_TRY(mark(pa, 1, s));
@@ -363,6 +374,49 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
       ML_TRY(cudaMemcpyAsync(pa->out, a->mem, sizeof(float) * D.M * D.d, cudaMemcpyDeviceToDevice, s));
     ML_TRY(mark(pa, 5, s));
   }
+  return MEMLAYER_OK;
+}
+
+// ---- host-buffer layer forward: chunked copy / compute pipeline ----
+constexpr int64_t HOST_MIN_CHUNK = 256;   // smaller chunks do not pay for their fixed costs
+
+struct HostPlan {
+  int chunks;
+  int64_t mc;          // tokens per chunk (the last may have fewer)
+  size_t work_bytes;   // chunk workspace
+  size_t stage_off_y;  // staging: h at work_bytes, y at stage_off_y
+  size_t bytes;
+};
+
+HostPlan host_plan(const Dims& D, int chunks) {
+  HostPlan p{};
+  int64_t c = chunks < 1 ? 1 : chunks;
+  while (c > 1 && (D.M + c - 1) / c < HOST_MIN_CHUNK) --c;
+  p.chunks = (int)c;
+  p.mc = D.M > 0 ? (D.M + c - 1) / c : 0;
+  Dims Dc = D;
+  Dc.M = p.mc;
+  Flags f;
+  f.layer = true;
+  p.work_bytes = layout(Dc, f, nullptr, nullptr);
+  p.stage_off_y = p.work_bytes + up(sizeof(float) * D.M * D.dm);
+  p.bytes = p.stage_off_y + up(sizeof(float) * D.M * D.dm);
+  return p;
+}
+
+// Two non-blocking copy streams per device (host-to-device, device-to-host),
+// created on first use and kept for the life of the process.
+int copy_streams(cudaStream_t* in, cudaStream_t* out) {
+  static std::mutex mu;
+  static cudaStream_t cs[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MEMLAYER_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < 2; ++i)
+    if (!cs[dev][i] && cudaStreamCreateWithFlags(&cs[dev][i], cudaStreamNonBlocking) != cudaSuccess)
+      return MEMLAYER_ERR_CUDA;
+  *in = cs[dev][0];
+  *out = cs[dev][1];
   return MEMLAYER_OK;
 }
 
@@ -633,6 +687,97 @@ int32_t memlayer_row_adagrad(const memlayer_config* cfg, const memlayer_read* re
                args->n_unique};
   ML_TRY(launch_rowgrad(R, L, (char*)workspace, nullptr, nullptr, nullptr, nullptr, &A, (cudaStream_t)stream));
   return MEMLAYER_OK;
+}
+
+// ---- host-buffer layer forward ----
+
+int32_t memlayer_layer_host_workspace_size(const memlayer_config* cfg, int32_t chunks, size_t* bytes) {
+  Dims D;
+  int st = check_config(cfg, &D, true);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  *bytes = host_plan(D, chunks).bytes;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_layer_forward_host(const memlayer_config* cfg, const memlayer_layer_args* a, int32_t chunks,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, true);
+  if (st) return st;
+  if (!a) return MEMLAYER_ERR_BAD_POINTER;
+  const memlayer_pool_args* pa = &a->pool;
+  if (pa->subkey_counts || pa->slot_counts || pa->balance_loss || pa->top1_weight) return MEMLAYER_ERR_UNSUPPORTED;
+  if (D.M > 0 && (!a->h || !a->y)) return MEMLAYER_ERR_BAD_POINTER;
+  const HostPlan P = host_plan(D, chunks);
+  if (!workspace || workspace_bytes < P.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  if (D.M == 0) return layer_impl(cfg, a, workspace, P.work_bytes, (cudaStream_t)stream, nullptr,
+                                  MEMLAYER_PHASE_ALL);
+  cudaStream_t s = (cudaStream_t)stream, cin = nullptr, cout = nullptr;
+  if ((st = copy_streams(&cin, &cout))) return st;
+  float* stage_h = reinterpret_cast<float*>((char*)workspace + P.work_bytes);
+  float* stage_y = reinterpret_cast<float*>((char*)workspace + P.stage_off_y);
+  // the chunks share one chunk-sized workspace layout
+  memlayer_config cc = *cfg;
+  cc.tokens = P.mc;
+  Dims Dc;
+  if ((st = check_config(&cc, &Dc, true))) return st;
+  Flags f;
+  f.layer = true;
+  Work W;
+  layout(Dc, f, (char*)workspace, &W);
+  const int n = P.chunks;
+  cudaEvent_t ev[2 * MEMLAYER_HOST_MAX_CHUNKS + 2];
+  const int nev = 2 * n + 2;
+  if (n > MEMLAYER_HOST_MAX_CHUNKS) return MEMLAYER_ERR_BAD_SHAPE;
+  for (int i = 0; i < nev; ++i)
+    if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess) {
+      for (int j = 0; j < i; ++j) cudaEventDestroy(ev[j]);
+      return MEMLAYER_ERR_CUDA;
+    }
+  auto run = [&]() -> int {
+    // copies start after the caller's earlier work on `stream` (staging reuse)
+    ML_TRY(cudaEventRecord(ev[2 * n], s));
+    ML_TRY(cudaStreamWaitEvent(cin, ev[2 * n], 0));
+    ML_TRY(cudaStreamWaitEvent(cout, ev[2 * n], 0));
+    for (int c = 0; c < n; ++c) {
+      const int64_t t0 = c * P.mc, tn = (c + 1 == n) ? D.M - t0 : P.mc;
+      ML_TRY(cudaMemcpyAsync(stage_h + t0 * D.dm, a->h + t0 * D.dm, sizeof(float) * tn * D.dm,
+                             cudaMemcpyHostToDevice, cin));
+      ML_TRY(cudaEventRecord(ev[c], cin));
+    }
+    for (int c = 0; c < n; ++c) {
+      const int64_t t0 = c * P.mc, tn = (c + 1 == n) ? D.M - t0 : P.mc;
+      memlayer_config ck = *cfg;
+      ck.tokens = tn;
+      memlayer_layer_args ak = *a;
+      memlayer_pool_args& pk = ak.pool;
+      ak.h = stage_h + t0 * D.dm;
+      ak.y = stage_y + t0 * D.dm;
+      if (a->mem) ak.mem = a->mem + t0 * D.d;
+      if (pa->out) pk.out = pa->out + t0 * D.d;
+      if (pa->slots) pk.slots = pa->slots + t0 * D.H * D.k;
+      if (pa->weights) pk.weights = pa->weights + t0 * D.H * D.k;
+      if (pa->gumbel) pk.gumbel = pa->gumbel + t0 * D.H * 2 * D.n;
+      if (pa->queries_unit) pk.queries_unit = pa->queries_unit + t0 * D.H * D.dk;
+      pk.temperature = (c + 1 == n) ? pa->temperature : nullptr;
+      pk.stage_events = nullptr;
+      ML_TRY(cudaStreamWaitEvent(s, ev[c], 0));
+      int r = layer_impl(&ck, &ak, workspace, P.work_bytes, s, nullptr, MEMLAYER_PHASE_ALL, c > 0, &W);
+      if (r) return r;
+      ML_TRY(cudaEventRecord(ev[n + c], s));
+      ML_TRY(cudaStreamWaitEvent(cout, ev[n + c], 0));
+      ML_TRY(cudaMemcpyAsync(a->y + t0 * D.dm, stage_y + t0 * D.dm, sizeof(float) * tn * D.dm,
+                             cudaMemcpyDeviceToHost, cout));
+    }
+    ML_TRY(cudaEventRecord(ev[2 * n + 1], cout));
+    ML_TRY(cudaStreamWaitEvent(s, ev[2 * n + 1], 0));   // the caller's stream covers the whole call
+    return MEMLAYER_OK;
+  };
+  st = run();
+  for (int i = 0; i < nev; ++i) cudaEventDestroy(ev[i]);   // released once the recorded work completes
+  return st;
 }
 
 }  // extern "C"

@@ -248,14 +248,22 @@ __global__ void __launch_bounds__(256) shard_reduce_kernel(const __grid_constant
   const int64_t m = (int64_t)blockIdx.x * per + t;
   if (!ok || t >= per || m >= M) return;
   const float4* part = reinterpret_cast<const float4*>(mine + S.off.part);
+  // all counts, then all partial loads in flight at once
+  int cnt[MEMLAYER_MAX_SHARDS];
+#pragma unroll
+  for (int o = 0; o < MEMLAYER_MAX_SHARDS; ++o) cnt[o] = o < P ? own_cnt[m * P + o] : 0;
+  float4 x[MEMLAYER_MAX_SHARDS];
+#pragma unroll
+  for (int o = 0; o < MEMLAYER_MAX_SHARDS; ++o)
+    x[o] = cnt[o] > 0 ? __ldcg(part + ((int64_t)o * S.mcap + m) * d4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int o = 0; o < P; ++o) {          // owners in rank order: deterministic
-    if (own_cnt[m * P + o] == 0) continue;
-    const float4 x = __ldcg(part + ((int64_t)o * S.mcap + m) * d4 + i);
-    acc.x += x.x;
-    acc.y += x.y;
-    acc.z += x.z;
-    acc.w += x.w;
+#pragma unroll
+  for (int o = 0; o < MEMLAYER_MAX_SHARDS; ++o) {   // owners in rank order: deterministic
+    if (cnt[o] == 0) continue;
+    acc.x += x[o].x;
+    acc.y += x[o].y;
+    acc.z += x[o].z;
+    acc.w += x[o].w;
   }
   const int64_t at = m * d4 + i;
   if (out) reinterpret_cast<float4*>(out)[at] = acc;

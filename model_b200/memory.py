@@ -216,6 +216,48 @@ class MemoryLayer:
             "pool": P.init(seed, device, values_dtype)["params"],
         }
 
+    def apply_host(self, params, h_host: torch.Tensor, *, chunks: int = 4, device="cuda",
+                   shuffle_reads: bool = False, stream: Optional[torch.cuda.Stream] = None,
+                   check: bool = False):
+        """Inference forward with the hidden state and the output in host
+        memory (memlayer_layer_forward_host): the host-to-device copy, the
+        layer and the device-to-host copy overlap chunk by chunk.  Returns
+        (y_host [..., d_model] pinned, aux on the device)."""
+        P = self.pool
+        if h_host.is_cuda or h_host.dtype != torch.float32:
+            raise TypeError("h_host must be a float32 host tensor")
+        h_host = h_host.contiguous()
+        if not h_host.is_pinned():
+            h_host = h_host.pin_memory()
+        lead = tuple(h_host.shape[:-1])
+        M = int(math.prod(lead)) if lead else 1
+        device = torch.device(device)
+        r, g_, o = (params[f"{n}_{self.layer}"] for n in ("router", "mem_gate", "mem_out"))
+        cfg = P.config(M, params["pool"]["values"].dtype, self.d_model)
+        a, keep = P._pool_args(params["pool"], M, device, train=False, noise_scale=1.0,
+                               shuffle_reads=shuffle_reads, rngs=None, gumbel=None, stats=False)
+        a.top1_weight = None                              # a per-call mean: not produced chunk by chunk
+        w = {k: _cuda_f32(v, k) for k, v in (("wr", r["kernel"]), ("br", r["bias"]), ("wg", g_["kernel"]),
+                                             ("bg", g_["bias"]), ("wo", o["kernel"]), ("bo", o["bias"]))}
+        y = torch.empty(*lead, self.d_model, dtype=torch.float32).pin_memory()
+        la = L.MemlayerLayerArgs(h=h_host.data_ptr(), w_router=_ptr(w["wr"]), b_router=_ptr(w["br"]),
+                                 w_gate=_ptr(w["wg"]), b_gate=_ptr(w["bg"]), w_out=_ptr(w["wo"]),
+                                 b_out=_ptr(w["bo"]), y=y.data_ptr(), mem=None, pool=a)
+        nbytes = C.c_size_t()
+        L.check(L.lib().memlayer_layer_host_workspace_size(C.byref(cfg), chunks, C.byref(nbytes)),
+                "memlayer_layer_host_workspace_size")
+        ws = _workspace(nbytes.value, device)
+        s = (stream or torch.cuda.current_stream(device)).cuda_stream
+        L.check(L.lib().memlayer_layer_forward_host(C.byref(cfg), C.byref(la), chunks, ws.data_ptr(), nbytes.value,
+                                                    s), "memlayer_layer_forward_host")
+        if check:
+            _raise_device_status(cfg, ws, s)
+        torch.cuda.current_stream(device).synchronize() if stream is None else stream.synchronize()
+        aux = {"slots": keep["slots"].reshape(*lead, P.heads, P.top_k),
+               "weights": keep["weights"].reshape(*lead, P.heads, P.top_k),
+               "temperature": keep["temperature"].reshape(())}
+        return y, aux
+
     def apply(self, params, h: torch.Tensor, *, train: bool = False, noise_scale: float = 1.0,
               shuffle_reads: bool = False, rngs=None, gumbel=None, stats: bool = False,
               stream: Optional[torch.cuda.Stream] = None, check: bool = False):

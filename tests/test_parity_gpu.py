@@ -221,3 +221,21 @@ def test_gpu_shapes_against_oracle(name, stats):
             assert_rel(got["y"], orc["y"], tol if recipe.get("values_dtype") else OUT_RTOL_F32, "y")
     if recipe.get("layer") and stats:
         assert_rel(got["queries"].reshape(M, H, 2, -1), orc["route"]["q"], 1e-5, "unit queries")
+
+
+@pytest.mark.parametrize("M,chunks", [(8192, 4), (3000, 3), (1000, 8), (200, 4)])
+def test_gpu_layer_forward_host_buffers(M, chunks):
+    """memlayer_layer_forward_host (host h / y, chunked copy-compute
+    pipeline) gives the device entry's results bit for bit."""
+    from model_b200 import MemoryLayer, MemoryPool
+    pool = MemoryPool(n_sub_keys=128, heads=4, d_key=128, d_value=128, top_k=16)
+    layer = MemoryLayer(pool, d_model=128, layer=1)
+    params = layer.init(4)
+    h = torch.randn(M, 128, generator=torch.Generator().manual_seed(M))
+    y_dev, _, aux_dev = layer.apply(params, h.cuda(), check=True)
+    for _ in range(2):                 # the workspace / staging buffers are reused across calls
+        y_host, aux = layer.apply_host(params, h, chunks=chunks, check=True)
+    torch.cuda.synchronize()
+    assert torch.equal(aux["slots"], aux_dev["slots"])
+    assert torch.equal(aux["weights"], aux_dev["weights"])
+    assert torch.equal(y_host, y_dev.cpu())
