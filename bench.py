@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--host-chunks", type=int, default=4,
                     help="chunks of the host-buffer pipeline timed as e2e (memlayer_layer_forward_host)")
+    ap.add_argument("--workload", choices=["cfg0", "cfg2", "cfg3", "cfg4"], default="cfg0",
+                    help="cfg0 (default, the driver's line): configs[0] layer forward; cfg2: configs[2] decode "
+                         "latency on a 67M-slot fp16 table; cfg3: configs[3] billion-slot bf16 table "
+                         "row-sharded over >= 4 GPUs; cfg4: configs[4] forward + fetched-row Adagrad")
     ap.add_argument("--pool", choices=["sharded", "replicated"], default="sharded",
                     help="N>1: row-shard the value table over the ranks (default) or replicate it")
     return ap.parse_args()
@@ -137,12 +141,23 @@ def make_inputs(torch, device, W, values_dtype, seed, value_rows=None):
         "w_router": glorot(dm, H * dk), "b_router": torch.zeros(H * dk, device=device),
         "sub_keys": torch.randn(H, 2, n, dk // 2, device=device, generator=g) * math.sqrt(1 / 128),
         "log_t": torch.full((1,), math.log(10.0), device=device),
-        "values": (torch.randn(n * n if value_rows is None else value_rows, d, device=device, generator=g)
-                   * 0.02).to(vdt),
+        # drawn in the table's own dtype (no float32 copy of a large table)
+        "values": torch.randn(n * n if value_rows is None else value_rows, d, device=device, generator=g,
+                              dtype=vdt).mul_(0.02),
         "w_gate": glorot(dm, d), "b_gate": torch.zeros(d, device=device),
         "w_out": glorot(d, dm), "b_out": torch.zeros(dm, device=device),
     }
     return x
+
+
+def clustered_hidden(torch, device, T, dm, seed, centers=64, sigma=0.3, zipf_a=1.1):
+    """configs[3] / [4] hidden states: 64 Gaussian centres ~ N(0, I) with
+    Zipf(1.1) cluster weights (p_r ~ r^-1.1), plus sigma * N(0, I)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    c = torch.randn(centers, dm, device=device, generator=g)
+    p = torch.arange(1, centers + 1, device=device, dtype=torch.float64) ** -zipf_a
+    idx = torch.multinomial((p / p.sum()).float(), T, replacement=True, generator=g)
+    return c[idx] + sigma * torch.randn(T, dm, device=device, generator=g)
 
 
 class LayerCall:
@@ -496,6 +511,184 @@ def run_ours(args, W, rank, world):
     return line
 
 
+# ---------------------------------------------------------------- other configs
+def _events(torch, n):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def _common_line(W, world, steps, warmup, ms, value, unit, dtype, extra):
+    line = {"metric": "memory-layer tokens/s", "value": value, "unit": unit, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (seeded)", "config": {"workload": W["name"], **{k: W[k] for k in W if k != "name"}}}
+    line.update(extra)
+    return line
+
+
+def run_cfg4(args):
+    """configs[4]: configs[0] shapes, f32 values, 8192 Zipf-clustered tokens;
+    step = layer forward with routing statistics + fetched-row gradients of a
+    synthetic probe gradient + global-norm clip + row-wise Adagrad on the
+    touched rows.  The backward through the router is not built, so the probe
+    gradient is drawn, not computed."""
+    import torch
+
+    from model_b200 import _lib as L
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    W = dict(WORKLOAD, name="cfg4_sparse_update", values_dtype="f32")
+    x = make_inputs(torch, device, W, "f32", W["seed"])
+    T, d, H, k = W["tokens_per_gpu"], W["d_value"], W["heads"], W["top_k"]
+    x["h"] = clustered_hidden(torch, device, T, W["d_model"], W["seed"] + 1)
+    call = LayerCall(torch, L, W, x, device, "f32")
+    cnt_slot = torch.empty(W["n_sub_keys"] ** 2, device=device)
+    cnt_sub = torch.empty(H, 2, W["n_sub_keys"], device=device)
+    bal = torch.empty(1, device=device)
+    call.args.pool.slot_counts, call.args.pool.subkey_counts = cnt_slot.data_ptr(), cnt_sub.data_ptr()
+    call.args.pool.balance_loss = bal.data_ptr()
+    accum = torch.zeros(W["n_sub_keys"] ** 2, device=device)
+    g = torch.randn(T, d, device=device, generator=torch.Generator(device=device).manual_seed(7)) * 1e-3
+    rest = torch.tensor([0.5], device=device)
+    scale = torch.empty(1, device=device)
+    n_u = torch.empty(1, dtype=torch.int32, device=device)
+    # the C call of memlayer_row_adagrad, built once (train.py:378-383, 396-399)
+    reads = (L.MemlayerRead * 1)(L.MemlayerRead(slots=call.slots.data_ptr(), weights=call.weights.data_ptr(),
+                                                grad=g.data_ptr(), tokens=T))
+    ada = L.MemlayerAdagradArgs(values=x["values"].data_ptr(), accum=accum.data_ptr(), lr=0.01, grad_clip=1.0,
+                                rest_sq_norm=rest.data_ptr(), clip_scale=scale.data_ptr(), n_unique=n_u.data_ptr())
+    rb = C.c_size_t()
+    L.check(L.lib().memlayer_rowgrad_workspace_size(C.byref(call.cfg), T * H * k, C.byref(rb)), "rowgrad ws")
+    rws = torch.empty(rb.value, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    lib = L.lib()
+
+    def update():
+        L.check(lib.memlayer_row_adagrad(C.byref(call.cfg), reads, 1, C.byref(ada), rws.data_ptr(), rb.value,
+                                         stream.cuda_stream), "memlayer_row_adagrad")
+    for _ in range(args.warmup):
+        flush.zero_()
+        call(stream)
+        update()
+    torch.cuda.synchronize()
+    K = args.steps
+    e0, e1, e2 = _events(torch, K), _events(torch, K), _events(torch, K)
+    for i in range(K):
+        flush.zero_()
+        e0[i].record(stream)
+        call(stream)
+        e1[i].record(stream)
+        update()
+        e2[i].record(stream)
+    torch.cuda.synchronize()
+    fwd = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
+    upd = statistics.mean(e1[i].elapsed_time(e2[i]) for i in range(K))
+    out = {"n_unique": n_u, "clip_scale": scale}
+    U = int(out["n_unique"].item())
+    F = T * H * k
+    hbm, src = peaks()
+    upd_bytes = F * 8 + T * d * 4 + U * (2 * d * 4 + 8)
+    ms = fwd + upd
+    return _common_line(W, 1, K, args.warmup, ms, T / (ms * 1e-3), "tokens/s", "f32", {
+        "scaling": "weak", "stages_ms": {"forward": fwd, "row_grad_adagrad": upd},
+        "unique_rows": U, "fetches": F, "clip_scale": float(out["clip_scale"].item()),
+        "row_update": {"algorithmic_bytes": upd_bytes, "achieved_gbs": upd_bytes / (upd * 1e-3) / 1e9,
+                       "peak": hbm, "peak_source": src, "frac": upd_bytes / (upd * 1e-3) / 1e9 / hbm,
+                       "bytes_note": "slots+weights of every fetch, one read of every probe-gradient row, "
+                                     "read+write of every touched value row and accumulator"},
+        "note": "probe gradient drawn (router backward not built); L2 flushed before every step"})
+
+
+def run_cfg2(args):
+    """configs[2] decode: n_sub_keys 8192 (67,108,864 slots x 256 fp16 =
+    34.4 GB, HBM-resident), H 4, top_k 16, d_key 128, d_model 256; one call
+    per decode step at batch 1, 8 and 64; per-step device latency."""
+    import torch
+
+    from model_b200 import _lib as L
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    res = {}
+    W = dict(WORKLOAD, name="cfg2_decode", n_sub_keys=8192, d_key=128, values_dtype="f16")
+    x = None
+    for B in (1, 8, 64):
+        Wb = dict(W, tokens_per_gpu=B)
+        if x is None:
+            x = make_inputs(torch, device, Wb, "f16", W["seed"])
+        else:
+            x["h"] = torch.randn(B, W["d_model"], device=device)
+        call = LayerCall(torch, L, Wb, x, device, "f16")
+        stream = torch.cuda.current_stream(device)
+        for _ in range(args.warmup):
+            call(stream)
+        torch.cuda.synchronize()
+        ev = [_events(torch, 2) for _ in range(args.steps)]
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            call(stream)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        t = sorted(e[0].elapsed_time(e[1]) * 1000 for e in ev)
+        res[B] = {"p50_us": t[len(t) // 2], "p90_us": t[int(len(t) * 0.9)], "tokens_per_s": B / (t[len(t) // 2] * 1e-6)}
+    return _common_line(W, 1, args.steps, args.warmup, res[64]["p50_us"] / 1000, res[64]["tokens_per_s"],
+                        "tokens/s", "f16", {"scaling": "n/a", "decode": res,
+                                            "note": "value = batch 64; per-step device time, L2 not flushed "
+                                                    "(decode steps run back to back)"})
+
+
+def run_cfg3(args, rank, world):
+    """n_sub_keys 32768 (2^30 slots x 256 bf16 = 550 GB)
+    row-sharded over the ranks, H 8, top_k 32, d_key 256, d_model 256;
+    65,536 Zipf-clustered tokens in total (65,536 / N per rank)."""
+    import torch
+
+    from model_b200 import _lib as L
+    from model_b200.shard import shard_rows
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(device)
+    W = dict(WORKLOAD, name="cfg3_billion_slot_prefill", n_sub_keys=32768, heads=8, top_k=32, d_key=256,
+             values_dtype="bf16", tokens_per_gpu=65536 // world)
+    rows = shard_rows(W["n_sub_keys"] ** 2, rank, world)
+    x = make_inputs(torch, device, W, "bf16", W["seed"], rows)
+    x["h"] = clustered_hidden(torch, device, W["tokens_per_gpu"], W["d_model"], W["seed"] + 1 + rank)
+    call = ShardedLayerCall(torch, L, W, x, device, "bf16")
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        call(stream)
+    torch.cuda.synchronize()
+    K = args.steps
+    ev = [_events(torch, L.STAGE_EVENTS) for _ in range(K)]
+    pev = [_events(torch, 2) for _ in range(K)]
+    for row in ev:
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    for i in range(K):
+        call(stream, ev[i], pev[i])
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    ms = statistics.mean(ev[i][0].elapsed_time(ev[i][5]) for i in range(K))
+    st = lambda a, b: statistics.mean(ev[i][a].elapsed_time(ev[i][b]) for i in range(K))  # noqa: E731
+    stages = {"projections": st(0, 1), "score_topk": st(2, 3), "combine_push": st(3, 4),
+              "shard_gather": statistics.mean(pev[i][0].elapsed_time(pev[i][1]) for i in range(K)),
+              "reduce_out": statistics.mean(pev[i][1].elapsed_time(ev[i][5]) for i in range(K))}
+    t = torch.tensor([ms] + list(stages.values()), dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    call.comm.close()
+    if rank != 0:
+        return None
+    ms = float(t[0])
+    stages = dict(zip(stages, t[1:].tolist()))
+    score_flops = 2 * 65536 * W["heads"] * 2 * W["n_sub_keys"] * (W["d_key"] // 2)
+    tp, _ = tensor_peak()
+    return _common_line(W, world, K, args.warmup, ms, 65536 / (ms * 1e-3), "tokens/s", "bf16", {
+        "scaling": "strong", "stages_ms_max_over_ranks": stages,
+        "score_tflops_per_gpu": score_flops / world / (stages["score_topk"] * 1e-3) / 1e12,
+        "tensor_peak": tp, "note": "no L2 flush (the 68.7 GB/GPU table and 1.1 TFLOP/GPU score GEMM dwarf L2)"})
+
+
 def main():
     args = parse()
     W = dict(WORKLOAD, values_dtype=args.values_dtype, tokens_per_gpu=args.tokens)
@@ -509,6 +702,12 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     if args.impl == "reference":
         line = run_reference(args, W, rank)
+    elif args.workload == "cfg4":
+        line = run_cfg4(args)
+    elif args.workload == "cfg2":
+        line = run_cfg2(args)
+    elif args.workload == "cfg3":
+        line = run_cfg3(args, rank, world)
     else:
         line = run_ours(args, W, rank, world)
     if line is not None:

@@ -43,14 +43,41 @@ struct ProjArgs {
   float* out;          // [M][N]
 };
 
-// One query half of one row: q = acc + b_router, q_len and the unit half as
-// tf32 hi / lo (+ float32 when requested), memory.py:136-138.  TMEM is read
-// in pieces of up to 64 columns with one wait each: once for |q|^2, once to
-// write.
+// Per-warp staging tile for coalesced epilogue stores: 32 rows x 16 floats,
+// row stride 20 floats (conflict-free float4 writes by row-owning lanes).
+constexpr int STG_LD = 20;
+constexpr int STG_FLOATS = 32 * STG_LD;
+
+// The 32 lanes of a warp each hold 16 consecutive values of their own row
+// (row = row0 + lane).  Written through the staging tile so that every
+// store instruction covers 8 rows x 64 contiguous bytes instead of 32 rows x
+// 16 bytes.  dst0 points at row0's first column; rows >= nrows are skipped.
+__device__ __forceinline__ void store16_rows(float* stg, const float (&v)[16], float* dst0, int64_t stride,
+                                             int64_t nrows, int lane) {
+#pragma unroll
+  for (int j = 0; j < 16; j += 4)
+    *reinterpret_cast<float4*>(stg + lane * STG_LD + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2), c = (lane & 3) * 4;
+    const float4 x = *reinterpret_cast<const float4*>(stg + r * STG_LD + c);
+    if (r < nrows) *reinterpret_cast<float4*>(dst0 + r * stride + c) = x;
+  }
+  __syncwarp();
+}
+
+// One query half of the warp's 32 rows: q = acc + b_router, q_len and the
+// unit half as tf32 hi / lo (+ float32 when requested), memory.py:136-138.
+// TMEM is read in pieces of up to 64 columns with one wait each: once for
+// |q|^2, once to write.
 template <int HALF>
-__device__ __forceinline__ void router_half(const ProjArgs& G, uint32_t taddr, int ns, int64_t row, bool rok,
-                                            const float* sbias) {
+__device__ __forceinline__ void router_half(const ProjArgs& G, uint32_t taddr, int ns, int64_t row0, int lane,
+                                            const float* sbias, float* stg) {
   constexpr int P = HALF < 64 ? HALF : 64;
+  const int64_t row = row0 + lane;
+  const bool rok = row < G.M;
+  const int64_t nrows = G.M - row0;
   float ss = 0.f;
 #pragma unroll
   for (int p0 = 0; p0 < HALF; p0 += P) {
@@ -68,9 +95,10 @@ __device__ __forceinline__ void router_half(const ProjArgs& G, uint32_t taddr, i
   const float tt = ss + 1e-6f;
   const float rn = 1.0f / sqrtf(tt);
   if (rok) G.qlen[row * G.hc_count + hc] = sqrtf(tt) / sqrtf((float)HALF);
-  float* dqn = (rok && G.qn) ? G.qn + (row * G.hc_count + hc) * HALF : nullptr;
-  float* dhi = (rok && G.q_hi) ? G.q_hi + ((int64_t)hc * G.M + row) * HALF : nullptr;
-  float* dlo = (rok && G.q_hi) ? G.q_lo + ((int64_t)hc * G.M + row) * HALF : nullptr;
+  // row0's first element in each destination
+  float* dhi = G.q_hi ? G.q_hi + ((int64_t)hc * G.M + row0) * HALF : nullptr;
+  float* dlo = G.q_hi ? G.q_lo + ((int64_t)hc * G.M + row0) * HALF : nullptr;
+  float* dqn = G.qn ? G.qn + (row0 * G.hc_count + hc) * HALF : nullptr;
 #pragma unroll
   for (int p0 = 0; p0 < HALF; p0 += P) {
     uint32_t r[P];
@@ -78,19 +106,19 @@ __device__ __forceinline__ void router_half(const ProjArgs& G, uint32_t taddr, i
     for (int c = 0; c < P; c += 32) tc::tmem_ld32(taddr + p0 + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
     tc::tmem_wait_ld();
 #pragma unroll
-    for (int t = 0; t < P; t += 4) {
-      float h4[4], l4[4], u4[4];
+    for (int t = 0; t < P; t += 16) {
+      float u[16], h[16], l[16];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        u4[j] = (__uint_as_float(r[t + j]) + sbias[ns + p0 + t + j]) * rn;
-        h4[j] = tc::to_tf32(u4[j]);
-        l4[j] = tc::to_tf32(u4[j] - h4[j]);
+      for (int j = 0; j < 16; ++j) {
+        u[j] = (__uint_as_float(r[t + j]) + sbias[ns + p0 + t + j]) * rn;
+        h[j] = tc::to_tf32(u[j]);
+        l[j] = tc::to_tf32(u[j] - h[j]);
       }
       if (dhi) {
-        *reinterpret_cast<float4*>(dhi + p0 + t) = make_float4(h4[0], h4[1], h4[2], h4[3]);
-        *reinterpret_cast<float4*>(dlo + p0 + t) = make_float4(l4[0], l4[1], l4[2], l4[3]);
+        store16_rows(stg, h, dhi + p0 + t, HALF, nrows, lane);
+        store16_rows(stg, l, dlo + p0 + t, HALF, nrows, lane);
       }
-      if (dqn) *reinterpret_cast<float4*>(dqn + p0 + t) = make_float4(u4[0], u4[1], u4[2], u4[3]);
+      if (dqn) store16_rows(stg, u, dqn + p0 + t, (int64_t)G.hc_count * HALF, nrows, lane);
     }
   }
 }
@@ -109,6 +137,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   for (int i = threadIdx.x; i < G.N; i += blockDim.x) sbias[i] = G.bias ? G.bias[i] : 0.f;
   volatile int* abort = &ctl->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // per-epilogue-warp staging tiles after the bias vector
+  float* stg = sbias + ((G.N + 255) / 256) * 256 + (warp >= 2 ? (warp - 2) * STG_FLOATS : 0);
   const int units = m_tiles * n_tiles;
   // unit u = (n tile, m tile), m fastest: neighbouring CTAs share the B tile
   auto coords = [&](int u, int& arow, int& brow0, int& nch) {
@@ -131,7 +161,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t aph = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const int nt = u / m_tiles, mt = u - nt * m_tiles;
-      const int64_t row = (int64_t)mt * tc::PIPE_M + quarter * 32 + lane;
+      const int64_t row0 = (int64_t)mt * tc::PIPE_M + quarter * 32;   // the warp's first row
+      const int64_t row = row0 + lane;
       const bool rok = row < G.M;
       if (!__all_sync(FULL, tc::mbar_wait(&ctl->tfull[acc], aph, abort, err, 14))) break;
       tc::fence_after_sync();
@@ -144,36 +175,37 @@ __global__ void __launch_bounds__(THREADS, 1)
         // router columns: whole query halves (half divides 128, NR % 128 == 0)
         for (int seg = 0; seg < ncols; seg += G.half) {
           if (G.half == 128)
-            router_half<128>(G, taddr + c0 + seg, n0 + seg, row, rok, sbias);
+            router_half<128>(G, taddr + c0 + seg, n0 + seg, row0, lane, sbias, stg);
           else if (G.half == 64)
-            router_half<64>(G, taddr + c0 + seg, n0 + seg, row, rok, sbias);
+            router_half<64>(G, taddr + c0 + seg, n0 + seg, row0, lane, sbias, stg);
           else
-            router_half<32>(G, taddr + c0 + seg, n0 + seg, row, rok, sbias);
+            router_half<32>(G, taddr + c0 + seg, n0 + seg, row0, lane, sbias, stg);
         }
       } else {
         // gate columns (silu) or plain bias columns, 32 at a time
         const int ld = EPI == EPI_ROUTER_GATE ? G.N - G.NR : G.N;
-        float* dst = EPI == EPI_ROUTER_GATE ? G.gate + row * ld + (n0 - G.NR) : G.out + row * ld + n0;
+        float* dst0 = EPI == EPI_ROUTER_GATE ? G.gate + row0 * ld + (n0 - G.NR) : G.out + row0 * ld + n0;
+        float* dst = dst0 + (int64_t)lane * ld;
+        const bool vec = (ld & 3) == 0 && (n0 & 3) == 0;
         for (int cc = 0; cc < ncols; cc += 32) {
           uint32_t r[32];
           tc::tmem_ld32(taddr + c0 + cc, r);
           tc::tmem_wait_ld();
-          if (rok) {
-            float v[32];
+          float v[32];
 #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              float x = __uint_as_float(r[t]) + (cc + t < ncols ? sbias[n0 + cc + t] : 0.f);
-              if (EPI == EPI_ROUTER_GATE) x = x / (1.0f + expf(-x));      // model.py:118 silu
-              v[t] = x;
-            }
-            if (cc + 32 <= ncols) {
+          for (int t = 0; t < 32; ++t) {
+            float x = __uint_as_float(r[t]) + (cc + t < ncols ? sbias[n0 + cc + t] : 0.f);
+            if (EPI == EPI_ROUTER_GATE) x = x / (1.0f + expf(-x));      // model.py:118 silu
+            v[t] = x;
+          }
 #pragma unroll
-              for (int t = 0; t < 32; t += 4)
-                *reinterpret_cast<float4*>(dst + cc + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
-            } else {
+          for (int g = 0; g < 32; g += 16) {
+            if (vec && cc + g + 16 <= ncols) {
+              store16_rows(stg, *reinterpret_cast<float(*)[16]>(&v[g]), dst0 + cc + g, ld, G.M - row0, lane);
+            } else if (rok) {
 #pragma unroll
-              for (int t = 0; t < 32; ++t)
-                if (cc + t < ncols) dst[cc + t] = v[t];
+              for (int t = 0; t < 16; ++t)
+                if (cc + g + t < ncols) dst[cc + g + t] = v[g + t];
             }
           }
         }
@@ -201,7 +233,9 @@ cudaError_t launch_proj(const ProjArgs& G, const float* a_hi, const float* a_lo,
                         const float* b_lo, int* err, cudaStream_t s) {
   if (G.M == 0) return cudaSuccess;
   const int BN = bn_for(EPI, G.N);
-  const uint32_t bias_bytes = ((uint32_t)G.N * 4 + 1023) / 1024 * 1024;
+  // bias vector (padded to 256 floats) + one staging tile per epilogue warp
+  const uint32_t bias_bytes =
+      (((uint32_t)(G.N + 255) / 256 * 256 * 4 + EPI_WARPS * STG_FLOATS * 4) + 1023) / 1024 * 1024;
   tc::PipeShape P = tc::pipe_shape(BN, G.K, bias_bytes);
   if (P.stages < 2) return cudaErrorInvalidConfiguration;
   CUtensorMap m[4];

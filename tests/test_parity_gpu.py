@@ -239,3 +239,42 @@ def test_gpu_layer_forward_host_buffers(M, chunks):
     assert torch.equal(aux["slots"], aux_dev["slots"])
     assert torch.equal(aux["weights"], aux_dev["weights"])
     assert torch.equal(y_host, y_dev.cpu())
+
+
+def _big_pool_case(n, H, dk, d, k, vdt, M, seed):
+    """Routing of the large configs against the oracle; the read against a
+    torch gather of the same table with the kernel's own slots and weights."""
+    from model_b200 import MemoryPool
+    pool = MemoryPool(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k)
+    g = torch.Generator("cuda").manual_seed(seed)
+    sk = torch.randn(H, 2, n, dk // 2, device="cuda", generator=g)
+    values = torch.randn(n * n, d, device="cuda", generator=g, dtype=vdt).mul_(0.02)   # no float32 copy
+    params = {"sub_keys": sk, "values": values,
+              "log_temperature": torch.tensor(np.log(10.0), device="cuda", dtype=torch.float32)}
+    q = torch.randn(M, H, dk, device="cuda", generator=g)
+    out, aux = pool.apply({"params": params}, q, stats=False, check=True)
+    torch.cuda.synchronize()
+    cfg = ref.PoolConfig(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k)
+    r = ref.route(cfg, q.cpu().numpy(), sk.cpu().numpy(), float(np.log(10.0)))
+    check_slots(aux["slots"].cpu().numpy(), r["slots"], r["scores"], n)
+    w_ref = ref.softmax(r["slot_scores"])
+    same = (aux["slots"].cpu().numpy() == r["slots"]).all(-1)
+    np.testing.assert_allclose(aux["weights"].cpu().numpy()[same], w_ref[same], rtol=1e-5, atol=1e-7)
+    rows = values[aux["slots"].long()].float()                       # [M, H, k, d]
+    want = torch.einsum("mhk,mhkd->md", aux["weights"], rows)
+    assert_rel(out.cpu().numpy(), want.cpu().numpy(), 1e-5, "read")
+    del values, rows
+    torch.cuda.empty_cache()
+
+
+def test_gpu_cfg2_pool_shapes_decode_batches():
+    """n_sub_keys 8192 (67,108,864 slots), H 4, d_key 128, top_k 16,
+    fp16 rows (d reduced to 64 to bound the test's memory), decode batches."""
+    for M in (1, 8, 64):
+        _big_pool_case(8192, 4, 128, 64, 16, torch.float16, M, seed=M)
+
+
+def test_gpu_cfg3_pool_shapes():
+    """configs[3] routing: n_sub_keys 32768 (2^30 slots), H 8, d_key 256,
+    top_k 32, bf16 rows (d reduced to 16: a 34 GB table on one GPU)."""
+    _big_pool_case(32768, 8, 256, 16, 32, torch.bfloat16, 48, seed=3)
