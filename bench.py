@@ -621,14 +621,19 @@ def run_cfg2(args):
         for _ in range(args.warmup):
             call(stream)
         torch.cuda.synchronize()
-        ev = [_events(torch, 2) for _ in range(args.steps)]
-        for i in range(args.steps):
-            ev[i][0].record(stream)
-            call(stream)
-            ev[i][1].record(stream)
+        ev = [_events(torch, L.STAGE_EVENTS) for _ in range(args.steps)]
+        for row in ev:
+            for e in row:
+                e.record(stream)
         torch.cuda.synchronize()
-        t = sorted(e[0].elapsed_time(e[1]) * 1000 for e in ev)
-        res[B] = {"p50_us": t[len(t) // 2], "p90_us": t[int(len(t) * 0.9)], "tokens_per_s": B / (t[len(t) // 2] * 1e-6)}
+        for i in range(args.steps):
+            call(stream, ev[i])
+        torch.cuda.synchronize()
+        t = sorted(e[0].elapsed_time(e[5]) * 1000 for e in ev)
+        st = lambda a, b: statistics.median(e[a].elapsed_time(e[b]) * 1000 for e in ev)  # noqa: E731
+        res[B] = {"p50_us": t[len(t) // 2], "p90_us": t[int(len(t) * 0.9)], "tokens_per_s": B / (t[len(t) // 2] * 1e-6),
+                  "stages_us": {"prep_projections": st(0, 2), "score_topk": st(2, 3), "combine_gather": st(3, 4),
+                                "finalize_out": st(4, 5)}}
     return _common_line(W, 1, args.steps, args.warmup, res[64]["p50_us"] / 1000, res[64]["tokens_per_s"],
                         "tokens/s", "f16", {"scaling": "n/a", "decode": res,
                                             "note": "value = batch 64; per-step device time, L2 not flushed "

@@ -78,7 +78,10 @@ size_t layout(const Dims& D, const Flags& f, char* ws, Work* W) {
   w.fin_part = (double*)take(sizeof(double) * 64);
   w.keys_n = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
   w.qn = (float*)take(sizeof(float) * rows * D.half);
-  if (score_tc_supported(D)) {
+  // few tokens (decode): split-key score path; tensor-core tiles need many tokens
+  const bool small = score_small_supported(D);
+  if (small) w.small = (float*)take(score_small_scratch_bytes(D));
+  if (score_tc_supported(D) && !small) {
     w.k_hi = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
     w.k_lo = (float*)take(sizeof(float) * D.H * 2 * D.n * D.half);
     w.q_hi = (float*)take(sizeof(float) * rows * D.half);
@@ -164,6 +167,8 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
   const bool bal = a->balance_loss != nullptr;
   if (W.q_hi)
     ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, bal, s));
+  else if (W.small && !bal)
+    ML_TRY(launch_score_small(D, w2, a->gumbel, W.small, s));
   else
     ML_TRY(launch_score_topk(D, w2, a->gumbel, bal, s));
   if (bal) ML_TRY(launch_balance(D, w2, a->balance_loss, s));

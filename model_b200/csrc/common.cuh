@@ -70,6 +70,7 @@ struct Work {
   float* weights = nullptr;    // [M,H,k] when the caller passes none
   float* out = nullptr;        // [M,d] when the caller passes none
   int* own_cnt = nullptr;      // [M,world] entries each owner rank gathers (row-sharded pool)
+  float* small = nullptr;      // slice top-k lists of the few-token score path
 };
 
 constexpr int SCORE_TM = 128;   // tokens per score tile
@@ -196,6 +197,9 @@ cudaError_t launch_score_topk_tc(const Dims& D, const Work& W, const float* gumb
                                  cudaStream_t s);
 cudaError_t launch_score_topk(const Dims& D, const Work& W, const float* gumbel, bool want_balance,
                               cudaStream_t s);
+bool score_small_supported(const Dims& D);
+size_t score_small_scratch_bytes(const Dims& D);
+cudaError_t launch_score_small(const Dims& D, const Work& W, const float* gumbel, float* scratch, cudaStream_t s);
 cudaError_t launch_balance(const Dims& D, const Work& W, float* balance_loss, cudaStream_t s);
 cudaError_t launch_combine_gather(const Dims& D, const Work& W, const void* values, int* slots, float* weights,
                                   float* out, float* mem_gated, float* memg_hi, float* memg_lo, const float* gate,

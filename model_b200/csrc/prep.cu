@@ -148,9 +148,58 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   }
 }
 
+// Few rows (decode): C[m, n] = sum_k A[m, k] B[k, n] (+ bias, silu).  Lane =
+// output column (coalesced rows of B), the 8 warps of a CTA split K into
+// contiguous ranges and their partial sums are added in warp order through
+// shared memory (deterministic); up to GV_M rows per CTA.
+constexpr int GV_M = 8;
+
+__global__ void __launch_bounds__(256) gemv_f32_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                       const float* __restrict__ bias, float* __restrict__ C,
+                                                       int64_t M, int N, int K, int silu) {
+  __shared__ float part[8][GV_M][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int n = blockIdx.x * 32 + lane;
+  const int64_t m0 = (int64_t)blockIdx.y * GV_M;
+  const int kper = (K + 7) / 8, k0 = w * kper, k1 = min(K, k0 + kper);
+  float acc[GV_M];
+#pragma unroll
+  for (int i = 0; i < GV_M; ++i) acc[i] = 0.f;
+  if (n < N) {
+#pragma unroll 4
+    for (int k = k0; k < k1; ++k) {
+      const float b = __ldg(B + (int64_t)k * N + n);
+#pragma unroll
+      for (int i = 0; i < GV_M; ++i)
+        if (m0 + i < M) acc[i] = fmaf(__ldg(A + (m0 + i) * K + k), b, acc[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < GV_M; ++i) part[w][i][lane] = acc[i];
+  __syncthreads();
+  if (w == 0 && n < N) {
+#pragma unroll
+    for (int i = 0; i < GV_M; ++i) {
+      if (m0 + i >= M) break;
+      float x = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < 8; ++ww) x += part[ww][i][lane];
+      if (bias) x += bias[n];
+      if (silu) x = x / (1.0f + expf(-x));
+      C[(m0 + i) * N + n] = x;
+    }
+  }
+}
+
 cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float* C, int64_t M, int N, int K,
                         bool silu, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
+  if (M <= 4 * GV_M) {
+    gemv_f32_kernel<<<dim3((N + 31) / 32, (unsigned)((M + GV_M - 1) / GV_M)), 256, 0, s>>>(A, B, bias, C, M, N, K,
+                                                                                         silu ? 1 : 0);
+    count_launch();
+    return cudaGetLastError();
+  }
   dim3 grid((N + GB_N - 1) / GB_N, (unsigned)((M + GB_M - 1) / GB_M));
   gemm_f32_kernel<<<grid, 256, 0, s>>>(A, B, bias, C, M, N, K, silu ? 1 : 0);
   count_launch();

@@ -278,3 +278,38 @@ def test_gpu_cfg3_pool_shapes():
     """configs[3] routing: n_sub_keys 32768 (2^30 slots), H 8, d_key 256,
     top_k 32, bf16 rows (d reduced to 16: a 34 GB table on one GPU)."""
     _big_pool_case(32768, 8, 256, 16, 32, torch.bfloat16, 48, seed=3)
+
+
+@pytest.mark.parametrize("M,n,k,qscale,noisy", [(1, 300, 16, False, False), (7, 300, 8, True, False),
+                                                 (33, 1000, 32, False, True), (64, 2048, 16, True, True),
+                                                 (64, 256, 4, False, False)])
+def test_gpu_few_token_score_path(M, n, k, qscale, noisy):
+    """Decode-size calls (M <= 64, no routing statistics) take the split-key
+    score path: slots, weights and the read against the oracle, with ragged
+    last slices, query_scale and selection noise."""
+    from model_b200 import MemoryPool
+    H, dk, d = 2, 64, 32
+    pool = MemoryPool(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=qscale,
+                      routing_noise=2.0 if noisy else 0.0)
+    rng = np.random.default_rng(M * 1000 + n)
+    sk = rng.standard_normal((H, 2, n, dk // 2)).astype(np.float32)
+    values = (rng.standard_normal((n * n, d)) * 0.02).astype(np.float32)
+    q = rng.standard_normal((M, H, dk)).astype(np.float32)
+    gum = rng.gumbel(size=(M, H, 2, n)).astype(np.float32) if noisy else None
+    params = {"sub_keys": _dev(sk), "values": _dev(values),
+              "log_temperature": torch.tensor(np.log(10.0), dtype=torch.float32, device="cuda")}
+    kw = dict(train=noisy, stats=False, check=True)
+    if noisy:
+        kw["gumbel"] = _dev(gum)
+    out, aux = pool.apply({"params": params}, _dev(q), **kw)
+    torch.cuda.synchronize()
+    cfg = ref.PoolConfig(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=qscale,
+                         routing_noise=2.0 if noisy else 0.0)
+    o_ref, a_ref = ref.pool_forward(cfg, q, sk, float(np.log(10.0)), values, train=noisy, gumbel=gum,
+                                    with_stats=False)
+    r = ref.route(cfg, q, sk, float(np.log(10.0)), noisy, gum)
+    check_slots(aux["slots"].cpu().numpy(), a_ref["slots"], r["select"], n)
+    same = (aux["slots"].cpu().numpy() == a_ref["slots"]).all(-1)
+    np.testing.assert_allclose(aux["weights"].cpu().numpy()[same], a_ref["weights"][same], rtol=1e-5, atol=1e-7)
+    if same.all():
+        assert_rel(out.cpu().numpy(), o_ref, OUT_RTOL_F32, "out")
