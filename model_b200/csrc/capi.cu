@@ -96,8 +96,10 @@ size_t layout(const Dims& D, const Flags& f, char* ws, Work* W) {
     w.clean_idx = (int*)take(sizeof(int) * rows * D.k);
     w.row_max = (float*)take(sizeof(float) * rows);
     w.row_sum = (float*)take(sizeof(float) * rows);
-    w.p_part = (float*)take(sizeof(float) * tiles * D.H * 2 * D.n);
+    w.p_part = (float*)take(sizeof(float) * tiles * 4 * D.H * 2 * D.n);   // 4 lane quarters per tile (TC pass)
     w.clean_cnt = (float*)take(sizeof(float) * D.H * 2 * D.n);
+    w.bal_part = (double*)take(sizeof(double) * ((D.H * 2 * D.n + 31) / 32));
+    w.bal_ctr = (int*)take(sizeof(int));
   }
   if (f.layer) {
     const int64_t NRD = (int64_t)D.H * D.dk + D.d;

@@ -71,6 +71,8 @@ struct Work {
   float* out = nullptr;        // [M,d] when the caller passes none
   int* own_cnt = nullptr;      // [M,world] entries each owner rank gathers (row-sharded pool)
   float* small = nullptr;      // slice top-k lists of the few-token score path
+  double* bal_part = nullptr;  // [H*2*n/32] per-block sums of the balance loss
+  int* bal_ctr = nullptr;      // [1] blocks done in the balance-loss reduction (reset by its last block)
 };
 
 constexpr int SCORE_TM = 128;   // tokens per score tile
@@ -201,6 +203,7 @@ bool score_small_supported(const Dims& D);
 size_t score_small_scratch_bytes(const Dims& D);
 cudaError_t launch_score_small(const Dims& D, const Work& W, const float* gumbel, float* scratch, cudaStream_t s);
 cudaError_t launch_balance(const Dims& D, const Work& W, float* balance_loss, cudaStream_t s);
+cudaError_t launch_balance_tc(const Dims& D, const Work& W, int* planes, cudaStream_t s);
 cudaError_t launch_combine_gather(const Dims& D, const Work& W, const void* values, int* slots, float* weights,
                                   float* out, float* mem_gated, float* memg_hi, float* memg_lo, const float* gate,
                                   float* slot_counts, float* subkey_counts, cudaStream_t s);

@@ -212,26 +212,45 @@ __global__ void count_clean_kernel(Dims D, const int* __restrict__ idx, float* _
 }
 
 // balance_loss = n * mean_{h,c} sum_i f[h,c,i] * P[h,c,i]   (memory.py:214)
-__global__ void balance_finalize_kernel(Dims D, const float* __restrict__ p_part, int tiles,
-                                        const float* __restrict__ cnt, float* __restrict__ out) {
-  __shared__ double red[32];
+// balance_loss = n * mean_{h,c} sum_i f[h,c,i] * P[h,c,i]   (memory.py:214).
+// One block per 32 sub-keys: the 8 warps add disjoint sets of the `planes`
+// partial column sums (lane = sub-key), the sets are added in warp order,
+// then f * P is summed per block; the last block (ticket) adds the block sums
+// in block order.  Every sum has a fixed order: the result is deterministic.
+__global__ void __launch_bounds__(256) balance_finalize_kernel(Dims D, const float* __restrict__ p_part, int planes,
+                                                               const float* __restrict__ cnt,
+                                                               double* __restrict__ part, int* __restrict__ ticket,
+                                                               float* __restrict__ out) {
+  __shared__ double red[8][32];
+  __shared__ bool last;
   const int64_t total = (int64_t)D.H * 2 * D.n;
-  double acc = 0.0;
-  const double inv_mk = 1.0 / ((double)D.M * D.k);
-  for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
-    double P = 0.0;
-    for (int t = 0; t < tiles; ++t) P += (double)p_part[(int64_t)t * total + e];
-    P /= (double)D.M;
-    acc += ((double)cnt[e] * inv_mk) * P;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t e = (int64_t)blockIdx.x * 32 + lane;
+  double P = 0.0;
+  if (e < total)
+    for (int t = w; t < planes; t += 8) P += (double)p_part[(int64_t)t * total + e];
+  red[w][lane] = P;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (w == 0) {
+    double Pe = 0.0;
+    for (int ww = 0; ww < 8; ++ww) Pe += red[ww][lane];
+    const double inv_mk = 1.0 / ((double)D.M * D.k);
+    double c = e < total ? ((double)cnt[e] * inv_mk) * (Pe / (double)D.M) : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(FULL, c, o);
+    if (lane == 0) {
+      part[blockIdx.x] = c;
+      __threadfence();
+      last = atomicAdd(ticket, 1) == (int)gridDim.x - 1;
+    }
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
     double t = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    for (unsigned b = 0; b < gridDim.x; ++b) t += ((volatile double*)part)[b];
     out[0] = D.M > 0 ? (float)((double)D.n * t / (double)(D.H * 2)) : __int_as_float(0x7fc00000);
+    *ticket = 0;
   }
 }
 
@@ -269,22 +288,30 @@ cudaError_t launch_score_topk(const Dims& D, const Work& W, const float* gumbel,
 }
 
 cudaError_t launch_balance(const Dims& D, const Work& W, float* balance_loss, cudaStream_t s) {
-  const int tiles = (int)((D.M + TM - 1) / TM);
+  int planes = (int)((D.M + TM - 1) / TM);
   cudaError_t e = cudaMemsetAsync(W.clean_cnt, 0, sizeof(float) * D.H * 2 * D.n, s);
   if (e != cudaSuccess) return e;
   if (D.M > 0) {
-    size_t smem = (size_t)(D.half * TM + D.half * TN + TM * (TN + 1)) * sizeof(float);
-    e = cudaFuncSetAttribute(balance_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    balance_cols_kernel<<<dim3(tiles, D.H * 2), NT, smem, s>>>(D, W.qn, W.qlen, W.keys_n, W.scal, W.row_max,
-                                                               W.row_sum, W.p_part);
+    if (W.q_hi) {
+      // tensor-core pass over the same query / key halves as the score kernel
+      if ((e = launch_balance_tc(D, W, &planes, s)) != cudaSuccess) return e;
+    } else {
+      size_t smem = (size_t)(D.half * TM + D.half * TN + TM * (TN + 1)) * sizeof(float);
+      e = cudaFuncSetAttribute(balance_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      balance_cols_kernel<<<dim3(planes, D.H * 2), NT, smem, s>>>(D, W.qn, W.qlen, W.keys_n, W.scal, W.row_max,
+                                                                  W.row_sum, W.p_part);
+      count_launch();
+    }
     const int* idx = D.noisy ? W.clean_idx : W.sub_idx;
     int64_t total = D.M * D.H * 2 * D.k;
     unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
     count_clean_kernel<<<blocks, 256, 0, s>>>(D, idx, W.clean_cnt);
-    count_launch(2);
+    count_launch();
   }
-  balance_finalize_kernel<<<1, 1024, 0, s>>>(D, W.p_part, tiles, W.clean_cnt, balance_loss);
+  if ((e = cudaMemsetAsync(W.bal_ctr, 0, sizeof(int), s)) != cudaSuccess) return e;   // workspace starts undefined
+  const unsigned fb = (unsigned)((D.H * 2 * D.n + 31) / 32);
+  balance_finalize_kernel<<<fb, 256, 0, s>>>(D, W.p_part, planes, W.clean_cnt, W.bal_part, W.bal_ctr, balance_loss);
   count_launch();
   return cudaGetLastError();
 }
