@@ -167,8 +167,9 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
   Work w2 = W;
   w2.qn = qn;
   const bool bal = a->balance_loss != nullptr;
-  if (W.q_hi)
-    ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, bal, s));
+  if (W.q_hi)   // the tensor-core balance pass computes its own row max / sum: the score kernel
+                // needs its statistics variant only for the clean top-k of noisy calls
+    ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, bal && D.noisy, s));
   else if (W.small && !bal)
     ML_TRY(launch_score_small(D, w2, a->gumbel, W.small, s));
   else

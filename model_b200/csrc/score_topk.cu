@@ -201,6 +201,25 @@ __global__ void __launch_bounds__(NT) balance_cols_kernel(Dims D, const float* _
   }
 }
 
+// Clean top-k counts per sub-key, through a shared-memory histogram per
+// block (skewed routing makes global atomics on a few sub-keys serialise);
+// integer-valued float adds are exact, so the order does not matter.
+__global__ void count_clean_smem_kernel(Dims D, const int* __restrict__ idx, float* __restrict__ cnt) {
+  extern __shared__ float hist[];
+  const int bins = D.H * 2 * D.n;
+  for (int i = threadIdx.x; i < bins; i += blockDim.x) hist[i] = 0.f;
+  __syncthreads();
+  const int64_t total = D.M * D.H * 2 * D.k;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / D.k;
+    const int hc = (int)(row % (D.H * 2));
+    atomicAdd(&hist[hc * D.n + idx[e]], 1.f);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < bins; i += blockDim.x)
+    if (hist[i] != 0.f) atomicAdd(&cnt[i], hist[i]);
+}
+
 // Clean top-k counts per sub-key (the f of memory.py:208-209).
 __global__ void count_clean_kernel(Dims D, const int* __restrict__ idx, float* __restrict__ cnt) {
   int64_t total = D.M * D.H * 2 * D.k;
@@ -306,7 +325,11 @@ cudaError_t launch_balance(const Dims& D, const Work& W, float* balance_loss, cu
     const int* idx = D.noisy ? W.clean_idx : W.sub_idx;
     int64_t total = D.M * D.H * 2 * D.k;
     unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
-    count_clean_kernel<<<blocks, 256, 0, s>>>(D, idx, W.clean_cnt);
+    const size_t hbytes = sizeof(float) * D.H * 2 * D.n;
+    if (hbytes <= 48 * 1024)
+      count_clean_smem_kernel<<<blocks < 296 ? blocks : 296, 256, hbytes, s>>>(D, idx, W.clean_cnt);
+    else
+      count_clean_kernel<<<blocks, 256, 0, s>>>(D, idx, W.clean_cnt);
     count_launch();
   }
   if ((e = cudaMemsetAsync(W.bal_ctr, 0, sizeof(int), s)) != cudaSuccess) return e;   // workspace starts undefined

@@ -77,12 +77,14 @@ __device__ __forceinline__ void pipe_finish(PipeCtl* ctl, uint32_t tmem_base) {
   }
 }
 
-// Producer (one thread).  coords(u, &arow, &brow0, &nchunks).
+// Producer (one thread).  coords(u, &arow, &brow0, &nchunks).  With wrap > 0
+// chunk j of a unit reads B rows from chunk j % wrap (a unit that passes
+// over the same B rows several times).
 template <class Coords>
 __device__ __forceinline__ void pipe_produce(PipeCtl* ctl, const PipeShape& P, uint8_t* tiles, int units,
                                              const CUtensorMap* tA_hi, const CUtensorMap* tA_lo,
                                              const CUtensorMap* tB_hi, const CUtensorMap* tB_lo, Coords coords,
-                                             int* err) {
+                                             int* err, int wrap = 0) {
   volatile int* abort = &ctl->abort;
   prefetch_tmap(tA_hi);
   prefetch_tmap(tA_lo);
@@ -94,7 +96,7 @@ __device__ __forceinline__ void pipe_produce(PipeCtl* ctl, const PipeShape& P, u
     int arow, brow0, nch;
     coords(u, arow, brow0, nch);
     for (int j = 0; j < nch; ++j) {
-      const int brow = brow0 + j * P.BN;
+      const int brow = brow0 + (wrap > 0 ? j % wrap : j) * P.BN;
       for (int kc = 0; kc < P.kchunks; ++kc) {
         if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 11)) return;
         uint8_t* st = tiles + (size_t)s * P.stage_bytes;
