@@ -5,8 +5,10 @@
 // A read out[m] = sum_f w_f V[s_f] gives dL/dV[s] = sum over the fetches f
 // of slot s of w_f * g[m_f], g = dL/dout.  The fetches of all reads (memory
 // layers sharing the pool) are numbered in concatenation order and
-//   1. sorted by slot with a stable LSD radix sort (so each slot's fetches
-//      stay in fetch order and every sum below has a fixed order);
+//   1. sorted by slot with a stable LSD radix sort of up to 10 bits per pass
+//      (per-block digit counts, a per-digit scan, warp-stable scatter), so
+//      each slot's fetches stay in fetch order and every sum below has a
+//      fixed order;
 //   2. cut into segments of equal slot (uniq = the segments' slots,
 //      ascending, as jnp.unique returns them);
 //   3. summed per segment by one warp per chunk of 64 sorted fetches: a
@@ -35,28 +37,31 @@ constexpr int RS_WARP_ITEMS = RS_TILE / 8;        // 512 keys per warp
 constexpr int SEG_TILE = 1024;                    // flags per scan block
 constexpr int CHUNK = 64;                         // sorted fetches per row warp
 constexpr int SQ_BLOCKS = 64;
+constexpr int MAX_DIGITS = 1024;                 // radix digits per pass (<= 10 bits)
+constexpr uint32_t DROPPED = 0x80000000u;        // fetch-id flag: out-of-range slot, contributes zero
 
-// ---- 1. keys: slot of every fetch (bad ids sort last as key N) ----
-__global__ void rg_keys_kernel(RowGradK R, uint32_t* keys, uint32_t* vals, int* bad, int* err) {
+// ---- 1. keys: slot of every fetch (an out-of-range id is recorded and its
+// fetch is flagged to contribute nothing) ----
+__global__ void rg_keys_kernel(RowGradK R, uint32_t* keys, uint32_t* vals, int* err) {
   const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= R.F) return;
   int r = 0;
   while (r + 1 < R.n_reads && f >= R.off[r + 1]) ++r;
   const int s = R.slots[r][f - R.off[r]];
-  uint32_t key = (uint32_t)s;
-  if (s < 0 || (int64_t)s >= R.N) {   // only a caller bug can cause this: record it, drop the fetch
+  uint32_t key = (uint32_t)s, val = (uint32_t)f;
+  if (s < 0 || (int64_t)s >= R.N) {   // only a caller bug can cause this: record it, the fetch adds nothing
     atomicCAS(err, 0, 23);
-    atomicAdd(bad, 1);
-    key = (uint32_t)R.N;
+    key = (uint32_t)(R.N - 1);
+    val |= DROPPED;
   }
   keys[f] = key;
-  vals[f] = (uint32_t)f;
+  vals[f] = val;
 }
 
 // ---- 2. stable LSD radix sort ----
 __global__ void __launch_bounds__(RS_THREADS) rs_hist_kernel(const uint32_t* keys, int64_t F, int shift,
                                                              int digits, int nblk, int* hist) {
-  __shared__ int cnt[256];
+  __shared__ int cnt[MAX_DIGITS];
   for (int i = threadIdx.x; i < digits; i += RS_THREADS) cnt[i] = 0;
   __syncthreads();
   const int64_t t0 = (int64_t)blockIdx.x * RS_TILE;
@@ -105,14 +110,70 @@ __global__ void __launch_bounds__(1024) scan_excl_kernel(int* a, int64_t n, int*
   if (total && t == 1023) *total = run;
 }
 
+// Exclusive scan of each digit's row of per-block counts (one block per
+// digit, in place); dtot[d] = the digit's total.
+__global__ void __launch_bounds__(256) rs_digit_scan_kernel(int* hist, int nblk, int* dtot) {
+  __shared__ int wsum[8];
+  const int d = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  int* row = hist + (int64_t)d * nblk;
+  const int per = (nblk + 255) / 256, b = t * per, e = min(b + per, nblk);
+  int s = 0;
+  for (int i = b; i < e; ++i) s += row[i];
+  int x = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(FULL, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[w] = x;
+  __syncthreads();
+  int wb = 0;
+  for (int i = 0; i < w; ++i) wb += wsum[i];
+  int run = wb + x - s;
+  for (int i = b; i < e; ++i) {
+    const int v = row[i];
+    row[i] = run;
+    run += v;
+  }
+  if (t == 255) dtot[d] = wb + x;
+}
+
 __global__ void __launch_bounds__(RS_THREADS) rs_scatter_kernel(const uint32_t* kin, const uint32_t* vin, int64_t F,
                                                                 int shift, int digits, int nblk, const int* hist,
-                                                                uint32_t* kout, uint32_t* vout) {
-  __shared__ int wcnt[8][256];
-  __shared__ int base[256];
+                                                                const int* dtot, uint32_t* kout, uint32_t* vout) {
+  __shared__ int wcnt[8][MAX_DIGITS];
+  __shared__ int base[MAX_DIGITS];
+  __shared__ int wsum[RS_THREADS / 32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < 8 * 256; i += RS_THREADS) (&wcnt[0][0])[i] = 0;
-  for (int i = threadIdx.x; i < digits; i += RS_THREADS) base[i] = hist[(int64_t)i * nblk + blockIdx.x];
+  for (int i = threadIdx.x; i < 8 * MAX_DIGITS; i += RS_THREADS) (&wcnt[0][0])[i] = 0;
+  // base[d] = keys of smaller digits (exclusive scan of the digit totals)
+  //         + keys of digit d in earlier blocks
+  {
+    constexpr int PER = MAX_DIGITS / RS_THREADS;   // 4 digits per thread
+    int v[PER], s = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int dg = threadIdx.x * PER + j;
+      v[j] = dg < digits ? dtot[dg] : 0;
+      s += v[j];
+    }
+    int x = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(FULL, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    int run = x - s;
+    for (int i = 0; i < w; ++i) run += wsum[i];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int dg = threadIdx.x * PER + j;
+      if (dg < digits) base[dg] = run + hist[(int64_t)dg * nblk + blockIdx.x];
+      run += v[j];
+    }
+  }
   __syncthreads();
   const uint32_t mask = (uint32_t)digits - 1;
   const unsigned lt = (1u << lane) - 1u;
@@ -126,7 +187,7 @@ __global__ void __launch_bounds__(RS_THREADS) rs_scatter_kernel(const uint32_t* 
     const bool ok = e < F;
     k[r] = ok ? kin[e] : 0u;
     v[r] = ok ? vin[e] : 0u;
-    const int dg = ok ? (int)((k[r] >> shift) & mask) : 256 + lane;   // padding lanes never match
+    const int dg = ok ? (int)((k[r] >> shift) & mask) : MAX_DIGITS + lane;   // padding lanes never match
     const unsigned peers = __match_any_sync(FULL, dg);
     rk[r] = ok ? wcnt[w][dg] + __popc(peers & lt) : -1;
     __syncwarp();
@@ -160,8 +221,8 @@ __device__ __forceinline__ bool seg_head(const uint32_t* keys, int64_t i, int64_
   return i < Fv && (i == 0 || keys[i] != keys[i - 1]);
 }
 
-__global__ void __launch_bounds__(256) seg_count_kernel(const uint32_t* keys, int64_t F, const int* bad, int* tot) {
-  const int64_t Fv = F - *bad;
+__global__ void __launch_bounds__(256) seg_count_kernel(const uint32_t* keys, int64_t F, int* tot) {
+  const int64_t Fv = F;
   const int64_t b0 = (int64_t)blockIdx.x * SEG_TILE;
   int c = 0;
   for (int i = threadIdx.x; i < SEG_TILE; i += 256) c += seg_head(keys, b0 + i, Fv);
@@ -178,11 +239,10 @@ __global__ void __launch_bounds__(256) seg_count_kernel(const uint32_t* keys, in
 
 // seg_id of every sorted fetch, seg_start / slot of every segment, and the
 // sentinels seg_start[U] = F_valid and *n_seg = U.
-__global__ void __launch_bounds__(256) seg_write_kernel(const uint32_t* keys, int64_t F, const int* bad,
-                                                        const int* tot_scanned, int nb, int* seg_id, int* seg_start,
-                                                        int* uniq, int* n_seg) {
+__global__ void __launch_bounds__(256) seg_write_kernel(const uint32_t* keys, int64_t F, const int* tot_scanned,
+                                                        int nb, int* seg_id, int* seg_start, int* uniq, int* n_seg) {
   __shared__ int ws[8];
-  const int64_t Fv = F - *bad;
+  const int64_t Fv = F;
   const int64_t b0 = (int64_t)blockIdx.x * SEG_TILE;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   int run = tot_scanned[blockIdx.x];
@@ -226,13 +286,14 @@ struct Fetch {
 __device__ __forceinline__ Fetch load_fetch(const RowGradK& R, const int* seg_id, const uint32_t* vals, int64_t i) {
   Fetch x;
   x.seg = seg_id[i];
-  const int64_t f = vals[i];
+  const uint32_t raw = vals[i];
+  const int64_t f = raw & ~DROPPED;
   int r = 0;
   while (r + 1 < R.n_reads && f >= R.off[r + 1]) ++r;
   const int64_t lf = f - R.off[r];
   x.read = r;
   x.token = (int)(lf / R.hk);
-  x.w = R.weights[r][lf];
+  x.w = (raw & DROPPED) ? 0.f : R.weights[r][lf];
   return x;
 }
 
@@ -286,12 +347,11 @@ __device__ __forceinline__ void flush(const RowGradK& R, const int* seg_start, i
 }
 
 template <int VPL>
-__global__ void __launch_bounds__(256) rg_rows_kernel(RowGradK R, const int* bad, const int* seg_id,
-                                                      const uint32_t* vals, const int* seg_start, float* rows,
-                                                      float* rowsq, float* spill) {
+__global__ void __launch_bounds__(256) rg_rows_kernel(RowGradK R, const int* seg_id, const uint32_t* vals,
+                                                      const int* seg_start, float* rows, float* rowsq, float* spill) {
   const int lane = threadIdx.x & 31;
   const int64_t chunk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int64_t Fv = R.F - *bad;
+  const int64_t Fv = R.F;
   const int64_t i0 = chunk * CHUNK;
   if (i0 >= Fv) return;
   const int64_t i1 = i0 + CHUNK < Fv ? i0 + CHUNK : Fv;
@@ -325,12 +385,11 @@ __global__ void __launch_bounds__(256) rg_rows_kernel(RowGradK R, const int* bad
 // One warp per chunk: the chunk where a boundary-crossing segment starts
 // adds the partials of every chunk the segment covers, in chunk order.
 template <int VPL>
-__global__ void __launch_bounds__(256) rg_span_kernel(RowGradK R, const int* bad, const int* seg_id,
-                                                      const int* seg_start, float* rows, float* rowsq,
-                                                      const float* spill) {
+__global__ void __launch_bounds__(256) rg_span_kernel(RowGradK R, const int* seg_id, const int* seg_start,
+                                                      float* rows, float* rowsq, const float* spill) {
   const int lane = threadIdx.x & 31;
   const int64_t chunk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int64_t Fv = R.F - *bad;
+  const int64_t Fv = R.F;
   const int64_t i0 = chunk * CHUNK;
   if (i0 >= Fv) return;
   const int64_t i1 = i0 + CHUNK < Fv ? i0 + CHUNK : Fv;
@@ -476,8 +535,8 @@ RowGradLayout rowgrad_layout(int64_t F, int64_t N, int d) {
   auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
   RowGradLayout L{};
   int bits = 1;
-  while (bits < 32 && (((int64_t)1 << bits) <= N)) ++bits;   // keys in [0, N]
-  L.passes = (bits + 7) / 8;
+  while (bits < 32 && (((int64_t)1 << bits) < N)) ++bits;    // keys in [0, N - 1]
+  L.passes = (bits + 9) / 10;
   L.rbits = (bits + L.passes - 1) / L.passes;
   L.nblk = F > 0 ? (F + RS_TILE - 1) / RS_TILE : 1;
   L.nseg_blk = F > 0 ? (F + SEG_TILE - 1) / SEG_TILE : 1;
@@ -489,13 +548,14 @@ RowGradLayout rowgrad_layout(int64_t F, int64_t N, int d) {
     o += up(bytes);
     return at;
   };
-  L.o_small = take(256);                                  // bad fetches, segments, ticket
+  L.o_small = take(256);                                  // segment count, ticket
   L.o_err = take(256);                                    // status word (offset 256, as in the forward layouts)
   L.o_keys_a = take(4 * F);
   L.o_vals_a = take(4 * F);
   L.o_keys_b = take(4 * F);
   L.o_vals_b = take(4 * F);
   L.o_hist = take(4 * ((int64_t)1 << L.rbits) * L.nblk);
+  L.o_dtot = take(4 * ((int64_t)1 << L.rbits));
   L.o_segtot = take(4 * L.nseg_blk);
   L.o_seg_id = take(4 * F);
   L.o_seg_start = take(4 * (L.cap + 1));
@@ -513,7 +573,8 @@ cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, 
                            int* n_unique_out, float* sq_out, const RowAdagrad* ada, cudaStream_t s) {
   int* small = reinterpret_cast<int*>(ws + L.o_small);
   int* err = reinterpret_cast<int*>(ws + L.o_err);
-  int* bad = small, *n_seg = small + 1, *ticket = small + 2;
+  int* n_seg = small + 1, *ticket = small + 2;
+  int* dtot = reinterpret_cast<int*>(ws + L.o_dtot);
   uint32_t* ka = reinterpret_cast<uint32_t*>(ws + L.o_keys_a);
   uint32_t* va = reinterpret_cast<uint32_t*>(ws + L.o_vals_a);
   uint32_t* kb = reinterpret_cast<uint32_t*>(ws + L.o_keys_b);
@@ -532,29 +593,29 @@ cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, 
   if ((e = cudaMemsetAsync(small, 0, 512, s)) != cudaSuccess) return e;   // counters and status word
   const int64_t F = R.F;
   if (F > 0) {
-    rg_keys_kernel<<<(unsigned)((F + 255) / 256), 256, 0, s>>>(R, ka, va, bad, err);
+    rg_keys_kernel<<<(unsigned)((F + 255) / 256), 256, 0, s>>>(R, ka, va, err);
     count_launch();
     const int digits = 1 << L.rbits;
     for (int p = 0; p < L.passes; ++p) {
       const int shift = p * L.rbits;
       rs_hist_kernel<<<(unsigned)L.nblk, RS_THREADS, 0, s>>>(ka, F, shift, digits, (int)L.nblk, hist);
-      scan_excl_kernel<<<1, 1024, 0, s>>>(hist, (int64_t)digits * L.nblk, nullptr);
-      rs_scatter_kernel<<<(unsigned)L.nblk, RS_THREADS, 0, s>>>(ka, va, F, shift, digits, (int)L.nblk, hist, kb, vb);
+      rs_digit_scan_kernel<<<(unsigned)digits, 256, 0, s>>>(hist, (int)L.nblk, dtot);
+      rs_scatter_kernel<<<(unsigned)L.nblk, RS_THREADS, 0, s>>>(ka, va, F, shift, digits, (int)L.nblk, hist, dtot,
+                                                                kb, vb);
       count_launch(3);
       uint32_t* t = ka; ka = kb; kb = t;
       t = va; va = vb; vb = t;
     }
     // sorted keys / fetch ids are now in (ka, va)
-    seg_count_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, bad, segtot);
+    seg_count_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, segtot);
     scan_excl_kernel<<<1, 1024, 0, s>>>(segtot, L.nseg_blk, nullptr);
-    seg_write_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, bad, segtot, (int)L.nseg_blk, seg_id, seg_start,
-                                                          uniq, n_seg);
+    seg_write_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, segtot, (int)L.nseg_blk, seg_id, seg_start, uniq,
+                                                          n_seg);
     count_launch(3);
     const unsigned wblocks = (unsigned)((L.chunks + 7) / 8);
-    ML_VPL(vpl_for(R.d), (rg_rows_kernel<VP><<<wblocks, 256, 0, s>>>(R, bad, seg_id, va, seg_start, rows, rowsq,
+    ML_VPL(vpl_for(R.d), (rg_rows_kernel<VP><<<wblocks, 256, 0, s>>>(R, seg_id, va, seg_start, rows, rowsq,
                                                                       spill)));
-    ML_VPL(vpl_for(R.d), (rg_span_kernel<VP><<<wblocks, 256, 0, s>>>(R, bad, seg_id, seg_start, rows, rowsq,
-                                                                      spill)));
+    ML_VPL(vpl_for(R.d), (rg_span_kernel<VP><<<wblocks, 256, 0, s>>>(R, seg_id, seg_start, rows, rowsq, spill)));
     count_launch(2);
   }
   rg_sqnorm_kernel<<<SQ_BLOCKS, 256, 0, s>>>(rowsq, n_seg, part, ticket, sq_out, sqd);
