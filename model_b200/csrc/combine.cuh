@@ -8,7 +8,9 @@
 // candidates rank ahead, so only the candidates with (i+1)(j+1) <= k can be
 // selected (8 / 20 / 50 / 119 of them for k = 4 / 8 / 16 / 32).  Those are
 // sorted across the warp by a bitonic network on (value desc, flat index
-// asc), which is lax.top_k's order on the full k*k list (memory.py:171).
+// asc), which is lax.top_k's order on the full k*k list (memory.py:171);
+// candidates under a lower bound of the k-th best sum are dropped first, so
+// the sort is usually 32 wide.
 #pragma once
 
 #include "common.cuh"
@@ -32,9 +34,12 @@ __device__ __forceinline__ void load_group(const VT* p, float (&o)[VEC]) {
   }
 }
 
-// Eligible stage-2 candidates (i, j) with (i+1)(j+1) <= k, row-major.
+// Eligible stage-2 candidates (i, j) with (i+1)(j+1) <= k, row-major, and
+// the k candidates with the smallest (i+1)(j+1): the minimum of their sums is
+// a lower bound of the k-th best sum (at least k candidates reach it).
 struct PairTable {
   uint16_t ij[128];  // i | j << 8
+  uint16_t lb[32];   // the k most dominant pairs
   int count;
 };
 
@@ -44,7 +49,25 @@ inline PairTable make_pairs(int k) {
   for (int i = 0; i < k; ++i)
     for (int j = 0; j < k && (i + 1) * (j + 1) <= k; ++j) t.ij[c++] = (uint16_t)(i | (j << 8));
   t.count = c;
+  int n = 0;
+  for (int prod = 1; n < k; ++prod)          // products in increasing order, row-major within one
+    for (int i = 0; i < k && n < k; ++i)
+      if (prod % (i + 1) == 0 && prod / (i + 1) - 1 < k) t.lb[n++] = (uint16_t)(i | ((prod / (i + 1) - 1) << 8));
   return t;
+}
+
+// Position of the n-th (0-based) set bit of m; requires n < popc(m).
+__device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
+  int pos = 0;
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1) {
+    const int c = __popc((unsigned)(((uint64_t)m >> pos) & ((1ull << w) - 1)));
+    if (c <= n) {
+      n -= c;
+      pos += w;
+    }
+  }
+  return pos;
 }
 
 // Bitonic sort of 32*C (value, flat) pairs held C per lane (position
@@ -103,8 +126,8 @@ struct HeadPick {
 // One (token m, head h) on one warp.  `tab` is the pair table staged in
 // shared memory; ra indexes the head's first-half stage-1 list.
 template <int KM>
-__device__ __forceinline__ HeadPick combine_head(const Dims& D, const uint16_t* tab, int pair_count,
-                                                 const int* __restrict__ sub_idx,
+__device__ __forceinline__ HeadPick combine_head(const Dims& D, const uint16_t* tab, const uint16_t* lbtab,
+                                                 int pair_count, const int* __restrict__ sub_idx,
                                                  const float* __restrict__ sub_score,
                                                  const float* __restrict__ sub_sel, int64_t ra, int lane,
                                                  int* __restrict__ err) {
@@ -135,13 +158,55 @@ __device__ __forceinline__ HeadPick combine_head(const Dims& D, const uint16_t* 
     cv[r] = ok ? x + y : -INFINITY;                  // memory.py:168 cand_select
     cf[r] = ok ? i * k + j : (1 << 30) + slot;       // flat index in the k*k grid
   }
-  warp_sort_desc<C>(cv, cf, lane);
-  // lane r < k takes sorted position r
-  int my_flat = 0;
+  // candidates below the k-th best's lower bound cannot be selected: when at
+  // most 32 remain, one per lane, a 32-wide sort replaces the 32*C-wide one
+  unsigned msk[C];
+  int basep[C], tot = 64;
+  if constexpr (C > 1) {
+    const int lij = lane < k ? lbtab[lane] : 0;
+    const float lbs = __shfl_sync(FULL, as, lij & 0xFF) + __shfl_sync(FULL, bs, lij >> 8);
+    float bound = lane < k ? lbs : INFINITY;
 #pragma unroll
-  for (int r = 0; r < C; ++r) {
-    const int f = __shfl_sync(FULL, cf[r], lane / C);
-    if ((lane % C) == r) my_flat = f;
+    for (int o = 16; o > 0; o >>= 1) bound = fminf(bound, __shfl_xor_sync(FULL, bound, o));
+    tot = 0;
+#pragma unroll
+    for (int r = 0; r < C; ++r) {
+      msk[r] = __ballot_sync(FULL, cv[r] >= bound);
+      basep[r] = tot;
+      tot += __popc(msk[r]);
+    }
+  }
+  int my_flat = 0;
+  if (C > 1 && tot <= 32) {
+    int rr = -1, nn = 0;
+#pragma unroll
+    for (int r = 0; r < C; ++r)
+      if (rr < 0 && lane < basep[r] + __popc(msk[r])) {
+        rr = r;
+        nn = lane - basep[r];
+      }
+    const int src = rr >= 0 ? nth_set_bit(msk[rr], nn) : 0;
+    float v1[1] = {-INFINITY};
+    int f1[1] = {(1 << 30) + 128 + lane};      // padding: distinct, ranks last
+#pragma unroll
+    for (int r = 0; r < C; ++r) {
+      const float tv = __shfl_sync(FULL, cv[r], src);
+      const int tf = __shfl_sync(FULL, cf[r], src);
+      if (rr == r) {
+        v1[0] = tv;
+        f1[0] = tf;
+      }
+    }
+    warp_sort_desc<1>(v1, f1, lane);
+    my_flat = f1[0];
+  } else {
+    warp_sort_desc<C>(cv, cf, lane);
+    // lane r < k takes sorted position r
+#pragma unroll
+    for (int r = 0; r < C; ++r) {
+      const int f = __shfl_sync(FULL, cf[r], lane / C);
+      if ((lane % C) == r) my_flat = f;
+    }
   }
   const int fi = lk ? my_flat / k : 0, fj = lk ? my_flat - (my_flat / k) * k : 0;
   const float s = __shfl_sync(FULL, ac, fi) + __shfl_sync(FULL, bc, fj);     // memory.py:172

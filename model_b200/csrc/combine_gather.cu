@@ -27,7 +27,9 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
     float* __restrict__ top1_part, int* __restrict__ err) {
   extern __shared__ float red[];  // [H][d]
   __shared__ uint16_t tab[128];   // pair table, staged for divergent per-lane reads
+  __shared__ uint16_t lbtab[32];
   for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
+  for (int i = threadIdx.x; i < 32; i += blockDim.x) lbtab[i] = pairs.lb[i];
   __syncthreads();
   const int64_t m = blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -35,7 +37,7 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
   const int64_t ra = ((m * D.H + h) * 2) * k;
 
   const bool lk = lane < k;
-  const HeadPick p = combine_head<KM>(D, tab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
+  const HeadPick p = combine_head<KM>(D, tab, lbtab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
   const int slot = p.slot, ia = p.ia, ib = p.ib;
   const float w = p.w, top1 = p.top1;
   const int64_t ow = (m * D.H + h) * k;

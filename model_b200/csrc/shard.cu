@@ -100,8 +100,10 @@ __global__ void __launch_bounds__(1024) shard_push_kernel(
     float* __restrict__ subkey_counts, float* __restrict__ top1_part, int* __restrict__ own_cnt,
     int* __restrict__ err) {
   __shared__ uint16_t tab[128];
+  __shared__ uint16_t lbtab[32];
   __shared__ int cnt_s[32][MEMLAYER_MAX_SHARDS];   // [warp][owner] entries
   for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
+  for (int i = threadIdx.x; i < 32; i += blockDim.x) lbtab[i] = pairs.lb[i];
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = wid / D.H, h = wid - t * D.H;        // token slot in the CTA, head
   const int k = D.k, P = S.world;
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(1024) shard_push_kernel(
     __syncthreads();                                 // tab staged / previous cnt_s consumed
     if (active) {
       const int64_t ra = ((m * D.H + h) * 2) * k;
-      const HeadPick p = combine_head<KM>(D, tab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
+      const HeadPick p = combine_head<KM>(D, tab, lbtab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
       w = p.w;
       const int64_t ow = (m * D.H + h) * k;
       if (lk) {
