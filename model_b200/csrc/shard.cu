@@ -177,7 +177,12 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant
     const int64_t m = gw - (int64_t)srot * S.mcap;
     const int src = (S.rank + srot) % P;
     const char* mine = S.peer[S.rank];
-    if (wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + src, S.epoch, err, 31)) {
+    // lane 0 acquires the source's flag; __syncwarp orders the other lanes' reads after it
+    bool ready = true;
+    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + src, S.epoch, err, 31);
+    ready = __shfl_sync(FULL, ready, 0);
+    __syncwarp();
+    if (ready) {
       const int m_src = reinterpret_cast<const volatile int*>(mine + S.off.meta)[src];
       const int64_t grp = (int64_t)src * S.mcap + m;
       const int c = m < m_src ? reinterpret_cast<const volatile int*>(mine + S.off.cnt)[grp] : 0;
@@ -242,9 +247,16 @@ __global__ void __launch_bounds__(256) shard_reduce_kernel(const __grid_constant
                                                            float* __restrict__ memg_lo, int* __restrict__ err) {
   const int P = S.world, d4 = S.d / 4;
   const char* mine = S.peer[S.rank];
-  bool ok = true;
-  for (int o = 0; o < P && ok; ++o)
-    ok = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_part) + o, S.epoch, err, 32);
+  // thread 0 acquires every owner's flag; the barrier orders the CTA's reads after it
+  __shared__ bool ok_s;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int o = 0; o < P && ok; ++o)
+      ok = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_part) + o, S.epoch, err, 32);
+    ok_s = ok;
+  }
+  __syncthreads();
+  const bool ok = ok_s;
   const int per = blockDim.x / d4;
   const int t = threadIdx.x / d4, i = threadIdx.x - t * d4;
   const int64_t m = (int64_t)blockIdx.x * per + t;
