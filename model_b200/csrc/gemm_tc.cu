@@ -236,14 +236,18 @@ cudaError_t launch_proj(const ProjArgs& G, const float* a_hi, const float* a_lo,
   // bias vector (padded to 256 floats) + one staging tile per epilogue warp
   const uint32_t bias_bytes =
       (((uint32_t)(G.N + 255) / 256 * 256 * 4 + EPI_WARPS * STG_FLOATS * 4) + 1023) / 1024 * 1024;
-  tc::PipeShape P = tc::pipe_shape(BN, G.K, bias_bytes);
+  // 32-element K stages (128-byte swizzle).  16-element stages (64-byte
+  // swizzle, twice the ring depth) measured the same: the epilogue, not
+  // operand latency, bounds this GEMM.
+  constexpr int BK = 32;
+  tc::PipeShape P = tc::pipe_shape(BN, G.K, bias_bytes, BK);
   if (P.stages < 2) return cudaErrorInvalidConfiguration;
   CUtensorMap m[4];
   cudaError_t e;
-  if ((e = make_tmap_f32(&m[0], a_hi, G.M, G.K, tc::PIPE_M)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[1], a_lo, G.M, G.K, tc::PIPE_M)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[2], b_hi, G.N, G.K, BN)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[3], b_lo, G.N, G.K, BN)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[0], a_hi, G.M, G.K, tc::PIPE_M, BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[1], a_lo, G.M, G.K, tc::PIPE_M, BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[2], b_hi, G.N, G.K, BN, BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[3], b_lo, G.N, G.K, BN, BK)) != cudaSuccess) return e;
   const size_t smem = 2048 + (size_t)P.stages * P.stage_bytes + bias_bytes;
   auto kern = proj_gemm_tc_kernel<EPI>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)

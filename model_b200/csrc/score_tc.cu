@@ -741,16 +741,18 @@ cudaError_t launch_tc_k(const Dims& D, const Work& W, const float* gumbel, bool 
 
 }  // namespace
 
-cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                          uint32_t box_k) {
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
+  if (box_k != 16 && box_k != 32) return cudaErrorInvalidValue;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols * sizeof(float)};
-  cuuint32_t box[2] = {(cuuint32_t)TC_K, box_rows};
+  cuuint32_t box[2] = {box_k, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, box_k == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 

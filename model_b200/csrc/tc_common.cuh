@@ -90,6 +90,12 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// Same for 64-byte rows (SWIZZLE_64B, 8-row groups 512 bytes apart).
+__device__ __forceinline__ uint64_t sdesc_k_sw64(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+
 // Instruction descriptor: kind::tf32, D float32, A/B tf32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -168,6 +174,8 @@ __device__ __forceinline__ float to_tf32(float x) {
 
 // Host: 2-D tensor map over a row-major float32 matrix [rows, cols] with a
 // (box_rows x 32)-element box and 128-byte swizzle (cols * 4 % 16 == 0).
-cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+// box_k = 32 (128-byte rows, 128-byte swizzle) or 16 (64-byte rows, 64-byte swizzle)
+cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                          uint32_t box_k = 32);
 
 }  // namespace ml

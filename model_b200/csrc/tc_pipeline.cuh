@@ -28,16 +28,20 @@ struct PipeCtl {
 struct PipeShape {
   int BN;          // B rows per chunk (MMA N)
   int stages;      // smem ring depth
-  int kchunks;     // K / 32
+  int bk;          // K elements per stage: 32 (128-byte swizzled rows) or 16 (64-byte)
+  int kchunks;     // K / bk
   uint32_t a_bytes, b_bytes, stage_bytes;
 };
 
-__host__ __device__ inline PipeShape pipe_shape(int BN, int K, uint32_t extra_smem) {
+// bk = 16 halves the stage size so that twice as many stages fit (deeper
+// prefetch for operands read from L2).
+__host__ __device__ inline PipeShape pipe_shape(int BN, int K, uint32_t extra_smem, int bk = PIPE_K) {
   PipeShape P;
   P.BN = BN;
-  P.kchunks = K / PIPE_K;
-  P.a_bytes = PIPE_M * PIPE_K * 4;
-  P.b_bytes = BN * PIPE_K * 4;
+  P.bk = bk;
+  P.kchunks = K / bk;
+  P.a_bytes = PIPE_M * bk * 4;
+  P.b_bytes = BN * bk * 4;
   P.stage_bytes = 2 * P.a_bytes + 2 * P.b_bytes;
   const uint32_t limit = 227 * 1024;
   int st = (int)((limit - 2048 - extra_smem) / P.stage_bytes);
@@ -101,10 +105,10 @@ __device__ __forceinline__ void pipe_produce(PipeCtl* ctl, const PipeShape& P, u
         if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 11)) return;
         uint8_t* st = tiles + (size_t)s * P.stage_bytes;
         mbar_expect_tx(&ctl->full[s], P.stage_bytes);
-        tma_load_2d(st, tA_hi, &ctl->full[s], kc * PIPE_K, arow);
-        tma_load_2d(st + P.a_bytes, tA_lo, &ctl->full[s], kc * PIPE_K, arow);
-        tma_load_2d(st + 2 * P.a_bytes, tB_hi, &ctl->full[s], kc * PIPE_K, brow);
-        tma_load_2d(st + 2 * P.a_bytes + P.b_bytes, tB_lo, &ctl->full[s], kc * PIPE_K, brow);
+        tma_load_2d(st, tA_hi, &ctl->full[s], kc * P.bk, arow);
+        tma_load_2d(st + P.a_bytes, tA_lo, &ctl->full[s], kc * P.bk, arow);
+        tma_load_2d(st + 2 * P.a_bytes, tB_hi, &ctl->full[s], kc * P.bk, brow);
+        tma_load_2d(st + 2 * P.a_bytes + P.b_bytes, tB_lo, &ctl->full[s], kc * P.bk, brow);
         if (++s == P.stages) {
           s = 0;
           ph ^= 1;
@@ -134,14 +138,26 @@ __device__ __forceinline__ void pipe_mma(PipeCtl* ctl, const PipeShape& P, uint8
         fence_after_sync();
         const uint32_t a_hi = smem_u32(tiles + (size_t)s * P.stage_bytes);
         const uint32_t a_lo = a_hi + P.a_bytes, b_hi = a_hi + 2 * P.a_bytes, b_lo = b_hi + P.b_bytes;
+        if (P.bk == PIPE_K) {
 #pragma unroll
-        for (int k8 = 0; k8 < PIPE_K / 8; ++k8) {
-          const uint32_t off = k8 * 32;  // 8 tf32 = 32 bytes along K inside the swizzled row
-          const uint64_t dah = sdesc_k_sw128(a_hi + off), dal = sdesc_k_sw128(a_lo + off);
-          const uint64_t dbh = sdesc_k_sw128(b_hi + off), dbl = sdesc_k_sw128(b_lo + off);
-          mma_tf32(d, dah, dbh, idesc, (kc | k8) != 0);
-          mma_tf32(d, dah, dbl, idesc, 1);
-          mma_tf32(d, dal, dbh, idesc, 1);
+          for (int k8 = 0; k8 < PIPE_K / 8; ++k8) {
+            const uint32_t off = k8 * 32;  // 8 tf32 = 32 bytes along K inside the swizzled row
+            const uint64_t dah = sdesc_k_sw128(a_hi + off), dal = sdesc_k_sw128(a_lo + off);
+            const uint64_t dbh = sdesc_k_sw128(b_hi + off), dbl = sdesc_k_sw128(b_lo + off);
+            mma_tf32(d, dah, dbh, idesc, (kc | k8) != 0);
+            mma_tf32(d, dah, dbl, idesc, 1);
+            mma_tf32(d, dal, dbh, idesc, 1);
+          }
+        } else {
+#pragma unroll
+          for (int k8 = 0; k8 < 2; ++k8) {     // 16 tf32 = one 64-byte swizzled row
+            const uint32_t off = k8 * 32;
+            const uint64_t dah = sdesc_k_sw64(a_hi + off), dal = sdesc_k_sw64(a_lo + off);
+            const uint64_t dbh = sdesc_k_sw64(b_hi + off), dbl = sdesc_k_sw64(b_lo + off);
+            mma_tf32(d, dah, dbh, idesc, (kc | k8) != 0);
+            mma_tf32(d, dah, dbl, idesc, 1);
+            mma_tf32(d, dal, dbh, idesc, 1);
+          }
         }
         mma_commit(&ctl->empty[s]);  // the stage is free once these MMAs have read it
         if (++s == P.stages) {
