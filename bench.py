@@ -59,6 +59,9 @@ def parse():
                     help="cfg0 (default, the driver's line): configs[0] layer forward; cfg2: configs[2] decode "
                          "latency on a 67M-slot fp16 table; cfg3: configs[3] billion-slot bf16 table "
                          "row-sharded over >= 4 GPUs; cfg4: configs[4] forward + fetched-row Adagrad")
+    ap.add_argument("--emulate-ranks", type=int, default=0,
+                    help="time the row-sharded phases of P ranks driven from one process on one GPU "
+                         "(all ROUTE, then all GATHER, then all REDUCE); for profiling without NVLink")
     ap.add_argument("--pool", choices=["sharded", "replicated"], default="sharded",
                     help="N>1: row-shard the value table over the ranks (default) or replicate it")
     return ap.parse_args()
@@ -694,6 +697,57 @@ def run_cfg3(args, rank, world):
         "tensor_peak": tp, "note": "no L2 flush (the 68.7 GB/GPU table and 1.1 TFLOP/GPU score GEMM dwarf L2)"})
 
 
+def run_emulated(args):
+    """configs[0] shapes on P communicators of one process and one GPU: each
+    phase is launched for every rank before the next phase, so no kernel
+    waits on a later launch.  Reports per-phase device time per rank."""
+    import torch
+
+    from model_b200 import MemoryLayer, MemoryPool
+    from model_b200 import _lib as L
+    from model_b200.shard import ShardedCall, emulated_comms, shard_values
+    world = args.emulate_ranks
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    W = dict(WORKLOAD, tokens_per_gpu=args.tokens)
+    pool = MemoryPool(n_sub_keys=W["n_sub_keys"], heads=W["heads"], d_key=W["d_key"], d_value=W["d_value"],
+                      top_k=W["top_k"])
+    layer = MemoryLayer(pool, d_model=W["d_model"], layer=1)
+    params = layer.init(W["seed"])
+    T = W["tokens_per_gpu"]
+    comms = emulated_comms(pool.config(T, torch.float32, W["d_model"]), world)
+    calls = []
+    for r in range(world):
+        p = dict(params, pool=dict(params["pool"], values=shard_values(params["pool"]["values"], r, world)))
+        h = torch.randn(T, W["d_model"], device=device, generator=torch.Generator(device=device).manual_seed(r))
+        calls.append(ShardedCall(layer, comms[r], p, h))
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    res = {ph: [] for ph in ("route", "gather", "reduce")}
+    for it in range(args.warmup + args.steps):
+        for ph, code in (("route", L.PHASE_ROUTE), ("gather", L.PHASE_GATHER), ("reduce", L.PHASE_REDUCE)):
+            ev = []
+            for c in calls:
+                flush.zero_()
+                e0, e1 = _events(torch, 2)
+                e0.record(stream)
+                c.run(code)
+                e1.record(stream)
+                ev.append((e0, e1))
+            torch.cuda.synchronize()
+            if it >= args.warmup:
+                res[ph] += [a.elapsed_time(b) for a, b in ev]
+    for c in calls:
+        c.check()
+        c.comm.close()
+    ms = {k: statistics.median(v) for k, v in res.items()}
+    return {"metric": "row-sharded phase time per rank (emulated ranks, one GPU)", "value": sum(ms.values()),
+            "unit": "ms", "n_gpus": 1, "emulated_ranks": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "phases_ms": ms, "config": {"workload": "cfg0_layer_forward_sharded_emulated",
+                                                                   "tokens_per_rank": T},
+            "note": "partial rows and inbox entries stay in this GPU's memory: no NVLink traffic"}
+
+
 def main():
     args = parse()
     W = dict(WORKLOAD, values_dtype=args.values_dtype, tokens_per_gpu=args.tokens)
@@ -707,6 +761,8 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     if args.impl == "reference":
         line = run_reference(args, W, rank)
+    elif args.emulate_ranks:
+        line = run_emulated(args)
     elif args.workload == "cfg4":
         line = run_cfg4(args)
     elif args.workload == "cfg2":
