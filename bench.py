@@ -59,6 +59,9 @@ def parse():
                     help="cfg0 (default, the driver's line): configs[0] layer forward; cfg2: configs[2] decode "
                          "latency on a 67M-slot fp16 table; cfg3: configs[3] billion-slot bf16 table "
                          "row-sharded over >= 4 GPUs; cfg4: configs[4] forward + fetched-row Adagrad")
+    ap.add_argument("--split", action="store_true",
+                    help="N>1: one call per step with the exchange in two overlapped token halves "
+                         "(MEMLAYER_PHASE_SPLIT); default: the three phases one after another")
     ap.add_argument("--emulate-ranks", type=int, default=0,
                     help="time the row-sharded phases of P ranks driven from one process on one GPU "
                          "(all ROUTE, then all GATHER, then all REDUCE); for profiling without NVLink")
@@ -217,9 +220,17 @@ class ShardedLayerCall(LayerCall):
         self.ws_bytes = nb.value
 
     def __call__(self, stream, events=None, phase_events=None):
+        """phase_events None: one call, the two token halves overlapped
+        (the step the bench times); else the three phases one after another
+        with events between them (times the owner-side gather alone)."""
         for i in range(self.L.STAGE_EVENTS):
             self.events.events[i] = None if events is None else events[i].cuda_event
         f = self.L.lib().memlayer_layer_forward_sharded
+        if phase_events is None:
+            self.L.check(f(C.byref(self.cfg), C.byref(self.args), self.comm.handle,
+                           self.L.PHASE_ALL | self.L.PHASE_SPLIT, self.ws.data_ptr(), self.ws_bytes,
+                           stream.cuda_stream), "memlayer_layer_forward_sharded")
+            return
         for j, ph in enumerate((self.L.PHASE_ROUTE, self.L.PHASE_GATHER, self.L.PHASE_REDUCE)):
             self.L.check(f(C.byref(self.cfg), C.byref(self.args), self.comm.handle, ph, self.ws.data_ptr(),
                            self.ws_bytes, stream.cuda_stream), "memlayer_layer_forward_sharded")
@@ -361,13 +372,14 @@ def run_ours(args, W, rank, world):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    overlapped = sharded and args.split
     with ClockSampler(device.index) as clk:
         for i in range(K):
             flush.zero_()
-            if sharded:
-                call(stream, ev[i], pev[i])
+            if sharded and not overlapped:
+                call(stream, ev[i], pev[i])    # the three phases, events between them
             else:
-                call(stream, ev[i])
+                call(stream, ev[i])            # single GPU, or one split call
         torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -376,13 +388,32 @@ def run_ours(args, W, rank, world):
     stage = lambda a, b: statistics.mean(ev[i][a].elapsed_time(ev[i][b]) for i in range(K))  # noqa: E731
     stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
               "combine_gather": stage(3, 4), "finalize_out": stage(4, 5)}
-    if sharded:
+    if sharded and not overlapped:
         pstage = lambda f: statistics.mean(f(i) for i in range(K))  # noqa: E731
         stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
                   "combine_push": stage(3, 4),
                   "finalize": pstage(lambda i: ev[i][4].elapsed_time(pev[i][0])),
-                  "shard_gather": pstage(lambda i: pev[i][0].elapsed_time(pev[i][1])),
+                  "shard_gather_alone": pstage(lambda i: pev[i][0].elapsed_time(pev[i][1])),
                   "reduce_out": pstage(lambda i: pev[i][1].elapsed_time(ev[i][5]))}
+    if overlapped:
+        stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
+                  "combine_push": stage(3, 4), "exchange_reduce_out": stage(4, 5)}
+        # the owner-side gather alone: the three phases one after another,
+        # untimed in the step figure, for the gather kernel's roofline
+        G = min(K, 20)
+        gev = [[torch.cuda.Event(enable_timing=True) for _ in range(L.STAGE_EVENTS)] for _ in range(G)]
+        for row in gev:
+            for e in row:
+                e.record(stream)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        for i in range(G):
+            flush.zero_()
+            call(stream, gev[i], pev[i])
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        stages["shard_gather_alone"] = statistics.mean(pev[i][0].elapsed_time(pev[i][1]) for i in range(G))
+        stages["phased_step"] = statistics.mean(gev[i][0].elapsed_time(gev[i][5]) for i in range(G))
     ms = statistics.mean(step_ms)
 
     # ---- e2e through the C ABI with host buffers ----
@@ -446,7 +477,7 @@ def run_ours(args, W, rank, world):
         e2e_run(inflight, 2)
     e2e_ms = e2e_run(inflight, K)
     e2e_serial_ms = e2e_run(1, max(1, K // 2))
-    gather_stage = stages["shard_gather"] if sharded else stages["combine_gather"]
+    gather_stage = stages["shard_gather_alone"] if sharded else stages["combine_gather"]
     stats = torch.tensor([ms, e2e_ms, gather_stage, stages["score_topk"], e2e_serial_ms], dtype=torch.float64,
                          device=device)
     if world > 1:
@@ -490,7 +521,8 @@ def run_ours(args, W, rank, world):
         "config": {"workload": W["name"], **{k: W[k] for k in W if k != "name"},
                    "values_dtype": args.values_dtype,
                    "l2": "flushed before every step (256 MiB write, outside the step events)",
-                   "parallelism": (f"pool-row-shard{world}" if sharded else f"replicas{world}") if world > 1
+                   "parallelism": (f"pool-row-shard{world}" + ("-split" if overlapped else "") if sharded
+                                   else f"replicas{world}") if world > 1
                    else "single"},
         "roofline": {"kernel": dominant, "peak_source": src,
                      **{k: v for k, v in kernels[dominant].items() if k != "ms"}},

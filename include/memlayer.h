@@ -211,7 +211,13 @@ typedef enum {
   MEMLAYER_PHASE_ROUTE = 1,
   MEMLAYER_PHASE_GATHER = 2,
   MEMLAYER_PHASE_REDUCE = 4,
-  MEMLAYER_PHASE_ALL = 7
+  MEMLAYER_PHASE_ALL = 7,
+  /* Exchange in two token halves.  With all three phases in one call, the
+   * second half's push runs while the first half is gathered (on a stream
+   * the library keeps per device, ordered by events) and the first half's
+   * reduce while the second is gathered; `stream` covers the whole call.
+   * Every rank must pass the same flag in the same call. */
+  MEMLAYER_PHASE_SPLIT = 8
 } memlayer_shard_phase;
 
 /* Value rows held by `rank`: the slots s < pool_size with s % world == rank. */

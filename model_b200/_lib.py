@@ -37,7 +37,7 @@ class MemlayerConfig(C.Structure):
 STAGE_EVENTS = 6
 MAX_SHARDS = 8
 IPC_HANDLE_BYTES = 64
-PHASE_ROUTE, PHASE_GATHER, PHASE_REDUCE, PHASE_ALL = 1, 2, 4, 7
+PHASE_ROUTE, PHASE_GATHER, PHASE_REDUCE, PHASE_ALL, PHASE_SPLIT = 1, 2, 4, 7, 8
 
 
 class MemlayerStageEvents(C.Structure):

@@ -159,11 +159,19 @@ cudaError_t mark(const memlayer_pool_args* a, int i, cudaStream_t s) {
 
 // Routing from prepared unit queries onward: score + per-half top-k,
 // balance statistics, k*k combine + softmax + gather (+ gate), aux finalise.
+// The push of a row-sharded call: one launch per token half; after_a (if
+// set) is recorded between the halves.
+struct ShardRun {
+  ShardK half[2];
+  bool split;
+  cudaEvent_t after_a;
+};
+
 // With `sh` (row-sharded pool) stage 2 pushes its entries to the owner ranks
 // instead of gathering; out / memg / gate are then unused.
 int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, float* qn, int* slots,
                   float* weights, float* out, float* memg, float* memg_hi, float* memg_lo, const float* gate,
-                  cudaStream_t s, const ShardK* sh = nullptr) {
+                  cudaStream_t s, const ShardRun* sh = nullptr) {
   Work w2 = W;
   w2.qn = qn;
   const bool bal = a->balance_loss != nullptr;
@@ -178,9 +186,13 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
   if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
   if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
   ML_TRY(mark(a, 3, s));
-  if (sh)
-    ML_TRY(launch_shard_push(D, w2, *sh, slots, weights, a->slot_counts, a->subkey_counts, W.own_cnt, s));
-  else
+  if (sh) {
+    ML_TRY(launch_shard_push(D, w2, sh->half[0], slots, weights, a->slot_counts, a->subkey_counts, W.own_cnt, s));
+    if (sh->split) {
+      if (sh->after_a) ML_TRY(cudaEventRecord(sh->after_a, s));
+      ML_TRY(launch_shard_push(D, w2, sh->half[1], slots, weights, a->slot_counts, a->subkey_counts, W.own_cnt, s));
+    }
+  } else
     ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, memg_hi, memg_lo, gate,
                                  a->slot_counts, a->subkey_counts, s));
   ML_TRY(mark(a, 4, s));
@@ -226,7 +238,86 @@ ShardK shard_k(const memlayer_shard_comm* comm, const Dims& D) {
   S.d = D.d;
   S.rows = shard_rows(D.N, comm->rank, comm->world);
   S.epoch = comm->epoch;
+  S.hf = 0;
+  S.t0 = 0;
+  S.t1 = D.M;
+  S.span = S.mcap;
   return S;
+}
+
+// The two token halves of a split call (or the whole call as half 0).
+ShardRun shard_run(const memlayer_shard_comm* comm, const Dims& D, bool split) {
+  ShardRun R{};
+  R.split = split;
+  R.half[0] = shard_k(comm, D);
+  if (split) {
+    const int64_t h0 = (D.M + 1) / 2;
+    R.half[0].t1 = h0;
+    R.half[0].span = (R.half[0].mcap + 1) / 2;
+    R.half[1] = R.half[0];
+    R.half[1].hf = 1;
+    R.half[1].t0 = h0;
+    R.half[1].t1 = D.M;
+  }
+  return R;
+}
+
+// Stream the library keeps per device for the overlapped gathers of split calls.
+int aux_stream(cudaStream_t* out) {
+  static std::mutex mu;
+  static cudaStream_t st[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MEMLAYER_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!st[dev] && cudaStreamCreateWithFlags(&st[dev], cudaStreamNonBlocking) != cudaSuccess) return MEMLAYER_ERR_CUDA;
+  *out = st[dev];
+  return MEMLAYER_OK;
+}
+
+// Events of one overlapped split call (released when their work completes).
+struct SplitEvents {
+  cudaEvent_t e[4] = {};   // push A done, route done, gather A done, gather B done
+  int create() {
+    for (int i = 0; i < 4; ++i)
+      if (cudaEventCreateWithFlags(&e[i], cudaEventDisableTiming) != cudaSuccess) return MEMLAYER_ERR_CUDA;
+    return MEMLAYER_OK;
+  }
+  ~SplitEvents() {
+    for (int i = 0; i < 4; ++i)
+      if (e[i]) cudaEventDestroy(e[i]);
+  }
+};
+
+// Gather + reduce of a sharded call.  Overlapped: the gathers run on the
+// aux stream (half A after push A, half B after the whole route), the
+// reduces on `s` after their half's gather.  `reduce(half)` launches one
+// half's reduce.
+template <class Reduce>
+int shard_gather_reduce(const Dims& D, const ShardRun& R, const void* values, int* err, bool gather, bool reduce,
+                        bool overlap, SplitEvents* ev, cudaStream_t s, Reduce reduce_half) {
+  const int halves = R.split ? 2 : 1;
+  if (overlap) {
+    cudaStream_t aux = nullptr;
+    int st = aux_stream(&aux);
+    if (st) return st;
+    ML_TRY(cudaEventRecord(ev->e[1], s));                       // route (and push B) done
+    ML_TRY(cudaStreamWaitEvent(aux, ev->e[0], 0));
+    ML_TRY(launch_shard_gather(D, R.half[0], values, err, aux));
+    ML_TRY(cudaEventRecord(ev->e[2], aux));
+    ML_TRY(cudaStreamWaitEvent(aux, ev->e[1], 0));
+    ML_TRY(launch_shard_gather(D, R.half[1], values, err, aux));
+    ML_TRY(cudaEventRecord(ev->e[3], aux));
+    ML_TRY(cudaStreamWaitEvent(s, ev->e[2], 0));
+    ML_TRY(reduce_half(R.half[0]));
+    ML_TRY(cudaStreamWaitEvent(s, ev->e[3], 0));
+    ML_TRY(reduce_half(R.half[1]));
+    return MEMLAYER_OK;
+  }
+  if (gather)
+    for (int h = 0; h < halves; ++h) ML_TRY(launch_shard_gather(D, R.half[h], values, err, s));
+  if (reduce)
+    for (int h = 0; h < halves; ++h) ML_TRY(reduce_half(R.half[h]));
+  return MEMLAYER_OK;
 }
 
 // MemoryPool.__call__, single GPU (comm == nullptr) or row-sharded.
@@ -260,23 +351,29 @@ int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* wor
     ML_TRY(mark(a, 5, s));
     return MEMLAYER_OK;
   }
+  const bool split = (phases & MEMLAYER_PHASE_SPLIT) != 0;
+  const bool overlap = split && (phases & MEMLAYER_PHASE_ALL) == MEMLAYER_PHASE_ALL;
+  SplitEvents ev;
+  if (overlap && (st = ev.create())) return st;
+  if (phases & MEMLAYER_PHASE_ROUTE) ++comm->epoch;
+  ShardRun R = shard_run(comm, D, split);
+  R.after_a = overlap ? ev.e[0] : nullptr;
   if (phases & MEMLAYER_PHASE_ROUTE) {
-    ++comm->epoch;
-    const ShardK S = shard_k(comm, D);
     ML_TRY(mark(a, 0, s));
     ML_TRY(mark(a, 1, s));
     if ((st = prep_keys(D, cfg, a, W, s))) return st;
     ML_TRY(launch_normalize_queries(D, a->queries, qn, W.qlen, W.q_hi, W.q_lo, s));
     ML_TRY(mark(a, 2, s));
-    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, nullptr, nullptr, nullptr, nullptr, nullptr, s, &S)))
+    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, nullptr, nullptr, nullptr, nullptr, nullptr, s, &R)))
       return st;
   }
-  const ShardK S = shard_k(comm, D);
-  if (phases & MEMLAYER_PHASE_GATHER) ML_TRY(launch_shard_gather(D, S, a->values, W.err, s));
-  if (phases & MEMLAYER_PHASE_REDUCE) {
-    ML_TRY(launch_shard_reduce(D, S, W.own_cnt, nullptr, a->out, nullptr, nullptr, nullptr, W.err, s));
-    ML_TRY(mark(a, 5, s));
-  }
+  auto reduce_half = [&](const ShardK& K) {
+    return launch_shard_reduce(D, K, W.own_cnt, nullptr, a->out, nullptr, nullptr, nullptr, W.err, s);
+  };
+  if ((st = shard_gather_reduce(D, R, a->values, W.err, (phases & MEMLAYER_PHASE_GATHER) != 0,
+                                (phases & MEMLAYER_PHASE_REDUCE) != 0, overlap, &ev, s, reduce_half)))
+    return st;
+  if (phases & MEMLAYER_PHASE_REDUCE) ML_TRY(mark(a, 5, s));
   return MEMLAYER_OK;
 }
 
@@ -319,12 +416,17 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
   float* qn = pa->queries_unit ? pa->queries_unit : W.qn;
   const bool route = !comm || (phases & MEMLAYER_PHASE_ROUTE);
   const bool reduce = !comm || (phases & MEMLAYER_PHASE_REDUCE);
-  ShardK S{};
+  const bool split = comm && (phases & MEMLAYER_PHASE_SPLIT) != 0;
+  const bool overlap = split && (phases & MEMLAYER_PHASE_ALL) == MEMLAYER_PHASE_ALL;
+  SplitEvents ev;
+  if (overlap && (st = ev.create())) return st;
+  ShardRun R{};
   if (comm) {
     if (route) ++comm->epoch;
-    S = shard_k(comm, D);
+    R = shard_run(comm, D, split);
+    R.after_a = overlap ? ev.e[0] : nullptr;
   }
-  const ShardK* sh = comm ? &S : nullptr;
+  const ShardRun* sh = comm ? &R : nullptr;
   if (W.h_hi) {
     if (route) {
       ML_TRY(mark(pa, 0, s));
@@ -352,12 +454,15 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
       if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, nullptr, W.memg_hi, W.memg_lo, W.gate, s, sh)))
         return st;
     }
-    if (comm && (phases & MEMLAYER_PHASE_GATHER)) ML_TRY(launch_shard_gather(D, S, pa->values, W.err, s));
-    if (reduce) {
-      if (comm)
-        ML_TRY(launch_shard_reduce(D, S, W.own_cnt, W.gate, out, nullptr, W.memg_hi, W.memg_lo, W.err, s));
-      ML_TRY(launch_out_tc(D, W, a->b_out, a->y, s));                           // model.py:119
+    if (comm) {
+      auto reduce_half = [&](const ShardK& K) {
+        return launch_shard_reduce(D, K, W.own_cnt, W.gate, out, nullptr, W.memg_hi, W.memg_lo, W.err, s);
+      };
+      if ((st = shard_gather_reduce(D, R, pa->values, W.err, (phases & MEMLAYER_PHASE_GATHER) != 0, reduce, overlap,
+                                    &ev, s, reduce_half)))
+        return st;
     }
+    if (reduce) ML_TRY(launch_out_tc(D, W, a->b_out, a->y, s));                 // model.py:119
   } else {
     // SIMT float32 projections
     if (route) {
@@ -371,11 +476,15 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
       if ((st = run_route_mix(D, pa, W, qn, slots, weights, out, W.memg, nullptr, nullptr, W.gate, s, sh)))
         return st;
     }
-    if (comm && (phases & MEMLAYER_PHASE_GATHER)) ML_TRY(launch_shard_gather(D, S, pa->values, W.err, s));
-    if (reduce) {
-      if (comm) ML_TRY(launch_shard_reduce(D, S, W.own_cnt, W.gate, out, W.memg, nullptr, nullptr, W.err, s));
-      ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));  // model.py:119
+    if (comm) {
+      auto reduce_half = [&](const ShardK& K) {
+        return launch_shard_reduce(D, K, W.own_cnt, W.gate, out, W.memg, nullptr, nullptr, W.err, s);
+      };
+      if ((st = shard_gather_reduce(D, R, pa->values, W.err, (phases & MEMLAYER_PHASE_GATHER) != 0, reduce, overlap,
+                                    &ev, s, reduce_half)))
+        return st;
     }
+    if (reduce) ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));  // model.py:119
   }
   if (reduce) {
     if (a->mem && pa->out && pa->out != a->mem && D.M > 0)
@@ -642,7 +751,8 @@ int32_t memlayer_pool_forward_sharded(const memlayer_config* cfg, const memlayer
                                       memlayer_shard_comm* comm, int32_t phases, void* workspace,
                                       size_t workspace_bytes, void* stream) {
   if (!comm) return MEMLAYER_ERR_BAD_POINTER;
-  if (phases < 1 || phases > MEMLAYER_PHASE_ALL) return MEMLAYER_ERR_BAD_SHAPE;
+  if ((phases & MEMLAYER_PHASE_ALL) == 0 || (phases & ~(MEMLAYER_PHASE_ALL | MEMLAYER_PHASE_SPLIT)))
+    return MEMLAYER_ERR_BAD_SHAPE;
   return pool_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
 }
 
@@ -650,7 +760,8 @@ int32_t memlayer_layer_forward_sharded(const memlayer_config* cfg, const memlaye
                                        memlayer_shard_comm* comm, int32_t phases, void* workspace,
                                        size_t workspace_bytes, void* stream) {
   if (!comm) return MEMLAYER_ERR_BAD_POINTER;
-  if (phases < 1 || phases > MEMLAYER_PHASE_ALL) return MEMLAYER_ERR_BAD_SHAPE;
+  if ((phases & MEMLAYER_PHASE_ALL) == 0 || (phases & ~(MEMLAYER_PHASE_ALL | MEMLAYER_PHASE_SPLIT)))
+    return MEMLAYER_ERR_BAD_SHAPE;
   return layer_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
 }
 

@@ -74,17 +74,21 @@ __device__ __forceinline__ int* flag_ptr(const ShardK& S, int rank, int64_t off,
 }
 
 // Called by thread 0 of every CTA after the CTA's stores: the last CTA
-// publishes the epoch into `flag_off`[S.rank] of every rank (and, when
-// meta >= 0, the token count into meta[S.rank] first).
-__device__ void publish_when_last(const ShardK& S, int ticket_slot, int64_t flag_off, int meta) {
+// publishes the epoch into flag `flag_off`[S.hf][S.rank] of every rank (and,
+// with `meta`, this half's token range into meta[S.hf][S.rank] first).
+__device__ void publish_when_last(const ShardK& S, int ticket_slot, int64_t flag_off, bool meta) {
   fence_sys();
   int* ticket = reinterpret_cast<int*>(S.peer[S.rank] + S.off.tickets) + ticket_slot;
   if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
   *ticket = 0;   // every CTA has counted: ready for the next call
   fence_sys();
+  const int slot = S.hf * MEMLAYER_MAX_SHARDS + S.rank;
   for (int o = 0; o < S.world; ++o) {
-    if (meta >= 0) *flag_ptr(S, o, S.off.meta, S.rank) = meta;
-    st_release_sys(flag_ptr(S, o, flag_off, S.rank), S.epoch);
+    if (meta) {
+      *flag_ptr(S, o, S.off.meta, slot * 2) = (int)S.t0;
+      *flag_ptr(S, o, S.off.meta, slot * 2 + 1) = (int)S.t1;
+    }
+    st_release_sys(flag_ptr(S, o, flag_off, slot), S.epoch);
   }
 }
 
@@ -109,9 +113,9 @@ __global__ void __launch_bounds__(1024) shard_push_kernel(
   const int k = D.k, P = S.world;
   const bool lk = lane < k;
   const unsigned lt = (1u << lane) - 1u;
-  for (int64_t m0 = (int64_t)blockIdx.x * tpc; m0 < D.M; m0 += (int64_t)gridDim.x * tpc) {
+  for (int64_t m0 = S.t0 + (int64_t)blockIdx.x * tpc; m0 < S.t1; m0 += (int64_t)gridDim.x * tpc) {
     const int64_t m = m0 + t;
-    const bool active = m < D.M;
+    const bool active = m < S.t1;
     int own = -1, pos = 0, lrow = 0;
     float w = 0.f;
     __syncthreads();                                 // tab staged / previous cnt_s consumed
@@ -160,7 +164,7 @@ __global__ void __launch_bounds__(1024) shard_push_kernel(
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) publish_when_last(S, 0, S.off.flags_in, (int)D.M);
+  if (threadIdx.x == 0) publish_when_last(S, S.hf * 2, S.off.flags_in, true);
 }
 
 // ---------------------------------------------------------------------------
@@ -172,20 +176,22 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * 8 + warp;
   const int P = S.world, d = S.d;
-  if (gw < (int64_t)P * S.mcap) {
-    const int srot = (int)(gw / S.mcap);
-    const int64_t m = gw - (int64_t)srot * S.mcap;
+  if (gw < (int64_t)P * S.span) {
+    const int srot = (int)(gw / S.span);
+    const int64_t li = gw - (int64_t)srot * S.span;
     const int src = (S.rank + srot) % P;
+    const int slot = S.hf * MEMLAYER_MAX_SHARDS + src;
     const char* mine = S.peer[S.rank];
     // lane 0 acquires the source's flag; __syncwarp orders the other lanes' reads after it
     bool ready = true;
-    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + src, S.epoch, err, 31);
+    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + slot, S.epoch, err, 31);
     ready = __shfl_sync(FULL, ready, 0);
     __syncwarp();
     if (ready) {
-      const int m_src = reinterpret_cast<const volatile int*>(mine + S.off.meta)[src];
+      const volatile int* meta = reinterpret_cast<const volatile int*>(mine + S.off.meta) + slot * 2;
+      const int64_t m = meta[0] + li;            // the source's token
       const int64_t grp = (int64_t)src * S.mcap + m;
-      const int c = m < m_src ? reinterpret_cast<const volatile int*>(mine + S.off.cnt)[grp] : 0;
+      const int c = m < meta[1] ? reinterpret_cast<const volatile int*>(mine + S.off.cnt)[grp] : 0;
       if (c > 0) {
         const int2* ent = reinterpret_cast<const int2*>(mine + S.off.inbox) + grp * S.hk;
         float acc[CH][VEC];
@@ -234,7 +240,7 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) publish_when_last(S, 1, S.off.flags_part, -1);
+  if (threadIdx.x == 0) publish_when_last(S, S.hf * 2 + 1, S.off.flags_part, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -252,15 +258,16 @@ __global__ void __launch_bounds__(256) shard_reduce_kernel(const __grid_constant
   if (threadIdx.x == 0) {
     bool ok = true;
     for (int o = 0; o < P && ok; ++o)
-      ok = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_part) + o, S.epoch, err, 32);
+      ok = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_part) + S.hf * MEMLAYER_MAX_SHARDS + o,
+                      S.epoch, err, 32);
     ok_s = ok;
   }
   __syncthreads();
   const bool ok = ok_s;
   const int per = blockDim.x / d4;
   const int t = threadIdx.x / d4, i = threadIdx.x - t * d4;
-  const int64_t m = (int64_t)blockIdx.x * per + t;
-  if (!ok || t >= per || m >= M) return;
+  const int64_t m = S.t0 + (int64_t)blockIdx.x * per + t;
+  if (!ok || t >= per || m >= S.t1) return;
   const float4* part = reinterpret_cast<const float4*>(mine + S.off.part);
   // all counts, then all partial loads in flight at once
   int cnt[MEMLAYER_MAX_SHARDS];
@@ -301,7 +308,7 @@ inline int ch_for(int groups) {
 
 template <typename VT, int VEC>
 cudaError_t gather_ch(const ShardK& S, const VT* values, int* err, cudaStream_t s) {
-  const int64_t warps = (int64_t)S.world * S.mcap;
+  const int64_t warps = (int64_t)S.world * S.span;
   const unsigned grid = (unsigned)((warps + 7) / 8);
   switch (ch_for(S.d / VEC)) {
     case 1: shard_gather_kernel<VT, VEC, 1><<<grid, 256, 0, s>>>(S, values, err); break;
@@ -338,7 +345,7 @@ cudaError_t launch_shard_push(const Dims& D, const Work& W, const ShardK& S, int
   const int tpc = D.H >= 16 ? 1 : 16 / D.H;
   const dim3 block(32 * D.H * tpc);
   const int per_sm = 2048 / (int)block.x;
-  const int64_t groups = (D.M + tpc - 1) / tpc;
+  const int64_t groups = (S.t1 - S.t0 + tpc - 1) / tpc;
   const unsigned grid = (unsigned)(groups < 1 ? 1 : groups < 148LL * per_sm ? groups : 148LL * per_sm);
 #define ML_SP(KV)                                                                                               \
   shard_push_kernel<KV><<<grid, block, 0, s>>>(D, tpc, pairs, S, W.sub_idx, W.sub_score, W.sub_sel, slots, weights, \
@@ -365,7 +372,8 @@ cudaError_t launch_shard_reduce(const Dims& D, const ShardK& S, const int* own_c
                                 float* memg, float* memg_hi, float* memg_lo, int* err, cudaStream_t s) {
   const int d4 = S.d / 4;
   const int per = 256 / d4;
-  const unsigned grid = (unsigned)(D.M > 0 ? (D.M + per - 1) / per : 1);
+  const int64_t n = S.t1 - S.t0;
+  const unsigned grid = (unsigned)(n > 0 ? (n + per - 1) / per : 1);
   shard_reduce_kernel<<<grid, 256, 0, s>>>(S, D.M, own_cnt, gate, out, memg, memg_hi, memg_lo, err);
   count_launch();
   return cudaGetLastError();

@@ -9,10 +9,10 @@ namespace ml {
 // Byte offsets inside a communicator buffer.  Every rank's buffer has the
 // same layout, so a rank addresses a peer's region with the peer's base.
 struct ShardOff {
-  int64_t flags_in;    // [MAX] int: epoch of the inbox each source rank has filled
-  int64_t flags_part;  // [MAX] int: epoch of the partials each owner rank has stored
-  int64_t meta;        // [MAX] int: token count of each source rank's call
-  int64_t tickets;     // [4] int: CTA completion counters (local use)
+  int64_t flags_in;    // [2 halves][MAX] int: epoch of the inbox each source rank has filled
+  int64_t flags_part;  // [2][MAX] int: epoch of the partials each owner rank has stored
+  int64_t meta;        // [2][MAX][2] int: token range [lo, hi) of each source rank's half
+  int64_t tickets;     // [2][2] int: CTA completion counters of push / gather (local use)
   int64_t cnt;         // [world][mcap] int: entries from source rank per token
   int64_t inbox;       // [world][mcap][hk] int2: (local row, weight bits) per entry
   int64_t part;        // [world][mcap][d] float: partial sum of owner rank per token
@@ -29,6 +29,10 @@ struct ShardK {
   int d;           // d_value
   int64_t rows;    // value rows held by this rank
   int epoch;       // current call
+  // token half of this launch: flags / tickets / meta slots `hf`, this rank's
+  // tokens [t0, t1), gather grid over `span` tokens per source rank
+  int hf;
+  int64_t t0, t1, span;
 };
 
 ShardOff shard_layout(int world, int64_t mcap, int hk, int d);

@@ -196,9 +196,11 @@ class ShardedMemoryLayer:
     def pool(self) -> MemoryPool:
         return self.layer.pool
 
-    def apply(self, params, h: torch.Tensor, *, check: bool = False, stream=None, **kw):
+    def apply(self, params, h: torch.Tensor, *, check: bool = False, stream=None, split: bool = True, **kw):
+        """``split``: exchange in two token halves, the second half's push
+        overlapping the first half's gather (MEMLAYER_PHASE_SPLIT)."""
         call = ShardedCall(self.layer, self.comm, params, h, **kw)
-        call.run(L.PHASE_ALL, stream)
+        call.run(L.PHASE_ALL | (L.PHASE_SPLIT if split else 0), stream)
         if check:
             call.check(stream)
         return call.result()

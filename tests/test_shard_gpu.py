@@ -22,7 +22,7 @@ def _layer(n=64, H=4, dk=64, d=64, k=16, dm=64, seed=0, vdt=torch.float32, **kw)
     return layer, layer.init(seed, values_dtype=vdt)
 
 
-def _run(layer, params, hs, world, repeats=2, **kw):
+def _run(layer, params, hs, world, repeats=2, split=False, **kw):
     from model_b200 import _lib as L
     from model_b200.shard import ShardedCall, emulated_comms, shard_values
     cap = max(1, max(h.shape[0] for h in hs))
@@ -36,7 +36,7 @@ def _run(layer, params, hs, world, repeats=2, **kw):
     for _ in range(repeats):           # later calls reuse the buffers with a new epoch
         for ph in (L.PHASE_ROUTE, L.PHASE_GATHER, L.PHASE_REDUCE):
             for c in calls:
-                c.run(ph)
+                c.run(ph | (L.PHASE_SPLIT if split else 0))
     torch.cuda.synchronize()
     for c in calls:
         c.check()
@@ -109,3 +109,12 @@ def test_sharded_cfg0_shapes_against_oracle():
                   float(params["pool"]["log_temperature"]))
     check_slots(got[0][2]["slots"][:64].cpu().numpy(), aux["slots"], r["scores"], P.n_sub_keys)
     assert_rel(got[0][1][:64].cpu().numpy(), out, OUT_RTOL_F32, "mem vs oracle")
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_sharded_split_halves(world):
+    """MEMLAYER_PHASE_SPLIT: the exchange in two token halves (phase by
+    phase here: both halves' pushes, both gathers, both reduces)."""
+    layer, params = _layer()
+    hs = [_hidden(m, 64, 110 + r) for r, m in enumerate([301, 0, 1, 129, 300, 7, 64, 2][:world])]
+    _compare(layer, params, hs, _run(layer, params, hs, world, split=True))

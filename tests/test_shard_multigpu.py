@@ -42,8 +42,8 @@ def _worker(rank, world, port, outdir, vdt_name):
         comm = connect(pool.config(M, vdt, 128))
         local = dict(params, pool=dict(params["pool"], values=shard_values(params["pool"]["values"], rank, world)))
         sharded = ShardedMemoryLayer(layer, comm)
-        for _ in range(3):
-            y, mem, aux = sharded.apply(local, h, check=True)
+        for i in range(4):   # plain and split (overlapped halves) calls, alternating
+            y, mem, aux = sharded.apply(local, h, check=True, split=bool(i % 2))
         torch.cuda.synchronize()
         dist.barrier()
         y0, mem0, aux0 = layer.apply(params, h, check=True)
