@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--host-chunks", type=int, default=4,
                     help="chunks of the host-buffer pipeline timed as e2e (memlayer_layer_forward_host)")
-    ap.add_argument("--workload", choices=["cfg0", "cfg2", "cfg3", "cfg4"], default="cfg0",
+    ap.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg0",
                     help="cfg0 (default, the driver's line): configs[0] layer forward; cfg2: configs[2] decode "
                          "latency on a 67M-slot fp16 table; cfg3: configs[3] billion-slot bf16 table "
                          "row-sharded over >= 4 GPUs; cfg4: configs[4] forward + fetched-row Adagrad")
@@ -559,6 +559,53 @@ def _common_line(W, world, steps, warmup, ms, value, unit, dtype, extra):
     return line
 
 
+def run_cfg1(args):
+    """configs[1]'s memory layers: batch 32 x seq 256 = 8192 tokens, d_model
+    256, memory layers 1 and 3 sharing one pool of 262,144 x 256 fp16 rows,
+    H 4, top_k 16, d_key 128 (the reference run's setting).  A step is the two
+    memory-layer calls of one model forward (each with its own router / gate
+    / output kernels and hidden state); the backbone is not part of this
+    library."""
+    import torch
+
+    from model_b200 import _lib as L
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    W = dict(WORKLOAD, name="cfg1_model_memory_layers", d_key=128, values_dtype="f16")
+    xs = [make_inputs(torch, device, W, "f16", W["seed"] + i) for i in range(2)]
+    xs[1]["values"] = xs[0]["values"]                 # one shared pool
+    xs[1]["sub_keys"] = xs[0]["sub_keys"]
+    calls = [LayerCall(torch, L, W, x, device, "f16") for x in xs]
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    for _ in range(args.warmup):
+        flush.zero_()
+        for c in calls:
+            c(stream)
+    torch.cuda.synchronize()
+    K = args.steps
+    e = [_events(torch, 3) for _ in range(K)]
+    for i in range(K):
+        flush.zero_()
+        e[i][0].record(stream)
+        calls[0](stream)
+        e[i][1].record(stream)
+        calls[1](stream)
+        e[i][2].record(stream)
+    torch.cuda.synchronize()
+    l1 = statistics.mean(x[0].elapsed_time(x[1]) for x in e)
+    l3 = statistics.mean(x[1].elapsed_time(x[2]) for x in e)
+    ms = l1 + l3
+    T = W["tokens_per_gpu"]
+    hbm, src = peaks()
+    rows = 2 * T * W["heads"] * W["top_k"] * W["d_value"] * 2   # fp16 rows of both layers
+    return _common_line(W, 1, K, args.warmup, ms, T / (ms * 1e-3), "tokens/s", "f16", {
+        "scaling": "weak", "stages_ms": {"memory_layer_1": l1, "memory_layer_3": l3},
+        "gather_row_gbs": rows / (ms * 1e-3) / 1e9, "hbm_peak": hbm, "peak_source": src,
+        "note": "the two memory-layer calls of one model forward; the attention / FFN backbone of configs[1] is "
+                "outside this library.  L2 flushed before every step"})
+
+
 def run_cfg4(args):
     """configs[4]: configs[0] shapes, f32 values, 8192 Zipf-clustered tokens;
     step = layer forward with routing statistics + fetched-row gradients of a
@@ -797,6 +844,8 @@ def main():
         line = run_emulated(args)
     elif args.workload == "cfg4":
         line = run_cfg4(args)
+    elif args.workload == "cfg1":
+        line = run_cfg1(args)
     elif args.workload == "cfg2":
         line = run_cfg2(args)
     elif args.workload == "cfg3":
