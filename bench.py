@@ -390,6 +390,27 @@ def run_ours(args, W, rank, world):
     stage = lambda a, b: statistics.mean(ev[i][a].elapsed_time(ev[i][b]) for i in range(K))  # noqa: E731
     stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
               "combine_gather": stage(3, 4), "finalize_out": stage(4, 5)}
+    if not sharded:
+        # the library overlaps the second token half's score with the first
+        # half's gather inside each call; the kernels' own times for the
+        # roofline come from a pass with that overlap off (MEMLAYER_OVERLAP=0)
+        G = min(K, 20)
+        gev = [[torch.cuda.Event(enable_timing=True) for _ in range(L.STAGE_EVENTS)] for _ in range(G)]
+        for row in gev:
+            for e in row:
+                e.record(stream)
+        torch.cuda.synchronize()
+        os.environ["MEMLAYER_OVERLAP"] = "0"
+        for i in range(G):
+            flush.zero_()
+            call(stream, gev[i])
+        torch.cuda.synchronize()
+        del os.environ["MEMLAYER_OVERLAP"]
+        gst = lambda a, b: statistics.mean(gev[i][a].elapsed_time(gev[i][b]) for i in range(G))  # noqa: E731
+        stages = {"projections": stage(0, 1), "prep": stage(1, 2),
+                  "score_and_first_half_gather": stage(2, 3), "second_half_gather": stage(3, 4),
+                  "finalize_out": stage(4, 5),
+                  "score_topk": gst(2, 3), "combine_gather": gst(3, 4), "unoverlapped_step": gst(0, 5)}
     if sharded and not overlapped:
         pstage = lambda f: statistics.mean(f(i) for i in range(K))  # noqa: E731
         stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),

@@ -1,6 +1,7 @@
 // C ABI of the memory layer (include/memlayer.h): argument validation,
 // workspace layout and the launch sequence of one forward call.
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -159,6 +160,20 @@ cudaError_t mark(const memlayer_pool_args* a, int i, cudaStream_t s) {
 
 // Routing from prepared unit queries onward: score + per-half top-k,
 // balance statistics, k*k combine + softmax + gather (+ gate), aux finalise.
+int aux_stream(cudaStream_t* out);
+
+// Intra-call overlap of the single-GPU forward (score of the second token
+// half beside the gather of the first); MEMLAYER_OVERLAP=0 in the
+// environment turns it off (stage timing of the bench's roofline pass).
+bool overlap_enabled() {
+  const char* v = getenv("MEMLAYER_OVERLAP");
+  return !(v && v[0] == '0');
+}
+
+// score CTAs beside the first half's gather (of 148 SMs); 100 / 120 / 132 /
+// 140 measured 0.290 / 0.291 / 0.292 / 0.294 ms per configs[0] step
+constexpr int OVERLAP_SCORE_CTAS = 100;
+
 // The push of a row-sharded call: one launch per token half; after_a (if
 // set) is recorded between the halves.
 struct ShardRun {
@@ -175,6 +190,43 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
   Work w2 = W;
   w2.qn = qn;
   const bool bal = a->balance_loss != nullptr;
+  const int mt_all = (int)((D.M + SCORE_TM - 1) / SCORE_TM);
+  if (!sh && W.q_hi && !bal && mt_all >= 16 && overlap_enabled()) {
+    // two token halves: the second half's score kernel (on fewer SMs) runs
+    // beside the first half's gather (HBM-bound) on a second stream
+    cudaStream_t aux = nullptr;
+    int st = aux_stream(&aux);
+    if (st) return st;
+    cudaEvent_t ev[2] = {};
+    for (int i = 0; i < 2; ++i)
+      if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess) {
+        if (ev[0]) cudaEventDestroy(ev[0]);
+        return MEMLAYER_ERR_CUDA;
+      }
+    auto body = [&]() -> int {
+      const int mta = mt_all / 2;
+      const int64_t ha = (int64_t)mta * SCORE_TM;
+      if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
+      if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
+      ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, false, s, 0, mta, 0));
+      ML_TRY(cudaEventRecord(ev[0], s));
+      ML_TRY(cudaStreamWaitEvent(aux, ev[0], 0));
+      ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, memg_hi, memg_lo, gate,
+                                   a->slot_counts, a->subkey_counts, aux, 0, ha));
+      ML_TRY(cudaEventRecord(ev[1], aux));
+      ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, false, s, mta, mt_all - mta, OVERLAP_SCORE_CTAS));
+      ML_TRY(mark(a, 3, s));
+      ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, memg_hi, memg_lo, gate,
+                                   a->slot_counts, a->subkey_counts, s, ha, D.M - ha));
+      ML_TRY(cudaStreamWaitEvent(s, ev[1], 0));
+      ML_TRY(mark(a, 4, s));
+      ML_TRY(launch_finalize(D, w2, a->top1_weight, a->temperature, s));
+      return MEMLAYER_OK;
+    };
+    st = body();
+    for (int i = 0; i < 2; ++i) cudaEventDestroy(ev[i]);   // released once their work completes
+    return st;
+  }
   if (W.q_hi)   // the tensor-core balance pass computes its own row max / sum: the score kernel
                 // needs its statistics variant only for the clean top-k of noisy calls
     ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, bal && D.noisy, s));
@@ -262,15 +314,22 @@ ShardRun shard_run(const memlayer_shard_comm* comm, const Dims& D, bool split) {
   return R;
 }
 
-// Stream the library keeps per device for the overlapped gathers of split calls.
+// Streams the library keeps per device for work it overlaps with the
+// caller's stream (the gathers of split sharded calls, the first token half's
+// gather of a single-GPU call); handed out round robin so that calls running
+// on different caller streams do not queue behind each other.
 int aux_stream(cudaStream_t* out) {
+  constexpr int POOL = 4;
   static std::mutex mu;
-  static cudaStream_t st[64] = {};
+  static cudaStream_t st[64][POOL] = {};
+  static unsigned next[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MEMLAYER_ERR_CUDA;
   std::lock_guard<std::mutex> lock(mu);
-  if (!st[dev] && cudaStreamCreateWithFlags(&st[dev], cudaStreamNonBlocking) != cudaSuccess) return MEMLAYER_ERR_CUDA;
-  *out = st[dev];
+  const unsigned i = next[dev]++ % POOL;
+  if (!st[dev][i] && cudaStreamCreateWithFlags(&st[dev][i], cudaStreamNonBlocking) != cudaSuccess)
+    return MEMLAYER_ERR_CUDA;
+  *out = st[dev][i];
   return MEMLAYER_OK;
 }
 

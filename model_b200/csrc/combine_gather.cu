@@ -24,14 +24,14 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
     const VT* __restrict__ values, int* __restrict__ slots, float* __restrict__ weights, float* __restrict__ out,
     float* __restrict__ memg, float* __restrict__ memg_hi, float* __restrict__ memg_lo,
     const float* __restrict__ gate, float* __restrict__ slot_counts, float* __restrict__ subkey_counts,
-    float* __restrict__ top1_part, int* __restrict__ err) {
+    float* __restrict__ top1_part, int* __restrict__ err, int64_t m0) {
   extern __shared__ float red[];  // [H][d]
   __shared__ uint16_t tab[128];   // pair table, staged for divergent per-lane reads
   __shared__ uint16_t lbtab[32];
   for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
   for (int i = threadIdx.x; i < 32; i += blockDim.x) lbtab[i] = pairs.lb[i];
   __syncthreads();
-  const int64_t m = blockIdx.x;
+  const int64_t m = m0 + blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k = D.k, d = D.d;
   const int64_t ra = ((m * D.H + h) * 2) * k;
@@ -104,13 +104,13 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
 template <int KM, typename VT, int VEC>
 cudaError_t launch_ch(const Dims& D, int ch, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Work& W,
                       const VT* values, int* slots, float* weights, float* out, float* memg, float* mhi, float* mlo,
-                      const float* gate, float* slot_counts, float* subkey_counts) {
+                      const float* gate, float* slot_counts, float* subkey_counts, int64_t m0) {
   const PairTable pairs = make_pairs(D.k);
 #define ML_CG(CHV)                                                                                             \
   combine_gather_kernel<KM, VT, VEC, CHV><<<grid, block, smem, s>>>(D, pairs, W.sub_idx, W.sub_score, W.sub_sel, \
                                                                     values, slots, weights, out, memg, mhi, \
                                                                     mlo, gate, slot_counts, subkey_counts,  \
-                                                                    W.top1_part, W.err)
+                                                                    W.top1_part, W.err, m0)
   switch (ch) {
     case 1: ML_CG(1); break;
     case 2: ML_CG(2); break;
@@ -131,32 +131,35 @@ inline int ch_for(int groups) {
 template <int KM>
 cudaError_t launch_k(const Dims& D, const Work& W, const void* values, int* slots, float* weights, float* out,
                      float* memg, float* mhi, float* mlo, const float* gate, float* slot_counts,
-                     float* subkey_counts, cudaStream_t s) {
-  dim3 grid((unsigned)D.M), block(32 * D.H);
+                     float* subkey_counts, cudaStream_t s, int64_t m0, int64_t count) {
+  dim3 grid((unsigned)count), block(32 * D.H);
   size_t smem = sizeof(float) * D.H * D.d;
   const bool aligned = (reinterpret_cast<uintptr_t>(values) & 15) == 0;
   if (D.vdtype == MEMLAYER_F16)
     return launch_ch<KM, __half, 8>(D, ch_for(D.d / 8), grid, block, smem, s, W, (const __half*)values, slots,
-                                    weights, out, memg, mhi, mlo, gate, slot_counts, subkey_counts);
+                                    weights, out, memg, mhi, mlo, gate, slot_counts, subkey_counts, m0);
   if (D.vdtype == MEMLAYER_BF16)
     return launch_ch<KM, __nv_bfloat16, 8>(D, ch_for(D.d / 8), grid, block, smem, s, W,
                                            (const __nv_bfloat16*)values, slots, weights, out, memg, mhi, mlo,
-                                           gate, slot_counts, subkey_counts);
+                                           gate, slot_counts, subkey_counts, m0);
   if (D.d % 4 == 0 && aligned)
     return launch_ch<KM, float, 4>(D, ch_for(D.d / 4), grid, block, smem, s, W, (const float*)values, slots,
-                                   weights, out, memg, mhi, mlo, gate, slot_counts, subkey_counts);
+                                   weights, out, memg, mhi, mlo, gate, slot_counts, subkey_counts, m0);
   return launch_ch<KM, float, 1>(D, ch_for(D.d), grid, block, smem, s, W, (const float*)values, slots, weights,
-                                 out, memg, mhi, mlo, gate, slot_counts, subkey_counts);
+                                 out, memg, mhi, mlo, gate, slot_counts, subkey_counts, m0);
 }
 
 }  // namespace
 
 cudaError_t launch_combine_gather(const Dims& D, const Work& W, const void* values, int* slots, float* weights,
                                   float* out, float* mem_gated, float* memg_hi, float* memg_lo, const float* gate,
-                                  float* slot_counts, float* subkey_counts, cudaStream_t s) {
-  if (D.M == 0) return cudaSuccess;
-#define ML_K(KV) \
-  launch_k<KV>(D, W, values, slots, weights, out, mem_gated, memg_hi, memg_lo, gate, slot_counts, subkey_counts, s)
+                                  float* slot_counts, float* subkey_counts, cudaStream_t s, int64_t m0,
+                                  int64_t count) {
+  if (count <= 0) count = D.M - m0;
+  if (count <= 0) return cudaSuccess;
+#define ML_K(KV)                                                                                              \
+  launch_k<KV>(D, W, values, slots, weights, out, mem_gated, memg_hi, memg_lo, gate, slot_counts, subkey_counts, s, \
+               m0, count)
   switch (D.kmax) {
     case 4: return ML_K(4);
     case 8: return ML_K(8);

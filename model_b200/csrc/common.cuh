@@ -195,8 +195,10 @@ cudaError_t launch_prep_keys(const Dims& D, const float* sub_keys, const float* 
 cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, float* qlen, float* q_hi,
                                      float* q_lo, cudaStream_t s);
 bool score_tc_supported(const Dims& D);
+// mtn > 0: only the 128-token tiles [mt0, mt0 + mtn); max_ctas > 0 caps the
+// persistent grid (leaving SMs to a kernel running beside it)
 cudaError_t launch_score_topk_tc(const Dims& D, const Work& W, const float* gumbel, bool want_balance,
-                                 cudaStream_t s);
+                                 cudaStream_t s, int mt0 = 0, int mtn = 0, int max_ctas = 0);
 cudaError_t launch_score_topk(const Dims& D, const Work& W, const float* gumbel, bool want_balance,
                               cudaStream_t s);
 bool score_small_supported(const Dims& D);
@@ -204,9 +206,11 @@ size_t score_small_scratch_bytes(const Dims& D);
 cudaError_t launch_score_small(const Dims& D, const Work& W, const float* gumbel, float* scratch, cudaStream_t s);
 cudaError_t launch_balance(const Dims& D, const Work& W, float* balance_loss, cudaStream_t s);
 cudaError_t launch_balance_tc(const Dims& D, const Work& W, int* planes, cudaStream_t s);
+// count > 0: only tokens [m0, m0 + count)
 cudaError_t launch_combine_gather(const Dims& D, const Work& W, const void* values, int* slots, float* weights,
                                   float* out, float* mem_gated, float* memg_hi, float* memg_lo, const float* gate,
-                                  float* slot_counts, float* subkey_counts, cudaStream_t s);
+                                  float* slot_counts, float* subkey_counts, cudaStream_t s, int64_t m0 = 0,
+                                  int64_t count = 0);
 bool proj_tc_supported(const Dims& D);
 cudaError_t launch_split(const float* x, int64_t n, float* hi, float* lo, cudaStream_t s);
 cudaError_t launch_transpose_split(const float* W, int K, int N, float* hi, float* lo, int row0, cudaStream_t s);

@@ -44,7 +44,8 @@ constexpr int ACC_STRIDE = tc::PIPE_ACC_STRIDE;
 
 struct TcShape {
   tc::PipeShape P;
-  int m_tiles;
+  int m_tiles;     // 128-token tiles of this launch
+  int mt0;         // first tile of this launch
   int n_chunks;
   uint32_t merge_off;
 };
@@ -368,7 +369,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // unit u = (codebook hc, 128-token tile mt): A rows of q in [hc][M][half],
   // B rows of the codebook's keys in [hc][n][half]
   auto coords = [&](int u, int& arow, int& brow0, int& nch) {
-    const int hc = u / S.m_tiles, mt = u - hc * S.m_tiles;
+    const int hc = u / S.m_tiles, mt = S.mt0 + u - hc * S.m_tiles;
     arow = (int)(hc * D.M + (int64_t)mt * TC_M);
     brow0 = hc * D.n;
     nch = S.n_chunks;
@@ -402,7 +403,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint32_t aph = 0, pph = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-      const int hc = u / S.m_tiles, mt = u - hc * S.m_tiles;
+      const int hc = u / S.m_tiles, mt = S.mt0 + u - hc * S.m_tiles;
       const int h = hc >> 1, c = hc & 1;
       const int64_t m = (int64_t)mt * TC_M + r_in_tile;
       const bool owner = m < D.M;
@@ -696,14 +697,20 @@ TcShape tc_shape(const Dims& D) {
   TcShape S;
   S.P = tc::pipe_shape(bn_for(D), D.half, merge_bytes(D));
   S.m_tiles = (int)((D.M + TC_M - 1) / TC_M);
+  S.mt0 = 0;
   S.n_chunks = (D.n + S.P.BN - 1) / S.P.BN;
   S.merge_off = 1024 + S.P.stages * S.P.stage_bytes;
   return S;
 }
 
 template <int KM, bool NOISY, bool BAL, bool QS>
-cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaStream_t s) {
+cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaStream_t s, int mt0, int mtn,
+                        int max_ctas) {
   TcShape S = tc_shape(D);
+  if (mtn > 0) {   // a range of 128-token tiles
+    S.mt0 = mt0;
+    S.m_tiles = mtn;
+  }
   if (S.P.stages < 2) return cudaErrorInvalidConfiguration;
   CUtensorMap m[4];
   cudaError_t e;
@@ -719,6 +726,7 @@ cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaS
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (max_ctas > 0 && max_ctas < sms) sms = max_ctas;
   const int units = S.m_tiles * D.H * 2;
   const int grid = units < sms ? units : sms;
   kern<<<grid, TC_THREADS, smem, s>>>(m[0], m[1], m[2], m[3], D, S, W.qlen, gumbel, W.scal, W.sub_idx, W.sub_score,
@@ -728,15 +736,20 @@ cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaS
 }
 
 template <int KM, bool QS>
-cudaError_t launch_tc_q(const Dims& D, const Work& W, const float* gumbel, bool bal, cudaStream_t s) {
+cudaError_t launch_tc_q(const Dims& D, const Work& W, const float* gumbel, bool bal, cudaStream_t s, int mt0,
+                        int mtn, int mc) {
   if (D.noisy)
-    return bal ? launch_tc_t<KM, true, true, QS>(D, W, gumbel, s) : launch_tc_t<KM, true, false, QS>(D, W, gumbel, s);
-  return bal ? launch_tc_t<KM, false, true, QS>(D, W, gumbel, s) : launch_tc_t<KM, false, false, QS>(D, W, gumbel, s);
+    return bal ? launch_tc_t<KM, true, true, QS>(D, W, gumbel, s, mt0, mtn, mc)
+               : launch_tc_t<KM, true, false, QS>(D, W, gumbel, s, mt0, mtn, mc);
+  return bal ? launch_tc_t<KM, false, true, QS>(D, W, gumbel, s, mt0, mtn, mc)
+             : launch_tc_t<KM, false, false, QS>(D, W, gumbel, s, mt0, mtn, mc);
 }
 
 template <int KM>
-cudaError_t launch_tc_k(const Dims& D, const Work& W, const float* gumbel, bool bal, cudaStream_t s) {
-  return D.qscale ? launch_tc_q<KM, true>(D, W, gumbel, bal, s) : launch_tc_q<KM, false>(D, W, gumbel, bal, s);
+cudaError_t launch_tc_k(const Dims& D, const Work& W, const float* gumbel, bool bal, cudaStream_t s, int mt0,
+                        int mtn, int mc) {
+  return D.qscale ? launch_tc_q<KM, true>(D, W, gumbel, bal, s, mt0, mtn, mc)
+                  : launch_tc_q<KM, false>(D, W, gumbel, bal, s, mt0, mtn, mc);
 }
 
 }  // namespace
@@ -765,12 +778,12 @@ bool score_tc_supported(const Dims& D) {
 }
 
 cudaError_t launch_score_topk_tc(const Dims& D, const Work& W, const float* gumbel, bool want_balance,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, int mt0, int mtn, int max_ctas) {
   switch (D.kmax) {
-    case 4: return launch_tc_k<4>(D, W, gumbel, want_balance, s);
-    case 8: return launch_tc_k<8>(D, W, gumbel, want_balance, s);
-    case 16: return launch_tc_k<16>(D, W, gumbel, want_balance, s);
-    case 32: return launch_tc_k<32>(D, W, gumbel, want_balance, s);
+    case 4: return launch_tc_k<4>(D, W, gumbel, want_balance, s, mt0, mtn, max_ctas);
+    case 8: return launch_tc_k<8>(D, W, gumbel, want_balance, s, mt0, mtn, max_ctas);
+    case 16: return launch_tc_k<16>(D, W, gumbel, want_balance, s, mt0, mtn, max_ctas);
+    case 32: return launch_tc_k<32>(D, W, gumbel, want_balance, s, mt0, mtn, max_ctas);
     default: return cudaErrorInvalidValue;
   }
 }
