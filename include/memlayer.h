@@ -19,6 +19,9 @@
  *     aligned.  The workspace's contents need not be initialised.
  *   - Calls are stream-ordered on the given cudaStream_t (passed as void*),
  *     return as soon as the work is enqueued and never synchronise the device.
+ *     A large call may run part of its work on a stream the library keeps per
+ *     device (ordered by events); the given stream waits for that work before
+ *     the call's last launch, so ordering on the given stream is unchanged.
  *   - No C++ exception crosses this boundary; errors are memlayer_status codes.
  *     Argument errors are detected on the host before anything is enqueued.
  *   - Thread safety: calls on different streams may run concurrently from

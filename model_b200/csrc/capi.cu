@@ -186,12 +186,12 @@ struct ShardRun {
 // instead of gathering; out / memg / gate are then unused.
 int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, float* qn, int* slots,
                   float* weights, float* out, float* memg, float* memg_hi, float* memg_lo, const float* gate,
-                  cudaStream_t s, const ShardRun* sh = nullptr) {
+                  cudaStream_t s, const ShardRun* sh = nullptr, bool allow_overlap = true) {
   Work w2 = W;
   w2.qn = qn;
   const bool bal = a->balance_loss != nullptr;
   const int mt_all = (int)((D.M + SCORE_TM - 1) / SCORE_TM);
-  if (!sh && W.q_hi && !bal && mt_all >= 16 && overlap_enabled()) {
+  if (allow_overlap && !sh && W.q_hi && !bal && mt_all >= 16 && overlap_enabled()) {
     // two token halves: the second half's score kernel (on fewer SMs) runs
     // beside the first half's gather (HBM-bound) on a second stream
     cudaStream_t aux = nullptr;
@@ -381,7 +381,7 @@ int shard_gather_reduce(const Dims& D, const ShardRun& R, const void* values, in
 
 // MemoryPool.__call__, single GPU (comm == nullptr) or row-sharded.
 int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* workspace, size_t workspace_bytes,
-              cudaStream_t s, memlayer_shard_comm* comm, int phases) {
+              cudaStream_t s, memlayer_shard_comm* comm, int phases, bool allow_overlap = true) {
   Dims D;
   int st = check_config(cfg, &D, false);
   if (st) return st;
@@ -405,7 +405,8 @@ int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* wor
     if ((st = prep_keys(D, cfg, a, W, s))) return st;
     ML_TRY(launch_normalize_queries(D, a->queries, qn, W.qlen, W.q_hi, W.q_lo, s));
     ML_TRY(mark(a, 2, s));
-    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, a->out, nullptr, nullptr, nullptr, nullptr, s)))
+    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, a->out, nullptr, nullptr, nullptr, nullptr, s,
+                            nullptr, allow_overlap)))
       return st;
     ML_TRY(mark(a, 5, s));
     return MEMLAYER_OK;
@@ -626,6 +627,14 @@ int rowgrad_setup(const memlayer_config* cfg, const memlayer_read* reads, int n_
 }
 
 }  // namespace
+
+// MemoryPool forward on the caller's stream only: no event, no library
+// stream (the allocation-free entry point).
+int32_t pool_forward_single_stream(const memlayer_config* cfg, const memlayer_pool_args* args, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  return pool_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, MEMLAYER_PHASE_ALL, false);
+}
+
 }  // namespace ml
 
 using namespace ml;

@@ -185,6 +185,11 @@ struct VecLoad<__nv_bfloat16> {
   __device__ __forceinline__ static float scalar(const __nv_bfloat16* p) { return __bfloat162float(p[0]); }
 };
 
+// memlayer_pool_forward without the intra-call overlap: every launch on
+// `stream`, no event or library stream is created.
+int32_t pool_forward_single_stream(const memlayer_config* cfg, const memlayer_pool_args* args, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 // Counts every kernel launch made by this library (memlayer_kernel_launch_count).
 void count_launch(int n = 1);
 

@@ -4,7 +4,9 @@
 // buffer for this call: a runtime whose custom-call operands are fixed when
 // the program is compiled, or a serving loop that must not enter the CUDA
 // allocator on its per-token path.  This entry point runs the same kernels
-// as memlayer_pool_forward, with the workspace carved from a fixed array in
+// as memlayer_pool_forward, all on the caller's stream (without the
+// library-stream overlap memlayer_pool_forward uses for large calls), with
+// the workspace carved from a fixed array in
 // the library's own device memory (MEMLAYER_NOALLOC_SCRATCH_BYTES; every GPU
 // that loads the library holds it until the process exits).
 //
@@ -53,5 +55,6 @@ extern "C" int32_t memlayer_pool_forward_noalloc(const memlayer_config* cfg, con
   void* ws = nullptr;
   st = ml::scratch_for_current_device(&ws);
   if (st != MEMLAYER_OK) return st;
-  return memlayer_pool_forward(cfg, args, ws, (size_t)MEMLAYER_NOALLOC_SCRATCH_BYTES, stream);
+  // every launch on the caller's stream: no event or stream is created either
+  return ml::pool_forward_single_stream(cfg, args, ws, (size_t)MEMLAYER_NOALLOC_SCRATCH_BYTES, stream);
 }
