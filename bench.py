@@ -637,7 +637,8 @@ def run_cfg4(args):
     """configs[4]: configs[0] shapes, f32 values, 8192 Zipf-clustered tokens;
     step = layer forward with routing statistics + fetched-row gradients of a
     synthetic probe gradient + global-norm clip + row-wise Adagrad on the
-    touched rows.  The backward through the router is not built, so the probe
+    touched rows + key_diversity_loss with its gradient.  revive_dead_keys
+    (every revive_every steps in the reference) is timed once beside it.  The backward through the router is not built, so the probe
     gradient is drawn, not computed."""
     import torch
 
@@ -674,13 +675,25 @@ def run_cfg4(args):
     def update():
         L.check(lib.memlayer_row_adagrad(C.byref(call.cfg), reads, 1, C.byref(ada), rws.data_ptr(), rb.value,
                                          stream.cuda_stream), "memlayer_row_adagrad")
+    # key_diversity_loss and its gradient, scaled by key_diversity_coef (train.py:327-329)
+    kd_loss = torch.empty(1, device=device)
+    kd_grad = torch.empty_like(x["sub_keys"])
+    kb = C.c_size_t()
+    L.check(lib.memlayer_key_diversity_workspace_size(C.byref(call.cfg), C.byref(kb)), "key diversity ws")
+    kws = torch.empty(max(kb.value, 256), dtype=torch.uint8, device=device)
+
+    def diversity():
+        L.check(lib.memlayer_key_diversity(C.byref(call.cfg), x["sub_keys"].data_ptr(), kd_loss.data_ptr(),
+                                           kd_grad.data_ptr(), 0.01, kws.data_ptr(), kb.value, stream.cuda_stream),
+                "memlayer_key_diversity")
     for _ in range(args.warmup):
         flush.zero_()
         call(stream)
         update()
+        diversity()
     torch.cuda.synchronize()
     K = args.steps
-    e0, e1, e2 = _events(torch, K), _events(torch, K), _events(torch, K)
+    e0, e1, e2, e3 = _events(torch, K), _events(torch, K), _events(torch, K), _events(torch, K)
     for i in range(K):
         flush.zero_()
         e0[i].record(stream)
@@ -688,17 +701,35 @@ def run_cfg4(args):
         e1[i].record(stream)
         update()
         e2[i].record(stream)
+        diversity()
+        e3[i].record(stream)
     torch.cuda.synchronize()
     fwd = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
     upd = statistics.mean(e1[i].elapsed_time(e2[i]) for i in range(K))
+    div = statistics.mean(e2[i].elapsed_time(e3[i]) for i in range(K))
+    # revive_dead_keys (every revive_every steps in the reference trainer), timed on its own on copies
+    from model_b200 import keys as KM
+    q_sample = torch.nn.functional.normalize(torch.randn(4096, H, 2, W["d_key"] // 2, device=device), dim=-1)
+    usage = torch.distributions.Dirichlet(torch.full((W["n_sub_keys"],), 0.3)).sample((H, 2)).to(device)
+    rv0, rv1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        KM.revive_dead_keys(x["sub_keys"], usage, q_sample, 0.5, generator=torch.Generator(device).manual_seed(1))
+    pick = torch.randint(0, 4096, (H, 2, W["n_sub_keys"]), device=device)
+    normal = torch.randn_like(x["sub_keys"])
+    rv0.record(stream)
+    _, _, rdead = KM.revive_dead_keys(x["sub_keys"], usage, q_sample, 0.5, pick=pick, normal=normal)
+    rv1.record(stream)
+    torch.cuda.synchronize()
+    revive_ms = rv0.elapsed_time(rv1)
     out = {"n_unique": n_u, "clip_scale": scale}
     U = int(out["n_unique"].item())
     F = T * H * k
     hbm, src = peaks()
     upd_bytes = F * 8 + T * d * 4 + U * (2 * d * 4 + 8)
-    ms = fwd + upd
+    ms = fwd + upd + div
     return _common_line(W, 1, K, args.warmup, ms, T / (ms * 1e-3), "tokens/s", "f32", {
-        "scaling": "weak", "stages_ms": {"forward": fwd, "row_grad_adagrad": upd},
+        "scaling": "weak", "stages_ms": {"forward": fwd, "row_grad_adagrad": upd, "key_diversity": div},
+        "revive_dead_keys_ms": revive_ms, "revived": int(rdead.sum().item()),
         "unique_rows": U, "fetches": F, "clip_scale": float(out["clip_scale"].item()),
         "row_update": {"algorithmic_bytes": upd_bytes, "achieved_gbs": upd_bytes / (upd * 1e-3) / 1e9,
                        "peak": hbm, "peak_source": src, "frac": upd_bytes / (upd * 1e-3) / 1e9 / hbm,

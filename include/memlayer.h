@@ -320,6 +320,44 @@ int32_t memlayer_row_adagrad(const memlayer_config* cfg, const memlayer_read* re
                              const memlayer_adagrad_args* args, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* ---- Sub-key maintenance (training) -------------------------------------
+ * cfg supplies heads, n_sub_keys and d_key (tokens and d_value are
+ * checked but unused).  sub_keys is [H, 2, n, d_key/2] float32. */
+
+/* Workspace bytes of memlayer_key_diversity. */
+int32_t memlayer_key_diversity_workspace_size(const memlayer_config* cfg, size_t* bytes);
+
+/* key_diversity_loss (memory_pool_model/memory.py:230-240): loss [1] = mean
+ * over codebooks and ordered pairs i != j of the squared cosine of the
+ * l2-normalised sub-keys; grad [H, 2, n, d_key/2] = grad_scale * d loss /
+ * d sub_keys (the trainer adds key_diversity_coef * loss, train.py:327-329,
+ * so grad_scale = key_diversity_coef gives its gradient).  Either output
+ * may be NULL, not both.  n = 1 gives NaN, as the reference's 0/0. */
+int32_t memlayer_key_diversity(const memlayer_config* cfg, const float* sub_keys, float* loss, float* grad,
+                               float grad_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+typedef struct {
+  float* sub_keys;               /* [H, 2, n, d_key/2], updated in place */
+  float* usage;                  /* [H, 2, n] EMA usage (rows sum to 1), updated in place */
+  const float* queries;          /* [query_tokens, H, 2, d_key/2] unit query halves (aux["queries"]) */
+  int64_t query_tokens;          /* >= 1 */
+  const int32_t* pick;           /* [H, 2, n] token drawn for each key (randint(0, query_tokens)) */
+  const float* noise;            /* [H, 2, n, d_key/2] standard normal draws */
+  float threshold;               /* dead when usage < threshold / n (train.py revive_threshold) */
+  float noise_scale;             /* the reference's `noise` argument (default 0.05) */
+  int32_t* dead;                 /* [H, 2, n] optional output: 1 where revived */
+  float* moment0;                /* optional [H, 2, n, d_key/2] optimiser moments of sub_keys, */
+  float* moment1;                /*   zeroed on revived rows (train.py:497-509), or NULL */
+} memlayer_revive_args;
+
+/* revive_dead_keys (memory_pool_model/memory.py:243-281) with the random
+ * draws passed in (the reference draws pick and noise from its rng inside
+ * the call): a dead key becomes l2_normalize(queries[pick, h, c] +
+ * noise_scale * noise), its usage 1/n, and each [h, c] usage row is divided
+ * by its sum.  A pick outside [0, query_tokens) is wrapped once if negative
+ * and then clamped, as the reference's gather does. */
+int32_t memlayer_revive_dead_keys(const memlayer_config* cfg, const memlayer_revive_args* args, void* stream);
+
 /* Size of the library's built-in scratch array used by
  * memlayer_pool_forward_noalloc (64 MiB, held on every GPU that loads the
  * library until the process exits). */

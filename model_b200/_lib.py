@@ -101,6 +101,22 @@ class MemlayerAdagradArgs(C.Structure):
     ]
 
 
+class MemlayerReviveArgs(C.Structure):
+    _fields_ = [
+        ("sub_keys", C.c_void_p),
+        ("usage", C.c_void_p),
+        ("queries", C.c_void_p),
+        ("query_tokens", C.c_int64),
+        ("pick", C.c_void_p),
+        ("noise", C.c_void_p),
+        ("threshold", C.c_float),
+        ("noise_scale", C.c_float),
+        ("dead", C.c_void_p),
+        ("moment0", C.c_void_p),
+        ("moment1", C.c_void_p),
+    ]
+
+
 DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "MMA wait timed out",
                  14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
                  21: "sub-key id out of range", 22: "sharded row id out of range",
@@ -182,6 +198,13 @@ def lib() -> C.CDLL:
         L.memlayer_row_adagrad.restype = C.c_int32
         L.memlayer_row_adagrad.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerRead), C.c_int32,
                                            C.POINTER(MemlayerAdagradArgs), C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_key_diversity_workspace_size.restype = C.c_int32
+        L.memlayer_key_diversity_workspace_size.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(C.c_size_t)]
+        L.memlayer_key_diversity.restype = C.c_int32
+        L.memlayer_key_diversity.argtypes = [C.POINTER(MemlayerConfig), C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                                             C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_revive_dead_keys.restype = C.c_int32
+        L.memlayer_revive_dead_keys.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerReviveArgs), C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

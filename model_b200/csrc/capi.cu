@@ -10,6 +10,7 @@
 #include <new>
 
 #include "common.cuh"
+#include "keys.cuh"
 #include "rowgrad.cuh"
 #include "shard.cuh"
 
@@ -873,6 +874,42 @@ int32_t memlayer_row_adagrad(const memlayer_config* cfg, const memlayer_read* re
   RowAdagrad A{args->values, args->accum, args->lr, args->grad_clip, args->rest_sq_norm, args->clip_scale,
                args->n_unique};
   ML_TRY(launch_rowgrad(R, L, (char*)workspace, nullptr, nullptr, nullptr, nullptr, &A, (cudaStream_t)stream));
+  return MEMLAYER_OK;
+}
+
+// ---- sub-key maintenance ----
+
+int32_t memlayer_key_diversity_workspace_size(const memlayer_config* cfg, size_t* bytes) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  *bytes = (size_t)key_div_layout(D.H * 2, D.n, D.half).bytes;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_key_diversity(const memlayer_config* cfg, const float* sub_keys, float* loss, float* grad,
+                               float grad_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!sub_keys || (!loss && !grad)) return MEMLAYER_ERR_BAD_POINTER;
+  const KeyDivLayout L = key_div_layout(D.H * 2, D.n, D.half);
+  if (!workspace || workspace_bytes < (size_t)L.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  ML_TRY(launch_key_diversity(sub_keys, D.H * 2, D.n, D.half, (char*)workspace, loss, grad, grad_scale,
+                              (cudaStream_t)stream));
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_revive_dead_keys(const memlayer_config* cfg, const memlayer_revive_args* a, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!a || !a->sub_keys || !a->usage || !a->queries || !a->pick || !a->noise) return MEMLAYER_ERR_BAD_POINTER;
+  if (a->query_tokens < 1) return MEMLAYER_ERR_BAD_SHAPE;
+  ML_TRY(launch_revive(a->sub_keys, a->usage, a->queries, a->query_tokens, a->pick, a->noise, D.H * 2, D.n, D.half,
+                       a->threshold, a->noise_scale, a->dead, a->moment0, a->moment1, (cudaStream_t)stream));
   return MEMLAYER_OK;
 }
 

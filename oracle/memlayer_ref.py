@@ -8,6 +8,8 @@ KumarDev7/model:
 * ``memory_pool_model/model.py:108-120``  router Dense, SiLU gate, output Dense
 * ``memory_pool_model/train.py:146-172``  fetched-row gradients (unique + segment sum)
 * ``memory_pool_model/train.py:396-416``  global-norm clip + row-wise Adagrad
+* ``memory_pool_model/memory.py:230-281`` ``key_diversity_loss`` (with its
+  gradient) and ``revive_dead_keys`` (random draws passed in)
 
 It is the checker, never the product: only ``tests/``, ``__graft_entry__.smoke``
 and the ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import
@@ -289,3 +291,49 @@ def clip_scale(g_rest_sq_norm: float, g_rows: np.ndarray, grad_clip: float) -> n
     """train.py:396-398: min(1, clip / (global_norm + 1e-6))."""
     gnorm = np.sqrt(np.float64(g_rest_sq_norm) + np.sum(g_rows.astype(np.float64) ** 2))
     return F32(min(1.0, grad_clip / (gnorm + 1e-6)))
+
+
+# --------------------------------------------------------------------------
+# Sub-key maintenance (memory.py:230-281)
+# --------------------------------------------------------------------------
+def key_diversity_loss(sub_keys: np.ndarray):
+    """memory.py:230-240: mean squared off-diagonal cosine inside each
+    codebook, and its gradient with respect to sub_keys (the loss enters the
+    trainer's loss with key_diversity_coef, train.py:327-329).
+    Returns (loss float32, grad [H, 2, n, half] float32)."""
+    x = np.asarray(sub_keys, F32)
+    H, C, n, d = x.shape
+    ss = np.sum(x * x, axis=-1, keepdims=True, dtype=F32)
+    r = (F32(1.0) / np.sqrt(ss + F32(1e-6))).astype(F32)
+    k = (x * r).astype(F32)                                               # memory.py:31
+    gram = np.einsum("hcnd,hcmd->hcnm", k, k).astype(F32)
+    off = gram * (F32(1.0) - np.eye(n, dtype=F32))
+    denom = F32(H * C * n * (n - 1))
+    loss = F32(np.sum(off.astype(np.float64) ** 2) / denom)
+    # d loss / d k = 4 / denom * off @ k ; then the normalisation's backward
+    dk = (F32(4.0) / denom * np.einsum("hcnm,hcmd->hcnd", off, k)).astype(F32)
+    dot = np.sum(x * dk, axis=-1, keepdims=True, dtype=F32)
+    dx = (r * dk - (r ** 3) * dot * x).astype(F32)
+    return loss, dx
+
+
+def revive_dead_keys(sub_keys: np.ndarray, usage: np.ndarray, queries: np.ndarray, pick: np.ndarray,
+                     noise: np.ndarray, threshold: float, noise_scale: float = 0.05):
+    """memory.py:243-281 with the random draws passed in: pick [H, 2, n]
+    token indices into queries [M, H, 2, half], noise [H, 2, n, half]
+    standard normal.  Returns (new_sub_keys, new_usage, dead)."""
+    H, C, n, d = sub_keys.shape
+    dead = usage < F32(threshold) / F32(n)
+    h_idx = np.arange(H)[:, None, None]
+    c_idx = np.arange(C)[None, :, None]
+    M = np.asarray(queries).shape[0]
+    pick = np.asarray(pick, np.int64)
+    pick = np.clip(np.where(pick < 0, pick + M, pick), 0, M - 1)         # XLA gather: clamped indices
+    rep = np.asarray(queries, F32)[pick, h_idx, c_idx]                    # [H, C, n, d]
+    rep = (rep + F32(noise_scale) * np.asarray(noise, F32)).astype(F32)
+    rep = l2_normalize(rep)
+    new_keys = np.where(dead[..., None], rep, sub_keys).astype(F32)
+    new_usage = np.where(dead, F32(1.0) / F32(n), usage).astype(F32)
+    new_usage = (new_usage / np.sum(new_usage, axis=-1, keepdims=True, dtype=F32)).astype(F32)
+    return new_keys, new_usage, dead
+
