@@ -358,6 +358,40 @@ typedef struct {
  * and then clamped, as the reference's gather does. */
 int32_t memlayer_revive_dead_keys(const memlayer_config* cfg, const memlayer_revive_args* args, void* stream);
 
+/* ---- Owner-sharded row update (row-sharded table, training) -------------
+ * Replaces fetched_row_grads_sharded + the replicated update
+ * (memory_pool_model/train.py:175-206, 378-399): with the table row-sharded
+ * as in memlayer_layer_forward_sharded (slot s on rank s % world, local row
+ * s / world), each rank merges its own fetches, pushes every merged row to
+ * its owner over NVLink, the owner merges the rows of all ranks in rank
+ * order, and the global-norm clip (sum over every owner's rows, identical on
+ * all ranks) and row-wise Adagrad update the owner's rows only.  Phases
+ * (memlayer_shard_phase): ROUTE = local merge + push, GATHER = owner merge +
+ * publish of its squared norm, REDUCE = clip + Adagrad; waits are bounded
+ * (status 33: inbox, 34: norm partials).  Float32 tables only. */
+
+/* Communicator for the row update: cfg->tokens = the most tokens of one read
+ * on any rank, n_reads = memory layers sharing the pool.  Wire the peers as
+ * for memlayer_shard_comm_create (ipc_handle / open_peers or set_peer,
+ * destroy); forward calls reject it. */
+int32_t memlayer_shard_comm_create_rowgrad(const memlayer_config* cfg, int32_t n_reads, int32_t rank, int32_t world,
+                                           memlayer_shard_comm** comm);
+
+/* Workspace bytes of memlayer_row_adagrad_sharded for `fetches` = sum over
+ * this rank's reads of tokens * H * k. */
+int32_t memlayer_shard_rowgrad_workspace_size(const memlayer_shard_comm* comm, int64_t fetches, size_t* bytes);
+
+/* One row-update step on this rank: reads = this rank's reads (tokens of
+ * this rank); args->values / args->accum = this rank's rows
+ * [memlayer_shard_rows(n*n, rank, world), d] / [rows]; clip_scale = the
+ * global scale (same on every rank); n_unique = local rows this rank
+ * updated.  rest_sq_norm must be the same on every rank.  Every rank calls
+ * every step with the same phases; pass the same reads and workspace to
+ * every phase of one step. */
+int32_t memlayer_row_adagrad_sharded(const memlayer_config* cfg, const memlayer_read* reads, int32_t n_reads,
+                                     const memlayer_adagrad_args* args, memlayer_shard_comm* comm, int32_t phases,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* Size of the library's built-in scratch array used by
  * memlayer_pool_forward_noalloc (64 MiB, held on every GPU that loads the
  * library until the process exits). */

@@ -120,8 +120,9 @@ class MemlayerReviveArgs(C.Structure):
 DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "MMA wait timed out",
                  14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
                  21: "sub-key id out of range", 22: "sharded row id out of range",
-                 23: "fetched slot id out of range",
-                 31: "peer inbox wait timed out", 32: "peer partial-sum wait timed out"}
+                 23: "fetched slot id out of range", 24: "row push beyond inbox capacity",
+                 31: "peer inbox wait timed out", 32: "peer partial-sum wait timed out",
+                 33: "row-gradient inbox wait timed out", 34: "norm partial wait timed out"}
 
 
 class MemlayerError(RuntimeError):
@@ -205,6 +206,15 @@ def lib() -> C.CDLL:
                                              C.c_void_p, C.c_size_t, C.c_void_p]
         L.memlayer_revive_dead_keys.restype = C.c_int32
         L.memlayer_revive_dead_keys.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerReviveArgs), C.c_void_p]
+        L.memlayer_shard_comm_create_rowgrad.restype = C.c_int32
+        L.memlayer_shard_comm_create_rowgrad.argtypes = [C.POINTER(MemlayerConfig), C.c_int32, C.c_int32, C.c_int32,
+                                                         C.POINTER(C.c_void_p)]
+        L.memlayer_shard_rowgrad_workspace_size.restype = C.c_int32
+        L.memlayer_shard_rowgrad_workspace_size.argtypes = [C.c_void_p, C.c_int64, C.POINTER(C.c_size_t)]
+        L.memlayer_row_adagrad_sharded.restype = C.c_int32
+        L.memlayer_row_adagrad_sharded.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerRead), C.c_int32,
+                                                   C.POINTER(MemlayerAdagradArgs), C.c_void_p, C.c_int32, C.c_void_p,
+                                                   C.c_size_t, C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

@@ -263,6 +263,7 @@ int prep_keys(const Dims& D, const memlayer_config* c, const memlayer_pool_args*
 // every peer mapped, and this thread on the communicator's device.
 int check_shard(const memlayer_config* c, const void* values, const memlayer_shard_comm* comm) {
   if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if (comm->kind != 0) return MEMLAYER_ERR_BAD_SHAPE;
   const memlayer_config& k = comm->cfg;
   if (c->heads != k.heads || c->n_sub_keys != k.n_sub_keys || c->d_key != k.d_key || c->d_value != k.d_value ||
       c->top_k != k.top_k || c->values_dtype != k.values_dtype || c->tokens > k.tokens)
@@ -609,6 +610,7 @@ int rowgrad_setup(const memlayer_config* cfg, const memlayer_read* reads, int n_
   *R = RowGradK{};
   R->n_reads = n_reads;
   R->N = D.N;
+  R->Nslot = D.N;
   R->hk = D.H * D.k;
   R->d = D.d;
   R->off[0] = 0;
@@ -784,7 +786,8 @@ int32_t memlayer_shard_comm_set_peer(memlayer_shard_comm* comm, int32_t peer, co
   if (!comm || !other) return MEMLAYER_ERR_BAD_POINTER;
   if (peer < 0 || peer >= comm->world || peer == comm->rank || comm->opened[peer]) return MEMLAYER_ERR_BAD_SHAPE;
   // peers address each other's buffers with their own offsets: shapes must agree
-  if (other->world != comm->world || other->rank != peer || other->off.bytes != comm->off.bytes ||
+  if (other->world != comm->world || other->rank != peer || other->kind != comm->kind ||
+      other->off.bytes != comm->off.bytes ||
       other->cfg.tokens != comm->cfg.tokens || other->cfg.heads != comm->cfg.heads ||
       other->cfg.top_k != comm->cfg.top_k || other->cfg.d_value != comm->cfg.d_value)
     return MEMLAYER_ERR_BAD_SHAPE;
@@ -800,6 +803,168 @@ int32_t memlayer_shard_comm_destroy(memlayer_shard_comm* comm) {
   if (comm->base && cudaFree(comm->base) != cudaSuccess) st = MEMLAYER_ERR_CUDA;
   delete comm;
   return st;
+}
+
+// ---- owner-sharded row update ----
+
+int32_t memlayer_shard_comm_create_rowgrad(const memlayer_config* cfg, int32_t n_reads, int32_t rank, int32_t world,
+                                           memlayer_shard_comm** comm) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  *comm = nullptr;
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (world < 1 || world > MEMLAYER_MAX_SHARDS || rank < 0 || rank >= world) return MEMLAYER_ERR_BAD_SHAPE;
+  if (n_reads < 1 || n_reads > MEMLAYER_MAX_READS) return MEMLAYER_ERR_BAD_SHAPE;
+  if (D.d % 4) return MEMLAYER_ERR_UNSUPPORTED;
+  if (cfg->values_dtype != MEMLAYER_F32) return MEMLAYER_ERR_UNSUPPORTED;
+  memlayer_shard_comm* c = new (std::nothrow) memlayer_shard_comm;
+  if (!c) return MEMLAYER_ERR_CUDA;
+  c->rank = rank;
+  c->world = world;
+  c->cfg = *cfg;
+  c->kind = 1;
+  c->n_reads = n_reads;
+  if (cudaGetDevice(&c->device) != cudaSuccess) {
+    delete c;
+    return MEMLAYER_ERR_CUDA;
+  }
+  const int64_t stride = (D.N + world - 1) / world;
+  const int64_t fetch_cap = (int64_t)n_reads * (cfg->tokens > 0 ? cfg->tokens : 1) * D.H * D.k;
+  c->rcap = fetch_cap < stride ? fetch_cap : stride;
+  c->roff = row_shard_layout(world, c->rcap, D.d);
+  c->off.bytes = c->roff.bytes;
+  if (cudaMalloc(&c->base, (size_t)c->roff.bytes) != cudaSuccess) {
+    delete c;
+    return MEMLAYER_ERR_CUDA;
+  }
+  if (cudaMemset(c->base, 0, (size_t)c->roff.bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(c->base);
+    delete c;
+    return MEMLAYER_ERR_CUDA;
+  }
+  c->peer[rank] = c->base;
+  *comm = c;
+  return MEMLAYER_OK;
+}
+
+namespace {
+
+struct RowPlan {
+  RowGradLayout L;
+  int64_t o_small, o_mkey, o_mref, o_head, o_rowsq, o_mrow, bytes;
+};
+
+RowPlan row_plan(const memlayer_shard_comm* comm, const RowGradK& R) {
+  RowPlan P{};
+  P.L = rowgrad_layout(R.F, R.N, R.d);
+  const int64_t n = (int64_t)comm->world * comm->rcap;
+  int64_t o = (int64_t)up((size_t)P.L.bytes);
+  auto take = [&](int64_t b) {
+    const int64_t at = o;
+    o += (int64_t)up((size_t)b);
+    return at;
+  };
+  P.o_small = take(256);
+  P.o_mkey = take(4 * n);
+  P.o_mref = take(4 * n);
+  P.o_head = take(4 * n);
+  P.o_rowsq = take(4 * n);
+  P.o_mrow = take(4 * n * R.d);
+  P.bytes = o;
+  return P;
+}
+
+// The read descriptors with owner-grouped sort keys for this communicator.
+int row_setup(const memlayer_config* cfg, const memlayer_read* reads, int n_reads, const memlayer_shard_comm* comm,
+              RowGradK* R) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if (comm->kind != 1) return MEMLAYER_ERR_BAD_SHAPE;
+  int st = rowgrad_setup(cfg, reads, n_reads, R);
+  if (st) return st;
+  const memlayer_config& k = comm->cfg;
+  if (cfg->heads != k.heads || cfg->n_sub_keys != k.n_sub_keys || cfg->d_value != k.d_value ||
+      cfg->top_k != k.top_k || n_reads > comm->n_reads)
+    return MEMLAYER_ERR_BAD_SHAPE;
+  for (int r = 0; r < n_reads; ++r)
+    if (reads[r].tokens > (k.tokens > 0 ? k.tokens : 1)) return MEMLAYER_ERR_BAD_SHAPE;
+  const int64_t stride = (R->Nslot + comm->world - 1) / comm->world;
+  R->kworld = comm->world;
+  R->kstride = stride;
+  R->N = stride * comm->world;
+  return MEMLAYER_OK;
+}
+
+RowShardK row_k(const memlayer_shard_comm* comm, const RowGradK& R) {
+  RowShardK K{};
+  for (int p = 0; p < comm->world; ++p) K.peer[p] = comm->peer[p];
+  K.off = comm->roff;
+  K.rank = comm->rank;
+  K.world = comm->world;
+  K.cap = comm->rcap;
+  K.stride = R.kstride;
+  K.rows = shard_rows(R.Nslot, comm->rank, comm->world);
+  K.d = R.d;
+  K.epoch = comm->epoch;
+  return K;
+}
+
+}  // namespace
+
+int32_t memlayer_shard_rowgrad_workspace_size(const memlayer_shard_comm* comm, int64_t fetches, size_t* bytes) {
+  if (!comm || !bytes) return MEMLAYER_ERR_BAD_POINTER;
+  if (comm->kind != 1) return MEMLAYER_ERR_BAD_SHAPE;
+  if (fetches < 0 || fetches >= (1LL << 31)) return MEMLAYER_ERR_BAD_SHAPE;
+  RowGradK R{};
+  R.F = fetches;
+  R.d = comm->cfg.d_value;
+  R.Nslot = (int64_t)comm->cfg.n_sub_keys * comm->cfg.n_sub_keys;
+  R.kstride = (R.Nslot + comm->world - 1) / comm->world;
+  R.N = R.kstride * comm->world;
+  *bytes = (size_t)row_plan(comm, R).bytes;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_row_adagrad_sharded(const memlayer_config* cfg, const memlayer_read* reads, int32_t n_reads,
+                                     const memlayer_adagrad_args* args, memlayer_shard_comm* comm, int32_t phases,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  RowGradK R;
+  int st = row_setup(cfg, reads, n_reads, comm, &R);
+  if (st) return st;
+  if (!args || !args->values || !args->accum || !aligned16(args->values)) return MEMLAYER_ERR_BAD_POINTER;
+  if (cfg->values_dtype != MEMLAYER_F32) return MEMLAYER_ERR_UNSUPPORTED;
+  if (phases < 1 || phases > MEMLAYER_PHASE_ALL) return MEMLAYER_ERR_BAD_SHAPE;
+  for (int p = 0; p < comm->world; ++p)
+    if (!comm->peer[p]) return MEMLAYER_ERR_BAD_POINTER;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return MEMLAYER_ERR_CUDA;
+  const RowPlan P = row_plan(comm, R);
+  if (!workspace || workspace_bytes < (size_t)P.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  char* ws = (char*)workspace;
+  const cudaStream_t s = (cudaStream_t)stream;
+  int* err = reinterpret_cast<int*>(ws + P.L.o_err);
+  if (phases & MEMLAYER_PHASE_ROUTE) ++comm->epoch;
+  const RowShardK K = row_k(comm, R);
+  RowMerge G;
+  G.small = reinterpret_cast<int*>(ws + P.o_small);
+  G.mkey = reinterpret_cast<int*>(ws + P.o_mkey);
+  G.mref = reinterpret_cast<int*>(ws + P.o_mref);
+  G.head = reinterpret_cast<int*>(ws + P.o_head);
+  G.rowsq = reinterpret_cast<float*>(ws + P.o_rowsq);
+  G.mrow = reinterpret_cast<float*>(ws + P.o_mrow);
+  if (phases & MEMLAYER_PHASE_ROUTE) {
+    // local merge with owner-grouped keys; uniq / rows / segment count stay in the workspace
+    ML_TRY(launch_rowgrad(R, P.L, ws, nullptr, nullptr, nullptr, nullptr, nullptr, s));
+    const int* n_seg = reinterpret_cast<const int*>(ws + P.L.o_small) + 1;
+    ML_TRY(launch_rows_push(K, reinterpret_cast<const int*>(ws + P.L.o_uniq),
+                            reinterpret_cast<const float*>(ws + P.L.o_rows), n_seg, P.L.cap, err, s));
+  }
+  if (phases & MEMLAYER_PHASE_GATHER) ML_TRY(launch_rows_merge(K, G, err, s));
+  if (phases & MEMLAYER_PHASE_REDUCE)
+    ML_TRY(launch_rows_apply(K, G, args->values, args->accum, args->lr, args->grad_clip, args->rest_sq_norm,
+                             args->clip_scale, args->n_unique, err, s));
+  return MEMLAYER_OK;
 }
 
 int32_t memlayer_shard_workspace_size(const memlayer_config* cfg, int32_t world, int32_t layer, size_t* bytes) {

@@ -48,8 +48,9 @@ __global__ void rg_keys_kernel(RowGradK R, uint32_t* keys, uint32_t* vals, int* 
   int r = 0;
   while (r + 1 < R.n_reads && f >= R.off[r + 1]) ++r;
   const int s = R.slots[r][f - R.off[r]];
-  uint32_t key = (uint32_t)s, val = (uint32_t)f;
-  if (s < 0 || (int64_t)s >= R.N) {   // only a caller bug can cause this: record it, the fetch adds nothing
+  uint32_t key = R.kworld > 1 ? (uint32_t)((s % R.kworld) * R.kstride + s / R.kworld) : (uint32_t)s;
+  uint32_t val = (uint32_t)f;
+  if (s < 0 || (int64_t)s >= R.Nslot) {   // only a caller bug can cause this: record it, the fetch adds nothing
     atomicCAS(err, 0, 23);
     key = (uint32_t)(R.N - 1);
     val |= DROPPED;

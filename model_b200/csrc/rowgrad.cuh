@@ -13,7 +13,10 @@ struct RowGradK {
   int64_t off[MEMLAYER_MAX_READS + 1];   // first fetch of each read; off[n_reads] = F
   int n_reads;
   int64_t F;    // fetches in all reads
-  int64_t N;    // pool rows
+  int64_t N;    // key space: pool rows, or world * kstride with owner-grouped keys
+  int64_t Nslot;    // pool rows (slot ids must lie in [0, Nslot))
+  int kworld;       // > 1: sort key of slot s = (s % kworld) * kstride + s / kworld
+  int64_t kstride;
   int hk;       // heads * top_k
   int d;        // d_value
 };

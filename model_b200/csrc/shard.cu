@@ -33,42 +33,6 @@ namespace ml {
 
 namespace {
 
-constexpr long long kPeerWaitNs = 2000000000LL;   // 2 s
-
-__device__ __forceinline__ long long global_ns() {
-  long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-// Wait until *flag has reached epoch (wrap-safe).  Gives up after the time
-// limit, or at once when another wait of this call already gave up.
-__device__ bool wait_epoch(const int* flag, int epoch, int* err, int code) {
-  if (ld_acquire_sys(flag) - epoch >= 0) return true;
-  const long long t0 = global_ns();
-  while (true) {
-    if (*(volatile int*)err != 0) return false;
-    __nanosleep(128);
-    if (ld_acquire_sys(flag) - epoch >= 0) return true;
-    if (global_ns() - t0 > kPeerWaitNs) {
-      atomicCAS(err, 0, code);
-      return false;
-    }
-  }
-}
-
 __device__ __forceinline__ int* flag_ptr(const ShardK& S, int rank, int64_t off, int slot) {
   return reinterpret_cast<int*>(S.peer[rank] + off) + slot;
 }

@@ -35,7 +35,90 @@ struct ShardK {
   int64_t t0, t1, span;
 };
 
+// ---- hand-off between ranks through flags in peer memory ----
+constexpr long long kPeerWaitNs = 2000000000LL;   // 2 s
+
+__device__ __forceinline__ long long global_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Wait until *flag has reached epoch (wrap-safe).  Gives up after the time
+// limit, or at once when another wait of this call already gave up.
+__device__ inline bool wait_epoch(const int* flag, int epoch, int* err, int code) {
+  if (ld_acquire_sys(flag) - epoch >= 0) return true;
+  const long long t0 = global_ns();
+  while (true) {
+    if (*(volatile int*)err != 0) return false;
+    __nanosleep(128);
+    if (ld_acquire_sys(flag) - epoch >= 0) return true;
+    if (global_ns() - t0 > kPeerWaitNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
 ShardOff shard_layout(int world, int64_t mcap, int hk, int d);
+
+// ---- owner-sharded row update (training) ----
+// Byte offsets inside a row-update communicator buffer (same on every rank).
+struct RowShardOff {
+  int64_t flags_in;   // [MAX] int: epoch of the row list each source rank has pushed
+  int64_t flags_sq;   // [MAX] int: epoch of the squared-norm partial each owner rank has stored
+  int64_t tickets;    // [4] int: CTA completion counter of the push (local use)
+  int64_t cnt;        // [MAX] int: rows pushed by each source rank
+  int64_t sq;         // [MAX] double: each owner rank's sum of its merged rows^2
+  int64_t lin;        // [world][cap] int: local row of each pushed row (ascending per source)
+  int64_t rin;        // [world][cap][d] float: the pushed row gradients
+  int64_t bytes;
+};
+
+struct RowShardK {
+  char* peer[MEMLAYER_MAX_SHARDS];
+  RowShardOff off;
+  int rank, world;
+  int64_t cap;      // rows per (source, owner) inbox
+  int64_t stride;   // ceil(pool rows / world): owner-grouped key = owner * stride + local row
+  int64_t rows;     // value rows held by this rank
+  int d;
+  int epoch;
+};
+
+RowShardOff row_shard_layout(int world, int64_t cap, int d);
+
+// Pointers of the merge region of a sharded row-update workspace.
+struct RowMerge {
+  int* small;      // [0] merged entries T, [1] touched local rows
+  int* mkey;       // [world * cap] local row of each merged entry (stable by source rank)
+  int* mref;       // [world * cap] inbox entry (source * cap + index) of each merged entry
+  int* head;       // [world * cap] 1 at the first entry of each local row
+  float* rowsq;    // [world * cap] squared norm of each merged row (at its head)
+  float* mrow;     // [world * cap][d] merged row gradient (at its head)
+};
+
+// ROUTE: push this rank's merged rows (owner-grouped keys, ascending) to the owners.
+cudaError_t launch_rows_push(const RowShardK& K, const int* uniq, const float* rows, const int* n_seg, int64_t ucap,
+                             int* err, cudaStream_t s);
+// GATHER: merge the sources' row lists in rank order, publish this owner's squared norm.
+cudaError_t launch_rows_merge(const RowShardK& K, const RowMerge& G, int* err, cudaStream_t s);
+// REDUCE: global-norm clip over every owner's partial, row-wise Adagrad on this rank's rows.
+cudaError_t launch_rows_apply(const RowShardK& K, const RowMerge& G, float* values, float* accum, float lr,
+                              float clip, const float* rest_sq, float* scale_out, int* n_unique_out, int* err,
+                              cudaStream_t s);
 
 // Stage 2 + push of (local row, weight) entries to the owner ranks
 // (replaces launch_combine_gather in the sharded forward).
@@ -60,4 +143,9 @@ struct memlayer_shard_comm {
   char* peer[MEMLAYER_MAX_SHARDS] = {};       // every rank's buffer as seen from this GPU
   bool opened[MEMLAYER_MAX_SHARDS] = {};      // mapped through cudaIpcOpenMemHandle
   int epoch = 0;                              // last call started by the route phase
+  // kind 1: row-update communicator (memlayer_shard_comm_create_rowgrad)
+  int kind = 0;
+  int n_reads = 0;                            // reads (memory layers) per call it was sized for
+  int64_t rcap = 0;                           // rows per (source, owner) inbox
+  ml::RowShardOff roff{};
 };

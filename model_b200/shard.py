@@ -48,12 +48,19 @@ def owner_of(slots: torch.Tensor, world: int):
 class ShardComm:
     """This rank's communicator (memlayer_shard_comm) for one set of shapes."""
 
-    def __init__(self, cfg: L.MemlayerConfig, rank: int, world: int):
+    def __init__(self, cfg: L.MemlayerConfig, rank: int, world: int, n_reads: Optional[int] = None):
+        """``n_reads`` given: a row-update communicator
+        (memlayer_shard_comm_create_rowgrad) for that many memory layers."""
         self.rank, self.world = rank, world
         self.cfg = cfg
+        self.n_reads = n_reads
         h = C.c_void_p()
-        L.check(L.lib().memlayer_shard_comm_create(C.byref(cfg), rank, world, C.byref(h)),
-                "memlayer_shard_comm_create")
+        if n_reads is None:
+            L.check(L.lib().memlayer_shard_comm_create(C.byref(cfg), rank, world, C.byref(h)),
+                    "memlayer_shard_comm_create")
+        else:
+            L.check(L.lib().memlayer_shard_comm_create_rowgrad(C.byref(cfg), n_reads, rank, world, C.byref(h)),
+                    "memlayer_shard_comm_create_rowgrad")
         self.handle = h
         dev, nbytes = C.c_int32(), C.c_size_t()
         L.check(L.lib().memlayer_shard_comm_info(h, None, None, C.byref(dev), C.byref(nbytes)),
@@ -100,9 +107,10 @@ def exchange_handles(handle: bytes, group=None) -> List[bytes]:
     return [bytes(h) for h in out]
 
 
-def connect(cfg: L.MemlayerConfig, group=None) -> ShardComm:
-    """Create this rank's communicator and map every peer's buffer.  Collective
-    over ``group``: every rank calls it with the same shapes."""
+def connect(cfg: L.MemlayerConfig, group=None, n_reads: Optional[int] = None) -> ShardComm:
+    """Create this rank's communicator (a row-update one with ``n_reads``)
+    and map every peer's buffer.  Collective over ``group``: every rank calls
+    it with the same shapes."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
@@ -111,16 +119,16 @@ def connect(cfg: L.MemlayerConfig, group=None) -> ShardComm:
     dist.all_gather_object(shapes, mine, group=group)
     if any(s != mine for s in shapes):
         raise ValueError("every rank must create its communicator with the same config")
-    comm = ShardComm(cfg, dist.get_rank(group), world)
+    comm = ShardComm(cfg, dist.get_rank(group), world, n_reads)
     comm.open_peers(exchange_handles(comm.ipc_handle(), group))
     dist.barrier(group)
     return comm
 
 
-def emulated_comms(cfg: L.MemlayerConfig, world: int) -> List[ShardComm]:
+def emulated_comms(cfg: L.MemlayerConfig, world: int, n_reads: Optional[int] = None) -> List[ShardComm]:
     """``world`` communicators in this process on the current device, wired to
     each other directly (no IPC): for driving every rank from one process."""
-    comms = [ShardComm(cfg, r, world) for r in range(world)]
+    comms = [ShardComm(cfg, r, world, n_reads) for r in range(world)]
     for c in comms:
         for o in comms:
             if o is not c:

@@ -119,3 +119,70 @@ def rowwise_adagrad(values: torch.Tensor, accum: torch.Tensor, aux: Dict, probe_
         if code:
             raise L.DeviceError(f"device status {code}: {L.DEVICE_ERRORS.get(code, 'unknown')}")
     return {"clip_scale": scale, "n_unique": n_unique}
+
+
+class ShardedRowUpdate:
+    """One rank's owner-sharded row update over a row-update communicator
+    (``model_b200.shard.connect(cfg, n_reads=...)``): ``values`` / ``accum``
+    are this rank's rows (slot s on rank s % world, local row s / world);
+    ``aux`` / ``probe_grads`` hold this rank's reads.  ``run(phases)`` runs
+    ROUTE (local merge + push), GATHER (owner merge) and REDUCE (clip +
+    Adagrad) -- every rank must run every phase of a step."""
+
+    def __init__(self, comm, values: torch.Tensor, accum: torch.Tensor, aux: Dict, probe_grads: Dict,
+                 layers: Sequence[int], *, lr: float, grad_clip: float,
+                 rest_sq_norm: Optional[torch.Tensor] = None):
+        if values.dtype != torch.float32 or not values.is_cuda or not values.is_contiguous():
+            raise TypeError("values must be a contiguous float32 CUDA tensor")
+        if accum.dtype != torch.float32 or accum.numel() != values.shape[0] or not accum.is_contiguous():
+            raise TypeError("accum must be a contiguous float32 tensor with one entry per local row")
+        self.comm = comm
+        reads, self._keep, H, k, d = _reads(aux, probe_grads, layers)
+        self.device = values.device
+        self.cfg = _config(comm.cfg.n_sub_keys ** 2, H, k, d)
+        F = sum(r.tokens for r in reads) * H * k
+        self.scale = torch.empty(1, dtype=torch.float32, device=self.device)
+        self.n_unique = torch.empty(1, dtype=torch.int32, device=self.device)
+        self._rest = None if rest_sq_norm is None else rest_sq_norm.to(self.device, torch.float32).reshape(1).contiguous()
+        self.args = L.MemlayerAdagradArgs(values=values.data_ptr(), accum=accum.data_ptr(), lr=float(lr),
+                                          grad_clip=float(grad_clip),
+                                          rest_sq_norm=None if self._rest is None else self._rest.data_ptr(),
+                                          clip_scale=self.scale.data_ptr(), n_unique=self.n_unique.data_ptr())
+        nb = C.c_size_t()
+        L.check(L.lib().memlayer_shard_rowgrad_workspace_size(comm.handle, F, C.byref(nb)),
+                "memlayer_shard_rowgrad_workspace_size")
+        self.nbytes = nb.value
+        self.ws = _workspace(nb.value, self.device)
+        self._arr = (L.MemlayerRead * len(reads))(*reads)
+        self._n = len(reads)
+        self._values, self._accum = values, accum
+
+    def run(self, phases: int = L.PHASE_ALL, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        L.check(L.lib().memlayer_row_adagrad_sharded(C.byref(self.cfg), self._arr, self._n, C.byref(self.args),
+                                                     self.comm.handle, phases, self.ws.data_ptr(), self.nbytes, s),
+                "memlayer_row_adagrad_sharded")
+
+    def check(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        code = L.device_status(self.cfg, self.ws.data_ptr(), s)
+        if code:
+            raise L.DeviceError(f"device status {code}: {L.DEVICE_ERRORS.get(code, 'unknown')}")
+
+    def result(self) -> Dict[str, torch.Tensor]:
+        return {"clip_scale": self.scale, "n_unique": self.n_unique}
+
+
+def sharded_rowwise_adagrad(values: torch.Tensor, accum: torch.Tensor, aux: Dict, probe_grads: Dict,
+                            layers: Sequence[int], comm, *, lr: float, grad_clip: float,
+                            rest_sq_norm: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None,
+                            check: bool = False) -> Dict[str, torch.Tensor]:
+    """The row-sharded counterpart of :func:`rowwise_adagrad` (train.py:175-206
+    merge + :378-399 clip and update): all three phases on this rank.
+    Returns {"clip_scale" (global), "n_unique" (rows this rank updated)}."""
+    up = ShardedRowUpdate(comm, values, accum, aux, probe_grads, layers, lr=lr, grad_clip=grad_clip,
+                          rest_sq_norm=rest_sq_norm)
+    up.run(L.PHASE_ALL, stream)
+    if check:
+        up.check(stream)
+    return up.result()

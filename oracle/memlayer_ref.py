@@ -6,7 +6,8 @@ KumarDev7/model:
 * ``memory_pool_model/memory.py:30-57``   l2-normalise and top-k helpers
 * ``memory_pool_model/memory.py:119-227`` ``MemoryPool.__call__``
 * ``memory_pool_model/model.py:108-120``  router Dense, SiLU gate, output Dense
-* ``memory_pool_model/train.py:146-172``  fetched-row gradients (unique + segment sum)
+* ``memory_pool_model/train.py:146-206``  fetched-row gradients (unique + segment sum),
+  single device and data-parallel (local merge, all-gather, second merge)
 * ``memory_pool_model/train.py:396-416``  global-norm clip + row-wise Adagrad
 * ``memory_pool_model/memory.py:230-281`` ``key_diversity_loss`` (with its
   gradient) and ``revive_dead_keys`` (random draws passed in)
@@ -275,6 +276,32 @@ def fetched_row_grads(slots: np.ndarray, weights: np.ndarray, g_out: np.ndarray,
     uniq, inv = np.unique(sl, return_inverse=True)
     rows = np.zeros((uniq.shape[0], g_out.shape[-1]), F32)
     np.add.at(rows, inv.reshape(-1), contrib)
+    return uniq.astype(np.int64), rows
+
+
+def fetched_row_grads_sharded(per_device, pool_size: int):
+    """train.py:175-206: every device merges its own fetches
+    (fetched_row_grads), the devices' merged (uniq, rows) are concatenated in
+    device order (the tiled all_gather) and merged once more (_merge_rows,
+    train.py:160-172: unique + segment sum in concatenation order).
+    per_device = [(slots, weights, g_out), ...]; a device with no tokens
+    passes empty arrays."""
+    us, rs = [], []
+    d = None
+    for slots, weights, g_out in per_device:
+        d = g_out.shape[-1]
+        if g_out.shape[0] == 0:
+            continue
+        u, r = fetched_row_grads(slots, weights, g_out, pool_size)
+        us.append(u)
+        rs.append(r)
+    if not us:
+        return np.zeros(0, np.int64), np.zeros((0, d), F32)
+    u_all = np.concatenate(us)
+    r_all = np.concatenate(rs).astype(F32)
+    uniq, inv = np.unique(u_all, return_inverse=True)
+    rows = np.zeros((uniq.shape[0], r_all.shape[1]), F32)
+    np.add.at(rows, inv.reshape(-1), r_all)
     return uniq.astype(np.int64), rows
 
 
