@@ -633,48 +633,71 @@ def run_cfg1(args):
                 "outside this library.  L2 flushed before every step"})
 
 
-def run_cfg4(args):
-    """configs[4]: configs[0] shapes, f32 values, 8192 Zipf-clustered tokens;
-    step = layer forward with routing statistics + fetched-row gradients of a
-    synthetic probe gradient + global-norm clip + row-wise Adagrad on the
-    touched rows + key_diversity_loss with its gradient.  revive_dead_keys
-    (every revive_every steps in the reference) is timed once beside it.  The backward through the router is not built, so the probe
-    gradient is drawn, not computed."""
+def run_cfg4(args, rank=0, world=1):
+    """configs[0] shapes, f32 values, 8192 Zipf-clustered tokens
+    per GPU; step = layer forward with routing statistics + fetched-row
+    gradients of a synthetic probe gradient + global-norm clip + row-wise
+    Adagrad on the touched rows + key_diversity_loss with its gradient.
+    revive_dead_keys (every revive_every steps in the reference) is timed
+    once beside it (rank 0).  The backward through the router is not built,
+    so the probe gradient is drawn, not computed.  With N > 1 the table is
+    row-sharded: the sharded forward, then the owner-sharded row update
+    (each rank's merged rows pushed to their owners over NVLink); times are
+    the max over ranks."""
     import torch
 
     from model_b200 import _lib as L
-    device = torch.device("cuda", 0)
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)) if world > 1 else 0)
     torch.cuda.set_device(device)
     W = dict(WORKLOAD, name="cfg4_sparse_update", values_dtype="f32")
-    x = make_inputs(torch, device, W, "f32", W["seed"])
+    N = W["n_sub_keys"] ** 2
     T, d, H, k = W["tokens_per_gpu"], W["d_value"], W["heads"], W["top_k"]
-    x["h"] = clustered_hidden(torch, device, T, W["d_model"], W["seed"] + 1)
-    call = LayerCall(torch, L, W, x, device, "f32")
-    cnt_slot = torch.empty(W["n_sub_keys"] ** 2, device=device)
+    if world > 1:
+        from model_b200.shard import connect, shard_rows
+        rows = shard_rows(N, rank, world)
+        x = make_inputs(torch, device, W, "f32", W["seed"], rows)
+        x["h"] = clustered_hidden(torch, device, T, W["d_model"], W["seed"] + 1 + rank)
+        call = ShardedLayerCall(torch, L, W, x, device, "f32")
+    else:
+        rows = N
+        x = make_inputs(torch, device, W, "f32", W["seed"])
+        x["h"] = clustered_hidden(torch, device, T, W["d_model"], W["seed"] + 1)
+        call = LayerCall(torch, L, W, x, device, "f32")
+    cnt_slot = torch.empty(N, device=device)
     cnt_sub = torch.empty(H, 2, W["n_sub_keys"], device=device)
     bal = torch.empty(1, device=device)
     call.args.pool.slot_counts, call.args.pool.subkey_counts = cnt_slot.data_ptr(), cnt_sub.data_ptr()
     call.args.pool.balance_loss = bal.data_ptr()
-    accum = torch.zeros(W["n_sub_keys"] ** 2, device=device)
-    g = torch.randn(T, d, device=device, generator=torch.Generator(device=device).manual_seed(7)) * 1e-3
+    accum = torch.zeros(rows, device=device)
+    g = torch.randn(T, d, device=device, generator=torch.Generator(device=device).manual_seed(7 + rank)) * 1e-3
     rest = torch.tensor([0.5], device=device)
     scale = torch.empty(1, device=device)
     n_u = torch.empty(1, dtype=torch.int32, device=device)
-    # the C call of memlayer_row_adagrad, built once (train.py:378-383, 396-399)
+    # the C call of memlayer_row_adagrad (train.py:378-383, 396-399), or of
+    # memlayer_row_adagrad_sharded on the row-sharded table, built once
     reads = (L.MemlayerRead * 1)(L.MemlayerRead(slots=call.slots.data_ptr(), weights=call.weights.data_ptr(),
                                                 grad=g.data_ptr(), tokens=T))
     ada = L.MemlayerAdagradArgs(values=x["values"].data_ptr(), accum=accum.data_ptr(), lr=0.01, grad_clip=1.0,
                                 rest_sq_norm=rest.data_ptr(), clip_scale=scale.data_ptr(), n_unique=n_u.data_ptr())
     rb = C.c_size_t()
-    L.check(L.lib().memlayer_rowgrad_workspace_size(C.byref(call.cfg), T * H * k, C.byref(rb)), "rowgrad ws")
+    lib = L.lib()
+    if world > 1:
+        rcomm = connect(call.cfg, n_reads=1)
+        L.check(lib.memlayer_shard_rowgrad_workspace_size(rcomm.handle, T * H * k, C.byref(rb)), "rowgrad ws")
+    else:
+        L.check(lib.memlayer_rowgrad_workspace_size(C.byref(call.cfg), T * H * k, C.byref(rb)), "rowgrad ws")
     rws = torch.empty(rb.value, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
-    lib = L.lib()
 
     def update():
-        L.check(lib.memlayer_row_adagrad(C.byref(call.cfg), reads, 1, C.byref(ada), rws.data_ptr(), rb.value,
-                                         stream.cuda_stream), "memlayer_row_adagrad")
+        if world > 1:
+            L.check(lib.memlayer_row_adagrad_sharded(C.byref(call.cfg), reads, 1, C.byref(ada), rcomm.handle,
+                                                     L.PHASE_ALL, rws.data_ptr(), rb.value, stream.cuda_stream),
+                    "memlayer_row_adagrad_sharded")
+        else:
+            L.check(lib.memlayer_row_adagrad(C.byref(call.cfg), reads, 1, C.byref(ada), rws.data_ptr(), rb.value,
+                                             stream.cuda_stream), "memlayer_row_adagrad")
     # key_diversity_loss and its gradient, scaled by key_diversity_coef (train.py:327-329)
     kd_loss = torch.empty(1, device=device)
     kd_grad = torch.empty_like(x["sub_keys"])
@@ -692,6 +715,8 @@ def run_cfg4(args):
         update()
         diversity()
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     K = args.steps
     e0, e1, e2, e3 = _events(torch, K), _events(torch, K), _events(torch, K), _events(torch, K)
     for i in range(K):
@@ -704,9 +729,26 @@ def run_cfg4(args):
         diversity()
         e3[i].record(stream)
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    step = statistics.mean(e0[i].elapsed_time(e3[i]) for i in range(K))
     fwd = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
     upd = statistics.mean(e1[i].elapsed_time(e2[i]) for i in range(K))
     div = statistics.mean(e2[i].elapsed_time(e3[i]) for i in range(K))
+    U = int(n_u.item())
+    if world > 1:
+        t = torch.tensor([step, fwd, upd, div], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        u_all = torch.tensor([U], dtype=torch.int64, device=device)
+        torch.distributed.all_reduce(u_all)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        rcomm.close()
+        call.comm.close()
+        if rank != 0:
+            return None
+        step, fwd, upd, div = t.tolist()
+        U = int(u_all.item())
     # revive_dead_keys (every revive_every steps in the reference trainer), timed on its own on copies
     from model_b200 import keys as KM
     q_sample = torch.nn.functional.normalize(torch.randn(4096, H, 2, W["d_key"] // 2, device=device), dim=-1)
@@ -721,21 +763,20 @@ def run_cfg4(args):
     rv1.record(stream)
     torch.cuda.synchronize()
     revive_ms = rv0.elapsed_time(rv1)
-    out = {"n_unique": n_u, "clip_scale": scale}
-    U = int(out["n_unique"].item())
     F = T * H * k
     hbm, src = peaks()
-    upd_bytes = F * 8 + T * d * 4 + U * (2 * d * 4 + 8)
-    ms = fwd + upd + div
-    return _common_line(W, 1, K, args.warmup, ms, T / (ms * 1e-3), "tokens/s", "f32", {
+    upd_bytes = F * 8 + T * d * 4 + U * (2 * d * 4 + 8) // world
+    return _common_line(W, world, K, args.warmup, step, world * T / (step * 1e-3), "tokens/s", "f32", {
         "scaling": "weak", "stages_ms": {"forward": fwd, "row_grad_adagrad": upd, "key_diversity": div},
+        "stage_note": "max over ranks of each stage" if world > 1 else "per-stage means",
         "revive_dead_keys_ms": revive_ms, "revived": int(rdead.sum().item()),
-        "unique_rows": U, "fetches": F, "clip_scale": float(out["clip_scale"].item()),
+        "unique_rows": U, "fetches": F * world, "clip_scale": float(scale.item()),
         "row_update": {"algorithmic_bytes": upd_bytes, "achieved_gbs": upd_bytes / (upd * 1e-3) / 1e9,
                        "peak": hbm, "peak_source": src, "frac": upd_bytes / (upd * 1e-3) / 1e9 / hbm,
-                       "bytes_note": "slots+weights of every fetch, one read of every probe-gradient row, "
-                                     "read+write of every touched value row and accumulator"},
-        "note": "probe gradient drawn (router backward not built); L2 flushed before every step"})
+                       "bytes_note": "per rank: slots+weights of every fetch, one read of every probe-gradient row, "
+                                     "read+write of its share of the touched value rows and accumulators"},
+        "note": "probe gradient drawn (router backward not built); L2 flushed before every step"
+                + ("; table row-sharded, owner-sharded row update over NVLink" if world > 1 else "")})
 
 
 def run_cfg2(args):
@@ -901,7 +942,7 @@ def main():
     elif args.emulate_ranks:
         line = run_emulated(args)
     elif args.workload == "cfg4":
-        line = run_cfg4(args)
+        line = run_cfg4(args, rank, world)
     elif args.workload == "cfg1":
         line = run_cfg1(args)
     elif args.workload == "cfg2":

@@ -69,3 +69,68 @@ def test_sharded_across_gpus(world, vdt_name, tmp_path):
         same, e_mem, e_y = np.load(tmp_path / f"r{rank}.npy")
         assert same == 1.0, f"rank {rank}: routing differs"
         assert e_mem <= 1e-5 and e_y <= 1e-5, f"rank {rank}: mem {e_mem:.2e} y {e_y:.2e}"
+
+
+def _row_worker(rank, world, port, outdir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from model_b200 import _lib as L
+    from model_b200.shard import connect
+    from model_b200.sparse import sharded_rowwise_adagrad
+    from oracle import memlayer_ref as ref
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        n_sub, H, k, d, lr, clip, rest = 64, 4, 8, 64, 0.05, 1.0, 0.25
+        N = n_sub * n_sub
+        rng = np.random.default_rng(1)                              # same table on every rank
+        values = rng.standard_normal((N, d)).astype(np.float32)
+        acc = (rng.random(N) * 0.1).astype(np.float32)
+        per = []
+        for r in range(world):                                       # every rank's reads (seeded)
+            rr = np.random.default_rng(50 + r)
+            M = 40 + 17 * r
+            hot = np.random.default_rng(3).permutation(N)
+            s = hot[np.minimum(rr.zipf(1.1, size=(M, H, k)), N) - 1].astype(np.int32)
+            w = rr.random((M, H, k)).astype(np.float32)
+            g = (rr.standard_normal((M, d)) * 0.1).astype(np.float32)
+            per.append((s, w, g))
+        cfg = L.MemlayerConfig(tokens=40 + 17 * (world - 1), heads=H, n_sub_keys=n_sub, d_key=16, d_value=d,
+                               top_k=k, d_model=16, values_dtype=L.F32, routing_noise=0.0, min_temperature=1.0,
+                               max_temperature=1.0)
+        comm = connect(cfg, n_reads=1)
+        v = torch.from_numpy(values[rank::world].copy()).cuda()
+        a = torch.from_numpy(acc[rank::world].copy()).cuda()
+        s, w, g = per[rank]
+        out = sharded_rowwise_adagrad(v, a, {"slots": [torch.from_numpy(s).cuda()],
+                                             "weights": [torch.from_numpy(w).cuda()]},
+                                      {0: torch.from_numpy(g).cuda()}, [0], comm, lr=lr, grad_clip=clip,
+                                      rest_sq_norm=torch.tensor([rest]), check=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        uniq, rows = ref.fetched_row_grads_sharded(per, N)
+        scale = ref.clip_scale(rest, rows, clip)
+        ref.rowwise_adagrad(values, acc, uniq, rows * scale, lr)
+        e_v = float(np.abs(v.cpu().numpy() - values[rank::world]).max() / np.abs(values).max())
+        e_a = float(np.abs(a.cpu().numpy() - acc[rank::world]).max() / np.abs(acc).max())
+        e_s = abs(float(out["clip_scale"]) - float(scale)) / float(scale)
+        np.save(os.path.join(outdir, f"row{rank}.npy"), np.array([e_v, e_a, e_s]))
+        dist.barrier()
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_owner_sharded_update_across_gpus(world, tmp_path):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    mp.spawn(_row_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for rank in range(world):
+        e_v, e_a, e_s = np.load(tmp_path / f"row{rank}.npy")
+        assert e_v <= 1e-5 and e_a <= 1e-5 and e_s <= 1e-6, f"rank {rank}: {e_v:.2e} {e_a:.2e} {e_s:.2e}"
