@@ -320,6 +320,21 @@ int32_t memlayer_row_adagrad(const memlayer_config* cfg, const memlayer_read* re
                              const memlayer_adagrad_args* args, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* ---- Value table in page-locked host memory (the host tier) -------------
+ * memory.py:180-183 with host_pool.fetch (host_pool.py:206-220): the value
+ * table lives off the GPU (a pool larger than HBM) and only the fetched rows
+ * come in.  args->values points to page-locked host memory the device can
+ * read (cudaHostAlloc / cudaMallocHost, or cudaHostRegister with
+ * cudaHostRegisterMapped; device memory also works).  The GPU routes the
+ * tokens, removes duplicate read slots, copies each distinct row once from
+ * host memory into the workspace and mixes from there: outputs, slots,
+ * weights and statistics are those of memlayer_pool_forward on the same
+ * table, bit for bit.  Same arguments as memlayer_pool_forward; the
+ * workspace holds a staging copy of up to min(tokens * H * k, n*n) rows. */
+int32_t memlayer_host_table_workspace_size(const memlayer_config* cfg, size_t* bytes);
+int32_t memlayer_pool_forward_host_table(const memlayer_config* cfg, const memlayer_pool_args* args, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+
 /* ---- Sub-key maintenance (training) -------------------------------------
  * cfg supplies heads, n_sub_keys and d_key (tokens and d_value are
  * checked but unused).  sub_keys is [H, 2, n, d_key/2] float32. */

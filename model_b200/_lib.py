@@ -121,6 +121,7 @@ DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "M
                  14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
                  21: "sub-key id out of range", 22: "sharded row id out of range",
                  23: "fetched slot id out of range", 24: "row push beyond inbox capacity",
+                 25: "host-table row id out of range",
                  31: "peer inbox wait timed out", 32: "peer partial-sum wait timed out",
                  33: "row-gradient inbox wait timed out", 34: "norm partial wait timed out"}
 
@@ -215,6 +216,11 @@ def lib() -> C.CDLL:
         L.memlayer_row_adagrad_sharded.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerRead), C.c_int32,
                                                    C.POINTER(MemlayerAdagradArgs), C.c_void_p, C.c_int32, C.c_void_p,
                                                    C.c_size_t, C.c_void_p]
+        L.memlayer_host_table_workspace_size.restype = C.c_int32
+        L.memlayer_host_table_workspace_size.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(C.c_size_t)]
+        L.memlayer_pool_forward_host_table.restype = C.c_int32
+        L.memlayer_pool_forward_host_table.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerPoolArgs),
+                                                       C.c_void_p, C.c_size_t, C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

@@ -10,6 +10,7 @@
 #include <new>
 
 #include "common.cuh"
+#include "host_table.cuh"
 #include "keys.cuh"
 #include "rowgrad.cuh"
 #include "shard.cuh"
@@ -383,7 +384,8 @@ int shard_gather_reduce(const Dims& D, const ShardRun& R, const void* values, in
 
 // MemoryPool.__call__, single GPU (comm == nullptr) or row-sharded.
 int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* workspace, size_t workspace_bytes,
-              cudaStream_t s, memlayer_shard_comm* comm, int phases, bool allow_overlap = true) {
+              cudaStream_t s, memlayer_shard_comm* comm, int phases, bool allow_overlap = true,
+              bool route_only = false) {
   Dims D;
   int st = check_config(cfg, &D, false);
   if (st) return st;
@@ -402,13 +404,19 @@ int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* wor
   layout(D, f, (char*)workspace, &W);
   float* qn = a->queries_unit ? a->queries_unit : W.qn;
   if (!comm) {
+    memlayer_pool_args ro;
+    if (route_only) {   // stage 2 writes slots / weights, no gather
+      ro = *a;
+      ro.values = nullptr;
+      a = &ro;
+    }
     ML_TRY(mark(a, 0, s));
     ML_TRY(mark(a, 1, s));
     if ((st = prep_keys(D, cfg, a, W, s))) return st;
     ML_TRY(launch_normalize_queries(D, a->queries, qn, W.qlen, W.q_hi, W.q_lo, s));
     ML_TRY(mark(a, 2, s));
-    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, a->out, nullptr, nullptr, nullptr, nullptr, s,
-                            nullptr, allow_overlap)))
+    if ((st = run_route_mix(D, a, W, qn, a->slots, a->weights, route_only ? nullptr : a->out, nullptr, nullptr,
+                            nullptr, nullptr, s, nullptr, allow_overlap && !route_only)))
       return st;
     ML_TRY(mark(a, 5, s));
     return MEMLAYER_OK;
@@ -1039,6 +1047,92 @@ int32_t memlayer_row_adagrad(const memlayer_config* cfg, const memlayer_read* re
   RowAdagrad A{args->values, args->accum, args->lr, args->grad_clip, args->rest_sq_norm, args->clip_scale,
                args->n_unique};
   ML_TRY(launch_rowgrad(R, L, (char*)workspace, nullptr, nullptr, nullptr, nullptr, &A, (cudaStream_t)stream));
+  return MEMLAYER_OK;
+}
+
+// ---- value table in page-locked host memory ----
+
+namespace {
+
+struct TablePlan {
+  size_t fwd;              // pool-forward workspace (at offset 0: its status word is the call's)
+  RowGradLayout L;         // sort of the read slots
+  int64_t o_sort, o_inv, o_stage, cap, bytes;
+};
+
+TablePlan table_plan(const Dims& D, const Flags& f) {
+  TablePlan P{};
+  P.fwd = layout(D, f, nullptr, nullptr);
+  const int64_t F = D.M * D.H * D.k;
+  P.L = rowgrad_layout(F, D.N, 0);
+  P.cap = F < D.N ? F : D.N;
+  int64_t o = (int64_t)up(P.fwd);
+  P.o_sort = o;
+  o += (int64_t)up((size_t)P.L.bytes);
+  P.o_inv = o;
+  o += (int64_t)up((size_t)(4 * F));
+  P.o_stage = o;
+  o += (int64_t)up((size_t)(P.cap * D.d * table_elem_bytes(D.vdtype)));
+  P.bytes = o;
+  return P;
+}
+
+}  // namespace
+
+int32_t memlayer_host_table_workspace_size(const memlayer_config* cfg, size_t* bytes) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.balance = true;
+  *bytes = (size_t)table_plan(D, f).bytes;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_pool_forward_host_table(const memlayer_config* cfg, const memlayer_pool_args* a, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, false);
+  if (st) return st;
+  if ((st = check_pool_args(D, a, false))) return st;
+  // the table must be readable by this device: page-locked host memory (or device memory)
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, a->values) != cudaSuccess) {
+    cudaGetLastError();
+    return MEMLAYER_ERR_BAD_POINTER;
+  }
+  if (attr.type == cudaMemoryTypeUnregistered || !attr.devicePointer) return MEMLAYER_ERR_BAD_POINTER;
+  const void* table = attr.devicePointer;
+  Flags f;
+  f.balance = a->balance_loss != nullptr;
+  const TablePlan P = table_plan(D, f);
+  if (!workspace || workspace_bytes < (size_t)P.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  const cudaStream_t s = (cudaStream_t)stream;
+  if ((st = pool_impl(cfg, a, workspace, P.fwd, s, nullptr, MEMLAYER_PHASE_ALL, false, true))) return st;
+  if (D.M == 0) return MEMLAYER_OK;
+  char* ws = (char*)workspace;
+  resolve_noise(&D, cfg, a);
+  RowGradK R{};
+  R.n_reads = 1;
+  R.slots[0] = a->slots;
+  R.weights[0] = a->weights;
+  R.off[0] = 0;
+  R.off[1] = D.M * D.H * D.k;
+  R.F = R.off[1];
+  R.N = D.N;
+  R.Nslot = D.N;
+  R.hk = D.H * D.k;
+  R.d = 0;
+  R.kadd = D.shuffle ? D.N / 2 + 1 : 0;   // the read slot (memory.py:179)
+  int* inv = reinterpret_cast<int*>(ws + P.o_inv);
+  char* sort_ws = ws + P.o_sort;
+  ML_TRY(launch_sort_unique(R, P.L, sort_ws, inv, s));
+  int* err = reinterpret_cast<int*>(ws + 256);   // the forward's status word
+  ML_TRY(launch_table_fetch(D, table, reinterpret_cast<const int*>(sort_ws + P.L.o_uniq),
+                            reinterpret_cast<const int*>(sort_ws + P.L.o_small) + 1, P.cap, ws + P.o_stage, err, s));
+  ML_TRY(launch_table_mix(D, ws + P.o_stage, inv, a->weights, a->out, s));
   return MEMLAYER_OK;
 }
 

@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(1024) combine_gather_kernel(
     }
   }
   if (lane == 0 && top1_part) top1_part[m * D.H + h] = top1;
+  if (values == nullptr) return;   // routing only (the host-table read gathers afterwards)
 
   // read (slot + N/2 + 1) % N under shuffle_reads (memory.py:179)
   const int64_t rs = D.shuffle ? ((int64_t)slot + D.N / 2 + 1) % D.N : (int64_t)slot;

@@ -48,7 +48,8 @@ __global__ void rg_keys_kernel(RowGradK R, uint32_t* keys, uint32_t* vals, int* 
   int r = 0;
   while (r + 1 < R.n_reads && f >= R.off[r + 1]) ++r;
   const int s = R.slots[r][f - R.off[r]];
-  uint32_t key = R.kworld > 1 ? (uint32_t)((s % R.kworld) * R.kstride + s / R.kworld) : (uint32_t)s;
+  uint32_t key = R.kworld > 1 ? (uint32_t)((s % R.kworld) * R.kstride + s / R.kworld)
+                 : R.kadd > 0 ? (uint32_t)(((int64_t)s + R.kadd) % R.Nslot) : (uint32_t)s;
   uint32_t val = (uint32_t)f;
   if (s < 0 || (int64_t)s >= R.Nslot) {   // only a caller bug can cause this: record it, the fetch adds nothing
     atomicCAS(err, 0, 23);
@@ -520,6 +521,14 @@ __global__ void __launch_bounds__(256) rg_adagrad_kernel(const int* n_seg, const
   if (lane == 0) accum[s] = a;
 }
 
+// inv[fetch] = its segment (sorted position i holds fetch vals[i])
+__global__ void rg_inverse_kernel(const uint32_t* vals, const int* seg_id, int64_t F, int* inv) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= F) return;
+  const uint32_t v = vals[i];
+  inv[v & ~DROPPED] = (v & DROPPED) ? -1 : seg_id[i];
+}
+
 inline int vpl_for(int d) { return d <= 128 ? 4 : d <= 256 ? 8 : d <= 512 ? 16 : 32; }
 
 #define ML_VPL(V, CALL) \
@@ -570,11 +579,15 @@ RowGradLayout rowgrad_layout(int64_t F, int64_t N, int d) {
   return L;
 }
 
-cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, int* uniq_out, float* rows_out,
-                           int* n_unique_out, float* sq_out, const RowAdagrad* ada, cudaStream_t s) {
+namespace {
+
+// Keys of every fetch, the stable radix passes and the segments; on return
+// (*ka, *va) hold the sorted keys / fetch ids.  F > 0.
+cudaError_t sort_segments(const RowGradK& R, const RowGradLayout& L, char* ws, uint32_t** ka_out, uint32_t** va_out,
+                          int* uniq, cudaStream_t s) {
   int* small = reinterpret_cast<int*>(ws + L.o_small);
   int* err = reinterpret_cast<int*>(ws + L.o_err);
-  int* n_seg = small + 1, *ticket = small + 2;
+  int* n_seg = small + 1;
   int* dtot = reinterpret_cast<int*>(ws + L.o_dtot);
   uint32_t* ka = reinterpret_cast<uint32_t*>(ws + L.o_keys_a);
   uint32_t* va = reinterpret_cast<uint32_t*>(ws + L.o_vals_a);
@@ -582,6 +595,53 @@ cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, 
   uint32_t* vb = reinterpret_cast<uint32_t*>(ws + L.o_vals_b);
   int* hist = reinterpret_cast<int*>(ws + L.o_hist);
   int* segtot = reinterpret_cast<int*>(ws + L.o_segtot);
+  int* seg_id = reinterpret_cast<int*>(ws + L.o_seg_id);
+  int* seg_start = reinterpret_cast<int*>(ws + L.o_seg_start);
+  const int64_t F = R.F;
+  rg_keys_kernel<<<(unsigned)((F + 255) / 256), 256, 0, s>>>(R, ka, va, err);
+  count_launch();
+  const int digits = 1 << L.rbits;
+  for (int p = 0; p < L.passes; ++p) {
+    const int shift = p * L.rbits;
+    rs_hist_kernel<<<(unsigned)L.nblk, RS_THREADS, 0, s>>>(ka, F, shift, digits, (int)L.nblk, hist);
+    rs_digit_scan_kernel<<<(unsigned)digits, 256, 0, s>>>(hist, (int)L.nblk, dtot);
+    rs_scatter_kernel<<<(unsigned)L.nblk, RS_THREADS, 0, s>>>(ka, va, F, shift, digits, (int)L.nblk, hist, dtot, kb,
+                                                              vb);
+    count_launch(3);
+    uint32_t* t = ka; ka = kb; kb = t;
+    t = va; va = vb; vb = t;
+  }
+  // sorted keys / fetch ids are now in (ka, va)
+  seg_count_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, segtot);
+  scan_excl_kernel<<<1, 1024, 0, s>>>(segtot, L.nseg_blk, nullptr);
+  seg_write_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, segtot, (int)L.nseg_blk, seg_id, seg_start, uniq,
+                                                        n_seg);
+  count_launch(3);
+  *ka_out = ka;
+  *va_out = va;
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_sort_unique(const RowGradK& R, const RowGradLayout& L, char* ws, int* inv, cudaStream_t s) {
+  cudaError_t e;
+  if ((e = cudaMemsetAsync(ws + L.o_small, 0, 512, s)) != cudaSuccess) return e;   // counters and status word
+  if (R.F == 0) return cudaSuccess;
+  uint32_t *ka, *va;
+  if ((e = sort_segments(R, L, ws, &ka, &va, reinterpret_cast<int*>(ws + L.o_uniq), s)) != cudaSuccess) return e;
+  rg_inverse_kernel<<<(unsigned)((R.F + 255) / 256), 256, 0, s>>>(va, reinterpret_cast<const int*>(ws + L.o_seg_id),
+                                                                  R.F, inv);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, int* uniq_out, float* rows_out,
+                           int* n_unique_out, float* sq_out, const RowAdagrad* ada, cudaStream_t s) {
+  int* small = reinterpret_cast<int*>(ws + L.o_small);
+  int* n_seg = small + 1, *ticket = small + 2;
+  uint32_t* ka = nullptr;
+  uint32_t* va = nullptr;
   int* seg_id = reinterpret_cast<int*>(ws + L.o_seg_id);
   int* seg_start = reinterpret_cast<int*>(ws + L.o_seg_start);
   int* uniq = uniq_out ? uniq_out : reinterpret_cast<int*>(ws + L.o_uniq);
@@ -594,25 +654,7 @@ cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, 
   if ((e = cudaMemsetAsync(small, 0, 512, s)) != cudaSuccess) return e;   // counters and status word
   const int64_t F = R.F;
   if (F > 0) {
-    rg_keys_kernel<<<(unsigned)((F + 255) / 256), 256, 0, s>>>(R, ka, va, err);
-    count_launch();
-    const int digits = 1 << L.rbits;
-    for (int p = 0; p < L.passes; ++p) {
-      const int shift = p * L.rbits;
-      rs_hist_kernel<<<(unsigned)L.nblk, RS_THREADS, 0, s>>>(ka, F, shift, digits, (int)L.nblk, hist);
-      rs_digit_scan_kernel<<<(unsigned)digits, 256, 0, s>>>(hist, (int)L.nblk, dtot);
-      rs_scatter_kernel<<<(unsigned)L.nblk, RS_THREADS, 0, s>>>(ka, va, F, shift, digits, (int)L.nblk, hist, dtot,
-                                                                kb, vb);
-      count_launch(3);
-      uint32_t* t = ka; ka = kb; kb = t;
-      t = va; va = vb; vb = t;
-    }
-    // sorted keys / fetch ids are now in (ka, va)
-    seg_count_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, segtot);
-    scan_excl_kernel<<<1, 1024, 0, s>>>(segtot, L.nseg_blk, nullptr);
-    seg_write_kernel<<<(unsigned)L.nseg_blk, 256, 0, s>>>(ka, F, segtot, (int)L.nseg_blk, seg_id, seg_start, uniq,
-                                                          n_seg);
-    count_launch(3);
+    if ((e = sort_segments(R, L, ws, &ka, &va, uniq, s)) != cudaSuccess) return e;
     const unsigned wblocks = (unsigned)((L.chunks + 7) / 8);
     ML_VPL(vpl_for(R.d), (rg_rows_kernel<VP><<<wblocks, 256, 0, s>>>(R, seg_id, va, seg_start, rows, rowsq,
                                                                       spill)));

@@ -17,6 +17,7 @@ struct RowGradK {
   int64_t Nslot;    // pool rows (slot ids must lie in [0, Nslot))
   int kworld;       // > 1: sort key of slot s = (s % kworld) * kstride + s / kworld
   int64_t kstride;
+  int64_t kadd;     // > 0: sort key of slot s = (s + kadd) % Nslot (the read slot under shuffle_reads)
   int hk;       // heads * top_k
   int d;        // d_value
 };
@@ -42,5 +43,10 @@ struct RowAdagrad {
 RowGradLayout rowgrad_layout(int64_t F, int64_t N, int d);
 cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, int* uniq_out, float* rows_out,
                            int* n_unique_out, float* sq_out, const RowAdagrad* ada, cudaStream_t s);
+
+// Sort + segments only: the distinct keys in ascending order at L.o_uniq,
+// their count at small[1] (L.o_small), and for every fetch f its segment:
+// inv[f] = index of its key in uniq (out-of-range slots: -1).
+cudaError_t launch_sort_unique(const RowGradK& R, const RowGradLayout& L, char* ws, int* inv, cudaStream_t s);
 
 }  // namespace ml

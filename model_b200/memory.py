@@ -70,8 +70,6 @@ class MemoryPool:
         # memory.py:95-96
         assert self.d_key % 2 == 0, "d_key must be even (split into two halves)"
         assert self.top_k <= self.n_sub_keys
-        if self.host_pool:
-            raise NotImplementedError("host_pool tables are not served by the B200 memory layer")
 
     @property
     def pool_size(self) -> int:
@@ -115,13 +113,21 @@ class MemoryPool:
             gumbel = -torch.log(-torch.log(u))
         return _cuda_f32(gumbel, "gumbel")
 
-    def _pool_args(self, params, M, device, *, train, noise_scale, shuffle_reads, rngs, gumbel, stats):
-        p = params["params"] if "params" in params else params
-        sub_keys = _cuda_f32(p["sub_keys"], "sub_keys")
+    def _values(self, p) -> torch.Tensor:
+        """The value table: a CUDA tensor, or with ``host_pool`` the named
+        host table's page-locked rows (memory.py:90-92, 180-183)."""
+        if self.host_pool:
+            from .host_table import get
+            return get(self.host_pool).values
         values = p["values"]
         if not values.is_cuda:
             raise TypeError("values must be a CUDA tensor (no CPU path)")
-        values = values.contiguous()
+        return values.contiguous()
+
+    def _pool_args(self, params, M, device, *, train, noise_scale, shuffle_reads, rngs, gumbel, stats):
+        p = params["params"] if "params" in params else params
+        sub_keys = _cuda_f32(p["sub_keys"], "sub_keys")
+        values = self._values(p)
         log_t = _cuda_f32(torch.as_tensor(p["log_temperature"], device=device).reshape(1), "log_temperature")
         H, k, n = self.heads, self.top_k, self.n_sub_keys
         keep = dict(sub_keys=sub_keys, values=values, log_t=log_t)
@@ -173,18 +179,21 @@ class MemoryPool:
         M = int(math.prod(lead)) if lead else 1
         device = queries.device
         p = variables["params"] if "params" in variables else variables
-        cfg = self.config(M, p["values"].dtype)
+        cfg = self.config(M, self._values(p).dtype)
         a, keep = self._pool_args(variables, M, device, train=train, noise_scale=noise_scale,
                                   shuffle_reads=shuffle_reads, rngs=rngs, gumbel=gumbel, stats=stats)
         out = torch.empty(*lead, self.d_value, dtype=torch.float32, device=device)
         a.queries = queries.data_ptr()
         a.out = out.data_ptr()
         nbytes = C.c_size_t()
-        L.check(L.lib().memlayer_pool_workspace_size(C.byref(cfg), C.byref(nbytes)), "memlayer_pool_workspace_size")
+        lib = L.lib()
+        # host_pool: the GPU fetches each distinct row from host memory once per call
+        size_fn, fwd_fn = ((lib.memlayer_host_table_workspace_size, lib.memlayer_pool_forward_host_table)
+                           if self.host_pool else (lib.memlayer_pool_workspace_size, lib.memlayer_pool_forward))
+        L.check(size_fn(C.byref(cfg), C.byref(nbytes)), "workspace size")
         ws = _workspace(nbytes.value, device)
         s = (stream or torch.cuda.current_stream(device)).cuda_stream
-        L.check(L.lib().memlayer_pool_forward(C.byref(cfg), C.byref(a), ws.data_ptr(), nbytes.value, s),
-                "memlayer_pool_forward")
+        L.check(fwd_fn(C.byref(cfg), C.byref(a), ws.data_ptr(), nbytes.value, s), "pool forward")
         if check:
             _raise_device_status(cfg, ws, s)
         return out, self._aux(keep, lead, stats)
@@ -201,6 +210,13 @@ class MemoryLayer:
     pool: MemoryPool
     d_model: int
     layer: int = 1
+
+    def __post_init__(self):
+        if self.pool.host_pool:
+            # the fused block reads the table from HBM; a host table is read
+            # through MemoryPool.apply (memlayer_pool_forward_host_table)
+            raise NotImplementedError("MemoryLayer needs the value table in device memory; use MemoryPool.apply "
+                                      "for a host_pool table")
 
     def init(self, seed: int = 0, device="cuda", values_dtype=torch.float32) -> Dict[str, Any]:
         g = torch.Generator(device="cpu").manual_seed(seed + 1)
