@@ -57,10 +57,11 @@ def parse():
                     help="host-buffer calls in flight (on as many streams) in the e2e measurement")
     ap.add_argument("--host-chunks", type=int, default=1,
                     help="chunks of the host-buffer pipeline timed as e2e (memlayer_layer_forward_host)")
-    ap.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg0",
+    ap.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4", "host"], default="cfg0",
                     help="cfg0 (default, the driver's line): configs[0] layer forward; cfg2: configs[2] decode "
                          "latency on a 67M-slot fp16 table; cfg3: configs[3] billion-slot bf16 table "
-                         "row-sharded over >= 4 GPUs; cfg4: configs[4] forward + fetched-row Adagrad")
+                         "row-sharded over >= 4 GPUs; cfg4: configs[4] forward + fetched-row Adagrad; host: configs[2] "
+                         "shapes with the table in page-locked host memory")
     ap.add_argument("--split", action="store_true",
                     help="N>1: one call per step with the exchange in two overlapped token halves "
                          "(MEMLAYER_PHASE_SPLIT); default: the three phases one after another")
@@ -779,6 +780,74 @@ def run_cfg4(args, rank=0, world=1):
                 + ("; table row-sharded, owner-sharded row update over NVLink" if world > 1 else "")})
 
 
+def run_host(args):
+    """configs[2] shapes (H 4, top_k 16, d_key 128, d_value 256 fp16) with the
+    value table in page-locked host memory (the reference's host tier,
+    memory.py:180-183): n_sub_keys 4096 (16.8 M slots x 512 B = 8.6 GB
+    pinned; smaller when the host has less than 4x that available).  Per call
+    latency at batch 1, 8 and 64 and the 8192-token throughput; host-link
+    bytes = distinct rows x 512 B (each crosses once per call)."""
+    import torch
+
+    from model_b200 import _lib as L
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    n_sub, H, k, dk, d = 4096, 4, 16, 128, 256
+    avail = 0
+    with open("/proc/meminfo") as f:
+        for line in f:
+            if line.startswith("MemAvailable:"):
+                avail = int(line.split()[1]) * 1024
+    while n_sub > 512 and 4 * n_sub * n_sub * d * 2 > avail:
+        n_sub //= 2
+    N = n_sub * n_sub
+    table = torch.empty(N, d, dtype=torch.float16, pin_memory=True)
+    g = torch.Generator(device=device).manual_seed(0)
+    step = 1 << 20
+    for s0 in range(0, N, step):     # filled from the GPU: fast and seeded
+        s1 = min(s0 + step, N)
+        table[s0:s1].copy_((torch.randn(s1 - s0, d, device=device, generator=g) * 0.02).half())
+    torch.cuda.synchronize()
+    sub_keys = torch.randn(H, 2, n_sub, dk // 2, device=device, generator=g) * (1 / 128) ** 0.5
+    log_t = torch.tensor([math.log(10.0)], device=device)
+    stream = torch.cuda.current_stream(device)
+    res = {}
+    for M in (1, 8, 64, 8192):
+        cfg = L.MemlayerConfig(tokens=M, heads=H, n_sub_keys=n_sub, d_key=dk, d_value=d, top_k=k, d_model=256,
+                               values_dtype=L.F16, routing_noise=1.0, min_temperature=10.0, max_temperature=100.0)
+        q = torch.randn(M, H, dk, device=device, generator=g)
+        out = torch.empty(M, d, device=device)
+        sl = torch.empty(M, H, k, dtype=torch.int32, device=device)
+        w = torch.empty(M, H, k, device=device)
+        a = L.MemlayerPoolArgs(queries=q.data_ptr(), sub_keys=sub_keys.data_ptr(), log_temperature=log_t.data_ptr(),
+                               values=table.data_ptr(), out=out.data_ptr(), slots=sl.data_ptr(), weights=w.data_ptr())
+        nb = C.c_size_t()
+        L.check(L.lib().memlayer_host_table_workspace_size(C.byref(cfg), C.byref(nb)), "host table ws")
+        ws = torch.empty(nb.value, dtype=torch.uint8, device=device)
+        f = L.lib().memlayer_pool_forward_host_table
+        for _ in range(args.warmup):
+            L.check(f(C.byref(cfg), C.byref(a), ws.data_ptr(), nb.value, stream.cuda_stream), "host table fwd")
+        torch.cuda.synchronize()
+        reps = max(args.steps, 20) if M < 8192 else args.steps
+        e0, e1 = _events(torch, 2)
+        e0.record(stream)
+        for _ in range(reps):
+            L.check(f(C.byref(cfg), C.byref(a), ws.data_ptr(), nb.value, stream.cuda_stream), "host table fwd")
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        U = int(torch.unique(sl).numel())
+        res[str(M)] = {"ms_per_call": ms, "tokens_per_s": M / (ms * 1e-3), "distinct_rows": U,
+                       "fetches": M * H * k, "host_link_gbs": U * d * 2 / (ms * 1e-3) / 1e9}
+    big = res["8192"]
+    W = dict(WORKLOAD, name="host_table_cfg2_shapes", n_sub_keys=n_sub, d_key=dk, values_dtype="f16",
+             tokens_per_gpu=8192)
+    return _common_line(W, 1, args.steps, args.warmup, big["ms_per_call"], big["tokens_per_s"], "tokens/s", "f16", {
+        "scaling": "weak", "per_batch": res, "table_bytes_pinned_host": N * d * 2,
+        "note": "value table in page-locked host memory; each distinct row crosses the host link once per call; "
+                "no L2 flush (the host table is not cached in HBM)"})
+
+
 def run_cfg2(args):
     """configs[2] decode: n_sub_keys 8192 (67,108,864 slots x 256 fp16 =
     34.4 GB, HBM-resident), H 4, top_k 16, d_key 128, d_model 256; one call
@@ -947,6 +1016,8 @@ def main():
         line = run_cfg1(args)
     elif args.workload == "cfg2":
         line = run_cfg2(args)
+    elif args.workload == "host":
+        line = run_host(args)
     elif args.workload == "cfg3":
         line = run_cfg3(args, rank, world)
     else:
