@@ -1128,7 +1128,11 @@ int32_t memlayer_pool_forward_host_table(const memlayer_config* cfg, const memla
   R.kadd = D.shuffle ? D.N / 2 + 1 : 0;   // the read slot (memory.py:179)
   int* inv = reinterpret_cast<int*>(ws + P.o_inv);
   char* sort_ws = ws + P.o_sort;
-  ML_TRY(launch_sort_unique(R, P.L, sort_ws, inv, s));
+  if (R.F <= TABLE_SMALL_F)   // decode-size calls: one CTA instead of the radix passes
+    ML_TRY(launch_table_unique_small(a->slots, (int)R.F, D.N, R.kadd, reinterpret_cast<int*>(sort_ws + P.L.o_uniq),
+                                     reinterpret_cast<int*>(sort_ws + P.L.o_small) + 1, inv, s));
+  else
+    ML_TRY(launch_sort_unique(R, P.L, sort_ws, inv, s));
   int* err = reinterpret_cast<int*>(ws + 256);   // the forward's status word
   ML_TRY(launch_table_fetch(D, table, reinterpret_cast<const int*>(sort_ws + P.L.o_uniq),
                             reinterpret_cast<const int*>(sort_ws + P.L.o_small) + 1, P.cap, ws + P.o_stage, err, s));

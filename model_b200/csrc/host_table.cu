@@ -23,6 +23,85 @@ namespace ml {
 
 namespace {
 
+// Distinct read slots of a small call (F <= TABLE_SMALL_F fetches) in one
+// CTA: (read slot, fetch) pairs bitonic-sorted in shared memory (the fetch
+// index makes the order stable), segment heads counted with a block scan.
+// Writes what the radix pipeline writes: uniq[u] ascending, *n_seg and
+// inv[fetch] = u.
+__global__ void __launch_bounds__(1024) table_unique_small_kernel(const int* __restrict__ slots, int F, int64_t N,
+                                                                  int64_t kadd, int* __restrict__ uniq,
+                                                                  int* __restrict__ n_seg, int* __restrict__ inv) {
+  __shared__ unsigned long long kv[TABLE_SMALL_F];
+  __shared__ int wsum[32];
+  int P2 = 1;
+  while (P2 < F) P2 <<= 1;
+  for (int i = threadIdx.x; i < P2; i += blockDim.x) {
+    unsigned long long v = ~0ull;
+    if (i < F) {
+      const int64_t s = slots[i];
+      const int64_t key = kadd > 0 ? (s + kadd) % N : s;   // the read slot (memory.py:179)
+      v = ((unsigned long long)key << 32) | (unsigned)i;
+    }
+    kv[i] = v;
+  }
+  __syncthreads();
+  for (int size = 2; size <= P2; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P2; i += blockDim.x) {
+        const int l = i ^ stride;
+        if (l > i) {
+          const unsigned long long a = kv[i], b = kv[l];
+          const bool up = (i & size) == 0;
+          if ((a > b) == up) {
+            kv[i] = b;
+            kv[l] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  // each thread: 4 consecutive sorted entries; exclusive scan of the heads
+  constexpr int PER = TABLE_SMALL_F / 1024;
+  const int i0 = threadIdx.x * PER;
+  int head[PER], cnt = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = i0 + j;
+    head[j] = (i < F) && (i == 0 || (kv[i] >> 32) != (kv[i - 1] >> 32));
+    cnt += head[j];
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(FULL, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < (int)(blockDim.x >> 5) ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(FULL, w, o);
+      if (lane >= o) w += y;
+    }
+    wsum[lane] = w;   // inclusive over warps
+  }
+  __syncthreads();
+  int run = incl - cnt + (warp > 0 ? wsum[warp - 1] : 0);   // heads before this thread's entries
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = i0 + j;
+    if (i >= F) break;
+    run += head[j];
+    const int u = run - 1;
+    if (head[j]) uniq[u] = (int)(kv[i] >> 32);
+    inv[(int)(kv[i] & 0xffffffffu)] = u;
+  }
+  if (threadIdx.x == blockDim.x - 1) *n_seg = wsum[31];
+}
+
 // Rows of row_bytes (a multiple of 16) as uint4 words; ROWS rows per warp
 // iteration so that several loads are in flight on the host link.
 template <int ROWS>
@@ -164,6 +243,14 @@ cudaError_t mix_ch(const Dims& D, const VT* staging, const int* inv, const float
 }  // namespace
 
 int64_t table_elem_bytes(int vdtype) { return vdtype == MEMLAYER_F32 ? 4 : 2; }
+
+cudaError_t launch_table_unique_small(const int* slots, int F, int64_t N, int64_t kadd, int* uniq, int* n_seg,
+                                      int* inv, cudaStream_t s) {
+  if (F < 1 || F > TABLE_SMALL_F) return cudaErrorInvalidValue;
+  table_unique_small_kernel<<<1, 1024, 0, s>>>(slots, F, N, kadd, uniq, n_seg, inv);
+  count_launch();
+  return cudaGetLastError();
+}
 
 cudaError_t launch_table_fetch(const Dims& D, const void* table, const int* uniq, const int* n_seg, int64_t cap,
                                void* staging, int* err, cudaStream_t s) {

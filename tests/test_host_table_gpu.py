@@ -29,9 +29,10 @@ def _pair(n_sub, H, dk, d, k, dtype, seed=0):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 @pytest.mark.parametrize("shuffle", [False, True])
-def test_host_table_matches_device_table(dtype, shuffle):
+@pytest.mark.parametrize("M", [5, 128, 300])   # 160 / 4096 fetches: one-CTA dedup; 9600: radix sort
+def test_host_table_matches_device_table(dtype, shuffle, M):
     pool_d, pool_h, params, table = _pair(64, 4, 64, 64, 8, dtype)
-    q = torch.randn(300, 4, 64, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+    q = torch.randn(M, 4, 64, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
     out_d, aux_d = pool_d.apply(params, q, shuffle_reads=shuffle, check=True)
     pv = {k: v for k, v in params["params"].items() if k != "values"}   # no values param with a host pool
     out_h, aux_h = pool_h.apply({"params": pv}, q, shuffle_reads=shuffle, check=True)
