@@ -170,6 +170,14 @@ __device__ __forceinline__ void st_shared_if(float* p, float v, bool pred) {
                : "memory");
 }
 
+// Predicated 8-byte shared store of (a, b) (no branch).
+__device__ __forceinline__ void st_shared2_if(float2* p, float a, float b, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.shared.v2.f32 [%0], {%1, %2};\n\t}" ::"r"(
+                   tc::smem_u32(p)),
+               "f"(a), "f"(b), "r"((int)pred)
+               : "memory");
+}
+
 template <bool QS>
 __device__ __forceinline__ float score_of(uint32_t bits, float T, float ql) {
   float sc = __fmul_rn(__uint_as_float(bits), T);   // memory.py:150
@@ -185,7 +193,7 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&x)[64]) {
 }
 
 template <bool QS>
-__device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, float ql, bool owner,
+__device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, float ql, bool owner, bool first,
                                            float (&rv)[16], int (&ri)[16], float* buf) {
   // A. 16th largest of the 32 group maxima (groups of 4 cosines)
   float lo[16], hi[16];
@@ -211,9 +219,9 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
   float tau = score_of<QS>(__float_as_uint(g16), T, ql);
   if (!owner) tau = INFINITY;
 
-  // B. candidate scores (>= tau) into this thread's buffer slots.  Slot
-  // offsets come from per-8-value prefix counts, so the running count is
-  // a chain of 16 additions, not 128.
+  // B. candidate (score, key) pairs (score >= tau) into this thread's slots,
+  // in key order.  Slot offsets come from per-8-value prefix counts, so the
+  // running count is a chain of 16 additions, not 128.
   int cnt = 0;
 #pragma unroll
   for (int part = 0; part < 2; ++part) {
@@ -230,7 +238,11 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
         run += sc[i] >= tau;
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) st_shared_if(buf + ((cnt + off[i]) & 31) * 256, sc[i], sc[i] >= tau);
+      for (int i = 0; i < 8; ++i) {
+        const int slot = (cnt + off[i]) & 31;
+        st_shared_if(buf + slot * 256, sc[i], sc[i] >= tau);
+        st_shared_if(buf + (32 + slot) * 256, __int_as_float(key0 + part * 64 + 8 * g + i), sc[i] >= tau);
+      }
       cnt += run;
     }
   }
@@ -249,32 +261,17 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
 #pragma unroll
   for (int i = 0; i < 16; ++i) tstar = fminf(tstar, fmaxf(va[i], vb[15 - i]));
 
-  // D. (score, key) of every value >= t*, in key order (16 unless t* is tied)
+  // D. the candidates >= t*, compacted in place (still in key order; 16
+  // unless t* is tied)
   int cnt2 = 0;
   const float tst = owner ? tstar : INFINITY;
-#pragma unroll
-  for (int part = 0; part < 2; ++part) {
-    uint32_t x[64];
-    tmem_ld64(taddr + part * 64, x);
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      float sc[8];
-      int off[8], run = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        sc[i] = score_of<QS>(x[8 * g + i], T, ql);
-        off[i] = run;
-        run += sc[i] >= tst;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const bool c = sc[i] >= tst;
-        const int slot = (cnt2 + off[i]) & 15;
-        st_shared_if(buf + slot * 256, sc[i], c);
-        st_shared_if(buf + (16 + slot) * 256, __int_as_float(key0 + part * 64 + 8 * g + i), c);
-      }
-      cnt2 += run;
-    }
+#pragma unroll 8
+  for (int j = 0; j < 32; ++j) {
+    const float v = buf[j * 256], kf = buf[(32 + j) * 256];
+    const bool c = (j < cnt) && (v >= tst);
+    st_shared_if(buf + (cnt2 & 15) * 256, v, c);
+    st_shared_if(buf + (32 + (cnt2 & 15)) * 256, kf, c);
+    cnt2 += c;
   }
   if (__any_sync(FULL, owner && cnt2 != 16)) return false;
   float pv[16];
@@ -282,10 +279,18 @@ __device__ __forceinline__ bool fast_top16(uint32_t taddr, int key0, float T, fl
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     pv[i] = owner ? buf[i * 256] : -INFINITY;
-    pc[i] = owner ? __float_as_int(buf[(16 + i) * 256]) : (1 << 30) + i;
+    pc[i] = owner ? __float_as_int(buf[(32 + i) * 256]) : (1 << 30) + i;
   }
   sort_desc_pairs<16>(pv, pc);
-  merge_top_pairs<16>(rv, ri, pv, pc);
+  if (first) {   // the row's list is still empty
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      rv[i] = pv[i];
+      ri[i] = pc[i];
+    }
+  } else {
+    merge_top_pairs<16>(rv, ri, pv, pc);
+  }
   return true;
 }
 
@@ -427,7 +432,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         bool fast_done = false;
         if constexpr (FAST16) {
           if (ce - cb == HALF_BN_FULL)
-            fast_done = fast_top16<QS>(taddr + cb, key0 + cb, T, ql, owner, R.v, R.ix, fbuf);
+            fast_done = fast_top16<QS>(taddr + cb, key0 + cb, T, ql, owner, j == 0, R.v, R.ix, fbuf);
         }
         if (!fast_done) {
         // pass A: a lower bound of this half-chunk's k-th best selection
@@ -684,18 +689,26 @@ inline int bn_for(const Dims& D) {
   return D.n >= cap ? cap : ((D.n + 15) / 16) * 16;
 }
 
+// The exact top-16 fast path runs for clean k <= 16 selections without
+// balance statistics.
+inline bool fast_path(const Dims& D, bool bal) { return D.kmax == 16 && !D.noisy && !bal; }
+
 // Epilogue shared memory: the row-merge buffer, aliased with the 32-slot
-// per-thread candidate buffer of the k <= 16 clean fast path.
-inline uint32_t merge_bytes(const Dims& D) {
+// per-thread (score, key) candidate buffer of the fast path.
+inline uint32_t merge_bytes(const Dims& D, bool bal) {
   const uint32_t per = 8u + (D.noisy ? 4u : 0u);
   const uint32_t merge = TC_M * D.kmax * per + TC_M * 8u;
-  const uint32_t fast = 32u * 4u * (TC_THREADS - 64);
+  const uint32_t fast = fast_path(D, bal) ? 64u * 4u * (TC_THREADS - 64) : 0u;
   return merge > fast ? merge : fast;
 }
 
-TcShape tc_shape(const Dims& D) {
+// 16-element K stages (64-byte swizzle): three 48 KB stages leave room for
+// the fast path's 64 KB candidate buffer.
+constexpr int SCORE_BK = 16;
+
+TcShape tc_shape(const Dims& D, bool bal) {
   TcShape S;
-  S.P = tc::pipe_shape(bn_for(D), D.half, merge_bytes(D));
+  S.P = tc::pipe_shape(bn_for(D), D.half, merge_bytes(D, bal), SCORE_BK);
   S.m_tiles = (int)((D.M + TC_M - 1) / TC_M);
   S.mt0 = 0;
   S.n_chunks = (D.n + S.P.BN - 1) / S.P.BN;
@@ -706,7 +719,7 @@ TcShape tc_shape(const Dims& D) {
 template <int KM, bool NOISY, bool BAL, bool QS>
 cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaStream_t s, int mt0, int mtn,
                         int max_ctas) {
-  TcShape S = tc_shape(D);
+  TcShape S = tc_shape(D, BAL);
   if (mtn > 0) {   // a range of 128-token tiles
     S.mt0 = mt0;
     S.m_tiles = mtn;
@@ -715,11 +728,11 @@ cudaError_t launch_tc_t(const Dims& D, const Work& W, const float* gumbel, cudaS
   CUtensorMap m[4];
   cudaError_t e;
   const uint64_t arows = (uint64_t)D.M * D.H * 2, brows = (uint64_t)D.n * D.H * 2;
-  if ((e = make_tmap_f32(&m[0], W.q_hi, arows, D.half, TC_M)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[1], W.q_lo, arows, D.half, TC_M)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[2], W.k_hi, brows, D.half, S.P.BN)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[3], W.k_lo, brows, D.half, S.P.BN)) != cudaSuccess) return e;
-  const size_t smem = 1024 + (size_t)S.merge_off + merge_bytes(D);
+  if ((e = make_tmap_f32(&m[0], W.q_hi, arows, D.half, TC_M, SCORE_BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[1], W.q_lo, arows, D.half, TC_M, SCORE_BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[2], W.k_hi, brows, D.half, S.P.BN, SCORE_BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[3], W.k_lo, brows, D.half, S.P.BN, SCORE_BK)) != cudaSuccess) return e;
+  const size_t smem = 1024 + (size_t)S.merge_off + merge_bytes(D, BAL);
   auto kern = score_topk_tc_kernel<KM, NOISY, BAL, QS>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
     return e;
