@@ -172,9 +172,21 @@ bool overlap_enabled() {
   return !(v && v[0] == '0');
 }
 
-// score CTAs beside the first half's gather (of 148 SMs); 100 / 120 / 132 /
-// 140 measured 0.290 / 0.291 / 0.292 / 0.294 ms per configs[0] step
-constexpr int OVERLAP_SCORE_CTAS = 100;
+// Score CTAs of the second part, beside the first part's gather (of 148
+// SMs).  The first part is a whole number of rounds of (tile, codebook)
+// units over every SM.  configs[0] (64 tiles x 8 codebooks): first part 37
+// tiles (296 units = 2 rounds), second part on 108 CTAs: 0.2745 ms per
+// step, against 0.2786 for 32 tiles / 100 CTAs, 0.2747 for 37 / 100,
+// 0.2750 for 37 / 74, 0.2835 for 32 / 128 and 0.2774 for 18 / 123.
+constexpr int OVERLAP_SCORE_CTAS = 108;
+
+// First-part tiles: half of the units rounded up to whole rounds over `sms` CTAs.
+int overlap_first_tiles(int mt_all, int hc, int sms) {
+  const int units = mt_all * hc;
+  const int rounds = (units / 2 + sms - 1) / sms;
+  const int mta = rounds * sms / hc;
+  return mta >= 1 && mta < mt_all ? mta : mt_all / 2;
+}
 
 // The push of a row-sharded call: one launch per token half; after_a (if
 // set) is recorded between the halves.
@@ -206,7 +218,10 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
         return MEMLAYER_ERR_CUDA;
       }
     auto body = [&]() -> int {
-      const int mta = mt_all / 2;
+      int dev = 0, sms = 148;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const int mta = overlap_first_tiles(mt_all, D.H * 2, sms);
       const int64_t ha = (int64_t)mta * SCORE_TM;
       if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
       if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
