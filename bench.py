@@ -890,10 +890,38 @@ def run_cfg2(args):
         res[B] = {"p50_us": t[len(t) // 2], "p90_us": t[int(len(t) * 0.9)], "tokens_per_s": B / (t[len(t) // 2] * 1e-6),
                   "stages_us": {"prep_projections": st(0, 2), "score_topk": st(2, 3), "combine_gather": st(3, 4),
                                 "finalize_out": st(4, 5)}}
+        # the same layer call as one CUDA graph per decode step (model_b200.generate.LayerDecodeStep);
+        # host-observed rate: each step issued, run and waited for, as a token-by-token loop does
+        from model_b200 import MemoryLayer, MemoryPool
+        from model_b200.generate import LayerDecodeStep, decode_steps_per_second
+        pool = MemoryPool(n_sub_keys=W["n_sub_keys"], heads=W["heads"], d_key=W["d_key"], d_value=W["d_value"],
+                          top_k=W["top_k"])
+        layer = MemoryLayer(pool, d_model=W["d_model"], layer=1)
+        lp = {"router_1": {"kernel": x["w_router"], "bias": x["b_router"]},
+              "mem_gate_1": {"kernel": x["w_gate"], "bias": x["b_gate"]},
+              "mem_out_1": {"kernel": x["w_out"], "bias": x["b_out"]},
+              "pool": {"sub_keys": x["sub_keys"], "values": x["values"], "log_temperature": x["log_t"]}}
+        gstep = LayerDecodeStep(layer, lp, B)
+        estep = LayerDecodeStep(layer, lp, B, graph=False)
+        for _ in range(args.warmup):
+            gstep.step(x["h"])
+            estep.step(x["h"])
+        ge = _events(torch, 2 * args.steps)
+        for i in range(args.steps):
+            ge[2 * i].record(stream)
+            gstep.step(x["h"], stream)
+            ge[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+        gt = sorted(ge[2 * i].elapsed_time(ge[2 * i + 1]) * 1000 for i in range(args.steps))
+        res[B]["graph_p50_us"] = gt[len(gt) // 2]
+        res[B]["host_steps_per_s"] = {"eager": decode_steps_per_second(estep, 200),
+                                      "graph": decode_steps_per_second(gstep, 200)}
     return _common_line(W, 1, args.steps, args.warmup, res[64]["p50_us"] / 1000, res[64]["tokens_per_s"],
                         "tokens/s", "f16", {"scaling": "n/a", "decode": res,
                                             "note": "value = batch 64; per-step device time, L2 not flushed "
-                                                    "(decode steps run back to back)"})
+                                                    "(decode steps run back to back); graph_p50_us: the same "
+                                                    "call replayed as a CUDA graph; host_steps_per_s: steps "
+                                                    "issued and waited for one at a time"})
 
 
 def run_cfg3(args, rank, world):
