@@ -184,6 +184,17 @@ int32_t memlayer_layer_forward_host(const memlayer_config* cfg, const memlayer_l
  * Has no counterpart in the reference (its errors are Python exceptions). */
 int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* workspace, int32_t* code, void* stream);
 
+/* memlayer_layer_forward for a call whose sub-key normalisation and
+ * Dense-kernel preparation already ran on this workspace: the previous call
+ * on `workspace` was memlayer_layer_forward (or this function) with the
+ * same cfg, sub_keys, log_temperature, Dense kernels and biases, unchanged
+ * since.  Only the hidden state and what follows from it are recomputed;
+ * results equal memlayer_layer_forward's.  For decode loops (one call per
+ * generated token on fixed weights; no counterpart in the reference, whose
+ * jitted step recomputes everything).  Single GPU. */
+int32_t memlayer_layer_forward_prepared(const memlayer_config* cfg, const memlayer_layer_args* args, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
 /* ---- Row-sharded value table over the GPUs of one node -------------------
  * No counterpart in the reference, which replicates every parameter,
  * the value table included, on each device of its data-parallel mesh

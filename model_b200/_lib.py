@@ -221,6 +221,9 @@ def lib() -> C.CDLL:
         L.memlayer_pool_forward_host_table.restype = C.c_int32
         L.memlayer_pool_forward_host_table.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerPoolArgs),
                                                        C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_layer_forward_prepared.restype = C.c_int32
+        L.memlayer_layer_forward_prepared.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
+                                                      C.c_void_p, C.c_size_t, C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

@@ -553,8 +553,8 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
     if (route) {
       ML_TRY(mark(pa, 0, s));
       if (!later_chunk && (st = prep_keys(D, cfg, pa, W, s))) return st;
-      ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, W.qraw, D.M, D.H * D.dk, D.dm, false, s));
-      ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, W.gate, D.M, D.d, D.dm, true, s));
+      ML_TRY(launch_gemm2(a->h, a->w_router, a->b_router, W.qraw, D.H * D.dk, false,       // model.py:110-111
+                          a->w_gate, a->b_gate, W.gate, D.d, true, D.M, D.dm, s));          // model.py:118
       ML_TRY(mark(pa, 1, s));
       ML_TRY(launch_normalize_queries(D, W.qraw, qn, W.qlen, W.q_hi, W.q_lo, s));
       ML_TRY(mark(pa, 2, s));
@@ -1189,6 +1189,26 @@ int32_t memlayer_revive_dead_keys(const memlayer_config* cfg, const memlayer_rev
   ML_TRY(launch_revive(a->sub_keys, a->usage, a->queries, a->query_tokens, a->pick, a->noise, D.H * 2, D.n, D.half,
                        a->threshold, a->noise_scale, a->dead, a->moment0, a->moment1, (cudaStream_t)stream));
   return MEMLAYER_OK;
+}
+
+// ---- layer forward reusing the previous call's preparation ----
+
+int32_t memlayer_layer_forward_prepared(const memlayer_config* cfg, const memlayer_layer_args* a, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, true);
+  if (st) return st;
+  if (!a) return MEMLAYER_ERR_BAD_POINTER;
+  Flags f;
+  f.layer = true;
+  f.balance = a->pool.balance_loss != nullptr;
+  const size_t need = layout(D, f, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  Work W;
+  layout(D, f, (char*)workspace, &W);
+  ML_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), (cudaStream_t)stream));   // this call's status word
+  return layer_impl(cfg, a, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, MEMLAYER_PHASE_ALL, true);
 }
 
 // ---- host-buffer layer forward ----

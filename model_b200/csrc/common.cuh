@@ -228,5 +228,10 @@ cudaError_t launch_prep_layer(const Dims& D, const Work& W, const float* sub_key
                               const float* w_gate, const float* b_gate, const float* w_out, cudaStream_t s);
 cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float* C, int64_t M, int N, int K,
                         bool silu, cudaStream_t s);
+// Two products of the same A (C0 = A B0 (+ bias0, silu), C1 = A B1 ...): one
+// launch for decode-size M, else two launch_gemm calls.
+cudaError_t launch_gemm2(const float* A, const float* B0, const float* bias0, float* C0, int N0, bool silu0,
+                         const float* B1, const float* bias1, float* C1, int N1, bool silu1, int64_t M, int K,
+                         cudaStream_t s);
 
 }  // namespace ml

@@ -154,12 +154,26 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 // shared memory (deterministic); up to GV_M rows per CTA.
 constexpr int GV_M = 8;
 
-__global__ void __launch_bounds__(256) gemv_f32_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                                                       const float* __restrict__ bias, float* __restrict__ C,
-                                                       int64_t M, int N, int K, int silu) {
+struct GemvOut {
+  const float* B;      // [K, N]
+  const float* bias;   // [N] or nullptr
+  float* C;            // [M, N]
+  int N, silu;
+};
+
+// Up to two products of the same A in one launch: column blocks
+// [0, nb0) compute out0, the rest out1 (the router and gate Dense layers of
+// a decode step share the hidden state).
+__global__ void __launch_bounds__(256) gemv_f32_kernel(const float* __restrict__ A, GemvOut out0, GemvOut out1,
+                                                       int nb0, int64_t M, int K) {
   __shared__ float part[8][GV_M][32];
+  const bool second = (int)blockIdx.x >= nb0;
+  const float* __restrict__ B = second ? out1.B : out0.B;
+  const float* __restrict__ bias = second ? out1.bias : out0.bias;
+  float* __restrict__ C = second ? out1.C : out0.C;
+  const int N = second ? out1.N : out0.N, silu = second ? out1.silu : out0.silu;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int n = blockIdx.x * 32 + lane;
+  const int n = ((int)blockIdx.x - (second ? nb0 : 0)) * 32 + lane;
   const int64_t m0 = (int64_t)blockIdx.y * GV_M;
   const int kper = (K + 7) / 8, k0 = w * kper, k1 = min(K, k0 + kper);
   float acc[GV_M];
@@ -195,13 +209,29 @@ cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float
                         bool silu, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   if (M <= 4 * GV_M) {
-    gemv_f32_kernel<<<dim3((N + 31) / 32, (unsigned)((M + GV_M - 1) / GV_M)), 256, 0, s>>>(A, B, bias, C, M, N, K,
-                                                                                         silu ? 1 : 0);
+    const GemvOut o{B, bias, C, N, silu ? 1 : 0};
+    const int nb = (N + 31) / 32;
+    gemv_f32_kernel<<<dim3(nb, (unsigned)((M + GV_M - 1) / GV_M)), 256, 0, s>>>(A, o, o, nb, M, K);
     count_launch();
     return cudaGetLastError();
   }
   dim3 grid((N + GB_N - 1) / GB_N, (unsigned)((M + GB_M - 1) / GB_M));
   gemm_f32_kernel<<<grid, 256, 0, s>>>(A, B, bias, C, M, N, K, silu ? 1 : 0);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm2(const float* A, const float* B0, const float* bias0, float* C0, int N0, bool silu0,
+                         const float* B1, const float* bias1, float* C1, int N1, bool silu1, int64_t M, int K,
+                         cudaStream_t s) {
+  if (M == 0) return cudaSuccess;
+  if (M > 4 * GV_M) {
+    cudaError_t e = launch_gemm(A, B0, bias0, C0, M, N0, K, silu0, s);
+    return e != cudaSuccess ? e : launch_gemm(A, B1, bias1, C1, M, N1, K, silu1, s);
+  }
+  const GemvOut o0{B0, bias0, C0, N0, silu0 ? 1 : 0}, o1{B1, bias1, C1, N1, silu1 ? 1 : 0};
+  const int nb0 = (N0 + 31) / 32, nb1 = (N1 + 31) / 32;
+  gemv_f32_kernel<<<dim3(nb0 + nb1, (unsigned)((M + GV_M - 1) / GV_M)), 256, 0, s>>>(A, o0, o1, nb0, M, K);
   count_launch();
   return cudaGetLastError();
 }

@@ -9,8 +9,11 @@ product-key search, gather, gate, output projection) is built once on
 static device buffers, warmed up, and captured into a CUDA graph; each step
 copies the new hidden states in and replays the graph, so a decode step
 costs one graph launch instead of the call's host work and its kernel
-launches.  Outputs are bit-identical to ``MemoryLayer.apply`` on the same
-inputs (the same kernels run in the same order).
+launches.  The captured call is ``memlayer_layer_forward_prepared``: the
+sub-key normalisation and the Dense-kernel preparation done by the warm-up
+call stay in the workspace, since the weights do not change between decode
+steps (``refresh()`` redoes them after a weight update).  Outputs are
+bit-identical to ``MemoryLayer.apply`` on the same inputs.
 
 The backbone around the layer (embedding, attention with its KV cache,
 feed-forward blocks, logits: model.py:15-127) is not part of this package.
@@ -63,21 +66,30 @@ class LayerDecodeStep:
         self.nbytes = nbytes.value
         self.ws = _workspace(self.nbytes, device)
         self.graph = None
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            self._call(s, prepared=False)     # prepares sub-keys and Dense kernels in the workspace
+            self._call(s, prepared=True)      # sets kernel attributes outside the capture
+        s.synchronize()
         if graph:
-            s = torch.cuda.Stream(device)
-            s.wait_stream(torch.cuda.current_stream(device))
-            with torch.cuda.stream(s):
-                for _ in range(2):            # first calls set up kernel attributes outside the capture
-                    self._call(s)
-            s.synchronize()
             self.graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph, stream=s):
-                self._call(s)
-            torch.cuda.current_stream(device).wait_stream(s)
+                self._call(s, prepared=True)
+        torch.cuda.current_stream(device).wait_stream(s)
 
-    def _call(self, stream: torch.cuda.Stream) -> None:
-        L.check(L.lib().memlayer_layer_forward(C.byref(self.cfg), C.byref(self.args), self.ws.data_ptr(),
-                                               self.nbytes, stream.cuda_stream), "memlayer_layer_forward")
+    def _call(self, stream: torch.cuda.Stream, prepared: bool = True) -> None:
+        lib = L.lib()
+        f = lib.memlayer_layer_forward_prepared if prepared else lib.memlayer_layer_forward
+        L.check(f(C.byref(self.cfg), C.byref(self.args), self.ws.data_ptr(), self.nbytes, stream.cuda_stream),
+                "memlayer_layer_forward")
+
+    def refresh(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Redo the sub-key and Dense-kernel preparation after the layer's
+        weights changed in place (the graph keeps reading the same buffers)."""
+        s = stream or torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(s):
+            self._call(s, prepared=False)
 
     def step(self, h: torch.Tensor, stream: Optional[torch.cuda.Stream] = None
              ) -> Tuple[torch.Tensor, torch.Tensor, Dict[str, torch.Tensor]]:

@@ -44,3 +44,19 @@ def test_graph_step_rejects_wrong_batch():
     step = LayerDecodeStep(layer, layer.init(0), 4)
     with pytest.raises(ValueError):
         step.step(torch.zeros(5, 32, device="cuda"))
+
+
+def test_refresh_after_weight_update():
+    pool = MemoryPool(n_sub_keys=128, heads=2, d_key=64, d_value=64, top_k=8)
+    layer = MemoryLayer(pool, d_model=64, layer=1)
+    params = layer.init(0)
+    step = LayerDecodeStep(layer, params, 8)
+    h = torch.randn(8, 64, device="cuda", generator=torch.Generator("cuda").manual_seed(3))
+    with torch.no_grad():                         # an in-place weight update
+        params["pool"]["sub_keys"].mul_(-1.0)
+        params["router_1"]["kernel"].add_(0.5)
+    step.refresh()
+    y, _, aux = step.step(h)
+    y0, _, aux0 = layer.apply(params, h)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y0) and torch.equal(aux["slots"], aux0["slots"])
