@@ -512,8 +512,16 @@ def run_ours(args, W, rank, world):
     gather_stage = stages["shard_gather_alone"] if sharded else stages["combine_gather"]
     stats = torch.tensor([ms, e2e_ms, gather_stage, stages["score_topk"], e2e_serial_ms], dtype=torch.float64,
                          device=device)
+    rank_stages = None
     if world > 1:
         torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
+        # every rank's own step and stages (the step figure is their max)
+        names = sorted(stages)
+        mine = torch.tensor([statistics.mean(step_ms)] + [stages[k] for k in names], dtype=torch.float64,
+                            device=device)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        torch.distributed.all_gather(allr, mine)
+        rank_stages = [dict(zip(["step"] + names, t.tolist())) for t in allr]
     ms, e2e_ms, gather_ms, score_ms, e2e_serial_ms = stats.tolist()
     if sharded:                    # every rank's kernels are done before the peers are unmapped
         torch.cuda.synchronize()
@@ -562,6 +570,7 @@ def run_ours(args, W, rank, world):
         "gather_gbs": rows_b / (gather_ms * 1e-3) / 1e9,
         **({"nvlink_partial_gbs_per_gpu": nvlink_b / (gather_ms * 1e-3) / 1e9} if sharded else {}),
         "stages_ms": stages,
+        **({"stages_ms_per_rank": rank_stages} if rank_stages else {}),
         "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h_hosts[0].numel() * 4, "d2h_bytes_per_step": y_hosts[0].numel() * 4,
                 "api": e2e_api, "ms_per_step": e2e_ms, "calls_in_flight": inflight,
