@@ -751,9 +751,29 @@ def run_cfg4(args, rank=0, world=1):
     fwd = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
     upd = statistics.mean(e1[i].elapsed_time(e2[i]) for i in range(K))
     div = statistics.mean(e2[i].elapsed_time(e3[i]) for i in range(K))
+    # the same forward with the training-time selection noise (memory.py:155-159: a
+    # standard Gumbel sample scaled by routing_noise * noise_scale), which takes the
+    # score kernel's general top-k path
+    gum = -torch.log(-torch.log(torch.rand(T, H, 2, W["n_sub_keys"], device=device,
+                                           generator=torch.Generator(device=device).manual_seed(11))
+                                .clamp_(min=torch.finfo(torch.float32).tiny)))
+    call.args.pool.train, call.args.pool.noise_scale, call.args.pool.gumbel = 1, 1.0, gum.data_ptr()
+    for _ in range(args.warmup):
+        flush.zero_()
+        call(stream)
+    torch.cuda.synchronize()
+    n0, n1 = _events(torch, K), _events(torch, K)
+    for i in range(K):
+        flush.zero_()
+        n0[i].record(stream)
+        call(stream)
+        n1[i].record(stream)
+    torch.cuda.synchronize()
+    fwd_noisy = statistics.mean(n0[i].elapsed_time(n1[i]) for i in range(K))
+    call.args.pool.train, call.args.pool.gumbel = 0, None
     U = int(n_u.item())
     if world > 1:
-        t = torch.tensor([step, fwd, upd, div], dtype=torch.float64, device=device)
+        t = torch.tensor([step, fwd, upd, div, fwd_noisy], dtype=torch.float64, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         u_all = torch.tensor([U], dtype=torch.int64, device=device)
         torch.distributed.all_reduce(u_all)
@@ -763,7 +783,7 @@ def run_cfg4(args, rank=0, world=1):
         call.comm.close()
         if rank != 0:
             return None
-        step, fwd, upd, div = t.tolist()
+        step, fwd, upd, div, fwd_noisy = t.tolist()
         U = int(u_all.item())
     # revive_dead_keys (every revive_every steps in the reference trainer), timed on its own on copies
     from model_b200 import keys as KM
@@ -784,6 +804,7 @@ def run_cfg4(args, rank=0, world=1):
     upd_bytes = F * 8 + T * d * 4 + U * (2 * d * 4 + 8) // world
     return _common_line(W, world, K, args.warmup, step, world * T / (step * 1e-3), "tokens/s", "f32", {
         "scaling": "weak", "stages_ms": {"forward": fwd, "row_grad_adagrad": upd, "key_diversity": div},
+        "forward_with_selection_noise_ms": fwd_noisy,
         "stage_note": "max over ranks of each stage" if world > 1 else "per-stage means",
         "revive_dead_keys_ms": revive_ms, "revived": int(rdead.sum().item()),
         "unique_rows": U, "fetches": F * world, "clip_scale": float(scale.item()),

@@ -482,6 +482,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           // s > v[KM-1] and s >= tau  <=>  s >= max(tau, succ(v[KM-1]))
           const float thr = fmaxf(thr_base, succ_f32(R.v[KM - 1]));
           const float cthr = RS::CLEAN ? (owner ? succ_f32(R.cv[KM - 1]) : INFINITY) : 0.f;
+          // this row's 16 Gumbel values: four streaming 16-byte loads (read once)
+          float gv[NOISY ? 16 : 1];
+          if constexpr (NOISY) {
+            const float* gp = owner ? grow + key0 + cc : nullptr;
+            if (owner && nv == 16 && (reinterpret_cast<uintptr_t>(gp) & 15) == 0) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 v4 = __ldcs(reinterpret_cast<const float4*>(gp) + q);
+                gv[4 * q] = v4.x;
+                gv[4 * q + 1] = v4.y;
+                gv[4 * q + 2] = v4.z;
+                gv[4 * q + 3] = v4.w;
+              }
+            } else {
+#pragma unroll
+              for (int t = 0; t < 16; ++t) gv[t] = (owner && t < nv) ? gp[t] : 0.f;
+            }
+          }
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
             const float cosv = __uint_as_float(r[t]);
@@ -489,8 +507,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if constexpr (QS) score = __fmul_rn(score, ql);            // memory.py:151-152
             float s_sel = score;
             if constexpr (NOISY) {
-              const float g = (owner && t < nv) ? grow[key0 + cc + t] : 0.f;
-              s_sel = __fadd_rn(score, __fmul_rn(D.noise_coef, g));    // memory.py:158
+              s_sel = __fadd_rn(score, __fmul_rn(D.noise_coef, gv[t]));   // memory.py:158
               scr[t] = score;
             }
             sel[t] = s_sel;
