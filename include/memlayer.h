@@ -191,7 +191,11 @@ int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* worksp
  * since.  Only the hidden state and what follows from it are recomputed;
  * results equal memlayer_layer_forward's.  For decode loops (one call per
  * generated token on fixed weights; no counterpart in the reference, whose
- * jitted step recomputes everything).  Single GPU. */
+ * jitted step recomputes everything).  Single GPU.  Returns
+ * MEMLAYER_ERR_WORKSPACE, before launching anything, when the last
+ * successful memlayer_layer_forward on `workspace` had another cfg or other
+ * sub-key, temperature or Dense-kernel pointers (in-place changes of those
+ * buffers are the caller's to track). */
 int32_t memlayer_layer_forward_prepared(const memlayer_config* cfg, const memlayer_layer_args* args, void* workspace,
                                         size_t workspace_bytes, void* stream);
 

@@ -7,6 +7,7 @@
 #include <atomic>
 
 #include <mutex>
+#include <unordered_map>
 #include <new>
 
 #include "common.cuh"
@@ -654,6 +655,39 @@ int rowgrad_setup(const memlayer_config* cfg, const memlayer_read* reads, int n_
 
 }  // namespace
 
+// What memlayer_layer_forward prepared in each workspace (sub-key
+// normalisation, Dense-kernel splits): the config and the weight pointers of
+// the last successful call, so that memlayer_layer_forward_prepared can refuse
+// a workspace prepared for other arguments.  In-place changes of the weights
+// cannot be seen here; the caller's contract covers them.
+struct Prepared {
+  memlayer_config cfg;
+  const void* ptr[8];
+};
+std::mutex g_prep_mu;
+std::unordered_map<const void*, Prepared> g_prepared;
+
+Prepared prepared_of(const memlayer_config* cfg, const memlayer_layer_args* a) {
+  Prepared p{};
+  p.cfg = *cfg;
+  const void* v[8] = {a->pool.sub_keys, a->pool.log_temperature, a->w_router, a->b_router,
+                      a->w_gate,        a->b_gate,                a->w_out,    a->b_out};
+  for (int i = 0; i < 8; ++i) p.ptr[i] = v[i];
+  return p;
+}
+
+void record_prepared(const void* ws, const memlayer_config* cfg, const memlayer_layer_args* a) {
+  std::lock_guard<std::mutex> lk(g_prep_mu);
+  g_prepared[ws] = prepared_of(cfg, a);
+}
+
+bool is_prepared(const void* ws, const memlayer_config* cfg, const memlayer_layer_args* a) {
+  const Prepared want = prepared_of(cfg, a);
+  std::lock_guard<std::mutex> lk(g_prep_mu);
+  auto it = g_prepared.find(ws);
+  return it != g_prepared.end() && memcmp(&it->second, &want, sizeof(Prepared)) == 0;
+}
+
 // MemoryPool forward on the caller's stream only: no event, no library
 // stream (the allocation-free entry point).
 int32_t pool_forward_single_stream(const memlayer_config* cfg, const memlayer_pool_args* args, void* workspace,
@@ -714,7 +748,9 @@ int32_t memlayer_pool_forward(const memlayer_config* cfg, const memlayer_pool_ar
 
 int32_t memlayer_layer_forward(const memlayer_config* cfg, const memlayer_layer_args* a, void* workspace,
                                size_t workspace_bytes, void* stream) {
-  return layer_impl(cfg, a, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, MEMLAYER_PHASE_ALL);
+  const int st = layer_impl(cfg, a, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, MEMLAYER_PHASE_ALL);
+  if (st == MEMLAYER_OK) record_prepared(workspace, cfg, a);
+  return st;
 }
 
 int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* workspace, int32_t* code, void* stream) {
@@ -1205,6 +1241,7 @@ int32_t memlayer_layer_forward_prepared(const memlayer_config* cfg, const memlay
   const size_t need = layout(D, f, nullptr, nullptr);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
     return MEMLAYER_ERR_WORKSPACE;
+  if (!is_prepared(workspace, cfg, a)) return MEMLAYER_ERR_WORKSPACE;   // not prepared for these arguments
   Work W;
   layout(D, f, (char*)workspace, &W);
   ML_TRY(cudaMemsetAsync(W.err, 0, sizeof(int), (cudaStream_t)stream));   // this call's status word

@@ -114,3 +114,15 @@ def test_pool_mirror_keeps_reference_assertions():
     import torch
     with pytest.raises(TypeError):
         pool.apply({"params": {}}, torch.zeros(3, 2, 8))  # CPU tensor: no CPU path
+
+
+def test_prepared_layer_call_refuses_an_unprepared_workspace():
+    # no memlayer_layer_forward ran on this workspace: refused before any launch
+    c = cfg(tokens=4)
+    nb = C.c_size_t()
+    assert L.lib().memlayer_layer_workspace_size(C.byref(c), C.byref(nb)) == L.OK
+    la = L.MemlayerLayerArgs(h=256, w_router=256, w_gate=256, w_out=256, y=256,
+                             pool=L.MemlayerPoolArgs(sub_keys=256, log_temperature=256, values=256))
+    assert L.lib().memlayer_layer_forward_prepared(C.byref(c), C.byref(la), 1 << 20, nb.value,
+                                                   None) == L.ERR_WORKSPACE
+    assert L.lib().memlayer_layer_forward_prepared(C.byref(c), None, 1 << 20, nb.value, None) == L.ERR_BAD_POINTER
