@@ -5,7 +5,8 @@ KumarDev7/model:
 
 * ``memory_pool_model/memory.py:30-57``   l2-normalise and top-k helpers
 * ``memory_pool_model/memory.py:119-227`` ``MemoryPool.__call__``
-* ``memory_pool_model/model.py:108-120``  router Dense, SiLU gate, output Dense
+* ``memory_pool_model/model.py:108-120``  router Dense, SiLU gate, output Dense, and
+  the gradients through that block (``layer_backward``)
 * ``memory_pool_model/train.py:146-206``  fetched-row gradients (unique + segment sum),
   single device and data-parallel (local merge, all-gather, second merge)
 * ``memory_pool_model/train.py:396-416``  global-norm clip + row-wise Adagrad
@@ -260,6 +261,107 @@ def layer_forward(cfg: PoolConfig, h: np.ndarray, w_router, b_router, sub_keys, 
     gate = silu(dense(h, w_gate, b_gate))                               # model.py:118
     y = dense((mem * gate).astype(F32), w_out, b_out)                   # model.py:119
     return y, mem, aux
+
+
+def layer_backward(cfg: PoolConfig, h, w_router, b_router, sub_keys, log_t, values, w_gate, b_gate, w_out,
+                   b_out, dy, *, balance_coef: float = 0.0, route_through_pool: bool = False,
+                   train: bool = False, gumbel=None, noise_scale: float = 1.0, shuffle_reads: bool = False):
+    """Gradients of sum(dy * y) + balance_coef * balance_loss through one
+    memory layer (model.py:110-119 with memory.py:133-214), as the reference
+    trainer's jax.value_and_grad computes them with sparse_grad (the value
+    table gets none; its rows' gradient is the read-output gradient
+    ``probe``, model.py:114-115).  Routing (top-k indices) comes from the
+    float32 forward and carries no gradient; the temperature clamp is
+    straight-through (memory.py:141-146); the balance term reaches every
+    sub-key through the softmax over all keys (memory.py:210-214).
+    route_through_pool: the gate reads stop_gradient(h) (model.py:116-117).
+    Computed in float64.  Returns a dict of float64 arrays: h, w_router,
+    b_router, sub_keys, log_temperature, w_gate, b_gate, w_out, b_out, probe
+    ([T, d_value]), plus the forward's slots and weights."""
+    f64 = np.float64
+    H, n, k = cfg.heads, cfg.n_sub_keys, cfg.top_k
+    half = cfg.d_key // 2
+    T_ = h.shape[0]
+    q_raw = dense(h, w_router, b_router).reshape(T_, H, cfg.d_key)
+    r = route(cfg, q_raw, sub_keys, log_t, train, gumbel, noise_scale)
+    w = softmax(r["slot_scores"]).astype(f64)                                # memory.py:178
+    N = cfg.pool_size
+    read = (r["slots"] + N // 2 + 1) % N if shuffle_reads else r["slots"]    # memory.py:179
+    V = np.asarray(values, f64)
+    fetched = V[read]                                                        # [T, H, k, d]
+    mem = np.einsum("mhk,mhkd->md", w, fetched)                              # memory.py:192
+    hh = np.asarray(h, f64)
+    zg = hh @ np.asarray(w_gate, f64) + (0.0 if b_gate is None else np.asarray(b_gate, f64))
+    sig = 1.0 / (1.0 + np.exp(-zg))
+    gate = zg * sig                                                          # model.py:118
+    dy = np.asarray(dy, f64)
+    out = {}
+    # model.py:119  y = (mem * gate) W_out + b_out
+    memg = mem * gate
+    out["w_out"] = memg.T @ dy
+    out["b_out"] = dy.sum(0)
+    dmemg = dy @ np.asarray(w_out, f64).T
+    dmem = dmemg * gate
+    out["probe"] = dmem                                                      # model.py:114-115
+    dgate = dmemg * mem
+    dzg = dgate * sig * (1.0 + zg * (1.0 - sig))                             # silu'
+    out["w_gate"] = hh.T @ dzg
+    out["b_gate"] = dzg.sum(0)
+    dh = np.zeros_like(hh) if route_through_pool else dzg @ np.asarray(w_gate, f64).T
+    # memory.py:192  d weights = dmem . fetched row, then the softmax (:178)
+    dw = np.einsum("md,mhkd->mhk", dmem, fetched)
+    dss = w * (dw - np.sum(w * dw, axis=-1, keepdims=True))
+    # memory.py:166-172  slot score = scores[0, idx_a] + scores[1, idx_b]
+    dscores = np.zeros((T_, H, 2, n), f64)
+    mi = np.arange(T_)[:, None, None]
+    hi = np.arange(H)[None, :, None]
+    np.add.at(dscores, (mi, hi, 0, r["idx_a"]), dss)
+    np.add.at(dscores, (mi, hi, 1, r["idx_b"]), dss)
+    Tv = f64(r["temperature"])
+    cos = np.asarray(r["cos"], f64)
+    qn = np.asarray(r["q"], f64)
+    q_len = np.asarray(r["q_len"], f64)
+    # memory.py:205-214  balance_loss = n * mean_{h,c} sum_i f_i P_i
+    dcos_bal = np.zeros_like(cos)
+    if balance_coef != 0.0:
+        st = pool_stats(cfg, r, train and cfg.routing_noise > 0 and gumbel is not None)
+        fcount = np.asarray(st["balance_f"], f64)                             # [H, 2, n], no gradient
+        dP = balance_coef * n / (H * 2) * fcount
+        p = np.asarray(r["scores"], f64) if cfg.balance_temperature_grad else cos * Tv
+        p = p - p.max(-1, keepdims=True)
+        sm = np.exp(p)
+        sm /= sm.sum(-1, keepdims=True)
+        dp = sm * (dP[None] - np.sum(sm * dP[None], axis=-1, keepdims=True)) / T_
+        if cfg.balance_temperature_grad:
+            dscores += dp
+        else:
+            dcos_bal = dp * Tv                                               # sg(T): no temperature gradient
+    # memory.py:150-152  scores = cos * T (* q_len)
+    scale = Tv * (q_len if cfg.query_scale else 1.0)
+    dcos = dscores * scale + dcos_bal
+    dT = np.sum(dscores * cos * (q_len if cfg.query_scale else 1.0))
+    out["log_temperature"] = dT * Tv                                         # straight-through clamp
+    dq_len = np.sum(dscores * cos * Tv, axis=-1, keepdims=True) if cfg.query_scale else 0.0
+    # memory.py:149  cos = q_hat . k_hat
+    keys_n = np.asarray(l2_normalize(sub_keys), f64)
+    dqn = np.einsum("mhcn,hcnd->mhcd", dcos, keys_n)
+    dkn = np.einsum("mhcn,mhcd->hcnd", dcos, qn)
+    # memory.py:136-138, 139  normalisation backward (x * rsqrt(|x|^2 + 1e-6))
+    q = q_raw.reshape(T_, H, 2, half).astype(f64)
+    rq = 1.0 / np.sqrt(np.sum(q * q, -1, keepdims=True) + 1e-6)
+    dq = rq * dqn - rq ** 3 * np.sum(q * dqn, -1, keepdims=True) * q
+    if cfg.query_scale:
+        dq = dq + dq_len * q * rq / np.sqrt(half)
+    x = np.asarray(sub_keys, f64)
+    rk = 1.0 / np.sqrt(np.sum(x * x, -1, keepdims=True) + 1e-6)
+    out["sub_keys"] = rk * dkn - rk ** 3 * np.sum(x * dkn, -1, keepdims=True) * x
+    dq = dq.reshape(T_, H * cfg.d_key)
+    out["w_router"] = hh.T @ dq                                              # model.py:110
+    out["b_router"] = dq.sum(0)
+    out["h"] = dh + dq @ np.asarray(w_router, f64).T
+    out["slots"] = r["slots"]
+    out["weights"] = w.astype(F32)
+    return out
 
 
 # --------------------------------------------------------------------------
