@@ -388,6 +388,43 @@ typedef struct {
  * and then clamped, as the reference's gather does. */
 int32_t memlayer_revive_dead_keys(const memlayer_config* cfg, const memlayer_revive_args* args, void* stream);
 
+/* ---- Layer backward (training) --------------------------------------------
+ * Gradients of sum(dy * y) + balance_coef * balance_loss through one memory
+ * layer (model.py:110-119 with memory.py:133-214), as the reference trainer's
+ * jax.value_and_grad computes them with sparse_grad: the value table gets no
+ * gradient; its rows' gradient is the read-output gradient `probe`
+ * (model.py:114-115), the input of memlayer_fetched_row_grads.  Routing
+ * (the forward's slots, weights and clean top-k counts) carries no gradient;
+ * the temperature clamp is straight-through.  Outputs may be NULL. */
+typedef struct {
+  const float* dy;               /* [M, d_model] d loss / d y (model.py:119's term) */
+  float balance_coef;            /* the trainer's balance_coef (train.py:328); 0: no balance term */
+  int32_t route_through_pool;    /* the gate reads stop_gradient(h) (model.py:116-117) */
+  const void* forward_workspace; /* the forward call's workspace, unchanged since (its clean top-k
+                                    counts feed the balance term); needed when balance_coef != 0 */
+  float* dh;                     /* [M, d_model] */
+  float* dw_router;              /* [d_model, H*d_key] */
+  float* db_router;              /* [H*d_key] */
+  float* dsub_keys;              /* [H, 2, n, d_key/2] */
+  float* dlog_temperature;       /* [1] */
+  float* dw_gate;                /* [d_model, d] */
+  float* db_gate;                /* [d] */
+  float* dw_out;                 /* [d, d_model] */
+  float* db_out;                 /* [d_model] */
+  float* probe;                  /* [M, d] d loss / d read output */
+} memlayer_layer_grads;
+
+/* Workspace bytes of memlayer_layer_backward (balance != 0: with the balance term). */
+int32_t memlayer_layer_backward_workspace_size(const memlayer_config* cfg, int32_t balance, size_t* bytes);
+
+/* `args` = the forward's layer arguments (h, Dense kernels and biases,
+ * sub_keys, log_temperature, values, its slots / weights outputs, and
+ * balance_loss non-NULL when balance_coef != 0).  d_key/2 must be a
+ * multiple of 4 and at most 128. */
+int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer_args* args,
+                                const memlayer_layer_grads* grads, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* ---- Owner-sharded row update (row-sharded table, training) -------------
  * Replaces fetched_row_grads_sharded + the replicated update
  * (memory_pool_model/train.py:175-206, 378-399): with the table row-sharded

@@ -117,6 +117,25 @@ class MemlayerReviveArgs(C.Structure):
     ]
 
 
+class MemlayerLayerGrads(C.Structure):
+    _fields_ = [
+        ("dy", C.c_void_p),
+        ("balance_coef", C.c_float),
+        ("route_through_pool", C.c_int32),
+        ("forward_workspace", C.c_void_p),
+        ("dh", C.c_void_p),
+        ("dw_router", C.c_void_p),
+        ("db_router", C.c_void_p),
+        ("dsub_keys", C.c_void_p),
+        ("dlog_temperature", C.c_void_p),
+        ("dw_gate", C.c_void_p),
+        ("db_gate", C.c_void_p),
+        ("dw_out", C.c_void_p),
+        ("db_out", C.c_void_p),
+        ("probe", C.c_void_p),
+    ]
+
+
 DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "MMA wait timed out",
                  14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
                  21: "sub-key id out of range", 22: "sharded row id out of range",
@@ -224,6 +243,12 @@ def lib() -> C.CDLL:
         L.memlayer_layer_forward_prepared.restype = C.c_int32
         L.memlayer_layer_forward_prepared.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
                                                       C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_layer_backward_workspace_size.restype = C.c_int32
+        L.memlayer_layer_backward_workspace_size.argtypes = [C.POINTER(MemlayerConfig), C.c_int32,
+                                                             C.POINTER(C.c_size_t)]
+        L.memlayer_layer_backward.restype = C.c_int32
+        L.memlayer_layer_backward.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
+                                              C.POINTER(MemlayerLayerGrads), C.c_void_p, C.c_size_t, C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

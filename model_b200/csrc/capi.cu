@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "host_table.cuh"
+#include "layer_bwd.cuh"
 #include "keys.cuh"
 #include "rowgrad.cuh"
 #include "shard.cuh"
@@ -1224,6 +1225,181 @@ int32_t memlayer_revive_dead_keys(const memlayer_config* cfg, const memlayer_rev
   if (a->query_tokens < 1) return MEMLAYER_ERR_BAD_SHAPE;
   ML_TRY(launch_revive(a->sub_keys, a->usage, a->queries, a->query_tokens, a->pick, a->noise, D.H * 2, D.n, D.half,
                        a->threshold, a->noise_scale, a->dead, a->moment0, a->moment1, (cudaStream_t)stream));
+  return MEMLAYER_OK;
+}
+
+// ---- layer backward ----
+
+namespace {
+
+struct BwdPlan {
+  RowGradLayout L;
+  int64_t F, cap;
+  int64_t o_qraw, o_qn, o_qlen, o_keys, o_scal, o_zg, o_dmemg, o_memg, o_dzg, o_dqhat, o_dqlen, o_dT, o_ent_s,
+      o_ent_w, o_rg, o_uniq, o_rows, o_dkhat, o_dq, o_cbal, o_dTrow, o_dqlrow, bytes;
+};
+
+BwdPlan bwd_plan(const Dims& D, bool balance) {
+  BwdPlan P{};
+  const int64_t M = D.M, HC = D.H * 2, half = D.half, NK = HC * D.n;
+  P.F = M * HC * D.k;
+  P.L = rowgrad_layout(P.F, NK, (int)half);
+  P.cap = P.F < NK ? P.F : NK;
+  int64_t o = 512;   // small words; the status word at 256, as in the forward layouts
+  auto take = [&](int64_t b) {
+    const int64_t at = o;
+    o += (int64_t)up((size_t)(b > 0 ? b : 0));
+    return at;
+  };
+  P.o_qraw = take(4 * M * D.H * D.dk);
+  P.o_qn = take(4 * M * HC * half);
+  P.o_qlen = take(4 * M * HC);
+  P.o_keys = take(4 * NK * half);
+  P.o_scal = take(16);
+  P.o_zg = take(4 * M * D.d);
+  P.o_dmemg = take(4 * M * D.d);
+  P.o_memg = take(4 * M * D.d);
+  P.o_dzg = take(4 * M * D.d);
+  P.o_dqhat = take(4 * M * HC * half);
+  P.o_dqlen = take(4 * M * HC);
+  P.o_dT = take(4 * M * D.H);
+  P.o_ent_s = take(4 * P.F);
+  P.o_ent_w = take(4 * P.F);
+  P.o_rg = take(P.L.bytes);
+  P.o_uniq = take(4 * P.cap);
+  P.o_rows = take(4 * P.cap * half);
+  P.o_dkhat = take(4 * NK * half);
+  P.o_dq = take(4 * M * HC * half);
+  P.o_cbal = balance ? take(4 * HC * M * D.n) : 0;
+  P.o_dTrow = balance ? take(4 * HC * M) : 0;
+  P.o_dqlrow = balance ? take(4 * M * HC) : 0;
+  P.bytes = o;
+  return P;
+}
+
+int check_bwd(const memlayer_config* cfg, Dims* D) {
+  int st = check_config(cfg, D, true);
+  if (st) return st;
+  if (D->half % 4 || D->half > 128) return MEMLAYER_ERR_UNSUPPORTED;
+  if ((int64_t)D->H * 2 * D->n >= (1LL << 31) || D->M * D->H * 2 * D->k >= (1LL << 31)) return MEMLAYER_ERR_BAD_SHAPE;
+  return MEMLAYER_OK;
+}
+
+}  // namespace
+
+int32_t memlayer_layer_backward_workspace_size(const memlayer_config* cfg, int32_t balance, size_t* bytes) {
+  Dims D;
+  int st = check_bwd(cfg, &D);
+  if (st) return st;
+  if (!bytes) return MEMLAYER_ERR_BAD_POINTER;
+  *bytes = (size_t)bwd_plan(D, balance != 0).bytes;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer_args* a, const memlayer_layer_grads* g,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_bwd(cfg, &D);
+  if (st) return st;
+  if (!a || !g) return MEMLAYER_ERR_BAD_POINTER;
+  const memlayer_pool_args* pa = &a->pool;
+  if (!pa->sub_keys || !pa->log_temperature || !pa->values) return MEMLAYER_ERR_BAD_POINTER;
+  if (D.M > 0 && (!a->h || !a->w_router || !a->w_gate || !a->w_out || !pa->slots || !pa->weights || !g->dy))
+    return MEMLAYER_ERR_BAD_POINTER;
+  if (!aligned16(pa->values) && D.vdtype != MEMLAYER_F32) return MEMLAYER_ERR_BAD_POINTER;
+  const bool balance = g->balance_coef != 0.f;
+  if (balance && (!g->forward_workspace || !pa->balance_loss)) return MEMLAYER_ERR_BAD_POINTER;
+  resolve_noise(&D, cfg, pa);
+  const BwdPlan P = bwd_plan(D, balance);
+  if (!workspace || workspace_bytes < (size_t)P.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  const cudaStream_t s = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  auto F32p = [&](int64_t off) { return reinterpret_cast<float*>(ws + off); };
+  int* small = reinterpret_cast<int*>(ws);
+  ML_TRY(cudaMemsetAsync(ws, 0, 512, s));
+  const int64_t M = D.M, H = D.H, HC = H * 2, half = D.half, n = D.n, d = D.d, dm = D.dm, NR = H * D.dk;
+  if (M == 0) return MEMLAYER_OK;
+  float* qn = F32p(P.o_qn);
+  float* qlen = F32p(P.o_qlen);
+  float* keys_n = F32p(P.o_keys);
+  float* scal = F32p(P.o_scal);
+  // forward activations: unit keys and temperature (memory.py:139-146), q (model.py:110), gate input (:118)
+  ML_TRY(launch_prep_keys(D, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature, keys_n,
+                          nullptr, nullptr, scal, small + 64, small + 65, s));
+  ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, F32p(P.o_qraw), M, (int)NR, (int)dm, false, s));
+  ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, nullptr, nullptr, s));
+  ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, F32p(P.o_zg), M, (int)d, (int)dm, false, s));
+  // d (mem * gate) = dy W_out^T (model.py:119)
+  ML_TRY(launch_gemm_strided(g->dy, dm, 1, a->w_out, 1, dm, F32p(P.o_dmemg), d, M, d, dm, false, s));
+  float* probe = g->probe ? g->probe : F32p(P.o_dmemg);   // in place when the caller keeps no probe
+  LayerBwd B{pa->slots, pa->weights, F32p(P.o_dmemg), F32p(P.o_zg), qn, qlen, keys_n, scal, probe, F32p(P.o_memg),
+             F32p(P.o_dzg), F32p(P.o_dqhat), F32p(P.o_dqlen), F32p(P.o_dT),
+             reinterpret_cast<int*>(ws + P.o_ent_s), F32p(P.o_ent_w)};
+  ML_TRY(launch_route_bwd(D, pa->values, B, s));
+  float* dkhat = F32p(P.o_dkhat);
+  if (balance) {
+    // memory.py:205-214: the softmax over every sub-key, from the recomputed cosines
+    Flags ff;
+    ff.layer = true;
+    ff.balance = true;
+    Work FW;
+    layout(D, ff, (char*)g->forward_workspace, &FW);
+    float* C = F32p(P.o_cbal);
+    for (int hc = 0; hc < HC; ++hc)   // cos[hc] = Q_hat[hc] K_hat[hc]^T
+      ML_TRY(launch_gemm_strided(qn + hc * half, HC * half, 1, keys_n + (int64_t)hc * n * half, 1, half,
+                                 C + (int64_t)hc * M * n, n, M, n, half, false, s));
+    ML_TRY(launch_bal_rows(D, C, FW.clean_cnt, qlen, scal, g->balance_coef, F32p(P.o_dTrow), F32p(P.o_dqlrow), s));
+    for (int hc = 0; hc < HC; ++hc) {
+      // d q_hat[hc] += d cos[hc] K_hat[hc];  d k_hat[hc] = d cos[hc]^T Q_hat[hc]
+      ML_TRY(launch_gemm_strided(C + (int64_t)hc * M * n, n, 1, keys_n + (int64_t)hc * n * half, half, 1,
+                                 F32p(P.o_dqhat) + hc * half, HC * half, M, half, n, true, s));
+      ML_TRY(launch_gemm_strided(C + (int64_t)hc * M * n, 1, n, qn + hc * half, HC * half, 1,
+                                 dkhat + (int64_t)hc * n * half, half, n, half, M, false, s));
+    }
+  } else {
+    ML_TRY(cudaMemsetAsync(dkhat, 0, sizeof(float) * HC * n * half, s));
+  }
+  // the sparse sub-key gradient: sum over entries of d cos * q_hat row, per sub-key
+  RowGradK R{};
+  R.n_reads = 1;
+  R.slots[0] = reinterpret_cast<const int*>(ws + P.o_ent_s);
+  R.weights[0] = F32p(P.o_ent_w);
+  R.grad[0] = qn;
+  R.off[0] = 0;
+  R.off[1] = P.F;
+  R.F = P.F;
+  R.N = HC * n;
+  R.Nslot = HC * n;
+  R.hk = D.k;
+  R.d = (int)half;
+  ML_TRY(launch_rowgrad(R, P.L, ws + P.o_rg, reinterpret_cast<int*>(ws + P.o_uniq), F32p(P.o_rows), nullptr,
+                        nullptr, nullptr, s));
+  ML_TRY(launch_scatter_rows(reinterpret_cast<const int*>(ws + P.o_uniq), F32p(P.o_rows), P.cap, HC * n, (int)half,
+                             dkhat, s));
+  if (g->dsub_keys)
+    ML_TRY(launch_norm_bwd(keys_n, dkhat, nullptr, HC * n, (int)half, pa->sub_keys, nullptr, nullptr, g->dsub_keys,
+                           s));
+  // d q (memory.py:136-138)
+  float* dq = F32p(P.o_dq);
+  ML_TRY(launch_norm_bwd(qn, F32p(P.o_dqhat), qlen, M * HC, (int)half, nullptr, D.qscale ? F32p(P.o_dqlen) : nullptr,
+                         (balance && D.btgrad && D.qscale) ? F32p(P.o_dqlrow) : nullptr, dq, s));
+  if (g->dlog_temperature)
+    ML_TRY(launch_dlogt(F32p(P.o_dT), M * H, (balance && D.btgrad) ? F32p(P.o_dTrow) : nullptr,
+                        (balance && D.btgrad) ? HC * M : 0, scal, g->dlog_temperature, s));
+  // Dense-layer gradients (model.py:110, 118, 119)
+  if (g->dw_router) ML_TRY(launch_gemm_strided(a->h, 1, dm, dq, NR, 1, g->dw_router, NR, dm, NR, M, false, s));
+  if (g->db_router) ML_TRY(launch_colsum(dq, M, NR, NR, g->db_router, s));
+  if (g->dw_gate)
+    ML_TRY(launch_gemm_strided(a->h, 1, dm, F32p(P.o_dzg), d, 1, g->dw_gate, d, dm, d, M, false, s));
+  if (g->db_gate) ML_TRY(launch_colsum(F32p(P.o_dzg), M, d, d, g->db_gate, s));
+  if (g->dw_out) ML_TRY(launch_gemm_strided(F32p(P.o_memg), 1, d, g->dy, dm, 1, g->dw_out, dm, d, dm, M, false, s));
+  if (g->db_out) ML_TRY(launch_colsum(g->dy, M, dm, dm, g->db_out, s));
+  if (g->dh) {
+    ML_TRY(launch_gemm_strided(dq, NR, 1, a->w_router, 1, NR, g->dh, dm, M, dm, NR, false, s));
+    if (!g->route_through_pool)
+      ML_TRY(launch_gemm_strided(F32p(P.o_dzg), d, 1, a->w_gate, 1, d, g->dh, dm, M, dm, d, true, s));
+  }
   return MEMLAYER_OK;
 }
 

@@ -1,0 +1,44 @@
+// Backward of one memory layer: internal launchers (layer_bwd.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace ml {
+
+// Buffers of the routing backward kernel (one CTA per token).
+struct LayerBwd {
+  const int* slots;        // [M, H, k] the forward's slots
+  const float* weights;    // [M, H, k] the forward's weights
+  const float* dmemg;      // [M, d] d loss / d (mem * gate)
+  const float* zg;         // [M, d] gate pre-activation h W_gate + b_gate
+  const float* qn;         // [M, H, 2, half] unit query halves
+  const float* qlen;       // [M, H, 2]
+  const float* keys_n;     // [H * 2, n, half] unit sub-keys
+  const float* scal;       // [1] temperature
+  float* probe;            // [M, d] d loss / d read output
+  float* memg;             // [M, d] mem * gate
+  float* dzg;              // [M, d]
+  float* dqhat;            // [M, H, 2, half]
+  float* dqlen;            // [M, H, 2]
+  float* dT_part;          // [M * H]
+  int* ent_slot;           // [M, H, 2, k] (codebook * n + sub-key) of each slot-score gradient entry
+  float* ent_w;            // [M, H, 2, k] its d cos
+};
+
+// C (+)= op(A) op(B) with A(i, k) = A[i sai + k sak], B(k, j) = B[k sbk + j sbj], C[i ldc + j].
+cudaError_t launch_gemm_strided(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
+                                float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
+                                cudaStream_t s);
+cudaError_t launch_colsum(const float* X, int64_t rows, int64_t cols, int64_t ld, float* out, cudaStream_t s);
+cudaError_t launch_route_bwd(const Dims& D, const void* values, const LayerBwd& B, cudaStream_t s);
+// C: [H * 2][M][n] cosines in, d cos out (balance term)
+cudaError_t launch_bal_rows(const Dims& D, float* C, const float* cnt, const float* qlen, const float* scal, float coef,
+                            float* dT_row, float* dql_row, cudaStream_t s);
+cudaError_t launch_norm_bwd(const float* xhat, const float* dxhat, const float* len, int64_t rows, int half,
+                            const float* raw, const float* dlen, const float* dlen2, float* dx, cudaStream_t s);
+cudaError_t launch_scatter_rows(const int* uniq, const float* rows, int64_t cap, int64_t N, int half, float* dst,
+                                cudaStream_t s);
+cudaError_t launch_dlogt(const float* a, int64_t na, const float* b, int64_t nb, const float* scal, float* out,
+                         cudaStream_t s);
+
+}  // namespace ml

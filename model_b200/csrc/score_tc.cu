@@ -170,14 +170,6 @@ __device__ __forceinline__ void st_shared_if(float* p, float v, bool pred) {
                : "memory");
 }
 
-// Predicated 8-byte shared store of (a, b) (no branch).
-__device__ __forceinline__ void st_shared2_if(float2* p, float a, float b, bool pred) {
-  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.shared.v2.f32 [%0], {%1, %2};\n\t}" ::"r"(
-                   tc::smem_u32(p)),
-               "f"(a), "f"(b), "r"((int)pred)
-               : "memory");
-}
-
 template <bool QS>
 __device__ __forceinline__ float score_of(uint32_t bits, float T, float ql) {
   float sc = __fmul_rn(__uint_as_float(bits), T);   // memory.py:150

@@ -274,11 +274,68 @@ class MemoryLayer:
                "temperature": keep["temperature"].reshape(())}
         return y, aux
 
+    def apply_train(self, params, h: torch.Tensor, *, train: bool = True, noise_scale: float = 1.0,
+                    shuffle_reads: bool = False, rngs=None, gumbel=None,
+                    stream: Optional[torch.cuda.Stream] = None, check: bool = False):
+        """The training forward (routing statistics on) keeping what
+        ``backward`` needs: returns (y, mem, aux, ctx)."""
+        y, mem, aux, ctx = self._forward(params, h, train=train, noise_scale=noise_scale,
+                                         shuffle_reads=shuffle_reads, rngs=rngs, gumbel=gumbel, stats=True,
+                                         stream=stream, check=check)
+        return y, mem, aux, ctx
+
+    def backward(self, ctx: Dict[str, Any], dy: torch.Tensor, *, balance_coef: float = 0.0,
+                 route_through_pool: bool = False, stream: Optional[torch.cuda.Stream] = None,
+                 check: bool = False) -> Dict[str, torch.Tensor]:
+        """Gradients of sum(dy * y) + balance_coef * balance_loss for the
+        forward of ``ctx`` (memlayer_layer_backward): the reference's
+        parameter names (``router_i`` / ``mem_gate_i`` / ``mem_out_i`` kernel
+        and bias, ``pool`` sub_keys and log_temperature), ``h``, and
+        ``probe`` = d loss / d read output, the row update's input."""
+        P = self.pool
+        dev = ctx["device"]
+        M, dm, d = ctx["M"], self.d_model, P.d_value
+        dy = _cuda_f32(dy, "dy").reshape(M, dm)
+        g = {"h": torch.empty(M, dm, device=dev), "w_router": torch.empty(dm, P.heads * P.d_key, device=dev),
+             "b_router": torch.empty(P.heads * P.d_key, device=dev),
+             "sub_keys": torch.empty(P.heads, 2, P.n_sub_keys, P.d_key // 2, device=dev),
+             "log_temperature": torch.empty(1, device=dev), "w_gate": torch.empty(dm, d, device=dev),
+             "b_gate": torch.empty(d, device=dev), "w_out": torch.empty(d, dm, device=dev),
+             "b_out": torch.empty(dm, device=dev), "probe": torch.empty(M, d, device=dev)}
+        ga = L.MemlayerLayerGrads(dy=dy.data_ptr(), balance_coef=float(balance_coef),
+                                  route_through_pool=int(bool(route_through_pool)),
+                                  forward_workspace=ctx["ws"].data_ptr(), dh=g["h"].data_ptr(),
+                                  dw_router=g["w_router"].data_ptr(), db_router=g["b_router"].data_ptr(),
+                                  dsub_keys=g["sub_keys"].data_ptr(), dlog_temperature=g["log_temperature"].data_ptr(),
+                                  dw_gate=g["w_gate"].data_ptr(), db_gate=g["b_gate"].data_ptr(),
+                                  dw_out=g["w_out"].data_ptr(), db_out=g["b_out"].data_ptr(),
+                                  probe=g["probe"].data_ptr())
+        nb = C.c_size_t()
+        L.check(L.lib().memlayer_layer_backward_workspace_size(C.byref(ctx["cfg"]), int(balance_coef != 0.0),
+                                                               C.byref(nb)), "memlayer_layer_backward_workspace_size")
+        ws = _workspace(nb.value, dev)
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        L.check(L.lib().memlayer_layer_backward(C.byref(ctx["cfg"]), C.byref(ctx["la"]), C.byref(ga), ws.data_ptr(),
+                                                nb.value, s), "memlayer_layer_backward")
+        if check:
+            _raise_device_status(ctx["cfg"], ws, s)
+        i = self.layer
+        return {"h": g["h"], f"router_{i}": {"kernel": g["w_router"], "bias": g["b_router"]},
+                f"mem_gate_{i}": {"kernel": g["w_gate"], "bias": g["b_gate"]},
+                f"mem_out_{i}": {"kernel": g["w_out"], "bias": g["b_out"]},
+                "pool": {"sub_keys": g["sub_keys"], "log_temperature": g["log_temperature"].reshape(())},
+                "probe": g["probe"]}
+
     def apply(self, params, h: torch.Tensor, *, train: bool = False, noise_scale: float = 1.0,
               shuffle_reads: bool = False, rngs=None, gumbel=None, stats: bool = False,
               stream: Optional[torch.cuda.Stream] = None, check: bool = False):
         """Returns (y [..., d_model], mem [..., d_value], aux); y is the term
         model.py:119 adds into the layer's update."""
+        y, mem, aux, _ = self._forward(params, h, train=train, noise_scale=noise_scale, shuffle_reads=shuffle_reads,
+                                       rngs=rngs, gumbel=gumbel, stats=stats, stream=stream, check=check)
+        return y, mem, aux
+
+    def _forward(self, params, h, *, train, noise_scale, shuffle_reads, rngs, gumbel, stats, stream, check):
         P = self.pool
         h = _cuda_f32(h, "h")
         lead = tuple(h.shape[:-1])
@@ -304,4 +361,6 @@ class MemoryLayer:
                 "memlayer_layer_forward")
         if check:
             _raise_device_status(cfg, ws, s)
-        return y, mem, P._aux(keep, lead, stats)
+        ctx = {"cfg": cfg, "la": la, "ws": ws, "keep": keep, "w": w, "h": h, "y": y, "mem": mem, "M": M,
+               "device": device}
+        return y, mem, P._aux(keep, lead, stats), ctx

@@ -1,0 +1,84 @@
+"""GPU parity of the memory-layer backward (memlayer_layer_backward) against
+the oracle's layer_backward (model.py:110-119 with memory.py:133-214, values
+excluded as with sparse_grad), through MemoryLayer.apply_train / backward.
+
+Each gradient must match within 1e-4 of its largest entry (float32 sums in
+fixed orders against the oracle's float64); the forward's slots are first
+checked equal to the oracle's (the gradients follow the routing)."""
+
+import numpy as np
+import pytest
+import torch
+
+from model_b200 import MemoryLayer, MemoryPool
+from oracle import memlayer_ref as ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+
+
+def _case(n, H, dk, d, k, dm, M, seed, vdt=torch.float32, query_scale=False, btgrad=False):
+    pool = MemoryPool(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=query_scale,
+                      balance_temperature_grad=btgrad, min_temperature=5.0, max_temperature=50.0)
+    layer = MemoryLayer(pool, d_model=dm, layer=1)
+    params = layer.init(seed, values_dtype=vdt)
+    with torch.no_grad():
+        params["pool"]["log_temperature"].fill_(float(np.log(12.0)))
+        for name in ("router_1", "mem_gate_1", "mem_out_1"):
+            params[name]["bias"].normal_(0.0, 0.1, generator=torch.Generator("cuda").manual_seed(seed))
+    h = torch.randn(M, dm, device="cuda", generator=torch.Generator("cuda").manual_seed(seed + 1))
+    dy = torch.randn(M, dm, device="cuda", generator=torch.Generator("cuda").manual_seed(seed + 2))
+    cfg = ref.PoolConfig(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=query_scale,
+                         balance_temperature_grad=btgrad, min_temperature=5.0, max_temperature=50.0)
+    return layer, params, h, dy, cfg
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _check(layer, params, h, dy, cfg, bal, rtp=False, gumbel=None):
+    train = gumbel is not None
+    y, mem, aux, ctx = layer.apply_train(params, h, train=train, gumbel=gumbel, check=True)
+    g = layer.backward(ctx, dy, balance_coef=bal, route_through_pool=rtp, check=True)
+    torch.cuda.synchronize()
+    p = params
+    want = ref.layer_backward(cfg, _np(h), _np(p["router_1"]["kernel"]), _np(p["router_1"]["bias"]),
+                              _np(p["pool"]["sub_keys"]), float(p["pool"]["log_temperature"]),
+                              _np(p["pool"]["values"]), _np(p["mem_gate_1"]["kernel"]), _np(p["mem_gate_1"]["bias"]),
+                              _np(p["mem_out_1"]["kernel"]), _np(p["mem_out_1"]["bias"]), _np(dy),
+                              balance_coef=bal, route_through_pool=rtp, train=train,
+                              gumbel=None if gumbel is None else _np(gumbel))
+    assert np.array_equal(_np(aux["slots"]).astype(np.int64), want["slots"]), "forward routing differs from the oracle"
+    got = {"h": g["h"], "w_router": g["router_1"]["kernel"], "b_router": g["router_1"]["bias"],
+           "sub_keys": g["pool"]["sub_keys"], "log_temperature": g["pool"]["log_temperature"],
+           "w_gate": g["mem_gate_1"]["kernel"], "b_gate": g["mem_gate_1"]["bias"],
+           "w_out": g["mem_out_1"]["kernel"], "b_out": g["mem_out_1"]["bias"], "probe": g["probe"]}
+    for name, t in got.items():
+        a, b = _np(t).reshape(-1), np.asarray(want[name], np.float64).reshape(-1)
+        scale = max(np.abs(b).max(), 1e-12)
+        err = np.abs(a - b).max() / scale
+        assert err <= TOL, f"{name}: {err:.2e} of max |grad| {scale:.3e}"
+
+
+@pytest.mark.parametrize("bal", [0.0, 0.7])
+@pytest.mark.parametrize("query_scale", [False, True])
+def test_backward_matches_oracle_small(bal, query_scale):
+    _check(*_case(32, 2, 32, 32, 8, 48, 100, seed=3, query_scale=query_scale), bal)
+
+
+def test_backward_temperature_grad_and_route_through_pool():
+    _check(*_case(32, 2, 32, 32, 8, 48, 100, seed=4, query_scale=True, btgrad=True), 0.3, rtp=True)
+
+
+def test_backward_half_table_and_noisy_forward():
+    layer, params, h, dy, cfg = _case(48, 2, 32, 64, 8, 32, 77, seed=5, vdt=torch.float16)
+    gumbel = -torch.log(-torch.log(torch.rand(77, 2, 2, 48, device="cuda",
+                                              generator=torch.Generator("cuda").manual_seed(9)).clamp_(min=1e-12)))
+    _check(layer, params, h, dy, cfg, 0.5, gumbel=gumbel)
+
+
+def test_backward_cfg0_shapes():
+    # configs[0] shapes at 512 tokens: H 4, n 512, d_key 256, d 256, k 16, d_model 256
+    _check(*_case(512, 4, 256, 256, 16, 256, 512, seed=6), 0.01)
