@@ -651,15 +651,17 @@ def run_cfg1(args):
 
 def run_cfg4(args, rank=0, world=1):
     """configs[0] shapes, f32 values, 8192 Zipf-clustered tokens
-    per GPU; step = layer forward with routing statistics + fetched-row
-    gradients of a synthetic probe gradient + global-norm clip + row-wise
-    Adagrad on the touched rows + key_diversity_loss with its gradient.
+    per GPU; step = layer forward with routing statistics + backward through
+    the router (balance term included; the read-output gradient feeds the row
+    update) + fetched-row gradients + global-norm clip + row-wise Adagrad on
+    the touched rows + key_diversity_loss with its gradient.
     revive_dead_keys (every revive_every steps in the reference) is timed
-    once beside it (rank 0).  The backward through the router is not built,
-    so the probe gradient is drawn, not computed.  With N > 1 the table is
-    row-sharded: the sharded forward, then the owner-sharded row update
-    (each rank's merged rows pushed to their owners over NVLink); times are
-    the max over ranks."""
+    once beside it (rank 0).  The upstream gradient of the layer's output is
+    drawn (the backbone is not built).  With N > 1 the table is row-sharded:
+    the sharded forward, then the owner-sharded row update (each rank's
+    merged rows pushed to their owners over NVLink) with a drawn probe
+    gradient (the layer backward is single-GPU); times are the max over
+    ranks."""
     import torch
 
     from model_b200 import _lib as L
@@ -685,7 +687,31 @@ def run_cfg4(args, rank=0, world=1):
     call.args.pool.slot_counts, call.args.pool.subkey_counts = cnt_slot.data_ptr(), cnt_sub.data_ptr()
     call.args.pool.balance_loss = bal.data_ptr()
     accum = torch.zeros(rows, device=device)
+    lib = L.lib()
+    # the backward through the router (memlayer_layer_backward, single GPU): the
+    # upstream gradient dy of the layer's output is drawn (no backbone); its
+    # read-output gradient is the probe gradient the row update consumes
+    # (model.py:114-115).  Row-sharded (N > 1): no backward yet, the probe
+    # gradient is drawn.
+    dm = W["d_model"]
+    dy = torch.randn(T, dm, device=device, generator=torch.Generator(device=device).manual_seed(13 + rank)) * 1e-3
     g = torch.randn(T, d, device=device, generator=torch.Generator(device=device).manual_seed(7 + rank)) * 1e-3
+    if world == 1:
+        gb = {n_: torch.empty(*sh, device=device) for n_, sh in (
+            ("dh", (T, dm)), ("dw_router", (dm, H * W["d_key"])), ("db_router", (H * W["d_key"],)),
+            ("dsub_keys", tuple(x["sub_keys"].shape)), ("dlog_temperature", (1,)), ("dw_gate", (dm, d)),
+            ("db_gate", (d,)), ("dw_out", (d, dm)), ("db_out", (dm,)))}
+        ga = L.MemlayerLayerGrads(dy=dy.data_ptr(), balance_coef=0.01, route_through_pool=0,
+                                  forward_workspace=call.ws.data_ptr(), probe=g.data_ptr(),
+                                  **{n_: t.data_ptr() for n_, t in gb.items()})
+        bnb = C.c_size_t()
+        L.check(lib.memlayer_layer_backward_workspace_size(C.byref(call.cfg), 1, C.byref(bnb)), "backward ws")
+        bws = torch.empty(bnb.value, dtype=torch.uint8, device=device)
+
+    def backward():
+        if world == 1:
+            L.check(lib.memlayer_layer_backward(C.byref(call.cfg), C.byref(call.args), C.byref(ga), bws.data_ptr(),
+                                                bnb.value, stream.cuda_stream), "memlayer_layer_backward")
     rest = torch.tensor([0.5], device=device)
     scale = torch.empty(1, device=device)
     n_u = torch.empty(1, dtype=torch.int32, device=device)
@@ -696,7 +722,6 @@ def run_cfg4(args, rank=0, world=1):
     ada = L.MemlayerAdagradArgs(values=x["values"].data_ptr(), accum=accum.data_ptr(), lr=0.01, grad_clip=1.0,
                                 rest_sq_norm=rest.data_ptr(), clip_scale=scale.data_ptr(), n_unique=n_u.data_ptr())
     rb = C.c_size_t()
-    lib = L.lib()
     if world > 1:
         rcomm = connect(call.cfg, n_reads=1)
         L.check(lib.memlayer_shard_rowgrad_workspace_size(rcomm.handle, T * H * k, C.byref(rb)), "rowgrad ws")
@@ -728,18 +753,21 @@ def run_cfg4(args, rank=0, world=1):
     for _ in range(args.warmup):
         flush.zero_()
         call(stream)
+        backward()
         update()
         diversity()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     K = args.steps
-    e0, e1, e2, e3 = _events(torch, K), _events(torch, K), _events(torch, K), _events(torch, K)
+    e0, e1, e2, e3, eb = (_events(torch, K) for _ in range(5))
     for i in range(K):
         flush.zero_()
         e0[i].record(stream)
         call(stream)
         e1[i].record(stream)
+        backward()
+        eb[i].record(stream)
         update()
         e2[i].record(stream)
         diversity()
@@ -749,7 +777,8 @@ def run_cfg4(args, rank=0, world=1):
         torch.distributed.barrier()
     step = statistics.mean(e0[i].elapsed_time(e3[i]) for i in range(K))
     fwd = statistics.mean(e0[i].elapsed_time(e1[i]) for i in range(K))
-    upd = statistics.mean(e1[i].elapsed_time(e2[i]) for i in range(K))
+    bwd = statistics.mean(e1[i].elapsed_time(eb[i]) for i in range(K))
+    upd = statistics.mean(eb[i].elapsed_time(e2[i]) for i in range(K))
     div = statistics.mean(e2[i].elapsed_time(e3[i]) for i in range(K))
     # the same forward with the training-time selection noise (memory.py:155-159: a
     # standard Gumbel sample scaled by routing_noise * noise_scale), which takes the
@@ -773,7 +802,7 @@ def run_cfg4(args, rank=0, world=1):
     call.args.pool.train, call.args.pool.gumbel = 0, None
     U = int(n_u.item())
     if world > 1:
-        t = torch.tensor([step, fwd, upd, div, fwd_noisy], dtype=torch.float64, device=device)
+        t = torch.tensor([step, fwd, bwd, upd, div, fwd_noisy], dtype=torch.float64, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         u_all = torch.tensor([U], dtype=torch.int64, device=device)
         torch.distributed.all_reduce(u_all)
@@ -783,7 +812,7 @@ def run_cfg4(args, rank=0, world=1):
         call.comm.close()
         if rank != 0:
             return None
-        step, fwd, upd, div, fwd_noisy = t.tolist()
+        step, fwd, bwd, upd, div, fwd_noisy = t.tolist()
         U = int(u_all.item())
     # revive_dead_keys (every revive_every steps in the reference trainer), timed on its own on copies
     from model_b200 import keys as KM
@@ -803,7 +832,8 @@ def run_cfg4(args, rank=0, world=1):
     hbm, src = peaks()
     upd_bytes = F * 8 + T * d * 4 + U * (2 * d * 4 + 8) // world
     return _common_line(W, world, K, args.warmup, step, world * T / (step * 1e-3), "tokens/s", "f32", {
-        "scaling": "weak", "stages_ms": {"forward": fwd, "row_grad_adagrad": upd, "key_diversity": div},
+        "scaling": "weak", "stages_ms": {"forward": fwd, "backward": bwd, "row_grad_adagrad": upd,
+                                         "key_diversity": div},
         "forward_with_selection_noise_ms": fwd_noisy,
         "stage_note": "max over ranks of each stage" if world > 1 else "per-stage means",
         "revive_dead_keys_ms": revive_ms, "revived": int(rdead.sum().item()),
@@ -812,8 +842,11 @@ def run_cfg4(args, rank=0, world=1):
                        "peak": hbm, "peak_source": src, "frac": upd_bytes / (upd * 1e-3) / 1e9 / hbm,
                        "bytes_note": "per rank: slots+weights of every fetch, one read of every probe-gradient row, "
                                      "read+write of its share of the touched value rows and accumulators"},
-        "note": "probe gradient drawn (router backward not built); L2 flushed before every step"
-                + ("; table row-sharded, owner-sharded row update over NVLink" if world > 1 else "")})
+        "note": ("upstream gradient dy drawn (no backbone); backward through the router with the balance "
+                 "term (coef 0.01) gives the row update's probe gradient; L2 flushed before every step")
+                if world == 1 else
+                ("table row-sharded, owner-sharded row update over NVLink; the layer backward is single-GPU, "
+                 "so the probe gradient is drawn here; L2 flushed before every step")})
 
 
 def run_host(args):

@@ -59,7 +59,8 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
             if verbose and out.strip():
                 print(out)
     if jobs or not os.path.exists(LIB):
-        run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"])
+        run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-lcublas", "-Xlinker",
+             "-rpath=/usr/local/cuda/lib64", "-lrt", "-ldl", "-lpthread"])
     return LIB
 
 

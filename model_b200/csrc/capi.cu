@@ -1236,7 +1236,7 @@ struct BwdPlan {
   RowGradLayout L;
   int64_t F, cap;
   int64_t o_qraw, o_qn, o_qlen, o_keys, o_scal, o_zg, o_dmemg, o_memg, o_dzg, o_dqhat, o_dqlen, o_dT, o_ent_s,
-      o_ent_w, o_rg, o_uniq, o_rows, o_dkhat, o_dq, o_cbal, o_dTrow, o_dqlrow, bytes;
+      o_ent_w, o_rg, o_uniq, o_rows, o_dkhat, o_dq, o_cbal, o_dTrow, o_dqlrow, o_ones, bytes;
 };
 
 BwdPlan bwd_plan(const Dims& D, bool balance) {
@@ -1273,6 +1273,7 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
   P.o_cbal = balance ? take(4 * HC * M * D.n) : 0;
   P.o_dTrow = balance ? take(4 * HC * M) : 0;
   P.o_dqlrow = balance ? take(4 * M * HC) : 0;
+  P.o_ones = take(4 * M);
   P.bytes = o;
   return P;
 }
@@ -1327,9 +1328,11 @@ int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer
   // forward activations: unit keys and temperature (memory.py:139-146), q (model.py:110), gate input (:118)
   ML_TRY(launch_prep_keys(D, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature, keys_n,
                           nullptr, nullptr, scal, small + 64, small + 65, s));
-  ML_TRY(launch_gemm(a->h, a->w_router, a->b_router, F32p(P.o_qraw), M, (int)NR, (int)dm, false, s));
+  ML_TRY(launch_bias_rows(a->b_router, M, NR, F32p(P.o_qraw), s));
+  ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, true, s));
   ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, nullptr, nullptr, s));
-  ML_TRY(launch_gemm(a->h, a->w_gate, a->b_gate, F32p(P.o_zg), M, (int)d, (int)dm, false, s));
+  ML_TRY(launch_bias_rows(a->b_gate, M, d, F32p(P.o_zg), s));
+  ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, true, s));
   // d (mem * gate) = dy W_out^T (model.py:119)
   ML_TRY(launch_gemm_strided(g->dy, dm, 1, a->w_out, 1, dm, F32p(P.o_dmemg), d, M, d, dm, false, s));
   float* probe = g->probe ? g->probe : F32p(P.o_dmemg);   // in place when the caller keeps no probe
@@ -1388,13 +1391,15 @@ int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer
     ML_TRY(launch_dlogt(F32p(P.o_dT), M * H, (balance && D.btgrad) ? F32p(P.o_dTrow) : nullptr,
                         (balance && D.btgrad) ? HC * M : 0, scal, g->dlog_temperature, s));
   // Dense-layer gradients (model.py:110, 118, 119)
+  const float* ones = F32p(P.o_ones);
+  ML_TRY(launch_fill(F32p(P.o_ones), M, 1.f, s));
   if (g->dw_router) ML_TRY(launch_gemm_strided(a->h, 1, dm, dq, NR, 1, g->dw_router, NR, dm, NR, M, false, s));
-  if (g->db_router) ML_TRY(launch_colsum(dq, M, NR, NR, g->db_router, s));
+  if (g->db_router) ML_TRY(launch_colsum(dq, M, NR, NR, ones, g->db_router, s));
   if (g->dw_gate)
     ML_TRY(launch_gemm_strided(a->h, 1, dm, F32p(P.o_dzg), d, 1, g->dw_gate, d, dm, d, M, false, s));
-  if (g->db_gate) ML_TRY(launch_colsum(F32p(P.o_dzg), M, d, d, g->db_gate, s));
+  if (g->db_gate) ML_TRY(launch_colsum(F32p(P.o_dzg), M, d, d, ones, g->db_gate, s));
   if (g->dw_out) ML_TRY(launch_gemm_strided(F32p(P.o_memg), 1, d, g->dy, dm, 1, g->dw_out, dm, d, dm, M, false, s));
-  if (g->db_out) ML_TRY(launch_colsum(g->dy, M, dm, dm, g->db_out, s));
+  if (g->db_out) ML_TRY(launch_colsum(g->dy, M, dm, dm, ones, g->db_out, s));
   if (g->dh) {
     ML_TRY(launch_gemm_strided(dq, NR, 1, a->w_router, 1, NR, g->dh, dm, M, dm, NR, false, s));
     if (!g->route_through_pool)

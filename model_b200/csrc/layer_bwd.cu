@@ -18,10 +18,15 @@
 //   bal_row_kernel     (balance term) per (token, codebook) row the softmax
 //                      of p over all n keys from the recomputed cosines, and
 //                      d p = s (dP - sum dP s) / M turned into d cos;
-//   gemm_strided       float32 GEMMs with arbitrary strides (Dense-layer
-//                      gradients, the dense balance contractions);
+//   plain GEMMs        (recomputed projections, Dense-layer gradients, the
+//                      dense balance contractions) through cuBLAS SGEMM in
+//                      float32 (no TF32);
 //   norm backward      x * rsqrt(|x|^2 + 1e-6) for the queries and sub-keys.
 // Every sum runs in a fixed order: results are deterministic.
+#include <cublas_v2.h>
+
+#include <mutex>
+
 #include "combine.cuh"
 #include "layer_bwd.cuh"
 
@@ -29,73 +34,38 @@ namespace ml {
 
 namespace {
 
-// ---------------------------------------------------------------------------
-// C (+)= op(A) op(B): A(i, k) = A[i * sai + k * sak], B(k, j) = B[k * sbk + j * sbj],
-// C[i * ldc + j]; 64 x 64 tiles, 16-deep K slices, 4 x 4 outputs per thread.
-// ---------------------------------------------------------------------------
-constexpr int SG_T = 64, SG_K = 16;
-
-__global__ void __launch_bounds__(256) gemm_strided_kernel(const float* __restrict__ A, int64_t sai, int64_t sak,
-                                                           const float* __restrict__ B, int64_t sbk, int64_t sbj,
-                                                           float* __restrict__ C, int64_t ldc, int64_t M, int64_t N,
-                                                           int64_t K, int accumulate) {
-  __shared__ float As[SG_K][SG_T + 4];
-  __shared__ float Bs[SG_K][SG_T + 4];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int64_t i0 = (int64_t)blockIdx.y * SG_T, j0 = (int64_t)blockIdx.x * SG_T;
-  float acc[4][4] = {};
-  for (int64_t k0 = 0; k0 < K; k0 += SG_K) {
-    for (int e = threadIdx.x; e < SG_K * SG_T; e += 256) {
-      const int kk = e / SG_T, ii = e - kk * SG_T;
-      const int64_t gi = i0 + ii, gk = k0 + kk, gj = j0 + ii;
-      As[kk][ii] = (gi < M && gk < K) ? A[gi * sai + gk * sak] : 0.f;
-      Bs[kk][ii] = (gj < N && gk < K) ? B[gk * sbk + gj * sbj] : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < SG_K; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        a[p] = As[kk][ty * 4 + p];
-        b[p] = Bs[kk][tx * 4 + p];
-      }
-#pragma unroll
-      for (int p = 0; p < 4; ++p)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[p][q] = fmaf(a[p], b[q], acc[p][q]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int p = 0; p < 4; ++p)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int64_t i = i0 + ty * 4 + p, j = j0 + tx * 4 + q;
-      if (i < M && j < N) {
-        float* c = C + i * ldc + j;
-        *c = accumulate ? *c + acc[p][q] : acc[p][q];
-      }
-    }
+// C[i, j] = bias[j] (the Dense layers' bias, before the GEMM accumulates).
+__global__ void bias_rows_kernel(const float* __restrict__ bias, int64_t rows, int64_t cols, float* __restrict__ C) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= rows * cols) return;
+  C[e] = bias ? bias[e % cols] : 0.f;
 }
 
-// out[j] = sum over rows of X[row * ld + j], rows in order (bias gradients).
-__global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ X, int64_t rows, int64_t cols,
-                                                     int64_t ld, float* __restrict__ out) {
-  __shared__ float part[8][32];
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int64_t j = (int64_t)blockIdx.x * 32 + lane;
-  const int64_t per = (rows + 7) / 8, r0 = w * per, r1 = r0 + per < rows ? r0 + per : rows;
-  float s = 0.f;
-  if (j < cols)
-    for (int64_t r = r0; r < r1; ++r) s += X[r * ld + j];
-  part[w][lane] = s;
-  __syncthreads();
-  if (w == 0 && j < cols) {
-    float t = 0.f;
-    for (int ww = 0; ww < 8; ++ww) t += part[ww][lane];
-    out[j] = t;
+// One cuBLAS handle per device (created on first use, float32 arithmetic
+// only: no TF32 or other reduced-precision modes); calls are serialised
+// because a handle is bound to one stream at a time.
+std::mutex g_blas_mu;
+cublasHandle_t g_blas[64] = {};
+
+cudaError_t blas_handle(cublasHandle_t* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!g_blas[dev]) {
+    cublasHandle_t h = nullptr;
+    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return cudaErrorInitializationError;
+    if (cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH) != CUBLAS_STATUS_SUCCESS) {
+      cublasDestroy(h);
+      return cudaErrorInitializationError;
+    }
+    g_blas[dev] = h;
   }
+  *out = g_blas[dev];
+  return cudaSuccess;
+}
+
+__global__ void fill_kernel(float* __restrict__ x, int64_t n, float v) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e < n) x[e] = v;
 }
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
@@ -404,19 +374,47 @@ cudaError_t route_bwd_ch(const Dims& D, const VT* values, const LayerBwd& B, cud
 
 }  // namespace
 
+// Row-major C[M, N] (ld ldc) = A' B' as cuBLAS's column-major C^T = B'^T A'^T:
+// A'(i, k) = A[i sai + k sak] with sak == 1 (row-major, ld sai) or sai == 1
+// (transposed, ld sak); B' likewise with sbj == 1 or sbk == 1.
 cudaError_t launch_gemm_strided(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
                                 float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
                                 cudaStream_t s) {
   if (M == 0 || N == 0) return cudaSuccess;
-  const dim3 grid((unsigned)((N + SG_T - 1) / SG_T), (unsigned)((M + SG_T - 1) / SG_T));
-  gemm_strided_kernel<<<grid, 256, 0, s>>>(A, sai, sak, B, sbk, sbj, C, ldc, M, N, K, accumulate ? 1 : 0);
+  if (!((sak == 1) || (sai == 1)) || !((sbj == 1) || (sbk == 1))) return cudaErrorInvalidValue;
+  const cublasOperation_t opA = sak == 1 ? CUBLAS_OP_N : CUBLAS_OP_T;
+  const int64_t lda = sak == 1 ? sai : sak;
+  const cublasOperation_t opB = sbj == 1 ? CUBLAS_OP_N : CUBLAS_OP_T;
+  const int64_t ldb = sbj == 1 ? sbk : sbj;
+  const float one = 1.f, beta = accumulate ? 1.f : 0.f;
+  std::lock_guard<std::mutex> lk(g_blas_mu);
+  cublasHandle_t h;
+  cudaError_t e = blas_handle(&h);
+  if (e != cudaSuccess) return e;
+  if (cublasSetStream(h, s) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
+  const cublasStatus_t st = cublasSgemm(h, opB, opA, (int)N, (int)M, (int)K, &one, B, (int)ldb, A, (int)lda, &beta,
+                                        C, (int)ldc);
+  return st == CUBLAS_STATUS_SUCCESS ? cudaGetLastError() : cudaErrorUnknown;
+}
+
+cudaError_t launch_bias_rows(const float* bias, int64_t rows, int64_t cols, float* C, cudaStream_t s) {
+  const int64_t n = rows * cols;
+  if (n == 0) return cudaSuccess;
+  bias_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(bias, rows, cols, C);
   count_launch();
   return cudaGetLastError();
 }
 
-cudaError_t launch_colsum(const float* X, int64_t rows, int64_t cols, int64_t ld, float* out, cudaStream_t s) {
+// out[j] = sum over rows of X[row * ld + j] (bias gradients): ones^T X in cuBLAS.
+cudaError_t launch_colsum(const float* X, int64_t rows, int64_t cols, int64_t ld, const float* ones, float* out,
+                          cudaStream_t s) {
   if (cols == 0) return cudaSuccess;
-  colsum_kernel<<<(unsigned)((cols + 31) / 32), 256, 0, s>>>(X, rows, cols, ld, out);
+  return launch_gemm_strided(ones, rows, 1, X, ld, 1, out, cols, 1, cols, rows, false, s);
+}
+
+cudaError_t launch_fill(float* x, int64_t n, float v, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  fill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, n, v);
   count_launch();
   return cudaGetLastError();
 }
