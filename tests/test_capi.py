@@ -38,6 +38,7 @@ def test_struct_sizes_match_header_layout():
     assert C.sizeof(L.MemlayerLayerArgs) == 9 * 8 + C.sizeof(L.MemlayerPoolArgs)
     assert C.sizeof(L.MemlayerRead) == 4 * 8
     assert C.sizeof(L.MemlayerAdagradArgs) == 2 * 8 + 2 * 4 + 3 * 8
+    assert C.sizeof(L.MemlayerLayerGrads) == 8 + 4 + 4 + 8 + 10 * 8   # dy, coef, flag, forward ws, 10 outputs
 
 
 def cfg(**kw):
@@ -126,3 +127,29 @@ def test_prepared_layer_call_refuses_an_unprepared_workspace():
     assert L.lib().memlayer_layer_forward_prepared(C.byref(c), C.byref(la), 1 << 20, nb.value,
                                                    None) == L.ERR_WORKSPACE
     assert L.lib().memlayer_layer_forward_prepared(C.byref(c), None, 1 << 20, nb.value, None) == L.ERR_BAD_POINTER
+
+
+def test_layer_backward_arguments_rejected_on_the_host():
+    lib = L.lib()
+    c = cfg(tokens=64, d_key=64, d_value=64, d_model=64)
+    nb = C.c_size_t()
+    assert lib.memlayer_layer_backward_workspace_size(C.byref(c), 1, C.byref(nb)) == L.OK
+    nb0 = C.c_size_t()
+    assert lib.memlayer_layer_backward_workspace_size(C.byref(c), 0, C.byref(nb0)) == L.OK
+    assert nb0.value < nb.value                                     # the balance term's buffers
+    assert lib.memlayer_layer_backward_workspace_size(C.byref(cfg(d_key=6)), 0, C.byref(nb0)) == L.ERR_UNSUPPORTED
+    la = L.MemlayerLayerArgs(h=256, w_router=256, w_gate=256, w_out=256, y=256,
+                             pool=L.MemlayerPoolArgs(sub_keys=256, log_temperature=256, values=256, slots=256,
+                                                     weights=256))
+    g = L.MemlayerLayerGrads(dy=256, balance_coef=0.0)
+    assert lib.memlayer_layer_backward(C.byref(c), None, C.byref(g), 1 << 20, nb.value, None) == L.ERR_BAD_POINTER
+    assert lib.memlayer_layer_backward(C.byref(c), C.byref(la), None, 1 << 20, nb.value, None) == L.ERR_BAD_POINTER
+    # the balance term needs the forward's workspace and its balance_loss output
+    gb = L.MemlayerLayerGrads(dy=256, balance_coef=0.01)
+    assert lib.memlayer_layer_backward(C.byref(c), C.byref(la), C.byref(gb), 1 << 20, nb.value,
+                                       None) == L.ERR_BAD_POINTER
+    # workspace missing, short or misaligned
+    assert lib.memlayer_layer_backward(C.byref(c), C.byref(la), C.byref(g), None, nb.value, None) == L.ERR_WORKSPACE
+    assert lib.memlayer_layer_backward(C.byref(c), C.byref(la), C.byref(g), 1 << 20, 64, None) == L.ERR_WORKSPACE
+    assert lib.memlayer_layer_backward(C.byref(c), C.byref(la), C.byref(g), (1 << 20) + 16, nb.value,
+                                       None) == L.ERR_WORKSPACE
