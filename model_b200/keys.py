@@ -20,7 +20,7 @@ from typing import Optional, Sequence, Tuple
 import torch
 
 from . import _lib as L
-from .memory import _workspace
+from .memory import _workspace, on_stream
 
 
 def _config(sub_keys: torch.Tensor) -> L.MemlayerConfig:
@@ -39,6 +39,7 @@ def _f32(t: torch.Tensor, name: str) -> torch.Tensor:
     return t.to(torch.float32).contiguous()
 
 
+@on_stream
 def key_diversity_loss(sub_keys: torch.Tensor, *, grad: bool = False, grad_scale: float = 1.0,
                        stream: Optional[torch.cuda.Stream] = None):
     """memory.py:230-240: mean squared off-diagonal cosine of the unit
@@ -60,6 +61,7 @@ def key_diversity_loss(sub_keys: torch.Tensor, *, grad: bool = False, grad_scale
     return (loss, g) if grad else loss
 
 
+@on_stream
 def revive_dead_keys(sub_keys: torch.Tensor, subkey_usage: torch.Tensor, queries: torch.Tensor,
                      threshold: float, noise: float = 0.05, *, pick: Optional[torch.Tensor] = None,
                      normal: Optional[torch.Tensor] = None, generator: Optional[torch.Generator] = None,

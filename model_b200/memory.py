@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes as C
 import dataclasses
+import functools
 import math
 from typing import Any, Dict, Optional, Tuple
 
@@ -41,6 +42,21 @@ def _raise_device_status(cfg, ws: torch.Tensor, stream_ptr: int) -> None:
 def _workspace(nbytes: int, device) -> torch.Tensor:
     # torch's caching allocator hands out 512-byte aligned blocks
     return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+
+
+def on_stream(fn):
+    """Runs ``fn`` with its ``stream`` keyword argument as the current CUDA
+    stream.  The workspaces, converted inputs and outputs that ``fn``
+    allocates then belong to the stream its kernels run on: the caching
+    allocator reuses a block freed when ``fn`` returns only in that stream's
+    order, never while the kernels still read it."""
+    @functools.wraps(fn)
+    def wrapped(*args, stream: Optional[torch.cuda.Stream] = None, **kw):
+        if stream is None:
+            return fn(*args, stream=None, **kw)
+        with torch.cuda.stream(stream):
+            return fn(*args, stream=stream, **kw)
+    return wrapped
 
 
 @dataclasses.dataclass
@@ -163,6 +179,7 @@ class MemoryPool:
                        slot_counts=keep["slot_counts"], queries=keep["queries_unit"])
         return aux
 
+    @on_stream
     def apply(self, variables, queries: torch.Tensor, *, train: bool = False, sparse_grad: bool = False,
               noise_scale: float = 1.0, shuffle_reads: bool = False, rngs=None,
               gumbel: Optional[torch.Tensor] = None, stats: bool = True,
@@ -232,6 +249,7 @@ class MemoryLayer:
             "pool": P.init(seed, device, values_dtype)["params"],
         }
 
+    @on_stream
     def apply_host(self, params, h_host: torch.Tensor, *, chunks: int = 4, device="cuda",
                    shuffle_reads: bool = False, stream: Optional[torch.cuda.Stream] = None,
                    check: bool = False):
@@ -284,6 +302,7 @@ class MemoryLayer:
                                          stream=stream, check=check)
         return y, mem, aux, ctx
 
+    @on_stream
     def backward(self, ctx: Dict[str, Any], dy: torch.Tensor, *, balance_coef: float = 0.0,
                  route_through_pool: bool = False, stream: Optional[torch.cuda.Stream] = None,
                  check: bool = False) -> Dict[str, torch.Tensor]:
@@ -335,6 +354,7 @@ class MemoryLayer:
                                        rngs=rngs, gumbel=gumbel, stats=stats, stream=stream, check=check)
         return y, mem, aux
 
+    @on_stream
     def _forward(self, params, h, *, train, noise_scale, shuffle_reads, rngs, gumbel, stats, stream, check):
         P = self.pool
         h = _cuda_f32(h, "h")

@@ -25,7 +25,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from . import _lib as L
-from .memory import MemoryLayer, MemoryPool, _cuda_f32, _ptr, _raise_device_status, _workspace
+from .memory import MemoryLayer, MemoryPool, _cuda_f32, _ptr, _raise_device_status, _workspace, on_stream
 
 
 def shard_rows(pool_size: int, rank: int, world: int) -> int:
@@ -204,6 +204,7 @@ class ShardedMemoryLayer:
     def pool(self) -> MemoryPool:
         return self.layer.pool
 
+    @on_stream
     def apply(self, params, h: torch.Tensor, *, check: bool = False, stream=None, split: bool = True, **kw):
         """``split``: exchange in two token halves, the second half's push
         overlapping the first half's gather (MEMLAYER_PHASE_SPLIT)."""

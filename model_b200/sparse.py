@@ -19,7 +19,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 
 from . import _lib as L
-from .memory import _workspace
+from .memory import _workspace, on_stream
 
 
 def _reads(aux, probe_grads, layers) -> Tuple[List[L.MemlayerRead], list, int, int, int]:
@@ -57,6 +57,7 @@ def _config(pool_size: int, H: int, k: int, d: int) -> L.MemlayerConfig:
                             values_dtype=L.F32, routing_noise=0.0, min_temperature=1.0, max_temperature=1.0)
 
 
+@on_stream
 def fetched_row_grads(aux: Dict, probe_grads: Dict, layers: Sequence[int], pool_size: int, *,
                       stream: Optional[torch.cuda.Stream] = None, with_sq_norm: bool = False):
     """train.py:146-172: ``(uniq [cap], rows [cap, d])``, cap = min(fetches,
@@ -86,6 +87,7 @@ def fetched_row_grads(aux: Dict, probe_grads: Dict, layers: Sequence[int], pool_
     return out
 
 
+@on_stream
 def rowwise_adagrad(values: torch.Tensor, accum: torch.Tensor, aux: Dict, probe_grads: Dict,
                     layers: Sequence[int], *, lr: float, grad_clip: float,
                     rest_sq_norm: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None,
@@ -173,6 +175,7 @@ class ShardedRowUpdate:
         return {"clip_scale": self.scale, "n_unique": self.n_unique}
 
 
+@on_stream
 def sharded_rowwise_adagrad(values: torch.Tensor, accum: torch.Tensor, aux: Dict, probe_grads: Dict,
                             layers: Sequence[int], comm, *, lr: float, grad_clip: float,
                             rest_sq_norm: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None,
