@@ -483,6 +483,10 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
   if (comm && (st = check_shard(cfg, a->pool.values, comm))) return st;
   resolve_noise(&D, cfg, &a->pool);
   if (D.noisy && !a->pool.gumbel && D.M > 0) return MEMLAYER_ERR_BAD_POINTER;
+  // no tokens on one GPU: no Dense work, only the pool's per-call outputs
+  // (temperature, statistics), as the pool entry gives them for no queries
+  if (D.M == 0 && !comm && !given) return pool_impl(cfg, &a->pool, workspace, workspace_bytes, s, nullptr,
+                                                    MEMLAYER_PHASE_ALL);
   Flags f;
   f.layer = true;
   f.balance = a->pool.balance_loss != nullptr;
@@ -1320,7 +1324,15 @@ int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer
   int* small = reinterpret_cast<int*>(ws);
   ML_TRY(cudaMemsetAsync(ws, 0, 512, s));
   const int64_t M = D.M, H = D.H, HC = H * 2, half = D.half, n = D.n, d = D.d, dm = D.dm, NR = H * D.dk;
-  if (M == 0) return MEMLAYER_OK;
+  if (M == 0) {
+    // no tokens: every parameter gradient is zero (dh and probe are empty)
+    const struct { float* p; int64_t n; } zero[] = {
+        {g->dw_router, dm * NR}, {g->db_router, NR}, {g->dsub_keys, HC * n * half}, {g->dlog_temperature, 1},
+        {g->dw_gate, dm * d},    {g->db_gate, d},    {g->dw_out, d * dm},           {g->db_out, dm}};
+    for (const auto& z : zero)
+      if (z.p) ML_TRY(cudaMemsetAsync(z.p, 0, sizeof(float) * z.n, s));
+    return MEMLAYER_OK;
+  }
   float* qn = F32p(P.o_qn);
   float* qlen = F32p(P.o_qlen);
   float* keys_n = F32p(P.o_keys);

@@ -82,3 +82,16 @@ def test_backward_half_table_and_noisy_forward():
 def test_backward_cfg0_shapes():
     # configs[0] shapes at 512 tokens: H 4, n 512, d_key 256, d 256, k 16, d_model 256
     _check(*_case(512, 4, 256, 256, 16, 256, 512, seed=6), 0.01)
+
+
+def test_backward_no_tokens():
+    layer, params, h, dy, _ = _case(32, 2, 32, 32, 8, 48, 100, seed=6)
+    y, mem, aux, ctx = layer.apply_train(params, h[:0], check=True)
+    assert y.shape == (0, 48) and mem.shape == (0, 32) and aux["slots"].shape == (0, 2, 8)
+    g = layer.backward(ctx, dy[:0], balance_coef=0.5, check=True)
+    torch.cuda.synchronize()
+    assert g["h"].shape == (0, 48) and g["probe"].shape == (0, 32)
+    for name in ("router_1", "mem_gate_1", "mem_out_1"):
+        for leaf in ("kernel", "bias"):
+            assert not g[name][leaf].any(), f"{name}/{leaf} not zero for no tokens"
+    assert not g["pool"]["sub_keys"].any() and float(g["pool"]["log_temperature"]) == 0.0
