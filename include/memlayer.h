@@ -425,6 +425,24 @@ int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer
                                 const memlayer_layer_grads* grads, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* The same backward on a row-sharded table (model.py:110-119 with
+ * memory.py:133-214 under the reference trainer's data parallelism,
+ * train.py:229-236, with the table split over the ranks as in
+ * memlayer_layer_forward_sharded): call it after that forward on `comm`, once
+ * per forward, with the forward's `args` (`mem`, else `pool.out`, holding its
+ * read output).  Each rank publishes its probe rows; each owner returns
+ * probe . row for every read of its rows (the forward's inbox entries: no
+ * value row crosses NVLink); the rest is local.  Phases as the forward's:
+ * ROUTE = projections, probe published; GATHER = this owner's dots; REDUCE =
+ * routing backward from the owners' dots, then the Dense, sub-key and
+ * temperature gradients of this rank's tokens, which the caller sums over
+ * the ranks as data-parallel training does.  Every rank runs every phase;
+ * waits are bounded (status 35: probe rows, 36: dots).  One workspace of
+ * memlayer_layer_backward_workspace_size bytes serves every phase of a call. */
+int32_t memlayer_layer_backward_sharded(const memlayer_config* cfg, const memlayer_layer_args* args,
+                                        const memlayer_layer_grads* grads, memlayer_shard_comm* comm,
+                                        int32_t phases, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Owner-sharded row update (row-sharded table, training) -------------
  * Replaces fetched_row_grads_sharded + the replicated update
  * (memory_pool_model/train.py:175-206, 378-399): with the table row-sharded

@@ -142,7 +142,8 @@ DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "M
                  23: "fetched slot id out of range", 24: "row push beyond inbox capacity",
                  25: "host-table row id out of range",
                  31: "peer inbox wait timed out", 32: "peer partial-sum wait timed out",
-                 33: "row-gradient inbox wait timed out", 34: "norm partial wait timed out"}
+                 33: "row-gradient inbox wait timed out", 34: "norm partial wait timed out",
+                 35: "peer probe-row wait timed out", 36: "peer dot wait timed out"}
 
 
 class MemlayerError(RuntimeError):
@@ -249,6 +250,10 @@ def lib() -> C.CDLL:
         L.memlayer_layer_backward.restype = C.c_int32
         L.memlayer_layer_backward.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
                                               C.POINTER(MemlayerLayerGrads), C.c_void_p, C.c_size_t, C.c_void_p]
+        L.memlayer_layer_backward_sharded.restype = C.c_int32
+        L.memlayer_layer_backward_sharded.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
+                                                      C.POINTER(MemlayerLayerGrads), C.c_void_p, C.c_int32,
+                                                      C.c_void_p, C.c_size_t, C.c_void_p]
         if L.memlayer_abi_version() != 1:
             raise ImportError("libmemlayer.so ABI version mismatch; rebuild")
         _lib = L

@@ -1301,8 +1301,14 @@ int32_t memlayer_layer_backward_workspace_size(const memlayer_config* cfg, int32
   return MEMLAYER_OK;
 }
 
-int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer_args* a, const memlayer_layer_grads* g,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+// The layer backward, single GPU (comm == nullptr: every step) or on a
+// row-sharded table after memlayer_layer_forward_sharded, in phases:
+// ROUTE = recomputed projections, d (mem * gate), probe rows published;
+// GATHER = this rank's dots for every source's reads of its rows;
+// REDUCE = routing backward from the owners' dots, then the local rest.
+static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args* a, const memlayer_layer_grads* g,
+                          void* workspace, size_t workspace_bytes, cudaStream_t s, memlayer_shard_comm* comm,
+                          int phases) {
   Dims D;
   int st = check_bwd(cfg, &D);
   if (st) return st;
@@ -1312,18 +1318,38 @@ int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer
   if (D.M > 0 && (!a->h || !a->w_router || !a->w_gate || !a->w_out || !pa->slots || !pa->weights || !g->dy))
     return MEMLAYER_ERR_BAD_POINTER;
   if (!aligned16(pa->values) && D.vdtype != MEMLAYER_F32) return MEMLAYER_ERR_BAD_POINTER;
+  const float* fwd_mem = a->mem ? a->mem : pa->out;   // sharded: the forward's read output
+  if (comm) {
+    if ((st = check_shard(cfg, pa->values, comm))) return st;
+    if (D.M > 0 && !fwd_mem) return MEMLAYER_ERR_BAD_POINTER;
+  }
   const bool balance = g->balance_coef != 0.f;
   if (balance && (!g->forward_workspace || !pa->balance_loss)) return MEMLAYER_ERR_BAD_POINTER;
   resolve_noise(&D, cfg, pa);
   const BwdPlan P = bwd_plan(D, balance);
   if (!workspace || workspace_bytes < (size_t)P.bytes || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
     return MEMLAYER_ERR_WORKSPACE;
-  const cudaStream_t s = (cudaStream_t)stream;
+  const bool route = !comm || (phases & MEMLAYER_PHASE_ROUTE);
+  const bool gather = comm && (phases & MEMLAYER_PHASE_GATHER);
+  const bool reduce = !comm || (phases & MEMLAYER_PHASE_REDUCE);
+  if (comm && route) {
+    // one backward per forward: the owners' inboxes hold that forward's reads
+    if (comm->epoch == 0 || comm->bwd_epoch == comm->epoch) return MEMLAYER_ERR_BAD_SHAPE;
+    comm->bwd_epoch = comm->epoch;
+  }
   char* ws = (char*)workspace;
   auto F32p = [&](int64_t off) { return reinterpret_cast<float*>(ws + off); };
   int* small = reinterpret_cast<int*>(ws);
-  ML_TRY(cudaMemsetAsync(ws, 0, 512, s));
+  if (route) ML_TRY(cudaMemsetAsync(ws, 0, 512, s));
   const int64_t M = D.M, H = D.H, HC = H * 2, half = D.half, n = D.n, d = D.d, dm = D.dm, NR = H * D.dk;
+  const ShardK SK = comm ? shard_k(comm, D) : ShardK{};
+  float* probe = g->probe ? g->probe : F32p(P.o_dmemg);   // in place when the caller keeps no probe
+  if (comm && M == 0) {
+    // no tokens here: publish the empty probe, serve the other ranks' reads
+    if (route) ML_TRY(launch_shard_probe(SK, 0, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, s));
+    if (gather) ML_TRY(launch_shard_dots(D, SK, pa->values, small + 64, s));
+    if (!reduce) return MEMLAYER_OK;
+  }
   if (M == 0) {
     // no tokens: every parameter gradient is zero (dh and probe are empty)
     const struct { float* p; int64_t n; } zero[] = {
@@ -1337,21 +1363,33 @@ int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer
   float* qlen = F32p(P.o_qlen);
   float* keys_n = F32p(P.o_keys);
   float* scal = F32p(P.o_scal);
-  // forward activations: unit keys and temperature (memory.py:139-146), q (model.py:110), gate input (:118)
-  ML_TRY(launch_prep_keys(D, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature, keys_n,
-                          nullptr, nullptr, scal, small + 64, small + 65, s));
-  ML_TRY(launch_bias_rows(a->b_router, M, NR, F32p(P.o_qraw), s));
-  ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, true, s));
-  ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, nullptr, nullptr, s));
-  ML_TRY(launch_bias_rows(a->b_gate, M, d, F32p(P.o_zg), s));
-  ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, true, s));
-  // d (mem * gate) = dy W_out^T (model.py:119)
-  ML_TRY(launch_gemm_strided(g->dy, dm, 1, a->w_out, 1, dm, F32p(P.o_dmemg), d, M, d, dm, false, s));
-  float* probe = g->probe ? g->probe : F32p(P.o_dmemg);   // in place when the caller keeps no probe
   LayerBwd B{pa->slots, pa->weights, F32p(P.o_dmemg), F32p(P.o_zg), qn, qlen, keys_n, scal, probe, F32p(P.o_memg),
              F32p(P.o_dzg), F32p(P.o_dqhat), F32p(P.o_dqlen), F32p(P.o_dT),
              reinterpret_cast<int*>(ws + P.o_ent_s), F32p(P.o_ent_w)};
-  ML_TRY(launch_route_bwd(D, pa->values, B, s));
+  if (route) {
+    // forward activations: unit keys and temperature (memory.py:139-146), q (model.py:110), gate input (:118)
+    ML_TRY(launch_prep_keys(D, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature, keys_n,
+                            nullptr, nullptr, scal, small + 64, small + 65, s));
+    ML_TRY(launch_bias_rows(a->b_router, M, NR, F32p(P.o_qraw), s));
+    ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, true, s));
+    ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, nullptr, nullptr, s));
+    ML_TRY(launch_bias_rows(a->b_gate, M, d, F32p(P.o_zg), s));
+    ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, true, s));
+    // d (mem * gate) = dy W_out^T (model.py:119)
+    ML_TRY(launch_gemm_strided(g->dy, dm, 1, a->w_out, 1, dm, F32p(P.o_dmemg), d, M, d, dm, false, s));
+    if (comm) ML_TRY(launch_shard_probe(SK, M, B.dmemg, B.zg, fwd_mem, probe, B.memg, B.dzg, s));
+  }
+  if (gather) ML_TRY(launch_shard_dots(D, SK, pa->values, small + 64, s));
+  if (!reduce) return MEMLAYER_OK;
+  if (comm) {
+    const char* mine = comm->peer[comm->rank];
+    const BwdShard X{reinterpret_cast<const float*>(mine + comm->off.dots),
+                     reinterpret_cast<const int*>(mine + comm->off.flags_dots), SK.mcap, comm->world, comm->epoch,
+                     small + 64};
+    ML_TRY(launch_route_bwd_sharded(D, B, X, s));
+  } else {
+    ML_TRY(launch_route_bwd(D, pa->values, B, s));
+  }
   float* dkhat = F32p(P.o_dkhat);
   if (balance) {
     // memory.py:205-214: the softmax over every sub-key, from the recomputed cosines
@@ -1418,6 +1456,19 @@ int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer
       ML_TRY(launch_gemm_strided(F32p(P.o_dzg), d, 1, a->w_gate, 1, d, g->dh, dm, M, dm, d, true, s));
   }
   return MEMLAYER_OK;
+}
+
+int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer_args* a, const memlayer_layer_grads* g,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  return layer_bwd_impl(cfg, a, g, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, MEMLAYER_PHASE_ALL);
+}
+
+int32_t memlayer_layer_backward_sharded(const memlayer_config* cfg, const memlayer_layer_args* a,
+                                        const memlayer_layer_grads* g, memlayer_shard_comm* comm, int32_t phases,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if ((phases & MEMLAYER_PHASE_ALL) == 0 || (phases & ~MEMLAYER_PHASE_ALL)) return MEMLAYER_ERR_BAD_SHAPE;
+  return layer_bwd_impl(cfg, a, g, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
 }
 
 // ---- layer forward reusing the previous call's preparation ----

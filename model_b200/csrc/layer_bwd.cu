@@ -29,6 +29,7 @@
 
 #include "combine.cuh"
 #include "layer_bwd.cuh"
+#include "shard.cuh"
 
 namespace ml {
 
@@ -74,13 +75,14 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf
 // route_bwd_kernel: one CTA per token, warp h = pool head.  d <= 1024,
 // half <= 128, k <= 32.
 // ---------------------------------------------------------------------------
-template <typename VT, int VEC, int CH>
+template <typename VT, int VEC, int CH, bool SH>
 __global__ void __launch_bounds__(1024) route_bwd_kernel(
     Dims D, const VT* __restrict__ values, const int* __restrict__ slots, const float* __restrict__ weights,
     const float* __restrict__ dmemg, const float* __restrict__ zg, const float* __restrict__ qn,
     const float* __restrict__ qlen, const float* __restrict__ keys_n, const float* __restrict__ scal,
     float* __restrict__ probe, float* __restrict__ memg, float* __restrict__ dzg, float* __restrict__ dqhat,
-    float* __restrict__ dqlen, float* __restrict__ dT_part, int* __restrict__ ent_slot, float* __restrict__ ent_w) {
+    float* __restrict__ dqlen, float* __restrict__ dT_part, int* __restrict__ ent_slot, float* __restrict__ ent_w,
+    const BwdShard X) {
   extern __shared__ float bsm[];
   float* red = bsm;                 // [H][d]
   float* dmem_s = bsm + D.H * D.d;  // [d]
@@ -95,6 +97,34 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
   // read (slot + N/2 + 1) % N under shuffle_reads (memory.py:179)
   const int64_t rs_l = D.shuffle ? ((int64_t)slot_l + D.N / 2 + 1) % D.N : (int64_t)slot_l;
   const int groups = d / VEC;
+  float dw_l = 0.f;
+  if constexpr (SH) {
+    // row-sharded table: probe, memg and dzg come from the probe kernel, and
+    // dw_r = probe . V[read slot r] from the slot's owner rank, stored in the
+    // owner's inbox order (per owner: heads in order, then lanes in order)
+    __shared__ int cnt_s[32][MEMLAYER_MAX_SHARDS];
+    __shared__ int ok_s;
+    const int P = X.world;
+    if (threadIdx.x == 0) {
+      bool ok = true;
+      for (int o = 0; o < P && ok; ++o) ok = wait_epoch(X.flags + o, X.epoch, X.err, 36);
+      ok_s = ok;
+    }
+    const int own = lane < k ? (int)(rs_l % P) : -1;
+    const unsigned lt = (1u << lane) - 1u;
+    int pos = 0;
+    for (int o = 0; o < P; ++o) {
+      const unsigned mk = __ballot_sync(FULL, own == o);
+      if (own == o) pos = __popc(mk & lt);
+      if (lane == 0) cnt_s[h][o] = __popc(mk);
+    }
+    __syncthreads();
+    if (own >= 0 && ok_s) {
+      int base = 0;
+      for (int hh = 0; hh < h; ++hh) base += cnt_s[hh][own];
+      dw_l = __ldcg(X.dots + ((int64_t)own * X.mcap + m) * ((int64_t)D.H * k) + base + pos);
+    }
+  } else {
   // 1. mem = sum_h sum_r w V[read slot] (memory.py:192), as the forward gather
   float acc[CH][VEC];
 #pragma unroll
@@ -137,7 +167,6 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
   }
   __syncthreads();
   // 3. dw_r = dmem . V[read slot r]; softmax backward (memory.py:178)
-  float dw_l = 0.f;
   for (int r = 0; r < k; ++r) {
     const int64_t row = __shfl_sync(FULL, rs_l, r);
     float s = 0.f;
@@ -153,6 +182,7 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
     }
     s = warp_sum(s);
     if (lane == r) dw_l = s;
+  }
   }
   const float swdw = warp_sum(lane < k ? w_l * dw_l : 0.f);
   const float dss_l = lane < k ? w_l * (dw_l - swdw) : 0.f;
@@ -346,19 +376,19 @@ inline int ch_for(int groups) {
   return ch <= 1 ? 1 : ch <= 2 ? 2 : ch <= 4 ? 4 : ch <= 8 ? 8 : -1;
 }
 
-template <typename VT, int VEC>
-cudaError_t route_bwd_ch(const Dims& D, const VT* values, const LayerBwd& B, cudaStream_t s) {
-  const size_t smem = sizeof(float) * ((size_t)D.H * D.d + D.d);
+template <typename VT, int VEC, bool SH>
+cudaError_t route_bwd_ch(const Dims& D, const VT* values, const LayerBwd& B, const BwdShard& X, cudaStream_t s) {
+  const size_t smem = SH ? 0 : sizeof(float) * ((size_t)D.H * D.d + D.d);
   const dim3 grid((unsigned)D.M), block(32 * D.H);
 #define ML_RB(CHV)                                                                                              \
   {                                                                                                             \
-    auto kern = route_bwd_kernel<VT, VEC, CHV>;                                                                 \
+    auto kern = route_bwd_kernel<VT, VEC, CHV, SH>;                                                             \
     if (smem > 48 * 1024) {                                                                                     \
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
       if (e != cudaSuccess) return e;                                                                           \
     }                                                                                                           \
     kern<<<grid, block, smem, s>>>(D, values, B.slots, B.weights, B.dmemg, B.zg, B.qn, B.qlen, B.keys_n, B.scal, \
-                                   B.probe, B.memg, B.dzg, B.dqhat, B.dqlen, B.dT_part, B.ent_slot, B.ent_w);    \
+                                   B.probe, B.memg, B.dzg, B.dqhat, B.dqlen, B.dT_part, B.ent_slot, B.ent_w, X); \
   }
   switch (ch_for(D.d / VEC)) {
     case 1: ML_RB(1); break;
@@ -421,11 +451,18 @@ cudaError_t launch_fill(float* x, int64_t n, float v, cudaStream_t s) {
 
 cudaError_t launch_route_bwd(const Dims& D, const void* values, const LayerBwd& B, cudaStream_t s) {
   if (D.M == 0) return cudaSuccess;
-  if (D.vdtype == MEMLAYER_F16) return route_bwd_ch<__half, 8>(D, (const __half*)values, B, s);
-  if (D.vdtype == MEMLAYER_BF16) return route_bwd_ch<__nv_bfloat16, 8>(D, (const __nv_bfloat16*)values, B, s);
+  const BwdShard X{};
+  if (D.vdtype == MEMLAYER_F16) return route_bwd_ch<__half, 8, false>(D, (const __half*)values, B, X, s);
+  if (D.vdtype == MEMLAYER_BF16)
+    return route_bwd_ch<__nv_bfloat16, 8, false>(D, (const __nv_bfloat16*)values, B, X, s);
   if (D.d % 4 == 0 && (reinterpret_cast<uintptr_t>(values) & 15) == 0)
-    return route_bwd_ch<float, 4>(D, (const float*)values, B, s);
-  return route_bwd_ch<float, 1>(D, (const float*)values, B, s);
+    return route_bwd_ch<float, 4, false>(D, (const float*)values, B, X, s);
+  return route_bwd_ch<float, 1, false>(D, (const float*)values, B, X, s);
+}
+
+cudaError_t launch_route_bwd_sharded(const Dims& D, const LayerBwd& B, const BwdShard& X, cudaStream_t s) {
+  if (D.M == 0) return cudaSuccess;
+  return route_bwd_ch<float, 4, true>(D, nullptr, B, X, s);
 }
 
 cudaError_t launch_bal_rows(const Dims& D, float* C, const float* cnt, const float* qlen, const float* scal, float coef,

@@ -25,6 +25,17 @@ struct LayerBwd {
   float* ent_w;            // [M, H, 2, k] its d cos
 };
 
+// Row-sharded table: where the routing backward finds the per-read dots
+// probe . V[read slot] that the owner ranks stored (shard.cu), and the flags
+// (one per owner, in this rank's buffer) that say they are complete.
+struct BwdShard {
+  const float* dots;   // [world][mcap][H * k] in each owner's inbox order
+  const int* flags;    // [world] epoch of each owner's dots
+  int64_t mcap;
+  int world, epoch;
+  int* err;            // status word (36: an owner's dots did not arrive in time)
+};
+
 // C (+)= op(A) op(B) with A(i, k) = A[i sai + k sak], B(k, j) = B[k sbk + j sbj], C[i ldc + j]
 // (cuBLAS SGEMM, float32; one of sai / sak and one of sbk / sbj must be 1).
 cudaError_t launch_gemm_strided(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
@@ -36,6 +47,9 @@ cudaError_t launch_colsum(const float* X, int64_t rows, int64_t cols, int64_t ld
                           cudaStream_t s);
 cudaError_t launch_fill(float* x, int64_t n, float v, cudaStream_t s);
 cudaError_t launch_route_bwd(const Dims& D, const void* values, const LayerBwd& B, cudaStream_t s);
+// The routing backward of the row-sharded layer: dw from the owners' dots
+// (values are not read; probe / memg / dzg already written by the probe kernel).
+cudaError_t launch_route_bwd_sharded(const Dims& D, const LayerBwd& B, const BwdShard& X, cudaStream_t s);
 // C: [H * 2][M][n] cosines in, d cos out (balance term)
 cudaError_t launch_bal_rows(const Dims& D, float* C, const float* cnt, const float* qlen, const float* scal, float coef,
                             float* dT_row, float* dql_row, cudaStream_t s);

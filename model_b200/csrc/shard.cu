@@ -265,6 +265,122 @@ __global__ void __launch_bounds__(256) shard_reduce_kernel(const __grid_constant
   }
 }
 
+// ---------------------------------------------------------------------------
+// backward: probe rows out, dots back
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float sigmoid_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// The last CTA writes `count` into slot S.rank of `meta_off` (when >= 0) and
+// release-stores the epoch into slot S.rank of `flag_off`, in every rank's buffer.
+__device__ void publish_backward(const ShardK& S, int ticket_slot, int64_t flag_off, int64_t meta_off, int count) {
+  fence_sys();
+  int* ticket = reinterpret_cast<int*>(S.peer[S.rank] + S.off.tickets) + ticket_slot;
+  if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
+  *ticket = 0;
+  fence_sys();
+  for (int o = 0; o < S.world; ++o) {
+    if (meta_off >= 0) *flag_ptr(S, o, meta_off, S.rank) = count;
+    st_release_sys(flag_ptr(S, o, flag_off, S.rank), S.epoch);
+  }
+}
+
+// probe = dmemg * silu(zg), memg = mem * silu(zg), dzg = dmemg * mem * silu'(zg)
+// (model.py:118-119), the same expressions as the single-GPU routing backward.
+// `probe` may be `dmemg` itself (same element read, then written).
+__global__ void __launch_bounds__(256) shard_probe_kernel(const __grid_constant__ ShardK S, int64_t M,
+                                                          const float* dmemg, const float* __restrict__ zg,
+                                                          const float* __restrict__ mem, float* probe,
+                                                          float* __restrict__ memg, float* __restrict__ dzg) {
+  float* mine = reinterpret_cast<float*>(S.peer[S.rank] + S.off.probe);
+  const int64_t n = M * S.d;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float z = zg[i], sg = sigmoid_(z), gate = z * sg;
+    const float dm = dmemg[i], mv = mem[i];
+    const float p = dm * gate;
+    probe[i] = p;
+    mine[i] = p;
+    memg[i] = mv * gate;
+    dzg[i] = dm * mv * sg * (1.0f + z * (1.0f - sg));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) publish_backward(S, 4, S.off.flags_probe, S.off.bmeta, (int)M);
+}
+
+// One warp per (source rank, token): the source's probe row crosses NVLink
+// once, then probe . V[row] for each of the token's inbox entries from the
+// forward (lanes over d, then a warp sum), stored into the source's dots.
+template <typename VT, int VEC, int CH>
+__global__ void __launch_bounds__(256) shard_dots_kernel(const __grid_constant__ ShardK S,
+                                                         const VT* __restrict__ values, int* __restrict__ err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * 8 + warp;
+  const int P = S.world, d = S.d;
+  if (gw < (int64_t)P * S.mcap) {
+    const int srot = (int)(gw / S.mcap);
+    const int64_t m = gw - (int64_t)srot * S.mcap;
+    const int src = (S.rank + srot) % P;
+    const char* mine = S.peer[S.rank];
+    bool ready = true;
+    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_probe) + src, S.epoch, err, 35);
+    ready = __shfl_sync(FULL, ready, 0);
+    __syncwarp();
+    if (ready) {
+      const int64_t msrc = reinterpret_cast<const volatile int*>(mine + S.off.bmeta)[src];
+      const int64_t grp = (int64_t)src * S.mcap + m;
+      const int c = m < msrc ? reinterpret_cast<const volatile int*>(mine + S.off.cnt)[grp] : 0;
+      if (c > 0) {
+        const int groups = d / VEC;
+        const float* pr = reinterpret_cast<const float*>(S.peer[src] + S.off.probe) + m * d;
+        float p[CH][VEC];
+#pragma unroll
+        for (int a = 0; a < CH; ++a) {
+          const int g = a * 32 + lane;
+#pragma unroll
+          for (int v = 0; v < VEC; v += 4) {
+            const float4 x = g < groups ? __ldcg(reinterpret_cast<const float4*>(pr + g * VEC + v))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+            p[a][v] = x.x;
+            p[a][v + 1] = x.y;
+            p[a][v + 2] = x.z;
+            p[a][v + 3] = x.w;
+          }
+        }
+        const int2* ent = reinterpret_cast<const int2*>(mine + S.off.inbox) + grp * S.hk;
+        float* dst = reinterpret_cast<float*>(S.peer[src] + S.off.dots) + ((int64_t)S.rank * S.mcap + m) * S.hk;
+        for (int b0 = 0; b0 < c; b0 += 32) {
+          const int row_l = (b0 + lane < c) ? __ldcg(ent + b0 + lane).x : 0;
+          const int nb = min(32, c - b0);
+          float dot_l = 0.f;
+          for (int j = 0; j < nb; ++j) {
+            const int row = __shfl_sync(FULL, row_l, j);
+            float acc = 0.f;
+            if ((unsigned)row < (unsigned)S.rows) {
+              const VT* base = values + (int64_t)row * d;
+#pragma unroll
+              for (int a = 0; a < CH; ++a) {
+                const int g = a * 32 + lane;
+                if (g < groups) {
+                  float x[VEC];
+                  load_group<VT, VEC>(base + g * VEC, x);
+#pragma unroll
+                  for (int v = 0; v < VEC; ++v) acc = fmaf(p[a][v], x[v], acc);
+                }
+              }
+            } else if (lane == 0) {
+              atomicCAS(err, 0, 22);                   // only a bug upstream can cause this
+            }
+            acc = warp_sum(acc);
+            if (lane == j) dot_l = acc;
+          }
+          if (lane < nb) dst[b0 + lane] = dot_l;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) publish_backward(S, 5, S.off.flags_dots, -1, 0);
+}
+
 inline int ch_for(int groups) {
   int ch = (groups + 31) / 32;
   return ch <= 1 ? 1 : ch <= 2 ? 2 : ch <= 4 ? 4 : ch <= 8 ? 8 : -1;
@@ -285,6 +401,21 @@ cudaError_t gather_ch(const ShardK& S, const VT* values, int* err, cudaStream_t 
   return cudaGetLastError();
 }
 
+template <typename VT, int VEC>
+cudaError_t dots_ch(const ShardK& S, const VT* values, int* err, cudaStream_t s) {
+  const int64_t warps = (int64_t)S.world * S.mcap;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+  switch (ch_for(S.d / VEC)) {
+    case 1: shard_dots_kernel<VT, VEC, 1><<<grid, 256, 0, s>>>(S, values, err); break;
+    case 2: shard_dots_kernel<VT, VEC, 2><<<grid, 256, 0, s>>>(S, values, err); break;
+    case 4: shard_dots_kernel<VT, VEC, 4><<<grid, 256, 0, s>>>(S, values, err); break;
+    case 8: shard_dots_kernel<VT, VEC, 8><<<grid, 256, 0, s>>>(S, values, err); break;
+    default: return cudaErrorInvalidValue;
+  }
+  count_launch();
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 ShardOff shard_layout(int world, int64_t mcap, int hk, int d) {
@@ -294,10 +425,15 @@ ShardOff shard_layout(int world, int64_t mcap, int hk, int d) {
   o.flags_part = 256;
   o.meta = 512;
   o.tickets = 768;
-  o.cnt = 1024;
+  o.flags_probe = 1024;
+  o.flags_dots = 1280;
+  o.bmeta = 1536;
+  o.cnt = 1792;
   o.inbox = o.cnt + up((int64_t)world * mcap * 4);
   o.part = o.inbox + up((int64_t)world * mcap * hk * 8);
-  o.bytes = o.part + up((int64_t)world * mcap * d * 4);
+  o.probe = o.part + up((int64_t)world * mcap * d * 4);
+  o.dots = o.probe + up(mcap * d * 4);
+  o.bytes = o.dots + up((int64_t)world * mcap * hk * 4);
   return o;
 }
 
@@ -341,6 +477,23 @@ cudaError_t launch_shard_reduce(const Dims& D, const ShardK& S, const int* own_c
   shard_reduce_kernel<<<grid, 256, 0, s>>>(S, D.M, own_cnt, gate, out, memg, memg_hi, memg_lo, err);
   count_launch();
   return cudaGetLastError();
+}
+
+cudaError_t launch_shard_probe(const ShardK& S, int64_t M, const float* dmemg, const float* zg, const float* mem,
+                               float* probe, float* memg, float* dzg, cudaStream_t s) {
+  // at least one CTA, to publish an empty call
+  const int64_t n = M * S.d;
+  const int64_t blocks = (n + 255) / 256;
+  const unsigned grid = (unsigned)(blocks < 1 ? 1 : blocks < 148 * 8 ? blocks : 148 * 8);
+  shard_probe_kernel<<<grid, 256, 0, s>>>(S, M, dmemg, zg, mem, probe, memg, dzg);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_shard_dots(const Dims& D, const ShardK& S, const void* values, int* err, cudaStream_t s) {
+  if (D.vdtype == MEMLAYER_F16) return dots_ch<__half, 8>(S, (const __half*)values, err, s);
+  if (D.vdtype == MEMLAYER_BF16) return dots_ch<__nv_bfloat16, 8>(S, (const __nv_bfloat16*)values, err, s);
+  return dots_ch<float, 4>(S, (const float*)values, err, s);
 }
 
 }  // namespace ml

@@ -12,10 +12,16 @@ struct ShardOff {
   int64_t flags_in;    // [2 halves][MAX] int: epoch of the inbox each source rank has filled
   int64_t flags_part;  // [2][MAX] int: epoch of the partials each owner rank has stored
   int64_t meta;        // [2][MAX][2] int: token range [lo, hi) of each source rank's half
-  int64_t tickets;     // [2][2] int: CTA completion counters of push / gather (local use)
+  int64_t tickets;     // [2][2] int: CTA completion counters of push / gather (local use);
+                       // [4], [5]: probe / dots kernels of the backward
+  int64_t flags_probe; // [MAX] int (backward): epoch of the probe rows each source rank has stored
+  int64_t flags_dots;  // [MAX] int (backward): epoch of the dots each owner rank has stored
+  int64_t bmeta;       // [MAX] int (backward): token count of each source rank's call
   int64_t cnt;         // [world][mcap] int: entries from source rank per token
   int64_t inbox;       // [world][mcap][hk] int2: (local row, weight bits) per entry
   int64_t part;        // [world][mcap][d] float: partial sum of owner rank per token
+  int64_t probe;       // [mcap][d] float (backward): this rank's d loss / d read output
+  int64_t dots;        // [world][mcap][hk] float (backward): probe . row per inbox entry, from each owner
   int64_t bytes;       // total
 };
 
@@ -132,6 +138,17 @@ cudaError_t launch_shard_gather(const Dims& D, const ShardK& S, const void* valu
 cudaError_t launch_shard_reduce(const Dims& D, const ShardK& S, const int* own_cnt, const float* gate, float* out,
                                 float* memg, float* memg_hi, float* memg_lo, int* err, cudaStream_t s);
 
+// ---- backward of the sharded layer (after its forward, on the same communicator) ----
+// Reader side: probe = dmemg * silu(zg) (model.py:118-119) for this rank's
+// M tokens, stored into the caller's probe and this rank's buffer, with
+// memg = mem * gate and dzg; then publishes the probe rows and M to every rank.
+cudaError_t launch_shard_probe(const ShardK& S, int64_t M, const float* dmemg, const float* zg, const float* mem,
+                               float* probe, float* memg, float* dzg, cudaStream_t s);
+// Owner side: for every inbox entry of the forward, probe . V[local row]
+// (lanes over d, then a warp sum: the single-GPU backward's order), stored
+// into the source rank's dots.
+cudaError_t launch_shard_dots(const Dims& D, const ShardK& S, const void* values_local, int* err, cudaStream_t s);
+
 }  // namespace ml
 
 // The communicator behind the C ABI's opaque memlayer_shard_comm.
@@ -143,6 +160,7 @@ struct memlayer_shard_comm {
   char* peer[MEMLAYER_MAX_SHARDS] = {};       // every rank's buffer as seen from this GPU
   bool opened[MEMLAYER_MAX_SHARDS] = {};      // mapped through cudaIpcOpenMemHandle
   int epoch = 0;                              // last call started by the route phase
+  int bwd_epoch = 0;                          // forward epoch whose backward has started
   // kind 1: row-update communicator (memlayer_shard_comm_create_rowgrad)
   int kind = 0;
   int n_reads = 0;                            // reads (memory layers) per call it was sized for

@@ -311,33 +311,41 @@ class MemoryLayer:
         parameter names (``router_i`` / ``mem_gate_i`` / ``mem_out_i`` kernel
         and bias, ``pool`` sub_keys and log_temperature), ``h``, and
         ``probe`` = d loss / d read output, the row update's input."""
-        P = self.pool
         dev = ctx["device"]
-        M, dm, d = ctx["M"], self.d_model, P.d_value
-        dy = _cuda_f32(dy, "dy").reshape(M, dm)
+        dy = _cuda_f32(dy, "dy").reshape(ctx["M"], self.d_model)
+        g, ga, ws, nb = self._grad_setup(ctx["cfg"], ctx["M"], dev, dy, balance_coef, route_through_pool, ctx["ws"])
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        L.check(L.lib().memlayer_layer_backward(C.byref(ctx["cfg"]), C.byref(ctx["la"]), C.byref(ga), ws.data_ptr(),
+                                                nb, s), "memlayer_layer_backward")
+        if check:
+            _raise_device_status(ctx["cfg"], ws, s)
+        return self._grad_result(g)
+
+    def _grad_setup(self, cfg, M: int, dev, dy: torch.Tensor, balance_coef: float, route_through_pool: bool,
+                    forward_ws: torch.Tensor):
+        """Gradient outputs, their memlayer_layer_grads and the backward workspace."""
+        P = self.pool
+        dm, d = self.d_model, P.d_value
         g = {"h": torch.empty(M, dm, device=dev), "w_router": torch.empty(dm, P.heads * P.d_key, device=dev),
              "b_router": torch.empty(P.heads * P.d_key, device=dev),
              "sub_keys": torch.empty(P.heads, 2, P.n_sub_keys, P.d_key // 2, device=dev),
              "log_temperature": torch.empty(1, device=dev), "w_gate": torch.empty(dm, d, device=dev),
              "b_gate": torch.empty(d, device=dev), "w_out": torch.empty(d, dm, device=dev),
-             "b_out": torch.empty(dm, device=dev), "probe": torch.empty(M, d, device=dev)}
+             "b_out": torch.empty(dm, device=dev), "probe": torch.empty(M, d, device=dev), "dy": dy}
         ga = L.MemlayerLayerGrads(dy=dy.data_ptr(), balance_coef=float(balance_coef),
                                   route_through_pool=int(bool(route_through_pool)),
-                                  forward_workspace=ctx["ws"].data_ptr(), dh=g["h"].data_ptr(),
+                                  forward_workspace=forward_ws.data_ptr(), dh=g["h"].data_ptr(),
                                   dw_router=g["w_router"].data_ptr(), db_router=g["b_router"].data_ptr(),
                                   dsub_keys=g["sub_keys"].data_ptr(), dlog_temperature=g["log_temperature"].data_ptr(),
                                   dw_gate=g["w_gate"].data_ptr(), db_gate=g["b_gate"].data_ptr(),
                                   dw_out=g["w_out"].data_ptr(), db_out=g["b_out"].data_ptr(),
                                   probe=g["probe"].data_ptr())
         nb = C.c_size_t()
-        L.check(L.lib().memlayer_layer_backward_workspace_size(C.byref(ctx["cfg"]), int(balance_coef != 0.0),
-                                                               C.byref(nb)), "memlayer_layer_backward_workspace_size")
-        ws = _workspace(nb.value, dev)
-        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
-        L.check(L.lib().memlayer_layer_backward(C.byref(ctx["cfg"]), C.byref(ctx["la"]), C.byref(ga), ws.data_ptr(),
-                                                nb.value, s), "memlayer_layer_backward")
-        if check:
-            _raise_device_status(ctx["cfg"], ws, s)
+        L.check(L.lib().memlayer_layer_backward_workspace_size(C.byref(cfg), int(balance_coef != 0.0), C.byref(nb)),
+                "memlayer_layer_backward_workspace_size")
+        return g, ga, _workspace(nb.value, dev), nb.value
+
+    def _grad_result(self, g) -> Dict[str, Any]:
         i = self.layer
         return {"h": g["h"], f"router_{i}": {"kernel": g["w_router"], "bias": g["b_router"]},
                 f"mem_gate_{i}": {"kernel": g["w_gate"], "bias": g["b_gate"]},

@@ -192,6 +192,39 @@ class ShardedCall:
         return self.y, self.mem, self.layer.pool._aux(self.keep, self.lead, self.stats)
 
 
+class ShardedBackward:
+    """The backward of one :class:`ShardedCall` (memlayer_layer_backward_sharded)
+    on the same communicator, once per forward and after it.  Like the
+    forward, its three phases can be run separately: ROUTE publishes this
+    rank's probe rows, GATHER computes this owner's dots for every rank's
+    reads of its rows, REDUCE finishes this rank's gradients."""
+
+    def __init__(self, call: ShardedCall, dy: torch.Tensor, *, balance_coef: float = 0.0,
+                 route_through_pool: bool = False):
+        if balance_coef != 0.0 and not call.stats:
+            raise ValueError("balance_coef != 0 needs the forward run with stats=True")
+        self.call = call
+        M = call.cfg.tokens
+        dy = _cuda_f32(dy, "dy").reshape(M, call.layer.d_model)
+        self.g, self.ga, self.ws, self.nbytes = call.layer._grad_setup(call.cfg, M, call.h.device, dy, balance_coef,
+                                                                       route_through_pool, call.ws)
+
+    def run(self, phases: int = L.PHASE_ALL, stream: Optional[torch.cuda.Stream] = None) -> None:
+        c = self.call
+        s = (stream or torch.cuda.current_stream(c.h.device)).cuda_stream
+        L.check(L.lib().memlayer_layer_backward_sharded(C.byref(c.cfg), C.byref(c.args), C.byref(self.ga),
+                                                        c.comm.handle, phases, self.ws.data_ptr(), self.nbytes, s),
+                "memlayer_layer_backward_sharded")
+
+    def check(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.call.h.device)).cuda_stream
+        _raise_device_status(self.call.cfg, self.ws, s)
+
+    def result(self) -> Dict:
+        """The gradients of this rank's tokens, keyed as MemoryLayer.backward's."""
+        return self.call.layer._grad_result(self.g)
+
+
 class ShardedMemoryLayer:
     """MemoryLayer whose value table is row-sharded over a communicator's
     ranks.  ``params["pool"]["values"]`` is this rank's local shard
@@ -213,3 +246,28 @@ class ShardedMemoryLayer:
         if check:
             call.check(stream)
         return call.result()
+
+    @on_stream
+    def apply_train(self, params, h: torch.Tensor, *, check: bool = False, stream=None, split: bool = False, **kw):
+        """The training forward (selection noise and routing statistics on,
+        as MemoryLayer.apply_train): returns (y, mem, aux, ctx), ``ctx`` for
+        :meth:`backward`."""
+        kw.setdefault("train", True)
+        kw.setdefault("stats", True)
+        call = ShardedCall(self.layer, self.comm, params, h, **kw)
+        call.run(L.PHASE_ALL | (L.PHASE_SPLIT if split else 0), stream)
+        if check:
+            call.check(stream)
+        return call.result() + (call,)
+
+    @on_stream
+    def backward(self, ctx: ShardedCall, dy: torch.Tensor, *, balance_coef: float = 0.0,
+                 route_through_pool: bool = False, check: bool = False, stream=None) -> Dict:
+        """MemoryLayer.backward for this rank's tokens; every rank calls it
+        for the same forward.  The Dense, sub-key and temperature gradients
+        are this rank's share, to be summed over the ranks."""
+        b = ShardedBackward(ctx, dy, balance_coef=balance_coef, route_through_pool=route_through_pool)
+        b.run(L.PHASE_ALL, stream)
+        if check:
+            b.check(stream)
+        return b.result()
