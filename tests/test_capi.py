@@ -153,3 +153,22 @@ def test_layer_backward_arguments_rejected_on_the_host():
     assert lib.memlayer_layer_backward(C.byref(c), C.byref(la), C.byref(g), 1 << 20, 64, None) == L.ERR_WORKSPACE
     assert lib.memlayer_layer_backward(C.byref(c), C.byref(la), C.byref(g), (1 << 20) + 16, nb.value,
                                        None) == L.ERR_WORKSPACE
+
+
+def test_sharded_layer_backward_arguments_rejected_on_the_host():
+    lib = L.lib()
+    c = cfg(tokens=64, d_key=64, d_value=64, d_model=64)
+    la = L.MemlayerLayerArgs(h=256, w_router=256, w_gate=256, w_out=256, y=256, mem=256,
+                             pool=L.MemlayerPoolArgs(sub_keys=256, log_temperature=256, values=256, slots=256,
+                                                     weights=256))
+    g = L.MemlayerLayerGrads(dy=256, balance_coef=0.0)
+    nb = C.c_size_t()
+    assert lib.memlayer_layer_backward_workspace_size(C.byref(c), 0, C.byref(nb)) == L.OK
+    # no communicator
+    assert lib.memlayer_layer_backward_sharded(C.byref(c), C.byref(la), C.byref(g), None, L.PHASE_ALL, 1 << 20,
+                                               nb.value, None) == L.ERR_BAD_POINTER
+    # phases outside ROUTE / GATHER / REDUCE are refused before the communicator is read
+    not_a_comm = C.create_string_buffer(64)
+    for phases in (0, L.PHASE_ALL | L.PHASE_SPLIT, 16):
+        assert lib.memlayer_layer_backward_sharded(C.byref(c), C.byref(la), C.byref(g), C.addressof(not_a_comm),
+                                                   phases, 1 << 20, nb.value, None) == L.ERR_BAD_SHAPE
