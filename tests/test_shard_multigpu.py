@@ -134,3 +134,60 @@ def test_owner_sharded_update_across_gpus(world, tmp_path):
     for rank in range(world):
         e_v, e_a, e_s = np.load(tmp_path / f"row{rank}.npy")
         assert e_v <= 1e-5 and e_a <= 1e-5 and e_s <= 1e-6, f"rank {rank}: {e_v:.2e} {e_a:.2e} {e_s:.2e}"
+
+
+def _bwd_worker(rank, world, port, outdir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from model_b200 import MemoryLayer, MemoryPool
+    from model_b200.shard import ShardedMemoryLayer, connect, shard_values
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        pool = MemoryPool(n_sub_keys=128, heads=4, d_key=128, d_value=128, top_k=16, min_temperature=5.0)
+        layer = MemoryLayer(pool, d_model=128, layer=1)
+        params = layer.init(0)                                        # same seed: same weights on every rank
+        M = 300 + 77 * rank
+        gen = torch.Generator("cuda").manual_seed(9 + rank)
+        h = torch.randn(M, 128, device="cuda", generator=gen)
+        dy = torch.randn(M, 128, device="cuda", generator=gen)
+        comm = connect(pool.config(300 + 77 * (world - 1), torch.float32, 128))
+        local = dict(params, pool=dict(params["pool"], values=shard_values(params["pool"]["values"], rank, world)))
+        sharded = ShardedMemoryLayer(layer, comm)
+        for _ in range(2):                                            # two steps on one communicator
+            y, mem, aux, ctx = sharded.apply_train(local, h, train=False, check=True)
+            g = sharded.backward(ctx, dy, balance_coef=0.3, check=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        y0, mem0, aux0, ctx0 = layer.apply_train(params, h, train=False, check=True)
+        g0 = layer.backward(ctx0, dy, balance_coef=0.3, check=True)
+        torch.cuda.synchronize()
+        errs = [0.0 if torch.equal(aux["slots"], aux0["slots"]) else 1.0]
+        for a, b in ((g["h"], g0["h"]), (g["probe"], g0["probe"]),
+                     (g["router_1"]["kernel"], g0["router_1"]["kernel"]),
+                     (g["mem_gate_1"]["kernel"], g0["mem_gate_1"]["kernel"]),
+                     (g["mem_out_1"]["kernel"], g0["mem_out_1"]["kernel"]),
+                     (g["pool"]["sub_keys"], g0["pool"]["sub_keys"]),
+                     (g["pool"]["log_temperature"], g0["pool"]["log_temperature"])):
+            errs.append(float((a - b).abs().max() / b.abs().max().clamp_min(1e-12)))
+        np.save(os.path.join(outdir, f"bwd{rank}.npy"), np.array(errs))
+        dist.barrier()
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_backward_across_gpus(world, tmp_path):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    mp.spawn(_bwd_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for rank in range(world):
+        errs = np.load(tmp_path / f"bwd{rank}.npy")
+        assert errs[0] == 0.0, f"rank {rank}: routing differs"
+        assert (errs[1:] <= 1e-5).all(), f"rank {rank}: gradient errors {errs[1:]}"
