@@ -1,8 +1,9 @@
 """Host-side logic of the row-sharded pool, on CPU: the striping of the value
-table, the C ABI's argument checks and sizes (no CUDA call is reached), and a
-world-size-2 gloo run of the sharded read -- every rank gathers the rows it
+table, the C ABI's argument checks and sizes (no CUDA call is reached), and
+world-size-2 gloo runs of the sharded read -- every rank gathers the rows it
 owns for every rank's tokens and the token owner adds the partials in rank
-order -- checked against the single-table oracle."""
+order -- and of the sharded backward's dot exchange, checked against the
+single-table oracle."""
 
 import ctypes as C
 import os
@@ -132,3 +133,65 @@ def test_gloo_two_ranks_sharded_read(tmp_path):
     mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     for rank in range(2):
         assert float(np.load(tmp_path / f"err{rank}.npy")[0]) <= 1e-6
+
+
+# ---------------------------------------------------------------------------
+# world-size-2 gloo run of the sharded backward's exchange: every rank sends
+# its probe rows, each owner returns probe . row for its entries of every
+# rank's reads in inbox order (per (source, token, owner): heads in order,
+# then lanes), and the reader maps the dots back to (head, lane) as the
+# routing backward does -- checked against the whole-table dots
+# ---------------------------------------------------------------------------
+def _inbox_order(own, o):
+    """(head, lane) of each entry of owner `o` for one token, in inbox order."""
+    return [(h, j) for h in range(own.shape[0]) for j in range(own.shape[1]) if own[h, j] == o]
+
+
+def _bwd_worker(rank, world, port, outdir):
+    import torch.distributed as dist
+
+    from oracle import memlayer_ref as ref
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = ref.PoolConfig(n_sub_keys=16, heads=2, d_key=16, d_value=8, top_k=4)
+        rng = np.random.default_rng(0)
+        N, d, M, H, k = cfg.pool_size, cfg.d_value, 24, cfg.heads, cfg.top_k
+        sub_keys = rng.standard_normal((H, 2, 16, 8)).astype(np.float32)
+        values = rng.standard_normal((N, d))
+        local = values[rank::world]
+        q = np.random.default_rng(100 + rank).standard_normal((M, H, cfg.d_key)).astype(np.float32)
+        read = (ref.route(cfg, q, sub_keys, float(np.log(10.0)))["slots"].astype(np.int64) + N // 2 + 1) % N
+        probe = np.random.default_rng(200 + rank).standard_normal((M, d))
+        # ROUTE: every owner sees every rank's reads and probe rows
+        all_r = [torch.empty(M, H, k, dtype=torch.int64) for _ in range(world)]
+        all_p = [torch.empty(M, d, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(all_r, torch.from_numpy(read))
+        dist.all_gather(all_p, torch.from_numpy(probe))
+        # GATHER: this owner's dots per (source, token), in inbox order
+        dots = np.zeros((world, M, H * k))
+        for src in range(world):
+            rs, pr = all_r[src].numpy(), all_p[src].numpy()
+            for m in range(M):
+                for i, (h, j) in enumerate(_inbox_order(rs[m] % world, rank)):
+                    dots[src, m, i] = pr[m] @ local[rs[m, h, j] // world]
+        back = [torch.empty(world, M, H * k, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(back, torch.from_numpy(dots))
+        # REDUCE: the reader finds each read's dot from its owner's list
+        dw = np.zeros((M, H, k))
+        for m in range(M):
+            for o in range(world):
+                for i, (h, j) in enumerate(_inbox_order(read[m] % world, o)):
+                    dw[m, h, j] = back[o][rank, m, i].item()
+        want = np.einsum("md,mhkd->mhk", probe, values[read])
+        np.save(os.path.join(outdir, f"bwd{rank}.npy"), np.array([np.abs(dw - want).max() / np.abs(want).max()]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_sharded_backward_dots(tmp_path):
+    import torch.multiprocessing as mp
+    mp.spawn(_bwd_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for rank in range(2):
+        assert float(np.load(tmp_path / f"bwd{rank}.npy")[0]) <= 1e-12
