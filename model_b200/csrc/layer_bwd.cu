@@ -14,8 +14,11 @@
 //                      split onto the two halves' sub-keys (slot = a n + b);
 //                      per distinct sub-key it adds dcos k_hat into d q_hat
 //                      and emits (sub-key, dcos) entries whose q_hat-weighted
-//                      sums are the sparse sub-key gradient;
-//   bal_row_kernel     (balance term) per (token, codebook) row the softmax
+//                      sums are the sparse sub-key gradient; on a
+//                      row-sharded table (SH) probe, mem * gate and the
+//                      gate gradient come from shard.cu's probe kernel and
+//                      each dw_r from the dots its row's owner returned;
+//   bal_row_kernel    (balance term) per (token, codebook) row the softmax
 //                      of p over all n keys from the recomputed cosines, and
 //                      d p = s (dP - sum dP s) / M turned into d cos;
 //   plain GEMMs        (recomputed projections, Dense-layer gradients, the
