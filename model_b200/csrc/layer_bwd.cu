@@ -18,7 +18,7 @@
 //                      row-sharded table (SH) probe, mem * gate and the
 //                      gate gradient come from shard.cu's probe kernel and
 //                      each dw_r from the dots its row's owner returned;
-//   bal_row_kernel    (balance term) per (token, codebook) row the softmax
+//   bal_row_kernel     (balance term) per (token, codebook) row the softmax
 //                      of p over all n keys from the recomputed cosines, and
 //                      d p = s (dP - sum dP s) / M turned into d cos;
 //   plain GEMMs        (recomputed projections, Dense-layer gradients, the
