@@ -69,6 +69,15 @@ def test_sharded_workspace_and_entry_checks():
                                               None) == L.ERR_BAD_POINTER
 
 
+def test_sharded_backward_needs_the_forward_statistics_for_the_balance_term():
+    import types
+
+    from model_b200.shard import ShardedBackward
+    call = types.SimpleNamespace(stats=False)      # a forward run without routing statistics
+    with pytest.raises(ValueError, match="stats=True"):
+        ShardedBackward(call, torch.zeros(1, 4), balance_coef=0.1)
+
+
 # ---------------------------------------------------------------------------
 # world-size-2 gloo run of the sharded read
 # ---------------------------------------------------------------------------
