@@ -42,6 +42,8 @@ WORKLOAD = dict(name="cfg0_layer_forward", tokens_per_gpu=8192, d_model=256, hea
                 top_k=16, d_value=256, values_dtype="f32", seed=0)
 FLUSH_BYTES = 256 << 20          # > 126 MB L2
 FALLBACK_HBM_GBS = 6650.0
+NOMINAL_HBM_GBS = 8000.0         # B200 HBM3e as NVIDIA quotes it (DGX; 7700 on HGX), for context
+NOMINAL_TF32_TFLOPS = 1100.0     # dense tf32 tensor peak as NVIDIA quotes it, for context
 
 
 def parse():
@@ -543,10 +545,13 @@ def run_ours(args, W, rank, world):
     score_tf = score_flops / (score_ms * 1e-3) / 1e12
     kernels = {
         gname: {"bound": "hbm", "ms": gather_ms, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "algorithmic_bytes_per_launch": alg_b,
+                "frac": achieved / hbm, "peak_nominal": NOMINAL_HBM_GBS, "frac_nominal": achieved / NOMINAL_HBM_GBS,
+                "algorithmic_bytes_per_launch": alg_b,
                 "traffic": None if traffic is None else traffic.get("bytes_per_launch")},
         "score_topk_tc_kernel": {"bound": "tensor", "ms": score_ms, "achieved": score_tf, "peak": bf16,
                                  "unit": "TFLOP/s", "frac": score_tf / bf16, "algorithmic_flops_per_launch": score_flops,
+                                 "issued_tf32_tflops": 3 * score_tf,
+                                 "frac_nominal_tf32": 3 * score_tf / NOMINAL_TF32_TFLOPS,
                                  "note": "float32-faithful score GEMM issued as 3 tf32 MMAs per product; "
                                          "peak is the measured dense bf16 figure",
                                  "traffic": None if load_traffic("score_topk_tc_kernel") is None
