@@ -123,3 +123,31 @@ def test_probe_gradient_feeds_the_row_update():
     np.add.at(dense, g["slots"].reshape(-1), (g["weights"][..., None].astype(np.float64)
                                                * g["probe"][:, None, None, :]).reshape(-1, cfg.d_value))
     np.testing.assert_allclose(rows, dense[uniq], rtol=1e-5, atol=1e-6)
+
+
+def _grads(cfg, p, values, dy, bal=0.0):
+    return ref.layer_backward(cfg, p["h"], p["w_router"], p["b_router"], p["sub_keys"], p["log_temperature"],
+                              values, p["w_gate"], p["b_gate"], p["w_out"], p["b_out"], dy, balance_coef=bal)
+
+
+def test_clamped_temperature_passes_gradient_and_balance_reaches_it_only_when_asked():
+    """test_memory_pool.py:79-101, gradient half: a temperature clamped at
+    its floor still gets the read loss's gradient (straight-through,
+    memory.py:141-146: d T / d log_t = the clamped T), and the balance loss
+    moves the temperature only under balance_temperature_grad."""
+    cfg, p, values, dy = _setup(3)                            # floor 5
+    clamped = dict(p, log_temperature=np.float32(np.log(2.0)))
+    at_floor = dict(p, log_temperature=np.float32(np.log(5.0)))
+    g_c, g_f = _grads(cfg, clamped, values, dy), _grads(cfg, at_floor, values, dy)
+    assert g_c["log_temperature"] != 0.0
+    assert np.array_equal(g_c["slots"], g_f["slots"])
+    np.testing.assert_allclose(g_c["log_temperature"], g_f["log_temperature"], rtol=1e-6)
+    zero = np.zeros_like(dy)
+    for btgrad in (False, True):
+        cfg_b, p_b, values_b, _ = _setup(3, btgrad=btgrad)
+        g_b = _grads(cfg_b, p_b, values_b, zero, bal=1.0)
+        if btgrad:
+            assert g_b["log_temperature"] != 0.0
+        else:
+            assert g_b["log_temperature"] == 0.0
+            assert np.abs(g_b["sub_keys"]).max() > 0.0          # the balance term still reaches the keys
