@@ -145,7 +145,7 @@ def test_gloo_two_ranks_sharded_read(tmp_path):
 
 
 # ---------------------------------------------------------------------------
-# world-size-2 gloo run of the sharded backward's exchange: every rank sends
+# gloo runs (2 and 3 ranks) of the sharded backward's exchange: every rank sends
 # its probe rows, each owner returns probe . row for its entries of every
 # rank's reads in inbox order (per (source, token, owner): heads in order,
 # then lanes), and the reader maps the dots back to (head, lane) as the
@@ -199,8 +199,9 @@ def _bwd_worker(rank, world, port, outdir):
         dist.destroy_process_group()
 
 
-def test_gloo_two_ranks_sharded_backward_dots(tmp_path):
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_ranks_sharded_backward_dots(world, tmp_path):
     import torch.multiprocessing as mp
-    mp.spawn(_bwd_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    for rank in range(2):
+    mp.spawn(_bwd_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for rank in range(world):
         assert float(np.load(tmp_path / f"bwd{rank}.npy")[0]) <= 1e-12
