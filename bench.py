@@ -70,6 +70,12 @@ def parse():
     ap.add_argument("--emulate-ranks", type=int, default=0,
                     help="time the row-sharded phases of P ranks driven from one process on one GPU "
                          "(all ROUTE, then all GATHER, then all REDUCE); for profiling without NVLink")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="row-sharded pool (N > 1): partial rows stored into the token owners' memory by the "
+                         "gather kernel (p2p), or the staged baseline: NCCL all-gather of the routing entries "
+                         "and reduce-scatter of the partial rows between the library's phases (nccl)")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="N > 1: skip the check of the sharded result against the single-GPU layer")
     ap.add_argument("--pool", choices=["sharded", "replicated"], default="sharded",
                     help="N>1: row-shard the value table over the ranks (default) or replicate it")
     return ap.parse_args()
@@ -224,23 +230,91 @@ class ShardedLayerCall(LayerCall):
         self.ws = torch.empty(nb.value, dtype=torch.uint8, device=device)
         self.ws_bytes = nb.value
 
-    def __call__(self, stream, events=None, phase_events=None):
-        """phase_events None: one call, the two token halves overlapped
-        (the step the bench times); else the three phases one after another
-        with events between them (times the owner-side gather alone)."""
+    def set_io(self, h, y):
+        self.args.h, self.args.y = h.data_ptr(), y.data_ptr()
+
+    def __call__(self, stream, events=None, phase_events=None, split=False):
+        """phase_events None: one call (``split``: the two token halves
+        overlapped); else the three phases one after another with events
+        between them (times the owner-side gather alone)."""
         for i in range(self.L.STAGE_EVENTS):
             self.events.events[i] = None if events is None else events[i].cuda_event
         f = self.L.lib().memlayer_layer_forward_sharded
         if phase_events is None:
             self.L.check(f(C.byref(self.cfg), C.byref(self.args), self.comm.handle,
-                           self.L.PHASE_ALL | self.L.PHASE_SPLIT, self.ws.data_ptr(), self.ws_bytes,
-                           stream.cuda_stream), "memlayer_layer_forward_sharded")
+                           self.L.PHASE_ALL | (self.L.PHASE_SPLIT if split else 0), self.ws.data_ptr(),
+                           self.ws_bytes, stream.cuda_stream), "memlayer_layer_forward_sharded")
             return
         for j, ph in enumerate((self.L.PHASE_ROUTE, self.L.PHASE_GATHER, self.L.PHASE_REDUCE)):
             self.L.check(f(C.byref(self.cfg), C.byref(self.args), self.comm.handle, ph, self.ws.data_ptr(),
                            self.ws_bytes, stream.cuda_stream), "memlayer_layer_forward_sharded")
             if phase_events is not None and j < 2:
                 phase_events[j].record(stream)
+
+
+class StagedLayerCall(LayerCall):
+    """The row-sharded layer with the NCCL exchange (the baseline the fused
+    peer-store gather is measured against): memlayer_layer_forward_staged's
+    ROUTE, an NCCL all-gather of every rank's packed (slot, weight) entries,
+    GATHER of this rank's rows for every rank's tokens, an NCCL
+    reduce-scatter of the partial rows, REDUCE (gate and output projection),
+    all on one stream."""
+
+    def __init__(self, torch, L, W, x, device, values_dtype, rank, world):
+        super().__init__(torch, L, W, x, device, values_dtype)
+        T, H, k, d = (W[q] for q in ("tokens_per_gpu", "heads", "top_k", "d_value"))
+        self.rank, self.world = rank, world
+        self.route = torch.empty(world, 2, T * H * k, dtype=torch.int32, device=device)
+        mine = self.route[rank]
+        self.slots = mine[0].view(T, H, k)
+        self.weights = mine[1].view(torch.float32).view(T, H, k)
+        self.args.pool.slots, self.args.pool.weights = self.slots.data_ptr(), self.weights.data_ptr()
+        self.partials = torch.empty(world, T, d, device=device)
+        self.mem_in = torch.empty(T, d, device=device)
+        self.sargs = L.MemlayerStagedArgs(all_slots=self.route.data_ptr(), all_weights=self.route[0, 1].data_ptr(),
+                                          route_stride=2 * T * H * k, partials=self.partials.data_ptr(),
+                                          mem=self.mem_in.data_ptr(), rank=rank, world=world)
+
+    def set_io(self, h, y):
+        self.args.h, self.args.y = h.data_ptr(), y.data_ptr()
+
+    def _phase(self, ph, stream):
+        self.L.check(self.L.lib().memlayer_layer_forward_staged(C.byref(self.cfg), C.byref(self.args),
+                                                                C.byref(self.sargs), ph, self.ws.data_ptr(),
+                                                                self.ws_bytes, stream.cuda_stream),
+                     "memlayer_layer_forward_staged")
+
+    def __call__(self, stream, events=None, phase_events=None, split=False):
+        """events: the route's stage events (0-4) and the end (5);
+        phase_events: after the all-gather, after the gather, after the
+        reduce-scatter."""
+        import torch.distributed as dist
+        for i in range(self.L.STAGE_EVENTS):
+            self.events.events[i] = None if events is None or i == 5 else events[i].cuda_event
+        with self.torch.cuda.stream(stream):
+            self._phase(self.L.PHASE_ROUTE, stream)
+            dist.all_gather_into_tensor(self.route.view(-1), self.route[self.rank].view(-1))
+            if phase_events is not None:
+                phase_events[0].record(stream)
+            self._phase(self.L.PHASE_GATHER, stream)
+            if phase_events is not None:
+                phase_events[1].record(stream)
+            dist.reduce_scatter_tensor(self.mem_in.view(-1), self.partials.view(-1))
+            if phase_events is not None:
+                phase_events[2].record(stream)
+            self._phase(self.L.PHASE_REDUCE, stream)
+            if events is not None:
+                events[5].record(stream)
+
+
+def staged_gather_bytes(W, values_dtype, world):
+    """Algorithmic bytes of one staged gather launch on one rank: its share
+    of all ranks' value rows, every rank's packed routing entries, and the
+    partial rows it writes (one per token of every rank)."""
+    T, H, k, d = W["tokens_per_gpu"], W["heads"], W["top_k"], W["d_value"]
+    es = {"f32": 4, "f16": 2, "bf16": 2}[values_dtype]
+    rows = T * H * k * d * es
+    return rows, rows + world * T * H * k * 8 + world * T * d * 4
 
 
 def shard_gather_bytes(W, values_dtype, world):
@@ -331,8 +405,9 @@ def cpu_oracle_rate(W, tokens, repeats=3, threads=None):
 def run_reference(args, W, rank):
     if rank != 0:
         return None
-    tokens = min(2048, args.tokens)
-    steps = max(1, args.steps // 20)
+    # every step is one forward of the full token batch on all host cores
+    tokens = args.tokens
+    steps = max(5, min(args.steps, 20))
     rate, cores, sample = cpu_oracle_rate(W, tokens, repeats=steps)
     line = {"impl": "reference", "metric": "memory-layer tokens/s", "value": rate, "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": steps, "warmup": 1, "ms_per_step": 1000.0 * tokens / rate,
@@ -351,24 +426,44 @@ def run_ours(args, W, rank, world):
     torch.cuda.set_device(device)
     lib = L.lib()
     sharded = world > 1 and args.pool == "sharded"
-    rows = None
+    staged = sharded and args.exchange == "nccl"
+    T, dm = W["tokens_per_gpu"], W["d_model"]
+    full_values = None
     if sharded:
-        from model_b200.shard import shard_rows
-        rows = shard_rows(W["n_sub_keys"] ** 2, rank, world)
-    x = make_inputs(torch, device, W, args.values_dtype, W["seed"] + rank, rows)
-    call = (ShardedLayerCall if sharded else LayerCall)(torch, L, W, x, device, args.values_dtype)
+        # one model on every rank: the same parameters and table (each rank
+        # keeps its rows s % world == rank), each rank's own tokens
+        x = make_inputs(torch, device, W, args.values_dtype, W["seed"])
+        full_values = x["values"]
+        x["values"] = full_values[rank::world].contiguous()
+        if args.no_parity:
+            full_values = None
+        g = torch.Generator(device=device).manual_seed(W["seed"] + 1 + rank)
+        x["h"] = torch.randn(T, dm, device=device, generator=g)
+        torch.cuda.empty_cache()
+    else:
+        x = make_inputs(torch, device, W, args.values_dtype, W["seed"] + rank)
+    if staged:
+        call = StagedLayerCall(torch, L, W, x, device, args.values_dtype, rank, world)
+    else:
+        call = (ShardedLayerCall if sharded else LayerCall)(torch, L, W, x, device, args.values_dtype)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
-    T = W["tokens_per_gpu"]
+    overlapped = sharded and args.split and not staged
+
+    def step(events=None, phase_events=None):
+        if sharded:
+            call(stream, events, phase_events, split=overlapped and phase_events is None)
+        else:
+            call(stream, events)
 
     for _ in range(args.warmup):
         flush.zero_()
-        call(stream)
+        step()
     torch.cuda.synchronize()
 
     K = args.steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(L.STAGE_EVENTS)] for _ in range(K)]
-    pev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)] if sharded else None
+    pev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)] if sharded else None
     for row in ev:                 # create the driver events before handing them to the library
         for e in row:
             e.record(stream)
@@ -377,20 +472,20 @@ def run_ours(args, W, rank, world):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    overlapped = sharded and args.split
     with ClockSampler(device.index) as clk:
         for i in range(K):
             flush.zero_()
             if sharded and not overlapped:
-                call(stream, ev[i], pev[i])    # the three phases, events between them
+                step(ev[i], pev[i])     # the phases one after another, events between them
             else:
-                call(stream, ev[i])            # single GPU, or one split call
+                step(ev[i])             # single GPU, or one split call
         torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     launches = (lib.memlayer_kernel_launch_count() - launches0) // K
     step_ms = [ev[i][0].elapsed_time(ev[i][5]) for i in range(K)]
     stage = lambda a, b: statistics.mean(ev[i][a].elapsed_time(ev[i][b]) for i in range(K))  # noqa: E731
+    pstage = lambda f: statistics.mean(f(i) for i in range(K))  # noqa: E731
     stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
               "combine_gather": stage(3, 4), "finalize_out": stage(4, 5)}
     if not sharded:
@@ -414,14 +509,20 @@ def run_ours(args, W, rank, world):
                   "score_and_first_half_gather": stage(2, 3), "second_half_gather": stage(3, 4),
                   "finalize_out": stage(4, 5),
                   "score_topk": gst(2, 3), "combine_gather": gst(3, 4), "unoverlapped_step": gst(0, 5)}
-    if sharded and not overlapped:
-        pstage = lambda f: statistics.mean(f(i) for i in range(K))  # noqa: E731
+    elif staged:
+        stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
+                  "combine": stage(3, 4),
+                  "finalize_allgather": pstage(lambda i: ev[i][4].elapsed_time(pev[i][0])),
+                  "staged_gather_alone": pstage(lambda i: pev[i][0].elapsed_time(pev[i][1])),
+                  "reduce_scatter": pstage(lambda i: pev[i][1].elapsed_time(pev[i][2])),
+                  "reduce_out": pstage(lambda i: pev[i][2].elapsed_time(ev[i][5]))}
+    elif not overlapped:
         stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
                   "combine_push": stage(3, 4),
                   "finalize": pstage(lambda i: ev[i][4].elapsed_time(pev[i][0])),
                   "shard_gather_alone": pstage(lambda i: pev[i][0].elapsed_time(pev[i][1])),
                   "reduce_out": pstage(lambda i: pev[i][1].elapsed_time(ev[i][5]))}
-    if overlapped:
+    else:
         stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
                   "combine_push": stage(3, 4), "exchange_reduce_out": stage(4, 5)}
         # the owner-side gather alone: the three phases one after another,
@@ -443,26 +544,76 @@ def run_ours(args, W, rank, world):
     ms = statistics.mean(step_ms)
 
     # ---- e2e through the C ABI with host buffers ----
-    # --inflight calls in flight on as many streams (separate host / staging
-    # buffers per call), as a server runs requests: one call's host-to-device
-    # copy overlaps another's layer, and the calls' kernels overlap on the
-    # GPU (an ALU-bound score kernel beside an HBM-bound gather).  Every step
-    # copies its hidden state in from pinned host memory and its output back;
-    # e2e = K steps of tokens over the device time of all K.  `e2e_serial`
-    # is the same with one call at a time.
+    # Every step copies its hidden state in from pinned host memory and its
+    # output back; e2e = K steps of tokens over the device time of all K.
+    # One GPU: --inflight calls in flight on as many streams (separate host /
+    # staging buffers per call), as a server runs requests: one call's
+    # host-to-device copy overlaps another's layer, and the calls' kernels
+    # overlap on the GPU (an ALU-bound score kernel beside an HBM-bound
+    # gather).  Sharded (every rank in lockstep on its default stream): the
+    # calls run one after another; hidden states and outputs are double
+    # buffered so that the next step's copy in and the previous step's copy
+    # out run on copy streams during the current step.  `e2e_serial` is one
+    # call at a time with its copies around it.
     NF = max(1, args.inflight)
     streams = [stream] + [torch.cuda.Stream(device) for _ in range(NF - 1)]
-    h_hosts = [x["h"].cpu().pin_memory() for _ in range(NF)]
-    y_hosts = [torch.empty_like(call.y, device="cpu").pin_memory() for _ in range(NF)]
+    nbuf = 2 if sharded else NF
+    h_hosts = [x["h"].cpu().pin_memory() for _ in range(nbuf)]
+    y_hosts = [torch.empty_like(call.y, device="cpu").pin_memory() for _ in range(nbuf)]
+    host_issue = []
     if sharded:
-
-        def host_step(j):
-            # the sharded call runs on the default stream (all ranks in lockstep)
-            x["h"].copy_(h_hosts[j], non_blocking=True)
-            call(stream)
-            y_hosts[j].copy_(call.y, non_blocking=True)
+        h_dev = [x["h"], torch.empty_like(x["h"])]
+        y_dev = [call.y, torch.empty_like(call.y)]
+        cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_call = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
         inflight = 1
-        e2e_api = "memlayer_layer_forward_sharded with host copies around it"
+        e2e_api = ("memlayer_layer_forward_staged with NCCL all-gather / reduce-scatter" if staged
+                   else "memlayer_layer_forward_sharded") + \
+            ", host copies double-buffered on two copy streams"
+
+        def e2e_run(pipelined, steps):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            torch.distributed.barrier()
+            start.record(stream)
+            cin.wait_event(start)
+            cout.wait_event(start)
+            t0 = time.perf_counter()
+            for i in range(steps):
+                b = i % 2 if pipelined else 0
+                with torch.cuda.stream(cin):
+                    if i >= 2 or not pipelined:
+                        cin.wait_event(ev_call[b])      # the call that last read h_dev[b] is done
+                    h_dev[b].copy_(h_hosts[b], non_blocking=True)
+                    ev_in[b].record(cin)
+                stream.wait_event(ev_in[b])
+                if i >= 2 or not pipelined:
+                    stream.wait_event(ev_out[b])        # y_dev[b] of an earlier step is copied out
+                call.set_io(h_dev[b], y_dev[b])
+                step()
+                ev_call[b].record(stream)
+                with torch.cuda.stream(cout):
+                    cout.wait_event(ev_call[b])
+                    y_hosts[b].copy_(y_dev[b], non_blocking=True)
+                    ev_out[b].record(cout)
+                if not pipelined:
+                    stream.wait_event(ev_out[b])
+            host_issue.append((time.perf_counter() - t0) * 1e3 / steps)
+            stream.wait_stream(cout)
+            end.record(stream)
+            torch.cuda.synchronize()
+            call.set_io(h_dev[0], y_dev[0])
+            return start.elapsed_time(end) / steps
+
+        for e in ev_call + ev_out:
+            e.record(stream)
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_run(True, 2)
+        e2e_ms = e2e_run(True, K)
+        e2e_host_issue_ms = host_issue[-1]
+        e2e_serial_ms = e2e_run(False, max(1, K // 2))
     else:
         hnb = C.c_size_t()
         L.check(lib.memlayer_layer_host_workspace_size(C.byref(call.cfg), args.host_chunks, C.byref(hnb)), "host ws")
@@ -487,31 +638,69 @@ def run_ours(args, W, rank, world):
         e2e_api = (f"memlayer_layer_forward_host ({args.host_chunks} chunk(s), pinned host h / y), "
                    f"{NF} calls in flight on {NF} streams")
 
-    host_issue = []
+        def e2e_run(n_inflight, steps):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            start.record(stream)
+            for st in streams[1:n_inflight]:
+                st.wait_event(start)
+            t0 = time.perf_counter()
+            for i in range(steps):
+                with torch.cuda.stream(streams[i % n_inflight]):
+                    host_step(i % n_inflight)
+            host_issue.append((time.perf_counter() - t0) * 1e3 / steps)   # host time to issue one call
+            for st in streams[1:n_inflight]:
+                stream.wait_stream(st)
+            end.record(stream)
+            torch.cuda.synchronize()
+            return start.elapsed_time(end) / steps
 
-    def e2e_run(n_inflight, steps):
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        start.record(stream)
-        for st in streams[1:n_inflight]:
-            st.wait_event(start)
-        t0 = time.perf_counter()
-        for i in range(steps):
-            with torch.cuda.stream(streams[i % n_inflight]):
-                host_step(i % n_inflight)
-        host_issue.append((time.perf_counter() - t0) * 1e3 / steps)   # host time to issue one call
-        for st in streams[1:n_inflight]:
-            stream.wait_stream(st)
-        end.record(stream)
-        torch.cuda.synchronize()
-        return start.elapsed_time(end) / steps
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_run(inflight, 2)
+        e2e_ms = e2e_run(inflight, K)
+        e2e_host_issue_ms = host_issue[-1]
+        e2e_serial_ms = e2e_run(1, max(1, K // 2))
 
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_run(inflight, 2)
-    e2e_ms = e2e_run(inflight, K)
-    e2e_host_issue_ms = host_issue[-1]
-    e2e_serial_ms = e2e_run(1, max(1, K // 2))
-    gather_stage = stages["shard_gather_alone"] if sharded else stages["combine_gather"]
+    # ---- parity of the sharded step (N > 1): the same tokens through the
+    # single-GPU layer with the whole table, on this rank's GPU ----
+    parity = None
+    if sharded and full_values is not None:
+        flush.zero_()
+        call.set_io(x["h"], call.y)
+        step()
+        torch.cuda.synchronize()
+        y_sh, slots_sh, w_sh = call.y.clone(), call.slots.clone(), call.weights.clone()
+        if staged:
+            mem_sh = call.mem_in.clone()
+        single = LayerCall(torch, L, W, dict(x, values=full_values), device, args.values_dtype)
+        single(stream)
+        torch.cuda.synchronize()
+        y1 = single.y
+        same_slots = bool(torch.equal(slots_sh, single.slots))
+        same_w = bool(torch.equal(w_sh, single.weights))
+        err = (y_sh.double() - y1.double()).abs()
+        ref_abs = y1.double().abs()
+        max_rel_y = float(err.max() / ref_abs.max().clamp_min(1e-30))
+        floor = 1e-3 * float(ref_abs.max())
+        max_elem_rel_y = float((err / (ref_abs + floor)).max())
+        pvec = torch.tensor([0.0 if same_slots else 1.0, 0.0 if same_w else 1.0, max_rel_y, max_elem_rel_y,
+                             float(not torch.isfinite(y_sh).all())], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(pvec, op=torch.distributed.ReduceOp.MAX)
+        parity = {"tokens": T * world, "checked_against": "memlayer_layer_forward on the whole table, "
+                  "same tokens, same GPU (every rank, max over ranks)",
+                  "slots_equal": pvec[0].item() == 0.0, "weights_equal": pvec[1].item() == 0.0,
+                  "max_rel_y": pvec[2].item(),
+                  "max_elem_rel_y": pvec[3].item(),
+                  "elem_rel_floor": "1e-3 x max|y| added to |y| per element",
+                  "tolerance": 1e-5 if args.values_dtype == "f32" else 2e-2,
+                  "nonfinite": pvec[4].item() != 0.0}
+        parity["ok"] = (parity["slots_equal"] and parity["weights_equal"] and not parity["nonfinite"]
+                        and parity["max_rel_y"] <= parity["tolerance"])
+        del single, full_values
+        torch.cuda.empty_cache()
+
+    gather_stage = (stages["staged_gather_alone"] if staged else stages["shard_gather_alone"] if sharded
+                    else stages["combine_gather"])
     stats = torch.tensor([ms, e2e_ms, gather_stage, stages["score_topk"], e2e_serial_ms], dtype=torch.float64,
                          device=device)
     rank_stages = None
@@ -525,7 +714,7 @@ def run_ours(args, W, rank, world):
         torch.distributed.all_gather(allr, mine)
         rank_stages = [dict(zip(["step"] + names, t.tolist())) for t in allr]
     ms, e2e_ms, gather_ms, score_ms, e2e_serial_ms = stats.tolist()
-    if sharded:                    # every rank's kernels are done before the peers are unmapped
+    if sharded and not staged:     # every rank's kernels are done before the peers are unmapped
         torch.cuda.synchronize()
         torch.distributed.barrier()
         call.comm.close()
@@ -534,20 +723,29 @@ def run_ours(args, W, rank, world):
 
     hbm, src = peaks()
     bf16, _ = tensor_peak()
-    gname = "shard_gather_kernel" if sharded else "combine_gather_kernel"
-    if sharded:
+    gname = "staged_gather_kernel" if staged else "shard_gather_kernel" if sharded else "combine_gather_kernel"
+    if staged:
+        rows_b, alg_b = staged_gather_bytes(W, args.values_dtype, world)
+        nvlink_b = 0
+    elif sharded:
         rows_b, alg_b, nvlink_b = shard_gather_bytes(W, args.values_dtype, world)
     else:
         (rows_b, alg_b), nvlink_b = gather_bytes(W, args.values_dtype), 0
     achieved = alg_b / (gather_ms * 1e-3) / 1e9
     traffic = load_traffic(gname)
+    traffic_src = None
+    if traffic is not None:
+        traffic_src = traffic.get("source", "ncu capture")
+        if sharded and traffic.get("world") not in (None, world):
+            traffic_src = f"{traffic_src} (captured at {traffic.get('world')} ranks, not at {world})"
     score_flops = score_gemm_flops(W)
     score_tf = score_flops / (score_ms * 1e-3) / 1e12
     kernels = {
         gname: {"bound": "hbm", "ms": gather_ms, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "peak_nominal": NOMINAL_HBM_GBS, "frac_nominal": achieved / NOMINAL_HBM_GBS,
                 "algorithmic_bytes_per_launch": alg_b,
-                "traffic": None if traffic is None else traffic.get("bytes_per_launch")},
+                "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
+                "traffic_source": traffic_src},
         "score_topk_tc_kernel": {"bound": "tensor", "ms": score_ms, "achieved": score_tf, "peak": bf16,
                                  "unit": "TFLOP/s", "frac": score_tf / bf16, "algorithmic_flops_per_launch": score_flops,
                                  "issued_tf32_tflops": 3 * score_tf,
@@ -566,21 +764,24 @@ def run_ours(args, W, rank, world):
         "config": {"workload": W["name"], **{k: W[k] for k in W if k != "name"},
                    "values_dtype": args.values_dtype,
                    "l2": "flushed before every step (256 MiB write, outside the step events)",
-                   "parallelism": (f"pool-row-shard{world}" + ("-split" if overlapped else "") if sharded
+                   "parallelism": (f"pool-row-shard{world}" + ("-nccl-staged" if staged else "-p2p")
+                                   + ("-split" if overlapped else "") if sharded
                                    else f"replicas{world}") if world > 1
                    else "single"},
         "roofline": {"kernel": dominant, "peak_source": src,
                      **{k: v for k, v in kernels[dominant].items() if k != "ms"}},
         "roofline_kernels": kernels,
         "gather_gbs": rows_b / (gather_ms * 1e-3) / 1e9,
-        **({"nvlink_partial_gbs_per_gpu": nvlink_b / (gather_ms * 1e-3) / 1e9} if sharded else {}),
+        **({"nvlink_partial_gbs_per_gpu": nvlink_b / (gather_ms * 1e-3) / 1e9} if sharded and not staged else {}),
         "stages_ms": stages,
         **({"stages_ms_per_rank": rank_stages} if rank_stages else {}),
+        **({"parity": parity} if parity is not None else {}),
         "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h_hosts[0].numel() * 4, "d2h_bytes_per_step": y_hosts[0].numel() * 4,
                 "api": e2e_api, "ms_per_step": e2e_ms, "calls_in_flight": inflight,
                 "host_issue_ms_per_call": e2e_host_issue_ms,
-                "note": "calls in flight overlap on the GPU, so e2e can exceed the one-call-at-a-time value",
+                "note": ("copies of one step overlap the neighbouring steps' layer calls" if sharded else
+                         "calls in flight overlap on the GPU, so e2e can exceed the one-call-at-a-time value"),
                 "l2": "not flushed: every step reads the 268 MB value table, larger than L2"},
         "e2e_serial": {"value": T * world / (e2e_serial_ms * 1e-3), "unit": "tokens/s",
                        "ms_per_step": e2e_serial_ms, "calls_in_flight": 1},
@@ -589,7 +790,7 @@ def run_ours(args, W, rank, world):
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        rate, cores, sample = cpu_oracle_rate(W, 2048)
+        rate, cores, sample = cpu_oracle_rate(W, W["tokens_per_gpu"])
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     return line
 

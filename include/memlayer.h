@@ -268,6 +268,14 @@ int32_t memlayer_shard_comm_open_peers(memlayer_shard_comm* comm, const void* ha
  * peer access enabled) as rank `peer` instead of an IPC mapping. */
 int32_t memlayer_shard_comm_set_peer(memlayer_shard_comm* comm, int32_t peer, const memlayer_shard_comm* other);
 
+/* Budget of every wait on another rank in this communicator's calls, in
+ * nanoseconds of the GPU's global timer (default 2 s; 1 us .. 60 s).  A wait
+ * that runs out records its code (31-36) in the workspace status word and
+ * makes the call's later waits give up at once, so a rank that never
+ * arrives leaves its peers with an error status, not a hang.  No counterpart
+ * in the reference. */
+int32_t memlayer_shard_comm_set_wait_budget(memlayer_shard_comm* comm, int64_t nanoseconds);
+
 /* Unmap the peers and free the buffer (after all calls have completed). */
 int32_t memlayer_shard_comm_destroy(memlayer_shard_comm* comm);
 
@@ -287,6 +295,44 @@ int32_t memlayer_pool_forward_sharded(const memlayer_config* cfg, const memlayer
 int32_t memlayer_layer_forward_sharded(const memlayer_config* cfg, const memlayer_layer_args* args,
                                        memlayer_shard_comm* comm, int32_t phases, void* workspace,
                                        size_t workspace_bytes, void* stream);
+
+/* ---- Row-sharded forward with a staged exchange ---------------------------
+ * The same row-sharded layer with the exchange left to the caller's
+ * collective library (NCCL's all-gather and reduce-scatter, for instance),
+ * run on the same stream between the phases; no communicator, no peer
+ * memory.  The data-parallel step it stands beside is the reference's
+ * all-gather of replicated tables (memory_pool_model/train.py:196-197); the
+ * row-sharded table itself has no counterpart in the reference.
+ *   ROUTE   projections and routing of this rank's M tokens: slots and
+ *           weights into args->pool.slots / weights [M, H, k]; the gate
+ *           stays in the workspace;
+ *   (caller: all-gather every rank's slots and weights, rank-major, into
+ *    all_slots / all_weights [world, M, H, k])
+ *   GATHER  for every token of every rank, the sum of w * V[row] over the
+ *           entries this rank owns (slot % world == rank; read slots under
+ *           shuffle_reads) -> partials [world, M, d], zero rows included;
+ *   (caller: reduce-scatter (sum) partials into mem [M, d])
+ *   REDUCE  gate and output projection from mem -> y (and mem into
+ *           args->mem / pool.out when given).
+ * Every rank passes the same cfg (cfg->tokens = M on every rank) and the
+ * same workspace to every phase of one call (memlayer_layer_workspace_size
+ * bytes).  values = this rank's local rows, as for the sharded forward.
+ * Partial rows are bit-identical to the peer-store exchange's; the sum over
+ * owners follows the collective's order. */
+typedef struct {
+  const int32_t* all_slots;      /* [world][M, H, k] every rank's slots, rank-major */
+  const float* all_weights;      /* [world][M, H, k] */
+  int64_t route_stride;          /* elements from one rank's block of all_slots / all_weights to the
+                                    next (0: M*H*k); lets one all-gather move slots and weights
+                                    packed as [world][2][M*H*k] */
+  float* partials;               /* [world, M, d] output of GATHER, 16-byte aligned */
+  const float* mem;              /* [M, d] input of REDUCE: the reduce-scattered partials */
+  int32_t rank, world;
+} memlayer_staged_args;
+
+int32_t memlayer_layer_forward_staged(const memlayer_config* cfg, const memlayer_layer_args* args,
+                                      const memlayer_staged_args* staged, int32_t phases, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 /* ---- Fetched-row gradients and row-wise Adagrad (training) ---------------
  * With sparse_grad the value table gets no dense gradient; the trainer

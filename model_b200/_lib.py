@@ -82,6 +82,18 @@ class MemlayerLayerArgs(C.Structure):
     ]
 
 
+class MemlayerStagedArgs(C.Structure):
+    _fields_ = [
+        ("all_slots", C.c_void_p),
+        ("all_weights", C.c_void_p),
+        ("route_stride", C.c_int64),
+        ("partials", C.c_void_p),
+        ("mem", C.c_void_p),
+        ("rank", C.c_int32),
+        ("world", C.c_int32),
+    ]
+
+
 MAX_READS = 8
 
 
@@ -195,6 +207,12 @@ def lib() -> C.CDLL:
         L.memlayer_shard_comm_open_peers.argtypes = [C.c_void_p, C.c_void_p]
         L.memlayer_shard_comm_set_peer.restype = C.c_int32
         L.memlayer_shard_comm_set_peer.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+        L.memlayer_shard_comm_set_wait_budget.restype = C.c_int32
+        L.memlayer_shard_comm_set_wait_budget.argtypes = [C.c_void_p, C.c_int64]
+        L.memlayer_layer_forward_staged.restype = C.c_int32
+        L.memlayer_layer_forward_staged.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
+                                                    C.POINTER(MemlayerStagedArgs), C.c_int32, C.c_void_p,
+                                                    C.c_size_t, C.c_void_p]
         L.memlayer_shard_comm_destroy.restype = C.c_int32
         L.memlayer_shard_comm_destroy.argtypes = [C.c_void_p]
         L.memlayer_shard_workspace_size.restype = C.c_int32

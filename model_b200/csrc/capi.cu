@@ -310,6 +310,7 @@ ShardK shard_k(const memlayer_shard_comm* comm, const Dims& D) {
   S.d = D.d;
   S.rows = shard_rows(D.N, comm->rank, comm->world);
   S.epoch = comm->epoch;
+  S.wait_ns = comm->wait_ns;
   S.hf = 0;
   S.t0 = 0;
   S.t1 = D.M;
@@ -468,9 +469,11 @@ int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* wor
 // later_chunk: a chunk after the first of memlayer_layer_forward_host, whose
 // sub-key / Dense-kernel preparation and status reset already ran on this
 // workspace; only the hidden state is split again.
+// route_only: projections and routing (slots, weights, the gate in the
+// workspace), no read and no output projection (ROUTE of the staged exchange).
 int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* workspace, size_t workspace_bytes,
                cudaStream_t s, memlayer_shard_comm* comm, int phases, bool later_chunk = false,
-               const Work* given = nullptr) {
+               const Work* given = nullptr, bool route_only = false) {
   Dims D;
   int st = check_config(cfg, &D, true);
   if (st) return st;
@@ -500,13 +503,19 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
       return MEMLAYER_ERR_WORKSPACE;
     layout(D, f, (char*)workspace, &W);
   }
+  memlayer_pool_args ro;
   const memlayer_pool_args* pa = &a->pool;
+  if (route_only) {           // stage 2 writes slots / weights only (no table read)
+    ro = a->pool;
+    ro.values = nullptr;
+    pa = &ro;
+  }
   int* slots = pa->slots ? pa->slots : W.slots;
   float* weights = pa->weights ? pa->weights : W.weights;
-  float* out = a->mem ? a->mem : pa->out;
+  float* out = route_only ? nullptr : a->mem ? a->mem : pa->out;
   float* qn = pa->queries_unit ? pa->queries_unit : W.qn;
   const bool route = !comm || (phases & MEMLAYER_PHASE_ROUTE);
-  const bool reduce = !comm || (phases & MEMLAYER_PHASE_REDUCE);
+  const bool reduce = (!comm || (phases & MEMLAYER_PHASE_REDUCE)) && !route_only;
   const bool split = comm && (phases & MEMLAYER_PHASE_SPLIT) != 0;
   const bool overlap = split && (phases & MEMLAYER_PHASE_ALL) == MEMLAYER_PHASE_ALL;
   SplitEvents ev;
@@ -774,6 +783,15 @@ int32_t memlayer_workspace_status(const memlayer_config* cfg, const void* worksp
 
 // ---- row-sharded pool ----
 
+// A phase mask of a sharded call: at least one phase, no unknown bit (SPLIT
+// only for the forward), and no REDUCE with ROUTE but without GATHER -- the
+// reduce would wait for this rank's own gather, which only a later call runs.
+static bool phase_mask_ok(int phases, bool allow_split) {
+  const int known = MEMLAYER_PHASE_ALL | (allow_split ? MEMLAYER_PHASE_SPLIT : 0);
+  if ((phases & MEMLAYER_PHASE_ALL) == 0 || (phases & ~known)) return false;
+  return !((phases & MEMLAYER_PHASE_ROUTE) && (phases & MEMLAYER_PHASE_REDUCE) && !(phases & MEMLAYER_PHASE_GATHER));
+}
+
 int64_t memlayer_shard_rows(int64_t pool_size, int32_t rank, int32_t world) {
   if (world < 1 || rank < 0 || rank >= world || pool_size < 0) return 0;
   return shard_rows(pool_size, rank, world);
@@ -856,6 +874,13 @@ int32_t memlayer_shard_comm_set_peer(memlayer_shard_comm* comm, int32_t peer, co
       other->cfg.top_k != comm->cfg.top_k || other->cfg.d_value != comm->cfg.d_value)
     return MEMLAYER_ERR_BAD_SHAPE;
   comm->peer[peer] = other->base;
+  return MEMLAYER_OK;
+}
+
+int32_t memlayer_shard_comm_set_wait_budget(memlayer_shard_comm* comm, int64_t nanoseconds) {
+  if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if (nanoseconds < 1000 || nanoseconds > 60000000000LL) return MEMLAYER_ERR_BAD_SHAPE;
+  comm->wait_ns = nanoseconds;
   return MEMLAYER_OK;
 }
 
@@ -970,6 +995,7 @@ RowShardK row_k(const memlayer_shard_comm* comm, const RowGradK& R) {
   K.rows = shard_rows(R.Nslot, comm->rank, comm->world);
   K.d = R.d;
   K.epoch = comm->epoch;
+  K.wait_ns = comm->wait_ns;
   return K;
 }
 
@@ -997,7 +1023,7 @@ int32_t memlayer_row_adagrad_sharded(const memlayer_config* cfg, const memlayer_
   if (st) return st;
   if (!args || !args->values || !args->accum || !aligned16(args->values)) return MEMLAYER_ERR_BAD_POINTER;
   if (cfg->values_dtype != MEMLAYER_F32) return MEMLAYER_ERR_UNSUPPORTED;
-  if (phases < 1 || phases > MEMLAYER_PHASE_ALL) return MEMLAYER_ERR_BAD_SHAPE;
+  if (!phase_mask_ok(phases, false)) return MEMLAYER_ERR_BAD_SHAPE;
   for (int p = 0; p < comm->world; ++p)
     if (!comm->peer[p]) return MEMLAYER_ERR_BAD_POINTER;
   int dev = -1;
@@ -1049,7 +1075,7 @@ int32_t memlayer_pool_forward_sharded(const memlayer_config* cfg, const memlayer
                                       memlayer_shard_comm* comm, int32_t phases, void* workspace,
                                       size_t workspace_bytes, void* stream) {
   if (!comm) return MEMLAYER_ERR_BAD_POINTER;
-  if ((phases & MEMLAYER_PHASE_ALL) == 0 || (phases & ~(MEMLAYER_PHASE_ALL | MEMLAYER_PHASE_SPLIT)))
+  if (!phase_mask_ok(phases, true))
     return MEMLAYER_ERR_BAD_SHAPE;
   return pool_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
 }
@@ -1058,7 +1084,7 @@ int32_t memlayer_layer_forward_sharded(const memlayer_config* cfg, const memlaye
                                        memlayer_shard_comm* comm, int32_t phases, void* workspace,
                                        size_t workspace_bytes, void* stream) {
   if (!comm) return MEMLAYER_ERR_BAD_POINTER;
-  if ((phases & MEMLAYER_PHASE_ALL) == 0 || (phases & ~(MEMLAYER_PHASE_ALL | MEMLAYER_PHASE_SPLIT)))
+  if (!phase_mask_ok(phases, true))
     return MEMLAYER_ERR_BAD_SHAPE;
   return layer_impl(cfg, args, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
 }
@@ -1334,8 +1360,8 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
   const bool reduce = !comm || (phases & MEMLAYER_PHASE_REDUCE);
   if (comm && route) {
     // one backward per forward: the owners' inboxes hold that forward's reads
+    // (claimed by the caller once this call's launches are enqueued)
     if (comm->epoch == 0 || comm->bwd_epoch == comm->epoch) return MEMLAYER_ERR_BAD_SHAPE;
-    comm->bwd_epoch = comm->epoch;
   }
   char* ws = (char*)workspace;
   auto F32p = [&](int64_t off) { return reinterpret_cast<float*>(ws + off); };
@@ -1385,7 +1411,7 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     const char* mine = comm->peer[comm->rank];
     const BwdShard X{reinterpret_cast<const float*>(mine + comm->off.dots),
                      reinterpret_cast<const int*>(mine + comm->off.flags_dots), SK.mcap, comm->world, comm->epoch,
-                     small + 64};
+                     small + 64, comm->wait_ns};
     ML_TRY(launch_route_bwd_sharded(D, B, X, s));
   } else {
     ML_TRY(launch_route_bwd(D, pa->values, B, s));
@@ -1467,8 +1493,71 @@ int32_t memlayer_layer_backward_sharded(const memlayer_config* cfg, const memlay
                                         const memlayer_layer_grads* g, memlayer_shard_comm* comm, int32_t phases,
                                         void* workspace, size_t workspace_bytes, void* stream) {
   if (!comm) return MEMLAYER_ERR_BAD_POINTER;
+  if (!phase_mask_ok(phases, false)) return MEMLAYER_ERR_BAD_SHAPE;
+  const int st = layer_bwd_impl(cfg, a, g, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
+  // the forward's inboxes are spent only once a ROUTE has been enqueued: a
+  // call refused or failed before that can be retried
+  if (st == MEMLAYER_OK && (phases & MEMLAYER_PHASE_ROUTE)) comm->bwd_epoch = comm->epoch;
+  return st;
+}
+
+// ---- staged exchange (the caller runs the collectives between phases) ----
+
+int32_t memlayer_layer_forward_staged(const memlayer_config* cfg, const memlayer_layer_args* a,
+                                      const memlayer_staged_args* x, int32_t phases, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  Dims D;
+  int st = check_config(cfg, &D, true);
+  if (st) return st;
+  if (!a || !x) return MEMLAYER_ERR_BAD_POINTER;
   if ((phases & MEMLAYER_PHASE_ALL) == 0 || (phases & ~MEMLAYER_PHASE_ALL)) return MEMLAYER_ERR_BAD_SHAPE;
-  return layer_bwd_impl(cfg, a, g, workspace, workspace_bytes, (cudaStream_t)stream, comm, phases);
+  if (x->world < 1 || x->world > MEMLAYER_MAX_SHARDS || x->rank < 0 || x->rank >= x->world)
+    return MEMLAYER_ERR_BAD_SHAPE;
+  if (x->route_stride < 0 || (x->route_stride > 0 && x->route_stride < cfg->tokens * cfg->heads * cfg->top_k))
+    return MEMLAYER_ERR_BAD_SHAPE;
+  if (D.d % 4) return MEMLAYER_ERR_UNSUPPORTED;
+  if ((st = check_pool_args(D, &a->pool, true))) return st;
+  if (!aligned16(a->pool.values) || !aligned16(x->partials) || !aligned16(x->mem) || !aligned16(a->mem))
+    return MEMLAYER_ERR_BAD_POINTER;
+  const bool route = phases & MEMLAYER_PHASE_ROUTE, gather = phases & MEMLAYER_PHASE_GATHER,
+             reduce = phases & MEMLAYER_PHASE_REDUCE;
+  if (D.M > 0) {
+    if (route && (!a->pool.slots || !a->pool.weights)) return MEMLAYER_ERR_BAD_POINTER;
+    if (gather && (!x->all_slots || !x->all_weights || !x->partials)) return MEMLAYER_ERR_BAD_POINTER;
+    if (reduce && (!x->mem || !a->w_out || !a->y)) return MEMLAYER_ERR_BAD_POINTER;
+  }
+  Flags f;
+  f.layer = true;
+  f.balance = a->pool.balance_loss != nullptr;
+  const size_t need = layout(D, f, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) % ALIGN))
+    return MEMLAYER_ERR_WORKSPACE;
+  Work W;
+  layout(D, f, (char*)workspace, &W);
+  const cudaStream_t s = (cudaStream_t)stream;
+  resolve_noise(&D, cfg, &a->pool);
+  if (route) {
+    if (D.M == 0) return MEMLAYER_OK;
+    if ((st = layer_impl(cfg, a, workspace, workspace_bytes, s, nullptr, MEMLAYER_PHASE_ALL, false, nullptr, true)))
+      return st;
+  }
+  if (gather)
+    ML_TRY(launch_staged_gather(D, x->all_slots, x->all_weights,
+                                x->route_stride > 0 ? x->route_stride : D.M * D.H * D.k, x->rank, x->world,
+                                shard_rows(D.N, x->rank, x->world), a->pool.values, x->partials, W.err, s));
+  if (reduce && D.M > 0) {
+    if (W.h_hi) {                                                                    // model.py:119
+      ML_TRY(launch_staged_gate(x->mem, W.gate, D.M * D.d, nullptr, W.memg_hi, W.memg_lo, s));
+      ML_TRY(launch_out_tc(D, W, a->b_out, a->y, s));
+    } else {
+      ML_TRY(launch_staged_gate(x->mem, W.gate, D.M * D.d, W.memg, nullptr, nullptr, s));
+      ML_TRY(launch_gemm(W.memg, a->w_out, a->b_out, a->y, D.M, D.dm, D.d, false, s));
+    }
+    float* mem_out = a->mem ? a->mem : a->pool.out;
+    if (mem_out && mem_out != x->mem)
+      ML_TRY(cudaMemcpyAsync(mem_out, x->mem, sizeof(float) * D.M * D.d, cudaMemcpyDeviceToDevice, s));
+  }
+  return MEMLAYER_OK;
 }
 
 // ---- layer forward reusing the previous call's preparation ----

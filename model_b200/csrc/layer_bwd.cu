@@ -110,10 +110,10 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
     const int P = X.world;
     if (threadIdx.x == 0) {
       bool ok = true;
-      for (int o = 0; o < P && ok; ++o) ok = wait_epoch(X.flags + o, X.epoch, X.err, 36);
+      for (int o = 0; o < P && ok; ++o) ok = wait_epoch(X.flags + o, X.epoch, X.err, 36, X.wait_ns);
       ok_s = ok;
     }
-    const int own = lane < k ? (int)(rs_l % P) : -1;
+    const int own = (lane < k && s_ok) ? (int)(rs_l % P) : -1;   // an id outside the table has no owner
     const unsigned lt = (1u << lane) - 1u;
     int pos = 0;
     for (int o = 0; o < P; ++o) {

@@ -34,6 +34,7 @@ struct BwdShard {
   int64_t mcap;
   int world, epoch;
   int* err;            // status word (36: an owner's dots did not arrive in time)
+  long long wait_ns;   // budget of the wait
 };
 
 // C (+)= op(A) op(B) with A(i, k) = A[i sai + k sak], B(k, j) = B[k sbk + j sbj], C[i ldc + j]

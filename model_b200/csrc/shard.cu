@@ -148,7 +148,8 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant
     const char* mine = S.peer[S.rank];
     // lane 0 acquires the source's flag; __syncwarp orders the other lanes' reads after it
     bool ready = true;
-    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + slot, S.epoch, err, 31);
+    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + slot, S.epoch, err, 31,
+                                      S.wait_ns);
     ready = __shfl_sync(FULL, ready, 0);
     __syncwarp();
     if (ready) {
@@ -223,7 +224,7 @@ __global__ void __launch_bounds__(256) shard_reduce_kernel(const __grid_constant
     bool ok = true;
     for (int o = 0; o < P && ok; ++o)
       ok = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_part) + S.hf * MEMLAYER_MAX_SHARDS + o,
-                      S.epoch, err, 32);
+                      S.epoch, err, 32, S.wait_ns);
     ok_s = ok;
   }
   __syncthreads();
@@ -321,7 +322,8 @@ __global__ void __launch_bounds__(256) shard_dots_kernel(const __grid_constant__
     const int src = (S.rank + srot) % P;
     const char* mine = S.peer[S.rank];
     bool ready = true;
-    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_probe) + src, S.epoch, err, 35);
+    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_probe) + src, S.epoch, err, 35,
+                                      S.wait_ns);
     ready = __shfl_sync(FULL, ready, 0);
     __syncwarp();
     if (ready) {
@@ -381,6 +383,97 @@ __global__ void __launch_bounds__(256) shard_dots_kernel(const __grid_constant__
   if (threadIdx.x == 0) publish_backward(S, 5, S.off.flags_dots, -1, 0);
 }
 
+// ---------------------------------------------------------------------------
+// staged exchange: the caller's collectives (NCCL all-gather / reduce-scatter)
+// move the routing entries and the partial rows between the phases
+// ---------------------------------------------------------------------------
+// One warp per token of every rank (`tokens` = world * M): of the token's
+// H*k (slot, weight) entries, those whose read slot this rank owns, summed in
+// (head, rank) order -- the order of the owner's inbox in the peer-store
+// gather, so both exchanges produce the same partial row bit for bit.
+template <typename VT, int VEC, int CH>
+__global__ void __launch_bounds__(256) staged_gather_kernel(Dims D, const int* __restrict__ slots,
+                                                            const float* __restrict__ weights, int64_t stride,
+                                                            int rank, int world, int64_t rows,
+                                                            const VT* __restrict__ values,
+                                                            float* __restrict__ partials, int* __restrict__ err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 8 + warp;   // token t % M of rank t / M
+  if (t >= (int64_t)world * D.M) return;
+  const int hk = D.H * D.k, d = D.d, groups = d / VEC;
+  const int64_t src = t / D.M;
+  slots += src * stride + (t - src * D.M) * hk;
+  weights += src * stride + (t - src * D.M) * hk;
+  float acc[CH][VEC];
+#pragma unroll
+  for (int a = 0; a < CH; ++a)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) acc[a][v] = 0.f;
+  for (int b0 = 0; b0 < hk; b0 += 32) {
+    int64_t rs = 0;
+    float w = 0.f;
+    bool mine = false;
+    if (b0 + lane < hk) {
+      const int sl = __ldcg(slots + b0 + lane);
+      w = __ldcg(weights + b0 + lane);
+      if (sl >= 0 && (int64_t)sl < D.N) {
+        rs = D.shuffle ? ((int64_t)sl + D.N / 2 + 1) % D.N : (int64_t)sl;   // memory.py:179
+        mine = (int)(rs % world) == rank;
+      } else {
+        atomicCAS(err, 0, 22);                   // only a bug upstream can cause this
+      }
+    }
+    const int64_t row_l = rs / world;
+    unsigned mk = __ballot_sync(FULL, mine && row_l < rows);
+    while (mk) {                                 // warp-uniform: entries in lane order
+      const int j = __ffs(mk) - 1;
+      mk &= mk - 1;
+      const int64_t row = __shfl_sync(FULL, row_l, j);
+      const float wr = __shfl_sync(FULL, w, j);
+      const VT* base = values + row * d;
+#pragma unroll
+      for (int a = 0; a < CH; ++a) {
+        const int g = a * 32 + lane;
+        if (g < groups) {
+          float x[VEC];
+          load_group<VT, VEC>(base + g * VEC, x);
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) acc[a][v] = fmaf(wr, x[v], acc[a][v]);
+        }
+      }
+    }
+  }
+  float* dst = partials + t * d;
+#pragma unroll
+  for (int a = 0; a < CH; ++a) {
+    const int g = a * 32 + lane;
+    if (g < groups) {
+#pragma unroll
+      for (int v = 0; v < VEC; v += 4)
+        *reinterpret_cast<float4*>(dst + g * VEC + v) =
+            make_float4(acc[a][v], acc[a][v + 1], acc[a][v + 2], acc[a][v + 3]);
+    }
+  }
+}
+
+// mem * gate (model.py:119) from the reduce-scattered read output, as the
+// float32 product or its tf32 halves for the tensor-core output GEMM.
+__global__ void __launch_bounds__(256) staged_gate_kernel(const float4* __restrict__ mem,
+                                                          const float4* __restrict__ gate, int64_t n4,
+                                                          float4* __restrict__ memg, float4* __restrict__ memg_hi,
+                                                          float4* __restrict__ memg_lo) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldcg(mem + i), g = gate[i];
+    const float4 v = make_float4(a.x * g.x, a.y * g.y, a.z * g.z, a.w * g.w);
+    if (memg) memg[i] = v;
+    if (memg_hi) {
+      const float4 hi = make_float4(tc_round(v.x), tc_round(v.y), tc_round(v.z), tc_round(v.w));
+      memg_hi[i] = hi;
+      memg_lo[i] = make_float4(tc_round(v.x - hi.x), tc_round(v.y - hi.y), tc_round(v.z - hi.z), tc_round(v.w - hi.w));
+    }
+  }
+}
+
 inline int ch_for(int groups) {
   int ch = (groups + 31) / 32;
   return ch <= 1 ? 1 : ch <= 2 ? 2 : ch <= 4 ? 4 : ch <= 8 ? 8 : -1;
@@ -412,6 +505,25 @@ cudaError_t dots_ch(const ShardK& S, const VT* values, int* err, cudaStream_t s)
     case 8: shard_dots_kernel<VT, VEC, 8><<<grid, 256, 0, s>>>(S, values, err); break;
     default: return cudaErrorInvalidValue;
   }
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <typename VT, int VEC>
+cudaError_t staged_ch(const Dims& D, const int* slots, const float* weights, int64_t stride, int rank, int world,
+                      int64_t rows, const VT* values, float* partials, int* err, cudaStream_t s) {
+  const unsigned grid = (unsigned)(((int64_t)world * D.M + 7) / 8);
+#define ML_SG(CHV) \
+  staged_gather_kernel<VT, VEC, CHV><<<grid, 256, 0, s>>>(D, slots, weights, stride, rank, world, rows, values, \
+                                                          partials, err)
+  switch (ch_for(D.d / VEC)) {
+    case 1: ML_SG(1); break;
+    case 2: ML_SG(2); break;
+    case 4: ML_SG(4); break;
+    case 8: ML_SG(8); break;
+    default: return cudaErrorInvalidValue;
+  }
+#undef ML_SG
   count_launch();
   return cudaGetLastError();
 }
@@ -494,6 +606,31 @@ cudaError_t launch_shard_dots(const Dims& D, const ShardK& S, const void* values
   if (D.vdtype == MEMLAYER_F16) return dots_ch<__half, 8>(S, (const __half*)values, err, s);
   if (D.vdtype == MEMLAYER_BF16) return dots_ch<__nv_bfloat16, 8>(S, (const __nv_bfloat16*)values, err, s);
   return dots_ch<float, 4>(S, (const float*)values, err, s);
+}
+
+cudaError_t launch_staged_gather(const Dims& D, const int* slots, const float* weights, int64_t stride, int rank,
+                                 int world, int64_t rows, const void* values, float* partials, int* err,
+                                 cudaStream_t s) {
+  if (D.M <= 0) return cudaSuccess;
+  if (D.vdtype == MEMLAYER_F16)
+    return staged_ch<__half, 8>(D, slots, weights, stride, rank, world, rows, (const __half*)values, partials, err, s);
+  if (D.vdtype == MEMLAYER_BF16)
+    return staged_ch<__nv_bfloat16, 8>(D, slots, weights, stride, rank, world, rows, (const __nv_bfloat16*)values,
+                                       partials, err, s);
+  return staged_ch<float, 4>(D, slots, weights, stride, rank, world, rows, (const float*)values, partials, err, s);
+}
+
+cudaError_t launch_staged_gate(const float* mem, const float* gate, int64_t n, float* memg, float* memg_hi,
+                               float* memg_lo, cudaStream_t s) {
+  const int64_t n4 = n / 4;
+  if (n4 <= 0) return cudaSuccess;
+  const int64_t blocks = (n4 + 255) / 256;
+  const unsigned grid = (unsigned)(blocks < 148 * 8 ? blocks : 148 * 8);
+  staged_gate_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(mem), reinterpret_cast<const float4*>(gate),
+                                          n4, reinterpret_cast<float4*>(memg), reinterpret_cast<float4*>(memg_hi),
+                                          reinterpret_cast<float4*>(memg_lo));
+  count_launch();
+  return cudaGetLastError();
 }
 
 }  // namespace ml

@@ -35,6 +35,7 @@ struct ShardK {
   int d;           // d_value
   int64_t rows;    // value rows held by this rank
   int epoch;       // current call
+  long long wait_ns;  // budget of each wait on another rank (communicator setting)
   // token half of this launch: flags / tickets / meta slots `hf`, this rank's
   // tokens [t0, t1), gather grid over `span` tokens per source rank
   int hf;
@@ -42,7 +43,7 @@ struct ShardK {
 };
 
 // ---- hand-off between ranks through flags in peer memory ----
-constexpr long long kPeerWaitNs = 2000000000LL;   // 2 s
+constexpr long long kPeerWaitNs = 2000000000LL;   // default wait budget: 2 s
 
 __device__ __forceinline__ long long global_ns() {
   long long t;
@@ -62,16 +63,16 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
 
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-// Wait until *flag has reached epoch (wrap-safe).  Gives up after the time
-// limit, or at once when another wait of this call already gave up.
-__device__ inline bool wait_epoch(const int* flag, int epoch, int* err, int code) {
+// Wait until *flag has reached epoch (wrap-safe).  Gives up after `budget_ns`
+// of the global timer, or at once when another wait of this call already gave up.
+__device__ inline bool wait_epoch(const int* flag, int epoch, int* err, int code, long long budget_ns) {
   if (ld_acquire_sys(flag) - epoch >= 0) return true;
   const long long t0 = global_ns();
   while (true) {
     if (*(volatile int*)err != 0) return false;
     __nanosleep(128);
     if (ld_acquire_sys(flag) - epoch >= 0) return true;
-    if (global_ns() - t0 > kPeerWaitNs) {
+    if (global_ns() - t0 > budget_ns) {
       atomicCAS(err, 0, code);
       return false;
     }
@@ -102,6 +103,7 @@ struct RowShardK {
   int64_t rows;     // value rows held by this rank
   int d;
   int epoch;
+  long long wait_ns;  // budget of each wait on another rank
 };
 
 RowShardOff row_shard_layout(int world, int64_t cap, int d);
@@ -138,6 +140,17 @@ cudaError_t launch_shard_gather(const Dims& D, const ShardK& S, const void* valu
 cudaError_t launch_shard_reduce(const Dims& D, const ShardK& S, const int* own_cnt, const float* gate, float* out,
                                 float* memg, float* memg_hi, float* memg_lo, int* err, cudaStream_t s);
 
+// ---- staged exchange: the caller's collectives run between the phases ----
+// For every token of every rank (world * D.M, rank-major; rank o's entries
+// start at o * stride), the sum of w * V[local row] over the entries this
+// rank owns -> partials [world * D.M][d].
+cudaError_t launch_staged_gather(const Dims& D, const int* slots, const float* weights, int64_t stride, int rank,
+                                 int world, int64_t rows, const void* values, float* partials, int* err,
+                                 cudaStream_t s);
+// mem * gate for the output projection (float32 product or tf32 halves).
+cudaError_t launch_staged_gate(const float* mem, const float* gate, int64_t n, float* memg, float* memg_hi,
+                               float* memg_lo, cudaStream_t s);
+
 // ---- backward of the sharded layer (after its forward, on the same communicator) ----
 // Reader side: probe = dmemg * silu(zg) (model.py:118-119) for this rank's
 // M tokens, stored into the caller's probe and this rank's buffer, with
@@ -161,6 +174,7 @@ struct memlayer_shard_comm {
   bool opened[MEMLAYER_MAX_SHARDS] = {};      // mapped through cudaIpcOpenMemHandle
   int epoch = 0;                              // last call started by the route phase
   int bwd_epoch = 0;                          // forward epoch whose backward has started
+  long long wait_ns = ml::kPeerWaitNs;        // budget of each wait on another rank
   // kind 1: row-update communicator (memlayer_shard_comm_create_rowgrad)
   int kind = 0;
   int n_reads = 0;                            // reads (memory layers) per call it was sized for

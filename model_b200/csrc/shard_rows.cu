@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(256) rows_rank_kernel(const __grid_constant__ 
   if (threadIdx.x == 0) {
     bool ok = true;
     for (int src = 0; src < K.world && ok; ++src)
-      ok = wait_epoch(reinterpret_cast<const int*>(mine + K.off.flags_in) + src, K.epoch, err, 33);
+      ok = wait_epoch(reinterpret_cast<const int*>(mine + K.off.flags_in) + src, K.epoch, err, 33, K.wait_ns);
     ok_s = ok;
   }
   __syncthreads();
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(256) rows_apply_kernel(const __grid_constant__
   if (threadIdx.x == 0) {
     bool ok = true;
     for (int o = 0; o < K.world && ok; ++o)
-      ok = wait_epoch(reinterpret_cast<const int*>(mine + K.off.flags_sq) + o, K.epoch, err, 34);
+      ok = wait_epoch(reinterpret_cast<const int*>(mine + K.off.flags_sq) + o, K.epoch, err, 34, K.wait_ns);
     ok_s = ok;
     if (ok) {
       double gn2 = 0.0;

@@ -86,6 +86,12 @@ class ShardComm:
         L.check(L.lib().memlayer_shard_comm_set_peer(self.handle, other.rank, other.handle),
                 "memlayer_shard_comm_set_peer")
 
+    def set_wait_budget(self, seconds: float) -> None:
+        """Budget of each wait on another rank (default 2 s): a wait that
+        runs out leaves status 31-36 in the call's workspace instead of a hang."""
+        L.check(L.lib().memlayer_shard_comm_set_wait_budget(self.handle, int(round(seconds * 1e9))),
+                "memlayer_shard_comm_set_wait_budget")
+
     def close(self) -> None:
         if self.handle:
             L.check(L.lib().memlayer_shard_comm_destroy(self.handle), "memlayer_shard_comm_destroy")
@@ -271,3 +277,83 @@ class ShardedMemoryLayer:
         if check:
             b.check(stream)
         return b.result()
+
+
+class StagedCall:
+    """One row-sharded memory-layer forward whose exchange runs through the
+    caller's collectives (memlayer_layer_forward_staged): ROUTE, an
+    all-gather of every rank's (slot, weight) entries, GATHER of this rank's
+    rows for every rank's tokens, a reduce-scatter of the partial rows, then
+    REDUCE (gate and output projection).  :meth:`run` uses NCCL through
+    ``torch.distributed``; the phases can also be driven one at a time
+    (tests emulate the collectives on one GPU).  Every rank passes the same
+    number of tokens."""
+
+    def __init__(self, layer: MemoryLayer, params: Dict, h: torch.Tensor, rank: int, world: int, *,
+                 train: bool = False, noise_scale: float = 1.0, shuffle_reads: bool = False, rngs=None,
+                 gumbel=None, stats: bool = False):
+        P = layer.pool
+        self.layer, self.rank, self.world, self.stats = layer, rank, world, stats
+        h = _cuda_f32(h, "h")
+        self.lead = tuple(h.shape[:-1])
+        M = int(math.prod(self.lead)) if self.lead else 1
+        device = h.device
+        pool = params["pool"]
+        values = pool["values"]
+        want = shard_rows(P.pool_size, rank, world)
+        if values.shape[0] != want:
+            raise ValueError(f"rank {rank} holds {want} rows, values has {values.shape[0]}")
+        self.cfg = P.config(M, values.dtype, layer.d_model)
+        hk = P.heads * P.top_k
+        # this rank's slots and weight bits land in its block of the packed
+        # [world][2][M*H*k] buffer that one all-gather fills
+        self.route = torch.empty(world, 2, M * hk, dtype=torch.int32, device=device)
+        self.partials = torch.empty(world, M, P.d_value, dtype=torch.float32, device=device)
+        self.mem_in = torch.empty(M, P.d_value, dtype=torch.float32, device=device)
+        r, g_, o = (params[f"{n}_{layer.layer}"] for n in ("router", "mem_gate", "mem_out"))
+        a, self.keep = P._pool_args(pool, M, device, train=train, noise_scale=noise_scale,
+                                    shuffle_reads=shuffle_reads, rngs=rngs, gumbel=gumbel, stats=stats)
+        mine = self.route[rank]
+        a.slots, a.weights = mine[0].data_ptr(), mine[1].data_ptr()
+        self.keep["slots"] = mine[0].view(M, P.heads, P.top_k)
+        self.keep["weights"] = mine[1].view(torch.float32).view(M, P.heads, P.top_k)
+        self.w = {k: _cuda_f32(v, k) for k, v in (("wr", r["kernel"]), ("br", r["bias"]), ("wg", g_["kernel"]),
+                                                  ("bg", g_["bias"]), ("wo", o["kernel"]), ("bo", o["bias"]))}
+        self.h = h
+        self.y = torch.empty(*self.lead, layer.d_model, dtype=torch.float32, device=device)
+        self.mem = torch.empty(*self.lead, P.d_value, dtype=torch.float32, device=device)
+        w = self.w
+        self.args = L.MemlayerLayerArgs(h=h.data_ptr(), w_router=_ptr(w["wr"]), b_router=_ptr(w["br"]),
+                                        w_gate=_ptr(w["wg"]), b_gate=_ptr(w["bg"]), w_out=_ptr(w["wo"]),
+                                        b_out=_ptr(w["bo"]), y=self.y.data_ptr(), mem=self.mem.data_ptr(), pool=a)
+        self.sargs = L.MemlayerStagedArgs(all_slots=self.route.data_ptr(), all_weights=self.route[0, 1].data_ptr(),
+                                          route_stride=2 * M * hk, partials=self.partials.data_ptr(),
+                                          mem=self.mem_in.data_ptr(), rank=rank, world=world)
+        nbytes = C.c_size_t()
+        L.check(L.lib().memlayer_layer_workspace_size(C.byref(self.cfg), C.byref(nbytes)),
+                "memlayer_layer_workspace_size")
+        self.nbytes = nbytes.value
+        self.ws = _workspace(self.nbytes, device)
+
+    def phase(self, ph: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.h.device)).cuda_stream
+        L.check(L.lib().memlayer_layer_forward_staged(C.byref(self.cfg), C.byref(self.args), C.byref(self.sargs),
+                                                      ph, self.ws.data_ptr(), self.nbytes, s),
+                "memlayer_layer_forward_staged")
+
+    def run(self, group=None) -> None:
+        """All phases with NCCL between them, on the current stream."""
+        import torch.distributed as dist
+        self.phase(L.PHASE_ROUTE)
+        dist.all_gather_into_tensor(self.route.view(-1), self.route[self.rank].view(-1), group=group)
+        self.phase(L.PHASE_GATHER)
+        dist.reduce_scatter_tensor(self.mem_in.view(-1), self.partials.view(-1), group=group)
+        self.phase(L.PHASE_REDUCE)
+
+    def check(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.h.device)).cuda_stream
+        _raise_device_status(self.cfg, self.ws, s)
+
+    def result(self):
+        """(y, mem, aux) as MemoryLayer.apply returns them."""
+        return self.y, self.mem, self.layer.pool._aux(self.keep, self.lead, self.stats)

@@ -49,3 +49,25 @@ def run_oracle(recipe: dict, with_stats: bool = True):
         gate = ref.silu(ref.dense(x["h"], x["w_gate"], x["b_gate"]))
         res["y"] = ref.dense((out * gate).astype(np.float32), x["w_out"], x["b_out"])
     return res
+
+
+def oracle_from_slots(recipe: dict, slots: np.ndarray, weights: np.ndarray) -> dict:
+    """The oracle's read output, layer output and routing counts recomputed
+    from a given selection (the GPU's own slots and weights): the check of
+    everything downstream of routing where a near-tie let the GPU pick
+    another slot than the oracle (memory.py:179-192,200-216, model.py:118-119)."""
+    cfg = pool_config(recipe)
+    x = case_inputs(recipe)
+    H, n, k = cfg.heads, cfg.n_sub_keys, cfg.top_k
+    s = np.asarray(slots).reshape(-1, H, k).astype(np.int64)
+    w = np.asarray(weights).reshape(-1, H, k).astype(np.float32)
+    out = ref.gather_mix(x["values"], s, w, recipe.get("shuffle_reads", False))
+    base_a = (np.arange(H) * 2 * n)[None, :, None]          # codebook (h, half 0) starts at 2h * n
+    ids = np.concatenate([(s // n + base_a).reshape(-1), (s % n + base_a + n).reshape(-1)])
+    res = dict(out=out,
+               subkey_counts=np.bincount(ids, minlength=H * 2 * n).astype(np.float32).reshape(H, 2, n),
+               slot_counts=np.bincount(s.reshape(-1), minlength=n * n).astype(np.float32))
+    if recipe.get("layer"):
+        gate = ref.silu(ref.dense(x["h"], x["w_gate"], x["b_gate"]))
+        res["y"] = ref.dense((out * gate).astype(np.float32), x["w_out"], x["b_out"])
+    return res

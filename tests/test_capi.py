@@ -39,6 +39,7 @@ def test_struct_sizes_match_header_layout():
     assert C.sizeof(L.MemlayerRead) == 4 * 8
     assert C.sizeof(L.MemlayerAdagradArgs) == 2 * 8 + 2 * 4 + 3 * 8
     assert C.sizeof(L.MemlayerLayerGrads) == 8 + 4 + 4 + 8 + 10 * 8   # dy, coef, flag, forward ws, 10 outputs
+    assert C.sizeof(L.MemlayerStagedArgs) == 5 * 8 + 2 * 4
 
 
 def cfg(**kw):
@@ -172,3 +173,58 @@ def test_sharded_layer_backward_arguments_rejected_on_the_host():
     for phases in (0, L.PHASE_ALL | L.PHASE_SPLIT, 16):
         assert lib.memlayer_layer_backward_sharded(C.byref(c), C.byref(la), C.byref(g), C.addressof(not_a_comm),
                                                    phases, 1 << 20, nb.value, None) == L.ERR_BAD_SHAPE
+
+
+def test_sharded_phase_masks_that_cannot_complete_are_refused():
+    """REDUCE with ROUTE but without GATHER would wait for this rank's own
+    gather, which no later launch of the call runs: refused on the host,
+    before the communicator is read."""
+    lib = L.lib()
+    c = cfg(tokens=64, d_key=64, d_value=64, d_model=64)
+    not_a_comm = C.addressof(C.create_string_buffer(64))
+    la = L.MemlayerLayerArgs(h=256, w_router=256, w_gate=256, w_out=256, y=256, mem=256,
+                             pool=L.MemlayerPoolArgs(sub_keys=256, log_temperature=256, values=256, slots=256,
+                                                     weights=256))
+    g = L.MemlayerLayerGrads(dy=256, balance_coef=0.0)
+    bad = L.PHASE_ROUTE | L.PHASE_REDUCE
+    assert lib.memlayer_layer_backward_sharded(C.byref(c), C.byref(la), C.byref(g), not_a_comm, bad, 1 << 20,
+                                               1 << 30, None) == L.ERR_BAD_SHAPE
+    assert lib.memlayer_layer_forward_sharded(C.byref(c), C.byref(la), not_a_comm, bad, 1 << 20, 1 << 30,
+                                              None) == L.ERR_BAD_SHAPE
+    assert lib.memlayer_layer_forward_sharded(C.byref(c), C.byref(la), not_a_comm, bad | L.PHASE_SPLIT, 1 << 20,
+                                              1 << 30, None) == L.ERR_BAD_SHAPE
+    pa = la.pool
+    assert lib.memlayer_pool_forward_sharded(C.byref(c), C.byref(pa), not_a_comm, bad, 1 << 20, 1 << 30,
+                                             None) == L.ERR_BAD_SHAPE
+    assert lib.memlayer_shard_comm_set_wait_budget(None, 1000000) == L.ERR_BAD_POINTER
+
+
+def test_staged_exchange_arguments_rejected_on_the_host():
+    lib = L.lib()
+    c = cfg(tokens=64, d_key=64, d_value=64, d_model=64)
+    nb = C.c_size_t()
+    assert lib.memlayer_layer_workspace_size(C.byref(c), C.byref(nb)) == L.OK
+    la = L.MemlayerLayerArgs(h=256, w_router=256, w_gate=256, w_out=256, y=256,
+                             pool=L.MemlayerPoolArgs(sub_keys=256, log_temperature=256, values=256, slots=256,
+                                                     weights=256))
+    ok = dict(all_slots=256, all_weights=256, partials=256, mem=256, rank=0, world=2)
+    f = lib.memlayer_layer_forward_staged
+
+    def call(phases=L.PHASE_ROUTE, ws=1 << 20, nbytes=None, args=la, **kw):
+        x = L.MemlayerStagedArgs(**dict(ok, **kw))
+        return f(C.byref(c), C.byref(args) if args is not None else None, C.byref(x), phases, ws,
+                 nb.value if nbytes is None else nbytes, None)
+
+    assert call(args=None) == L.ERR_BAD_POINTER
+    for phases in (0, 8, L.PHASE_ALL | L.PHASE_SPLIT):
+        assert call(phases=phases) == L.ERR_BAD_SHAPE
+    for rank, world in ((0, 0), (2, 2), (-1, 2), (0, 9)):
+        assert call(rank=rank, world=world) == L.ERR_BAD_SHAPE
+    assert call(route_stride=-1) == L.ERR_BAD_SHAPE
+    assert call(route_stride=64 * 4 * 16 - 1) == L.ERR_BAD_SHAPE        # shorter than one rank's entries
+    assert call(partials=256 + 8) == L.ERR_BAD_POINTER                   # misaligned
+    assert call(phases=L.PHASE_GATHER, all_slots=None) == L.ERR_BAD_POINTER
+    assert call(phases=L.PHASE_REDUCE, mem=None) == L.ERR_BAD_POINTER
+    assert call(ws=None) == L.ERR_WORKSPACE
+    assert call(nbytes=64) == L.ERR_WORKSPACE
+    assert call(ws=(1 << 20) + 16) == L.ERR_WORKSPACE

@@ -179,3 +179,20 @@ def test_rowwise_adagrad_changes_only_fetched_rows():
     changed = np.flatnonzero(np.any(v != before, axis=1))
     assert changed.tolist() == [3, 7] and acc[3] == 1.0
     np.testing.assert_allclose(v[3], before[3] - 0.1 / (1.0 + 1e-8), rtol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["medium", "cfg1_layer_fp16", "tiny_shuffle", "k32_h8"])
+def test_oracle_from_slots_reproduces_the_oracle(name):
+    """The recomputation used by the GPU tests when a near-tie swapped a
+    slot gives the oracle's own outputs and counts from the oracle's own
+    selection."""
+    from cases import oracle_from_slots, run_oracle
+    recipe, _ = load_golden(name)
+    orc = run_oracle(recipe)
+    fx = oracle_from_slots(recipe, orc["slots"], orc["weights"])
+    M = orc["slots"].shape[0]
+    np.testing.assert_array_equal(fx["out"].reshape(M, -1), orc["out"].reshape(M, -1))
+    np.testing.assert_array_equal(fx["subkey_counts"], orc["aux"]["subkey_counts"])
+    np.testing.assert_array_equal(fx["slot_counts"], orc["aux"]["slot_counts"])
+    if "y" in orc:
+        np.testing.assert_array_equal(fx["y"], orc["y"])

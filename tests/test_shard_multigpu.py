@@ -191,3 +191,53 @@ def test_sharded_backward_across_gpus(world, tmp_path):
         errs = np.load(tmp_path / f"bwd{rank}.npy")
         assert errs[0] == 0.0, f"rank {rank}: routing differs"
         assert (errs[1:] <= 1e-5).all(), f"rank {rank}: gradient errors {errs[1:]}"
+
+
+def _staged_worker(rank, world, port, outdir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from model_b200 import MemoryLayer, MemoryPool
+    from model_b200.shard import StagedCall, shard_values
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        pool = MemoryPool(n_sub_keys=128, heads=4, d_key=128, d_value=128, top_k=16)
+        layer = MemoryLayer(pool, d_model=128, layer=1)
+        params = layer.init(0)                                        # same seed: same table on every rank
+        M = 777
+        h = torch.randn(M, 128, device="cuda", generator=torch.Generator("cuda").manual_seed(5 + rank))
+        local = dict(params, pool=dict(params["pool"], values=shard_values(params["pool"]["values"], rank, world)))
+        call = StagedCall(layer, local, h, rank, world)
+        for _ in range(3):                                            # buffers reused across calls
+            call.run()
+        call.check()
+        y, mem, aux = call.result()
+        torch.cuda.synchronize()
+        y0, mem0, aux0 = layer.apply(params, h, check=True)
+        torch.cuda.synchronize()
+        same = bool(torch.equal(aux["slots"], aux0["slots"]) and torch.equal(aux["weights"], aux0["weights"]))
+        e_mem = float((mem - mem0).abs().max() / mem0.abs().max())
+        e_y = float((y - y0).abs().max() / y0.abs().max())
+        np.save(os.path.join(outdir, f"st{rank}.npy"), np.array([float(same), e_mem, e_y]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_staged_nccl_exchange_across_gpus(world, tmp_path):
+    """The NCCL-staged exchange (all-gather of the routing entries,
+    reduce-scatter of the partial rows) against the single-GPU layer."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    mp.spawn(_staged_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for rank in range(world):
+        same, e_mem, e_y = np.load(tmp_path / f"st{rank}.npy")
+        assert same == 1.0, f"rank {rank}: routing differs"
+        assert e_mem <= 1e-5 and e_y <= 1e-5, f"rank {rank}: mem {e_mem:.2e} y {e_y:.2e}"
