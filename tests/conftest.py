@@ -31,3 +31,19 @@ def load_golden(name):
 @pytest.fixture(scope="session")
 def golden():
     return load_golden
+
+
+def pytest_terminal_summary(terminalreporter):
+    """The largest per-element relative error (floor: parity.ELEM_FLOOR x
+    max|ref|) and max-normalised error of each compared quantity."""
+    try:
+        from parity import ELEM_FLOOR, ELEM_REPORT
+    except ImportError:
+        return
+    if not ELEM_REPORT:
+        return
+    terminalreporter.section("parity: largest errors per compared quantity")
+    terminalreporter.write_line(f"{'quantity':32s} {'per-element':>12s} {'max-normalised':>15s}  "
+                                f"(per-element floor {ELEM_FLOOR:g} x max|ref|)")
+    for k, (ee, e) in sorted(ELEM_REPORT.items()):
+        terminalreporter.write_line(f"{k[:32]:32s} {ee:12.3e} {e:15.3e}")
