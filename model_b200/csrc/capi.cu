@@ -258,10 +258,14 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
   if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
   ML_TRY(mark(a, 3, s));
   if (sh) {
-    ML_TRY(launch_shard_push(D, w2, sh->half[0], slots, weights, a->slot_counts, a->subkey_counts, W.own_cnt, s));
-    if (sh->split) {
-      if (sh->after_a) ML_TRY(cudaEventRecord(sh->after_a, s));
-      ML_TRY(launch_shard_push(D, w2, sh->half[1], slots, weights, a->slot_counts, a->subkey_counts, W.own_cnt, s));
+    // stage 2 as on one GPU (routing only), then the entries go to their owners
+    for (int hf = 0; hf < (sh->split ? 2 : 1); ++hf) {
+      const ShardK& K = sh->half[hf];
+      if (K.t1 > K.t0)
+        ML_TRY(launch_combine_gather(D, w2, nullptr, slots, weights, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                     a->slot_counts, a->subkey_counts, s, K.t0, K.t1 - K.t0));
+      ML_TRY(launch_shard_scatter(D, K, slots, weights, W.own_cnt, W.err, s));
+      if (hf == 0 && sh->split && sh->after_a) ML_TRY(cudaEventRecord(sh->after_a, s));
     }
   } else
     ML_TRY(launch_combine_gather(D, w2, a->values, slots, weights, out, memg, memg_hi, memg_lo, gate,

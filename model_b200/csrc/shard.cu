@@ -1,17 +1,18 @@
 // Row-sharded value table over the GPUs of one node (one process per GPU).
 //
 // Slot s lives on rank s % world as local row s / world (striped, so a
-// popular cluster of slots spreads over every rank).  One forward is three
-// kernels per rank, each fused with its transfer over NVLink:
+// popular cluster of slots spreads over every rank).  After stage 2 of the
+// search (the single-GPU routing kernel in routing-only mode), one forward
+// is three kernels per rank, each fused with its transfer over NVLink:
 //
-//   push    stage 2 of the search for this rank's tokens (as the single-GPU
-//           gather kernel), then every (local row, weight) entry is stored
+//   scatter every (local row, weight) entry of this rank's tokens is stored
 //           straight into its owner's inbox (peer memory), grouped per
 //           (source rank, token) in (head, rank) order;
 //   gather  each owner streams its local rows for every source rank's
-//           tokens (16-byte loads, float32 accumulation) and stores one
-//           partial row per (token, owner) straight into the token owner's
-//           buffer -- d floats cross NVLink instead of the H*k/world rows;
+//           tokens (16-byte loads, float32 accumulation; a persistent grid
+//           whose warps take work from whichever source is ready) and stores
+//           one partial row per (token, owner) straight into the token
+//           owner's buffer -- d floats cross NVLink instead of the H*k/world rows;
 //   reduce  the token owner adds the partials in rank order (deterministic)
 //           and applies the SiLU gate for the output projection.
 //
@@ -22,9 +23,11 @@
 // on timeout the kernel records a code in the caller's status word and
 // skips the work.  Buffers are reused across calls without a reset: a rank
 // cannot overwrite a peer's inbox or partials before the peer has consumed
-// them, because each rank's next push follows its own reduce, which waited
+// them, because each rank's next scatter follows its own reduce, which waited
 // for every owner's gather of the previous call.
 #include <stdlib.h>
+
+#include <algorithm>
 
 #include "combine.cuh"
 #include "shard.cuh"
@@ -40,11 +43,15 @@ __device__ __forceinline__ int* flag_ptr(const ShardK& S, int rank, int64_t off,
 // Called by thread 0 of every CTA after the CTA's stores: the last CTA
 // publishes the epoch into flag `flag_off`[S.hf][S.rank] of every rank (and,
 // with `meta`, this half's token range into meta[S.hf][S.rank] first).
-__device__ void publish_when_last(const ShardK& S, int ticket_slot, int64_t flag_off, bool meta) {
+// `reset` (n ints, local) is zeroed by the last CTA for the next call: every
+// CTA has finished with it once the ticket is complete.
+__device__ void publish_when_last(const ShardK& S, int ticket_slot, int64_t flag_off, bool meta,
+                                  int* reset = nullptr, int n_reset = 0) {
   fence_sys();
   int* ticket = reinterpret_cast<int*>(S.peer[S.rank] + S.off.tickets) + ticket_slot;
   if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
   *ticket = 0;   // every CTA has counted: ready for the next call
+  for (int i = 0; i < n_reset; ++i) reset[i] = 0;
   fence_sys();
   const int slot = S.hf * MEMLAYER_MAX_SHARDS + S.rank;
   for (int o = 0; o < S.world; ++o) {
@@ -57,73 +64,55 @@ __device__ void publish_when_last(const ShardK& S, int ticket_slot, int64_t flag
 }
 
 // ---------------------------------------------------------------------------
-// push: TPC tokens per CTA (one warp per (token, head)), grid-stride over the
-// tokens with one completion fence per CTA
+// scatter: after stage 2 has written this rank's slots and weights (the
+// single-GPU routing kernel, routing only), one warp per token stores each
+// (local row, weight) entry into its owner's inbox -- per owner, the
+// token's entries in (head, rank) order -- and the per-owner counts
 // ---------------------------------------------------------------------------
-template <int KM>
-__global__ void __launch_bounds__(1024) shard_push_kernel(
-    Dims D, int tpc, const __grid_constant__ PairTable pairs, const __grid_constant__ ShardK S,
-    const int* __restrict__ sub_idx, const float* __restrict__ sub_score, const float* __restrict__ sub_sel,
-    int* __restrict__ slots, float* __restrict__ weights, float* __restrict__ slot_counts,
-    float* __restrict__ subkey_counts, float* __restrict__ top1_part, int* __restrict__ own_cnt,
-    int* __restrict__ err) {
-  __shared__ uint16_t tab[128];
-  __shared__ uint16_t lbtab[32];
-  __shared__ int cnt_s[32][MEMLAYER_MAX_SHARDS];   // [warp][owner] entries
-  for (int i = threadIdx.x; i < pairs.count; i += blockDim.x) tab[i] = pairs.ij[i];
-  for (int i = threadIdx.x; i < 32; i += blockDim.x) lbtab[i] = pairs.lb[i];
-  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = wid / D.H, h = wid - t * D.H;        // token slot in the CTA, head
-  const int k = D.k, P = S.world;
-  const bool lk = lane < k;
+__global__ void __launch_bounds__(256) shard_scatter_kernel(const __grid_constant__ ShardK S, Dims D,
+                                                            const int* __restrict__ slots,
+                                                            const float* __restrict__ weights,
+                                                            int* __restrict__ own_cnt, int* __restrict__ err) {
+  const int lane = threadIdx.x & 31;
+  const int P = S.world, hk = S.hk;
   const unsigned lt = (1u << lane) - 1u;
-  for (int64_t m0 = S.t0 + (int64_t)blockIdx.x * tpc; m0 < S.t1; m0 += (int64_t)gridDim.x * tpc) {
-    const int64_t m = m0 + t;
-    const bool active = m < S.t1;
-    int own = -1, pos = 0, lrow = 0;
-    float w = 0.f;
-    __syncthreads();                                 // tab staged / previous cnt_s consumed
-    if (active) {
-      const int64_t ra = ((m * D.H + h) * 2) * k;
-      const HeadPick p = combine_head<KM>(D, tab, lbtab, pairs.count, sub_idx, sub_score, sub_sel, ra, lane, err);
-      w = p.w;
-      const int64_t ow = (m * D.H + h) * k;
-      if (lk) {
-        slots[ow + lane] = p.slot;
-        weights[ow + lane] = p.w;
-        if (slot_counts) atomicAdd(&slot_counts[p.slot], 1.f);                   // memory.py:216
-        if (subkey_counts) {                                                    // memory.py:205
-          atomicAdd(&subkey_counts[(int64_t)(h * 2) * D.n + p.ia], 1.f);
-          atomicAdd(&subkey_counts[(int64_t)(h * 2 + 1) * D.n + p.ib], 1.f);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t m = S.t0 + (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); m < S.t1; m += nw) {
+    int run[MEMLAYER_MAX_SHARDS];   // entries of each owner so far (warp-uniform)
+#pragma unroll
+    for (int o = 0; o < MEMLAYER_MAX_SHARDS; ++o) run[o] = 0;
+    for (int b0 = 0; b0 < hk; b0 += 32) {
+      const int e = b0 + lane;
+      int own = -1, lrow = 0, wbits = 0;
+      if (e < hk) {
+        const int sl = __ldcg(slots + m * hk + e);
+        wbits = __float_as_int(__ldcg(weights + m * hk + e));
+        if (sl >= 0 && (int64_t)sl < D.N) {
+          // read (slot + N/2 + 1) % N under shuffle_reads (memory.py:179)
+          const int64_t rs = D.shuffle ? ((int64_t)sl + D.N / 2 + 1) % D.N : (int64_t)sl;
+          own = (int)(rs % P);
+          lrow = (int)(rs / P);
+        } else {
+          atomicCAS(err, 0, 22);                 // only a bug upstream can cause this
         }
       }
-      if (lane == 0 && top1_part) top1_part[m * D.H + h] = p.top1;
-      // read (slot + N/2 + 1) % N under shuffle_reads (memory.py:179)
-      const int64_t rs = D.shuffle ? ((int64_t)p.slot + D.N / 2 + 1) % D.N : (int64_t)p.slot;
-      own = lk ? (int)(rs % P) : -1;
-      lrow = (int)(rs / P);
-      for (int o = 0; o < P; ++o) {
+      int pos = 0;
+#pragma unroll
+      for (int o = 0; o < MEMLAYER_MAX_SHARDS; ++o) {
+        if (o >= P) break;
         const unsigned mk = __ballot_sync(FULL, own == o);
-        if (own == o) pos = __popc(mk & lt);
-        if (lane == 0) cnt_s[wid][o] = __popc(mk);
+        if (own == o) pos = run[o] + __popc(mk & lt);
+        run[o] += __popc(mk);
       }
+      if (own >= 0)
+        reinterpret_cast<int2*>(S.peer[own] + S.off.inbox)[((int64_t)S.rank * S.mcap + m) * hk + pos] =
+            make_int2(lrow, wbits);
     }
-    __syncthreads();
-    if (active) {
-      // entries of (token, owner) in (head, rank) order
-      if (own >= 0) {
-        int base = 0;
-        for (int hh = 0; hh < h; ++hh) base += cnt_s[t * D.H + hh][own];
-        int2* dst = reinterpret_cast<int2*>(S.peer[own] + S.off.inbox) +
-                    ((int64_t)S.rank * S.mcap + m) * S.hk + base + pos;
-        *dst = make_int2(lrow, __float_as_int(w));
-      }
-      if (h == 0 && lane < P) {
-        const int o = lane;
-        int total = 0;
-        for (int hh = 0; hh < D.H; ++hh) total += cnt_s[t * D.H + hh][o];
-        reinterpret_cast<int*>(S.peer[o] + S.off.cnt)[(int64_t)S.rank * S.mcap + m] = total;
-        own_cnt[m * P + o] = total;
+#pragma unroll
+    for (int o = 0; o < MEMLAYER_MAX_SHARDS; ++o) {
+      if (o < P && lane == o) {
+        reinterpret_cast<int*>(S.peer[o] + S.off.cnt)[(int64_t)S.rank * S.mcap + m] = run[o];
+        own_cnt[m * P + o] = run[o];
       }
     }
   }
@@ -132,80 +121,157 @@ __global__ void __launch_bounds__(1024) shard_push_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// gather: one warp per (source rank, token); this rank's own tokens first
+// gather: a persistent grid; warps claim units of GATHER_TPU consecutive
+// tokens of one source rank from per-source counters, taking this rank's
+// own tokens first and then whichever source's inbox is ready, so a late
+// push holds up only the warps that have nothing else left to do
 // ---------------------------------------------------------------------------
+constexpr int GATHER_TPU = 4;
+constexpr int GATHER_CTR = 16;   // int slot of the per-source unit counters in the tickets region
+
+__device__ __forceinline__ int* gather_counters(const ShardK& S) {
+  return reinterpret_cast<int*>(S.peer[S.rank] + S.off.tickets) + GATHER_CTR + S.hf * MEMLAYER_MAX_SHARDS;
+}
+
 template <typename VT, int VEC, int CH>
 __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant__ ShardK S,
                                                            const VT* __restrict__ values, int* __restrict__ err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * 8 + warp;
-  const int P = S.world, d = S.d;
-  if (gw < (int64_t)P * S.span) {
-    const int srot = (int)(gw / S.span);
-    const int64_t li = gw - (int64_t)srot * S.span;
-    const int src = (S.rank + srot) % P;
-    const int slot = S.hf * MEMLAYER_MAX_SHARDS + src;
-    const char* mine = S.peer[S.rank];
-    // lane 0 acquires the source's flag; __syncwarp orders the other lanes' reads after it
-    bool ready = true;
-    if (lane == 0) ready = wait_epoch(reinterpret_cast<const int*>(mine + S.off.flags_in) + slot, S.epoch, err, 31,
-                                      S.wait_ns);
-    ready = __shfl_sync(FULL, ready, 0);
-    __syncwarp();
-    if (ready) {
-      const volatile int* meta = reinterpret_cast<const volatile int*>(mine + S.off.meta) + slot * 2;
-      const int64_t m = meta[0] + li;            // the source's token
-      const int64_t grp = (int64_t)src * S.mcap + m;
-      const int c = m < meta[1] ? reinterpret_cast<const volatile int*>(mine + S.off.cnt)[grp] : 0;
-      if (c > 0) {
-        const int2* ent = reinterpret_cast<const int2*>(mine + S.off.inbox) + grp * S.hk;
-        float acc[CH][VEC];
-#pragma unroll
-        for (int a = 0; a < CH; ++a)
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) acc[a][v] = 0.f;
-        const int groups = d / VEC;
-        for (int b0 = 0; b0 < c; b0 += 32) {
-          const int2 e = (b0 + lane < c) ? __ldcg(ent + b0 + lane) : make_int2(0, 0);
-          const int nb = min(32, c - b0);
-#pragma unroll 4
-          for (int j = 0; j < nb; ++j) {
-            const int row = __shfl_sync(FULL, e.x, j);
-            const float wr = __int_as_float(__shfl_sync(FULL, e.y, j));
-            if ((unsigned)row >= (unsigned)S.rows) {   // only a bug upstream can cause this
-              if (lane == 0) atomicCAS(err, 0, 22);
-              continue;
+  const int P = S.world, d = S.d, groups = d / VEC;
+  const char* mine = S.peer[S.rank];
+  const int* flags = reinterpret_cast<const int*>(mine + S.off.flags_in) + S.hf * MEMLAYER_MAX_SHARDS;
+  int* ctr = gather_counters(S);
+  // Sources seen ready by this CTA, and the warp that polls the flags: one
+  // poller per CTA at a time, the other idle warps back off, so that waiting
+  // warps do not flood L2 (where the peers' pushes land) with flag loads.
+  __shared__ unsigned ready_s;
+  __shared__ int poller_s;
+  if (threadIdx.x == 0) {
+    ready_s = 0u;
+    poller_s = -1;
+  }
+  __syncthreads();
+  const unsigned all = P >= 32 ? FULL : (1u << P) - 1u;
+  unsigned done = 0, ready = 0;   // per source (bit srot), warp-uniform; `ready`: acquired by this warp
+  long long t_idle = -1;          // lane 0: start of the current wait for any ready source
+  unsigned backoff = 64;
+  while (done != all) {
+    int pick = -1, u0 = 0, lo = 0, hi = 0;
+    if (lane == 0) {
+      for (int srot = 0; srot < P && pick < 0; ++srot) {
+        if ((done >> srot) & 1u) continue;
+        const int src = (S.rank + srot) % P;
+        const int slot = S.hf * MEMLAYER_MAX_SHARDS + src;
+        if (!((ready >> srot) & 1u)) {
+          if (!((*(volatile unsigned*)&ready_s >> srot) & 1u)) continue;
+          if (ld_acquire_sys(flags + src) - S.epoch < 0) continue;   // this warp's own acquire
+          ready |= 1u << srot;
+        }
+        const volatile int* meta = reinterpret_cast<const volatile int*>(mine + S.off.meta) + slot * 2;
+        const int mlo = meta[0], mhi = meta[1];
+        const int c = atomicAdd(ctr + src, GATHER_TPU);
+        if (c >= mhi - mlo) {
+          done |= 1u << srot;
+          continue;
+        }
+        pick = srot;
+        u0 = c;
+        lo = mlo;
+        hi = mhi;
+      }
+      if (pick >= 0) {
+        t_idle = -1;
+        backoff = 64;
+      } else if (done != all) {           // no claimable source seen ready: poll or back off
+        bool found = false;
+        if (atomicCAS(&poller_s, -1, warp) == -1) {
+          const unsigned rs = *(volatile unsigned*)&ready_s;
+          for (int srot = 0; srot < P; ++srot) {
+            if (((done | rs) >> srot) & 1u) continue;
+            if (ld_acquire_sys(flags + (S.rank + srot) % P) - S.epoch >= 0) {
+              atomicOr(&ready_s, 1u << srot);
+              found = true;
             }
-            const VT* base = values + (int64_t)row * d;
+          }
+          atomicExch(&poller_s, -1);
+        }
+        if (!found) {
+          if (*(volatile int*)err != 0) {
+            pick = -2;
+          } else if (t_idle < 0) {
+            t_idle = global_ns();
+          } else if (global_ns() - t_idle > S.wait_ns) {   // bounded wait on the other ranks' pushes
+            atomicCAS(err, 0, 31);
+            pick = -2;
+          } else {
+            __nanosleep(backoff);
+            backoff = backoff < 2048 ? backoff * 2 : 2048;
+          }
+        }
+      }
+    }
+    pick = __shfl_sync(FULL, pick, 0);
+    done = __shfl_sync(FULL, done, 0);
+    ready = __shfl_sync(FULL, ready, 0);
+    if (pick == -2) break;
+    if (pick < 0) continue;
+    u0 = __shfl_sync(FULL, u0, 0);
+    lo = __shfl_sync(FULL, lo, 0);
+    hi = __shfl_sync(FULL, hi, 0);
+    __syncwarp();   // lane 0's acquire of the flag orders the warp's reads of the inbox
+    const int src = (S.rank + pick) % P;
+    const int tend = min(u0 + GATHER_TPU, hi - lo);
+    for (int t = u0; t < tend; ++t) {
+      const int64_t m = lo + t;                  // the source's token
+      const int64_t grp = (int64_t)src * S.mcap + m;
+      const int c = __ldcg(reinterpret_cast<const int*>(mine + S.off.cnt) + grp);
+      if (c <= 0) continue;
+      const int2* ent = reinterpret_cast<const int2*>(mine + S.off.inbox) + grp * S.hk;
+      float acc[CH][VEC];
 #pragma unroll
-            for (int a = 0; a < CH; ++a) {
-              const int g = a * 32 + lane;
-              if (g < groups) {
-                float x[VEC];
-                load_group<VT, VEC>(base + g * VEC, x);
+      for (int a = 0; a < CH; ++a)
 #pragma unroll
-                for (int v = 0; v < VEC; ++v) acc[a][v] = fmaf(wr, x[v], acc[a][v]);
-              }
+        for (int v = 0; v < VEC; ++v) acc[a][v] = 0.f;
+      for (int b0 = 0; b0 < c; b0 += 32) {
+        const int2 e = (b0 + lane < c) ? __ldcg(ent + b0 + lane) : make_int2(0, 0);
+        const int nb = min(32, c - b0);
+#pragma unroll 4
+        for (int j = 0; j < nb; ++j) {
+          const int row = __shfl_sync(FULL, e.x, j);
+          const float wr = __int_as_float(__shfl_sync(FULL, e.y, j));
+          if ((unsigned)row >= (unsigned)S.rows) {   // only a bug upstream can cause this
+            if (lane == 0) atomicCAS(err, 0, 22);
+            continue;
+          }
+          const VT* base = values + (int64_t)row * d;
+#pragma unroll
+          for (int a = 0; a < CH; ++a) {
+            const int g = a * 32 + lane;
+            if (g < groups) {
+              float x[VEC];
+              load_group<VT, VEC>(base + g * VEC, x);
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) acc[a][v] = fmaf(wr, x[v], acc[a][v]);
             }
           }
         }
-        // the partial goes straight to the token owner's buffer
-        float* dst = reinterpret_cast<float*>(S.peer[src] + S.off.part) + ((int64_t)S.rank * S.mcap + m) * d;
+      }
+      // the partial goes straight to the token owner's buffer
+      float* dst = reinterpret_cast<float*>(S.peer[src] + S.off.part) + ((int64_t)S.rank * S.mcap + m) * d;
 #pragma unroll
-        for (int a = 0; a < CH; ++a) {
-          const int g = a * 32 + lane;
-          if (g < groups) {
+      for (int a = 0; a < CH; ++a) {
+        const int g = a * 32 + lane;
+        if (g < groups) {
 #pragma unroll
-            for (int v = 0; v < VEC; v += 4)
-              *reinterpret_cast<float4*>(dst + g * VEC + v) =
-                  make_float4(acc[a][v], acc[a][v + 1], acc[a][v + 2], acc[a][v + 3]);
-          }
+          for (int v = 0; v < VEC; v += 4)
+            *reinterpret_cast<float4*>(dst + g * VEC + v) =
+                make_float4(acc[a][v], acc[a][v + 1], acc[a][v + 2], acc[a][v + 3]);
         }
       }
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) publish_when_last(S, S.hf * 2 + 1, S.off.flags_part, false);
+  if (threadIdx.x == 0) publish_when_last(S, S.hf * 2 + 1, S.off.flags_part, false, ctr, P);
 }
 
 // ---------------------------------------------------------------------------
@@ -479,19 +545,37 @@ inline int ch_for(int groups) {
   return ch <= 1 ? 1 : ch <= 2 ? 2 : ch <= 4 ? 4 : ch <= 8 ? 8 : -1;
 }
 
-template <typename VT, int VEC>
-cudaError_t gather_ch(const ShardK& S, const VT* values, int* err, cudaStream_t s) {
-  const int64_t warps = (int64_t)S.world * S.span;
-  const unsigned grid = (unsigned)((warps + 7) / 8);
-  switch (ch_for(S.d / VEC)) {
-    case 1: shard_gather_kernel<VT, VEC, 1><<<grid, 256, 0, s>>>(S, values, err); break;
-    case 2: shard_gather_kernel<VT, VEC, 2><<<grid, 256, 0, s>>>(S, values, err); break;
-    case 4: shard_gather_kernel<VT, VEC, 4><<<grid, 256, 0, s>>>(S, values, err); break;
-    case 8: shard_gather_kernel<VT, VEC, 8><<<grid, 256, 0, s>>>(S, values, err); break;
-    default: return cudaErrorInvalidValue;
+// Persistent grid of the gather: the CTAs that fit on the device at once
+// (every CTA pays one system-scope fence), no more than there are units.
+template <typename VT, int VEC, int CHV>
+cudaError_t gather_launch(const ShardK& S, const VT* values, int* err, cudaStream_t s) {
+  static int per_sm = 0;   // resident CTAs per SM of this instantiation (same on every B200)
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, shard_gather_kernel<VT, VEC, CHV>, 256, 0) != cudaSuccess)
+      return cudaErrorInvalidValue;
+    per_sm = n > 0 ? n : 1;
   }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t units = (int64_t)S.world * ((S.span + GATHER_TPU - 1) / GATHER_TPU);
+  const int64_t ctas = (units + 7) / 8;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ctas, (int64_t)sms * per_sm));
+  shard_gather_kernel<VT, VEC, CHV><<<grid, 256, 0, s>>>(S, values, err);
   count_launch();
   return cudaGetLastError();
+}
+
+template <typename VT, int VEC>
+cudaError_t gather_ch(const ShardK& S, const VT* values, int* err, cudaStream_t s) {
+  switch (ch_for(S.d / VEC)) {
+    case 1: return gather_launch<VT, VEC, 1>(S, values, err, s);
+    case 2: return gather_launch<VT, VEC, 2>(S, values, err, s);
+    case 4: return gather_launch<VT, VEC, 4>(S, values, err, s);
+    case 8: return gather_launch<VT, VEC, 8>(S, values, err, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 template <typename VT, int VEC>
@@ -549,27 +633,16 @@ ShardOff shard_layout(int world, int64_t mcap, int hk, int d) {
   return o;
 }
 
-cudaError_t launch_shard_push(const Dims& D, const Work& W, const ShardK& S, int* slots, float* weights,
-                              float* slot_counts, float* subkey_counts, int* own_cnt, cudaStream_t s) {
-  const PairTable pairs = make_pairs(D.k);
-  // TPC tokens per CTA of up to 512 threads; at most one wave of CTAs (each
-  // pays one system-scope fence), at least one CTA to publish an empty call
-  const int tpc = D.H >= 16 ? 1 : 16 / D.H;
-  const dim3 block(32 * D.H * tpc);
-  const int per_sm = 2048 / (int)block.x;
-  const int64_t groups = (S.t1 - S.t0 + tpc - 1) / tpc;
-  const unsigned grid = (unsigned)(groups < 1 ? 1 : groups < 148LL * per_sm ? groups : 148LL * per_sm);
-#define ML_SP(KV)                                                                                               \
-  shard_push_kernel<KV><<<grid, block, 0, s>>>(D, tpc, pairs, S, W.sub_idx, W.sub_score, W.sub_sel, slots, weights, \
-                                               slot_counts, subkey_counts, W.top1_part, own_cnt, W.err)
-  switch (D.kmax) {
-    case 4: ML_SP(4); break;
-    case 8: ML_SP(8); break;
-    case 16: ML_SP(16); break;
-    case 32: ML_SP(32); break;
-    default: return cudaErrorInvalidValue;
-  }
-#undef ML_SP
+cudaError_t launch_shard_scatter(const Dims& D, const ShardK& S, const int* slots, const float* weights,
+                                 int* own_cnt, int* err, cudaStream_t s) {
+  // a persistent grid (every CTA pays one system-scope fence), at least one
+  // CTA to publish an empty call
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ctas = (S.t1 - S.t0 + 7) / 8;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ctas, (int64_t)sms * 8));
+  shard_scatter_kernel<<<grid, 256, 0, s>>>(S, D, slots, weights, own_cnt, err);
   count_launch();
   return cudaGetLastError();
 }

@@ -13,7 +13,8 @@ struct ShardOff {
   int64_t flags_part;  // [2][MAX] int: epoch of the partials each owner rank has stored
   int64_t meta;        // [2][MAX][2] int: token range [lo, hi) of each source rank's half
   int64_t tickets;     // [2][2] int: CTA completion counters of push / gather (local use);
-                       // [4], [5]: probe / dots kernels of the backward
+                       // [4], [5]: probe / dots kernels of the backward;
+                       // [16 + 8 * half + source]: the gather's unit counters (local use)
   int64_t flags_probe; // [MAX] int (backward): epoch of the probe rows each source rank has stored
   int64_t flags_dots;  // [MAX] int (backward): epoch of the dots each owner rank has stored
   int64_t bmeta;       // [MAX] int (backward): token count of each source rank's call
@@ -65,12 +66,17 @@ __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" 
 
 // Wait until *flag has reached epoch (wrap-safe).  Gives up after `budget_ns`
 // of the global timer, or at once when another wait of this call already gave up.
+// The polls back off (64 ns doubling to 2 us): many waiting CTAs would
+// otherwise flood the L2 slice that holds the flag, which is also where the
+// peers' stores for this call land.
 __device__ inline bool wait_epoch(const int* flag, int epoch, int* err, int code, long long budget_ns) {
   if (ld_acquire_sys(flag) - epoch >= 0) return true;
   const long long t0 = global_ns();
+  unsigned backoff = 64;
   while (true) {
     if (*(volatile int*)err != 0) return false;
-    __nanosleep(128);
+    __nanosleep(backoff);
+    backoff = backoff < 2048 ? backoff * 2 : 2048;
     if (ld_acquire_sys(flag) - epoch >= 0) return true;
     if (global_ns() - t0 > budget_ns) {
       atomicCAS(err, 0, code);
@@ -128,10 +134,10 @@ cudaError_t launch_rows_apply(const RowShardK& K, const RowMerge& G, float* valu
                               float clip, const float* rest_sq, float* scale_out, int* n_unique_out, int* err,
                               cudaStream_t s);
 
-// Stage 2 + push of (local row, weight) entries to the owner ranks
-// (replaces launch_combine_gather in the sharded forward).
-cudaError_t launch_shard_push(const Dims& D, const Work& W, const ShardK& S, int* slots, float* weights,
-                              float* slot_counts, float* subkey_counts, int* own_cnt, cudaStream_t s);
+// After stage 2 (routing only) of tokens [S.t0, S.t1): store every (local
+// row, weight) entry into its owner rank's inbox and publish the inbox.
+cudaError_t launch_shard_scatter(const Dims& D, const ShardK& S, const int* slots, const float* weights,
+                                 int* own_cnt, int* err, cudaStream_t s);
 // Owner side: gather local rows for every source rank's tokens and store the
 // partial sums into the token owners' buffers.
 cudaError_t launch_shard_gather(const Dims& D, const ShardK& S, const void* values_local, int* err,
