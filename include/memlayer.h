@@ -527,8 +527,11 @@ int32_t memlayer_row_adagrad_sharded(const memlayer_config* cfg, const memlayer_
                                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* Size of the library's built-in scratch array used by
- * memlayer_pool_forward_noalloc (64 MiB, held on every GPU that loads the
- * library until the process exits). */
+ * memlayer_pool_forward_noalloc (64 MiB).  A device holds it from the moment
+ * the library's code is loaded there -- with CUDA's default lazy module
+ * loading, at the first memlayer_pool_forward_noalloc call on that device;
+ * with eager loading (CUDA_MODULE_LOADING=EAGER), when the library is
+ * loaded -- until the process exits. */
 #define MEMLAYER_NOALLOC_SCRATCH_BYTES (64u << 20)
 
 /* MemoryPool.__call__ for callers that cannot allocate or pass a device

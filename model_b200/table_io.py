@@ -19,7 +19,7 @@ buffer (one copy per chunk on the caller's stream).
 from __future__ import annotations
 
 import os
-from typing import Dict, Optional, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 import torch
@@ -40,6 +40,16 @@ def _barrier(group):
     import torch.distributed as dist
     if dist.is_available() and dist.is_initialized():
         dist.barrier(group)
+
+
+def _gather_problems(problem: Optional[str], group) -> List[str]:
+    """Every rank's argument problem (None when fine), on every rank."""
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()):
+        return [problem] if problem else []
+    out: List[Optional[str]] = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, problem, group=group)
+    return [f"rank {r}: {p}" for r, p in enumerate(out) if p]
 
 
 def _local_rows(n_slots: int, rank: int, world: int) -> int:
@@ -93,14 +103,22 @@ def save_table(dest: str, arrays: Dict[str, torch.Tensor], n_slots: int, rank: i
     ``<key>.tmp.npy``, every rank writes its rows, rank 0 renames the file
     over ``<key>.npy`` once all ranks have flushed.
     """
+    problem = None
     for key, t in arrays.items():
         if key not in KEYS:
-            raise ValueError(f"unknown table array {key!r}; expected one of {KEYS}")
-        want = _local_rows(n_slots, rank, world)
-        if t.shape[0] != want:
-            raise ValueError(f"{key}: {t.shape[0]} local rows, expected {want} for rank {rank} of {world}")
-        if (key == "acc") != (t.dim() == 1):
-            raise ValueError(f"{key}: acc is [rows], the others [rows, dim]")
+            problem = f"unknown table array {key!r}; expected one of {KEYS}"
+        elif t.shape[0] != _local_rows(n_slots, rank, world):
+            problem = (f"{key}: {t.shape[0]} local rows, expected {_local_rows(n_slots, rank, world)} "
+                       f"for rank {rank} of {world}")
+        elif (key == "acc") != (t.dim() == 1):
+            problem = f"{key}: acc is [rows], the others [rows, dim]"
+        if problem:
+            break
+    # every rank learns of any rank's bad arguments before the first barrier,
+    # so all raise together instead of the others waiting in a collective
+    problems = _gather_problems(problem, group)
+    if problems:
+        raise ValueError("; ".join(problems))
     if rank == 0:
         os.makedirs(dest, exist_ok=True)
     _barrier(group)

@@ -103,3 +103,37 @@ def test_gloo_four_ranks_save_then_reshard(tmp_path):
             got = load_table(str(tmp_path), ["values", "acc"], rank=r, world=world)
             np.testing.assert_array_equal(got["values"].numpy(), full["values"][r::world])
             np.testing.assert_array_equal(got["acc"].numpy(), full["acc"][r::world])
+
+
+def _bad_rank_worker(rank, world, port, dest, outdir):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        full = _table(101, 4, seed=2)
+        local = {"values": torch.from_numpy(np.ascontiguousarray(full["values"][rank::world]))}
+        if rank == 1:
+            local["values"] = local["values"][:-1]                       # one row short
+        msg = ""
+        try:
+            save_table(dest, local, 101, rank=rank, world=world)
+        except ValueError as e:
+            msg = str(e)
+        with open(os.path.join(outdir, f"bad{rank}.txt"), "w") as f:
+            f.write(msg)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_bad_rows_on_one_rank_fail_every_rank(tmp_path):
+    """A rank with wrong arguments makes every rank raise before the first
+    barrier, instead of leaving the others blocked in a collective."""
+    import torch.multiprocessing as mp
+    dest = tmp_path / "snap"
+    mp.spawn(_bad_rank_worker, args=(3, _free_port(), str(dest), str(tmp_path)), nprocs=3, join=True)
+    for r in range(3):
+        msg = (tmp_path / f"bad{r}.txt").read_text()
+        assert "rank 1:" in msg and "local rows" in msg, (r, msg)
+    assert not (dest / "values.npy").exists()
