@@ -61,6 +61,9 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
     if jobs or not os.path.exists(LIB):
         run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-lcublas", "-Xlinker",
              "-rpath=/usr/local/cuda/lib64", "-lrt", "-ldl", "-lpthread"])
+    # the XLA FFI handlers of the JAX binding, where JAX is installed
+    from model_b200 import jax_ffi
+    jax_ffi.build(verbose=verbose)
     return LIB
 
 
