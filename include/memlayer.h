@@ -526,6 +526,76 @@ int32_t memlayer_row_adagrad_sharded(const memlayer_config* cfg, const memlayer_
                                      const memlayer_adagrad_args* args, memlayer_shard_comm* comm, int32_t phases,
                                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- The language model around the memory layer -------------------------
+ * MemoryPoolLM (memory_pool_model/model.py:15-127) in inference form and its
+ * decode step with a key / value cache (generate.py:23-65): token and
+ * position embeddings; per layer LayerNorm -> causal multi-head attention ->
+ * residual, LayerNorm -> feed-forward (Dense, GELU, Dense) or, in the memory
+ * layers, the memory-layer block (memlayer_layer_forward on the shared pool;
+ * both when memory_ffn) -> residual; final LayerNorm and tied logits.
+ * Dropout is the identity (inference).  LayerNorm is flax's (epsilon 1e-6,
+ * variance E[x^2] - E[x]^2), GELU its tanh form, attention scales the query
+ * by 1/sqrt(head_dim).  head_dim = d_model / n_heads must be 32 or 64;
+ * d_model <= 1024.  The status of a model call (token ids out of range: 26,
+ * and the memory layers' codes) is read with memlayer_workspace_status(&cfg->pool,
+ * workspace, ...). */
+#define MEMLAYER_MAX_LAYERS 32
+
+typedef struct {
+  int32_t vocab_size, max_len, d_model, n_layers, n_heads, ffn_mult;
+  uint32_t memory_layers;        /* bit i set: layer i reads the pool (config.py:31) */
+  int32_t memory_ffn;            /* memory layers keep their feed-forward (config.py:36) */
+  memlayer_config pool;          /* the shared pool's fields; tokens is ignored, d_model must match */
+} memlayer_model_config;
+
+/* One layer's parameters, float32, row-major; Dense kernels as [in, out].
+ * The flax attention parameters map as: w_qkv = [query | key | value]
+ * kernels [d_model, H, head_dim] reshaped to [d_model, d_model] and
+ * concatenated along the columns (b_qkv likewise); w_attn_out = the out
+ * kernel [H, head_dim, d_model] reshaped to [d_model, d_model]. */
+typedef struct {
+  const float *ln_attn_scale, *ln_attn_bias;    /* [d_model] ln_attn_i */
+  const float *w_qkv, *b_qkv;                   /* [d_model, 3*d_model], [3*d_model] attn_i */
+  const float *w_attn_out, *b_attn_out;         /* [d_model, d_model], [d_model] */
+  const float *ln_ffn_scale, *ln_ffn_bias;      /* [d_model] ln_ffn_i */
+  const float *w_ffn_in, *b_ffn_in;             /* [d_model, F], [F]; F = d_model*ffn_mult (when used) */
+  const float *w_ffn_out, *b_ffn_out;           /* [F, d_model], [d_model] */
+  const float *w_router, *b_router;             /* memory layers: router_i, mem_gate_i, mem_out_i */
+  const float *w_gate, *b_gate;
+  const float *w_out, *b_out;
+} memlayer_block_params;
+
+typedef struct {
+  const float* embedding;        /* [vocab_size, d_model] embed (also the tied output projection) */
+  const float* pos_embed;        /* [max_len, d_model] */
+  const memlayer_block_params* layers;   /* host array of n_layers entries */
+  const float *ln_final_scale, *ln_final_bias;
+  const float* sub_keys;         /* the shared pool: [H, 2, n, d_key/2] */
+  const float* log_temperature;  /* [1] */
+  const void* values;            /* [n*n, d] of pool.values_dtype */
+} memlayer_model_params;
+
+/* Workspace of memlayer_model_forward / memlayer_model_decode_step for
+ * `tokens` rows (batch * seq for a forward, batch for a decode step). */
+int32_t memlayer_model_workspace_size(const memlayer_model_config* cfg, int64_t tokens, size_t* bytes);
+
+/* logits [batch, seq, vocab] of tokens [batch, seq] (int32, device), seq <= max_len. */
+int32_t memlayer_model_forward(const memlayer_model_config* cfg, const memlayer_model_params* params,
+                               const int32_t* tokens, int64_t batch, int64_t seq, float* logits, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Bytes of the key / value cache of `batch` rows: [n_layers][2][batch][max_len][d_model] float32. */
+int32_t memlayer_model_cache_size(const memlayer_model_config* cfg, int64_t batch, size_t* bytes);
+
+/* One decode step: tokens [batch] (device) at position *pos (device int32,
+ * read on the GPU, so a captured CUDA graph can be replayed for every
+ * position) -> logits [batch, vocab]; the step's keys and values are written
+ * into `cache` at *pos, and the step attends to cache positions 0..*pos.  A
+ * fresh cache need not be cleared: positions beyond *pos are never read. */
+int32_t memlayer_model_decode_step(const memlayer_model_config* cfg, const memlayer_model_params* params,
+                                   const int32_t* tokens, int64_t batch, const int32_t* pos, void* cache,
+                                   float* logits, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Size of the library's built-in scratch array used by
  * memlayer_pool_forward_noalloc (64 MiB).  A device holds it from the moment
  * the library's code is loaded there -- with CUDA's default lazy module

@@ -94,6 +94,43 @@ class MemlayerStagedArgs(C.Structure):
     ]
 
 
+MAX_LAYERS = 32
+
+
+class MemlayerModelConfig(C.Structure):
+    _fields_ = [
+        ("vocab_size", C.c_int32),
+        ("max_len", C.c_int32),
+        ("d_model", C.c_int32),
+        ("n_layers", C.c_int32),
+        ("n_heads", C.c_int32),
+        ("ffn_mult", C.c_int32),
+        ("memory_layers", C.c_uint32),
+        ("memory_ffn", C.c_int32),
+        ("pool", MemlayerConfig),
+    ]
+
+
+class MemlayerBlockParams(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "ln_attn_scale", "ln_attn_bias", "w_qkv", "b_qkv", "w_attn_out", "b_attn_out", "ln_ffn_scale",
+        "ln_ffn_bias", "w_ffn_in", "b_ffn_in", "w_ffn_out", "b_ffn_out", "w_router", "b_router", "w_gate",
+        "b_gate", "w_out", "b_out")]
+
+
+class MemlayerModelParams(C.Structure):
+    _fields_ = [
+        ("embedding", C.c_void_p),
+        ("pos_embed", C.c_void_p),
+        ("layers", C.POINTER(MemlayerBlockParams)),
+        ("ln_final_scale", C.c_void_p),
+        ("ln_final_bias", C.c_void_p),
+        ("sub_keys", C.c_void_p),
+        ("log_temperature", C.c_void_p),
+        ("values", C.c_void_p),
+    ]
+
+
 MAX_READS = 8
 
 
@@ -152,7 +189,7 @@ DEVICE_ERRORS = {11: "producer wait timed out", 12: "MMA wait timed out", 13: "M
                  14: "epilogue wait timed out", 15: "epilogue pair wait timed out",
                  21: "sub-key id out of range", 22: "sharded row id out of range",
                  23: "fetched slot id out of range", 24: "row push beyond inbox capacity",
-                 25: "host-table row id out of range",
+                 25: "host-table row id out of range", 26: "token id or position out of range",
                  31: "peer inbox wait timed out", 32: "peer partial-sum wait timed out",
                  33: "row-gradient inbox wait timed out", 34: "norm partial wait timed out",
                  35: "peer probe-row wait timed out", 36: "peer dot wait timed out"}
@@ -213,6 +250,18 @@ def lib() -> C.CDLL:
         L.memlayer_layer_forward_staged.argtypes = [C.POINTER(MemlayerConfig), C.POINTER(MemlayerLayerArgs),
                                                     C.POINTER(MemlayerStagedArgs), C.c_int32, C.c_void_p,
                                                     C.c_size_t, C.c_void_p]
+        L.memlayer_model_workspace_size.restype = C.c_int32
+        L.memlayer_model_workspace_size.argtypes = [C.POINTER(MemlayerModelConfig), C.c_int64, C.POINTER(C.c_size_t)]
+        L.memlayer_model_cache_size.restype = C.c_int32
+        L.memlayer_model_cache_size.argtypes = [C.POINTER(MemlayerModelConfig), C.c_int64, C.POINTER(C.c_size_t)]
+        L.memlayer_model_forward.restype = C.c_int32
+        L.memlayer_model_forward.argtypes = [C.POINTER(MemlayerModelConfig), C.POINTER(MemlayerModelParams),
+                                             C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_size_t,
+                                             C.c_void_p]
+        L.memlayer_model_decode_step.restype = C.c_int32
+        L.memlayer_model_decode_step.argtypes = [C.POINTER(MemlayerModelConfig), C.POINTER(MemlayerModelParams),
+                                                 C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                 C.c_void_p, C.c_size_t, C.c_void_p]
         L.memlayer_shard_comm_destroy.restype = C.c_int32
         L.memlayer_shard_comm_destroy.argtypes = [C.c_void_p]
         L.memlayer_shard_workspace_size.restype = C.c_int32

@@ -14,6 +14,7 @@
 //                aux queries are requested);
 //                columns [NR, NR + d): gate = silu(acc + b_gate).
 //   BIAS         y = acc + bias.
+#include "backbone.cuh"
 #include "tc_pipeline.cuh"
 
 namespace ml {
@@ -24,7 +25,7 @@ constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int BN_MAX = 256;
 
-enum { EPI_ROUTER_GATE = 0, EPI_BIAS = 1 };
+enum { EPI_ROUTER_GATE = 0, EPI_BIAS = 1, EPI_GELU = 2 };
 
 struct ProjArgs {
   int64_t M;
@@ -39,9 +40,12 @@ struct ProjArgs {
   float* qlen;         // [M][hc]
   float* qn;           // [M][hc][half] or nullptr
   float* gate;         // [M][N - NR]
-  // BIAS
+  // BIAS / GELU
   float* out;          // [M][N]
+  int bias_smem;       // bias staged in shared memory (N <= BIAS_SMEM_MAX); else read from global
 };
+
+constexpr int BIAS_SMEM_MAX = 4096;
 
 // Per-warp staging tile for coalesced epilogue stores: 32 rows x 16 floats,
 // row stride 20 floats (conflict-free float4 writes by row-owning lanes).
@@ -134,11 +138,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* tiles = smem + 1024;
   // bias vector staged once per CTA (read as a broadcast by every row)
   float* sbias = reinterpret_cast<float*>(tiles + (size_t)P.stages * P.stage_bytes);
-  for (int i = threadIdx.x; i < G.N; i += blockDim.x) sbias[i] = G.bias ? G.bias[i] : 0.f;
+  const int nb_s = G.bias_smem ? G.N : 0;   // wide GEMMs (the tied logits) read the bias from global
+  for (int i = threadIdx.x; i < nb_s; i += blockDim.x) sbias[i] = G.bias ? G.bias[i] : 0.f;
   volatile int* abort = &ctl->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // per-epilogue-warp staging tiles after the bias vector
-  float* stg = sbias + ((G.N + 255) / 256) * 256 + (warp >= 2 ? (warp - 2) * STG_FLOATS : 0);
+  float* stg = sbias + ((nb_s + 255) / 256) * 256 + (warp >= 2 ? (warp - 2) * STG_FLOATS : 0);
   const int units = m_tiles * n_tiles;
   // unit u = (n tile, m tile), m fastest: neighbouring CTAs share the B tile
   auto coords = [&](int u, int& arow, int& brow0, int& nch) {
@@ -194,8 +199,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
-            float x = __uint_as_float(r[t]) + (cc + t < ncols ? sbias[n0 + cc + t] : 0.f);
+            const int n = n0 + cc + t;
+            float x = __uint_as_float(r[t]) +
+                      (cc + t < ncols ? (G.bias_smem ? sbias[n] : (G.bias ? __ldg(G.bias + n) : 0.f)) : 0.f);
             if (EPI == EPI_ROUTER_GATE) x = x / (1.0f + expf(-x));      // model.py:118 silu
+            if (EPI == EPI_GELU)                                         // model.py:104 nn.gelu (tanh form)
+              x = x * (0.5f * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * (x * x * x)))));
             v[t] = x;
           }
 #pragma unroll
@@ -234,8 +243,8 @@ cudaError_t launch_proj(const ProjArgs& G, const float* a_hi, const float* a_lo,
   if (G.M == 0) return cudaSuccess;
   const int BN = bn_for(EPI, G.N);
   // bias vector (padded to 256 floats) + one staging tile per epilogue warp
-  const uint32_t bias_bytes =
-      (((uint32_t)(G.N + 255) / 256 * 256 * 4 + EPI_WARPS * STG_FLOATS * 4) + 1023) / 1024 * 1024;
+  const uint32_t nb_s = G.bias_smem ? (uint32_t)G.N : 0u;
+  const uint32_t bias_bytes = (((nb_s + 255) / 256 * 256 * 4 + EPI_WARPS * STG_FLOATS * 4) + 1023) / 1024 * 1024;
   // 32-element K stages (128-byte swizzle).  16-element stages (64-byte
   // swizzle, twice the ring depth) measured the same: the epilogue, not
   // operand latency, bounds this GEMM.
@@ -359,6 +368,7 @@ cudaError_t launch_router_gate_tc(const Dims& D, const Work& W, const float* bia
   G.qlen = W.qlen;
   G.qn = qn_out;
   G.gate = W.gate;
+  G.bias_smem = 1;
   return launch_proj<EPI_ROUTER_GATE>(G, W.h_hi, W.h_lo, W.wrg_hi, W.wrg_lo, W.err, s);
 }
 
@@ -369,7 +379,30 @@ cudaError_t launch_out_tc(const Dims& D, const Work& W, const float* b_out, floa
   G.K = D.d;
   G.bias = b_out;
   G.out = y;
+  G.bias_smem = G.N <= BIAS_SMEM_MAX;
   return launch_proj<EPI_BIAS>(G, W.memg_hi, W.memg_lo, W.wo_hi, W.wo_lo, W.err, s);
+}
+
+// ---- general Dense layers of the backbone -------------------------------------
+
+bool dense_tc_supported(int64_t M, int K, int N) {
+  return M >= tc::PIPE_M && K % tc::PIPE_K == 0 && K >= tc::PIPE_K && N % 16 == 0 && N >= 16 &&
+         M < (1ll << 31);
+}
+
+cudaError_t launch_dense_tc(const float* a_hi, const float* a_lo, int64_t M, int K, const float* bt_hi,
+                            const float* bt_lo, int N, const float* bias, float* C, int act, int* err,
+                            cudaStream_t s) {
+  ProjArgs G{};
+  G.M = M;
+  G.N = N;
+  G.K = K;
+  G.bias = bias;
+  G.out = C;
+  G.bias_smem = N <= BIAS_SMEM_MAX;
+  if (act == ACT_GELU) return launch_proj<EPI_GELU>(G, a_hi, a_lo, bt_hi, bt_lo, err, s);
+  if (act != ACT_NONE) return cudaErrorInvalidValue;
+  return launch_proj<EPI_BIAS>(G, a_hi, a_lo, bt_hi, bt_lo, err, s);
 }
 
 }  // namespace ml

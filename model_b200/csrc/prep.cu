@@ -1,5 +1,6 @@
 // Normalisation, temperature, float32 GEMM (router / gate / output
 // projections) and the final aux reductions of the memory layer.
+#include "backbone.cuh"
 #include "tc_common.cuh"
 
 namespace ml {
@@ -86,14 +87,22 @@ cudaError_t launch_normalize_queries(const Dims& D, const float* q, float* qn, f
 }
 
 // ---------------------------------------------------------------------------
-// float32 SIMT GEMM: C[M,N] = A[M,K] @ B[K,N] + bias (+ silu), all row-major.
+// float32 SIMT GEMM: C[M,N] = act(A[M,K] @ B[K,N] + bias), all row-major.
 // 64x64 tile, 16-deep k-slices, 256 threads, 4x4 outputs per thread.
 // ---------------------------------------------------------------------------
 constexpr int GB_M = 64, GB_N = 64, GB_K = 16;
 
+// act: 0 none, 1 SiLU (model.py:118), 2 GELU with the tanh approximation
+// (flax's nn.gelu, model.py:104): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == 1) return v / (1.0f + expf(-v));
+  if (act == 2) return v * (0.5f * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * (v * v * v)))));
+  return v;
+}
+
 __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                        const float* __restrict__ bias, float* __restrict__ C,
-                                                       int64_t M, int N, int K, int silu) {
+                                                       int64_t M, int N, int K, int act) {
   __shared__ float As[GB_K][GB_M + 4];
   __shared__ float Bs[GB_K][GB_N + 4];
   int tid = threadIdx.x;
@@ -141,14 +150,12 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
     for (int j = 0; j < 4; ++j) {
       int gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
-      float v = acc[i][j] + (bias ? bias[gn] : 0.f);
-      if (silu) v = v / (1.0f + expf(-v));
-      C[gm * N + gn] = v;
+      C[gm * N + gn] = apply_act(acc[i][j] + (bias ? bias[gn] : 0.f), act);
     }
   }
 }
 
-// Few rows (decode): C[m, n] = sum_k A[m, k] B[k, n] (+ bias, silu).  Lane =
+// Few rows (decode): C[m, n] = act(sum_k A[m, k] B[k, n] + bias).  Lane =
 // output column (coalesced rows of B), the 8 warps of a CTA split K into
 // contiguous ranges and their partial sums are added in warp order through
 // shared memory (deterministic); up to GV_M rows per CTA.
@@ -158,7 +165,7 @@ struct GemvOut {
   const float* B;      // [K, N]
   const float* bias;   // [N] or nullptr
   float* C;            // [M, N]
-  int N, silu;
+  int N, act;
 };
 
 // Up to two products of the same A in one launch: column blocks
@@ -171,7 +178,7 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(const float* __restrict__
   const float* __restrict__ B = second ? out1.B : out0.B;
   const float* __restrict__ bias = second ? out1.bias : out0.bias;
   float* __restrict__ C = second ? out1.C : out0.C;
-  const int N = second ? out1.N : out0.N, silu = second ? out1.silu : out0.silu;
+  const int N = second ? out1.N : out0.N, act = second ? out1.act : out0.act;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int n = ((int)blockIdx.x - (second ? nb0 : 0)) * 32 + lane;
   const int64_t m0 = (int64_t)blockIdx.y * GV_M;
@@ -199,24 +206,28 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(const float* __restrict__
 #pragma unroll
       for (int ww = 0; ww < 8; ++ww) x += part[ww][i][lane];
       if (bias) x += bias[n];
-      if (silu) x = x / (1.0f + expf(-x));
-      C[(m0 + i) * N + n] = x;
+      C[(m0 + i) * N + n] = apply_act(x, act);
     }
   }
 }
 
 cudaError_t launch_gemm(const float* A, const float* B, const float* bias, float* C, int64_t M, int N, int K,
                         bool silu, cudaStream_t s) {
+  return launch_gemm_act(A, B, bias, C, M, N, K, silu ? 1 : 0, s);
+}
+
+cudaError_t launch_gemm_act(const float* A, const float* B, const float* bias, float* C, int64_t M, int N, int K,
+                            int act, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   if (M <= 4 * GV_M) {
-    const GemvOut o{B, bias, C, N, silu ? 1 : 0};
+    const GemvOut o{B, bias, C, N, act};
     const int nb = (N + 31) / 32;
     gemv_f32_kernel<<<dim3(nb, (unsigned)((M + GV_M - 1) / GV_M)), 256, 0, s>>>(A, o, o, nb, M, K);
     count_launch();
     return cudaGetLastError();
   }
   dim3 grid((N + GB_N - 1) / GB_N, (unsigned)((M + GB_M - 1) / GB_M));
-  gemm_f32_kernel<<<grid, 256, 0, s>>>(A, B, bias, C, M, N, K, silu ? 1 : 0);
+  gemm_f32_kernel<<<grid, 256, 0, s>>>(A, B, bias, C, M, N, K, act);
   count_launch();
   return cudaGetLastError();
 }
