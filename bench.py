@@ -808,51 +808,130 @@ def _common_line(W, world, steps, warmup, ms, value, unit, dtype, extra):
     return line
 
 
+def _model_params(torch, device, mc, values, sub_keys, seed=0):
+    """Seeded random-init parameters of a MemoryPoolLM (the reference's
+    shapes) created on the device, around an existing pool table."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    dm, H = mc.d_model, mc.n_heads
+    dh = dm // H
+
+    def r(*shape, std=1.0):
+        return torch.randn(*shape, device=device, generator=g) * std
+
+    def dense(fi, fo):
+        return {"kernel": r(fi, fo, std=fi ** -0.5), "bias": torch.zeros(fo, device=device)}
+
+    def ln():
+        return {"scale": torch.ones(dm, device=device), "bias": torch.zeros(dm, device=device)}
+
+    p = {"embed": {"embedding": r(mc.vocab_size, dm)}, "pos_embed": r(mc.max_len, dm, std=0.02)}
+    for i in range(mc.n_layers):
+        p[f"ln_attn_{i}"] = ln()
+        p[f"attn_{i}"] = {n: {"kernel": r(dm, H, dh, std=dm ** -0.5), "bias": torch.zeros(H, dh, device=device)}
+                          for n in ("query", "key", "value")}
+        p[f"attn_{i}"]["out"] = {"kernel": r(H, dh, dm, std=dm ** -0.5), "bias": torch.zeros(dm, device=device)}
+        p[f"ln_ffn_{i}"] = ln()
+        if i not in mc.memory_layers or mc.memory_ffn:
+            p[f"ffn_in_{i}"] = dense(dm, dm * mc.ffn_mult)
+            p[f"ffn_out_{i}"] = dense(dm * mc.ffn_mult, dm)
+        if i in mc.memory_layers:
+            p[f"router_{i}"] = dense(dm, mc.pool_heads * mc.d_key)
+            p[f"mem_gate_{i}"] = dense(dm, mc.d_value)
+            p[f"mem_out_{i}"] = dense(mc.d_value, dm)
+    p["pool"] = {"sub_keys": sub_keys, "values": values,
+                 "log_temperature": torch.tensor(math.log(10.0), device=device)}
+    p["ln_final"] = ln()
+    return p
+
+
 def run_cfg1(args):
-    """configs[1]'s memory layers: batch 32 x seq 256 = 8192 tokens, d_model
-    256, memory layers 1 and 3 sharing one pool of 262,144 x 256 fp16 rows,
-    H 4, top_k 16, d_key 128 (the reference run's setting).  A step is the two
-    memory-layer calls of one model forward (each with its own router / gate
-    / output kernels and hidden state); the backbone is not part of this
-    library."""
+    """configs[1], the full model forward: byte-BPE vocabulary 16,384, d_model
+    256, 4 layers, 4 attention heads, FFN x4, seq 256, batch 32, memory
+    layers 1 and 3 sharing one pool of 262,144 x 256 fp16 rows (H 4, top_k
+    16, d_key 128, the reference run's setting); random-init weights, tokens
+    uniform over the vocabulary.  A step is one memlayer_model_forward
+    (embeddings -> 4 layers -> tied logits [8192, 16384]); the two memory
+    layers' own time is measured separately (their calls alone)."""
     import torch
 
+    from model_b200 import MemoryPoolLM, ModelConfig
     from model_b200 import _lib as L
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    W = dict(WORKLOAD, name="cfg1_model_memory_layers", d_key=128, values_dtype="f16")
-    xs = [make_inputs(torch, device, W, "f16", W["seed"] + i) for i in range(2)]
-    xs[1]["values"] = xs[0]["values"]                 # one shared pool
-    xs[1]["sub_keys"] = xs[0]["sub_keys"]
-    calls = [LayerCall(torch, L, W, x, device, "f16") for x in xs]
+    W = dict(WORKLOAD, name="cfg1_model_forward", d_key=128, values_dtype="f16")
+    B, T = 32, 256
+    mc = ModelConfig(vocab_size=16384, max_len=T, d_model=256, n_layers=4, n_heads=4, ffn_mult=4,
+                     memory_layers=(1, 3), n_sub_keys=512, pool_heads=4, d_key=128, d_value=256, top_k=16)
+    x = make_inputs(torch, device, W, "f16", W["seed"])
+    model = MemoryPoolLM(mc)
+    prep = model.prepare(_model_params(torch, device, mc, x["values"], x["sub_keys"], W["seed"]))
+    g = torch.Generator(device=device).manual_seed(W["seed"] + 7)
+    tokens = torch.randint(0, mc.vocab_size, (B, T), device=device, generator=g, dtype=torch.int32)
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    launches0 = L.lib().memlayer_kernel_launch_count()
+    prep.forward(tokens, check=True)
+    launches = L.lib().memlayer_kernel_launch_count() - launches0
     for _ in range(args.warmup):
         flush.zero_()
-        for c in calls:
-            c(stream)
+        prep.forward(tokens)
     torch.cuda.synchronize()
     K = args.steps
-    e = [_events(torch, 3) for _ in range(K)]
+    e = [_events(torch, 2) for _ in range(K)]
+    with ClockSampler(device.index) as clk:
+        for i in range(K):
+            flush.zero_()
+            e[i][0].record(stream)
+            logits = prep.forward(tokens)
+            e[i][1].record(stream)
+        torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in e)
+    # the two memory layers' calls alone, on the same hidden-state size
+    xs = [x, make_inputs(torch, device, W, "f16", W["seed"] + 1)]
+    xs[1]["values"], xs[1]["sub_keys"] = x["values"], x["sub_keys"]
+    calls = [LayerCall(torch, L, W, xx, device, "f16") for xx in xs]
+    me = [_events(torch, 2) for _ in range(K)]
     for i in range(K):
         flush.zero_()
-        e[i][0].record(stream)
-        calls[0](stream)
-        e[i][1].record(stream)
-        calls[1](stream)
-        e[i][2].record(stream)
+        me[i][0].record(stream)
+        for c in calls:
+            c(stream)
+        me[i][1].record(stream)
     torch.cuda.synchronize()
-    l1 = statistics.mean(x[0].elapsed_time(x[1]) for x in e)
-    l3 = statistics.mean(x[1].elapsed_time(x[2]) for x in e)
-    ms = l1 + l3
-    T = W["tokens_per_gpu"]
-    hbm, src = peaks()
-    rows = 2 * T * W["heads"] * W["top_k"] * W["d_value"] * 2   # fp16 rows of both layers
-    return _common_line(W, 1, K, args.warmup, ms, T / (ms * 1e-3), "tokens/s", "f16", {
-        "scaling": "weak", "stages_ms": {"memory_layer_1": l1, "memory_layer_3": l3},
-        "gather_row_gbs": rows / (ms * 1e-3) / 1e9, "hbm_peak": hbm, "peak_source": src,
-        "note": "the two memory-layer calls of one model forward; the attention / FFN backbone of configs[1] is "
-                "outside this library.  L2 flushed before every step"})
+    mem_ms = statistics.mean(a.elapsed_time(b) for a, b in me)
+    # e2e: tokens in from pinned host memory, the logits' argmax back (the step's result)
+    tok_host = tokens.cpu().pin_memory()
+    tok_dev = torch.empty_like(tokens)
+    out_host = torch.empty(B, T, dtype=torch.int64).pin_memory()
+    ee = _events(torch, 2)
+    torch.cuda.synchronize()
+    ee[0].record(stream)
+    for i in range(K):
+        tok_dev.copy_(tok_host, non_blocking=True)
+        lg = prep.forward(tok_dev)
+        out_host.copy_(lg.argmax(-1), non_blocking=True)
+    ee[1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ee[0].elapsed_time(ee[1]) / K
+    dm, F, V = 256, 1024, mc.vocab_size
+    dense_per_token = 2 * (4 * 4 * dm * dm + 2 * 2 * dm * F + dm * V)   # qkv + out in 4 layers, 2 FFNs, logits
+    attn_per_token = 4 * 2 * 2 * (T // 2) * dm                          # QK^T and PV over half the keys
+    line = _common_line(W, 1, K, args.warmup, ms, B * T / (ms * 1e-3), "tokens/s", "f32", {
+        "metric": "model forward tokens/s", "scaling": "n/a",
+        "backbone_flops_per_token": dense_per_token + attn_per_token, "stages_ms": {"model_forward": ms, "memory_layers_alone": mem_ms},
+        "config": {"workload": "cfg1_model_forward", "vocab": mc.vocab_size, "d_model": 256, "layers": 4,
+                   "heads": 4, "ffn_mult": 4, "seq": T, "batch": B, "memory_layers": [1, 3],
+                   "pool": "262144 x 256 fp16, H 4, top_k 16, d_key 128", "values_dtype": "f16",
+                   "l2": "flushed before every step"},
+        "gpu_launches_per_step": int(launches),
+        "e2e": {"value": B * T / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": tok_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 8,
+                "api": "MemoryPoolLM (memlayer_model_forward), tokens copied in, argmax of the logits copied out"},
+        "clocks": clk.summary(),
+        "data": "synthetic: random-init weights, tokens uniform over the vocabulary",
+        "note": "float32 backbone on the tensor cores (3xTF32 Dense layers), float32 SIMT attention"})
+    del logits
+    return line
 
 
 def run_cfg4(args, rank=0, world=1):
@@ -1185,12 +1264,45 @@ def run_cfg2(args):
         res[B]["graph_p50_us"] = gt[len(gt) // 2]
         res[B]["host_steps_per_s"] = {"eager": decode_steps_per_second(estep, 200),
                                       "graph": decode_steps_per_second(gstep, 200)}
+    # the whole model's decode step around the same pool (4 layers, d_model 256, 4 heads, FFN x4,
+    # memory layers 1 and 3, 16,384-token vocabulary): MemoryPoolLM's Generator, one CUDA graph per step
+    from model_b200 import Generator, MemoryPoolLM, ModelConfig
+    mc = ModelConfig(vocab_size=16384, max_len=256, d_model=256, n_layers=4, n_heads=4, ffn_mult=4,
+                     memory_layers=(1, 3), n_sub_keys=W["n_sub_keys"], pool_heads=4, d_key=128, d_value=256, top_k=16)
+    prep = MemoryPoolLM(mc).prepare(_model_params(torch, device, mc, x["values"], x["sub_keys"], W["seed"]))
+    model_res = {}
+    for B in (1, 8, 64):
+        gen = Generator(MemoryPoolLM(mc), prep, batch_size=B)
+        tok = torch.randint(0, mc.vocab_size, (B,), device=device, dtype=torch.int32)
+        for i in range(args.warmup):
+            gen.step(tok, i)
+        gs = gen.stream
+        ge = _events(torch, 2 * args.steps)
+        for i in range(args.steps):
+            ge[2 * i].record(gs)
+            gen.step(tok, (args.warmup + i) % mc.max_len)
+            ge[2 * i + 1].record(gs)
+        torch.cuda.synchronize()
+        if gen.status():
+            raise RuntimeError(f"model decode step status {gen.status()}")
+        gt = sorted(ge[2 * i].elapsed_time(ge[2 * i + 1]) * 1000 for i in range(args.steps))
+        t0 = time.perf_counter()
+        n = 100
+        for i in range(n):
+            gen.step(tok, i % mc.max_len)
+            gs.synchronize()
+        host = n / (time.perf_counter() - t0)
+        model_res[B] = {"graph_p50_us": gt[len(gt) // 2], "graph_p90_us": gt[int(len(gt) * 0.9)],
+                        "tokens_per_s": B / (gt[len(gt) // 2] * 1e-6), "host_steps_per_s": host}
+        del gen
     return _common_line(W, 1, args.steps, args.warmup, res[64]["p50_us"] / 1000, res[64]["tokens_per_s"],
-                        "tokens/s", "f16", {"scaling": "n/a", "decode": res,
+                        "tokens/s", "f16", {"scaling": "n/a", "decode": res, "model_decode": model_res,
                                             "note": "value = batch 64; per-step device time, L2 not flushed "
                                                     "(decode steps run back to back); graph_p50_us: the same "
                                                     "call replayed as a CUDA graph; host_steps_per_s: steps "
-                                                    "issued and waited for one at a time"})
+                                                    "issued and waited for one at a time; model_decode: the "
+                                                    "whole model's decode step (backbone + both memory layers "
+                                                    "+ 16,384-way logits) around the same 34 GB pool"})
 
 
 def run_cfg3(args, rank, world):
