@@ -536,7 +536,7 @@ int32_t memlayer_row_adagrad_sharded(const memlayer_config* cfg, const memlayer_
  * Dropout is the identity (inference).  LayerNorm is flax's (epsilon 1e-6,
  * variance E[x^2] - E[x]^2), GELU its tanh form, attention scales the query
  * by 1/sqrt(head_dim).  head_dim = d_model / n_heads must be 32 or 64;
- * d_model <= 1024.  The status of a model call (token ids out of range: 26,
+ * d_model one of 32, 64, 128, 256, 512, 1024.  The status of a model call (token ids out of range: 26,
  * and the memory layers' codes) is read with memlayer_workspace_status(&cfg->pool,
  * workspace, ...). */
 #define MEMLAYER_MAX_LAYERS 32

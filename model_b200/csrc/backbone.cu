@@ -33,31 +33,47 @@ __global__ void __launch_bounds__(256) embed_kernel(const int* __restrict__ toke
 
 // x += y (when y is given), then h = LayerNorm(x) (model.py:87,96,124 with
 // flax's LayerNorm: eps 1e-6, variance E[x^2] - E[x]^2 clamped at 0,
-// (x - mean) * (rsqrt(var + eps) * scale) + bias).  One warp per row.
-constexpr int LN_MAX = 32;   // values per lane: d_model <= 1024
+// (x - mean) * (rsqrt(var + eps) * scale) + bias).  One warp per row, VPL
+// values per lane (d_model = 32 * VPL), 16-byte accesses when VPL % 4 == 0.
+template <int VPL>
 __global__ void __launch_bounds__(256) add_ln_kernel(float* __restrict__ x, const float* __restrict__ y,
                                                      const float* __restrict__ scale,
                                                      const float* __restrict__ bias, float* __restrict__ h,
-                                                     int64_t M, int dm) {
+                                                     int64_t M) {
+  constexpr int dm = 32 * VPL;
+  constexpr int V4 = VPL % 4 == 0 ? 4 : 1;   // elements per access
   const int64_t m = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
-  float v[LN_MAX];
+  float v[VPL];
   float s = 0.f, s2 = 0.f;
 #pragma unroll
-  for (int i = 0; i < LN_MAX; ++i) {
-    const int j = lane + 32 * i;
-    v[i] = 0.f;
-    if (j < dm) {
+  for (int i = 0; i < VPL; i += V4) {
+    const int j = (i / V4) * 32 * V4 + lane * V4;   // V4 consecutive columns per access
+    if constexpr (V4 == 4) {
+      float4 a = *reinterpret_cast<const float4*>(x + m * dm + j);
+      if (y) {
+        const float4 b = *reinterpret_cast<const float4*>(y + m * dm + j);
+        a = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+        *reinterpret_cast<float4*>(x + m * dm + j) = a;
+      }
+      v[i] = a.x;
+      v[i + 1] = a.y;
+      v[i + 2] = a.z;
+      v[i + 3] = a.w;
+    } else {
       float a = x[m * dm + j];
       if (y) {
         a += y[m * dm + j];
         x[m * dm + j] = a;
       }
       v[i] = a;
-      s += a;
-      s2 = fmaf(a, a, s2);
     }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    s += v[i];
+    s2 = fmaf(v[i], v[i], s2);
   }
   s = warp_sum(s);
   s2 = warp_sum(s2);
@@ -65,97 +81,187 @@ __global__ void __launch_bounds__(256) add_ln_kernel(float* __restrict__ x, cons
   const float var = fmaxf(0.f, s2 / (float)dm - mean * mean);
   const float r = 1.0f / sqrtf(var + 1e-6f);
 #pragma unroll
-  for (int i = 0; i < LN_MAX; ++i) {
-    const int j = lane + 32 * i;
-    if (j < dm) h[m * dm + j] = (v[i] - mean) * (r * scale[j]) + bias[j];
+  for (int i = 0; i < VPL; i += V4) {
+    const int j = (i / V4) * 32 * V4 + lane * V4;
+#pragma unroll
+    for (int t = 0; t < V4; ++t) h[m * dm + j + t] = (v[i + t] - mean) * (r * scale[j + t]) + bias[j + t];
   }
 }
 
 // Causal self-attention of whole sequences (model.py:88-95, flax
 // dot_product_attention): qkv [B*T, 3*dm] with the query, key and value of
 // head h at columns h*DH, dm + h*DH and 2*dm + h*DH; out [B*T, dm] in the
-// same head-major order.  A CTA takes 32 queries of one (batch, head) and
-// walks 32-key tiles up to the diagonal with an online softmax (running
-// max and sum in float32); 8 threads per query, each scoring 4 keys and
-// accumulating DH/8 output dims.
-constexpr int AQ = 32, AK = 32;
+// same head-major order.  A CTA takes 64 queries of one (batch, head) and
+// walks 64-key tiles up to the diagonal with an online softmax (running max
+// and sum in float32).  Both products are register-blocked float32 GEMM
+// tiles on 256 threads: S = Q K^T with a 4 x 4 block per thread (16-byte
+// shared-memory loads along the head dimension), then O += P V with a
+// 4-row x DH/16-column block per thread; the row statistics sit in shared
+// memory between the two.
+constexpr int AT = 64;   // queries and keys per tile
 
 template <int DH>
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restrict__ qkv, float* __restrict__ out,
                                                            int T, int H) {
-  __shared__ float qs[AQ][DH + 1];
-  __shared__ float ks[AK][DH + 1];
-  __shared__ float vs[AK][DH];
+  constexpr int LD = DH + 4;      // row stride of Q / K / V tiles (16-byte aligned rows)
+  constexpr int LS = AT + 4;      // row stride of the score tile
+  constexpr int OC = DH / 16;     // output columns per thread
+  extern __shared__ float4 asm_raw[];
+  float* qs = reinterpret_cast<float*>(asm_raw);   // [AT][LD], pre-divided by sqrt(DH)
+  float* ks = qs + AT * LD;                          // [AT][LD]
+  float* vs = ks + AT * LD;                          // [AT][LD]
+  float* ps = vs + AT * LD;                          // [AT][LS] scores, then probabilities
+  float* mrow = ps + AT * LS;                        // [AT] running max
+  float* lrow = mrow + AT;                           // [AT] running sum
+  float* crow = lrow + AT;                           // [AT] this tile's rescale of O
   const int dm = H * DH, ld = 3 * dm;
-  const int q0 = blockIdx.x * AQ, h = blockIdx.y;
+  const int q0 = blockIdx.x * AT, h = blockIdx.y;
   const int64_t b = blockIdx.z;
-  const int tid = threadIdx.x, qi = tid >> 3, part = tid & 7;
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const float rs = sqrtf((float)DH);
-  for (int e = tid; e < AQ * DH; e += 256) {
-    const int r = e / DH, c = e - r * DH;
+  for (int e = tid; e < AT * DH / 4; e += 256) {
+    const int r = e / (DH / 4), c = (e - r * (DH / 4)) * 4;
     const int t = q0 + r;
-    qs[r][c] = t < T ? qkv[(b * T + t) * ld + h * DH + c] / rs : 0.f;   // query / sqrt(depth)
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < T) v = *reinterpret_cast<const float4*>(qkv + (b * T + t) * ld + h * DH + c);
+    *reinterpret_cast<float4*>(qs + r * LD + c) = make_float4(v.x / rs, v.y / rs, v.z / rs, v.w / rs);
   }
-  constexpr int OD = DH / 8;
-  float acc[OD];
+  if (tid < AT) {
+    mrow[tid] = -FLT_MAX;
+    lrow[tid] = 0.f;
+  }
+  float o[4][OC];
 #pragma unroll
-  for (int i = 0; i < OD; ++i) acc[i] = 0.f;
-  float mrun = -FLT_MAX, lrun = 0.f;
-  const int tq = q0 + qi;                          // this thread's query
-  const int kend = min(T, q0 + AQ);                // keys past the block's last query are masked for all
-  for (int k0 = 0; k0 < kend; k0 += AK) {
-    __syncthreads();
-    for (int e = tid; e < AK * DH; e += 256) {
-      const int r = e / DH, c = e - r * DH;
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < OC; ++j) o[i][j] = 0.f;
+  const int kend = min(T, q0 + AT);
+  for (int k0 = 0; k0 < kend; k0 += AT) {
+    __syncthreads();   // previous tile's P / V consumed
+    for (int e = tid; e < AT * DH / 4; e += 256) {
+      const int r = e / (DH / 4), c = (e - r * (DH / 4)) * 4;
       const int t = k0 + r;
-      const int64_t row = (b * T + (t < T ? t : 0)) * ld;
-      ks[r][c] = t < T ? qkv[row + dm + h * DH + c] : 0.f;
-      vs[r][c] = t < T ? qkv[row + 2 * dm + h * DH + c] : 0.f;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (t < T) {
+        const float* row = qkv + (b * T + t) * ld + h * DH + c;
+        kv = *reinterpret_cast<const float4*>(row + dm);
+        vv = *reinterpret_cast<const float4*>(row + 2 * dm);
+      }
+      *reinterpret_cast<float4*>(ks + r * LD + c) = kv;
+      *reinterpret_cast<float4*>(vs + r * LD + c) = vv;
     }
     __syncthreads();
-    float sc[4];
-    float mt = -FLT_MAX;
+    // S = Q K^T: thread block rows ty + 16 i, columns tx + 16 j
+    float sc[4][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int kk = part * 4 + j, tk = k0 + kk;
-      float s = 0.f;
-#pragma unroll 8
-      for (int c = 0; c < DH; ++c) s = fmaf(qs[qi][c], ks[kk][c], s);
-      sc[j] = (tk <= tq && tk < T) ? s : -FLT_MAX;   // causal mask
-      mt = fmaxf(mt, sc[j]);
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < DH; c += 4) {
+      float4 a[4], bk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(qs + (ty + 16 * i) * LD + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bk[j] = *reinterpret_cast<const float4*>(ks + (tx + 16 * j) * LD + c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sc[i][j] = fmaf(a[i].x, bk[j].x, sc[i][j]);
+          sc[i][j] = fmaf(a[i].y, bk[j].y, sc[i][j]);
+          sc[i][j] = fmaf(a[i].z, bk[j].z, sc[i][j]);
+          sc[i][j] = fmaf(a[i].w, bk[j].w, sc[i][j]);
+        }
     }
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(FULL, mt, o));
-    const float mnew = fmaxf(mrun, mt);
-    float p[4], ps = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      p[j] = sc[j] == -FLT_MAX ? 0.f : expf(sc[j] - mnew);
-      ps += p[j];
-    }
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) ps += __shfl_xor_sync(FULL, ps, o);
-    const float corr = mrun == -FLT_MAX ? 0.f : expf(mrun - mnew);
-    lrun = lrun * corr + ps;
-    mrun = mnew;
-#pragma unroll
-    for (int i = 0; i < OD; ++i) acc[i] *= corr;
-    // every key of the tile: its probability from the thread that scored it
-#pragma unroll
-    for (int src = 0; src < 8; ++src) {
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float pk = __shfl_sync(FULL, p[j], (threadIdx.x & 24) | src);
-        const int kk = src * 4 + j;
+        const int tq = q0 + ty + 16 * i, tk = k0 + tx + 16 * j;
+        ps[(ty + 16 * i) * LS + tx + 16 * j] = (tk <= tq && tk < T) ? sc[i][j] : -FLT_MAX;   // causal mask
+      }
+    __syncthreads();
+    // online softmax per row: 4 threads per row, 16 columns each
+    {
+      const int r = tid >> 2, part = tid & 3;
+      float* pr = ps + r * LS + part * 16;
+      float mt = -FLT_MAX;
 #pragma unroll
-        for (int i = 0; i < OD; ++i) acc[i] = fmaf(pk, vs[kk][part * OD + i], acc[i]);
+      for (int c = 0; c < 16; ++c) mt = fmaxf(mt, pr[c]);
+      mt = fmaxf(mt, __shfl_xor_sync(FULL, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(FULL, mt, 2));
+      const float mold = mrow[r];
+      const float mnew = fmaxf(mold, mt);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float p = pr[c] == -FLT_MAX ? 0.f : expf(pr[c] - mnew);
+        pr[c] = p;
+        sum += p;
+      }
+      sum += __shfl_xor_sync(FULL, sum, 1);
+      sum += __shfl_xor_sync(FULL, sum, 2);
+      __syncwarp();
+      if (part == 0) {
+        const float corr = mold == -FLT_MAX ? 0.f : expf(mold - mnew);
+        crow[r] = corr;
+        lrow[r] = lrow[r] * corr + sum;
+        mrow[r] = mnew;
+      }
+    }
+    __syncthreads();
+    // O = O * corr + P V: thread rows ty + 16 i, columns tx * OC .. + OC
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float cr = crow[ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < OC; ++j) o[i][j] *= cr;
+    }
+#pragma unroll 2
+    for (int k = 0; k < AT; k += 4) {
+      float4 pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(ps + (ty + 16 * i) * LS + k);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        float vr[OC];
+        if constexpr (OC % 4 == 0) {
+#pragma unroll
+          for (int j = 0; j < OC; j += 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(vs + (k + kk) * LD + tx * OC + j);
+            vr[j] = v4.x;
+            vr[j + 1] = v4.y;
+            vr[j + 2] = v4.z;
+            vr[j + 3] = v4.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < OC; j += 2) {
+            const float2 v2 = *reinterpret_cast<const float2*>(vs + (k + kk) * LD + tx * OC + j);
+            vr[j] = v2.x;
+            vr[j + 1] = v2.y;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float p = kk == 0 ? pv[i].x : kk == 1 ? pv[i].y : kk == 2 ? pv[i].z : pv[i].w;
+#pragma unroll
+          for (int j = 0; j < OC; ++j) o[i][j] = fmaf(p, vr[j], o[i][j]);
+        }
       }
     }
   }
-  if (tq < T) {
-    const float inv = 1.0f / lrun;
+  __syncthreads();
 #pragma unroll
-    for (int i = 0; i < OD; ++i) out[(b * T + tq) * dm + h * DH + part * OD + i] = acc[i] * inv;
+  for (int i = 0; i < 4; ++i) {
+    const int r = ty + 16 * i, tq = q0 + r;
+    if (tq >= T) continue;
+    const float inv = 1.0f / lrow[r];
+    float* dst = out + (b * T + tq) * dm + h * DH + tx * OC;
+#pragma unroll
+    for (int j = 0; j < OC; j += 2)
+      *reinterpret_cast<float2*>(dst + j) = make_float2(o[i][j] * inv, o[i][j + 1] * inv);
   }
 }
 
@@ -289,23 +395,39 @@ cudaError_t launch_embed(const int* tokens, int64_t M, int T, const int* pos, co
 cudaError_t launch_add_ln(float* x, const float* y, const float* scale, const float* bias, float* h, int64_t M, int dm,
                           cudaStream_t s) {
   if (M == 0) return cudaSuccess;
-  if (dm > 32 * LN_MAX) return cudaErrorInvalidValue;
-  add_ln_kernel<<<(unsigned)((M + 7) / 8), 256, 0, s>>>(x, y, scale, bias, h, M, dm);
+  const unsigned grid = (unsigned)((M + 7) / 8);
+  switch (dm) {
+    case 32: add_ln_kernel<1><<<grid, 256, 0, s>>>(x, y, scale, bias, h, M); break;
+    case 64: add_ln_kernel<2><<<grid, 256, 0, s>>>(x, y, scale, bias, h, M); break;
+    case 128: add_ln_kernel<4><<<grid, 256, 0, s>>>(x, y, scale, bias, h, M); break;
+    case 256: add_ln_kernel<8><<<grid, 256, 0, s>>>(x, y, scale, bias, h, M); break;
+    case 512: add_ln_kernel<16><<<grid, 256, 0, s>>>(x, y, scale, bias, h, M); break;
+    case 1024: add_ln_kernel<32><<<grid, 256, 0, s>>>(x, y, scale, bias, h, M); break;
+    default: return cudaErrorInvalidValue;
+  }
+  count_launch();
+  return cudaGetLastError();
+}
+
+bool ln_supported(int dm) { return dm == 32 || dm == 64 || dm == 128 || dm == 256 || dm == 512 || dm == 1024; }
+
+template <int DH>
+cudaError_t attn_prefill_dh(const float* qkv, float* out, int64_t B, int T, int H, cudaStream_t s) {
+  const size_t smem = sizeof(float) * (3 * AT * (DH + 4) + AT * (AT + 4) + 3 * AT);
+  const cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((T + AT - 1) / AT), (unsigned)H, (unsigned)B);
+  attn_prefill_kernel<DH><<<grid, 256, smem, s>>>(qkv, out, T, H);
   count_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_attn_prefill(const float* qkv, float* out, int64_t B, int T, int H, int DH, cudaStream_t s) {
   if (B == 0 || T == 0) return cudaSuccess;
-  const dim3 grid((unsigned)((T + AQ - 1) / AQ), (unsigned)H, (unsigned)B);
-  if (DH == 64)
-    attn_prefill_kernel<64><<<grid, 256, 0, s>>>(qkv, out, T, H);
-  else if (DH == 32)
-    attn_prefill_kernel<32><<<grid, 256, 0, s>>>(qkv, out, T, H);
-  else
-    return cudaErrorInvalidValue;
-  count_launch();
-  return cudaGetLastError();
+  if (DH == 64) return attn_prefill_dh<64>(qkv, out, B, T, H, s);
+  if (DH == 32) return attn_prefill_dh<32>(qkv, out, B, T, H, s);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_attn_decode(const float* qkv, float* cache_k, float* cache_v, const int* pos, int max_len,

@@ -7,6 +7,7 @@
 namespace ml {
 
 bool attn_supported(int head_dim);
+bool ln_supported(int d_model);   // 32, 64, 128, 256, 512 or 1024
 cudaError_t launch_embed(const int* tokens, int64_t M, int T, const int* pos, const float* E, const float* Pe, int V,
                          int dm, int max_len, float* x, int* err, cudaStream_t s);
 cudaError_t launch_add_ln(float* x, const float* y, const float* scale, const float* bias, float* h, int64_t M, int dm,

@@ -39,7 +39,7 @@ int check_model(const memlayer_model_config* c, ModelDims* d) {
       c->n_heads < 1 || c->ffn_mult < 1 || c->d_model % c->n_heads)
     return MEMLAYER_ERR_BAD_SHAPE;
   const int dh = c->d_model / c->n_heads;
-  if (!attn_supported(dh) || c->d_model > 1024 || c->d_model % 4) return MEMLAYER_ERR_UNSUPPORTED;
+  if (!attn_supported(dh) || !ln_supported(c->d_model)) return MEMLAYER_ERR_UNSUPPORTED;
   if (c->n_layers < 32 && (c->memory_layers >> c->n_layers)) return MEMLAYER_ERR_BAD_SHAPE;
   d->V = c->vocab_size;
   d->L = c->n_layers;
