@@ -190,11 +190,26 @@ int overlap_first_tiles(int mt_all, int hc, int sms) {
   return mta >= 1 && mta < mt_all ? mta : mt_all / 2;
 }
 
-// The push of a row-sharded call: one launch per token half; after_a (if
-// set) is recorded between the halves.
+// Token split of an overlapped call: the first part's score kernel fills
+// whole rounds of the SMs, the second part's runs on fewer CTAs beside the
+// first part's gather.  0 when the call does not overlap.
+int64_t overlap_split(const Dims& D, bool tc_scores, bool balance) {
+  const int mt_all = (int)((D.M + SCORE_TM - 1) / SCORE_TM);
+  if (!tc_scores || balance || mt_all < 16 || !overlap_enabled()) return 0;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return (int64_t)overlap_first_tiles(mt_all, D.H * 2, sms) * SCORE_TM;
+}
+
+// The scatter of a row-sharded call: one per token half; after_a (if set)
+// is recorded between the halves.  overlap: the halves split at a tile
+// boundary (overlap_split) and the second half's score kernel runs after
+// the first half's scatter, beside the first half's gather.
 struct ShardRun {
   ShardK half[2];
   bool split;
+  bool overlap;
   cudaEvent_t after_a;
 };
 
@@ -245,6 +260,30 @@ int run_route_mix(const Dims& D, const memlayer_pool_args* a, const Work& W, flo
     st = body();
     for (int i = 0; i < 2; ++i) cudaEventDestroy(ev[i]);   // released once their work completes
     return st;
+  }
+  if (sh && sh->overlap && W.q_hi && !bal) {
+    // row-sharded, two halves: score(A), stage 2 + scatter(A), then score(B)
+    // on fewer CTAs while the owners gather half A (launched by the caller
+    // on the library stream after `after_a`), then stage 2 + scatter(B)
+    const int mta = (int)(sh->half[0].t1 / SCORE_TM);
+    if (a->slot_counts) ML_TRY(cudaMemsetAsync(a->slot_counts, 0, sizeof(float) * D.N, s));
+    if (a->subkey_counts) ML_TRY(cudaMemsetAsync(a->subkey_counts, 0, sizeof(float) * D.H * 2 * D.n, s));
+    for (int hf = 0; hf < 2; ++hf) {
+      const ShardK& K = sh->half[hf];
+      if (hf == 0)
+        ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, false, s, 0, mta, 0));
+      else
+        ML_TRY(launch_score_topk_tc(D, w2, a->gumbel, false, s, mta, mt_all - mta, OVERLAP_SCORE_CTAS));
+      if (hf == 1) ML_TRY(mark(a, 3, s));
+      if (K.t1 > K.t0)
+        ML_TRY(launch_combine_gather(D, w2, nullptr, slots, weights, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                     a->slot_counts, a->subkey_counts, s, K.t0, K.t1 - K.t0));
+      ML_TRY(launch_shard_scatter(D, K, slots, weights, W.own_cnt, W.err, s));
+      if (hf == 0 && sh->after_a) ML_TRY(cudaEventRecord(sh->after_a, s));
+    }
+    ML_TRY(mark(a, 4, s));
+    ML_TRY(launch_finalize(D, w2, a->top1_weight, a->temperature, s));
+    return MEMLAYER_OK;
   }
   if (W.q_hi)   // the tensor-core balance pass computes its own row max / sum: the score kernel
                 // needs its statistics variant only for the clean top-k of noisy calls
@@ -323,12 +362,13 @@ ShardK shard_k(const memlayer_shard_comm* comm, const Dims& D) {
 }
 
 // The two token halves of a split call (or the whole call as half 0).
-ShardRun shard_run(const memlayer_shard_comm* comm, const Dims& D, bool split) {
+ShardRun shard_run(const memlayer_shard_comm* comm, const Dims& D, bool split, int64_t at = 0) {
   ShardRun R{};
   R.split = split;
+  R.overlap = split && at > 0;
   R.half[0] = shard_k(comm, D);
   if (split) {
-    const int64_t h0 = (D.M + 1) / 2;
+    const int64_t h0 = at > 0 ? at : (D.M + 1) / 2;
     R.half[0].t1 = h0;
     R.half[0].span = (R.half[0].mcap + 1) / 2;
     R.half[1] = R.half[0];
@@ -448,7 +488,7 @@ int pool_impl(const memlayer_config* cfg, const memlayer_pool_args* a, void* wor
   SplitEvents ev;
   if (overlap && (st = ev.create())) return st;
   if (phases & MEMLAYER_PHASE_ROUTE) ++comm->epoch;
-  ShardRun R = shard_run(comm, D, split);
+  ShardRun R = shard_run(comm, D, split, overlap ? overlap_split(D, W.q_hi != nullptr, f.balance) : 0);
   R.after_a = overlap ? ev.e[0] : nullptr;
   if (phases & MEMLAYER_PHASE_ROUTE) {
     ML_TRY(mark(a, 0, s));
@@ -527,7 +567,7 @@ int layer_impl(const memlayer_config* cfg, const memlayer_layer_args* a, void* w
   ShardRun R{};
   if (comm) {
     if (route) ++comm->epoch;
-    R = shard_run(comm, D, split);
+    R = shard_run(comm, D, split, overlap ? overlap_split(D, W.q_hi != nullptr, f.balance) : 0);
     R.after_a = overlap ? ev.e[0] : nullptr;
   }
   const ShardRun* sh = comm ? &R : nullptr;

@@ -37,7 +37,9 @@ def _worker(rank, world, port, outdir, vdt_name):
         pool = MemoryPool(n_sub_keys=128, heads=4, d_key=128, d_value=128, top_k=16)
         layer = MemoryLayer(pool, d_model=128, layer=1)
         params = layer.init(0, values_dtype=vdt)                      # same seed: same table on every rank
-        M = 777
+        # 2600 tokens: 21 score tiles, so the split calls take the overlapped
+        # path (second half's score beside the first half's gather)
+        M = 2600
         h = torch.randn(M, 128, device="cuda", generator=torch.Generator("cuda").manual_seed(5 + rank))
         comm = connect(pool.config(M, vdt, 128))
         local = dict(params, pool=dict(params["pool"], values=shard_values(params["pool"]["values"], rank, world)))
