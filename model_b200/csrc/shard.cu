@@ -121,23 +121,79 @@ __global__ void __launch_bounds__(256) shard_scatter_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
-// gather: a persistent grid; warps claim units of GATHER_TPU consecutive
+// gather: a persistent grid; warps claim units of gather_tpu consecutive
 // tokens of one source rank from per-source counters, taking this rank's
 // own tokens first and then whichever source's inbox is ready, so a late
 // push holds up only the warps that have nothing else left to do
 // ---------------------------------------------------------------------------
-constexpr int GATHER_TPU = 4;
+// tokens per claimed unit: one with few sources (each token carries many
+// rows), more with many (little work per token, fewer counter atomics)
+__device__ __forceinline__ int gather_tpu(int world) { return world <= 2 ? 1 : world / 2; }
 constexpr int GATHER_CTR = 16;   // int slot of the per-source unit counters in the tickets region
 
 __device__ __forceinline__ int* gather_counters(const ShardK& S) {
   return reinterpret_cast<int*>(S.peer[S.rank] + S.off.tickets) + GATHER_CTR + S.hf * MEMLAYER_MAX_SHARDS;
 }
 
+// One token m of source src: its inbox entries' rows summed (float32), the
+// partial row stored into the token owner's buffer.  Warp-collective.
+template <typename VT, int VEC, int CH>
+__device__ __forceinline__ void gather_token(const ShardK& S, const VT* __restrict__ values, int src, int64_t m,
+                                             int lane, int* err) {
+  const char* mine = S.peer[S.rank];
+  const int d = S.d, groups = d / VEC;
+  const int64_t grp = (int64_t)src * S.mcap + m;
+  const int c = __ldcg(reinterpret_cast<const int*>(mine + S.off.cnt) + grp);
+  if (c <= 0) return;
+  const int2* ent = reinterpret_cast<const int2*>(mine + S.off.inbox) + grp * S.hk;
+  float acc[CH][VEC];
+#pragma unroll
+  for (int a = 0; a < CH; ++a)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) acc[a][v] = 0.f;
+  for (int b0 = 0; b0 < c; b0 += 32) {
+    const int2 e = (b0 + lane < c) ? __ldcg(ent + b0 + lane) : make_int2(0, 0);
+    const int nb = min(32, c - b0);
+#pragma unroll 4
+    for (int j = 0; j < nb; ++j) {
+      const int row = __shfl_sync(FULL, e.x, j);
+      const float wr = __int_as_float(__shfl_sync(FULL, e.y, j));
+      if ((unsigned)row >= (unsigned)S.rows) {   // only a bug upstream can cause this
+        if (lane == 0) atomicCAS(err, 0, 22);
+        continue;
+      }
+      const VT* base = values + (int64_t)row * d;
+#pragma unroll
+      for (int a = 0; a < CH; ++a) {
+        const int g = a * 32 + lane;
+        if (g < groups) {
+          float x[VEC];
+          load_group<VT, VEC>(base + g * VEC, x);
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) acc[a][v] = fmaf(wr, x[v], acc[a][v]);
+        }
+      }
+    }
+  }
+  // the partial goes straight to the token owner's buffer
+  float* dst = reinterpret_cast<float*>(S.peer[src] + S.off.part) + ((int64_t)S.rank * S.mcap + m) * d;
+#pragma unroll
+  for (int a = 0; a < CH; ++a) {
+    const int g = a * 32 + lane;
+    if (g < groups) {
+#pragma unroll
+      for (int v = 0; v < VEC; v += 4)
+        *reinterpret_cast<float4*>(dst + g * VEC + v) =
+            make_float4(acc[a][v], acc[a][v + 1], acc[a][v + 2], acc[a][v + 3]);
+    }
+  }
+}
+
 template <typename VT, int VEC, int CH>
 __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant__ ShardK S,
                                                            const VT* __restrict__ values, int* __restrict__ err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int P = S.world, d = S.d, groups = d / VEC;
+  const int P = S.world;
   const char* mine = S.peer[S.rank];
   const int* flags = reinterpret_cast<const int*>(mine + S.off.flags_in) + S.hf * MEMLAYER_MAX_SHARDS;
   int* ctr = gather_counters(S);
@@ -153,8 +209,34 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant
   __syncthreads();
   const unsigned all = P >= 32 ? FULL : (1u << P) - 1u;
   unsigned done = 0, ready = 0;   // per source (bit srot), warp-uniform; `ready`: acquired by this warp
+  // this rank's own tokens (its scatter ran earlier on this stream): a static
+  // grid-stride pass, one token per warp step, every warp of the grid busy
+  {
+    int ok = 0, lo = 0, hi = 0;
+    if (lane == 0 && ld_acquire_sys(flags + S.rank) - S.epoch >= 0) {
+      const volatile int* meta = reinterpret_cast<const volatile int*>(mine + S.off.meta) +
+                                 (S.hf * MEMLAYER_MAX_SHARDS + S.rank) * 2;
+      ok = 1;
+      lo = meta[0];
+      hi = meta[1];
+    }
+    ok = __shfl_sync(FULL, ok, 0);
+    if (ok) {
+      lo = __shfl_sync(FULL, lo, 0);
+      hi = __shfl_sync(FULL, hi, 0);
+      __syncwarp();
+      const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+      for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; t < hi - lo; t += nw)
+        gather_token<VT, VEC, CH>(S, values, S.rank, lo + t, lane, err);
+      done = 1u;
+      ready = 1u;
+    }
+  }
+  // the other sources: units claimed from per-source counters, whichever
+  // source's inbox is ready first
   long long t_idle = -1;          // lane 0: start of the current wait for any ready source
   unsigned backoff = 64;
+  const int tpu = gather_tpu(P);
   while (done != all) {
     int pick = -1, u0 = 0, lo = 0, hi = 0;
     if (lane == 0) {
@@ -169,7 +251,7 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant
         }
         const volatile int* meta = reinterpret_cast<const volatile int*>(mine + S.off.meta) + slot * 2;
         const int mlo = meta[0], mhi = meta[1];
-        const int c = atomicAdd(ctr + src, GATHER_TPU);
+        const int c = atomicAdd(ctr + src, tpu);
         if (c >= mhi - mlo) {
           done |= 1u << srot;
           continue;
@@ -220,55 +302,8 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const __grid_constant
     hi = __shfl_sync(FULL, hi, 0);
     __syncwarp();   // lane 0's acquire of the flag orders the warp's reads of the inbox
     const int src = (S.rank + pick) % P;
-    const int tend = min(u0 + GATHER_TPU, hi - lo);
-    for (int t = u0; t < tend; ++t) {
-      const int64_t m = lo + t;                  // the source's token
-      const int64_t grp = (int64_t)src * S.mcap + m;
-      const int c = __ldcg(reinterpret_cast<const int*>(mine + S.off.cnt) + grp);
-      if (c <= 0) continue;
-      const int2* ent = reinterpret_cast<const int2*>(mine + S.off.inbox) + grp * S.hk;
-      float acc[CH][VEC];
-#pragma unroll
-      for (int a = 0; a < CH; ++a)
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) acc[a][v] = 0.f;
-      for (int b0 = 0; b0 < c; b0 += 32) {
-        const int2 e = (b0 + lane < c) ? __ldcg(ent + b0 + lane) : make_int2(0, 0);
-        const int nb = min(32, c - b0);
-#pragma unroll 4
-        for (int j = 0; j < nb; ++j) {
-          const int row = __shfl_sync(FULL, e.x, j);
-          const float wr = __int_as_float(__shfl_sync(FULL, e.y, j));
-          if ((unsigned)row >= (unsigned)S.rows) {   // only a bug upstream can cause this
-            if (lane == 0) atomicCAS(err, 0, 22);
-            continue;
-          }
-          const VT* base = values + (int64_t)row * d;
-#pragma unroll
-          for (int a = 0; a < CH; ++a) {
-            const int g = a * 32 + lane;
-            if (g < groups) {
-              float x[VEC];
-              load_group<VT, VEC>(base + g * VEC, x);
-#pragma unroll
-              for (int v = 0; v < VEC; ++v) acc[a][v] = fmaf(wr, x[v], acc[a][v]);
-            }
-          }
-        }
-      }
-      // the partial goes straight to the token owner's buffer
-      float* dst = reinterpret_cast<float*>(S.peer[src] + S.off.part) + ((int64_t)S.rank * S.mcap + m) * d;
-#pragma unroll
-      for (int a = 0; a < CH; ++a) {
-        const int g = a * 32 + lane;
-        if (g < groups) {
-#pragma unroll
-          for (int v = 0; v < VEC; v += 4)
-            *reinterpret_cast<float4*>(dst + g * VEC + v) =
-                make_float4(acc[a][v], acc[a][v + 1], acc[a][v + 2], acc[a][v + 3]);
-        }
-      }
-    }
+    const int tend = min(u0 + tpu, hi - lo);
+    for (int t = u0; t < tend; ++t) gather_token<VT, VEC, CH>(S, values, src, lo + t, lane, err);
   }
   __syncthreads();
   if (threadIdx.x == 0) publish_when_last(S, S.hf * 2 + 1, S.off.flags_part, false, ctr, P);
@@ -559,8 +594,8 @@ cudaError_t gather_launch(const ShardK& S, const VT* values, int* err, cudaStrea
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t units = (int64_t)S.world * ((S.span + GATHER_TPU - 1) / GATHER_TPU);
-  const int64_t ctas = (units + 7) / 8;
+  // enough warps for one own token each (the static pass), at most the resident CTAs
+  const int64_t ctas = (S.span + 7) / 8;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ctas, (int64_t)sms * per_sm));
   shard_gather_kernel<VT, VEC, CHV><<<grid, 256, 0, s>>>(S, values, err);
   count_launch();
