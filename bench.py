@@ -475,10 +475,10 @@ def run_ours(args, W, rank, world):
     with ClockSampler(device.index) as clk:
         for i in range(K):
             flush.zero_()
-            if sharded and not overlapped:
-                step(ev[i], pev[i])     # the phases one after another, events between them
+            if staged:
+                step(ev[i], pev[i])     # the phases and the collectives, events between them
             else:
-                step(ev[i])             # single GPU, or one split call
+                step(ev[i])             # one call per step (single GPU, or the row-sharded call)
         torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -516,15 +516,14 @@ def run_ours(args, W, rank, world):
                   "staged_gather_alone": pstage(lambda i: pev[i][0].elapsed_time(pev[i][1])),
                   "reduce_scatter": pstage(lambda i: pev[i][1].elapsed_time(pev[i][2])),
                   "reduce_out": pstage(lambda i: pev[i][2].elapsed_time(ev[i][5]))}
-    elif not overlapped:
-        stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
-                  "combine_push": stage(3, 4),
-                  "finalize": pstage(lambda i: ev[i][4].elapsed_time(pev[i][0])),
-                  "shard_gather_alone": pstage(lambda i: pev[i][0].elapsed_time(pev[i][1])),
-                  "reduce_out": pstage(lambda i: pev[i][1].elapsed_time(ev[i][5]))}
     else:
+        # row-sharded: one call per timed step (issuing the three phases as
+        # separate calls costs enough host time per step that a rank whose
+        # host falls behind idles its GPU, and every other rank then waits
+        # for it in the exchange); the phases' own times come from a separate
+        # phased pass below, untimed in the step figure
         stages = {"projections": stage(0, 1), "prep": stage(1, 2), "score_topk": stage(2, 3),
-                  "combine_push": stage(3, 4), "exchange_reduce_out": stage(4, 5)}
+                  "combine_scatter": stage(3, 4), "finalize_exchange_reduce_out": stage(4, 5)}
         # the owner-side gather alone: the three phases one after another,
         # untimed in the step figure, for the gather kernel's roofline
         G = min(K, 20)
@@ -540,6 +539,7 @@ def run_ours(args, W, rank, world):
         torch.cuda.synchronize()
         torch.distributed.barrier()
         stages["shard_gather_alone"] = statistics.mean(pev[i][0].elapsed_time(pev[i][1]) for i in range(G))
+        stages["phased_reduce_out"] = statistics.mean(pev[i][1].elapsed_time(gev[i][5]) for i in range(G))
         stages["phased_step"] = statistics.mean(gev[i][0].elapsed_time(gev[i][5]) for i in range(G))
     ms = statistics.mean(step_ms)
 
