@@ -59,7 +59,7 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
             if verbose and out.strip():
                 print(out)
     if jobs or not os.path.exists(LIB):
-        run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-lcublas", "-Xlinker",
+        run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-Xlinker",
              "-rpath=/usr/local/cuda/lib64", "-lrt", "-ldl", "-lpthread"])
     # the XLA FFI handlers of the JAX binding, where JAX is installed
     from model_b200 import jax_ffi

@@ -28,6 +28,14 @@ cudaError_t launch_gemm_act(const float* A, const float* B, const float* bias, f
 // The tensor-core (3xTF32) form: A as tf32 halves [M, K], the weight as
 // tf32 halves of its transpose [N, K].  bias may be NULL; act NONE or GELU.
 bool dense_tc_supported(int64_t M, int K, int N);
+// Column tile of the tensor-core GEMM for N output columns.
+int dense_tc_bn(int N);
+// `slices` independent products in one launch (a split inner dimension):
+// slice s multiplies A rows [s m_pad, +M) by B rows [s n_pad, +N) (K each)
+// into C + s M N, no bias.  m_pad a multiple of 128, n_pad of the column tile.
+cudaError_t launch_dense_tc_sliced(const float* a_hi, const float* a_lo, int64_t M, int64_t m_pad, int K,
+                                   const float* bt_hi, const float* bt_lo, int N, int64_t n_pad, int slices,
+                                   float* C, int* err, cudaStream_t s);
 cudaError_t launch_dense_tc(const float* a_hi, const float* a_lo, int64_t M, int K, const float* bt_hi,
                             const float* bt_lo, int N, const float* bias, float* C, int act, int* err,
                             cudaStream_t s);

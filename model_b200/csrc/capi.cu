@@ -4,6 +4,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include <mutex>
@@ -15,6 +16,7 @@
 #include "layer_bwd.cuh"
 #include "keys.cuh"
 #include "rowgrad.cuh"
+#include "gemm_any.cuh"
 #include "shard.cuh"
 
 namespace ml {
@@ -1310,7 +1312,8 @@ struct BwdPlan {
   RowGradLayout L;
   int64_t F, cap;
   int64_t o_qraw, o_qn, o_qlen, o_keys, o_scal, o_zg, o_dmemg, o_memg, o_dzg, o_dqhat, o_dqlen, o_dT, o_ent_s,
-      o_ent_w, o_rg, o_uniq, o_rows, o_dkhat, o_dq, o_cbal, o_dTrow, o_dqlrow, o_ones, bytes;
+      o_ent_w, o_rg, o_uniq, o_rows, o_dkhat, o_dq, o_cbal, o_dTrow, o_dqlrow, o_ones, o_gemm, bytes;
+  size_t gemm_floats;   // scratch of the tensor-core GEMMs (operand halves, slice partials)
 };
 
 BwdPlan bwd_plan(const Dims& D, bool balance) {
@@ -1347,7 +1350,20 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
   P.o_cbal = balance ? take(4 * HC * M * D.n) : 0;
   P.o_dTrow = balance ? take(4 * HC * M) : 0;
   P.o_dqlrow = balance ? take(4 * M * HC) : 0;
-  P.o_ones = take(4 * M);
+  const int64_t widest = std::max<int64_t>({(int64_t)D.H * D.dk, (int64_t)D.dm, (int64_t)D.d});
+  P.o_ones = take(4 * (int64_t)colsum_scratch_floats(widest));   // column-sum partials of the bias gradients
+  // the largest operand / partial scratch over the backward's GEMMs
+  const int64_t NR = (int64_t)D.H * D.dk, d = D.d, dm = D.dm, n = D.n;
+  const int64_t shapes[][3] = {{M, NR, dm}, {M, d, dm}, {M, d, dm}, {dm, NR, M}, {dm, d, M}, {d, dm, M},
+                               {M, dm, NR}, {M, dm, d}, {M, n, half}, {M, half, n}, {n, half, M}};
+  size_t g = 0;
+  for (const auto& sh : shapes) {
+    if (!balance && (sh[1] == n || sh[2] == n || sh[0] == n) && (sh[1] == half || sh[2] == half)) continue;
+    const size_t f = gemm_any_scratch_floats(sh[0], sh[1], sh[2]);
+    g = f > g ? f : g;
+  }
+  P.gemm_floats = g;
+  P.o_gemm = take(4 * (int64_t)g);
   P.bytes = o;
   return P;
 }
@@ -1410,6 +1426,8 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
   char* ws = (char*)workspace;
   auto F32p = [&](int64_t off) { return reinterpret_cast<float*>(ws + off); };
   int* small = reinterpret_cast<int*>(ws);
+  const GemmScratch GS{F32p(P.o_gemm), P.gemm_floats};   // the GEMMs' operand halves and partials
+  int* gerr = small + 64;                                  // the status word (offset 256)
   if (route) ML_TRY(cudaMemsetAsync(ws, 0, 512, s));
   const int64_t M = D.M, H = D.H, HC = H * 2, half = D.half, n = D.n, d = D.d, dm = D.dm, NR = H * D.dk;
   const ShardK SK = comm ? shard_k(comm, D) : ShardK{};
@@ -1441,12 +1459,12 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     ML_TRY(launch_prep_keys(D, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature, keys_n,
                             nullptr, nullptr, scal, small + 64, small + 65, s));
     ML_TRY(launch_bias_rows(a->b_router, M, NR, F32p(P.o_qraw), s));
-    ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, true, s));
+    ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, true, GS, gerr, s));
     ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, nullptr, nullptr, s));
     ML_TRY(launch_bias_rows(a->b_gate, M, d, F32p(P.o_zg), s));
-    ML_TRY(launch_gemm_strided(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, true, s));
+    ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, true, GS, gerr, s));
     // d (mem * gate) = dy W_out^T (model.py:119)
-    ML_TRY(launch_gemm_strided(g->dy, dm, 1, a->w_out, 1, dm, F32p(P.o_dmemg), d, M, d, dm, false, s));
+    ML_TRY(launch_gemm_any(g->dy, dm, 1, a->w_out, 1, dm, F32p(P.o_dmemg), d, M, d, dm, false, GS, gerr, s));
     if (comm) ML_TRY(launch_shard_probe(SK, M, B.dmemg, B.zg, fwd_mem, probe, B.memg, B.dzg, s));
   }
   if (gather) ML_TRY(launch_shard_dots(D, SK, pa->values, small + 64, s));
@@ -1470,15 +1488,15 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     layout(D, ff, (char*)g->forward_workspace, &FW);
     float* C = F32p(P.o_cbal);
     for (int hc = 0; hc < HC; ++hc)   // cos[hc] = Q_hat[hc] K_hat[hc]^T
-      ML_TRY(launch_gemm_strided(qn + hc * half, HC * half, 1, keys_n + (int64_t)hc * n * half, 1, half,
-                                 C + (int64_t)hc * M * n, n, M, n, half, false, s));
+      ML_TRY(launch_gemm_any(qn + hc * half, HC * half, 1, keys_n + (int64_t)hc * n * half, 1, half,
+                             C + (int64_t)hc * M * n, n, M, n, half, false, GS, gerr, s));
     ML_TRY(launch_bal_rows(D, C, FW.clean_cnt, qlen, scal, g->balance_coef, F32p(P.o_dTrow), F32p(P.o_dqlrow), s));
     for (int hc = 0; hc < HC; ++hc) {
       // d q_hat[hc] += d cos[hc] K_hat[hc];  d k_hat[hc] = d cos[hc]^T Q_hat[hc]
-      ML_TRY(launch_gemm_strided(C + (int64_t)hc * M * n, n, 1, keys_n + (int64_t)hc * n * half, half, 1,
-                                 F32p(P.o_dqhat) + hc * half, HC * half, M, half, n, true, s));
-      ML_TRY(launch_gemm_strided(C + (int64_t)hc * M * n, 1, n, qn + hc * half, HC * half, 1,
-                                 dkhat + (int64_t)hc * n * half, half, n, half, M, false, s));
+      ML_TRY(launch_gemm_any(C + (int64_t)hc * M * n, n, 1, keys_n + (int64_t)hc * n * half, half, 1,
+                             F32p(P.o_dqhat) + hc * half, HC * half, M, half, n, true, GS, gerr, s));
+      ML_TRY(launch_gemm_any(C + (int64_t)hc * M * n, 1, n, qn + hc * half, HC * half, 1,
+                             dkhat + (int64_t)hc * n * half, half, n, half, M, false, GS, gerr, s));
     }
   } else {
     ML_TRY(cudaMemsetAsync(dkhat, 0, sizeof(float) * HC * n * half, s));
@@ -1511,19 +1529,20 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     ML_TRY(launch_dlogt(F32p(P.o_dT), M * H, (balance && D.btgrad) ? F32p(P.o_dTrow) : nullptr,
                         (balance && D.btgrad) ? HC * M : 0, scal, g->dlog_temperature, s));
   // Dense-layer gradients (model.py:110, 118, 119)
-  const float* ones = F32p(P.o_ones);
-  ML_TRY(launch_fill(F32p(P.o_ones), M, 1.f, s));
-  if (g->dw_router) ML_TRY(launch_gemm_strided(a->h, 1, dm, dq, NR, 1, g->dw_router, NR, dm, NR, M, false, s));
-  if (g->db_router) ML_TRY(launch_colsum(dq, M, NR, NR, ones, g->db_router, s));
+  float* cpart = F32p(P.o_ones);   // column-sum partials
+  if (g->dw_router)
+    ML_TRY(launch_gemm_any(a->h, 1, dm, dq, NR, 1, g->dw_router, NR, dm, NR, M, false, GS, gerr, s));
+  if (g->db_router) ML_TRY(launch_colsum_det(dq, M, NR, NR, cpart, g->db_router, s));
   if (g->dw_gate)
-    ML_TRY(launch_gemm_strided(a->h, 1, dm, F32p(P.o_dzg), d, 1, g->dw_gate, d, dm, d, M, false, s));
-  if (g->db_gate) ML_TRY(launch_colsum(F32p(P.o_dzg), M, d, d, ones, g->db_gate, s));
-  if (g->dw_out) ML_TRY(launch_gemm_strided(F32p(P.o_memg), 1, d, g->dy, dm, 1, g->dw_out, dm, d, dm, M, false, s));
-  if (g->db_out) ML_TRY(launch_colsum(g->dy, M, dm, dm, ones, g->db_out, s));
+    ML_TRY(launch_gemm_any(a->h, 1, dm, F32p(P.o_dzg), d, 1, g->dw_gate, d, dm, d, M, false, GS, gerr, s));
+  if (g->db_gate) ML_TRY(launch_colsum_det(F32p(P.o_dzg), M, d, d, cpart, g->db_gate, s));
+  if (g->dw_out)
+    ML_TRY(launch_gemm_any(F32p(P.o_memg), 1, d, g->dy, dm, 1, g->dw_out, dm, d, dm, M, false, GS, gerr, s));
+  if (g->db_out) ML_TRY(launch_colsum_det(g->dy, M, dm, dm, cpart, g->db_out, s));
   if (g->dh) {
-    ML_TRY(launch_gemm_strided(dq, NR, 1, a->w_router, 1, NR, g->dh, dm, M, dm, NR, false, s));
+    ML_TRY(launch_gemm_any(dq, NR, 1, a->w_router, 1, NR, g->dh, dm, M, dm, NR, false, GS, gerr, s));
     if (!g->route_through_pool)
-      ML_TRY(launch_gemm_strided(F32p(P.o_dzg), d, 1, a->w_gate, 1, d, g->dh, dm, M, dm, d, true, s));
+      ML_TRY(launch_gemm_any(F32p(P.o_dzg), d, 1, a->w_gate, 1, d, g->dh, dm, M, dm, d, true, GS, gerr, s));
   }
   return MEMLAYER_OK;
 }

@@ -1,0 +1,252 @@
+// The float32 GEMMs of the layer backward (model.py:110-119 and the balance
+// term of memory.py:205-214 differentiated): C (+)= op(A) op(B) with any
+// row / column strides, on the 5th-generation tensor cores through the
+// 3xTF32 GEMM of gemm_tc.cu.
+//
+//   1. both operands are gathered into K-major tf32 hi / lo halves in the
+//      caller's scratch (32 x 32 tiles through shared memory, so either
+//      stride order reads coalesced), zero-padded to a multiple of the K
+//      stage;
+//   2. a long inner dimension with few output tiles (the weight and sub-key
+//      gradients sum over every token) is cut into S slices that run as
+//      separate GEMM tiles, filling the SMs;
+//   3. the S partial products are added in slice order (deterministic) into
+//      C, on top of C's contents when accumulating.
+// Shapes the tensor-core GEMM does not take (fewer than 128 rows, a column
+// count that is not a multiple of 16) run on a float32 SIMT GEMM with the
+// same strides.
+#include <algorithm>
+
+#include "backbone.cuh"
+#include "gemm_any.cuh"
+#include "tc_common.cuh"
+
+namespace ml {
+
+namespace {
+
+constexpr int KQ = 32;   // K stage of the tensor-core GEMM
+
+// dst[s][r][kk] (rows_pad rows per slice) = tf32 halves of
+// src[r * s_row + k * s_col], k = s * Ks + kk, zero for k >= cols.
+__global__ void __launch_bounds__(256) gather_split_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                                                           int64_t s_row, int64_t s_col, int64_t Ks, int S,
+                                                           int64_t rows_pad, float* __restrict__ hi,
+                                                           float* __restrict__ lo) {
+  __shared__ float t[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, k0 = (int64_t)blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
+  if (s_col == 1) {          // rows contiguous along k: lanes over k
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i, k = k0 + tx;
+      t[i][tx] = (r < rows && k < cols) ? src[r * s_row + k] : 0.f;
+    }
+  } else {                   // columns contiguous along r: lanes over r
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + tx, k = k0 + i;
+      t[tx][i] = (r < rows && k < cols) ? src[r * s_row + k * s_col] : 0.f;
+    }
+  }
+  __syncthreads();
+  const int64_t kp = (int64_t)S * Ks;
+  for (int i = ty; i < 32; i += 8) {
+    const int64_t r = r0 + i, k = k0 + tx;
+    if (r >= rows || k >= kp) continue;
+    const int64_t sl = k / Ks, kk = k - sl * Ks;
+    const float v = t[i][tx];
+    const float h = tc::to_tf32(v);
+    const int64_t at = (sl * rows_pad + r) * Ks + kk;
+    hi[at] = h;
+    lo[at] = tc::to_tf32(v - h);
+  }
+}
+
+// C[i ldc + j] = (acc ? C : 0) + sum_s P[s][i][j], slices in order.
+__global__ void __launch_bounds__(256) sum_slices_kernel(const float* __restrict__ P, int S, int64_t M, int64_t N,
+                                                         float* __restrict__ C, int64_t ldc, int acc) {
+  const int64_t n = M * N;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / N, j = e - i * N;
+    float x = 0.f;
+    for (int s = 0; s < S; ++s) x += P[(int64_t)s * n + e];
+    float* c = C + i * ldc + j;
+    *c = acc ? *c + x : x;
+  }
+}
+
+// SIMT float32 GEMM with strides: 64 x 64 tile, 4 x 4 outputs per thread.
+constexpr int SB = 64, SK = 16;
+__global__ void __launch_bounds__(256) gemm_strided_simt_kernel(const float* __restrict__ A, int64_t sai, int64_t sak,
+                                                                const float* __restrict__ B, int64_t sbk,
+                                                                int64_t sbj, float* __restrict__ C, int64_t ldc,
+                                                                int64_t M, int64_t N, int64_t K, int acc) {
+  __shared__ float As[SK][SB + 4];
+  __shared__ float Bs[SK][SB + 4];
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const int64_t m0 = (int64_t)blockIdx.y * SB, n0 = (int64_t)blockIdx.x * SB;
+  float c[4][4] = {};
+  for (int64_t k0 = 0; k0 < K; k0 += SK) {
+    for (int e = tid; e < SB * SK; e += 256) {
+      const int mi = sak == 1 ? e / SK : e % SB, ki = sak == 1 ? e % SK : e / SB;
+      const int64_t gm = m0 + mi, gk = k0 + ki;
+      As[ki][mi] = (gm < M && gk < K) ? A[gm * sai + gk * sak] : 0.f;
+    }
+    for (int e = tid; e < SB * SK; e += 256) {
+      const int nj = sbj == 1 ? e % SB : e / SK, ki = sbj == 1 ? e / SB : e % SK;
+      const int64_t gn = n0 + nj, gk = k0 + ki;
+      Bs[ki][nj] = (gn < N && gk < K) ? B[gk * sbk + gn * sbj] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < SK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[i][j] = fmaf(a[i], b[j], c[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gm = m0 + ty * 4 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gn = n0 + tx * 4 + j;
+      if (gn >= N) continue;
+      float* cp = C + gm * ldc + gn;
+      *cp = acc ? *cp + c[i][j] : c[i][j];
+    }
+  }
+}
+
+// Column sums out[j] = sum_r X[r ld + j]: partial sums of 64-row... chunks,
+// then the chunks in order (deterministic).
+constexpr int CS_CHUNKS = 64;
+__global__ void __launch_bounds__(256) colsum_part_kernel(const float* __restrict__ X, int64_t rows, int64_t cols,
+                                                          int64_t ld, float* __restrict__ part) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= cols) return;
+  const int64_t per = (rows + CS_CHUNKS - 1) / CS_CHUNKS;
+  const int64_t r0 = blockIdx.y * per, r1 = min(rows, r0 + per);
+  float x = 0.f;
+  for (int64_t r = r0; r < r1; ++r) x += X[r * ld + j];
+  part[(int64_t)blockIdx.y * cols + j] = x;
+}
+
+__global__ void __launch_bounds__(256) colsum_final_kernel(const float* __restrict__ part, int64_t cols,
+                                                           float* __restrict__ out) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= cols) return;
+  float x = 0.f;
+  for (int c = 0; c < CS_CHUNKS; ++c) x += part[(int64_t)c * cols + j];
+  out[j] = x;
+}
+
+struct GemmPlan {
+  bool tc;
+  int S;
+  int64_t Ks, Kp, m_pad, n_pad;
+  size_t a_floats, b_floats, p_floats;
+};
+
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  GemmPlan g{};
+  g.tc = M >= 128 && N >= 16 && N % 16 == 0 && K >= 1 && M < (1ll << 31);
+  if (!g.tc) return g;
+  const int64_t cap = N > 256 ? 256 : 128;               // the tensor-core GEMM's column tile
+  const int64_t bn = N >= cap ? cap : (N + 15) / 16 * 16;
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int64_t kq = (K + KQ - 1) / KQ;                   // K stages
+  int64_t S = 1;
+  while (tiles * S < sms && kq / (S * 2) >= 8) S *= 2;    // slices of at least 8 stages
+  g.S = (int)S;
+  g.Ks = ((kq + S - 1) / S) * KQ;
+  g.Kp = g.Ks * S;
+  g.m_pad = S > 1 ? (M + 127) / 128 * 128 : M;          // slices start on whole tiles
+  g.n_pad = S > 1 ? (N + bn - 1) / bn * bn : N;
+  g.a_floats = 2 * (size_t)g.m_pad * g.Kp;
+  g.b_floats = 2 * (size_t)g.n_pad * g.Kp;
+  g.p_floats = (size_t)S * M * N;
+  return g;
+}
+
+int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+}  // namespace
+
+size_t gemm_any_scratch_floats(int64_t M, int64_t N, int64_t K) {
+  const GemmPlan g = gemm_plan(M, N, K, sm_count());
+  if (!g.tc) return 0;
+  return g.a_floats + g.b_floats + g.p_floats + 3 * 64;   // + alignment slack
+}
+
+cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
+                            float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
+                            const GemmScratch& sc, int* err, cudaStream_t s) {
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (K == 0) {
+    if (accumulate) return cudaSuccess;
+    return cudaErrorInvalidValue;   // the backward never asks for an empty product
+  }
+  const GemmPlan g = gemm_plan(M, N, K, sm_count());
+  if (!g.tc || sc.floats < gemm_any_scratch_floats(M, N, K)) {
+    const dim3 grid((unsigned)((N + SB - 1) / SB), (unsigned)((M + SB - 1) / SB));
+    gemm_strided_simt_kernel<<<grid, 256, 0, s>>>(A, sai, sak, B, sbk, sbj, C, ldc, M, N, K, accumulate ? 1 : 0);
+    count_launch();
+    return cudaGetLastError();
+  }
+  auto align64 = [](size_t x) { return (x + 63) / 64 * 64; };   // 256-byte aligned regions
+  float* a_hi = sc.p;
+  float* a_lo = a_hi + align64(g.a_floats / 2);
+  float* b_hi = a_lo + align64(g.a_floats / 2);
+  float* b_lo = b_hi + align64(g.b_floats / 2);
+  float* part = b_lo + align64(g.b_floats / 2);
+  // A'(i, k) = A[i sai + k sak];  B'(j, k) = B(k, j) = B[k sbk + j sbj]
+  gather_split_kernel<<<dim3((unsigned)((g.Kp + 31) / 32), (unsigned)((M + 31) / 32)), 256, 0, s>>>(
+      A, M, K, sai, sak, g.Ks, g.S, g.m_pad, a_hi, a_lo);
+  count_launch();
+  gather_split_kernel<<<dim3((unsigned)((g.Kp + 31) / 32), (unsigned)((N + 31) / 32)), 256, 0, s>>>(
+      B, N, K, sbj, sbk, g.Ks, g.S, g.n_pad, b_hi, b_lo);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const bool direct = g.S == 1 && ldc == N && !accumulate;
+  if (g.S == 1)
+    e = launch_dense_tc(a_hi, a_lo, M, (int)g.Ks, b_hi, b_lo, (int)N, nullptr, direct ? C : part, ACT_NONE, err, s);
+  else   // every slice's tiles in one launch, one partial product per slice
+    e = launch_dense_tc_sliced(a_hi, a_lo, M, g.m_pad, (int)g.Ks, b_hi, b_lo, (int)N, g.n_pad, g.S, part, err, s);
+  if (e != cudaSuccess) return e;
+  if (direct) return cudaSuccess;
+  const int64_t n = M * N;
+  const int64_t blocks = (n + 255) / 256;
+  sum_slices_kernel<<<(unsigned)std::min<int64_t>(blocks, 148 * 16), 256, 0, s>>>(part, g.S, M, N, C, ldc,
+                                                                                  accumulate ? 1 : 0);
+  count_launch();
+  return cudaGetLastError();
+}
+
+size_t colsum_scratch_floats(int64_t cols) { return (size_t)CS_CHUNKS * cols; }
+
+cudaError_t launch_colsum_det(const float* X, int64_t rows, int64_t cols, int64_t ld, float* part, float* out,
+                              cudaStream_t s) {
+  if (cols == 0) return cudaSuccess;
+  if (rows == 0) return cudaMemsetAsync(out, 0, sizeof(float) * cols, s);
+  colsum_part_kernel<<<dim3((unsigned)((cols + 255) / 256), CS_CHUNKS), 256, 0, s>>>(X, rows, cols, ld, part);
+  count_launch();
+  colsum_final_kernel<<<(unsigned)((cols + 255) / 256), 256, 0, s>>>(part, cols, out);
+  count_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace ml

@@ -43,6 +43,11 @@ struct ProjArgs {
   // BIAS / GELU
   float* out;          // [M][N]
   int bias_smem;       // bias staged in shared memory (N <= BIAS_SMEM_MAX); else read from global
+  // split inner dimension (BIAS epilogue): `slices` independent products,
+  // slice s reading A rows [s m_pad, +M) and B rows [s n_pad, +N) and
+  // writing out + s out_stride
+  int slices = 1;
+  int64_t m_pad = 0, n_pad = 0, out_stride = 0;
 };
 
 constexpr int BIAS_SMEM_MAX = 4096;
@@ -144,12 +149,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // per-epilogue-warp staging tiles after the bias vector
   float* stg = sbias + ((nb_s + 255) / 256) * 256 + (warp >= 2 ? (warp - 2) * STG_FLOATS : 0);
-  const int units = m_tiles * n_tiles;
-  // unit u = (n tile, m tile), m fastest: neighbouring CTAs share the B tile
+  const int per_slice = m_tiles * n_tiles;
+  const int units = per_slice * G.slices;
+  // unit u = (slice, n tile, m tile), m fastest: neighbouring CTAs share the B tile
   auto coords = [&](int u, int& arow, int& brow0, int& nch) {
-    const int nt = u / m_tiles, mt = u - nt * m_tiles;
-    arow = mt * tc::PIPE_M;
-    brow0 = nt * P.BN;
+    const int sl = u / per_slice, v = u - sl * per_slice;
+    const int nt = v / m_tiles, mt = v - nt * m_tiles;
+    arow = (int)(sl * G.m_pad) + mt * tc::PIPE_M;
+    brow0 = (int)(sl * G.n_pad) + nt * P.BN;
     nch = 1;
   };
   const uint32_t tmem_base = tc::pipe_init(ctl, P, EPI_WARPS);
@@ -165,7 +172,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      const int nt = u / m_tiles, mt = u - nt * m_tiles;
+      const int sl = u / per_slice, v = u - sl * per_slice;
+      const int nt = v / m_tiles, mt = v - nt * m_tiles;
+      float* outp = G.out ? G.out + sl * G.out_stride : nullptr;
       const int64_t row0 = (int64_t)mt * tc::PIPE_M + quarter * 32;   // the warp's first row
       const int64_t row = row0 + lane;
       const bool rok = row < G.M;
@@ -189,7 +198,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         // gate columns (silu) or plain bias columns, 32 at a time
         const int ld = EPI == EPI_ROUTER_GATE ? G.N - G.NR : G.N;
-        float* dst0 = EPI == EPI_ROUTER_GATE ? G.gate + row0 * ld + (n0 - G.NR) : G.out + row0 * ld + n0;
+        float* dst0 = EPI == EPI_ROUTER_GATE ? G.gate + row0 * ld + (n0 - G.NR) : outp + row0 * ld + n0;
         float* dst = dst0 + (int64_t)lane * ld;
         const bool vec = (ld & 3) == 0 && (n0 & 3) == 0;
         for (int cc = 0; cc < ncols; cc += 32) {
@@ -253,10 +262,12 @@ cudaError_t launch_proj(const ProjArgs& G, const float* a_hi, const float* a_lo,
   if (P.stages < 2) return cudaErrorInvalidConfiguration;
   CUtensorMap m[4];
   cudaError_t e;
-  if ((e = make_tmap_f32(&m[0], a_hi, G.M, G.K, tc::PIPE_M, BK)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[1], a_lo, G.M, G.K, tc::PIPE_M, BK)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[2], b_hi, G.N, G.K, BN, BK)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[3], b_lo, G.N, G.K, BN, BK)) != cudaSuccess) return e;
+  const uint64_t a_rows = G.slices > 1 ? (uint64_t)(G.slices * G.m_pad) : (uint64_t)G.M;
+  const uint64_t b_rows = G.slices > 1 ? (uint64_t)(G.slices * G.n_pad) : (uint64_t)G.N;
+  if ((e = make_tmap_f32(&m[0], a_hi, a_rows, G.K, tc::PIPE_M, BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[1], a_lo, a_rows, G.K, tc::PIPE_M, BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[2], b_hi, b_rows, G.K, BN, BK)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[3], b_lo, b_rows, G.K, BN, BK)) != cudaSuccess) return e;
   const size_t smem = 2048 + (size_t)P.stages * P.stage_bytes + bias_bytes;
   auto kern = proj_gemm_tc_kernel<EPI>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
@@ -265,7 +276,7 @@ cudaError_t launch_proj(const ProjArgs& G, const float* a_hi, const float* a_lo,
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int m_tiles = (int)((G.M + tc::PIPE_M - 1) / tc::PIPE_M), n_tiles = (G.N + BN - 1) / BN;
-  const int units = m_tiles * n_tiles;
+  const int units = m_tiles * n_tiles * G.slices;
   kern<<<units < sms ? units : sms, THREADS, smem, s>>>(m[0], m[1], m[2], m[3], G, P, m_tiles, n_tiles, err);
   count_launch();
   return cudaGetLastError();
@@ -384,6 +395,25 @@ cudaError_t launch_out_tc(const Dims& D, const Work& W, const float* b_out, floa
 }
 
 // ---- general Dense layers of the backbone -------------------------------------
+
+int dense_tc_bn(int N) { return bn_for(EPI_BIAS, N); }
+
+cudaError_t launch_dense_tc_sliced(const float* a_hi, const float* a_lo, int64_t M, int64_t m_pad, int K,
+                                   const float* bt_hi, const float* bt_lo, int N, int64_t n_pad, int slices,
+                                   float* C, int* err, cudaStream_t s) {
+  ProjArgs G{};
+  G.M = M;
+  G.N = N;
+  G.K = K;
+  G.bias = nullptr;
+  G.out = C;
+  G.bias_smem = 0;
+  G.slices = slices;
+  G.m_pad = m_pad;
+  G.n_pad = n_pad;
+  G.out_stride = M * N;
+  return launch_proj<EPI_BIAS>(G, a_hi, a_lo, bt_hi, bt_lo, err, s);
+}
 
 bool dense_tc_supported(int64_t M, int K, int N) {
   return M >= tc::PIPE_M && K % tc::PIPE_K == 0 && K >= tc::PIPE_K && N % 16 == 0 && N >= 16 &&

@@ -21,15 +21,12 @@
 //   bal_row_kernel     (balance term) per (token, codebook) row the softmax
 //                      of p over all n keys from the recomputed cosines, and
 //                      d p = s (dP - sum dP s) / M turned into d cos;
-//   plain GEMMs        (recomputed projections, Dense-layer gradients, the
-//                      dense balance contractions) through cuBLAS SGEMM in
-//                      float32 (no TF32);
+//   GEMMs              (recomputed projections, Dense-layer gradients, the
+//                      dense balance contractions) on the tensor cores as
+//                      3xTF32 (gemm_any.cu), long sums split over the SMs
+//                      and added back in a fixed order;
 //   norm backward      x * rsqrt(|x|^2 + 1e-6) for the queries and sub-keys.
 // Every sum runs in a fixed order: results are deterministic.
-#include <cublas_v2.h>
-
-#include <mutex>
-
 #include "combine.cuh"
 #include "layer_bwd.cuh"
 #include "shard.cuh"
@@ -45,27 +42,6 @@ __global__ void bias_rows_kernel(const float* __restrict__ bias, int64_t rows, i
   C[e] = bias ? bias[e % cols] : 0.f;
 }
 
-// One cuBLAS handle per device (created on first use, float32 arithmetic
-// only: no TF32 or other reduced-precision modes); calls are serialised
-// because a handle is bound to one stream at a time.
-std::mutex g_blas_mu;
-cublasHandle_t g_blas[64] = {};
-
-cudaError_t blas_handle(cublasHandle_t* out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!g_blas[dev]) {
-    cublasHandle_t h = nullptr;
-    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return cudaErrorInitializationError;
-    if (cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH) != CUBLAS_STATUS_SUCCESS) {
-      cublasDestroy(h);
-      return cudaErrorInitializationError;
-    }
-    g_blas[dev] = h;
-  }
-  *out = g_blas[dev];
-  return cudaSuccess;
-}
 
 __global__ void fill_kernel(float* __restrict__ x, int64_t n, float v) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -407,42 +383,12 @@ cudaError_t route_bwd_ch(const Dims& D, const VT* values, const LayerBwd& B, con
 
 }  // namespace
 
-// Row-major C[M, N] (ld ldc) = A' B' as cuBLAS's column-major C^T = B'^T A'^T:
-// A'(i, k) = A[i sai + k sak] with sak == 1 (row-major, ld sai) or sai == 1
-// (transposed, ld sak); B' likewise with sbj == 1 or sbk == 1.
-cudaError_t launch_gemm_strided(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
-                                float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
-                                cudaStream_t s) {
-  if (M == 0 || N == 0) return cudaSuccess;
-  if (!((sak == 1) || (sai == 1)) || !((sbj == 1) || (sbk == 1))) return cudaErrorInvalidValue;
-  const cublasOperation_t opA = sak == 1 ? CUBLAS_OP_N : CUBLAS_OP_T;
-  const int64_t lda = sak == 1 ? sai : sak;
-  const cublasOperation_t opB = sbj == 1 ? CUBLAS_OP_N : CUBLAS_OP_T;
-  const int64_t ldb = sbj == 1 ? sbk : sbj;
-  const float one = 1.f, beta = accumulate ? 1.f : 0.f;
-  std::lock_guard<std::mutex> lk(g_blas_mu);
-  cublasHandle_t h;
-  cudaError_t e = blas_handle(&h);
-  if (e != cudaSuccess) return e;
-  if (cublasSetStream(h, s) != CUBLAS_STATUS_SUCCESS) return cudaErrorUnknown;
-  const cublasStatus_t st = cublasSgemm(h, opB, opA, (int)N, (int)M, (int)K, &one, B, (int)ldb, A, (int)lda, &beta,
-                                        C, (int)ldc);
-  return st == CUBLAS_STATUS_SUCCESS ? cudaGetLastError() : cudaErrorUnknown;
-}
-
 cudaError_t launch_bias_rows(const float* bias, int64_t rows, int64_t cols, float* C, cudaStream_t s) {
   const int64_t n = rows * cols;
   if (n == 0) return cudaSuccess;
   bias_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(bias, rows, cols, C);
   count_launch();
   return cudaGetLastError();
-}
-
-// out[j] = sum over rows of X[row * ld + j] (bias gradients): ones^T X in cuBLAS.
-cudaError_t launch_colsum(const float* X, int64_t rows, int64_t cols, int64_t ld, const float* ones, float* out,
-                          cudaStream_t s) {
-  if (cols == 0) return cudaSuccess;
-  return launch_gemm_strided(ones, rows, 1, X, ld, 1, out, cols, 1, cols, rows, false, s);
 }
 
 cudaError_t launch_fill(float* x, int64_t n, float v, cudaStream_t s) {

@@ -37,15 +37,7 @@ struct BwdShard {
   long long wait_ns;   // budget of the wait
 };
 
-// C (+)= op(A) op(B) with A(i, k) = A[i sai + k sak], B(k, j) = B[k sbk + j sbj], C[i ldc + j]
-// (cuBLAS SGEMM, float32; one of sai / sak and one of sbk / sbj must be 1).
-cudaError_t launch_gemm_strided(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
-                                float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
-                                cudaStream_t s);
 cudaError_t launch_bias_rows(const float* bias, int64_t rows, int64_t cols, float* C, cudaStream_t s);
-// out[j] = sum over rows of X[row ld + j]; ones: `rows` floats equal to 1.
-cudaError_t launch_colsum(const float* X, int64_t rows, int64_t cols, int64_t ld, const float* ones, float* out,
-                          cudaStream_t s);
 cudaError_t launch_fill(float* x, int64_t n, float v, cudaStream_t s);
 cudaError_t launch_route_bwd(const Dims& D, const void* values, const LayerBwd& B, cudaStream_t s);
 // The routing backward of the row-sharded layer: dw from the owners' dots
