@@ -16,6 +16,7 @@
 #include "layer_bwd.cuh"
 #include "keys.cuh"
 #include "rowgrad.cuh"
+#include "bal_bwd_tc.cuh"
 #include "gemm_any.cuh"
 #include "shard.cuh"
 
@@ -1314,6 +1315,10 @@ struct BwdPlan {
   int64_t o_qraw, o_qn, o_qlen, o_keys, o_scal, o_zg, o_dmemg, o_memg, o_dzg, o_dqhat, o_dqlen, o_dT, o_ent_s,
       o_ent_w, o_rg, o_uniq, o_rows, o_dkhat, o_dq, o_cbal, o_dTrow, o_dqlrow, o_ones, o_gemm, bytes;
   size_t gemm_floats;   // scratch of the tensor-core GEMMs (operand halves, slice partials)
+  // balance term on the tensor cores (bal_bwd_tc.cu): operand halves and scratch
+  bool bal_tc;
+  BalBwdPlan bp;
+  int64_t o_qhi, o_qlo, o_khi, o_klo, o_kthi, o_ktlo, o_qthi, o_qtlo, o_dcthi, o_dctlo, o_bpart;
 };
 
 BwdPlan bwd_plan(const Dims& D, bool balance) {
@@ -1347,7 +1352,25 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
   P.o_rows = take(4 * P.cap * half);
   P.o_dkhat = take(4 * NK * half);
   P.o_dq = take(4 * M * HC * half);
-  P.o_cbal = balance ? take(4 * HC * M * D.n) : 0;
+  P.bal_tc = balance && bal_bwd_tc_supported(D);
+  if (P.bal_tc) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    P.bp = bal_bwd_plan(D, sms);
+    P.o_qhi = take(4 * P.bp.q_floats);
+    P.o_qlo = take(4 * P.bp.q_floats);
+    P.o_khi = take(4 * P.bp.k_floats);
+    P.o_klo = take(4 * P.bp.k_floats);
+    P.o_kthi = take(4 * P.bp.k_floats);
+    P.o_ktlo = take(4 * P.bp.k_floats);
+    P.o_qthi = take(4 * P.bp.qt_floats);
+    P.o_qtlo = take(4 * P.bp.qt_floats);
+    P.o_dcthi = take(4 * P.bp.dct_floats);
+    P.o_dctlo = take(4 * P.bp.dct_floats);
+    P.o_bpart = take(4 * P.bp.part_floats);
+  }
+  P.o_cbal = (balance && !P.bal_tc) ? take(4 * HC * M * D.n) : 0;
   P.o_dTrow = balance ? take(4 * HC * M) : 0;
   P.o_dqlrow = balance ? take(4 * M * HC) : 0;
   const int64_t widest = std::max<int64_t>({(int64_t)D.H * D.dk, (int64_t)D.dm, (int64_t)D.d});
@@ -1358,7 +1381,8 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
                                {M, dm, NR}, {M, dm, d}, {M, n, half}, {M, half, n}, {n, half, M}};
   size_t g = 0;
   for (const auto& sh : shapes) {
-    if (!balance && (sh[1] == n || sh[2] == n || sh[0] == n) && (sh[1] == half || sh[2] == half)) continue;
+    if ((!balance || P.bal_tc) && (sh[1] == n || sh[2] == n || sh[0] == n) && (sh[1] == half || sh[2] == half))
+      continue;
     const size_t f = gemm_any_scratch_floats(sh[0], sh[1], sh[2]);
     g = f > g ? f : g;
   }
@@ -1456,11 +1480,14 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
              reinterpret_cast<int*>(ws + P.o_ent_s), F32p(P.o_ent_w)};
   if (route) {
     // forward activations: unit keys and temperature (memory.py:139-146), q (model.py:110), gate input (:118)
+    // (+ the tf32 halves of the unit keys and queries for the balance term's MMAs)
     ML_TRY(launch_prep_keys(D, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature, keys_n,
-                            nullptr, nullptr, scal, small + 64, small + 65, s));
+                            P.bal_tc ? F32p(P.o_khi) : nullptr, P.bal_tc ? F32p(P.o_klo) : nullptr, scal, small + 64,
+                            small + 65, s));
     ML_TRY(launch_bias_rows(a->b_router, M, NR, F32p(P.o_qraw), s));
     ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, true, GS, gerr, s));
-    ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, nullptr, nullptr, s));
+    ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, P.bal_tc ? F32p(P.o_qhi) : nullptr,
+                                    P.bal_tc ? F32p(P.o_qlo) : nullptr, s));
     ML_TRY(launch_bias_rows(a->b_gate, M, d, F32p(P.o_zg), s));
     ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, true, GS, gerr, s));
     // d (mem * gate) = dy W_out^T (model.py:119)
@@ -1486,12 +1513,21 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     ff.balance = true;
     Work FW;
     layout(D, ff, (char*)g->forward_workspace, &FW);
-    float* C = F32p(P.o_cbal);
-    for (int hc = 0; hc < HC; ++hc)   // cos[hc] = Q_hat[hc] K_hat[hc]^T
+    if (P.bal_tc) {
+      const BalBwdBufs BB{qn, F32p(P.o_qhi), F32p(P.o_qlo), keys_n, F32p(P.o_khi), F32p(P.o_klo),
+                          F32p(P.o_kthi), F32p(P.o_ktlo), F32p(P.o_qthi), F32p(P.o_qtlo), F32p(P.o_dcthi),
+                          F32p(P.o_dctlo), F32p(P.o_bpart), FW.clean_cnt, qlen, scal, F32p(P.o_dqhat), dkhat,
+                          F32p(P.o_dTrow), F32p(P.o_dqlrow), gerr};
+      ML_TRY(launch_bal_bwd_tc(D, P.bp, BB, g->balance_coef, s));
+    }
+    float* C = P.bal_tc ? nullptr : F32p(P.o_cbal);
+    for (int hc = 0; C && hc < HC; ++hc)   // cos[hc] = Q_hat[hc] K_hat[hc]^T
       ML_TRY(launch_gemm_any(qn + hc * half, HC * half, 1, keys_n + (int64_t)hc * n * half, 1, half,
                              C + (int64_t)hc * M * n, n, M, n, half, false, GS, gerr, s));
-    ML_TRY(launch_bal_rows(D, C, FW.clean_cnt, qlen, scal, g->balance_coef, F32p(P.o_dTrow), F32p(P.o_dqlrow), s));
-    for (int hc = 0; hc < HC; ++hc) {
+    if (C)
+      ML_TRY(launch_bal_rows(D, C, FW.clean_cnt, qlen, scal, g->balance_coef, F32p(P.o_dTrow), F32p(P.o_dqlrow),
+                             s));
+    for (int hc = 0; C && hc < HC; ++hc) {
       // d q_hat[hc] += d cos[hc] K_hat[hc];  d k_hat[hc] = d cos[hc]^T Q_hat[hc]
       ML_TRY(launch_gemm_any(C + (int64_t)hc * M * n, n, 1, keys_n + (int64_t)hc * n * half, half, 1,
                              F32p(P.o_dqhat) + hc * half, HC * half, M, half, n, true, GS, gerr, s));

@@ -29,11 +29,15 @@ constexpr int KQ = 32;   // K stage of the tensor-core GEMM
 
 // dst[s][r][kk] (rows_pad rows per slice) = tf32 halves of
 // src[r * s_row + k * s_col], k = s * Ks + kk, zero for k >= cols.
+// blockIdx.z: batch (src + z src_b, hi / lo + z dst_b).
 __global__ void __launch_bounds__(256) gather_split_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
                                                            int64_t s_row, int64_t s_col, int64_t Ks, int S,
                                                            int64_t rows_pad, float* __restrict__ hi,
-                                                           float* __restrict__ lo) {
+                                                           float* __restrict__ lo, int64_t src_b, int64_t dst_b) {
   __shared__ float t[32][33];
+  src += blockIdx.z * src_b;
+  hi += blockIdx.z * dst_b;
+  lo += blockIdx.z * dst_b;
   const int64_t r0 = (int64_t)blockIdx.y * 32, k0 = (int64_t)blockIdx.x * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
   if (s_col == 1) {          // rows contiguous along k: lanes over k
@@ -214,10 +218,10 @@ cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const floa
   float* part = b_lo + align64(g.b_floats / 2);
   // A'(i, k) = A[i sai + k sak];  B'(j, k) = B(k, j) = B[k sbk + j sbj]
   gather_split_kernel<<<dim3((unsigned)((g.Kp + 31) / 32), (unsigned)((M + 31) / 32)), 256, 0, s>>>(
-      A, M, K, sai, sak, g.Ks, g.S, g.m_pad, a_hi, a_lo);
+      A, M, K, sai, sak, g.Ks, g.S, g.m_pad, a_hi, a_lo, 0, 0);
   count_launch();
   gather_split_kernel<<<dim3((unsigned)((g.Kp + 31) / 32), (unsigned)((N + 31) / 32)), 256, 0, s>>>(
-      B, N, K, sbj, sbk, g.Ks, g.S, g.n_pad, b_hi, b_lo);
+      B, N, K, sbj, sbk, g.Ks, g.S, g.n_pad, b_hi, b_lo, 0, 0);
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -231,6 +235,28 @@ cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const floa
   const int64_t n = M * N;
   const int64_t blocks = (n + 255) / 256;
   sum_slices_kernel<<<(unsigned)std::min<int64_t>(blocks, 148 * 16), 256, 0, s>>>(part, g.S, M, N, C, ldc,
+                                                                                  accumulate ? 1 : 0);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_split(const float* src, int64_t rows, int64_t cols, int64_t s_row, int64_t s_col,
+                                int64_t Ks, int S, int64_t rows_pad, float* hi, float* lo, int batch, int64_t src_b,
+                                int64_t dst_b, cudaStream_t s) {
+  if (rows == 0 || batch == 0) return cudaSuccess;
+  const int64_t kp = (int64_t)S * Ks;
+  gather_split_kernel<<<dim3((unsigned)((kp + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)batch), 256, 0,
+                        s>>>(src, rows, cols, s_row, s_col, Ks, S, rows_pad, hi, lo, src_b, dst_b);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sum_slices(const float* P, int S, int64_t M, int64_t N, float* C, int64_t ldc, bool accumulate,
+                              cudaStream_t s) {
+  const int64_t n = M * N;
+  if (n == 0) return cudaSuccess;
+  const int64_t blocks = (n + 255) / 256;
+  sum_slices_kernel<<<(unsigned)std::min<int64_t>(blocks, 148 * 16), 256, 0, s>>>(P, S, M, N, C, ldc,
                                                                                   accumulate ? 1 : 0);
   count_launch();
   return cudaGetLastError();

@@ -19,6 +19,16 @@ cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const floa
                             float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
                             const GemmScratch& sc, int* err, cudaStream_t s);
 
+// dst[s][r][kk] (rows_pad rows per slice) = tf32 hi / lo of src[r s_row + k s_col],
+// k = s Ks + kk (zero for k >= cols); `batch` such copies, src + z src_b -> dst + z dst_b.
+cudaError_t launch_gather_split(const float* src, int64_t rows, int64_t cols, int64_t s_row, int64_t s_col,
+                                int64_t Ks, int S, int64_t rows_pad, float* hi, float* lo, int batch, int64_t src_b,
+                                int64_t dst_b, cudaStream_t s);
+
+// C[i ldc + j] (+)= sum over s < S of P[s][i][j] (P: S blocks of M x N), slices in order.
+cudaError_t launch_sum_slices(const float* P, int S, int64_t M, int64_t N, float* C, int64_t ldc, bool accumulate,
+                              cudaStream_t s);
+
 // out[j] = sum over rows of X[r ld + j], deterministic (part: colsum_scratch_floats(cols)).
 size_t colsum_scratch_floats(int64_t cols);
 cudaError_t launch_colsum_det(const float* X, int64_t rows, int64_t cols, int64_t ld, float* part, float* out,

@@ -411,16 +411,30 @@ __global__ void __launch_bounds__(256) rg_span_kernel(RowGradK R, const int* seg
     acc[4 * c + 3] = x.w;
   }
   const int64_t last = (s1 - 1) / CHUNK;
-  for (int64_t c2 = chunk + 1; c2 <= last; ++c2) {
+  // A hot row's segment covers thousands of chunks: the partials are loaded
+  // SPAN_BATCH at a time (independent loads in flight) and added in chunk
+  // order, so the sum is the same as one chunk at a time.
+  constexpr int SPAN_BATCH = VPL <= 4 ? 16 : 64 / VPL;
+  for (int64_t c2 = chunk + 1; c2 <= last; c2 += SPAN_BATCH) {
+    const int nb = last - c2 + 1 < SPAN_BATCH ? (int)(last - c2 + 1) : SPAN_BATCH;
+    float4 x[SPAN_BATCH][VPL / 4];
 #pragma unroll
-    for (int c = 0; c < VPL / 4; ++c) {
-      const int e = (c * 32 + lane) * 4;
-      if (e < d) {
-        const float4 x = *reinterpret_cast<const float4*>(spill + (c2 * 2) * d + e);
-        acc[4 * c] += x.x;
-        acc[4 * c + 1] += x.y;
-        acc[4 * c + 2] += x.z;
-        acc[4 * c + 3] += x.w;
+    for (int b = 0; b < SPAN_BATCH; ++b)
+#pragma unroll
+      for (int c = 0; c < VPL / 4; ++c) {
+        const int e = (c * 32 + lane) * 4;
+        x[b][c] = (b < nb && e < d) ? *reinterpret_cast<const float4*>(spill + ((c2 + b) * 2) * d + e)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int b = 0; b < SPAN_BATCH; ++b) {
+      if (b >= nb) break;
+#pragma unroll
+      for (int c = 0; c < VPL / 4; ++c) {
+        acc[4 * c] += x[b][c].x;
+        acc[4 * c + 1] += x[b][c].y;
+        acc[4 * c + 2] += x[b][c].z;
+        acc[4 * c + 3] += x[b][c].w;
       }
     }
   }

@@ -84,6 +84,18 @@ def test_backward_cfg0_shapes():
     _check(*_case(512, 4, 256, 256, 16, 256, 512, seed=6), 0.01)
 
 
+@pytest.mark.parametrize("n,H,dk,M,qs,bt,bal", [
+    (128, 1, 64, 2100, True, True, 0.8),      # half 32; 17 token tiles in 9 slices: one padding tile
+    (256, 2, 128, 300, False, False, 0.6),    # half 64; a partial last tile
+    (512, 2, 256, 640, True, False, 1.0),     # half 128: the d q_hat accumulator spans 4 cosine chunks
+])
+def test_backward_balance_on_tensor_cores(n, H, dk, M, qs, bt, bal):
+    # sub-key counts that are multiples of 128 (up to 512) take the fused
+    # cosine -> softmax -> d cos kernel; a strong balance coefficient makes
+    # its share of every gradient visible
+    _check(*_case(n, H, dk, 64, 8, 64, M, seed=7 + n, query_scale=qs, btgrad=bt), bal)
+
+
 def test_backward_no_tokens():
     layer, params, h, dy, _ = _case(32, 2, 32, 32, 8, 48, 100, seed=6)
     y, mem, aux, ctx = layer.apply_train(params, h[:0], check=True)
