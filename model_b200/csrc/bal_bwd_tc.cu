@@ -12,19 +12,21 @@
 //
 // bal_bwd_tc_kernel, one persistent CTA per SM, one work unit per
 // (codebook, 128-token tile):
-//   warp 0   TMA producer: q_hat tile x sub-key chunk operands of the cosine
-//            MMA, then the transposed sub-keys, 32 keys per stage, of the
-//            d q_hat MMA (a two-stage ring);
+//   warp 0   TMA producer: q_hat K stages and the sub-key chunks streamed
+//            against each, then the transposed sub-keys, 32 keys per block,
+//            of the d q_hat MMA (one seven-block ring shared with the
+//            epilogue's d cos blocks);
 //   warp 1   MMA issuer: the 128 x n cosine tile into TMEM columns [0, n),
 //            then d q_hat (128 x half) into columns [0, half) -- issued only
 //            after the epilogue has read those cosine columns;
-//   warps 2-5 epilogue, one TMEM lane (token row) per thread: row max, then
-//            the sums, then per 32-key chunk d cos -> tf32 hi / lo, written
+//   warps 2-9 epilogue, one TMEM lane (token row) per thread, two warps per
+//            lane quarter taking alternate 32-key chunks: row max and sums
+//            (combined across the pair), then per chunk d cos -> tf32 hi / lo, written
 //            (a) into a shared-memory A-operand slot (128-byte swizzle,
 //            K-major) for the d q_hat MMA and (b) transposed to global
 //            memory, 32 consecutive tokens per store, as the A operand of the
-//            d k_hat GEMM; finally d q_hat is added into the caller's
-//            gradient.
+//            d k_hat GEMM; finally the tile's d q_hat is stored (the query
+//            norm backward adds it to the routing share).
 // The d k_hat GEMM is one launch of the sliced 3xTF32 GEMM (gemm_tc.cu) over
 // (token slice, codebook) pairs; the slices are added in order.
 // The [H*2, M, n] cosine / d cos matrices never reach HBM.
@@ -37,19 +39,33 @@ namespace ml {
 
 namespace {
 
-constexpr int BB_EPI_WARPS = 4;
+constexpr int BB_EPI_WARPS = 8;                     // two per TMEM lane quarter
+constexpr int BB_HALF_WARPS = BB_EPI_WARPS / 2;     // the warps of one chunk parity: one per quarter
 constexpr int BB_THREADS = 64 + 32 * BB_EPI_WARPS;
-constexpr int BB_RING = 2;                          // TMA ring stages
-constexpr int BB_ASLOTS = 3;                        // d cos operand slots (>= half / 32 - 1)
 constexpr uint32_t BB_TILE = 128 * 32 * 4;          // 128 rows x 32 tf32, 128-byte rows
-constexpr uint32_t BB_STAGE = 4 * BB_TILE;          // A hi / lo + B hi / lo (B rows <= 128)
-constexpr uint32_t BB_ASLOT = 2 * BB_TILE;          // d cos hi / lo
-constexpr uint32_t BB_SMEM = 2048 + BB_RING * BB_STAGE + BB_ASLOTS * BB_ASLOT;
+constexpr uint32_t BB_BLOCK = 2 * BB_TILE;          // one ring block: a hi / lo pair of tiles
+constexpr int BB_BLOCKS = 6;                        // ring depth (>= 1 + 128-key chunks)
+constexpr uint32_t BB_XCH = 8192;                   // row-statistics exchange of the warp pairs
+constexpr uint32_t BB_SMEM = 2048 + BB_BLOCKS * BB_BLOCK + BB_XCH;
 
+// One ring of 32 KB blocks carries, per work unit and in this order,
+//   for each K stage kc of the cosine MMA: Q(kc) = q_hat hi / lo [128 x 32],
+//     then K(kc, jc) = sub-key hi / lo [128 keys x 32] for every key chunk jc
+//     (Q(kc) stays resident while its key chunks stream past);
+//   for each 32-key chunk c of the d q_hat MMA: KT(c) = transposed sub-keys
+//     hi / lo [half x 32 keys], then D(c) = d cos hi / lo [128 x 32 keys],
+//     which the epilogue writes instead of TMA.
+// Producer, MMA issuer and epilogue walk the same block sequence, so a
+// block's position fixes its slot (pos % BB_BLOCKS) and phase.  full[] is
+// completed by 4 arrivals: the producer's expect_tx arrive plus 3 plain
+// arrives for a TMA block, one per epilogue warp of the chunk's parity for a
+// D block; empty[] by the MMA's commit.
+// The two epilogue warps of a lane quarter (same 32 rows) take the even and
+// the odd 32-key chunks and combine their row statistics through shared
+// memory (pair[] barriers, two arrivals each).
 struct BalCtl {
-  uint64_t full[BB_RING], empty[BB_RING];
-  uint64_t afull[BB_ASLOTS], aempty[BB_ASLOTS];
-  uint64_t sfull, sread, dqfull, tempty;
+  uint64_t full[BB_BLOCKS], empty[BB_BLOCKS];
+  uint64_t sfull, sread, dqfull, tempty, pair[4];
   uint32_t tmem_base;
   int abort;
 };
@@ -64,7 +80,7 @@ struct BalArgs {
   const float* cnt;     // [HC][n] clean top-k counts
   const float* qlen;    // [M][HC]
   const float* scal;    // [1] temperature
-  float* dqhat;         // [M][HC][half], accumulated
+  float* dqbal;         // [M][HC][half] the balance term's d q_hat
   float* dT_row;        // [HC][M]
   float* dql_row;       // [M][HC] or nullptr
   float* dct_hi;        // [S][HC][n][Ks]
@@ -72,8 +88,36 @@ struct BalArgs {
   int* err;
 };
 
+// Bounded rendezvous of the two warps of a lane quarter.
+__device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t& parity, int lane, volatile int* abort, int* err) {
+  __syncwarp();
+  if (lane == 0) tc::mbar_arrive(bar);
+  const bool ok = tc::mbar_wait(bar, parity, abort, err, 19);
+  parity ^= 1;
+  return __all_sync(FULL, ok);
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void ring_at(uint32_t pos, int& s, uint32_t& ph) {
+  s = (int)(pos % BB_BLOCKS);
+  ph = (pos / BB_BLOCKS) & 1;
+}
+
+// 3xTF32 MMAs of one 32-deep K stage: d (+)= A_hi B_hi + A_hi B_lo + A_lo B_hi.
+__device__ __forceinline__ void mma_stage(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
+                                          uint32_t idesc, bool first) {
+#pragma unroll
+  for (int k8 = 0; k8 < 4; ++k8) {
+    const uint32_t off = k8 * 32;
+    const uint64_t dah = tc::sdesc_k_sw128(a_hi + off), dal = tc::sdesc_k_sw128(a_lo + off);
+    const uint64_t dbh = tc::sdesc_k_sw128(b_hi + off), dbl = tc::sdesc_k_sw128(b_lo + off);
+    tc::mma_tf32(d, dah, dbh, idesc, (first && k8 == 0) ? 0u : 1u);
+    tc::mma_tf32(d, dah, dbl, idesc, 1);
+    tc::mma_tf32(d, dal, dbh, idesc, 1);
+  }
 }
 
 __global__ void __launch_bounds__(BB_THREADS, 1)
@@ -85,24 +129,23 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   BalCtl* ctl = reinterpret_cast<BalCtl*>(smem);
   uint8_t* ring = smem + 1024;
-  uint8_t* aslots = ring + BB_RING * BB_STAGE;
+  // [2 parities][128 rows][8]: row statistics at 0-2, temperature / q_len gradient shares at 4-5
+  float* xch = reinterpret_cast<float*>(ring + BB_BLOCKS * BB_BLOCK);
   volatile int* abort = &ctl->abort;
   int* err = A.err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = A.HC * A.m_tiles;
-  const int BN1 = A.n < 128 ? A.n : 128;   // keys per cosine MMA
+  const int nb = A.n / 128;                // 128-key chunks of the cosine MMA
   const int kq = A.half / 32;              // K stages of the cosine MMA
-  const int nch = A.n / 32;                // 32-key chunks
+  const int nch = A.n / 32;                // 32-key chunks of the d q_hat MMA
+  const uint32_t per_unit = (uint32_t)(kq * (1 + nb) + 2 * nch);   // ring blocks per unit
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < BB_RING; ++s) {
-      tc::mbar_init(&ctl->full[s], 1);
+    for (int s = 0; s < BB_BLOCKS; ++s) {
+      tc::mbar_init(&ctl->full[s], BB_HALF_WARPS);
       tc::mbar_init(&ctl->empty[s], 1);
     }
-    for (int s = 0; s < BB_ASLOTS; ++s) {
-      tc::mbar_init(&ctl->afull[s], BB_EPI_WARPS);
-      tc::mbar_init(&ctl->aempty[s], 1);
-    }
+    for (int q = 0; q < 4; ++q) tc::mbar_init(&ctl->pair[q], 2);
     tc::mbar_init(&ctl->sfull, 1);
     tc::mbar_init(&ctl->dqfull, 1);
     tc::mbar_init(&ctl->sread, BB_EPI_WARPS);
@@ -124,112 +167,103 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
       tc::prefetch_tmap(&tK_lo);
       tc::prefetch_tmap(&tKT_hi);
       tc::prefetch_tmap(&tKT_lo);
-      int s = 0;
-      uint32_t ph = 0;
-      auto next = [&]() {
-        if (++s == BB_RING) {
-          s = 0;
-          ph ^= 1;
-        }
+      uint32_t pos = 0;
+      // claim the next block for a TMA load of `bytes`; nullptr on timeout
+      auto claim = [&](uint32_t bytes, uint64_t*& bar) -> uint8_t* {
+        int s;
+        uint32_t ph;
+        ring_at(pos++, s, ph);
+        if (!tc::mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 17)) return nullptr;
+        bar = &ctl->full[s];
+        tc::mbar_expect_tx(bar, bytes);
+        for (int i = 1; i < BB_HALF_WARPS; ++i) tc::mbar_arrive(bar);
+        return ring + (size_t)s * BB_BLOCK;
       };
       const int tiles = (int)((A.M + 127) / 128);
       for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const int hc = u / A.m_tiles, mt = u - hc * A.m_tiles;
         // a padding tile (whole slices of the transposed d cos) reads real rows; its output is masked
         const int qrow = (int)(hc * A.M + (int64_t)(mt < tiles ? mt : 0) * 128);
-        // cosine MMA operands: q_hat rows (codebook-major) and sub-key rows
-        for (int jc = 0; jc < A.n / BN1; ++jc)
-          for (int kc = 0; kc < kq; ++kc) {
-            if (!tc::mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 17)) return;
-            uint8_t* st = ring + (size_t)s * BB_STAGE;
-            tc::mbar_expect_tx(&ctl->full[s], 2 * BB_TILE + 2 * (uint32_t)BN1 * 128);
-            tc::tma_load_2d(st, &tQ_hi, &ctl->full[s], kc * 32, qrow);
-            tc::tma_load_2d(st + BB_TILE, &tQ_lo, &ctl->full[s], kc * 32, qrow);
-            tc::tma_load_2d(st + 2 * BB_TILE, &tK_hi, &ctl->full[s], kc * 32, hc * A.n + jc * BN1);
-            tc::tma_load_2d(st + 2 * BB_TILE + BN1 * 128, &tK_lo, &ctl->full[s], kc * 32, hc * A.n + jc * BN1);
-            next();
+        uint64_t* bar;
+        for (int kc = 0; kc < kq; ++kc) {
+          uint8_t* b = claim(2 * BB_TILE, bar);
+          if (!b) return;
+          tc::tma_load_2d(b, &tQ_hi, bar, kc * 32, qrow);
+          tc::tma_load_2d(b + BB_TILE, &tQ_lo, bar, kc * 32, qrow);
+          for (int jc = 0; jc < nb; ++jc) {
+            if (!(b = claim(2 * BB_TILE, bar))) return;
+            tc::tma_load_2d(b, &tK_hi, bar, kc * 32, hc * A.n + jc * 128);
+            tc::tma_load_2d(b + BB_TILE, &tK_lo, bar, kc * 32, hc * A.n + jc * 128);
           }
-        // d q_hat MMA operand: transposed sub-keys [half rows x 32 keys]
+        }
         for (int c = 0; c < nch; ++c) {
-          if (!tc::mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 17)) return;
-          uint8_t* st = ring + (size_t)s * BB_STAGE;
-          tc::mbar_expect_tx(&ctl->full[s], 2 * (uint32_t)A.half * 128);
-          tc::tma_load_2d(st, &tKT_hi, &ctl->full[s], c * 32, hc * A.half);
-          tc::tma_load_2d(st + A.half * 128, &tKT_lo, &ctl->full[s], c * 32, hc * A.half);
-          next();
+          uint8_t* b = claim(2 * (uint32_t)A.half * 128, bar);
+          if (!b) return;
+          tc::tma_load_2d(b, &tKT_hi, bar, c * 32, hc * A.half);
+          tc::tma_load_2d(b + A.half * 128, &tKT_lo, bar, c * 32, hc * A.half);
+          ++pos;   // D(c): written by the epilogue
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc1 = tc::idesc_tf32(128, BN1), idesc2 = tc::idesc_tf32(128, A.half);
-      int s = 0, cg = 0;
-      uint32_t ph = 0, it = 0;
-      auto next = [&]() {
-        if (++s == BB_RING) {
-          s = 0;
-          ph ^= 1;
-        }
+      const uint32_t idesc1 = tc::idesc_tf32(128, 128), idesc2 = tc::idesc_tf32(128, A.half);
+      uint32_t pos = 0, it = 0;
+      // wait for the next block; its slot in s
+      auto take = [&](int& s) -> bool {
+        uint32_t ph;
+        ring_at(pos++, s, ph);
+        if (!tc::mbar_wait(&ctl->full[s], ph, abort, err, 18)) return false;
+        tc::fence_after_sync();
+        return true;
       };
       for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
         // TMEM free: the epilogue has finished the previous unit
         if (!tc::mbar_wait(&ctl->tempty, (it & 1) ^ 1, abort, err, 18)) return;
         tc::fence_after_sync();
-        for (int jc = 0; jc < A.n / BN1; ++jc) {
-          const uint32_t d = tmem_base + (uint32_t)(jc * BN1);
-          for (int kc = 0; kc < kq; ++kc) {
-            if (!tc::mbar_wait(&ctl->full[s], ph, abort, err, 18)) return;
-            tc::fence_after_sync();
-            const uint32_t a_hi = tc::smem_u32(ring + (size_t)s * BB_STAGE);
-            const uint32_t a_lo = a_hi + BB_TILE, b_hi = a_hi + 2 * BB_TILE, b_lo = b_hi + BN1 * 128;
-#pragma unroll
-            for (int k8 = 0; k8 < 4; ++k8) {
-              const uint32_t off = k8 * 32;
-              const uint64_t dah = tc::sdesc_k_sw128(a_hi + off), dal = tc::sdesc_k_sw128(a_lo + off);
-              const uint64_t dbh = tc::sdesc_k_sw128(b_hi + off), dbl = tc::sdesc_k_sw128(b_lo + off);
-              tc::mma_tf32(d, dah, dbh, idesc1, (kc | k8) != 0);
-              tc::mma_tf32(d, dah, dbl, idesc1, 1);
-              tc::mma_tf32(d, dal, dbh, idesc1, 1);
-            }
-            tc::mma_commit(&ctl->empty[s]);
-            next();
+        for (int kc = 0; kc < kq; ++kc) {
+          int sa, sb;
+          if (!take(sa)) return;
+          const uint32_t a_hi = tc::smem_u32(ring + (size_t)sa * BB_BLOCK), a_lo = a_hi + BB_TILE;
+          for (int jc = 0; jc < nb; ++jc) {
+            if (!take(sb)) return;
+            const uint32_t b_hi = tc::smem_u32(ring + (size_t)sb * BB_BLOCK), b_lo = b_hi + BB_TILE;
+            mma_stage(tmem_base + (uint32_t)(jc * 128), a_hi, a_lo, b_hi, b_lo, idesc1, kc == 0);
+            tc::mma_commit(&ctl->empty[sb]);
           }
+          tc::mma_commit(&ctl->empty[sa]);
         }
         tc::mma_commit(&ctl->sfull);   // cosines complete
-        for (int c = 0; c < nch; ++c, ++cg) {
-          const int slot = cg % BB_ASLOTS;
-          const uint32_t use = (uint32_t)(cg / BB_ASLOTS);
-          if (!tc::mbar_wait(&ctl->afull[slot], use & 1, abort, err, 18)) return;
+        for (int c = 0; c < nch; ++c) {
+          int sk, sd;
+          if (!take(sk) || !take(sd)) return;
           // d q_hat overwrites cosine columns [0, half): the epilogue has read them
           if (c == 0 && !tc::mbar_wait(&ctl->sread, it & 1, abort, err, 18)) return;
-          if (!tc::mbar_wait(&ctl->full[s], ph, abort, err, 18)) return;
           tc::fence_after_sync();
-          const uint32_t a_hi = tc::smem_u32(aslots + (size_t)slot * BB_ASLOT), a_lo = a_hi + BB_TILE;
-          const uint32_t b_hi = tc::smem_u32(ring + (size_t)s * BB_STAGE), b_lo = b_hi + A.half * 128;
-#pragma unroll
-          for (int k8 = 0; k8 < 4; ++k8) {
-            const uint32_t off = k8 * 32;
-            const uint64_t dah = tc::sdesc_k_sw128(a_hi + off), dal = tc::sdesc_k_sw128(a_lo + off);
-            const uint64_t dbh = tc::sdesc_k_sw128(b_hi + off), dbl = tc::sdesc_k_sw128(b_lo + off);
-            tc::mma_tf32(tmem_base, dah, dbh, idesc2, (c | k8) != 0);
-            tc::mma_tf32(tmem_base, dah, dbl, idesc2, 1);
-            tc::mma_tf32(tmem_base, dal, dbh, idesc2, 1);
-          }
-          tc::mma_commit(&ctl->empty[s]);
-          tc::mma_commit(&ctl->aempty[slot]);
-          next();
+          const uint32_t a_hi = tc::smem_u32(ring + (size_t)sd * BB_BLOCK), a_lo = a_hi + BB_TILE;
+          const uint32_t b_hi = tc::smem_u32(ring + (size_t)sk * BB_BLOCK), b_lo = b_hi + A.half * 128;
+          mma_stage(tmem_base, a_hi, a_lo, b_hi, b_lo, idesc2, c == 0);
+          tc::mma_commit(&ctl->empty[sk]);
+          tc::mma_commit(&ctl->empty[sd]);
         }
         tc::mma_commit(&ctl->dqfull);   // d q_hat complete
       }
     }
   } else {
     const int quarter = warp & 3;
+    const int hf = (warp - 2) >> 2;                    // this warp's chunk parity
     const int r = quarter * 32 + lane;                 // TMEM lane = row of the tile
     const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16);
     const float T = A.scal[0];
     const float invM = 1.0f / (float)A.M;
     const int Q = A.half / 32;                         // cosine chunks under the d q_hat accumulator
-    int cg = 0;
+    // the last chunk of this parity below Q (-1: none) -- after reading it the
+    // warp tells the MMA issuer that d q_hat may overwrite those columns
+    const int my_last = (Q - 1 - hf) >= 0 ? Q - 1 - ((Q - 1 - hf) & 1) : -1;
+    uint64_t* pbar = &ctl->pair[quarter];
+    uint32_t pph = 0;
+    float* mine = xch + (hf * 128 + r) * 8;
+    const float* other = xch + ((hf ^ 1) * 128 + r) * 8;
     uint32_t it = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
       const int hc = u / A.m_tiles, mt = u - hc * A.m_tiles;
@@ -238,28 +272,59 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
       const float ql = (A.qscale && owner) ? A.qlen[m * A.HC + hc] : 1.f;
       const float ps = A.btgrad ? T * ql : T;
       const float* cn = A.cnt + (int64_t)hc * A.n;
+      // counts of this warp's first two chunks, loaded while the cosines are computed
+      float cla = __ldg(cn + hf * 32 + lane) * A.dscale;
+      float clb = hf + 2 < nch ? __ldg(cn + (hf + 2) * 32 + lane) * A.dscale : 0.f;
       if (!__all_sync(FULL, tc::mbar_wait(&ctl->sfull, it & 1, abort, err, 19))) break;
       tc::fence_after_sync();
-      // row max, then the sum of exp and the count-weighted sum (memory.py:210-214)
-      float mx = -INFINITY;
-      for (int c0 = 0; c0 < A.n; c0 += 32) {
-        uint32_t v[32];
-        tc::tmem_ld32(taddr + c0, v);
-        tc::tmem_wait_ld();
+      // one pass over this warp's chunks: running max, sum of exp and the
+      // count-weighted sum (memory.py:210-214); each chunk's 32 counts are one
+      // coalesced load (issued a chunk ahead), handed to the lanes by shuffles;
+      // TMEM loads run one chunk ahead.
+      float mx = -INFINITY, sum = 0.f, sdp = 0.f;
+      auto stats = [&](const uint32_t (&v)[32], float cl) {
+        float cmax = -INFINITY;
 #pragma unroll
-        for (int t = 0; t < 32; ++t) mx = fmaxf(mx, __uint_as_float(v[t]) * ps);
-      }
-      float sum = 0.f, sdp = 0.f;
-      for (int c0 = 0; c0 < A.n; c0 += 32) {
-        uint32_t v[32];
-        tc::tmem_ld32(taddr + c0, v);
-        tc::tmem_wait_ld();
+        for (int t = 0; t < 32; ++t) cmax = fmaxf(cmax, __uint_as_float(v[t]) * ps);
+        const float nm = fmaxf(mx, cmax);
+        const float sc = __expf(mx - nm);              // 0 on the first chunk
+        sum *= sc;
+        sdp *= sc;
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const float e = expf(__uint_as_float(v[t]) * ps - mx);
+          const float e = __expf(__uint_as_float(v[t]) * ps - nm);
           sum += e;
-          sdp += e * __ldg(cn + c0 + t) * A.dscale;
+          sdp = fmaf(e, __shfl_sync(FULL, cl, t), sdp);
         }
+        mx = nm;
+      };
+      uint32_t va[32], vb[32];
+      // chunks hf, hf + 2, ...: nch / 2 of them, an even number (nch % 4 == 0)
+      tc::tmem_ld32(taddr + hf * 32, va);
+      for (int c = hf; c < nch; c += 4) {
+        tc::tmem_wait_ld_regs(va);
+        tc::tmem_ld32(taddr + (c + 2) * 32, vb);
+        const float cl0 = cla;
+        cla = c + 4 < nch ? __ldg(cn + (c + 4) * 32 + lane) * A.dscale : 0.f;
+        stats(va, cl0);
+        tc::tmem_wait_ld_regs(vb);
+        if (c + 4 < nch) tc::tmem_ld32(taddr + (c + 4) * 32, va);
+        const float cl1 = clb;
+        clb = c + 6 < nch ? __ldg(cn + (c + 6) * 32 + lane) * A.dscale : 0.f;
+        stats(vb, cl1);
+      }
+      // combine the pair's statistics, the even chunks' first (both warps get the same values)
+      mine[0] = mx;
+      mine[1] = sum;
+      mine[2] = sdp;
+      if (!pair_sync(pbar, pph, lane, abort, err)) break;
+      {
+        const float m0 = hf ? other[0] : mx, s0 = hf ? other[1] : sum, d0 = hf ? other[2] : sdp;
+        const float m1 = hf ? mx : other[0], s1 = hf ? sum : other[1], d1 = hf ? sdp : other[2];
+        mx = fmaxf(m0, m1);
+        const float e0 = __expf(m0 - mx), e1 = __expf(m1 - mx);
+        sum = s0 * e0 + s1 * e1;
+        sdp = d0 * e0 + d1 * e1;
       }
       sdp /= sum;                                      // sum_i dP_i s_i
       const float inv = 1.0f / sum;
@@ -269,17 +334,20 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
       float* gh = A.dct_hi + ((sl * A.HC + hc) * A.n) * (int64_t)A.Ks + kk;
       float* gl = A.dct_lo + ((sl * A.HC + hc) * A.n) * (int64_t)A.Ks + kk;
       float dTr = 0.f, dqr = 0.f;
-      bool ok = true;
-      for (int c = 0; c < nch; ++c, ++cg) {
-        uint32_t v[32];
-        tc::tmem_ld32(taddr + c * 32, v);
-        tc::tmem_wait_ld();
+      const uint32_t dpos0 = it * per_unit + (uint32_t)(kq * (1 + nb)) + 1;   // position of D(0)
+      if (my_last < 0) {   // no chunk of this parity under the accumulator
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ctl->sread);
+      }
+      // chunk c of d cos: into the ring block D(c) and, transposed, to global memory
+      auto dcos = [&](int c, const uint32_t (&v)[32], float cl) -> bool {
         float hi[32], lo[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
           const float cosv = __uint_as_float(v[t]);
-          const float sj = expf(cosv * ps - mx) * inv;
-          const float g = sj * (__ldg(cn + c * 32 + t) * A.dscale - sdp) * invM;   // d p_j
+          const float sj = __expf(cosv * ps - mx) * inv;
+          const float g = sj * (__shfl_sync(FULL, cl, t) - sdp) * invM;   // d p_j
           float dc;
           if (A.btgrad) {
             dTr += g * cosv * ql;
@@ -292,19 +360,17 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
           hi[t] = tc::to_tf32(dc);
           lo[t] = tc::to_tf32(dc - hi[t]);
         }
-        if (c == Q - 1) {   // columns [0, half) read: the d q_hat MMA may overwrite them
+        if (c == my_last) {   // columns [0, half) read: the d q_hat MMA may overwrite them
           tc::fence_before_sync();
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(&ctl->sread);
         }
-        const int slot = cg % BB_ASLOTS;
-        const uint32_t use = (uint32_t)(cg / BB_ASLOTS);
-        if (!__all_sync(FULL, tc::mbar_wait(&ctl->aempty[slot], (use & 1) ^ 1, abort, err, 19))) {
-          ok = false;
-          break;
-        }
-        // K-major 128-byte-swizzled row r of the slot: 16-byte chunk q at (q ^ (r & 7))
-        uint8_t* rowp = aslots + (size_t)slot * BB_ASLOT + r * 128;
+        int s;
+        uint32_t ph;
+        ring_at(dpos0 + 2 * (uint32_t)c, s, ph);
+        if (!__all_sync(FULL, tc::mbar_wait(&ctl->empty[s], ph ^ 1, abort, err, 19))) return false;
+        // K-major 128-byte-swizzled row r of the block: 16-byte chunk q at (q ^ (r & 7))
+        uint8_t* rowp = ring + (size_t)s * BB_BLOCK + r * 128;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const int at = ((q ^ (r & 7)) << 4);
@@ -314,7 +380,7 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&ctl->afull[slot]);
+        if (lane == 0) tc::mbar_arrive(&ctl->full[s]);
         // transposed d cos: key j's row, 32 consecutive tokens per warp store
         const int64_t kb = (int64_t)c * 32 * A.Ks;
 #pragma unroll
@@ -322,30 +388,48 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
           gh[kb + (int64_t)t * A.Ks] = hi[t];
           gl[kb + (int64_t)t * A.Ks] = lo[t];
         }
+        return true;
+      };
+      bool ok = true;
+      cla = __ldg(cn + hf * 32 + lane) * A.dscale;
+      clb = hf + 2 < nch ? __ldg(cn + (hf + 2) * 32 + lane) * A.dscale : 0.f;
+      tc::tmem_ld32(taddr + hf * 32, va);
+      for (int c = hf; ok && c < nch; c += 4) {
+        tc::tmem_wait_ld_regs(va);
+        tc::tmem_ld32(taddr + (c + 2) * 32, vb);
+        const float cl0 = cla;
+        cla = c + 4 < nch ? __ldg(cn + (c + 4) * 32 + lane) * A.dscale : 0.f;
+        ok = dcos(c, va, cl0);
+        tc::tmem_wait_ld_regs(vb);
+        if (ok && c + 4 < nch) tc::tmem_ld32(taddr + (c + 4) * 32, va);
+        const float cl1 = clb;
+        clb = c + 6 < nch ? __ldg(cn + (c + 6) * 32 + lane) * A.dscale : 0.f;
+        ok = ok && dcos(c + 2, vb, cl1);
       }
       if (!ok) break;
+      // the row's temperature / q_len gradient: the pair's two shares, even chunks first
+      mine[4] = dTr;
+      mine[5] = dqr;
+      if (!pair_sync(pbar, pph, lane, abort, err)) break;
+      if (hf == 0 && owner) {
+        A.dT_row[(int64_t)hc * A.M + m] = dTr + other[4];
+        if (A.dql_row) A.dql_row[m * A.HC + hc] = dqr + other[5];
+      }
       if (!__all_sync(FULL, tc::mbar_wait(&ctl->dqfull, it & 1, abort, err, 19))) break;
       tc::fence_after_sync();
-      float* dq = A.dqhat + (m * A.HC + hc) * A.half;
-      for (int c0 = 0; c0 < A.half; c0 += 32) {
+      // this codebook's share of d q_hat, stored (the query norm backward adds
+      // it); the pair takes alternate 32-column pieces
+      float* dq = A.dqbal + (m * A.HC + hc) * A.half;
+      for (int c0 = hf * 32; c0 < A.half; c0 += 64) {
         uint32_t v[32];
         tc::tmem_ld32(taddr + c0, v);
         tc::tmem_wait_ld();
         if (owner) {
 #pragma unroll
-          for (int t = 0; t < 32; t += 4) {
-            float4 x = *reinterpret_cast<float4*>(dq + c0 + t);
-            x.x += __uint_as_float(v[t]);
-            x.y += __uint_as_float(v[t + 1]);
-            x.z += __uint_as_float(v[t + 2]);
-            x.w += __uint_as_float(v[t + 3]);
-            *reinterpret_cast<float4*>(dq + c0 + t) = x;
-          }
+          for (int t = 0; t < 32; t += 4)
+            *reinterpret_cast<float4*>(dq + c0 + t) = make_float4(__uint_as_float(v[t]), __uint_as_float(v[t + 1]),
+                                                                  __uint_as_float(v[t + 2]), __uint_as_float(v[t + 3]));
         }
-      }
-      if (owner) {
-        A.dT_row[(int64_t)hc * A.M + m] = dTr;
-        if (A.dql_row) A.dql_row[m * A.HC + hc] = dqr;
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -401,11 +485,10 @@ cudaError_t launch_bal_bwd_tc(const Dims& D, const BalBwdPlan& P, const BalBwdBu
                                B.qt_hi, B.qt_lo, 1, 0, 0, s)) != cudaSuccess)
     return e;
   CUtensorMap m[6];
-  const int BN1 = n < 128 ? n : 128;
   if ((e = make_tmap_f32(&m[0], B.q_hi, (uint64_t)HC * D.M, half, 128)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[1], B.q_lo, (uint64_t)HC * D.M, half, 128)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[2], B.k_hi, (uint64_t)HC * n, half, BN1)) != cudaSuccess) return e;
-  if ((e = make_tmap_f32(&m[3], B.k_lo, (uint64_t)HC * n, half, BN1)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[2], B.k_hi, (uint64_t)HC * n, half, 128)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32(&m[3], B.k_lo, (uint64_t)HC * n, half, 128)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[4], B.kt_hi, (uint64_t)HC * half, n, half)) != cudaSuccess) return e;
   if ((e = make_tmap_f32(&m[5], B.kt_lo, (uint64_t)HC * half, n, half)) != cudaSuccess) return e;
   BalArgs A{};
@@ -421,7 +504,7 @@ cudaError_t launch_bal_bwd_tc(const Dims& D, const BalBwdPlan& P, const BalBwdBu
   A.cnt = B.cnt;
   A.qlen = B.qlen;
   A.scal = B.scal;
-  A.dqhat = B.dqhat;
+  A.dqbal = B.dqbal;
   A.dT_row = B.dT_row;
   A.dql_row = B.dql_row;
   A.dct_hi = B.dct_hi;

@@ -30,7 +30,7 @@ struct BalBwdBufs {
   const float* cnt;      // [H*2][n] the forward's clean top-k counts
   const float* qlen;     // [M][H*2]
   const float* scal;     // [1] temperature
-  float* dqhat;          // [M][H*2][half] (+= d cos K_hat)
+  float* dqbal;          // [M][H*2][half] (= d cos K_hat)
   float* dkhat;          // [H*2][n][half] (= d cos^T Q_hat)
   float* dT_row;         // [H*2][M]
   float* dql_row;        // [M][H*2] or nullptr

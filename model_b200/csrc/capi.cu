@@ -1318,7 +1318,7 @@ struct BwdPlan {
   // balance term on the tensor cores (bal_bwd_tc.cu): operand halves and scratch
   bool bal_tc;
   BalBwdPlan bp;
-  int64_t o_qhi, o_qlo, o_khi, o_klo, o_kthi, o_ktlo, o_qthi, o_qtlo, o_dcthi, o_dctlo, o_bpart;
+  int64_t o_qhi, o_qlo, o_khi, o_klo, o_kthi, o_ktlo, o_qthi, o_qtlo, o_dcthi, o_dctlo, o_bpart, o_dqbal;
 };
 
 BwdPlan bwd_plan(const Dims& D, bool balance) {
@@ -1369,6 +1369,7 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
     P.o_dcthi = take(4 * P.bp.dct_floats);
     P.o_dctlo = take(4 * P.bp.dct_floats);
     P.o_bpart = take(4 * P.bp.part_floats);
+    P.o_dqbal = take(4 * M * HC * half);
   }
   P.o_cbal = (balance && !P.bal_tc) ? take(4 * HC * M * D.n) : 0;
   P.o_dTrow = balance ? take(4 * HC * M) : 0;
@@ -1516,7 +1517,7 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     if (P.bal_tc) {
       const BalBwdBufs BB{qn, F32p(P.o_qhi), F32p(P.o_qlo), keys_n, F32p(P.o_khi), F32p(P.o_klo),
                           F32p(P.o_kthi), F32p(P.o_ktlo), F32p(P.o_qthi), F32p(P.o_qtlo), F32p(P.o_dcthi),
-                          F32p(P.o_dctlo), F32p(P.o_bpart), FW.clean_cnt, qlen, scal, F32p(P.o_dqhat), dkhat,
+                          F32p(P.o_dctlo), F32p(P.o_bpart), FW.clean_cnt, qlen, scal, F32p(P.o_dqbal), dkhat,
                           F32p(P.o_dTrow), F32p(P.o_dqlrow), gerr};
       ML_TRY(launch_bal_bwd_tc(D, P.bp, BB, g->balance_coef, s));
     }
@@ -1560,7 +1561,8 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
   // d q (memory.py:136-138)
   float* dq = F32p(P.o_dq);
   ML_TRY(launch_norm_bwd(qn, F32p(P.o_dqhat), qlen, M * HC, (int)half, nullptr, D.qscale ? F32p(P.o_dqlen) : nullptr,
-                         (balance && D.btgrad && D.qscale) ? F32p(P.o_dqlrow) : nullptr, dq, s));
+                         (balance && D.btgrad && D.qscale) ? F32p(P.o_dqlrow) : nullptr, dq, s,
+                         P.bal_tc ? F32p(P.o_dqbal) : nullptr));
   if (g->dlog_temperature)
     ML_TRY(launch_dlogt(F32p(P.o_dT), M * H, (balance && D.btgrad) ? F32p(P.o_dTrow) : nullptr,
                         (balance && D.btgrad) ? HC * M : 0, scal, g->dlog_temperature, s));

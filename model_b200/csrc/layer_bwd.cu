@@ -299,12 +299,14 @@ __global__ void __launch_bounds__(256) bal_row_kernel(Dims D, float* __restrict_
 __global__ void __launch_bounds__(256) norm_bwd_kernel(const float* __restrict__ xhat, const float* __restrict__ dxhat,
                                                        const float* __restrict__ rnorm_len, int64_t rows, int half,
                                                        const float* __restrict__ raw, const float* __restrict__ dlen,
-                                                       const float* __restrict__ dlen2, float* __restrict__ dx) {
+                                                       const float* __restrict__ dlen2, float* __restrict__ dx,
+                                                       const float* __restrict__ dxhat2) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const float* xr = xhat + row * half;
   const float* gr = dxhat + row * half;
+  const float* g2 = dxhat2 ? dxhat2 + row * half : nullptr;   // a second share of d x_hat (balance term)
   float r;
   if (raw) {   // sub-keys: r from the raw row
     float ss = 0.f;
@@ -314,11 +316,11 @@ __global__ void __launch_bounds__(256) norm_bwd_kernel(const float* __restrict__
     r = 1.0f / (rnorm_len[row] * sqrtf((float)half));
   }
   float dot = 0.f;
-  for (int i = lane; i < half; i += 32) dot = fmaf(xr[i], gr[i], dot);
+  for (int i = lane; i < half; i += 32) dot = fmaf(xr[i], g2 ? gr[i] + g2[i] : gr[i], dot);
   dot = warp_sum(dot);
   const float dl = (dlen ? dlen[row] : 0.f) + (dlen2 ? dlen2[row] : 0.f);
   for (int i = lane; i < half; i += 32)
-    dx[row * half + i] = r * (gr[i] - dot * xr[i]) + dl * xr[i] / sqrtf((float)half);
+    dx[row * half + i] = r * ((g2 ? gr[i] + g2[i] : gr[i]) - dot * xr[i]) + dl * xr[i] / sqrtf((float)half);
 }
 
 // dkhat[uniq[u]] += rows[u] (distinct ids; padding ids >= N skipped)
@@ -424,9 +426,11 @@ cudaError_t launch_bal_rows(const Dims& D, float* C, const float* cnt, const flo
 }
 
 cudaError_t launch_norm_bwd(const float* xhat, const float* dxhat, const float* len, int64_t rows, int half,
-                            const float* raw, const float* dlen, const float* dlen2, float* dx, cudaStream_t s) {
+                            const float* raw, const float* dlen, const float* dlen2, float* dx, cudaStream_t s,
+                            const float* dxhat2) {
   if (rows == 0) return cudaSuccess;
-  norm_bwd_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(xhat, dxhat, len, rows, half, raw, dlen, dlen2, dx);
+  norm_bwd_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(xhat, dxhat, len, rows, half, raw, dlen, dlen2, dx,
+                                                              dxhat2);
   count_launch();
   return cudaGetLastError();
 }

@@ -46,8 +46,10 @@ cudaError_t launch_route_bwd_sharded(const Dims& D, const LayerBwd& B, const Bwd
 // C: [H * 2][M][n] cosines in, d cos out (balance term)
 cudaError_t launch_bal_rows(const Dims& D, float* C, const float* cnt, const float* qlen, const float* scal, float coef,
                             float* dT_row, float* dql_row, cudaStream_t s);
+// dx from d x_hat (+ dxhat2, a second share of it, when given)
 cudaError_t launch_norm_bwd(const float* xhat, const float* dxhat, const float* len, int64_t rows, int half,
-                            const float* raw, const float* dlen, const float* dlen2, float* dx, cudaStream_t s);
+                            const float* raw, const float* dlen, const float* dlen2, float* dx, cudaStream_t s,
+                            const float* dxhat2 = nullptr);
 cudaError_t launch_scatter_rows(const int* uniq, const float* rows, int64_t cap, int64_t N, int half, float* dst,
                                 cudaStream_t s);
 cudaError_t launch_dlogt(const float* a, int64_t na, const float* b, int64_t nb, const float* scal, float* out,
