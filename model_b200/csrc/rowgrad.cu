@@ -13,10 +13,12 @@
 //      ascending, as jnp.unique returns them);
 //   3. summed per segment by one warp per chunk of 64 sorted fetches: a
 //      segment inside one chunk is written whole, a segment crossing chunk
-//      boundaries leaves one partial per chunk that a second kernel adds in
-//      chunk order -- so a slot fetched by thousands of tokens (Zipf-skewed
-//      routing) is spread over many warps and the result is still
-//      deterministic;
+//      boundaries leaves one partial per chunk; groups of 32 chunks lying
+//      inside one segment are pre-added (one warp per group), and the
+//      segment's first chunk adds its head chunks, the group sums and its
+//      tail chunks in order -- so a slot fetched by hundreds of thousands of
+//      fetches (Zipf-skewed routing) is spread over many warps, its final sum
+//      is a few hundred rows long, and the result is still deterministic;
 //   4. reduced to the squared norm of all row gradients (fixed order,
 //      float64 partials) for the global-norm clip;
 //   5. (Adagrad) one warp per touched row: g = scale * row,
@@ -36,6 +38,7 @@ constexpr int RS_TILE = RS_THREADS * RS_ITEMS;   // 4096 keys per sort block
 constexpr int RS_WARP_ITEMS = RS_TILE / 8;        // 512 keys per warp
 constexpr int SEG_TILE = 1024;                    // flags per scan block
 constexpr int CHUNK = 64;                         // sorted fetches per row warp
+constexpr int SPAN_GROUP = 32;                    // chunks per pre-added group of a long segment
 constexpr int SQ_BLOCKS = 64;
 constexpr int MAX_DIGITS = 1024;                 // radix digits per pass (<= 10 bits)
 constexpr uint32_t DROPPED = 0x80000000u;        // fetch-id flag: out-of-range slot, contributes zero
@@ -384,11 +387,66 @@ __global__ void __launch_bounds__(256) rg_rows_kernel(RowGradK R, const int* seg
   flush<VPL>(R, seg_start, u, i0, i1, acc, chunk, rows, rowsq, spill, lane);
 }
 
+// acc += rows p0, p0 + stride, ... (count of them, d floats each) in order;
+// the loads are issued SB at a time.
+template <int VPL>
+__device__ __forceinline__ void add_run(float (&acc)[VPL], const float* p0, int64_t stride, int64_t count, int d,
+                                        int lane) {
+  constexpr int SB = VPL <= 4 ? 16 : 64 / VPL;
+  for (int64_t i = 0; i < count; i += SB) {
+    const int nb = count - i < SB ? (int)(count - i) : SB;
+    float4 x[SB][VPL / 4];
+#pragma unroll
+    for (int b = 0; b < SB; ++b)
+#pragma unroll
+      for (int c = 0; c < VPL / 4; ++c) {
+        const int e = (c * 32 + lane) * 4;
+        x[b][c] = (b < nb && e < d) ? *reinterpret_cast<const float4*>(p0 + (i + b) * stride + e)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int b = 0; b < SB; ++b) {
+      if (b >= nb) break;
+#pragma unroll
+      for (int c = 0; c < VPL / 4; ++c) {
+        acc[4 * c] += x[b][c].x;
+        acc[4 * c + 1] += x[b][c].y;
+        acc[4 * c + 2] += x[b][c].z;
+        acc[4 * c + 3] += x[b][c].w;
+      }
+    }
+  }
+}
+
+// Group g of SPAN_GROUP chunks lying wholly inside one segment (which began
+// before the group and reaches its end): the sum of its chunks' partials, in
+// chunk order, one warp per group.  A hot row's segment covers thousands of
+// chunks; the span kernel then adds group sums instead of chunk partials.
+template <int VPL>
+__global__ void __launch_bounds__(256) rg_group_kernel(RowGradK R, const int* seg_id, const int* seg_start,
+                                                       const float* spill, float* grp, int64_t groups) {
+  const int lane = threadIdx.x & 31;
+  const int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (g >= groups) return;
+  const int64_t i0 = g * SPAN_GROUP * CHUNK, i1 = i0 + SPAN_GROUP * CHUNK;
+  if (i1 > R.F) return;
+  const int u = seg_id[i0];
+  if (!(seg_start[u] < i0 && seg_start[u + 1] >= i1)) return;
+  float acc[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
+  add_run<VPL>(acc, spill + (g * SPAN_GROUP * 2) * R.d, 2 * R.d, SPAN_GROUP, R.d, lane);
+  store_row<VPL>(acc, grp + g * R.d, R.d, lane);
+}
+
 // One warp per chunk: the chunk where a boundary-crossing segment starts
-// adds the partials of every chunk the segment covers, in chunk order.
+// adds the partials of every chunk the segment covers: its own tail
+// partial, the chunks up to the next group boundary, the group sums of the
+// whole groups inside the segment, then the remaining chunks -- a fixed order.
 template <int VPL>
 __global__ void __launch_bounds__(256) rg_span_kernel(RowGradK R, const int* seg_id, const int* seg_start,
-                                                      float* rows, float* rowsq, const float* spill) {
+                                                      float* rows, float* rowsq, const float* spill,
+                                                      const float* grp) {
   const int lane = threadIdx.x & 31;
   const int64_t chunk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int64_t Fv = R.F;
@@ -401,43 +459,25 @@ __global__ void __launch_bounds__(256) rg_span_kernel(RowGradK R, const int* seg
   float acc[VPL];
   const int d = R.d;
 #pragma unroll
-  for (int c = 0; c < VPL / 4; ++c) {
-    const int e = (c * 32 + lane) * 4;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (e < d) x = *reinterpret_cast<const float4*>(spill + (chunk * 2 + 1) * d + e);
-    acc[4 * c] = x.x;
-    acc[4 * c + 1] = x.y;
-    acc[4 * c + 2] = x.z;
-    acc[4 * c + 3] = x.w;
-  }
+  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
+  add_run<VPL>(acc, spill + (chunk * 2 + 1) * d, 0, 1, d, lane);
   const int64_t last = (s1 - 1) / CHUNK;
-  // A hot row's segment covers thousands of chunks: the partials are loaded
-  // SPAN_BATCH at a time (independent loads in flight) and added in chunk
-  // order, so the sum is the same as one chunk at a time.
-  constexpr int SPAN_BATCH = VPL <= 4 ? 16 : 64 / VPL;
-  for (int64_t c2 = chunk + 1; c2 <= last; c2 += SPAN_BATCH) {
-    const int nb = last - c2 + 1 < SPAN_BATCH ? (int)(last - c2 + 1) : SPAN_BATCH;
-    float4 x[SPAN_BATCH][VPL / 4];
-#pragma unroll
-    for (int b = 0; b < SPAN_BATCH; ++b)
-#pragma unroll
-      for (int c = 0; c < VPL / 4; ++c) {
-        const int e = (c * 32 + lane) * 4;
-        x[b][c] = (b < nb && e < d) ? *reinterpret_cast<const float4*>(spill + ((c2 + b) * 2) * d + e)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-    for (int b = 0; b < SPAN_BATCH; ++b) {
-      if (b >= nb) break;
-#pragma unroll
-      for (int c = 0; c < VPL / 4; ++c) {
-        acc[4 * c] += x[b][c].x;
-        acc[4 * c + 1] += x[b][c].y;
-        acc[4 * c + 2] += x[b][c].z;
-        acc[4 * c + 3] += x[b][c].w;
-      }
+  int64_t c = chunk + 1;
+  // head: up to the next group boundary
+  int64_t hb = (c + SPAN_GROUP - 1) / SPAN_GROUP * SPAN_GROUP;
+  if (hb > last + 1) hb = last + 1;
+  add_run<VPL>(acc, spill + (c * 2) * d, 2 * d, hb - c, d, lane);
+  c = hb;
+  // whole groups inside the segment
+  if (c % SPAN_GROUP == 0) {
+    const int64_t g0 = c / SPAN_GROUP, gend = s1 / ((int64_t)SPAN_GROUP * CHUNK);
+    if (gend > g0) {
+      add_run<VPL>(acc, grp + g0 * d, d, gend - g0, d, lane);
+      c = gend * SPAN_GROUP;
     }
   }
+  // tail
+  if (c <= last) add_run<VPL>(acc, spill + (c * 2) * d, 2 * d, last - c + 1, d, lane);
   store_row<VPL>(acc, rows + (int64_t)u * d, d, lane);
   const float q = row_sq<VPL>(acc);
   if (lane == 0) rowsq[u] = q;
@@ -587,6 +627,8 @@ RowGradLayout rowgrad_layout(int64_t F, int64_t N, int d) {
   L.o_rows = take(4 * L.cap * d);
   L.o_rowsq = take(4 * L.cap);
   L.o_spill = take(4 * L.chunks * 2 * d);
+  L.groups = (L.chunks + SPAN_GROUP - 1) / SPAN_GROUP;
+  L.o_grp = take(4 * L.groups * d);
   L.o_part = take(8 * SQ_BLOCKS);
   L.o_sq = take(8);
   L.bytes = o;
@@ -672,7 +714,14 @@ cudaError_t launch_rowgrad(const RowGradK& R, const RowGradLayout& L, char* ws, 
     const unsigned wblocks = (unsigned)((L.chunks + 7) / 8);
     ML_VPL(vpl_for(R.d), (rg_rows_kernel<VP><<<wblocks, 256, 0, s>>>(R, seg_id, va, seg_start, rows, rowsq,
                                                                       spill)));
-    ML_VPL(vpl_for(R.d), (rg_span_kernel<VP><<<wblocks, 256, 0, s>>>(R, seg_id, seg_start, rows, rowsq, spill)));
+    float* grp = reinterpret_cast<float*>(ws + L.o_grp);
+    if (L.chunks > SPAN_GROUP) {
+      ML_VPL(vpl_for(R.d), (rg_group_kernel<VP><<<(unsigned)((L.groups + 7) / 8), 256, 0, s>>>(R, seg_id, seg_start,
+                                                                                               spill, grp, L.groups)));
+      count_launch();
+    }
+    ML_VPL(vpl_for(R.d), (rg_span_kernel<VP><<<wblocks, 256, 0, s>>>(R, seg_id, seg_start, rows, rowsq, spill,
+                                                                      grp)));
     count_launch(2);
   }
   rg_sqnorm_kernel<<<SQ_BLOCKS, 256, 0, s>>>(rowsq, n_seg, part, ticket, sq_out, sqd);

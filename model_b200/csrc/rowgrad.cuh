@@ -25,9 +25,9 @@ struct RowGradK {
 // Byte offsets of the workspace regions (all 256-byte aligned).
 struct RowGradLayout {
   int passes, rbits;
-  int64_t nblk, nseg_blk, chunks, cap;
+  int64_t nblk, nseg_blk, chunks, groups, cap;
   int64_t o_small, o_err, o_keys_a, o_vals_a, o_keys_b, o_vals_b, o_hist, o_dtot, o_segtot, o_seg_id, o_seg_start, o_uniq,
-      o_rows, o_rowsq, o_spill, o_part, o_sq, bytes;
+      o_rows, o_rowsq, o_spill, o_grp, o_part, o_sq, bytes;
 };
 
 struct RowAdagrad {
