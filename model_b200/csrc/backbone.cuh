@@ -36,8 +36,9 @@ int dense_tc_bn(int N);
 cudaError_t launch_dense_tc_sliced(const float* a_hi, const float* a_lo, int64_t M, int64_t m_pad, int K,
                                    const float* bt_hi, const float* bt_lo, int N, int64_t n_pad, int slices,
                                    float* C, int* err, cudaStream_t s);
+// accumulate: C += A B^T + bias (no activation)
 cudaError_t launch_dense_tc(const float* a_hi, const float* a_lo, int64_t M, int K, const float* bt_hi,
                             const float* bt_lo, int N, const float* bias, float* C, int act, int* err,
-                            cudaStream_t s);
+                            cudaStream_t s, bool accumulate = false);
 
 }  // namespace ml

@@ -1485,12 +1485,11 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     ML_TRY(launch_prep_keys(D, pa->sub_keys, pa->log_temperature, cfg->min_temperature, cfg->max_temperature, keys_n,
                             P.bal_tc ? F32p(P.o_khi) : nullptr, P.bal_tc ? F32p(P.o_klo) : nullptr, scal, small + 64,
                             small + 65, s));
-    ML_TRY(launch_bias_rows(a->b_router, M, NR, F32p(P.o_qraw), s));
-    ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, true, GS, gerr, s));
+    ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_router, NR, 1, F32p(P.o_qraw), NR, M, NR, dm, false, GS, gerr, s,
+                           a->b_router));
     ML_TRY(launch_normalize_queries(D, F32p(P.o_qraw), qn, qlen, P.bal_tc ? F32p(P.o_qhi) : nullptr,
                                     P.bal_tc ? F32p(P.o_qlo) : nullptr, s));
-    ML_TRY(launch_bias_rows(a->b_gate, M, d, F32p(P.o_zg), s));
-    ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, true, GS, gerr, s));
+    ML_TRY(launch_gemm_any(a->h, dm, 1, a->w_gate, d, 1, F32p(P.o_zg), d, M, d, dm, false, GS, gerr, s, a->b_gate));
     // d (mem * gate) = dy W_out^T (model.py:119)
     ML_TRY(launch_gemm_any(g->dy, dm, 1, a->w_out, 1, dm, F32p(P.o_dmemg), d, M, d, dm, false, GS, gerr, s));
     if (comm) ML_TRY(launch_shard_probe(SK, M, B.dmemg, B.zg, fwd_mem, probe, B.memg, B.dzg, s));

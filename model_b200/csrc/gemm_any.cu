@@ -3,6 +3,9 @@
 // row / column strides, on the 5th-generation tensor cores through the
 // 3xTF32 GEMM of gemm_tc.cu.
 //
+//   0. operands whose rows or whose k run contiguously (16-byte aligned,
+//      at least one tile) go to gemm_raw_tc.cu, which loads them as stored
+//      and splits them inside the GEMM; otherwise:
 //   1. both operands are gathered into K-major tf32 hi / lo halves in the
 //      caller's scratch (32 x 32 tiles through shared memory, so either
 //      stride order reads coalesced), zero-padded to a multiple of the K
@@ -65,14 +68,16 @@ __global__ void __launch_bounds__(256) gather_split_kernel(const float* __restri
   }
 }
 
-// C[i ldc + j] = (acc ? C : 0) + sum_s P[s][i][j], slices in order.
+// C[i ldc + j] = (acc ? C : 0) + (bias ? bias[j] : 0) + sum_s P[s][i][j], slices in order.
 __global__ void __launch_bounds__(256) sum_slices_kernel(const float* __restrict__ P, int S, int64_t M, int64_t N,
-                                                         float* __restrict__ C, int64_t ldc, int acc) {
+                                                         float* __restrict__ C, int64_t ldc, int acc,
+                                                         const float* __restrict__ bias) {
   const int64_t n = M * N;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = e / N, j = e - i * N;
     float x = 0.f;
     for (int s = 0; s < S; ++s) x += P[(int64_t)s * n + e];
+    if (bias) x += bias[j];
     float* c = C + i * ldc + j;
     *c = acc ? *c + x : x;
   }
@@ -83,7 +88,8 @@ constexpr int SB = 64, SK = 16;
 __global__ void __launch_bounds__(256) gemm_strided_simt_kernel(const float* __restrict__ A, int64_t sai, int64_t sak,
                                                                 const float* __restrict__ B, int64_t sbk,
                                                                 int64_t sbj, float* __restrict__ C, int64_t ldc,
-                                                                int64_t M, int64_t N, int64_t K, int acc) {
+                                                                int64_t M, int64_t N, int64_t K, int acc,
+                                                                const float* __restrict__ bias) {
   __shared__ float As[SK][SB + 4];
   __shared__ float Bs[SK][SB + 4];
   const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
@@ -124,7 +130,8 @@ __global__ void __launch_bounds__(256) gemm_strided_simt_kernel(const float* __r
       const int64_t gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
       float* cp = C + gm * ldc + gn;
-      *cp = acc ? *cp + c[i][j] : c[i][j];
+      const float v = c[i][j] + (bias ? bias[gn] : 0.f);
+      *cp = acc ? *cp + v : v;
     }
   }
 }
@@ -197,16 +204,33 @@ size_t gemm_any_scratch_floats(int64_t M, int64_t N, int64_t K) {
 
 cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
                             float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
-                            const GemmScratch& sc, int* err, cudaStream_t s) {
+                            const GemmScratch& sc, int* err, cudaStream_t s, const float* bias) {
   if (M == 0 || N == 0) return cudaSuccess;
   if (K == 0) {
-    if (accumulate) return cudaSuccess;
+    if (accumulate && !bias) return cudaSuccess;
     return cudaErrorInvalidValue;   // the backward never asks for an empty product
+  }
+  if (gemm_raw_supported(A, sai, sak, B, sbk, sbj, M, N, K)) {
+    // operands split inside the GEMM (gemm_raw_tc.cu); K slices when few tiles
+    const int sms = sm_count();
+    const int64_t tiles = ((M + 127) / 128) * ((N + gemm_raw_bn(N) - 1) / gemm_raw_bn(N));
+    const int64_t kq = (K + KQ - 1) / KQ;
+    int64_t S = 1;
+    while (tiles * S < sms && kq / (S * 2) >= 8 && (size_t)(S * 2) * M * N <= sc.floats) S *= 2;
+    const int64_t per = (kq + S - 1) / S;
+    S = (kq + per - 1) / per;                                   // every slice non-empty
+    if (S == 1)
+      return launch_gemm_raw(A, sai, sak, B, sbk, sbj, M, N, K, 1, (int)per, C, 0, ldc, bias, accumulate, err, s);
+    cudaError_t e = launch_gemm_raw(A, sai, sak, B, sbk, sbj, M, N, K, (int)S, (int)per, sc.p, M * N, N, nullptr,
+                                    false, err, s);
+    if (e != cudaSuccess) return e;
+    return launch_sum_slices(sc.p, (int)S, M, N, C, ldc, accumulate, s, bias);
   }
   const GemmPlan g = gemm_plan(M, N, K, sm_count());
   if (!g.tc || sc.floats < gemm_any_scratch_floats(M, N, K)) {
     const dim3 grid((unsigned)((N + SB - 1) / SB), (unsigned)((M + SB - 1) / SB));
-    gemm_strided_simt_kernel<<<grid, 256, 0, s>>>(A, sai, sak, B, sbk, sbj, C, ldc, M, N, K, accumulate ? 1 : 0);
+    gemm_strided_simt_kernel<<<grid, 256, 0, s>>>(A, sai, sak, B, sbk, sbj, C, ldc, M, N, K, accumulate ? 1 : 0,
+                                                   bias);
     count_launch();
     return cudaGetLastError();
   }
@@ -225,9 +249,11 @@ cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const floa
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const bool direct = g.S == 1 && ldc == N && !accumulate;
+  // one slice over a dense C: the epilogue adds the bias and accumulates
+  const bool direct = g.S == 1 && ldc == N;
   if (g.S == 1)
-    e = launch_dense_tc(a_hi, a_lo, M, (int)g.Ks, b_hi, b_lo, (int)N, nullptr, direct ? C : part, ACT_NONE, err, s);
+    e = launch_dense_tc(a_hi, a_lo, M, (int)g.Ks, b_hi, b_lo, (int)N, direct ? bias : nullptr, direct ? C : part,
+                        ACT_NONE, err, s, direct && accumulate);
   else   // every slice's tiles in one launch, one partial product per slice
     e = launch_dense_tc_sliced(a_hi, a_lo, M, g.m_pad, (int)g.Ks, b_hi, b_lo, (int)N, g.n_pad, g.S, part, err, s);
   if (e != cudaSuccess) return e;
@@ -235,7 +261,7 @@ cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const floa
   const int64_t n = M * N;
   const int64_t blocks = (n + 255) / 256;
   sum_slices_kernel<<<(unsigned)std::min<int64_t>(blocks, 148 * 16), 256, 0, s>>>(part, g.S, M, N, C, ldc,
-                                                                                  accumulate ? 1 : 0);
+                                                                                  accumulate ? 1 : 0, bias);
   count_launch();
   return cudaGetLastError();
 }
@@ -252,12 +278,12 @@ cudaError_t launch_gather_split(const float* src, int64_t rows, int64_t cols, in
 }
 
 cudaError_t launch_sum_slices(const float* P, int S, int64_t M, int64_t N, float* C, int64_t ldc, bool accumulate,
-                              cudaStream_t s) {
+                              cudaStream_t s, const float* bias) {
   const int64_t n = M * N;
   if (n == 0) return cudaSuccess;
   const int64_t blocks = (n + 255) / 256;
   sum_slices_kernel<<<(unsigned)std::min<int64_t>(blocks, 148 * 16), 256, 0, s>>>(P, S, M, N, C, ldc,
-                                                                                  accumulate ? 1 : 0);
+                                                                                  accumulate ? 1 : 0, bias);
   count_launch();
   return cudaGetLastError();
 }

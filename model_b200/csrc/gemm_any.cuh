@@ -13,11 +13,11 @@ struct GemmScratch {
 // Scratch floats launch_gemm_any needs for these shapes (0: it runs on the SIMT path).
 size_t gemm_any_scratch_floats(int64_t M, int64_t N, int64_t K);
 
-// C[i ldc + j] (+)= sum_k A(i, k) B(k, j), A(i, k) = A[i sai + k sak],
+// C[i ldc + j] (+)= sum_k A(i, k) B(k, j) (+ bias[j]), A(i, k) = A[i sai + k sak],
 // B(k, j) = B[k sbk + j sbj]; any strides.
 cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
                             float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, bool accumulate,
-                            const GemmScratch& sc, int* err, cudaStream_t s);
+                            const GemmScratch& sc, int* err, cudaStream_t s, const float* bias = nullptr);
 
 // dst[s][r][kk] (rows_pad rows per slice) = tf32 hi / lo of src[r s_row + k s_col],
 // k = s Ks + kk (zero for k >= cols); `batch` such copies, src + z src_b -> dst + z dst_b.
@@ -25,9 +25,20 @@ cudaError_t launch_gather_split(const float* src, int64_t rows, int64_t cols, in
                                 int64_t Ks, int S, int64_t rows_pad, float* hi, float* lo, int batch, int64_t src_b,
                                 int64_t dst_b, cudaStream_t s);
 
-// C[i ldc + j] (+)= sum over s < S of P[s][i][j] (P: S blocks of M x N), slices in order.
+// C[i ldc + j] (+)= sum over s < S of P[s][i][j] (P: S blocks of M x N), slices in order (+ bias[j]).
 cudaError_t launch_sum_slices(const float* P, int S, int64_t M, int64_t N, float* C, int64_t ldc, bool accumulate,
-                              cudaStream_t s);
+                              cudaStream_t s, const float* bias = nullptr);
+
+// The GEMM that splits its operands itself (gemm_raw_tc.cu): A(i, k) =
+// A[i sai + k sak], B(k, j) = B[k sbk + j sbj], each with one unit stride.
+// Slice s of S (kq_slice 32-element K stages each) writes
+// out + s out_stride (row pitch ld), + bias and accumulated when asked.
+int gemm_raw_bn(int64_t N);
+bool gemm_raw_supported(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
+                        int64_t M, int64_t N, int64_t K);
+cudaError_t launch_gemm_raw(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
+                            int64_t M, int64_t N, int64_t K, int S, int kq_slice, float* out, int64_t out_stride,
+                            int64_t ld, const float* bias, bool accumulate, int* err, cudaStream_t s);
 
 // out[j] = sum over rows of X[r ld + j], deterministic (part: colsum_scratch_floats(cols)).
 size_t colsum_scratch_floats(int64_t cols);

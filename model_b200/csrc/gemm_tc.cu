@@ -48,6 +48,7 @@ struct ProjArgs {
   // writing out + s out_stride
   int slices = 1;
   int64_t m_pad = 0, n_pad = 0, out_stride = 0;
+  int accumulate = 0;  // BIAS: out += acc + bias (read-modify-write of the output)
 };
 
 constexpr int BIAS_SMEM_MAX = 4096;
@@ -60,9 +61,10 @@ constexpr int STG_FLOATS = 32 * STG_LD;
 // The 32 lanes of a warp each hold 16 consecutive values of their own row
 // (row = row0 + lane).  Written through the staging tile so that every
 // store instruction covers 8 rows x 64 contiguous bytes instead of 32 rows x
-// 16 bytes.  dst0 points at row0's first column; rows >= nrows are skipped.
+// 16 bytes.  dst0 points at row0's first column; rows >= nrows are skipped;
+// with add the destination's values are added (same coalesced pattern).
 __device__ __forceinline__ void store16_rows(float* stg, const float (&v)[16], float* dst0, int64_t stride,
-                                             int64_t nrows, int lane) {
+                                             int64_t nrows, int lane, bool add = false) {
 #pragma unroll
   for (int j = 0; j < 16; j += 4)
     *reinterpret_cast<float4*>(stg + lane * STG_LD + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -70,8 +72,18 @@ __device__ __forceinline__ void store16_rows(float* stg, const float (&v)[16], f
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int r = it * 8 + (lane >> 2), c = (lane & 3) * 4;
-    const float4 x = *reinterpret_cast<const float4*>(stg + r * STG_LD + c);
-    if (r < nrows) *reinterpret_cast<float4*>(dst0 + r * stride + c) = x;
+    float4 x = *reinterpret_cast<const float4*>(stg + r * STG_LD + c);
+    if (r < nrows) {
+      float4* d4 = reinterpret_cast<float4*>(dst0 + r * stride + c);
+      if (add) {
+        const float4 o = *d4;
+        x.x += o.x;
+        x.y += o.y;
+        x.z += o.z;
+        x.w += o.w;
+      }
+      *d4 = x;
+    }
   }
   __syncwarp();
 }
@@ -219,11 +231,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int g = 0; g < 32; g += 16) {
             if (vec && cc + g + 16 <= ncols) {
-              store16_rows(stg, *reinterpret_cast<float(*)[16]>(&v[g]), dst0 + cc + g, ld, G.M - row0, lane);
+              store16_rows(stg, *reinterpret_cast<float(*)[16]>(&v[g]), dst0 + cc + g, ld, G.M - row0, lane,
+                           G.accumulate != 0);
             } else if (rok) {
 #pragma unroll
               for (int t = 0; t < 16; ++t)
-                if (cc + g + t < ncols) dst[cc + g + t] = v[g + t];
+                if (cc + g + t < ncols) dst[cc + g + t] = G.accumulate ? dst[cc + g + t] + v[g + t] : v[g + t];
             }
           }
         }
@@ -422,7 +435,7 @@ bool dense_tc_supported(int64_t M, int K, int N) {
 
 cudaError_t launch_dense_tc(const float* a_hi, const float* a_lo, int64_t M, int K, const float* bt_hi,
                             const float* bt_lo, int N, const float* bias, float* C, int act, int* err,
-                            cudaStream_t s) {
+                            cudaStream_t s, bool accumulate) {
   ProjArgs G{};
   G.M = M;
   G.N = N;
@@ -430,6 +443,8 @@ cudaError_t launch_dense_tc(const float* a_hi, const float* a_lo, int64_t M, int
   G.bias = bias;
   G.out = C;
   G.bias_smem = N <= BIAS_SMEM_MAX;
+  G.accumulate = accumulate ? 1 : 0;
+  if (accumulate && act != ACT_NONE) return cudaErrorInvalidValue;
   if (act == ACT_GELU) return launch_proj<EPI_GELU>(G, a_hi, a_lo, bt_hi, bt_lo, err, s);
   if (act != ACT_NONE) return cudaErrorInvalidValue;
   return launch_proj<EPI_BIAS>(G, a_hi, a_lo, bt_hi, bt_lo, err, s);

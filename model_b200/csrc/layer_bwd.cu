@@ -35,14 +35,6 @@ namespace ml {
 
 namespace {
 
-// C[i, j] = bias[j] (the Dense layers' bias, before the GEMM accumulates).
-__global__ void bias_rows_kernel(const float* __restrict__ bias, int64_t rows, int64_t cols, float* __restrict__ C) {
-  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= rows * cols) return;
-  C[e] = bias ? bias[e % cols] : 0.f;
-}
-
-
 __global__ void fill_kernel(float* __restrict__ x, int64_t n, float v) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e < n) x[e] = v;
@@ -384,14 +376,6 @@ cudaError_t route_bwd_ch(const Dims& D, const VT* values, const LayerBwd& B, con
 }
 
 }  // namespace
-
-cudaError_t launch_bias_rows(const float* bias, int64_t rows, int64_t cols, float* C, cudaStream_t s) {
-  const int64_t n = rows * cols;
-  if (n == 0) return cudaSuccess;
-  bias_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(bias, rows, cols, C);
-  count_launch();
-  return cudaGetLastError();
-}
 
 cudaError_t launch_fill(float* x, int64_t n, float v, cudaStream_t s) {
   if (n == 0) return cudaSuccess;

@@ -37,7 +37,6 @@ struct BwdShard {
   long long wait_ns;   // budget of the wait
 };
 
-cudaError_t launch_bias_rows(const float* bias, int64_t rows, int64_t cols, float* C, cudaStream_t s);
 cudaError_t launch_fill(float* x, int64_t n, float v, cudaStream_t s);
 cudaError_t launch_route_bwd(const Dims& D, const void* values, const LayerBwd& B, cudaStream_t s);
 // The routing backward of the row-sharded layer: dw from the owners' dots
