@@ -966,6 +966,9 @@ def run_cfg4(args, rank=0, world=1):
         x = make_inputs(torch, device, W, "f32", W["seed"])
         x["h"] = clustered_hidden(torch, device, T, W["d_model"], W["seed"] + 1)
         call = LayerCall(torch, L, W, x, device, "f32")
+        # a training forward keeps its read output for the backward (as MemoryLayer.apply_train does)
+        mem_keep = torch.empty(T, W["d_value"], device=device)
+        call.args.mem = mem_keep.data_ptr()
     cnt_slot = torch.empty(N, device=device)
     cnt_sub = torch.empty(H, 2, W["n_sub_keys"], device=device)
     bal = torch.empty(1, device=device)

@@ -465,11 +465,11 @@ int32_t memlayer_layer_backward_workspace_size(const memlayer_config* cfg, int32
 
 /* `args` = the forward's layer arguments (h, Dense kernels and biases,
  * sub_keys, log_temperature, values, its slots / weights outputs, and
- * balance_loss non-NULL when balance_coef != 0).  d_key/2 must be a
- * multiple of 4 and at most 128.  The plain GEMMs run through one cuBLAS
- * handle per device on cuBLAS's default workspace: backward calls (sharded
- * ones included) on one device must not overlap on the GPU, e.g. run them
- * on one stream. */
+ * balance_loss non-NULL when balance_coef != 0); args->mem, when non-NULL,
+ * still holds the forward's read output, which the routing backward then
+ * reads instead of re-gathering it.  d_key/2 must be a multiple of 4 and at
+ * most 128.  Every GEMM runs on this library's tensor-core kernels inside
+ * the caller's workspace: backward calls on one device may overlap. */
 int32_t memlayer_layer_backward(const memlayer_config* cfg, const memlayer_layer_args* args,
                                 const memlayer_layer_grads* grads, void* workspace, size_t workspace_bytes,
                                 void* stream);

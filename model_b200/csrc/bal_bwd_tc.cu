@@ -23,12 +23,13 @@
 //            lane quarter taking alternate 32-key chunks: row max and sums
 //            (combined across the pair), then per chunk d cos -> tf32 hi / lo, written
 //            (a) into a shared-memory A-operand slot (128-byte swizzle,
-//            K-major) for the d q_hat MMA and (b) transposed to global
-//            memory, 32 consecutive tokens per store, as the A operand of the
-//            d k_hat GEMM; finally the tile's d q_hat is stored (the query
-//            norm backward adds it to the routing share).
-// The d k_hat GEMM is one launch of the sliced 3xTF32 GEMM (gemm_tc.cu) over
-// (token slice, codebook) pairs; the slices are added in order.
+//            K-major) for the d q_hat MMA and (b) as float32, transposed, to
+//            global memory, 32 consecutive tokens per store, as the A operand
+//            of the d k_hat GEMM; finally the tile's d q_hat is stored (the
+//            query norm backward adds it to the routing share).
+// The d k_hat GEMM is one launch of the operand-splitting GEMM
+// (gemm_raw_tc.cu), batched over the codebooks, reading the unit queries in
+// place; its K slices are added in order.
 // The [H*2, M, n] cosine / d cos matrices never reach HBM.
 #include "bal_bwd_tc.cuh"
 #include "backbone.cuh"
@@ -73,8 +74,8 @@ struct BalCtl {
 struct BalArgs {
   int64_t M;
   int HC, n, half;
-  int m_tiles;          // tiles per codebook, padded to whole token slices
-  int Ks;               // tokens per slice of the transposed d cos (multiple of 128)
+  int m_tiles;          // 128-token tiles
+  int64_t Mp;           // row pitch of the transposed d cos (m_tiles * 128)
   float dscale;
   int btgrad, qscale;
   const float* cnt;     // [HC][n] clean top-k counts
@@ -83,8 +84,7 @@ struct BalArgs {
   float* dqbal;         // [M][HC][half] the balance term's d q_hat
   float* dT_row;        // [HC][M]
   float* dql_row;       // [M][HC] or nullptr
-  float* dct_hi;        // [S][HC][n][Ks]
-  float* dct_lo;
+  float* dct;           // [HC][n][Mp] d cos, transposed
   int* err;
 };
 
@@ -179,11 +179,9 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
         for (int i = 1; i < BB_HALF_WARPS; ++i) tc::mbar_arrive(bar);
         return ring + (size_t)s * BB_BLOCK;
       };
-      const int tiles = (int)((A.M + 127) / 128);
       for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const int hc = u / A.m_tiles, mt = u - hc * A.m_tiles;
-        // a padding tile (whole slices of the transposed d cos) reads real rows; its output is masked
-        const int qrow = (int)(hc * A.M + (int64_t)(mt < tiles ? mt : 0) * 128);
+        const int qrow = (int)(hc * A.M + (int64_t)mt * 128);
         uint64_t* bar;
         for (int kc = 0; kc < kq; ++kc) {
           uint8_t* b = claim(2 * BB_TILE, bar);
@@ -328,11 +326,8 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
       }
       sdp /= sum;                                      // sum_i dP_i s_i
       const float inv = 1.0f / sum;
-      // the slice of the transposed d cos this tile lands in
-      const int64_t tok0 = (int64_t)mt * 128;
-      const int64_t sl = tok0 / A.Ks, kk = tok0 - sl * A.Ks + r;
-      float* gh = A.dct_hi + ((sl * A.HC + hc) * A.n) * (int64_t)A.Ks + kk;
-      float* gl = A.dct_lo + ((sl * A.HC + hc) * A.n) * (int64_t)A.Ks + kk;
+      // this row's column of the transposed d cos
+      float* gd = A.dct + ((int64_t)hc * A.n) * A.Mp + (int64_t)mt * 128 + r;
       float dTr = 0.f, dqr = 0.f;
       const uint32_t dpos0 = it * per_unit + (uint32_t)(kq * (1 + nb)) + 1;   // position of D(0)
       if (my_last < 0) {   // no chunk of this parity under the accumulator
@@ -357,6 +352,8 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
             dc = g * T;                                // sg(T)
           }
           dc = owner ? dc : 0.f;
+          // transposed d cos: key (c 32 + t)'s row, 32 consecutive tokens per warp store
+          gd[(int64_t)(c * 32 + t) * A.Mp] = dc;
           hi[t] = tc::to_tf32(dc);
           lo[t] = tc::to_tf32(dc - hi[t]);
         }
@@ -381,13 +378,6 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ctl->full[s]);
-        // transposed d cos: key j's row, 32 consecutive tokens per warp store
-        const int64_t kb = (int64_t)c * 32 * A.Ks;
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          gh[kb + (int64_t)t * A.Ks] = hi[t];
-          gl[kb + (int64_t)t * A.Ks] = lo[t];
-        }
         return true;
       };
       bool ok = true;
@@ -447,28 +437,26 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
 }  // namespace
 
 bool bal_bwd_tc_supported(const Dims& D) {
-  return D.n % 128 == 0 && D.n <= 512 && (D.half == 32 || D.half == 64 || D.half == 128) && D.M >= 1 &&
+  return D.n % 128 == 0 && D.n <= 512 && (D.half == 32 || D.half == 64 || D.half == 128) && D.M >= 128 &&
          (int64_t)D.H * 2 * D.M < (1ll << 31);
 }
 
 BalBwdPlan bal_bwd_plan(const Dims& D, int sms) {
   BalBwdPlan P{};
   const int64_t HC = D.H * 2, n = D.n, half = D.half;
-  const int64_t tiles = (D.M + 127) / 128;
-  // token slices of the d k_hat GEMM: enough (slice, codebook, key tile) units to fill the SMs
-  const int64_t per = HC * ((n + 127) / 128);
+  P.m_tiles = (int)((D.M + 127) / 128);
+  P.Mp = (int64_t)P.m_tiles * 128;
+  // K slices of the d k_hat GEMM (K = tokens): enough units to fill the SMs
+  const int64_t tiles = HC * (n / 128), kq = (D.M + 31) / 32;
   int64_t S = 1;
-  while (S < tiles && per * S < 2 * sms && S < 16) S *= 2;
-  const int64_t tps = (tiles + S - 1) / S;            // tiles per slice
-  P.S = (int)((tiles + tps - 1) / tps);
-  P.Ks = (int)(tps * 128);
-  P.m_tiles = P.S * (int)tps;
-  const int64_t Kp = (int64_t)P.S * P.Ks;
+  while (tiles * S < sms && kq / (S * 2) >= 8) S *= 2;
+  const int64_t per = (kq + S - 1) / S;
+  P.S = (int)((kq + per - 1) / per);
+  P.kq_slice = (int)per;
   P.q_floats = HC * D.M * half;
   P.k_floats = HC * n * half;
-  P.qt_floats = HC * half * Kp;
-  P.dct_floats = HC * n * Kp;
-  P.part_floats = (int64_t)P.S * HC * n * half;
+  P.dct_floats = HC * n * P.Mp;
+  P.part_floats = P.S > 1 ? (int64_t)P.S * HC * n * half : 0;
   return P;
 }
 
@@ -479,10 +467,6 @@ cudaError_t launch_bal_bwd_tc(const Dims& D, const BalBwdPlan& P, const BalBwdBu
   // transposed unit sub-keys [hc][half][n] (B operand of the d q_hat MMA)
   if ((e = launch_gather_split(B.keys_n, half, n, 1, half, n, 1, half, B.kt_hi, B.kt_lo, HC, (int64_t)n * half,
                                (int64_t)half * n, s)) != cudaSuccess)
-    return e;
-  // transposed unit queries [slice][hc * half][Ks] (B operand of the d k_hat GEMM)
-  if ((e = launch_gather_split(B.qn, (int64_t)HC * half, D.M, 1, (int64_t)HC * half, P.Ks, P.S, (int64_t)HC * half,
-                               B.qt_hi, B.qt_lo, 1, 0, 0, s)) != cudaSuccess)
     return e;
   CUtensorMap m[6];
   if ((e = make_tmap_f32(&m[0], B.q_hi, (uint64_t)HC * D.M, half, 128)) != cudaSuccess) return e;
@@ -497,7 +481,7 @@ cudaError_t launch_bal_bwd_tc(const Dims& D, const BalBwdPlan& P, const BalBwdBu
   A.n = n;
   A.half = half;
   A.m_tiles = P.m_tiles;
-  A.Ks = P.Ks;
+  A.Mp = P.Mp;
   A.dscale = coef * (float)n / (float)HC / (float)(D.M * D.k);   // dP = coef n / (2H) f, f = cnt / (M k)
   A.btgrad = D.btgrad;
   A.qscale = D.qscale;
@@ -507,8 +491,7 @@ cudaError_t launch_bal_bwd_tc(const Dims& D, const BalBwdPlan& P, const BalBwdBu
   A.dqbal = B.dqbal;
   A.dT_row = B.dT_row;
   A.dql_row = B.dql_row;
-  A.dct_hi = B.dct_hi;
-  A.dct_lo = B.dct_lo;
+  A.dct = B.dct;
   A.err = B.err;
   if ((e = cudaFuncSetAttribute(bal_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BB_SMEM)) !=
       cudaSuccess)
@@ -520,9 +503,15 @@ cudaError_t launch_bal_bwd_tc(const Dims& D, const BalBwdPlan& P, const BalBwdBu
   bal_bwd_tc_kernel<<<units < sms ? units : sms, BB_THREADS, BB_SMEM, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], A);
   count_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  // d k_hat[hc] = sum over slices of d cos[slice, hc]^T Q_hat[slice, hc]
-  if ((e = launch_dense_tc_sliced(B.dct_hi, B.dct_lo, n, n, P.Ks, B.qt_hi, B.qt_lo, half, half, P.S * HC, B.part,
-                                  B.err, s)) != cudaSuccess)
+  // d k_hat[hc] = d cos[hc]^T Q_hat[hc] (K = tokens), one batch per codebook
+  const int64_t ldq = (int64_t)HC * half;
+  if (!gemm_raw_supported(B.dct, P.Mp, 1, B.qn, ldq, 1, n, half, D.M)) return cudaErrorInvalidValue;
+  if (P.S == 1)
+    return launch_gemm_raw(B.dct, P.Mp, 1, B.qn, ldq, 1, n, half, D.M, 1, P.kq_slice, B.dkhat, 0, half, nullptr,
+                           false, B.err, s, HC, (int64_t)HC * n, ldq, (int64_t)n * half);
+  if ((e = launch_gemm_raw(B.dct, P.Mp, 1, B.qn, ldq, 1, n, half, D.M, P.S, P.kq_slice, B.part,
+                           (int64_t)HC * n * half, half, nullptr, false, B.err, s, HC, (int64_t)HC * n, ldq,
+                           (int64_t)n * half)) != cudaSuccess)
     return e;
   return launch_sum_slices(B.part, P.S, (int64_t)HC * n, half, B.dkhat, half, false, s);
 }

@@ -5,12 +5,13 @@
 
 namespace ml {
 
-// Token slices of the transposed d cos and the scratch sizes (floats).
+// Layout of the transposed d cos, the d k_hat GEMM's slices and the scratch sizes (floats).
 struct BalBwdPlan {
-  int S;          // token slices
-  int Ks;         // tokens per slice (a multiple of 128)
-  int m_tiles;    // 128-token tiles per codebook, S * Ks / 128
-  int64_t q_floats, k_floats, qt_floats, dct_floats, part_floats;
+  int m_tiles;    // 128-token tiles
+  int64_t Mp;     // row pitch of the transposed d cos (m_tiles * 128)
+  int S;          // K slices of the d k_hat GEMM
+  int kq_slice;   // 32-token K stages per slice
+  int64_t q_floats, k_floats, dct_floats, part_floats;
 };
 
 struct BalBwdBufs {
@@ -22,11 +23,8 @@ struct BalBwdBufs {
   const float* k_lo;
   float* kt_hi;          // [H*2][half][n] scratch
   float* kt_lo;
-  float* qt_hi;          // [S][H*2*half][Ks] scratch
-  float* qt_lo;
-  float* dct_hi;         // [S][H*2][n][Ks] scratch
-  float* dct_lo;
-  float* part;           // [S][H*2][n][half] scratch
+  float* dct;            // [H*2][n][Mp] scratch: d cos, transposed
+  float* part;           // [S][H*2][n][half] scratch (S > 1)
   const float* cnt;      // [H*2][n] the forward's clean top-k counts
   const float* qlen;     // [M][H*2]
   const float* scal;     // [1] temperature

@@ -1318,7 +1318,7 @@ struct BwdPlan {
   // balance term on the tensor cores (bal_bwd_tc.cu): operand halves and scratch
   bool bal_tc;
   BalBwdPlan bp;
-  int64_t o_qhi, o_qlo, o_khi, o_klo, o_kthi, o_ktlo, o_qthi, o_qtlo, o_dcthi, o_dctlo, o_bpart, o_dqbal;
+  int64_t o_qhi, o_qlo, o_khi, o_klo, o_kthi, o_ktlo, o_dct, o_bpart, o_dqbal;
 };
 
 BwdPlan bwd_plan(const Dims& D, bool balance) {
@@ -1364,10 +1364,7 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
     P.o_klo = take(4 * P.bp.k_floats);
     P.o_kthi = take(4 * P.bp.k_floats);
     P.o_ktlo = take(4 * P.bp.k_floats);
-    P.o_qthi = take(4 * P.bp.qt_floats);
-    P.o_qtlo = take(4 * P.bp.qt_floats);
-    P.o_dcthi = take(4 * P.bp.dct_floats);
-    P.o_dctlo = take(4 * P.bp.dct_floats);
+    P.o_dct = take(4 * P.bp.dct_floats);
     P.o_bpart = take(4 * P.bp.part_floats);
     P.o_dqbal = take(4 * M * HC * half);
   }
@@ -1503,6 +1500,7 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
                      small + 64, comm->wait_ns};
     ML_TRY(launch_route_bwd_sharded(D, B, X, s));
   } else {
+    B.mem_fwd = a->mem;   // the forward's read output when the caller kept it
     ML_TRY(launch_route_bwd(D, pa->values, B, s));
   }
   float* dkhat = F32p(P.o_dkhat);
@@ -1515,8 +1513,8 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
     layout(D, ff, (char*)g->forward_workspace, &FW);
     if (P.bal_tc) {
       const BalBwdBufs BB{qn, F32p(P.o_qhi), F32p(P.o_qlo), keys_n, F32p(P.o_khi), F32p(P.o_klo),
-                          F32p(P.o_kthi), F32p(P.o_ktlo), F32p(P.o_qthi), F32p(P.o_qtlo), F32p(P.o_dcthi),
-                          F32p(P.o_dctlo), F32p(P.o_bpart), FW.clean_cnt, qlen, scal, F32p(P.o_dqbal), dkhat,
+                          F32p(P.o_kthi), F32p(P.o_ktlo), F32p(P.o_dct), F32p(P.o_bpart), FW.clean_cnt, qlen,
+                          scal, F32p(P.o_dqbal), dkhat,
                           F32p(P.o_dTrow), F32p(P.o_dqlrow), gerr};
       ML_TRY(launch_bal_bwd_tc(D, P.bp, BB, g->balance_coef, s));
     }

@@ -136,9 +136,10 @@ __global__ void __launch_bounds__(256) gemm_strided_simt_kernel(const float* __r
   }
 }
 
-// Column sums out[j] = sum_r X[r ld + j]: partial sums of 64-row... chunks,
-// then the chunks in order (deterministic).
-constexpr int CS_CHUNKS = 64;
+// Column sums out[j] = sum_r X[r ld + j]: partial sums of CS_CHUNKS row
+// chunks (enough blocks to cover the SMs several times), then the chunks in
+// order (deterministic).
+constexpr int CS_CHUNKS = 256;
 __global__ void __launch_bounds__(256) colsum_part_kernel(const float* __restrict__ X, int64_t rows, int64_t cols,
                                                           int64_t ld, float* __restrict__ part) {
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

@@ -33,12 +33,17 @@ cudaError_t launch_sum_slices(const float* P, int S, int64_t M, int64_t N, float
 // A[i sai + k sak], B(k, j) = B[k sbk + j sbj], each with one unit stride.
 // Slice s of S (kq_slice 32-element K stages each) writes
 // out + s out_stride (row pitch ld), + bias and accumulated when asked.
+// batch > 1: `batch` products, product b on A rows [b M, +M) and B rows
+// [b N, +N) (the "row" index i of A, j of B), writing C + b c_boff; M a
+// multiple of 128 and N of the column tile.  a_rows / b_rows: the operands'
+// total rows (0: batch M / batch N).
 int gemm_raw_bn(int64_t N);
 bool gemm_raw_supported(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
                         int64_t M, int64_t N, int64_t K);
 cudaError_t launch_gemm_raw(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
                             int64_t M, int64_t N, int64_t K, int S, int kq_slice, float* out, int64_t out_stride,
-                            int64_t ld, const float* bias, bool accumulate, int* err, cudaStream_t s);
+                            int64_t ld, const float* bias, bool accumulate, int* err, cudaStream_t s, int batch = 1,
+                            int64_t a_rows = 0, int64_t b_rows = 0, int64_t c_boff = 0);
 
 // out[j] = sum over rows of X[r ld + j], deterministic (part: colsum_scratch_floats(cols)).
 size_t colsum_scratch_floats(int64_t cols);

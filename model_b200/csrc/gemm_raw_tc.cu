@@ -44,8 +44,11 @@ struct GrCtl {
 };
 
 struct GrArgs {
-  int64_t M, N, K;
+  int64_t M, N, K;      // per batch
   int BN;
+  int batch;            // independent products: A rows + b a_boff, B rows + b b_boff, C + b c_boff
+  int a_boff, b_boff;
+  int64_t c_boff;
   int a_kmajor, b_kmajor;   // operand loaded K-major (swizzled) or row-contiguous
   int m_tiles, n_tiles, S, kq_slice;   // kq_slice: 32-element K stages per slice
   float* out;               // slice s writes out + s out_stride (ld) ...
@@ -107,7 +110,8 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
   volatile int* abort = &ctl->abort;
   int* err = G.err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per_slice = G.m_tiles * G.n_tiles;
+  const int per_batch = G.m_tiles * G.n_tiles;
+  const int per_slice = per_batch * G.batch;
   const int units = per_slice * G.S;
   const uint32_t bbytes = (uint32_t)G.BN * 128;
 
@@ -133,10 +137,12 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem_base = ctl->tmem_base;
 
-  // unit u = (slice, column tile, row tile), row tile fastest
-  auto unit = [&](int u, int& sl, int& nt, int& mt) {
+  // unit u = (slice, batch, column tile, row tile), row tile fastest
+  auto unit = [&](int u, int& sl, int& b, int& nt, int& mt) {
     sl = u / per_slice;
-    const int v = u - sl * per_slice;
+    int v = u - sl * per_slice;
+    b = v / per_batch;
+    v -= b * per_batch;
     nt = v / G.m_tiles;
     mt = v - nt * G.m_tiles;
   };
@@ -153,22 +159,23 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        int sl, nt, mt;
-        unit(u, sl, nt, mt);
+        int sl, b, nt, mt;
+        unit(u, sl, b, nt, mt);
         const int nk = stages_of(sl);
+        const int ar = b * G.a_boff + mt * 128, br = b * G.b_boff + nt * G.BN;
         for (int kc = 0; kc < nk; ++kc) {
           const int k = (sl * G.kq_slice + kc) * 32;
           if (!tc::mbar_wait(&ctl->raw_empty[s], ph ^ 1, abort, err, 11)) return;
           uint8_t* st = raw + (size_t)s * 2 * GR_TILE;
           tc::mbar_expect_tx(&ctl->raw_full[s], GR_TILE + bbytes);
           if (G.a_kmajor)
-            tc::tma_load_2d(st, &tA, &ctl->raw_full[s], k, mt * 128);
+            tc::tma_load_2d(st, &tA, &ctl->raw_full[s], k, ar);
           else
-            tc::tma_load_2d(st, &tA, &ctl->raw_full[s], mt * 128, k);
+            tc::tma_load_2d(st, &tA, &ctl->raw_full[s], ar, k);
           if (G.b_kmajor)
-            tc::tma_load_2d(st + GR_TILE, &tB, &ctl->raw_full[s], k, nt * G.BN);
+            tc::tma_load_2d(st + GR_TILE, &tB, &ctl->raw_full[s], k, br);
           else
-            tc::tma_load_2d(st + GR_TILE, &tB, &ctl->raw_full[s], nt * G.BN, k);
+            tc::tma_load_2d(st + GR_TILE, &tB, &ctl->raw_full[s], br, k);
           if (++s == GR_RAW) {
             s = 0;
             ph ^= 1;
@@ -182,8 +189,8 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
       int s = 0, acc = 0;
       uint32_t ph = 0, aph = 0;
       for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        int sl, nt, mt;
-        unit(u, sl, nt, mt);
+        int sl, b, nt, mt;
+        unit(u, sl, b, nt, mt);
         const int nk = stages_of(sl);
         if (!tc::mbar_wait(&ctl->tempty[acc], aph ^ 1, abort, err, 12)) return;
         tc::fence_after_sync();
@@ -218,8 +225,8 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
     int rs = 0, ms = 0;
     uint32_t rph = 0, mph = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      int sl, nt, mt;
-      unit(u, sl, nt, mt);
+      int sl, b, nt, mt;
+      unit(u, sl, b, nt, mt);
       const int nk = stages_of(sl);
       bool ok = true;
       for (int kc = 0; kc < nk; ++kc) {
@@ -255,13 +262,13 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      int sl, nt, mt;
-      unit(u, sl, nt, mt);
+      int sl, b, nt, mt;
+      unit(u, sl, b, nt, mt);
       if (!__all_sync(FULL, tc::mbar_wait(&ctl->tfull[acc], aph, abort, err, 15))) break;
       tc::fence_after_sync();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 128);
       const int64_t row0 = (int64_t)mt * 128 + quarter * 32;
-      float* outp = G.out + sl * G.out_stride;
+      float* outp = G.out + sl * G.out_stride + b * G.c_boff;
       for (int cc = 0; cc < G.BN; cc += 32) {
         uint32_t v[32];
         tc::tmem_ld32(taddr + cc, v);
@@ -345,6 +352,7 @@ cudaError_t make_operand_map(CUtensorMap* map, const float* base, int64_t rows, 
 }
 
 bool operand_ok(const float* base, int64_t rows, int64_t K, int64_t sr, int64_t sk, int box_rows) {
+  if (rows >= (1ll << 31) || K >= (1ll << 31)) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
   if (sk == 1) return sr % 4 == 0 && sr >= K && K >= 32 && rows >= box_rows;
   if (sr == 1) return sk % 4 == 0 && sk >= rows && rows >= box_rows && K >= 32;
@@ -364,12 +372,20 @@ bool gemm_raw_supported(const float* A, int64_t sai, int64_t sak, const float* B
 
 cudaError_t launch_gemm_raw(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
                             int64_t M, int64_t N, int64_t K, int S, int kq_slice, float* out, int64_t out_stride,
-                            int64_t ld, const float* bias, bool accumulate, int* err, cudaStream_t s) {
+                            int64_t ld, const float* bias, bool accumulate, int* err, cudaStream_t s, int batch,
+                            int64_t a_rows, int64_t b_rows, int64_t c_boff) {
   GrArgs G{};
   G.M = M;
   G.N = N;
   G.K = K;
   G.BN = gemm_raw_bn(N);
+  G.batch = batch;
+  G.a_boff = (int)M;
+  G.b_boff = (int)N;
+  G.c_boff = c_boff;
+  if (batch > 1 && (M % 128 != 0 || N % G.BN != 0)) return cudaErrorInvalidValue;   // whole tiles per batch
+  if (a_rows < (int64_t)batch * M) a_rows = (int64_t)batch * M;
+  if (b_rows < (int64_t)batch * N) b_rows = (int64_t)batch * N;
   G.a_kmajor = sak == 1;
   G.b_kmajor = sbk == 1;
   G.m_tiles = (int)((M + 127) / 128);
@@ -385,15 +401,15 @@ cudaError_t launch_gemm_raw(const float* A, int64_t sai, int64_t sak, const floa
   G.err = err;
   CUtensorMap ta, tb;
   cudaError_t e;
-  if ((e = make_operand_map(&ta, A, M, K, sai, sak, 128)) != cudaSuccess) return e;
-  if ((e = make_operand_map(&tb, B, N, K, sbj, sbk, (uint32_t)G.BN)) != cudaSuccess) return e;
+  if ((e = make_operand_map(&ta, A, a_rows, K, sai, sak, 128)) != cudaSuccess) return e;
+  if ((e = make_operand_map(&tb, B, b_rows, K, sbj, sbk, (uint32_t)G.BN)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(gemm_raw_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GR_SMEM)) !=
       cudaSuccess)
     return e;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int units = G.m_tiles * G.n_tiles * S;
+  const int units = G.m_tiles * G.n_tiles * batch * S;
   gemm_raw_tc_kernel<<<units < sms ? units : sms, GR_THREADS, GR_SMEM, s>>>(ta, tb, G);
   count_launch();
   return cudaGetLastError();

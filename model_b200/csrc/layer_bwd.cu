@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
     const float* __restrict__ qlen, const float* __restrict__ keys_n, const float* __restrict__ scal,
     float* __restrict__ probe, float* __restrict__ memg, float* __restrict__ dzg, float* __restrict__ dqhat,
     float* __restrict__ dqlen, float* __restrict__ dT_part, int* __restrict__ ent_slot, float* __restrict__ ent_w,
-    const BwdShard X) {
+    const BwdShard X, const float* __restrict__ mem_fwd) {
   extern __shared__ float bsm[];
   float* red = bsm;                 // [H][d]
   float* dmem_s = bsm + D.H * D.d;  // [d]
@@ -96,12 +96,16 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
       dw_l = __ldcg(X.dots + ((int64_t)own * X.mcap + m) * ((int64_t)D.H * k) + base + pos);
     }
   } else {
-  // 1. mem = sum_h sum_r w V[read slot] (memory.py:192), as the forward gather
+  // 1. mem = sum_h sum_r w V[read slot] (memory.py:192), as the forward
+  // gather -- unless the forward's read output is given (one pass over the
+  // rows instead of two)
+  if (!mem_fwd) {
   float acc[CH][VEC];
 #pragma unroll
   for (int c = 0; c < CH; ++c)
 #pragma unroll
     for (int v = 0; v < VEC; ++v) acc[c][v] = 0.f;
+#pragma unroll 4
   for (int r = 0; r < k; ++r) {
     const int64_t row = __shfl_sync(FULL, rs_l, r);
     const float wr = __shfl_sync(FULL, w_l, r);
@@ -123,11 +127,15 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
 #pragma unroll
       for (int v = 0; v < VEC; ++v) red[h * d + g * VEC + v] = acc[c][v];
   }
+  }
   __syncthreads();
   // 2. gate, probe (d read output), mem * gate, d gate pre-activation (model.py:118-119)
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     float mv = 0.f;
-    for (int hh = 0; hh < D.H; ++hh) mv += red[hh * d + i];
+    if (mem_fwd)
+      mv = mem_fwd[m * d + i];
+    else
+      for (int hh = 0; hh < D.H; ++hh) mv += red[hh * d + i];
     const float z = zg[m * d + i], sg = sigmoidf_(z), gate = z * sg;
     const float dm_ = dmemg[m * d + i];
     const float dmem = dm_ * gate;
@@ -137,22 +145,37 @@ __global__ void __launch_bounds__(1024) route_bwd_kernel(
     dmem_s[i] = dmem;
   }
   __syncthreads();
-  // 3. dw_r = dmem . V[read slot r]; softmax backward (memory.py:178)
-  for (int r = 0; r < k; ++r) {
-    const int64_t row = __shfl_sync(FULL, rs_l, r);
-    float s = 0.f;
+  // 3. dw_r = dmem . V[read slot r]; softmax backward (memory.py:178).
+  // Four rows at a time: their loads in flight together, their four warp
+  // reductions interleaved.
+  constexpr int RB = 4;
+  for (int r0 = 0; r0 < k; r0 += RB) {
+    float s[RB];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int g = c * 32 + lane;
-      if (g < groups) {
-        float x[VEC];
-        load_group<VT, VEC>(values + row * d + g * VEC, x);
+    for (int b = 0; b < RB; ++b) {
+      s[b] = 0.f;
+      const int r = r0 + b;
+      const int64_t row = __shfl_sync(FULL, rs_l, r < k ? r : 0);
+      if (r < k) {
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) s = fmaf(dmem_s[g * VEC + v], x[v], s);
+        for (int c = 0; c < CH; ++c) {
+          const int g = c * 32 + lane;
+          if (g < groups) {
+            float x[VEC];
+            load_group<VT, VEC>(values + row * d + g * VEC, x);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) s[b] = fmaf(dmem_s[g * VEC + v], x[v], s[b]);
+          }
+        }
       }
     }
-    s = warp_sum(s);
-    if (lane == r) dw_l = s;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int b = 0; b < RB; ++b) s[b] += __shfl_xor_sync(FULL, s[b], o);
+#pragma unroll
+    for (int b = 0; b < RB; ++b)
+      if (lane == r0 + b) dw_l = s[b];
   }
   }
   const float swdw = warp_sum(lane < k ? w_l * dw_l : 0.f);
@@ -361,7 +384,8 @@ cudaError_t route_bwd_ch(const Dims& D, const VT* values, const LayerBwd& B, con
       if (e != cudaSuccess) return e;                                                                           \
     }                                                                                                           \
     kern<<<grid, block, smem, s>>>(D, values, B.slots, B.weights, B.dmemg, B.zg, B.qn, B.qlen, B.keys_n, B.scal, \
-                                   B.probe, B.memg, B.dzg, B.dqhat, B.dqlen, B.dT_part, B.ent_slot, B.ent_w, X); \
+                                   B.probe, B.memg, B.dzg, B.dqhat, B.dqlen, B.dT_part, B.ent_slot, B.ent_w, X,  \
+                                   B.mem_fwd);                                                                  \
   }
   switch (ch_for(D.d / VEC)) {
     case 1: ML_RB(1); break;

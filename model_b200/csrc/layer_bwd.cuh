@@ -23,6 +23,7 @@ struct LayerBwd {
   float* dT_part;          // [M * H]
   int* ent_slot;           // [M, H, 2, k] (codebook * n + sub-key) of each slot-score gradient entry
   float* ent_w;            // [M, H, 2, k] its d cos
+  const float* mem_fwd = nullptr;   // [M, d] the forward's read output, or nullptr: recomputed from the rows
 };
 
 // Row-sharded table: where the routing backward finds the per-read dots

@@ -38,9 +38,11 @@ def _np(t):
     return t.detach().float().cpu().numpy()
 
 
-def _check(layer, params, h, dy, cfg, bal, rtp=False, gumbel=None):
+def _check(layer, params, h, dy, cfg, bal, rtp=False, gumbel=None, drop_mem=False):
     train = gumbel is not None
     y, mem, aux, ctx = layer.apply_train(params, h, train=train, gumbel=gumbel, check=True)
+    if drop_mem:   # a caller that kept no read output: the backward re-gathers it
+        ctx["la"].mem = None
     g = layer.backward(ctx, dy, balance_coef=bal, route_through_pool=rtp, check=True)
     torch.cuda.synchronize()
     p = params
@@ -85,7 +87,7 @@ def test_backward_cfg0_shapes():
 
 
 @pytest.mark.parametrize("n,H,dk,M,qs,bt,bal", [
-    (128, 1, 64, 2100, True, True, 0.8),      # half 32; 17 token tiles in 9 slices: one padding tile
+    (128, 1, 64, 2100, True, True, 0.8),      # half 32; 17 token tiles, the last partial; K slices of d k_hat
     (256, 2, 128, 300, False, False, 0.6),    # half 64; a partial last tile
     (512, 2, 256, 640, True, False, 1.0),     # half 128: the d q_hat accumulator spans 4 cosine chunks
 ])
@@ -94,6 +96,12 @@ def test_backward_balance_on_tensor_cores(n, H, dk, M, qs, bt, bal):
     # cosine -> softmax -> d cos kernel; a strong balance coefficient makes
     # its share of every gradient visible
     _check(*_case(n, H, dk, 64, 8, 64, M, seed=7 + n, query_scale=qs, btgrad=bt), bal)
+
+
+@pytest.mark.parametrize("vdt", [torch.float32, torch.float16])
+def test_backward_without_forward_read_output(vdt):
+    # the configs[0] case's seed (its routing has no near-ties against the oracle)
+    _check(*_case(512, 4, 256, 256, 16, 256, 512, seed=6, vdt=vdt), 0.05, drop_mem=True)
 
 
 def test_backward_no_tokens():
