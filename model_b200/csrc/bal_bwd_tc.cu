@@ -446,12 +446,10 @@ BalBwdPlan bal_bwd_plan(const Dims& D, int sms) {
   const int64_t HC = D.H * 2, n = D.n, half = D.half;
   P.m_tiles = (int)((D.M + 127) / 128);
   P.Mp = (int64_t)P.m_tiles * 128;
-  // K slices of the d k_hat GEMM (K = tokens): enough units to fill the SMs
-  const int64_t tiles = HC * (n / 128), kq = (D.M + 31) / 32;
-  int64_t S = 1;
-  while (tiles * S < sms && kq / (S * 2) >= 8) S *= 2;
-  const int64_t per = (kq + S - 1) / S;
-  P.S = (int)((kq + per - 1) / per);
+  // K slices of the d k_hat GEMM (K = tokens)
+  int64_t S, per;
+  raw_slices(HC * (n / 128), (D.M + 31) / 32, HC * n * half, sms, (size_t)1 << 40, &S, &per);
+  P.S = (int)S;
   P.kq_slice = (int)per;
   P.q_floats = HC * D.M * half;
   P.k_floats = HC * n * half;

@@ -5,7 +5,9 @@
 //
 //   0. operands whose rows or whose k run contiguously (16-byte aligned,
 //      at least one tile) go to gemm_raw_tc.cu, which loads them as stored
-//      and splits them inside the GEMM; otherwise:
+//      and splits them inside the GEMM -- unless its tiles would convert the
+//      operands over six times over (short K, many tiles both ways: the
+//      recomputed router projection); otherwise:
 //   1. both operands are gathered into K-major tf32 hi / lo halves in the
 //      caller's scratch (32 x 32 tiles through shared memory, so either
 //      stride order reads coalesced), zero-padded to a multiple of the K
@@ -151,13 +153,24 @@ __global__ void __launch_bounds__(256) colsum_part_kernel(const float* __restric
   part[(int64_t)blockIdx.y * cols + j] = x;
 }
 
+// 32 columns per block; thread (column c, group g) adds chunks g, g + 8, ...
+// in order, then the 8 groups are added in order (deterministic).
 __global__ void __launch_bounds__(256) colsum_final_kernel(const float* __restrict__ part, int64_t cols,
                                                            float* __restrict__ out) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= cols) return;
+  __shared__ float red[8][33];
+  const int c = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int64_t j = (int64_t)blockIdx.x * 32 + c;
   float x = 0.f;
-  for (int c = 0; c < CS_CHUNKS; ++c) x += part[(int64_t)c * cols + j];
-  out[j] = x;
+  if (j < cols)
+    for (int q = g; q < CS_CHUNKS; q += 8) x += part[(int64_t)q * cols + j];
+  red[g][c] = x;
+  __syncthreads();
+  if (g == 0 && j < cols) {
+    float t = red[0][c];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) t += red[i][c];
+    out[j] = t;
+  }
 }
 
 struct GemmPlan {
@@ -197,6 +210,28 @@ int sm_count() {
 
 }  // namespace
 
+// K slices of the operand-splitting GEMM: the count that minimises
+// (rounds of units over the SMs) x (K stages per unit), plus the slice sum's
+// traffic (a stage of ~1.7 us against ~5000 bytes per ns); at least 8 stages a
+// slice, the partials within `cap` floats.
+void raw_slices(int64_t tiles, int64_t kq, int64_t out_elems, int sms, size_t cap, int64_t* S_out, int64_t* per_out) {
+  double best = 1e30;
+  int64_t bS = 1, bper = kq;
+  for (int64_t S = 1; S <= 64 && S <= kq; ++S) {
+    const int64_t per = (kq + S - 1) / S, s2 = (kq + per - 1) / per;   // every slice non-empty
+    if (s2 > 1 && (per < 8 || (size_t)s2 * out_elems > cap)) continue;
+    const int64_t rounds = (tiles * s2 + sms - 1) / sms;
+    const double cost = rounds * per * 1.7e3 + (s2 > 1 ? (double)(s2 + 2) * out_elems * 4 / 5000.0 : 0.0);   // ns
+    if (cost < best - 1e-9) {
+      best = cost;
+      bS = s2;
+      bper = per;
+    }
+  }
+  *S_out = bS;
+  *per_out = bper;
+}
+
 size_t gemm_any_scratch_floats(int64_t M, int64_t N, int64_t K) {
   const GemmPlan g = gemm_plan(M, N, K, sm_count());
   if (!g.tc) return 0;
@@ -211,15 +246,17 @@ cudaError_t launch_gemm_any(const float* A, int64_t sai, int64_t sak, const floa
     if (accumulate && !bias) return cudaSuccess;
     return cudaErrorInvalidValue;   // the backward never asks for an empty product
   }
-  if (gemm_raw_supported(A, sai, sak, B, sbk, sbj, M, N, K)) {
+  // The operand-splitting GEMM converts A once per column tile and B once per
+  // row tile; when that repeats the operands many times over (a short K with
+  // many tiles both ways) one splitting pass plus the pre-split GEMM is cheaper.
+  const int64_t mt = (M + 127) / 128, nt = (N + gemm_raw_bn(N) - 1) / gemm_raw_bn(N);
+  const double redundancy = ((double)M * K * nt + (double)N * K * mt) / ((double)M * K + (double)N * K);
+  const GemmPlan g0 = gemm_plan(M, N, K, sm_count());
+  const bool presplit = redundancy > 6.0 && g0.tc && sc.floats >= gemm_any_scratch_floats(M, N, K);
+  if (!presplit && gemm_raw_supported(A, sai, sak, B, sbk, sbj, M, N, K)) {
     // operands split inside the GEMM (gemm_raw_tc.cu); K slices when few tiles
-    const int sms = sm_count();
-    const int64_t tiles = ((M + 127) / 128) * ((N + gemm_raw_bn(N) - 1) / gemm_raw_bn(N));
-    const int64_t kq = (K + KQ - 1) / KQ;
-    int64_t S = 1;
-    while (tiles * S < sms && kq / (S * 2) >= 8 && (size_t)(S * 2) * M * N <= sc.floats) S *= 2;
-    const int64_t per = (kq + S - 1) / S;
-    S = (kq + per - 1) / per;                                   // every slice non-empty
+    int64_t S, per;
+    raw_slices(mt * nt, (K + KQ - 1) / KQ, M * N, sm_count(), sc.floats, &S, &per);
     if (S == 1)
       return launch_gemm_raw(A, sai, sak, B, sbk, sbj, M, N, K, 1, (int)per, C, 0, ldc, bias, accumulate, err, s);
     cudaError_t e = launch_gemm_raw(A, sai, sak, B, sbk, sbj, M, N, K, (int)S, (int)per, sc.p, M * N, N, nullptr,
@@ -297,7 +334,7 @@ cudaError_t launch_colsum_det(const float* X, int64_t rows, int64_t cols, int64_
   if (rows == 0) return cudaMemsetAsync(out, 0, sizeof(float) * cols, s);
   colsum_part_kernel<<<dim3((unsigned)((cols + 255) / 256), CS_CHUNKS), 256, 0, s>>>(X, rows, cols, ld, part);
   count_launch();
-  colsum_final_kernel<<<(unsigned)((cols + 255) / 256), 256, 0, s>>>(part, cols, out);
+  colsum_final_kernel<<<(unsigned)((cols + 31) / 32), 256, 0, s>>>(part, cols, out);
   count_launch();
   return cudaGetLastError();
 }

@@ -38,6 +38,9 @@ cudaError_t launch_sum_slices(const float* P, int S, int64_t M, int64_t N, float
 // multiple of 128 and N of the column tile.  a_rows / b_rows: the operands'
 // total rows (0: batch M / batch N).
 int gemm_raw_bn(int64_t N);
+// K slices (S) and 32-element stages per slice (per) for `tiles` output tiles
+// over kq stages, partials of out_elems floats each within cap floats.
+void raw_slices(int64_t tiles, int64_t kq, int64_t out_elems, int sms, size_t cap, int64_t* S, int64_t* per);
 bool gemm_raw_supported(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
                         int64_t M, int64_t N, int64_t K);
 cudaError_t launch_gemm_raw(const float* A, int64_t sai, int64_t sak, const float* B, int64_t sbk, int64_t sbj,
