@@ -27,9 +27,11 @@
 //            global memory, 32 consecutive tokens per store, as the A operand
 //            of the d k_hat GEMM; finally the tile's d q_hat is stored (the
 //            query norm backward adds it to the routing share).
-// The d k_hat GEMM is one launch of the operand-splitting GEMM
-// (gemm_raw_tc.cu), batched over the codebooks, reading the unit queries in
-// place; its K slices are added in order.
+// The routing backward's sparse d cos entries are then added into the
+// transposed d cos (sparse_into_dct_kernel) and the d k_hat GEMM -- one launch
+// of the operand-splitting GEMM (gemm_raw_tc.cu), batched over the codebooks,
+// reading the unit queries in place, K slices added in order -- gives the
+// whole sub-key gradient, dense and sparse parts together.
 // The [H*2, M, n] cosine / d cos matrices never reach HBM.
 #include "bal_bwd_tc.cuh"
 #include "backbone.cuh"
@@ -434,6 +436,22 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
   }
 }
 
+// The routing backward's sparse slot-score gradient (memory.py:162-178: one
+// d cos per distinct selected sub-key of a (token, codebook) row) added into
+// the transposed d cos matrix, so that one GEMM gives the whole sub-key
+// gradient.  One thread per entry; a row's entries have distinct keys and
+// rows own distinct columns, so no two threads touch one element.
+__global__ void sparse_into_dct_kernel(const int* __restrict__ ent_slot, const float* __restrict__ ent_w, int64_t F,
+                                       int k, int HC, int64_t Mp, float* __restrict__ dct) {
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= F) return;
+  const float w = ent_w[f];
+  if (w == 0.f) return;                       // padding (its key repeats the codebook's first)
+  const int64_t m = f / ((int64_t)k * HC);    // entries are [M][HC][k]
+  float* p = dct + (int64_t)ent_slot[f] * Mp + m;
+  *p += w;
+}
+
 }  // namespace
 
 bool bal_bwd_tc_supported(const Dims& D) {
@@ -501,6 +519,13 @@ cudaError_t launch_bal_bwd_tc(const Dims& D, const BalBwdPlan& P, const BalBwdBu
   bal_bwd_tc_kernel<<<units < sms ? units : sms, BB_THREADS, BB_SMEM, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], A);
   count_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // + the routing backward's sparse entries
+  {
+    const int64_t F = D.M * HC * D.k;
+    sparse_into_dct_kernel<<<(unsigned)((F + 255) / 256), 256, 0, s>>>(B.ent_slot, B.ent_w, F, D.k, HC, P.Mp, B.dct);
+    count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   // d k_hat[hc] = d cos[hc]^T Q_hat[hc] (K = tokens), one batch per codebook
   const int64_t ldq = (int64_t)HC * half;
   if (!gemm_raw_supported(B.dct, P.Mp, 1, B.qn, ldq, 1, n, half, D.M)) return cudaErrorInvalidValue;

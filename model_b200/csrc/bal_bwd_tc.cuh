@@ -33,6 +33,8 @@ struct BalBwdBufs {
   float* dT_row;         // [H*2][M]
   float* dql_row;        // [M][H*2] or nullptr
   int* err;              // status word (bounded waits: 17-19)
+  const int* ent_slot;   // [M][H*2][k] the routing backward's (codebook * n + sub-key) entries ...
+  const float* ent_w;    // ... and their d cos (0: padding), added into the d cos matrix
 };
 
 bool bal_bwd_tc_supported(const Dims& D);

@@ -1347,9 +1347,10 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
   P.o_dT = take(4 * M * D.H);
   P.o_ent_s = take(4 * P.F);
   P.o_ent_w = take(4 * P.F);
-  P.o_rg = take(P.L.bytes);
-  P.o_uniq = take(4 * P.cap);
-  P.o_rows = take(4 * P.cap * half);
+  const bool bal_tc = balance && bal_bwd_tc_supported(D);   // sub-key entries go through the balance GEMM
+  P.o_rg = bal_tc ? 0 : take(P.L.bytes);
+  P.o_uniq = bal_tc ? 0 : take(4 * P.cap);
+  P.o_rows = bal_tc ? 0 : take(4 * P.cap * half);
   P.o_dkhat = take(4 * NK * half);
   P.o_dq = take(4 * M * HC * half);
   P.bal_tc = balance && bal_bwd_tc_supported(D);
@@ -1515,7 +1516,8 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
       const BalBwdBufs BB{qn, F32p(P.o_qhi), F32p(P.o_qlo), keys_n, F32p(P.o_khi), F32p(P.o_klo),
                           F32p(P.o_kthi), F32p(P.o_ktlo), F32p(P.o_dct), F32p(P.o_bpart), FW.clean_cnt, qlen,
                           scal, F32p(P.o_dqbal), dkhat,
-                          F32p(P.o_dTrow), F32p(P.o_dqlrow), gerr};
+                          F32p(P.o_dTrow), F32p(P.o_dqlrow), gerr,
+                          reinterpret_cast<const int*>(ws + P.o_ent_s), F32p(P.o_ent_w)};
       ML_TRY(launch_bal_bwd_tc(D, P.bp, BB, g->balance_coef, s));
     }
     float* C = P.bal_tc ? nullptr : F32p(P.o_cbal);
@@ -1535,23 +1537,27 @@ static int layer_bwd_impl(const memlayer_config* cfg, const memlayer_layer_args*
   } else {
     ML_TRY(cudaMemsetAsync(dkhat, 0, sizeof(float) * HC * n * half, s));
   }
-  // the sparse sub-key gradient: sum over entries of d cos * q_hat row, per sub-key
-  RowGradK R{};
-  R.n_reads = 1;
-  R.slots[0] = reinterpret_cast<const int*>(ws + P.o_ent_s);
-  R.weights[0] = F32p(P.o_ent_w);
-  R.grad[0] = qn;
-  R.off[0] = 0;
-  R.off[1] = P.F;
-  R.F = P.F;
-  R.N = HC * n;
-  R.Nslot = HC * n;
-  R.hk = D.k;
-  R.d = (int)half;
-  ML_TRY(launch_rowgrad(R, P.L, ws + P.o_rg, reinterpret_cast<int*>(ws + P.o_uniq), F32p(P.o_rows), nullptr,
-                        nullptr, nullptr, s));
-  ML_TRY(launch_scatter_rows(reinterpret_cast<const int*>(ws + P.o_uniq), F32p(P.o_rows), P.cap, HC * n, (int)half,
-                             dkhat, s));
+  // the sparse sub-key gradient: sum over entries of d cos * q_hat row, per
+  // sub-key (with the balance term on the tensor cores the entries were
+  // added into its d cos matrix: its GEMM gave the whole sub-key gradient)
+  if (!P.bal_tc) {
+    RowGradK R{};
+    R.n_reads = 1;
+    R.slots[0] = reinterpret_cast<const int*>(ws + P.o_ent_s);
+    R.weights[0] = F32p(P.o_ent_w);
+    R.grad[0] = qn;
+    R.off[0] = 0;
+    R.off[1] = P.F;
+    R.F = P.F;
+    R.N = HC * n;
+    R.Nslot = HC * n;
+    R.hk = D.k;
+    R.d = (int)half;
+    ML_TRY(launch_rowgrad(R, P.L, ws + P.o_rg, reinterpret_cast<int*>(ws + P.o_uniq), F32p(P.o_rows), nullptr,
+                          nullptr, nullptr, s));
+    ML_TRY(launch_scatter_rows(reinterpret_cast<const int*>(ws + P.o_uniq), F32p(P.o_rows), P.cap, HC * n,
+                               (int)half, dkhat, s));
+  }
   if (g->dsub_keys)
     ML_TRY(launch_norm_bwd(keys_n, dkhat, nullptr, HC * n, (int)half, pa->sub_keys, nullptr, nullptr, g->dsub_keys,
                            s));

@@ -310,9 +310,10 @@ class MemoryLayer:
         forward of ``ctx`` (memlayer_layer_backward): the reference's
         parameter names (``router_i`` / ``mem_gate_i`` / ``mem_out_i`` kernel
         and bias, ``pool`` sub_keys and log_temperature), ``h``, and
-        ``probe`` = d loss / d read output, the row update's input.  Backward
-        calls on one device must not overlap on the GPU (their GEMMs share
-        cuBLAS's default workspace): issue them on one stream."""
+        ``probe`` = d loss / d read output, the row update's input.  The
+        forward's read output kept in ``ctx`` is read, not re-gathered; every
+        GEMM runs on the library's tensor-core kernels in the call's own
+        workspace, so backward calls may overlap."""
         dev = ctx["device"]
         dy = _cuda_f32(dy, "dy").reshape(ctx["M"], self.d_model)
         g, ga, ws, nb = self._grad_setup(ctx["cfg"], ctx["M"], dev, dy, balance_coef, route_through_pool, ctx["ws"])
