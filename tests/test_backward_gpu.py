@@ -98,6 +98,15 @@ def test_backward_balance_on_tensor_cores(n, H, dk, M, qs, bt, bal):
     _check(*_case(n, H, dk, 64, 8, 64, M, seed=7 + n, query_scale=qs, btgrad=bt), bal)
 
 
+def test_backward_balance_on_tensor_cores_noisy_forward():
+    # selection noise: the routing backward takes each selected sub-key's
+    # cosine from the forward's clean scores (not its noisy selection scores)
+    layer, params, h, dy, cfg = _case(128, 2, 64, 64, 8, 64, 300, seed=21, query_scale=True)
+    gumbel = -torch.log(-torch.log(torch.rand(300, 2, 2, 128, device="cuda",
+                                              generator=torch.Generator("cuda").manual_seed(22)).clamp_(min=1e-12)))
+    _check(layer, params, h, dy, cfg, 0.5, gumbel=gumbel)
+
+
 @pytest.mark.parametrize("vdt", [torch.float32, torch.float16])
 def test_backward_without_forward_read_output(vdt):
     # the configs[0] case's seed (its routing has no near-ties against the oracle)
