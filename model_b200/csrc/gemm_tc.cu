@@ -348,7 +348,10 @@ __global__ void concat_bias_kernel(const float* __restrict__ a, int na, const fl
 
 bool proj_tc_supported(const Dims& D) {
   const int NR = D.H * D.dk;
+  // NR + d >= 256: 256-column tiles, so each epilogue warp's 128 columns are
+  // all router columns (whole query halves, NR % 128 == 0) or all gate columns
   return D.M >= tc::PIPE_M && D.dm % tc::PIPE_K == 0 && D.d % tc::PIPE_K == 0 && NR % 128 == 0 &&
+         NR + D.d >= BN_MAX &&
          (NR + D.d) * 4 <= 16384 && D.dm * 4 <= 16384 &&
          (D.half == 32 || D.half == 64 || D.half == 128) && D.d % 16 == 0 && (D.dm >= BN_MAX || D.dm % 16 == 0) &&
          D.M < (1ll << 31);

@@ -208,6 +208,11 @@ SHAPES = {
                           d_model=96, biases=True),
     "layer_qscale_noise": dict(n_sub_keys=128, heads=2, d_key=256, d_value=128, top_k=8, M=384, seed=40, layer=True,
                                d_model=128, query_scale=True, noise=1.0, train=True, clustered=True),
+    # router 128 + gate 64 columns (< one 256-column tile): the float32 SIMT projections
+    "layer_n192": dict(n_sub_keys=128, heads=2, d_key=64, d_value=64, top_k=8, M=300, seed=41, layer=True,
+                       d_model=64, biases=True),
+    "layer_n192_qscale_noise": dict(n_sub_keys=128, heads=2, d_key=64, d_value=64, top_k=8, M=300, seed=42,
+                                    layer=True, d_model=64, query_scale=True, noise=1.0, train=True),
 }
 
 
@@ -340,3 +345,27 @@ def test_gpu_few_token_score_path(M, n, k, qscale, noisy):
     np.testing.assert_allclose(aux["weights"].cpu().numpy()[same], a_ref["weights"][same], rtol=1e-5, atol=1e-7)
     if same.all():
         assert_rel(out.cpu().numpy(), o_ref, OUT_RTOL_F32, "out")
+
+
+@pytest.mark.parametrize("half,k,stats", [(32, 8, False), (32, 8, True), (64, 8, True), (32, 16, True)])
+def test_gpu_tensor_core_noisy_selection_narrow_halves(half, k, stats):
+    """Selection noise on the tensor-core score path (>= 128 tokens) with
+    narrow query halves: slots, weights and the read against the oracle."""
+    from model_b200 import MemoryPool
+    M, H, n, d = 300, 2, 128, 32
+    dk = 2 * half
+    pool = MemoryPool(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=True, routing_noise=1.0)
+    rng = np.random.default_rng(half * 100 + k)
+    sk = rng.standard_normal((H, 2, n, half)).astype(np.float32)
+    values = (rng.standard_normal((n * n, d)) * 0.02).astype(np.float32)
+    q = rng.standard_normal((M, H, dk)).astype(np.float32)
+    gum = rng.gumbel(size=(M, H, 2, n)).astype(np.float32)
+    params = {"sub_keys": _dev(sk), "values": _dev(values),
+              "log_temperature": torch.tensor(np.log(10.0), dtype=torch.float32, device="cuda")}
+    out, aux = pool.apply({"params": params}, _dev(q), train=True, stats=stats, check=True, gumbel=_dev(gum))
+    torch.cuda.synchronize()
+    cfg = ref.PoolConfig(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=True, routing_noise=1.0)
+    o_ref, a_ref = ref.pool_forward(cfg, q, sk, float(np.log(10.0)), values, train=True, gumbel=gum,
+                                    with_stats=False)
+    r = ref.route(cfg, q, sk, float(np.log(10.0)), True, gum)
+    check_slots(aux["slots"].cpu().numpy(), a_ref["slots"], r["select"], n)
