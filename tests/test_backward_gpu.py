@@ -107,6 +107,15 @@ def test_backward_balance_on_tensor_cores_noisy_forward():
     _check(layer, params, h, dy, cfg, 0.5, gumbel=gumbel)
 
 
+@pytest.mark.parametrize("n,H,dk,d,dm,M", [
+    (32, 2, 32, 48, 40, 333),     # K tails (333 tokens, d_model 40), 48- and 64-column tiles
+    (32, 2, 32, 48, 50, 260),     # d_model 50: a row pitch the bulk copies cannot take (fallback GEMM)
+    (64, 3, 64, 80, 96, 200),     # 3 heads: 192 router columns
+])
+def test_backward_odd_shapes(n, H, dk, d, dm, M):
+    _check(*_case(n, H, dk, d, 8, dm, M, seed=50 + dm), 0.4)
+
+
 @pytest.mark.parametrize("vdt", [torch.float32, torch.float16])
 def test_backward_without_forward_read_output(vdt):
     # the configs[0] case's seed (its routing has no near-ties against the oracle)
