@@ -99,9 +99,6 @@ __device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t& parity, int l
   return __all_sync(FULL, ok);
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 __device__ __forceinline__ void ring_at(uint32_t pos, int& s, uint32_t& ph) {
   s = (int)(pos % BB_BLOCKS);
@@ -377,7 +374,7 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
           *reinterpret_cast<float4*>(rowp + BB_TILE + at) =
               make_float4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
         }
-        fence_proxy_async_smem();
+        tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ctl->full[s]);
         return true;

@@ -21,8 +21,6 @@
 // A long inner dimension with few output tiles is cut into S K slices (tile
 // coordinates, no copies); the partial products are added in slice order by
 // the caller.  Every mbarrier wait is bounded.
-#include <cudaTypedefs.h>
-
 #include "gemm_any.cuh"
 #include "tc_common.cuh"
 
@@ -59,9 +57,6 @@ struct GrArgs {
   int* err;
 };
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // Convert one raw tile of `rows` rows into K-major swizzled hi / lo tiles.
 __device__ __forceinline__ void convert_tile(const float* raw, bool kmajor, int rows, float* hi, float* lo, int t) {
@@ -239,7 +234,7 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
         float* m4 = reinterpret_cast<float*>(mma + (size_t)ms * 4 * GR_TILE);
         convert_tile(ra, G.a_kmajor, 128, m4, m4 + GR_TILE / 4, t);
         convert_tile(ra + GR_TILE / 4, G.b_kmajor, G.BN, m4 + 2 * GR_TILE / 4, m4 + 3 * GR_TILE / 4, t);
-        fence_proxy_async_smem();
+        tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
           tc::mbar_arrive(&ctl->raw_empty[rs]);
@@ -321,34 +316,13 @@ __global__ void __launch_bounds__(GR_THREADS, 1)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 // Operand element (r, k) at base[r sr + k sk]; rows x K.  K-major (sk == 1):
 // box 32 k x box_rows, 128-byte swizzle.  Row-contiguous (sr == 1): box
 // box_rows x 32 k, no swizzle.
 cudaError_t make_operand_map(CUtensorMap* map, const float* base, int64_t rows, int64_t K, int64_t sr, int64_t sk,
                              uint32_t box_rows) {
-  auto fn = encode();
-  if (!fn) return cudaErrorNotSupported;
-  const bool kmaj = sk == 1;
-  cuuint64_t dims[2] = {(cuuint64_t)(kmaj ? K : rows), (cuuint64_t)(kmaj ? rows : K)};
-  cuuint64_t strides[1] = {(cuuint64_t)((kmaj ? sr : sk) * sizeof(float))};
-  cuuint32_t box[2] = {kmaj ? 32u : box_rows, kmaj ? box_rows : 32u};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, kmaj ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+  if (sk == 1) return make_tmap_f32_2d(map, base, (uint64_t)K, (uint64_t)rows, (uint64_t)sr, 32, box_rows, true);
+  return make_tmap_f32_2d(map, base, (uint64_t)rows, (uint64_t)K, (uint64_t)sk, box_rows, 32, false);
 }
 
 bool operand_ok(const float* base, int64_t rows, int64_t K, int64_t sr, int64_t sk, int box_rows) {

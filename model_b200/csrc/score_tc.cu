@@ -791,6 +791,20 @@ cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, ui
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t make_tmap_f32_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                             uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch * sizeof(float)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 bool score_tc_supported(const Dims& D) {
   // the tensor maps' boxes (128 query rows, BN key rows) must fit inside the
   // [H*2*M, half] / [H*2*n, half] matrices

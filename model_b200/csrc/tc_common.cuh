@@ -74,6 +74,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Generic-proxy shared-memory writes made visible to the async proxy (TMA
+// stores, tcgen05.mma operand reads) before they are signalled.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -190,5 +194,10 @@ __device__ __forceinline__ float to_tf32(float x) {
 // box_k = 32 (128-byte rows, 128-byte swizzle) or 16 (64-byte rows, 64-byte swizzle)
 cudaError_t make_tmap_f32(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
                           uint32_t box_k = 32);
+// General 2-D float32 tensor map: `inner` contiguous elements per row, `outer`
+// rows `pitch` elements apart, a (box_inner x box_outer) box, 128-byte
+// swizzle (box_inner * 4 <= 128) or none.
+cudaError_t make_tmap_f32_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                             uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 
 }  // namespace ml
