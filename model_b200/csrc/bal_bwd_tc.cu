@@ -14,7 +14,7 @@
 // (codebook, 128-token tile):
 //   warp 0   TMA producer: q_hat K stages and the sub-key chunks streamed
 //            against each, then the transposed sub-keys, 32 keys per block,
-//            of the d q_hat MMA (one seven-block ring shared with the
+//            of the d q_hat MMA (one six-block ring shared with the
 //            epilogue's d cos blocks);
 //   warp 1   MMA issuer: the 128 x n cosine tile into TMEM columns [0, n),
 //            then d q_hat (128 x half) into columns [0, half) -- issued only
@@ -98,7 +98,6 @@ __device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t& parity, int l
   parity ^= 1;
   return __all_sync(FULL, ok);
 }
-
 
 __device__ __forceinline__ void ring_at(uint32_t pos, int& s, uint32_t& ph) {
   s = (int)(pos % BB_BLOCKS);

@@ -57,7 +57,6 @@ struct GrArgs {
   int* err;
 };
 
-
 // Convert one raw tile of `rows` rows into K-major swizzled hi / lo tiles.
 __device__ __forceinline__ void convert_tile(const float* raw, bool kmajor, int rows, float* hi, float* lo, int t) {
   if (kmajor) {   // same swizzled layout: elementwise
