@@ -18,9 +18,12 @@
 //                      row-sharded table (SH) probe, mem * gate and the
 //                      gate gradient come from shard.cu's probe kernel and
 //                      each dw_r from the dots its row's owner returned;
-//   bal_row_kernel     (balance term) per (token, codebook) row the softmax
-//                      of p over all n keys from the recomputed cosines, and
-//                      d p = s (dP - sum dP s) / M turned into d cos;
+//   bal_row_kernel     (balance term, shapes the fused tensor-core kernel of
+//                      bal_bwd_tc.cu does not take: n not a multiple of 128,
+//                      fewer than 128 tokens) per (token, codebook) row the
+//                      softmax of p over all n keys from the recomputed
+//                      cosines, and d p = s (dP - sum dP s) / M turned into
+//                      d cos;
 //   GEMMs              (recomputed projections, Dense-layer gradients, the
 //                      dense balance contractions) on the tensor cores as
 //                      3xTF32 (gemm_any.cu), long sums split over the SMs
