@@ -1347,13 +1347,14 @@ BwdPlan bwd_plan(const Dims& D, bool balance) {
   P.o_dT = take(4 * M * D.H);
   P.o_ent_s = take(4 * P.F);
   P.o_ent_w = take(4 * P.F);
-  const bool bal_tc = balance && bal_bwd_tc_supported(D);   // sub-key entries go through the balance GEMM
-  P.o_rg = bal_tc ? 0 : take(P.L.bytes);
-  P.o_uniq = bal_tc ? 0 : take(4 * P.cap);
-  P.o_rows = bal_tc ? 0 : take(4 * P.cap * half);
+  // the balance term on the tensor cores: the sub-key entries go through its
+  // GEMM, so the segment-sum scratch is not needed
+  P.bal_tc = balance && bal_bwd_tc_supported(D);
+  P.o_rg = P.bal_tc ? 0 : take(P.L.bytes);
+  P.o_uniq = P.bal_tc ? 0 : take(4 * P.cap);
+  P.o_rows = P.bal_tc ? 0 : take(4 * P.cap * half);
   P.o_dkhat = take(4 * NK * half);
   P.o_dq = take(4 * M * HC * half);
-  P.bal_tc = balance && bal_bwd_tc_supported(D);
   if (P.bal_tc) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
