@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--values-dtype", choices=["f32", "f16", "bf16"], default="f32")
     ap.add_argument("--tokens", type=int, default=WORKLOAD["tokens_per_gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--inflight", type=int, default=4,
+    ap.add_argument("--inflight", type=int, default=6,
                     help="host-buffer calls in flight (on as many streams) in the e2e measurement")
     ap.add_argument("--host-chunks", type=int, default=1,
                     help="chunks of the host-buffer pipeline timed as e2e (memlayer_layer_forward_host)")
