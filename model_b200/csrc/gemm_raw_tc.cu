@@ -370,7 +370,8 @@ cudaError_t launch_gemm_raw(const float* A, int64_t sai, int64_t sak, const floa
   G.ld = ld;
   G.bias = bias;
   G.accumulate = accumulate ? 1 : 0;
-  G.vec = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && (out_stride % 4 == 0);
+  G.vec = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && (out_stride % 4 == 0) &&
+          (c_boff % 4 == 0);
   G.err = err;
   CUtensorMap ta, tb;
   cudaError_t e;

@@ -18,17 +18,24 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-4
 
 
-def _case(n, H, dk, d, k, dm, M, seed, vdt=torch.float32, query_scale=False, btgrad=False):
+def _case(n, H, dk, d, k, dm, M, seed, vdt=torch.float32, query_scale=False, btgrad=False, cpu_rng=False):
+    # cpu_rng: biases, h and dy drawn on the host, so that a case's routing
+    # margins can be checked beforehand without a GPU
     pool = MemoryPool(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=query_scale,
                       balance_temperature_grad=btgrad, min_temperature=5.0, max_temperature=50.0)
     layer = MemoryLayer(pool, d_model=dm, layer=1)
     params = layer.init(seed, values_dtype=vdt)
+    dev = "cpu" if cpu_rng else "cuda"
     with torch.no_grad():
         params["pool"]["log_temperature"].fill_(float(np.log(12.0)))
+        g = torch.Generator("cpu").manual_seed(seed)
         for name in ("router_1", "mem_gate_1", "mem_out_1"):
-            params[name]["bias"].normal_(0.0, 0.1, generator=torch.Generator("cuda").manual_seed(seed))
-    h = torch.randn(M, dm, device="cuda", generator=torch.Generator("cuda").manual_seed(seed + 1))
-    dy = torch.randn(M, dm, device="cuda", generator=torch.Generator("cuda").manual_seed(seed + 2))
+            if cpu_rng:
+                params[name]["bias"].copy_(torch.empty(params[name]["bias"].shape).normal_(0.0, 0.1, generator=g))
+            else:
+                params[name]["bias"].normal_(0.0, 0.1, generator=torch.Generator("cuda").manual_seed(seed))
+    h = torch.randn(M, dm, device=dev, generator=torch.Generator(dev).manual_seed(seed + 1)).to("cuda")
+    dy = torch.randn(M, dm, device=dev, generator=torch.Generator(dev).manual_seed(seed + 2)).to("cuda")
     cfg = ref.PoolConfig(n_sub_keys=n, heads=H, d_key=dk, d_value=d, top_k=k, query_scale=query_scale,
                          balance_temperature_grad=btgrad, min_temperature=5.0, max_temperature=50.0)
     return layer, params, h, dy, cfg
@@ -96,6 +103,16 @@ def test_backward_balance_on_tensor_cores(n, H, dk, M, qs, bt, bal):
     # cosine -> softmax -> d cos kernel; a strong balance coefficient makes
     # its share of every gradient visible
     _check(*_case(n, H, dk, 64, 8, 64, M, seed=7 + n, query_scale=qs, btgrad=bt), bal)
+
+
+@pytest.mark.parametrize("n,H,dk,M,qs,bt,bal,seed", [
+    (128, 1, 256, 129, False, True, 0.9, 116),   # half 128 = n: d q_hat overwrites every cosine column; one token in the last tile
+    (384, 2, 64, 300, True, False, 0.7, 102),    # three 128-key blocks per K stage, twelve 32-key chunks
+])
+def test_backward_balance_on_tensor_cores_edge_shapes(n, H, dk, M, qs, bt, bal, seed):
+    # host-drawn inputs whose routing margins (the gap after the k-th score
+    # of each half and after the k-th of the k x k candidates) exceed 1e-4
+    _check(*_case(n, H, dk, 64, 8, 64, M, seed=seed, query_scale=qs, btgrad=bt, cpu_rng=True), bal)
 
 
 def test_backward_balance_on_tensor_cores_noisy_forward():
