@@ -323,7 +323,11 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
         sdp = d0 * e0 + d1 * e1;
       }
       sdp /= sum;                                      // sum_i dP_i s_i
-      const float inv = 1.0f / sum;
+      // d p_j = e_j / sum (dP_j - sdp) / M with e_j = exp(p_j - max); the row's
+      // constant factors folded into one (zero for a padding row), times sg(T)
+      // when d cos is T d p_j
+      const float gsc = owner ? (A.btgrad ? 1.0f / sum * invM : 1.0f / sum * invM * T) : 0.f;
+      const float Tq = T * ql;
       // this row's column of the transposed d cos
       float* gd = A.dct + ((int64_t)hc * A.n) * A.Mp + (int64_t)mt * 128 + r;
       float dTr = 0.f, dqr = 0.f;
@@ -339,17 +343,14 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
           const float cosv = __uint_as_float(v[t]);
-          const float sj = __expf(cosv * ps - mx) * inv;
-          const float g = sj * (__shfl_sync(FULL, cl, t) - sdp) * invM;   // d p_j
-          float dc;
+          const float e = __expf(cosv * ps - mx);
+          const float g = e * (__shfl_sync(FULL, cl, t) - sdp) * gsc;   // d p_j (T d p_j without btgrad)
+          float dc = g;
           if (A.btgrad) {
             dTr += g * cosv * ql;
             dqr += g * cosv * T;
-            dc = g * T * ql;
-          } else {
-            dc = g * T;                                // sg(T)
+            dc = g * Tq;
           }
-          dc = owner ? dc : 0.f;
           // transposed d cos: key (c 32 + t)'s row, 32 consecutive tokens per warp store
           gd[(int64_t)(c * 32 + t) * A.Mp] = dc;
           hi[t] = tc::to_tf32(dc);
