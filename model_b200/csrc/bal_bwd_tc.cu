@@ -49,7 +49,10 @@ constexpr uint32_t BB_TILE = 128 * 32 * 4;          // 128 rows x 32 tf32, 128-b
 constexpr uint32_t BB_BLOCK = 2 * BB_TILE;          // one ring block: a hi / lo pair of tiles
 constexpr int BB_BLOCKS = 6;                        // ring depth (>= 1 + 128-key chunks)
 constexpr uint32_t BB_XCH = 8192;                   // row-statistics exchange of the warp pairs
-constexpr uint32_t BB_SMEM = 2048 + BB_BLOCKS * BB_BLOCK + BB_XCH;
+constexpr int BB_WCNT = 256;                        // counts per epilogue warp: its n / 2 <= 256 keys
+constexpr uint32_t BB_CNTS = BB_EPI_WARPS * BB_WCNT * 4;
+constexpr uint32_t BB_SMEM = 2048 + BB_BLOCKS * BB_BLOCK + BB_XCH + BB_CNTS;
+constexpr float BB_LOG2E = 1.4426950408889634f;
 
 // One ring of 32 KB blocks carries, per work unit and in this order,
 //   for each K stage kc of the cosine MMA: Q(kc) = q_hat hi / lo [128 x 32],
@@ -90,6 +93,15 @@ struct BalArgs {
   int* err;
 };
 
+// 2^x (PTX ex2.approx.ftz.f32).  The softmax works in base 2: exp(p) =
+// 2^(p log2 e), with log2 e folded into the row's score scale, so each
+// exponential is one FFMA and one ex2.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Bounded rendezvous of the two warps of a lane quarter.
 __device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t& parity, int lane, volatile int* abort, int* err) {
   __syncwarp();
@@ -129,6 +141,8 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
   uint8_t* ring = smem + 1024;
   // [2 parities][128 rows][8]: row statistics at 0-2, temperature / q_len gradient shares at 4-5
   float* xch = reinterpret_cast<float*>(ring + BB_BLOCKS * BB_BLOCK);
+  // [8 epilogue warps][256]: the warp's counts (x dscale) of its chunks, 32 per chunk
+  float* cnts = xch + BB_XCH / 4;
   volatile int* abort = &ctl->abort;
   int* err = A.err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -260,6 +274,7 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
     uint32_t pph = 0;
     float* mine = xch + (hf * 128 + r) * 8;
     const float* other = xch + ((hf ^ 1) * 128 + r) * 8;
+    float* cw = cnts + (warp - 2) * BB_WCNT;           // chunk hf + 2 i at cw + 32 i
     uint32_t it = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
       const int hc = u / A.m_tiles, mt = u - hc * A.m_tiles;
@@ -267,47 +282,59 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
       const bool owner = m < A.M;
       const float ql = (A.qscale && owner) ? A.qlen[m * A.HC + hc] : 1.f;
       const float ps = A.btgrad ? T * ql : T;
+      const float psl = ps * BB_LOG2E;                 // score scale in base 2 (ps > 0)
       const float* cn = A.cnt + (int64_t)hc * A.n;
-      // counts of this warp's first two chunks, loaded while the cosines are computed
-      float cla = __ldg(cn + hf * 32 + lane) * A.dscale;
-      float clb = hf + 2 < nch ? __ldg(cn + (hf + 2) * 32 + lane) * A.dscale : 0.f;
+      // this warp's counts into its shared-memory slice while the cosines are
+      // computed (the warp's reads of the previous unit's counts are done)
+      {
+        float cr[BB_WCNT / 32];
+#pragma unroll
+        for (int i = 0; i < BB_WCNT / 32; ++i) cr[i] = hf + 2 * i < nch ? __ldg(cn + (hf + 2 * i) * 32 + lane) : 0.f;
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < BB_WCNT / 32; ++i)
+          if (hf + 2 * i < nch) cw[i * 32 + lane] = cr[i] * A.dscale;
+        __syncwarp();
+      }
       if (!__all_sync(FULL, tc::mbar_wait(&ctl->sfull, it & 1, abort, err, 19))) break;
       tc::fence_after_sync();
       // one pass over this warp's chunks: running max, sum of exp and the
-      // count-weighted sum (memory.py:210-214); each chunk's 32 counts are one
-      // coalesced load (issued a chunk ahead), handed to the lanes by shuffles;
-      // TMEM loads run one chunk ahead.
+      // count-weighted sum (memory.py:210-214), in base 2; a chunk's counts
+      // are 8 broadcast float4 loads; TMEM loads run one chunk ahead.
       float mx = -INFINITY, sum = 0.f, sdp = 0.f;
-      auto stats = [&](const uint32_t (&v)[32], float cl) {
-        float cmax = -INFINITY;
+      auto stats = [&](const uint32_t (&v)[32], const float* cs) {
+        float vmax = -INFINITY;
 #pragma unroll
-        for (int t = 0; t < 32; ++t) cmax = fmaxf(cmax, __uint_as_float(v[t]) * ps);
-        const float nm = fmaxf(mx, cmax);
-        const float sc = __expf(mx - nm);              // 0 on the first chunk
+        for (int t = 0; t < 32; ++t) vmax = fmaxf(vmax, __uint_as_float(v[t]));
+        const float nm = fmaxf(mx, vmax * psl);        // = max_t (v_t psl): psl > 0
+        const float sc = ex2(mx - nm);                 // 0 on the first chunk
         sum *= sc;
         sdp *= sc;
+        const float4* c4 = reinterpret_cast<const float4*>(cs);
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const float e = __expf(__uint_as_float(v[t]) * ps - nm);
-          sum += e;
-          sdp = fmaf(e, __shfl_sync(FULL, cl, t), sdp);
+        for (int q = 0; q < 8; ++q) {
+          const float4 cq = c4[q];
+          const float cv[4] = {cq.x, cq.y, cq.z, cq.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float e = ex2(fmaf(__uint_as_float(v[4 * q + e4]), psl, -nm));
+            sum += e;
+            sdp = fmaf(e, cv[e4], sdp);
+          }
         }
         mx = nm;
       };
       uint32_t va[32], vb[32];
-      // chunks hf, hf + 2, ...: nch / 2 of them, an even number (nch % 4 == 0)
+      // chunks hf, hf + 2, ...: nch / 2 of them, an even number (nch % 4 == 0);
+      // chunk c's counts at cw + 32 (c >> 1)
       tc::tmem_ld32(taddr + hf * 32, va);
       for (int c = hf; c < nch; c += 4) {
         tc::tmem_wait_ld_regs(va);
         tc::tmem_ld32(taddr + (c + 2) * 32, vb);
-        const float cl0 = cla;
-        cla = c + 4 < nch ? __ldg(cn + (c + 4) * 32 + lane) * A.dscale : 0.f;
-        stats(va, cl0);
+        stats(va, cw + (c >> 1) * 32);
         tc::tmem_wait_ld_regs(vb);
         if (c + 4 < nch) tc::tmem_ld32(taddr + (c + 4) * 32, va);
-        const float cl1 = clb;
-        clb = c + 6 < nch ? __ldg(cn + (c + 6) * 32 + lane) * A.dscale : 0.f;
-        stats(vb, cl1);
+        stats(vb, cw + ((c + 2) >> 1) * 32);
       }
       // combine the pair's statistics, the even chunks' first (both warps get the same values)
       mine[0] = mx;
@@ -318,7 +345,7 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
         const float m0 = hf ? other[0] : mx, s0 = hf ? other[1] : sum, d0 = hf ? other[2] : sdp;
         const float m1 = hf ? mx : other[0], s1 = hf ? sum : other[1], d1 = hf ? sdp : other[2];
         mx = fmaxf(m0, m1);
-        const float e0 = __expf(m0 - mx), e1 = __expf(m1 - mx);
+        const float e0 = ex2(m0 - mx), e1 = ex2(m1 - mx);
         sum = s0 * e0 + s1 * e1;
         sdp = d0 * e0 + d1 * e1;
       }
@@ -338,23 +365,30 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
         if (lane == 0) tc::mbar_arrive(&ctl->sread);
       }
       // chunk c of d cos: into the ring block D(c) and, transposed, to global memory
-      auto dcos = [&](int c, const uint32_t (&v)[32], float cl) -> bool {
+      auto dcos = [&](int c, const uint32_t (&v)[32]) -> bool {
         float hi[32], lo[32];
+        const float4* c4 = reinterpret_cast<const float4*>(cw + (c >> 1) * 32);
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const float cosv = __uint_as_float(v[t]);
-          const float e = __expf(cosv * ps - mx);
-          const float g = e * (__shfl_sync(FULL, cl, t) - sdp) * gsc;   // d p_j (T d p_j without btgrad)
-          float dc = g;
-          if (A.btgrad) {
-            dTr += g * cosv * ql;
-            dqr += g * cosv * T;
-            dc = g * Tq;
+        for (int q = 0; q < 8; ++q) {
+          const float4 cq = c4[q];
+          const float cv[4] = {cq.x, cq.y, cq.z, cq.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const int t = 4 * q + e4;
+            const float cosv = __uint_as_float(v[t]);
+            const float e = ex2(fmaf(cosv, psl, -mx));
+            const float g = e * (cv[e4] - sdp) * gsc;   // d p_j (T d p_j without btgrad)
+            float dc = g;
+            if (A.btgrad) {
+              dTr += g * cosv * ql;
+              dqr += g * cosv * T;
+              dc = g * Tq;
+            }
+            // transposed d cos: key (c 32 + t)'s row, 32 consecutive tokens per warp store
+            gd[(int64_t)(c * 32 + t) * A.Mp] = dc;
+            hi[t] = tc::to_tf32(dc);
+            lo[t] = tc::to_tf32(dc - hi[t]);
           }
-          // transposed d cos: key (c 32 + t)'s row, 32 consecutive tokens per warp store
-          gd[(int64_t)(c * 32 + t) * A.Mp] = dc;
-          hi[t] = tc::to_tf32(dc);
-          lo[t] = tc::to_tf32(dc - hi[t]);
         }
         if (c == my_last) {   // columns [0, half) read: the d q_hat MMA may overwrite them
           tc::fence_before_sync();
@@ -380,20 +414,14 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
         return true;
       };
       bool ok = true;
-      cla = __ldg(cn + hf * 32 + lane) * A.dscale;
-      clb = hf + 2 < nch ? __ldg(cn + (hf + 2) * 32 + lane) * A.dscale : 0.f;
       tc::tmem_ld32(taddr + hf * 32, va);
       for (int c = hf; ok && c < nch; c += 4) {
         tc::tmem_wait_ld_regs(va);
         tc::tmem_ld32(taddr + (c + 2) * 32, vb);
-        const float cl0 = cla;
-        cla = c + 4 < nch ? __ldg(cn + (c + 4) * 32 + lane) * A.dscale : 0.f;
-        ok = dcos(c, va, cl0);
+        ok = dcos(c, va);
         tc::tmem_wait_ld_regs(vb);
         if (ok && c + 4 < nch) tc::tmem_ld32(taddr + (c + 4) * 32, va);
-        const float cl1 = clb;
-        clb = c + 6 < nch ? __ldg(cn + (c + 6) * 32 + lane) * A.dscale : 0.f;
-        ok = ok && dcos(c + 2, vb, cl1);
+        ok = ok && dcos(c + 2, vb);
       }
       if (!ok) break;
       // the row's temperature / q_len gradient: the pair's two shares, even chunks first
