@@ -78,7 +78,14 @@ __global__ void __launch_bounds__(256) sum_slices_kernel(const float* __restrict
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = e / N, j = e - i * N;
     float x = 0.f;
-    for (int s = 0; s < S; ++s) x += P[(int64_t)s * n + e];
+    for (int s0 = 0; s0 < S; s0 += 8) {   // up to eight loads in flight, added in slice order
+      float a[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) a[q] = s0 + q < S ? P[(int64_t)(s0 + q) * n + e] : 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (s0 + q < S) x += a[q];
+    }
     if (bias) x += bias[j];
     float* c = C + i * ldc + j;
     *c = acc ? *c + x : x;

@@ -57,13 +57,6 @@ struct GrArgs {
   int* err;
 };
 
-// Round a finite float32 to tf32 (10 mantissa bits), nearest with ties away
-// from zero: add half of the dropped 13-bit unit to the magnitude bits and
-// clear them (a carry into the exponent is the correct rounding up).
-__device__ __forceinline__ float tf32_rna(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-
 // Convert one raw tile of `rows` rows into K-major swizzled hi / lo tiles.
 __device__ __forceinline__ void convert_tile(const float* raw, bool kmajor, int rows, float* hi, float* lo, int t) {
   if (kmajor) {   // same swizzled layout: elementwise
@@ -73,10 +66,10 @@ __device__ __forceinline__ void convert_tile(const float* raw, bool kmajor, int 
     for (int i = t; i < rows * 8; i += 128) {
       const float4 x = r4[i];
       float4 h, l;
-      h.x = tf32_rna(x.x); l.x = tf32_rna(x.x - h.x);
-      h.y = tf32_rna(x.y); l.y = tf32_rna(x.y - h.y);
-      h.z = tf32_rna(x.z); l.z = tf32_rna(x.z - h.z);
-      h.w = tf32_rna(x.w); l.w = tf32_rna(x.w - h.w);
+      h.x = tc::to_tf32(x.x); l.x = tc::to_tf32(x.x - h.x);
+      h.y = tc::to_tf32(x.y); l.y = tc::to_tf32(x.y - h.y);
+      h.z = tc::to_tf32(x.z); l.z = tc::to_tf32(x.z - h.z);
+      h.w = tc::to_tf32(x.w); l.w = tc::to_tf32(x.w - h.w);
       h4[i] = h;
       l4[i] = l;
     }
@@ -89,10 +82,10 @@ __device__ __forceinline__ void convert_tile(const float* raw, bool kmajor, int 
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       float4 h, l;
-      h.x = tf32_rna(v[4 * q]); l.x = tf32_rna(v[4 * q] - h.x);
-      h.y = tf32_rna(v[4 * q + 1]); l.y = tf32_rna(v[4 * q + 1] - h.y);
-      h.z = tf32_rna(v[4 * q + 2]); l.z = tf32_rna(v[4 * q + 2] - h.z);
-      h.w = tf32_rna(v[4 * q + 3]); l.w = tf32_rna(v[4 * q + 3] - h.w);
+      h.x = tc::to_tf32(v[4 * q]); l.x = tc::to_tf32(v[4 * q] - h.x);
+      h.y = tc::to_tf32(v[4 * q + 1]); l.y = tc::to_tf32(v[4 * q + 1] - h.y);
+      h.z = tc::to_tf32(v[4 * q + 2]); l.z = tc::to_tf32(v[4 * q + 2] - h.z);
+      h.w = tc::to_tf32(v[4 * q + 3]); l.w = tc::to_tf32(v[4 * q + 3] - h.w);
       const int at = (q ^ (t & 7)) << 4;
       *reinterpret_cast<float4*>(hrow + at) = h;
       *reinterpret_cast<float4*>(lrow + at) = l;

@@ -180,11 +180,13 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
                : "memory");
 }
 
-// Round-to-nearest tf32 value of x, as a float32 bit pattern.
+// tf32 value of a finite x (10 mantissa bits) as a float32 bit pattern,
+// rounded to nearest with ties away from zero: half of the dropped 13-bit
+// unit added to the magnitude bits, then those bits cleared (a carry into
+// the exponent is the correct rounding up).  Two integer instructions; the
+// same values as cvt.rna.tf32.f32, which measured slower in the converters.
 __device__ __forceinline__ float to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 }  // namespace tc
