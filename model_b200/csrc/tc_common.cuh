@@ -184,7 +184,7 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
 // rounded to nearest with ties away from zero: half of the dropped 13-bit
 // unit added to the magnitude bits, then those bits cleared (a carry into
 // the exponent is the correct rounding up).  Two integer instructions; the
-// same values as cvt.rna.tf32.f32, which measured slower in the converters.
+// rounding rule of cvt.rna.tf32.f32, which measured slower in the converters.
 __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
