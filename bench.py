@@ -98,7 +98,7 @@ class ClockSampler:
                0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
 
-    def __init__(self, index: int, period: float = 0.001):
+    def __init__(self, index: int, period: float = 0.005):
         self.samples, self.reasons, self.ok = [], set(), False
         self.period, self._stop = period, threading.Event()
         try:

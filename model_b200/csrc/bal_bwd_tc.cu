@@ -386,8 +386,8 @@ __global__ void __launch_bounds__(BB_THREADS, 1)
             }
             // transposed d cos: key (c 32 + t)'s row, 32 consecutive tokens per warp store
             gd[(int64_t)(c * 32 + t) * A.Mp] = dc;
-            hi[t] = tc::to_tf32(dc);
-            lo[t] = tc::to_tf32(dc - hi[t]);
+            hi[t] = tc::to_tf32_int(dc);
+            lo[t] = tc::to_tf32_int(dc - hi[t]);
           }
         }
         if (c == my_last) {   // columns [0, half) read: the d q_hat MMA may overwrite them

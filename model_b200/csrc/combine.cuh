@@ -17,10 +17,11 @@
 
 namespace ml {
 
-// rna_tf32(x): the high half of the 3xTF32 split used by the tensor-core GEMMs
-// (round to nearest, ties away, by an integer add and mask; x finite).
+// rna_tf32(x): the high half of the 3xTF32 split used by the tensor-core GEMMs.
 __device__ __forceinline__ float tc_round(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 // VEC consecutive value-row elements as float32.

@@ -66,10 +66,10 @@ __device__ __forceinline__ void convert_tile(const float* raw, bool kmajor, int 
     for (int i = t; i < rows * 8; i += 128) {
       const float4 x = r4[i];
       float4 h, l;
-      h.x = tc::to_tf32(x.x); l.x = tc::to_tf32(x.x - h.x);
-      h.y = tc::to_tf32(x.y); l.y = tc::to_tf32(x.y - h.y);
-      h.z = tc::to_tf32(x.z); l.z = tc::to_tf32(x.z - h.z);
-      h.w = tc::to_tf32(x.w); l.w = tc::to_tf32(x.w - h.w);
+      h.x = tc::to_tf32_int(x.x); l.x = tc::to_tf32_int(x.x - h.x);
+      h.y = tc::to_tf32_int(x.y); l.y = tc::to_tf32_int(x.y - h.y);
+      h.z = tc::to_tf32_int(x.z); l.z = tc::to_tf32_int(x.z - h.z);
+      h.w = tc::to_tf32_int(x.w); l.w = tc::to_tf32_int(x.w - h.w);
       h4[i] = h;
       l4[i] = l;
     }
@@ -82,10 +82,10 @@ __device__ __forceinline__ void convert_tile(const float* raw, bool kmajor, int 
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       float4 h, l;
-      h.x = tc::to_tf32(v[4 * q]); l.x = tc::to_tf32(v[4 * q] - h.x);
-      h.y = tc::to_tf32(v[4 * q + 1]); l.y = tc::to_tf32(v[4 * q + 1] - h.y);
-      h.z = tc::to_tf32(v[4 * q + 2]); l.z = tc::to_tf32(v[4 * q + 2] - h.z);
-      h.w = tc::to_tf32(v[4 * q + 3]); l.w = tc::to_tf32(v[4 * q + 3] - h.w);
+      h.x = tc::to_tf32_int(v[4 * q]); l.x = tc::to_tf32_int(v[4 * q] - h.x);
+      h.y = tc::to_tf32_int(v[4 * q + 1]); l.y = tc::to_tf32_int(v[4 * q + 1] - h.y);
+      h.z = tc::to_tf32_int(v[4 * q + 2]); l.z = tc::to_tf32_int(v[4 * q + 2] - h.z);
+      h.w = tc::to_tf32_int(v[4 * q + 3]); l.w = tc::to_tf32_int(v[4 * q + 3] - h.w);
       const int at = (q ^ (t & 7)) << 4;
       *reinterpret_cast<float4*>(hrow + at) = h;
       *reinterpret_cast<float4*>(lrow + at) = l;

@@ -180,12 +180,19 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
                : "memory");
 }
 
-// tf32 value of a finite x (10 mantissa bits) as a float32 bit pattern,
-// rounded to nearest with ties away from zero: half of the dropped 13-bit
-// unit added to the magnitude bits, then those bits cleared (a carry into
-// the exponent is the correct rounding up).  Two integer instructions; the
-// rounding rule of cvt.rna.tf32.f32, which measured slower in the converters.
+// Round-to-nearest tf32 value of x, as a float32 bit pattern.
 __device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// The same rounding (nearest, ties away from zero) of a finite x by integer
+// arithmetic: half of the dropped 13-bit unit added to the magnitude bits,
+// then those bits cleared (a carry into the exponent is the correct rounding
+// up).  Faster than the conversion instruction in the operand-splitting
+// GEMM's converter warps and the balance backward's epilogue.
+__device__ __forceinline__ float to_tf32_int(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
